@@ -1,0 +1,203 @@
+/*
+ * pk.h -- C ABI of libpocketinfer_b200.so, the B200 (sm_100a) implementation
+ * of pocketinfer's decode token loop and its 32-token prefill.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, returns an
+ * int status (PK_OK == 0) and leaves a message for pk_last_error() on failure.
+ * Nothing falls back to the CPU: a failure is an error status.
+ *
+ * Reference interfaces replaced (Aleinto97/pocket-workbench-android,
+ * paths relative to rust/pocketinfer/src/):
+ *   pk_supports            quant_int.rs:75-80 supported(), backend/opencl.rs:432-434 supports()
+ *   pk_q8_quantize         quant_int.rs:17-56 Q8Act::prepare
+ *   pk_matmul              model.rs:242-321 Pool::matmul (int8 act path, raw GGUF blocks)
+ *   pk_pack_weights /
+ *   pk_matmul_packed       the same contraction on the device weight layout
+ *   pk_backend_*           backend/opencl.rs:261-500 OpenClBackend::{new,selftest,supports,matvec}
+ *   pk_create/pk_load_gguf model.rs:698-723 Engine::load (+ gguf.rs, util.rs MappedFile)
+ *   pk_forward             model.rs:825-831 Engine::forward
+ *   pk_logits              model.rs:1231-1233 Engine::logits
+ *   pk_argmax              sampler.rs:26-36 sample() with temp <= 0
+ *   pk_generate            model.rs:1235-1352 Engine::generate (prefix-KV reuse included)
+ *   pk_request_stop        util.rs:274-282 request_stop / STOP_REQUESTED
+ *   pk_set_debug/get_dump  model.rs:870-872,942-1168 Engine.dbg intermediates
+ *
+ * Threading: one engine per host thread; calls on one engine are serialised
+ * by the caller (the reference serialises with a global Mutex, jni.rs:211).
+ * Op-level calls are ordered on the CUDA stream passed in (NULL = default).
+ */
+#ifndef PK_H
+#define PK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PK_OK 0
+#define PK_ERR_INVALID 1      /* bad argument, shape or layout */
+#define PK_ERR_UNSUPPORTED 2  /* tensor type not handled on the device */
+#define PK_ERR_CUDA 3         /* CUDA runtime / launch failure */
+#define PK_ERR_OOM 4          /* device or host allocation failed */
+#define PK_ERR_IO 5           /* file or GGUF parse error */
+#define PK_ERR_CONTEXT_FULL 6 /* position >= n_ctx */
+#define PK_ERR_STOPPED 7      /* pk_request_stop() observed */
+#define PK_ERR_TIMEOUT 8      /* a bounded device wait expired */
+
+/* GGML tensor type ids (quant.rs:3-17). */
+#define PK_TYPE_F32 0
+#define PK_TYPE_F16 1
+#define PK_TYPE_Q4_0 2
+#define PK_TYPE_Q8_0 8
+#define PK_TYPE_Q4_K 12
+#define PK_TYPE_Q6_K 14
+#define PK_TYPE_BF16 30
+
+/* Last error message of the calling thread ("" if none). */
+const char *pk_last_error(void);
+/* ABI version: major * 100 + minor. */
+int pk_version(void);
+
+/* 1 if the device matvec handles ttype (Q4_K, Q6_K, Q4_0, Q8_0), else 0.
+ * Replaces quant_int.rs:75-80 supported() and opencl.rs:432-434 supports(). */
+int pk_supports(uint32_t ttype);
+
+/* ---------------------------------------------------------------- op level */
+
+/* Quantised activations, Q8Act layout (quant_int.rs:3-10), device memory:
+ *   q   int8  [b][k]        (lane-major)
+ *   d   float [b][k / 32]
+ *   sum int32 [b][k / 32]
+ * k must be a multiple of 32. */
+typedef struct {
+  int8_t *q;
+  float *d;
+  int32_t *sum;
+  int k;
+  int b;
+} pk_q8act;
+
+/* Q8Act::prepare (quant_int.rs:17-56).  x is feature-major [k][b] (x[i*b+bi]),
+ * the reference's activation layout.  Bit-exact with the reference. */
+int pk_q8_quantize(const float *x, int k, int b, pk_q8act *act, void *stream);
+
+/* Pool::matmul with the int8 act path (model.rs:242-321, quant_int.rs:282-419).
+ * w: device pointer to raw GGUF blocks, n_rows rows of row_bytes each.
+ * out: [n_rows][b] (out[r*b + lane]), overwritten ("zero-filled then +=").
+ * Q6_K/Q4_0/Q8_0 rows are first packed into a stream-ordered temporary
+ * (cudaMallocAsync); callers that reuse a tensor should pack once with
+ * pk_pack_weights and call pk_matmul_packed. */
+int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows,
+              const pk_q8act *act, float *out, void *stream);
+
+/* Device weight layout: bytes needed for n_rows x k of ttype (>= raw size). */
+size_t pk_packed_bytes(uint32_t ttype, int k, int n_rows);
+/* Raw GGUF blocks (device) -> device layout (device, 16-byte aligned). */
+int pk_pack_weights(uint32_t ttype, const void *raw, size_t row_bytes, int k, int n_rows,
+                    void *packed, void *stream);
+/* Same contraction as pk_matmul on packed weights; out [n_rows][b]. */
+int pk_matmul_packed(uint32_t ttype, const void *packed, int k, int n_rows,
+                     const pk_q8act *act, float *out, void *stream);
+
+/* ------------------------------------------------- accelerator-backend level */
+
+/* Mirrors OpenClBackend (backend/opencl.rs:261-500): weights are host
+ * buffers (the GGUF mmap), copied to the device once and cached by
+ * (pointer, length); x and out are host buffers; the call is synchronous.
+ * x is quantised with Q8Act::prepare on the device, so results equal the
+ * reference's int8 path (not the f32 OpenCL kernels). */
+typedef struct pk_backend pk_backend;
+int pk_backend_new(int device, pk_backend **out);
+void pk_backend_free(pk_backend *be);
+/* opencl.rs:391-430: one Q4_K and one Q6_K block against the f32 dot,
+ * tolerance 2% + 0.01. */
+int pk_backend_selftest(pk_backend *be);
+int pk_backend_supports(pk_backend *be, uint32_t ttype);
+int pk_backend_matvec(pk_backend *be, uint32_t ttype, const void *w, size_t w_len, int k,
+                      const float *x, float *out, int n_rows);
+
+/* ------------------------------------------------------------- engine level */
+
+typedef struct pk_engine pk_engine;
+
+typedef struct {
+  int n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_rot, n_vocab, n_ctx;
+  float rope_theta, rms_eps;
+  size_t weight_bytes;      /* device weight bytes (packed layout) */
+  size_t kv_bytes;          /* device KV cache bytes */
+  size_t stream_bytes;      /* weight + norm + embedding-row bytes one decode token reads */
+} pk_model_info;
+
+typedef struct {
+  float temp;     /* <= 0: greedy argmax */
+  float top_p;
+  uint64_t seed;  /* splitmix64 (sampler.rs:1-19) */
+  int max_tokens;
+  int stop_at_eog; /* 1: stop on an end-of-generation id (tokenizer.rs:252) */
+} pk_gen_opts;
+
+typedef struct {
+  int prefill_tokens;
+  int prefill_cached_tokens;
+  double prefill_ms;
+  int gen_tokens;
+  double gen_ms;
+  char stop[32]; /* "max_tokens" | "eog" | "user_stop" | "context_full" | "callback_error" */
+} pk_gen_stats;
+
+/* Token callback: return 0 to abort ("callback_error"). */
+typedef int (*pk_token_cb)(uint32_t token, void *user);
+
+/* Engine::load split in two: create the device context, then load a GGUF.
+ * max_batch bounds the prefill chunk (<= 64, MAX_BATCH of model.rs:12). */
+int pk_create(int device, int n_ctx, int max_batch, pk_engine **out);
+int pk_load_gguf(pk_engine *eng, const char *path);
+void pk_destroy(pk_engine *eng);
+int pk_model_info_get(pk_engine *eng, pk_model_info *info);
+
+/* Engine::forward: invalidates prefix reuse.  ids/positions are host arrays. */
+int pk_forward(pk_engine *eng, const uint32_t *ids, const int *positions, int n, int want_logits);
+/* Copies the last logits (n_vocab floats) to host memory. */
+int pk_logits(pk_engine *eng, float *out, int n);
+/* Greedy sample of the current logits on the device (first maximum wins). */
+int pk_argmax(pk_engine *eng, uint32_t *token);
+/* Engine::generate.  out_ids receives up to out_cap generated ids. */
+int pk_generate(pk_engine *eng, const uint32_t *prompt, int n, const pk_gen_opts *opts,
+                pk_token_cb cb, void *user, uint32_t *out_ids, int out_cap, int *n_out,
+                pk_gen_stats *stats);
+
+/* Greedy decode loop kept on the device: n_steps steps of (argmax of the
+ * current logits -> feed the token back -> one b=1 forward), one CUDA-graph
+ * launch per step and no host synchronisation between steps.  Writes the
+ * produced ids; device_ms (nullable) receives the CUDA-event time of the
+ * steps measured on the engine's stream. */
+int pk_decode_steps_device(pk_engine *eng, int n_steps, uint32_t *out_ids, float *device_ms);
+/* Rewinds the sequence to pos tokens (0 < pos <= current length), keeping the
+ * current logits as the next step's input.  Positions >= pos are rewritten
+ * before they are read again.  Invalidates prefix reuse beyond pos. */
+int pk_set_position(pk_engine *eng, int pos);
+
+/* One decode step run eagerly with CUDA events around every kernel: per
+ * kernel name the launch count, device time and algorithmic bytes. */
+typedef struct {
+  char name[32];
+  int launches;
+  double ms;
+  double bytes;
+} pk_kernel_stat;
+int pk_decode_profile(pk_engine *eng, pk_kernel_stat *out, int cap, int *n_out);
+
+/* Records layer-0 intermediates for parity bisection (Engine.dbg). */
+int pk_set_debug(pk_engine *eng, int on);
+/* Copies the named layer-0 dump (token-major [b][dim]); returns elements via n_out. */
+int pk_get_dump(pk_engine *eng, const char *name, float *out, int cap, int *n_out);
+
+void pk_request_stop(void);
+void pk_clear_stop(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PK_H */

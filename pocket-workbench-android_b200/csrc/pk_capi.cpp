@@ -1,0 +1,405 @@
+// pk_capi.cpp -- extern "C" entry points declared in include/pk.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <utility>
+
+#include "pk.h"
+#include "pk_engine.h"
+
+namespace pk {
+
+static thread_local std::string t_err;
+
+int set_error(int code, const std::string &msg) {
+  t_err = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char *what) {
+  t_err = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return e == cudaErrorMemoryAllocation ? PK_ERR_OOM : PK_ERR_CUDA;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+#define CK(expr)                                          \
+  do {                                                    \
+    cudaError_t _e = (expr);                              \
+    if (_e != cudaSuccess) return cuda_error(_e, #expr);  \
+  } while (0)
+
+namespace {
+
+bool q8_ok(const pk_q8act *a, int k) {
+  return a && a->q && a->d && a->sum && a->k == k && a->b >= 1 && a->b <= 64;
+}
+
+Q8Dev to_dev(const pk_q8act *a) {
+  Q8Dev d;
+  d.q = a->q;
+  d.d = a->d;
+  d.s = a->sum;
+  d.k = a->k;
+  d.b = a->b;
+  return d;
+}
+
+int check_matvec_shape(uint32_t ttype, int k, int n_rows) {
+  if (!type_is_matvec((int)ttype))
+    return set_error(PK_ERR_UNSUPPORTED, "type " + std::to_string(ttype) + " not supported on the device");
+  int be = 0, bb = 0;
+  type_block((int)ttype, &be, &bb);
+  if (k <= 0 || n_rows <= 0 || k % be != 0 || k % 32 != 0)
+    return set_error(PK_ERR_INVALID, "k must be a positive multiple of the block size and of 32");
+  return PK_OK;
+}
+
+int matmul_packed(uint32_t ttype, const void *packed, int k, int n_rows, const pk_q8act *act, float *out,
+                  cudaStream_t st) {
+  const DevTensor w = packed_view((int)ttype, k, n_rows, packed);
+  const Q8Dev a = to_dev(act);
+  if (a.b == 1) {
+    B1Src src;
+    src.act = a;
+    CK(launch_mv_b1(w, src, out, false, st));
+  } else {
+    CK(launch_mv_lanes(w, a, out, a.b, 1, false, st));
+  }
+  return PK_OK;
+}
+
+// ---- host f32 dot for the backend self-test (quant.rs:260-287, 323-347, 377-441)
+float h_f16(uint16_t h) {
+  const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1Fu, mant = h & 0x3FFu;
+  float v;
+  if (exp == 0) v = std::ldexp((float)mant, -24);
+  else if (exp == 31) v = mant ? NAN : INFINITY;
+  else v = std::ldexp((float)(mant | 0x400u), (int)exp - 25);
+  return sign ? -v : v;
+}
+
+float host_dot_f32(uint32_t t, const uint8_t *w, int k, const float *x) {
+  float sum = 0.0f;
+  for (int blk = 0; blk < k / 256; blk++) {
+    if (t == PK_TYPE_Q4_K) {
+      const uint8_t *b = w + blk * 144;
+      const float d = h_f16((uint16_t)(b[0] | (b[1] << 8))), dmin = h_f16((uint16_t)(b[2] | (b[3] << 8)));
+      const uint8_t *sc = b + 4, *qs = b + 16;
+      for (int j = 0; j < 256; j++) {
+        const int n64 = j / 64, wi = j % 64, l = wi % 32, is = 2 * n64 + (wi >= 32);
+        int s, m;
+        if (is < 4) { s = sc[is] & 63; m = sc[is + 4] & 63; }
+        else { s = (sc[is + 4] & 0xF) | ((sc[is - 4] >> 6) << 4); m = (sc[is + 4] >> 4) | ((sc[is] >> 6) << 4); }
+        const int q = wi < 32 ? (qs[n64 * 32 + l] & 0xF) : (qs[n64 * 32 + l] >> 4);
+        sum += (d * (float)s * (float)q - dmin * (float)m) * x[blk * 256 + j];
+      }
+    } else {
+      const uint8_t *b = w + blk * 210;
+      const float d = h_f16((uint16_t)(b[208] | (b[209] << 8)));
+      for (int j = 0; j < 256; j++) {
+        const int half = j / 128, wi = j % 128, quarter = wi / 32, l = wi % 32, is = l / 16;
+        int lo = (quarter & 1) ? b[half * 64 + l + 32] : b[half * 64 + l];
+        lo = (quarter & 2) ? (lo >> 4) : (lo & 0xF);
+        const int q = (lo | (((b[128 + half * 32 + l] >> (2 * quarter)) & 3) << 4)) - 32;
+        sum += d * (float)(int8_t)b[192 + half * 8 + is + 2 * quarter] * (float)q * x[blk * 256 + j];
+      }
+    }
+  }
+  return sum;
+}
+
+}  // namespace
+
+// The OpenClBackend analogue (backend/opencl.rs:79-516).
+struct pk_backend {
+  int device = 0;
+  cudaStream_t st = nullptr;
+  std::map<std::pair<const void *, size_t>, void *> weights;  // (host ptr, len) -> packed device copy
+  float *d_x = nullptr, *d_out = nullptr;
+  size_t x_cap = 0, out_cap = 0;
+  Q8Dev act;
+  int act_k = 0;
+  ~pk_backend() {
+    if (st) cudaStreamSynchronize(st);
+    for (auto &kv : weights) cudaFree(kv.second);
+    cudaFree(d_x);
+    cudaFree(d_out);
+    cudaFree(act.q);
+    cudaFree(act.d);
+    cudaFree(act.s);
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
+struct pk_engine {
+  Engine eng;
+};
+
+extern "C" {
+
+const char *pk_last_error(void) { return t_err.c_str(); }
+int pk_version(void) { return 100; }
+int pk_supports(uint32_t ttype) { return type_is_matvec((int)ttype) ? 1 : 0; }
+
+int pk_q8_quantize(const float *x, int k, int b, pk_q8act *act, void *stream) {
+  if (!x || k <= 0 || k % 32 != 0 || b < 1 || b > 64)
+    return set_error(PK_ERR_INVALID, "pk_q8_quantize: k must be a positive multiple of 32 and b in 1..64");
+  if (!q8_ok(act, k) || act->b != b) return set_error(PK_ERR_INVALID, "pk_q8_quantize: activation buffer does not match k/b");
+  CK(launch_q8(x, b, 1, k, b, to_dev(act), (cudaStream_t)stream));
+  return PK_OK;
+}
+
+size_t pk_packed_bytes(uint32_t ttype, int k, int n_rows) {
+  if (!type_is_matvec((int)ttype) || k <= 0 || n_rows <= 0) return 0;
+  return packed_bytes((int)ttype, k, n_rows);
+}
+
+int pk_pack_weights(uint32_t ttype, const void *raw, size_t row_bytes, int k, int n_rows, void *packed, void *stream) {
+  int rc = check_matvec_shape(ttype, k, n_rows);
+  if (rc) return rc;
+  int be, bb;
+  type_block((int)ttype, &be, &bb);
+  if (row_bytes != (size_t)(k / be) * bb) return set_error(PK_ERR_INVALID, "row_bytes does not match k for this type");
+  if (!raw || !packed || ((uintptr_t)packed & 15)) return set_error(PK_ERR_INVALID, "packed buffer must be 16-byte aligned");
+  CK(launch_pack((int)ttype, raw, row_bytes, k, n_rows, packed, (cudaStream_t)stream));
+  return PK_OK;
+}
+
+int pk_matmul_packed(uint32_t ttype, const void *packed, int k, int n_rows, const pk_q8act *act, float *out,
+                     void *stream) {
+  int rc = check_matvec_shape(ttype, k, n_rows);
+  if (rc) return rc;
+  if (!q8_ok(act, k)) return set_error(PK_ERR_INVALID, "activation does not match k");
+  if (!packed || !out || ((uintptr_t)packed & 15)) return set_error(PK_ERR_INVALID, "packed weights must be 16-byte aligned");
+  return matmul_packed(ttype, packed, k, n_rows, act, out, (cudaStream_t)stream);
+}
+
+int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows, const pk_q8act *act, float *out,
+              void *stream) {
+  int rc = check_matvec_shape(ttype, k, n_rows);
+  if (rc) return rc;
+  if (!q8_ok(act, k)) return set_error(PK_ERR_INVALID, "activation does not match k");
+  int be, bb;
+  type_block((int)ttype, &be, &bb);
+  if (row_bytes != (size_t)(k / be) * bb) return set_error(PK_ERR_INVALID, "row_bytes does not match k for this type");
+  if (!w || !out) return set_error(PK_ERR_INVALID, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (ttype == PK_TYPE_Q4_K && ((uintptr_t)w & 15) == 0)  // the device layout of Q4_K is the GGUF layout
+    return matmul_packed(ttype, w, k, n_rows, act, out, st);
+  void *tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, packed_bytes((int)ttype, k, n_rows), st));
+  cudaError_t e = launch_pack((int)ttype, w, row_bytes, k, n_rows, tmp, st);
+  if (e != cudaSuccess) {
+    cudaFreeAsync(tmp, st);
+    return cuda_error(e, "pack");
+  }
+  rc = matmul_packed(ttype, tmp, k, n_rows, act, out, st);
+  cudaFreeAsync(tmp, st);
+  return rc;
+}
+
+int pk_backend_new(int device, pk_backend **out) {
+  if (!out) return set_error(PK_ERR_INVALID, "null out");
+  int n = 0;
+  CK(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return set_error(PK_ERR_INVALID, "no CUDA device " + std::to_string(device));
+  auto *be = new (std::nothrow) pk_backend();
+  if (!be) return set_error(PK_ERR_OOM, "out of host memory");
+  be->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&be->st, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete be;
+    return cuda_error(e, "pk_backend_new");
+  }
+  *out = be;
+  return PK_OK;
+}
+
+void pk_backend_free(pk_backend *be) { delete be; }
+
+int pk_backend_supports(pk_backend *, uint32_t ttype) { return pk_supports(ttype); }
+
+int pk_backend_matvec(pk_backend *be, uint32_t ttype, const void *w, size_t w_len, int k, const float *x, float *out,
+                      int n_rows) {
+  if (!be || !w || !x || !out) return set_error(PK_ERR_INVALID, "null argument");
+  int rc = check_matvec_shape(ttype, k, n_rows);
+  if (rc) return rc;
+  int bsz, bb;
+  type_block((int)ttype, &bsz, &bb);
+  const size_t row_bytes = (size_t)(k / bsz) * bb;
+  if (w_len != row_bytes * (size_t)n_rows) return set_error(PK_ERR_INVALID, "weight slice length does not match k x n_rows");
+  CK(cudaSetDevice(be->device));
+  auto key = std::make_pair(w, w_len);
+  auto it = be->weights.find(key);
+  void *packed = nullptr;
+  if (it == be->weights.end()) {
+    void *raw = nullptr;
+    CK(cudaMalloc(&packed, packed_bytes((int)ttype, k, n_rows)));
+    cudaError_t e = cudaMalloc(&raw, w_len);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(raw, w, w_len, cudaMemcpyHostToDevice, be->st);
+    if (e == cudaSuccess) e = launch_pack((int)ttype, raw, row_bytes, k, n_rows, packed, be->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(be->st);
+    cudaFree(raw);
+    if (e != cudaSuccess) {
+      cudaFree(packed);
+      return cuda_error(e, "weight upload");
+    }
+    be->weights[key] = packed;
+  } else {
+    packed = it->second;
+  }
+  if ((size_t)k * 4 > be->x_cap) {
+    cudaFree(be->d_x);
+    be->d_x = nullptr;
+    be->x_cap = 0;
+    CK(cudaMalloc((void **)&be->d_x, (size_t)k * 4));
+    be->x_cap = (size_t)k * 4;
+  }
+  if ((size_t)n_rows * 4 > be->out_cap) {
+    cudaFree(be->d_out);
+    be->d_out = nullptr;
+    be->out_cap = 0;
+    CK(cudaMalloc((void **)&be->d_out, (size_t)n_rows * 4));
+    be->out_cap = (size_t)n_rows * 4;
+  }
+  if (k > be->act_k) {
+    cudaFree(be->act.q);
+    cudaFree(be->act.d);
+    cudaFree(be->act.s);
+    be->act = Q8Dev();
+    be->act_k = 0;
+    CK(cudaMalloc((void **)&be->act.q, (size_t)k));
+    CK(cudaMalloc((void **)&be->act.d, (size_t)k / 32 * 4));
+    CK(cudaMalloc((void **)&be->act.s, (size_t)k / 32 * 4));
+    be->act_k = k;
+  }
+  Q8Dev a = be->act;
+  a.k = k;
+  a.b = 1;
+  CK(cudaMemcpyAsync(be->d_x, x, (size_t)k * 4, cudaMemcpyHostToDevice, be->st));
+  CK(launch_q8(be->d_x, 1, 1, k, 1, a, be->st));
+  B1Src src;
+  src.act = a;
+  CK(launch_mv_b1(packed_view((int)ttype, k, n_rows, packed), src, be->d_out, false, be->st));
+  CK(cudaMemcpyAsync(out, be->d_out, (size_t)n_rows * 4, cudaMemcpyDeviceToHost, be->st));
+  CK(cudaStreamSynchronize(be->st));
+  return PK_OK;
+}
+
+// backend/opencl.rs:391-430
+int pk_backend_selftest(pk_backend *be) {
+  if (!be) return set_error(PK_ERR_INVALID, "null backend");
+  const int k = 256;
+  float x[256];
+  for (int j = 0; j < k; j++) x[j] = (float)(j % 7) * 0.1f - 0.3f;
+  uint8_t w4[144], w6[210];
+  std::memset(w4, 0, sizeof(w4));
+  w4[0] = 0x00; w4[1] = 0x3C;
+  w4[4] = 1;
+  for (int i = 0; i < 128; i++) w4[16 + i] = 0x21;
+  for (int i = 0; i < 128; i++) w6[i] = 0x95;
+  for (int i = 0; i < 64; i++) w6[128 + i] = 0x1B;
+  for (int i = 0; i < 16; i++) w6[192 + i] = 2;
+  w6[208] = 0x00; w6[209] = 0x3C;
+  struct Case { uint32_t t; const uint8_t *w; size_t len; const char *name; } cases[2] = {
+      {PK_TYPE_Q4_K, w4, sizeof(w4), "q4_K"}, {PK_TYPE_Q6_K, w6, sizeof(w6), "q6_K"}};
+  int result = PK_OK;
+  for (auto &c : cases) {
+    float got = 0.0f;
+    int rc = pk_backend_matvec(be, c.t, c.w, c.len, k, x, &got, 1);
+    if (rc) { result = rc; break; }
+    const float want = host_dot_f32(c.t, c.w, k, x);
+    if (std::fabs(got - want) > std::fabs(want) * 0.02f + 0.01f) {
+      result = set_error(PK_ERR_INVALID, std::string(c.name) + " self-test failed: gpu=" + std::to_string(got) +
+                                             " cpu=" + std::to_string(want));
+      break;
+    }
+  }
+  for (auto &kv : be->weights) cudaFree(kv.second);  // clear_weight_cache (the buffers were stack-local)
+  be->weights.clear();
+  return result;
+}
+
+int pk_create(int device, int n_ctx, int max_batch, pk_engine **out) {
+  if (!out) return set_error(PK_ERR_INVALID, "null out");
+  auto *e = new (std::nothrow) pk_engine();
+  if (!e) return set_error(PK_ERR_OOM, "out of host memory");
+  int rc = e->eng.create(device, n_ctx, max_batch);
+  if (rc) {
+    delete e;
+    return rc;
+  }
+  *out = e;
+  return PK_OK;
+}
+
+int pk_load_gguf(pk_engine *e, const char *path) {
+  if (!e || !path) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.load(path);
+}
+
+void pk_destroy(pk_engine *e) { delete e; }
+
+int pk_model_info_get(pk_engine *e, pk_model_info *info) {
+  if (!e || !info) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.info(info);
+}
+
+int pk_forward(pk_engine *e, const uint32_t *ids, const int *positions, int n, int want_logits) {
+  if (!e || !ids || !positions) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.forward(ids, positions, n, want_logits != 0);
+}
+
+int pk_logits(pk_engine *e, float *out, int n) {
+  if (!e || !out) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.logits(out, n);
+}
+
+int pk_argmax(pk_engine *e, uint32_t *token) {
+  if (!e || !token) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.argmax(token);
+}
+
+int pk_generate(pk_engine *e, const uint32_t *prompt, int n, const pk_gen_opts *opts, pk_token_cb cb, void *user,
+                uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats) {
+  if (!e || !prompt || !opts) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.generate(prompt, n, *opts, cb, user, out_ids, out_cap, n_out, stats);
+}
+
+int pk_decode_steps_device(pk_engine *e, int n_steps, uint32_t *out_ids, float *device_ms) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.decode_steps_device(n_steps, out_ids, device_ms);
+}
+
+int pk_set_position(pk_engine *e, int pos) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.set_position(pos);
+}
+
+int pk_decode_profile(pk_engine *e, pk_kernel_stat *out, int cap, int *n_out) {
+  if (!e || (!out && cap > 0)) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.decode_profile(out, cap, n_out);
+}
+
+int pk_set_debug(pk_engine *e, int on) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.set_debug(on != 0);
+}
+
+int pk_get_dump(pk_engine *e, const char *name, float *out, int cap, int *n_out) {
+  if (!e || !name) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.get_dump(name, out, cap, n_out);
+}
+
+void pk_request_stop(void) { g_stop.store(true); }
+void pk_clear_stop(void) { g_stop.store(false); }
+
+}  // extern "C"

@@ -1,0 +1,747 @@
+// pk_engine.cu -- device engine: GGUF -> HBM, forward pass, decode graphs,
+// and Engine::generate with the reference's prefix-KV reuse rules.
+//
+// Reference: rust/pocketinfer/src/model.rs (Aleinto97/pocket-workbench-android)
+//   Config::from_gguf        :32-97      Model::load / finish :487-601
+//   KvCache                  :352-387    Scratch (RoPE tables) :408-461
+//   forward_inner / layers   :833-1172   generate            :1235-1352
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+
+#include "pk_engine.h"
+
+namespace pk {
+
+std::atomic<bool> g_stop{false};  // util.rs:274-282 STOP_REQUESTED
+
+#define PK_CK(expr)                                          \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return cuda_error(_e, #expr);     \
+  } while (0)
+
+static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+Engine::~Engine() {
+  if (st_) cudaStreamSynchronize(st_);
+  release_graphs();
+  cudaFree(d_weights_);
+  cudaFree(d_kcache_);
+  cudaFree(d_vcache_);
+  cudaFree(d_rope_cos_);
+  cudaFree(d_rope_sin_);
+  cudaFree(d_act_arena_);
+  cudaFreeHost(h_ids_);
+  cudaFreeHost(h_pos_);
+  cudaFreeHost(h_tok_);
+  if (st_) cudaStreamDestroy(st_);
+}
+
+void Engine::release_graphs() {
+  if (g_fwd1_) cudaGraphExecDestroy(g_fwd1_);
+  if (g_step_) cudaGraphExecDestroy(g_step_);
+  g_fwd1_ = g_step_ = nullptr;
+}
+
+int Engine::create(int device, int n_ctx, int max_batch) {
+  if (n_ctx <= 0 || max_batch <= 0 || max_batch > 64)
+    return set_error(PK_ERR_INVALID, "n_ctx must be > 0 and max_batch in 1..64");
+  int ndev = 0;
+  PK_CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_error(PK_ERR_INVALID, "no CUDA device " + std::to_string(device));
+  device_ = device;
+  n_ctx_ = n_ctx;
+  max_batch_ = max_batch;
+  PK_CK(cudaSetDevice(device_));
+  PK_CK(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
+  PK_CK(cudaHostAlloc((void **)&h_ids_, 64 * sizeof(uint32_t), cudaHostAllocDefault));
+  PK_CK(cudaHostAlloc((void **)&h_pos_, 64 * sizeof(int), cudaHostAllocDefault));
+  PK_CK(cudaHostAlloc((void **)&h_tok_, 4 * sizeof(uint32_t), cudaHostAllocDefault));
+  return PK_OK;
+}
+
+namespace {
+
+// Config::from_gguf (model.rs:32-97)
+int config_from_gguf(const Gguf &g, Config &c) {
+  const std::string arch = g.get_str("general.architecture");
+  const std::string p = arch.empty() ? "llama" : arch;
+  uint64_t v;
+  auto need = [&](const char *key, int *out) -> bool {
+    if (!g.get_u64(p + "." + key, &v)) return false;
+    *out = (int)v;
+    return true;
+  };
+  if (!need("block_count", &c.n_layer)) return set_error(PK_ERR_INVALID, "missing metadata " + p + ".block_count");
+  if (!need("embedding_length", &c.n_embd)) return set_error(PK_ERR_INVALID, "missing metadata " + p + ".embedding_length");
+  if (!need("feed_forward_length", &c.n_ff)) return set_error(PK_ERR_INVALID, "missing metadata " + p + ".feed_forward_length");
+  if (!need("attention.head_count", &c.n_head)) return set_error(PK_ERR_INVALID, "missing metadata " + p + ".attention.head_count");
+  if (c.n_layer == 0 || c.n_embd == 0 || c.n_ff == 0 || c.n_head == 0)
+    return set_error(PK_ERR_INVALID, "invalid model configuration: zero layer, hidden, FFN or head count");
+  c.n_head_kv = g.get_u64(p + ".attention.head_count_kv", &v) ? (int)v : c.n_head;
+  c.head_dim = g.get_u64(p + ".attention.key_length", &v) ? (int)v : c.n_embd / c.n_head;
+  if (c.head_dim == 0 || c.n_head_kv == 0 || c.n_head % c.n_head_kv != 0)
+    return set_error(PK_ERR_INVALID, "invalid GQA configuration");
+  if (g.get_u64(p + ".attention.value_length", &v) && (int)v != c.head_dim)
+    return set_error(PK_ERR_INVALID, "value head dimension differs from key dimension");
+  c.n_rot = g.get_u64(p + ".rope.dimension_count", &v) ? (int)v : c.head_dim;
+  float f;
+  c.rope_theta = g.get_f32(p + ".rope.freq_base", &f) ? f : 10000.0f;
+  c.rms_eps = g.get_f32(p + ".attention.layer_norm_rms_epsilon", &f) ? f : 1e-5f;
+  c.n_vocab = g.get_u64(p + ".vocab_size", &v) ? (int)v : 0;
+  if (c.n_rot == 0 || c.n_rot > c.head_dim || c.n_rot % 2 != 0 || !std::isfinite(c.rope_theta) || c.rope_theta <= 0.0f ||
+      !std::isfinite(c.rms_eps) || c.rms_eps <= 0.0f)
+    return set_error(PK_ERR_INVALID, "invalid RoPE / RMSNorm configuration");
+  if (c.head_dim > 256 || c.head_dim % 4 != 0)
+    return set_error(PK_ERR_UNSUPPORTED, "head_dim must be a multiple of 4 and <= 256 on the device");
+  if (c.n_embd % 32 != 0 || c.n_ff % 32 != 0)
+    return set_error(PK_ERR_UNSUPPORTED, "hidden and FFN sizes must be multiples of 32 for Q8 activations");
+  c.arch = p;
+  return PK_OK;
+}
+
+struct TRef {
+  std::string name;
+  int type = 0;
+  size_t ne0 = 0, ne1 = 0, row_bytes = 0, off = 0;
+};
+
+// Model::load find (model.rs:494-523)
+int find_tensor(const Gguf &g, const std::string &name, TRef &out) {
+  const GgufTensor *t = g.tensor(name);
+  if (!t) return set_error(PK_ERR_INVALID, "missing tensor " + name);
+  int be, bb;
+  if (!type_block((int)t->type, &be, &bb)) return set_error(PK_ERR_UNSUPPORTED, "tensor " + name + ": unsupported type");
+  if (t->type == 10 || t->type == 11)  // Q2_K / Q3_K
+    return set_error(PK_ERR_UNSUPPORTED, "tensor " + name + ": Q2_K/Q3_K are not handled");
+  if (t->ne.empty() || t->ne.size() > 2) return set_error(PK_ERR_INVALID, "tensor " + name + ": expected one or two nonzero dimensions");
+  for (auto n : t->ne)
+    if (n == 0) return set_error(PK_ERR_INVALID, "tensor " + name + ": expected one or two nonzero dimensions");
+  if (t->ne[0] % (uint64_t)be != 0) return set_error(PK_ERR_INVALID, "tensor " + name + ": dim0 not divisible by block");
+  out.name = name;
+  out.type = (int)t->type;
+  out.ne0 = (size_t)t->ne[0];
+  out.ne1 = t->ne.size() == 2 ? (size_t)t->ne[1] : 1;
+  out.row_bytes = out.ne0 / be * bb;
+  out.off = g.data_offset() + (size_t)t->offset;
+  if (out.off + out.row_bytes * out.ne1 > g.size() || out.off < g.data_offset())
+    return set_error(PK_ERR_INVALID, "tensor " + name + ": out of range");
+  return PK_OK;
+}
+
+int check_shape(const TRef &t, size_t cols, size_t rows) {  // model.rs:650-655
+  if (t.ne0 != cols || t.ne1 != rows)
+    return set_error(PK_ERR_INVALID, "tensor " + t.name + " has shape " + std::to_string(t.ne0) + "x" +
+                                         std::to_string(t.ne1) + ", expected " + std::to_string(cols) + "x" +
+                                         std::to_string(rows));
+  return PK_OK;
+}
+
+}  // namespace
+
+int Engine::load(const char *path) {
+  if (!st_) return set_error(PK_ERR_INVALID, "engine not created");
+  if (loaded_) return set_error(PK_ERR_INVALID, "engine already holds a model");
+  PK_CK(cudaSetDevice(device_));
+  Gguf g;
+  std::string err;
+  if (!g.open(path, err)) return set_error(PK_ERR_IO, err);
+  int rc = config_from_gguf(g, cfg_);
+  if (rc) return rc;
+  const Config &c = cfg_;
+  TRef embd, output, onorm;
+  if ((rc = find_tensor(g, "token_embd.weight", embd))) return rc;
+  if (g.tensor("output.weight")) {
+    if ((rc = find_tensor(g, "output.weight", output))) return rc;
+  } else {
+    output = embd;
+  }
+  if ((rc = find_tensor(g, "output_norm.weight", onorm))) return rc;
+  struct LRef { TRef q, k, v, o, an, gate, up, down, fn; };
+  std::vector<LRef> L(c.n_layer);
+  for (int i = 0; i < c.n_layer; i++) {
+    const std::string p = "blk." + std::to_string(i) + ".";
+    if ((rc = find_tensor(g, p + "attn_q.weight", L[i].q)) || (rc = find_tensor(g, p + "attn_k.weight", L[i].k)) ||
+        (rc = find_tensor(g, p + "attn_v.weight", L[i].v)) || (rc = find_tensor(g, p + "attn_output.weight", L[i].o)) ||
+        (rc = find_tensor(g, p + "attn_norm.weight", L[i].an)) || (rc = find_tensor(g, p + "ffn_gate.weight", L[i].gate)) ||
+        (rc = find_tensor(g, p + "ffn_up.weight", L[i].up)) || (rc = find_tensor(g, p + "ffn_down.weight", L[i].down)) ||
+        (rc = find_tensor(g, p + "ffn_norm.weight", L[i].fn)))
+      return rc;
+  }
+  // Model::finish (model.rs:571-601); without a tokenizer the vocabulary is
+  // the embedding's row count.
+  vocab_ = (int)embd.ne1;
+  if (embd.ne0 != (size_t)c.n_embd || (c.n_vocab != 0 && c.n_vocab != vocab_))
+    return set_error(PK_ERR_INVALID, "embedding / metadata / tokenizer vocab dimensions disagree");
+  const size_t qdim = (size_t)c.n_head * c.head_dim, kdim = (size_t)c.n_head_kv * c.head_dim;
+  if ((rc = check_shape(output, c.n_embd, vocab_)) || (rc = check_shape(onorm, c.n_embd, 1))) return rc;
+  for (auto &l : L) {
+    if ((rc = check_shape(l.an, c.n_embd, 1)) || (rc = check_shape(l.fn, c.n_embd, 1)) ||
+        (rc = check_shape(l.q, c.n_embd, qdim)) || (rc = check_shape(l.k, c.n_embd, kdim)) ||
+        (rc = check_shape(l.v, c.n_embd, kdim)) || (rc = check_shape(l.o, qdim, c.n_embd)) ||
+        (rc = check_shape(l.gate, c.n_embd, c.n_ff)) || (rc = check_shape(l.up, c.n_embd, c.n_ff)) ||
+        (rc = check_shape(l.down, c.n_ff, c.n_embd)))
+      return rc;
+    for (const TRef *t : {&l.q, &l.k, &l.v, &l.o, &l.gate, &l.up, &l.down})
+      if (!type_is_matvec(t->type))
+        return set_error(PK_ERR_UNSUPPORTED, "tensor " + t->name + ": the device matvec handles Q4_K/Q6_K/Q4_0/Q8_0");
+  }
+  if (!type_is_matvec(output.type))
+    return set_error(PK_ERR_UNSUPPORTED, "tensor " + output.name + ": the device matvec handles Q4_K/Q6_K/Q4_0/Q8_0");
+  if (qdim % 32 != 0) return set_error(PK_ERR_UNSUPPORTED, "n_head * head_dim must be a multiple of 32");
+
+  // ---- device weight arena: packed matrices | f32 norms | raw embedding
+  size_t total = 0, max_raw = 0;
+  auto mat_bytes = [&](const TRef &t) { return a256(packed_bytes(t.type, (int)t.ne0, (int)t.ne1)); };
+  stream_bytes_ = 0;
+  for (auto &l : L) {
+    for (const TRef *t : {&l.q, &l.k, &l.v, &l.o, &l.gate, &l.up, &l.down}) {
+      total += mat_bytes(*t);
+      max_raw = std::max(max_raw, t->row_bytes * t->ne1);
+      stream_bytes_ += t->row_bytes * t->ne1;
+    }
+    total += 2 * a256((size_t)c.n_embd * 4);
+    max_raw = std::max(max_raw, l.an.row_bytes);
+    stream_bytes_ += 2 * (size_t)c.n_embd * 4;
+  }
+  total += mat_bytes(output) + a256(embd.row_bytes * embd.ne1) + a256((size_t)c.n_embd * 4);
+  max_raw = std::max(max_raw, output.row_bytes * output.ne1);
+  stream_bytes_ += output.row_bytes * output.ne1 + (size_t)c.n_embd * 4 + embd.row_bytes;
+  PK_CK(cudaMalloc((void **)&d_weights_, total));
+  weight_bytes_ = total;
+  uint8_t *staging = nullptr;
+  PK_CK(cudaMalloc((void **)&staging, a256(max_raw)));
+  size_t off = 0;
+  const uint8_t *file = g.data();
+  auto upload_mat = [&](const TRef &t, DevTensor &dst) -> int {
+    uint8_t *slot = d_weights_ + off;
+    off += mat_bytes(t);
+    PK_CK(cudaMemcpy(staging, file + t.off, t.row_bytes * t.ne1, cudaMemcpyHostToDevice));
+    PK_CK(launch_pack(t.type, staging, t.row_bytes, (int)t.ne0, (int)t.ne1, slot, st_));
+    PK_CK(cudaStreamSynchronize(st_));
+    dst = packed_view(t.type, (int)t.ne0, (int)t.ne1, slot);
+    return PK_OK;
+  };
+  auto upload_norm = [&](const TRef &t, float **dst) -> int {
+    float *slot = (float *)(d_weights_ + off);
+    off += a256((size_t)c.n_embd * 4);
+    PK_CK(cudaMemcpy(staging, file + t.off, t.row_bytes, cudaMemcpyHostToDevice));
+    PK_CK(launch_dequant_rows(t.type, staging, t.row_bytes, (int)t.ne0, nullptr, 1, slot, st_));
+    PK_CK(cudaStreamSynchronize(st_));
+    *dst = slot;
+    return PK_OK;
+  };
+  layers_.resize(c.n_layer);
+  for (int i = 0; i < c.n_layer && !rc; i++) {
+    LayerDev &d = layers_[i];
+    if ((rc = upload_mat(L[i].q, d.q)) || (rc = upload_mat(L[i].k, d.k)) || (rc = upload_mat(L[i].v, d.v)) ||
+        (rc = upload_mat(L[i].o, d.o)) || (rc = upload_mat(L[i].gate, d.gate)) || (rc = upload_mat(L[i].up, d.up)) ||
+        (rc = upload_mat(L[i].down, d.down)) || (rc = upload_norm(L[i].an, &d.attn_norm)) ||
+        (rc = upload_norm(L[i].fn, &d.ffn_norm)))
+      break;
+  }
+  if (!rc) {
+    if (!(rc = upload_mat(output, output_))) rc = upload_norm(onorm, &output_norm_);
+  }
+  cudaFree(staging);
+  if (rc) return rc;
+  embd_raw_ = d_weights_ + off;
+  PK_CK(cudaMemcpy((void *)embd_raw_, file + embd.off, embd.row_bytes * embd.ne1, cudaMemcpyHostToDevice));
+  off += a256(embd.row_bytes * embd.ne1);
+  embd_type_ = embd.type;
+  embd_row_bytes_ = embd.row_bytes;
+
+  // ---- KV cache (model.rs:352-387): [layer][kv_head][n_ctx][dh] f32
+  kv_bytes_ = 2 * (size_t)c.n_layer * c.n_head_kv * n_ctx_ * c.head_dim * 4;
+  PK_CK(cudaMalloc((void **)&d_kcache_, kv_bytes_ / 2));
+  PK_CK(cudaMalloc((void **)&d_vcache_, kv_bytes_ / 2));
+  PK_CK(cudaMemset(d_kcache_, 0, kv_bytes_ / 2));
+  PK_CK(cudaMemset(d_vcache_, 0, kv_bytes_ / 2));
+
+  // ---- RoPE tables, computed exactly like Scratch::new / ensure_rope
+  // (model.rs:414-417, 452-457) with the C library's powf/cosf/sinf.
+  const int half = c.n_rot / 2;
+  std::vector<float> inv(std::max(half, 1)), tc((size_t)n_ctx_ * half), ts((size_t)n_ctx_ * half);
+  for (int i = 0; i < half; i++) inv[i] = 1.0f / powf(c.rope_theta, 2.0f * (float)i / (float)c.n_rot);
+  for (int p = 0; p < n_ctx_; p++)
+    for (int i = 0; i < half; i++) {
+      const float a = (float)p * inv[i];
+      tc[(size_t)p * half + i] = cosf(a);
+      ts[(size_t)p * half + i] = sinf(a);
+    }
+  PK_CK(cudaMalloc((void **)&d_rope_cos_, std::max<size_t>(tc.size(), 1) * 4));
+  PK_CK(cudaMalloc((void **)&d_rope_sin_, std::max<size_t>(ts.size(), 1) * 4));
+  PK_CK(cudaMemcpy(d_rope_cos_, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice));
+  PK_CK(cudaMemcpy(d_rope_sin_, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice));
+
+  // ---- activations and scratch (one arena)
+  const size_t B = max_batch_, ne = c.n_embd, ff = c.n_ff;
+  const size_t kmax = std::max(std::max(ne, ff), qdim);
+  att_nchunk_ = (n_ctx_ + ATTN_CHUNK - 1) / ATTN_CHUNK;
+  const size_t H = c.n_head, dh = c.head_dim;
+  const std::vector<size_t> sizes = {
+      B * ne * 4, B * qdim * 4, B * kdim * 4, B * kdim * 4, B * qdim * 4,  // x q k v attn
+      B * ff * 4, B * ff * 4, B * ff * 4, (size_t)vocab_ * 4,            // gate up h logits
+      B * kmax, B * (kmax / 32) * 4, B * (kmax / 32) * 4,                  // act q d s
+      B * H * n_ctx_ * 4, B * H * att_nchunk_ * 4, B * H * att_nchunk_ * 4, B * H * att_nchunk_ * dh * 4,
+      64 * 4, 64 * 4, 16, (size_t)n_ctx_ * 4 + 16, 16};                 // ids pos tok hist step
+  size_t arena = 0;
+  for (size_t s : sizes) arena += a256(s);
+  PK_CK(cudaMalloc((void **)&d_act_arena_, arena));
+  PK_CK(cudaMemset(d_act_arena_, 0, arena));
+  uint8_t *pa = d_act_arena_;
+  size_t si = 0;
+  auto take = [&]() {
+    uint8_t *r = pa;
+    pa += a256(sizes[si++]);
+    return r;
+  };
+  x_ = (float *)take(); q_ = (float *)take(); k_ = (float *)take(); v_ = (float *)take(); attn_ = (float *)take();
+  gate_ = (float *)take(); up_ = (float *)take(); h_ = (float *)take(); logits_ = (float *)take();
+  act_.q = (int8_t *)take(); act_.d = (float *)take(); act_.s = (int32_t *)take();
+  att_scores_ = (float *)take(); att_cmax_ = (float *)take(); att_csum_ = (float *)take(); att_cacc_ = (float *)take();
+  d_ids_ = (uint32_t *)take(); d_pos_ = (int *)take(); d_tok_ = (uint32_t *)take(); d_hist_ = (uint32_t *)take();
+  d_step_ = (int *)take();
+
+  // Tokenizer::from_gguf end-of-generation ids (tokenizer.rs:82-92)
+  uint64_t eos;
+  if (g.get_u64("tokenizer.ggml.eos_token_id", &eos)) eos_ids_.push_back((uint32_t)eos);
+  if (const GgufValue *tv = g.get("tokenizer.ggml.tokens"))
+    for (size_t i = 0; i < tv->arr_str.size(); i++) {
+      const std::string &s = tv->arr_str[i];
+      if (s == "<|im_end|>" || s == "<|eot|>" || s == "<|endoftext|>") eos_ids_.push_back((uint32_t)i);
+    }
+  std::sort(eos_ids_.begin(), eos_ids_.end());
+  eos_ids_.erase(std::unique(eos_ids_.begin(), eos_ids_.end()), eos_ids_.end());
+  PK_CK(cudaStreamSynchronize(st_));
+  loaded_ = true;
+  return PK_OK;
+}
+
+int Engine::info(pk_model_info *o) const {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  o->n_layer = cfg_.n_layer; o->n_embd = cfg_.n_embd; o->n_ff = cfg_.n_ff; o->n_head = cfg_.n_head;
+  o->n_head_kv = cfg_.n_head_kv; o->head_dim = cfg_.head_dim; o->n_rot = cfg_.n_rot; o->n_vocab = vocab_;
+  o->n_ctx = n_ctx_; o->rope_theta = cfg_.rope_theta; o->rms_eps = cfg_.rms_eps;
+  o->weight_bytes = weight_bytes_; o->kv_bytes = kv_bytes_; o->stream_bytes = stream_bytes_;
+  return PK_OK;
+}
+
+void Engine::dump(const char *name, const float *dev, size_t n) {
+  if (!dbg_on_) return;
+  std::vector<float> h(n);
+  cudaStreamSynchronize(st_);
+  cudaMemcpy(h.data(), dev, n * 4, cudaMemcpyDeviceToHost);
+  dbg_.emplace_back(name, std::move(h));
+}
+
+int Engine::prof_begin(const char *name, double bytes) {
+  if (!prof_) return PK_OK;
+  ProfMark m{name, bytes, nullptr, nullptr};
+  PK_CK(cudaEventCreate(&m.start));
+  PK_CK(cudaEventCreate(&m.stop));
+  PK_CK(cudaEventRecord(m.start, st_));
+  prof_->push_back(m);
+  return PK_OK;
+}
+
+int Engine::prof_end() {
+  if (!prof_) return PK_OK;
+  PK_CK(cudaEventRecord(prof_->back().stop, st_));
+  return PK_OK;
+}
+
+// Bytes of a matrix in the GGUF block layout (the algorithmic weight stream).
+static double mat_stream_bytes(const DevTensor &w) {
+  int be = 1, bb = 1;
+  type_block(w.type, &be, &bb);
+  return (double)w.rows * (double)(w.k / be) * (double)bb;
+}
+
+#define PROF(name, bytes, launch)                 \
+  do {                                            \
+    int _rc = prof_begin(name, (double)(bytes));  \
+    if (_rc) return _rc;                          \
+    PK_CK(launch);                                \
+    if ((_rc = prof_end())) return _rc;           \
+  } while (0)
+
+// The per-token kernel sequence (model.rs:857-1170).  Reads ids/positions
+// from d_ids_/d_pos_ so a b == 1 pass can be captured once as a CUDA graph.
+int Engine::enqueue_forward(int b, bool want_logits, bool cancellable) {
+  const Config &c = cfg_;
+  const int ne = c.n_embd, dh = c.head_dim, qdim = c.n_head * dh, kdim = c.n_head_kv * dh, ff = c.n_ff;
+  const size_t layer_kv = (size_t)c.n_head_kv * n_ctx_ * dh;
+  const double f4 = 4.0, kv_pos = (double)next_pos_ + 1.0;  // positions attended in a profiled decode step
+  PROF("k_dequant_rows", embd_row_bytes_ + ne * f4,
+       launch_dequant_rows(embd_type_, embd_raw_, embd_row_bytes_, ne, d_ids_, b, x_, st_));
+  dump("embd", x_, (size_t)b * ne);
+  AttnArgs at{};
+  at.q = q_; at.pos = d_pos_; at.out = attn_; at.b = b; at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh;
+  at.n_ctx = n_ctx_; at.scale = 1.0f / sqrtf((float)dh);
+  at.scores = att_scores_; at.cmax = att_cmax_; at.csum = att_csum_; at.cacc = att_cacc_; at.n_chunk = att_nchunk_;
+  for (int l = 0; l < c.n_layer; l++) {
+    if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
+    const LayerDev &L = layers_[l];
+    float *kc = d_kcache_ + l * layer_kv, *vc = d_vcache_ + l * layer_kv;
+    at.kcache = kc; at.vcache = vc;
+    if (b == 1) {
+      QkvArgs qa;
+      qa.wq = L.q; qa.wk = L.k; qa.wv = L.v;
+      qa.src.x = x_; qa.src.nw = L.attn_norm; qa.src.eps = c.rms_eps;
+      qa.pos = d_pos_; qa.rope_cos = d_rope_cos_; qa.rope_sin = d_rope_sin_;
+      qa.half = c.n_rot / 2; qa.dh = dh; qa.n_ctx = n_ctx_;
+      qa.qout = q_; qa.kcache = kc; qa.vcache = vc;
+      PROF("k_qkv_b1", mat_stream_bytes(L.q) + mat_stream_bytes(L.k) + mat_stream_bytes(L.v) + 2 * ne * f4 +
+                           (qdim + 2 * kdim) * f4,
+           launch_qkv_b1(qa, st_));
+      if (l == 0) dump("Qrope-0", q_, (size_t)qdim);
+      PROF("attention(3 kernels)", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, st_));
+      B1Src so;
+      so.x = attn_;
+      PROF("k_mv_b1", mat_stream_bytes(L.o) + qdim * f4 + 2 * ne * f4, launch_mv_b1(L.o, so, x_, true, st_));
+      if (l == 0) dump("ffn_inp-0", x_, (size_t)ne);
+      B1Src sf;
+      sf.x = x_; sf.nw = L.ffn_norm; sf.eps = c.rms_eps;
+      PROF("k_gateup_b1", mat_stream_bytes(L.gate) + mat_stream_bytes(L.up) + 2 * ne * f4 + ff * f4,
+           launch_gateup_b1(L.gate, L.up, sf, h_, st_));
+      B1Src sd;
+      sd.x = h_;
+      PROF("k_mv_b1", mat_stream_bytes(L.down) + ff * f4 + 2 * ne * f4, launch_mv_b1(L.down, sd, x_, true, st_));
+    } else {
+      Q8Dev a = act_;
+      a.k = ne; a.b = b;
+      PK_CK(launch_rmsnorm_q8(x_, L.attn_norm, c.rms_eps, ne, b, a, nullptr, st_));
+      PK_CK(launch_mv_lanes(L.q, a, q_, 1, qdim, false, st_));
+      PK_CK(launch_mv_lanes(L.k, a, k_, 1, kdim, false, st_));
+      PK_CK(launch_mv_lanes(L.v, a, v_, 1, kdim, false, st_));
+      if (l == 0) { dump("Qcur-0", q_, (size_t)b * qdim); dump("Kcur-0", k_, (size_t)b * kdim); dump("Vcur-0", v_, (size_t)b * kdim); }
+      PK_CK(launch_rope_kv(q_, k_, v_, b, d_pos_, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
+                           n_ctx_, kc, vc, st_));
+      if (l == 0) dump("Qrope-0", q_, (size_t)b * qdim);
+      PK_CK(launch_attention(at, st_));
+      a.k = qdim;
+      PK_CK(launch_q8(attn_, 1, qdim, qdim, b, a, st_));
+      PK_CK(launch_mv_lanes(L.o, a, x_, 1, ne, true, st_));
+      if (l == 0) dump("ffn_inp-0", x_, (size_t)b * ne);
+      a.k = ne;
+      PK_CK(launch_rmsnorm_q8(x_, L.ffn_norm, c.rms_eps, ne, b, a, nullptr, st_));
+      PK_CK(launch_mv_lanes(L.gate, a, gate_, 1, ff, false, st_));
+      PK_CK(launch_mv_lanes(L.up, a, up_, 1, ff, false, st_));
+      PK_CK(launch_swiglu(gate_, up_, h_, (long)b * ff, st_));
+      a.k = ff;
+      PK_CK(launch_q8(h_, 1, ff, ff, b, a, st_));
+      PK_CK(launch_mv_lanes(L.down, a, x_, 1, ne, true, st_));
+    }
+    if (l == 0) {
+      dump("kqv_out-0", attn_, (size_t)b * qdim);
+      dump("ffn_swiglu-0", h_, (size_t)b * ff);
+      dump("l_out-0", x_, (size_t)b * ne);
+    }
+  }
+  if (want_logits) {
+    if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
+    B1Src sh;
+    sh.x = x_ + (size_t)(b - 1) * ne; sh.nw = output_norm_; sh.eps = c.rms_eps;
+    PROF("k_mv_b1", mat_stream_bytes(output_) + 2 * ne * f4 + (double)vocab_ * f4,
+         launch_mv_b1(output_, sh, logits_, false, st_));
+    dump("result_output", logits_, (size_t)vocab_);
+  }
+  return PK_OK;
+}
+
+int Engine::ensure_graphs() {
+  if (g_fwd1_ && g_step_) return PK_OK;
+  release_graphs();
+  for (int which = 0; which < 2; which++) {
+    cudaGraph_t graph = nullptr;
+    PK_CK(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
+    int rc = PK_OK;
+    cudaError_t e = cudaSuccess;
+    if (which == 1) {
+      e = launch_argmax(logits_, vocab_, d_tok_, st_);
+      if (e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
+    }
+    if (e == cudaSuccess) rc = enqueue_forward(1, true, false);
+    cudaError_t ee = cudaStreamEndCapture(st_, &graph);
+    if (e != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return cuda_error(e, "decode graph capture");
+    }
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ee != cudaSuccess) return cuda_error(ee, "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGraphInstantiate");
+    (which == 0 ? g_fwd1_ : g_step_) = exec;
+  }
+  return PK_OK;
+}
+
+// forward_inner (model.rs:833-902)
+int Engine::forward_inner(const uint32_t *ids, const int *pos, int b, bool want_logits, bool cancellable) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (b <= 0 || b > max_batch_) return set_error(PK_ERR_INVALID, "invalid batch " + std::to_string(b));
+  for (int i = 0; i < b; i++) {
+    if (pos[i] < 0 || pos[i] >= n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+    if (ids[i] >= (uint32_t)vocab_) return set_error(PK_ERR_INVALID, "token " + std::to_string(ids[i]) + " out of vocab");
+  }
+  PK_CK(cudaSetDevice(device_));
+  std::memcpy(h_ids_, ids, b * sizeof(uint32_t));
+  std::memcpy(h_pos_, pos, b * sizeof(int));
+  PK_CK(cudaMemcpyAsync(d_ids_, h_ids_, b * sizeof(uint32_t), cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(d_pos_, h_pos_, b * sizeof(int), cudaMemcpyHostToDevice, st_));
+  have_logits_ = false;
+  if (b == 1 && want_logits && !dbg_on_) {
+    int rc = ensure_graphs();
+    if (rc) return rc;
+    PK_CK(cudaGraphLaunch(g_fwd1_, st_));
+  } else {
+    int rc = enqueue_forward(b, want_logits, cancellable);
+    if (rc) {
+      cudaStreamSynchronize(st_);
+      return rc;
+    }
+  }
+  PK_CK(cudaStreamSynchronize(st_));
+  PK_CK(cudaGetLastError());
+  next_pos_ = pos[b - 1] + 1;
+  have_logits_ = want_logits;
+  return PK_OK;
+}
+
+int Engine::forward(const uint32_t *ids, const int *pos, int n, bool want_logits) {  // model.rs:825-831
+  kv_tokens_.clear();
+  cached_prefill_len_ = 0;
+  dbg_.clear();
+  return forward_inner(ids, pos, n, want_logits, false);
+}
+
+int Engine::logits(float *out, int n) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  const int m = std::min(n, vocab_);
+  PK_CK(cudaMemcpyAsync(out, logits_, (size_t)m * 4, cudaMemcpyDeviceToHost, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  return PK_OK;
+}
+
+int Engine::argmax(uint32_t *tok) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  PK_CK(launch_argmax(logits_, vocab_, d_tok_, st_));
+  PK_CK(cudaMemcpyAsync(h_tok_, d_tok_, 4, cudaMemcpyDeviceToHost, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  *tok = h_tok_[0];
+  return PK_OK;
+}
+
+// Engine::generate (model.rs:1235-1352).  The device engine is this
+// process's only engine, so prefix reuse follows the reference's CPU rules
+// (cpu_only == true): full 32-token prefill chunks of an exactly matching
+// prefix are reused, decode tokens never are.
+int Engine::generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_token_cb cb, void *user,
+                     uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats) {
+  pk_gen_stats s;
+  std::memset(&s, 0, sizeof(s));
+  std::snprintf(s.stop, sizeof(s.stop), "max_tokens");
+  int nout = 0;
+  auto finish = [&](int rc) {
+    if (stats) *stats = s;
+    if (n_out) *n_out = nout;
+    return rc;
+  };
+  if (!loaded_) return finish(set_error(PK_ERR_INVALID, "no model loaded"));
+  if (n <= 0) return finish(set_error(PK_ERR_INVALID, "empty prompt"));
+  if (opts.temp > 0.0f)
+    return finish(set_error(PK_ERR_UNSUPPORTED, "temperature sampling is not implemented on the device; use temp <= 0"));
+  const auto t0 = std::chrono::steady_clock::now();
+  const int chunk = std::min(max_batch_, 32);
+  size_t common = 0;
+  while (common < kv_tokens_.size() && common < (size_t)n && kv_tokens_[common] == prompt[common]) common++;
+  const size_t reused = std::min(std::min(common, cached_prefill_len_), (size_t)n - 1) / chunk * chunk;
+  if (kv_tokens_.size() > reused) kv_tokens_.resize(reused);
+  cached_prefill_len_ = 0;
+  s.prefill_cached_tokens = (int)reused;
+  int off = (int)reused;
+  bool user_stop = false;
+  std::vector<int> positions(chunk);
+  while (off < n) {
+    if (g_stop.load()) { user_stop = true; break; }
+    const int m = std::min(chunk, n - off);
+    for (int i = 0; i < m; i++) positions[i] = off + i;
+    const bool last = off + m >= n;
+    const int rc = forward_inner(prompt + off, positions.data(), m, last, true);
+    if (rc) {
+      kv_tokens_.clear();
+      if (g_stop.load()) { user_stop = true; break; }
+      return finish(rc);
+    }
+    kv_tokens_.insert(kv_tokens_.end(), prompt + off, prompt + off + m);
+    off += m;
+  }
+  s.prefill_tokens = off - (int)reused;
+  s.prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  if (user_stop) {
+    std::snprintf(s.stop, sizeof(s.stop), "user_stop");
+    kv_tokens_.clear();
+    return finish(PK_OK);
+  }
+  cached_prefill_len_ = n;
+  int pos = n;
+  const auto g0 = std::chrono::steady_clock::now();
+  for (int i = 0; i < opts.max_tokens; i++) {
+    if (g_stop.load()) { std::snprintf(s.stop, sizeof(s.stop), "user_stop"); break; }
+    uint32_t tok = 0;
+    int rc = argmax(&tok);
+    if (rc) return finish(rc);
+    if (opts.stop_at_eog && std::binary_search(eos_ids_.begin(), eos_ids_.end(), tok)) {
+      std::snprintf(s.stop, sizeof(s.stop), "eog");
+      break;
+    }
+    s.gen_tokens++;
+    if (nout < out_cap && out_ids) out_ids[nout] = tok;
+    nout++;
+    if (cb && !cb(tok, user)) {
+      std::snprintf(s.stop, sizeof(s.stop), "callback_error");
+      kv_tokens_.clear();
+      cached_prefill_len_ = 0;
+      break;
+    }
+    if (i + 1 == opts.max_tokens) break;
+    if (pos >= n_ctx_) { std::snprintf(s.stop, sizeof(s.stop), "context_full"); break; }
+    rc = forward_inner(&tok, &pos, 1, true, true);
+    if (rc) {
+      kv_tokens_.clear();
+      cached_prefill_len_ = 0;
+      if (g_stop.load()) { std::snprintf(s.stop, sizeof(s.stop), "user_stop"); break; }
+      return finish(rc);
+    }
+    kv_tokens_.push_back(tok);
+    pos++;
+  }
+  if (std::strcmp(s.stop, "user_stop") == 0) {
+    kv_tokens_.clear();
+    cached_prefill_len_ = 0;
+  }
+  s.gen_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - g0).count();
+  return finish(PK_OK);
+}
+
+// n_steps greedy steps with the token fed back on the device: per step one
+// graph launch (argmax -> advance -> b=1 forward), no host round trip.
+int Engine::decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (!have_logits_) return set_error(PK_ERR_INVALID, "no logits: run a forward pass with want_logits first");
+  if (device_ms) *device_ms = 0.0f;
+  if (n_steps <= 0) return PK_OK;
+  if (next_pos_ + n_steps > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+  int rc = ensure_graphs();
+  if (rc) return rc;
+  h_pos_[0] = next_pos_ - 1;
+  PK_CK(cudaMemcpyAsync(d_pos_, h_pos_, sizeof(int), cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemsetAsync(d_step_, 0, sizeof(int), st_));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  PK_CK(cudaEventCreate(&e0));
+  PK_CK(cudaEventCreate(&e1));
+  cudaError_t e = cudaEventRecord(e0, st_);
+  for (int i = 0; i < n_steps && e == cudaSuccess; i++) e = cudaGraphLaunch(g_step_, st_);
+  if (e == cudaSuccess) e = cudaEventRecord(e1, st_);
+  std::vector<uint32_t> hist(n_steps);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(hist.data(), d_hist_, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, st_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st_);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (e != cudaSuccess) return cuda_error(e, "decode_steps_device");
+  if (device_ms) *device_ms = ms;
+  if (out_ids) std::memcpy(out_ids, hist.data(), (size_t)n_steps * 4);
+  kv_tokens_.insert(kv_tokens_.end(), hist.begin(), hist.end());
+  next_pos_ += n_steps;
+  return PK_OK;
+}
+
+int Engine::set_position(int pos) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (pos <= 0 || pos > next_pos_) return set_error(PK_ERR_INVALID, "position must be in 1..current length");
+  next_pos_ = pos;
+  if (kv_tokens_.size() > (size_t)pos) kv_tokens_.resize(pos);
+  cached_prefill_len_ = std::min(cached_prefill_len_, (size_t)pos);
+  return PK_OK;
+}
+
+int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (!have_logits_) return set_error(PK_ERR_INVALID, "no logits: run a forward pass with want_logits first");
+  if (next_pos_ + 1 > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+  std::vector<ProfMark> marks;
+  prof_ = &marks;
+  h_pos_[0] = next_pos_ - 1;
+  int rc = PK_OK;
+  cudaError_t e = cudaMemcpyAsync(d_pos_, h_pos_, sizeof(int), cudaMemcpyHostToDevice, st_);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_step_, 0, sizeof(int), st_);
+  if (e == cudaSuccess) {
+    rc = prof_begin("k_argmax", (double)vocab_ * 4.0);
+    if (!rc) e = launch_argmax(logits_, vocab_, d_tok_, st_);
+    if (!rc && e == cudaSuccess) rc = prof_end();
+    if (!rc && e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
+    if (!rc && e == cudaSuccess) rc = enqueue_forward(1, true, false);
+  }
+  prof_ = nullptr;
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st_);
+  std::vector<pk_kernel_stat> agg;
+  for (auto &m : marks) {
+    float ms = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, m.start, m.stop);
+    cudaEventDestroy(m.start);
+    cudaEventDestroy(m.stop);
+    pk_kernel_stat *s = nullptr;
+    for (auto &a : agg)
+      if (m.name == a.name) s = &a;
+    if (!s) {
+      agg.push_back(pk_kernel_stat{});
+      s = &agg.back();
+      std::snprintf(s->name, sizeof(s->name), "%s", m.name.c_str());
+    }
+    s->launches++;
+    s->ms += ms;
+    s->bytes += m.bytes;
+  }
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_error(e, "decode_profile");
+  uint32_t tok = 0;
+  PK_CK(cudaMemcpy(&tok, d_tok_, 4, cudaMemcpyDeviceToHost));
+  kv_tokens_.push_back(tok);
+  next_pos_ += 1;
+  for (int i = 0; i < (int)agg.size() && i < cap; i++) out[i] = agg[i];
+  if (n_out) *n_out = (int)agg.size();
+  return PK_OK;
+}
+
+int Engine::set_debug(bool on) {
+  dbg_on_ = on;
+  dbg_.clear();
+  return PK_OK;
+}
+
+int Engine::get_dump(const char *name, float *out, int cap, int *n_out) {
+  for (auto &d : dbg_)
+    if (d.first == name) {
+      const int n = (int)d.second.size();
+      if (out) std::memcpy(out, d.second.data(), (size_t)std::min(cap, n) * 4);
+      if (n_out) *n_out = n;
+      return PK_OK;
+    }
+  if (n_out) *n_out = 0;
+  return set_error(PK_ERR_INVALID, std::string("no dump named ") + name);
+}
+
+}  // namespace pk

@@ -1,0 +1,109 @@
+// pk_engine.h -- the device engine behind pk_create / pk_load_gguf / pk_generate.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <string>
+#include <vector>
+
+#include "pk.h"
+#include "pk_gguf.h"
+#include "pk_kernels.h"
+
+namespace pk {
+
+int set_error(int code, const std::string &msg);
+int cuda_error(cudaError_t e, const char *what);
+extern std::atomic<bool> g_stop;
+
+// model.rs:14-97 Config.
+struct Config {
+  std::string arch;
+  int n_layer = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, head_dim = 0, n_rot = 0, n_vocab = 0;
+  float rope_theta = 10000.0f, rms_eps = 1e-5f;
+};
+
+struct LayerDev {
+  DevTensor q, k, v, o, gate, up, down;
+  float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+class Engine {
+ public:
+  ~Engine();
+  int create(int device, int n_ctx, int max_batch);
+  int load(const char *path);
+  int info(pk_model_info *out) const;
+
+  int forward(const uint32_t *ids, const int *pos, int n, bool want_logits);
+  int logits(float *out, int n);
+  int argmax(uint32_t *tok);
+  int generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_token_cb cb, void *user,
+               uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats);
+  int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
+  int set_position(int pos);
+  int decode_profile(pk_kernel_stat *out, int cap, int *n_out);
+  int set_debug(bool on);
+  int get_dump(const char *name, float *out, int cap, int *n_out);
+
+ private:
+  int forward_inner(const uint32_t *ids, const int *pos, int b, bool want_logits, bool cancellable);
+  int enqueue_forward(int b, bool want_logits, bool cancellable);
+  int ensure_graphs();
+  void release_graphs();
+  void dump(const char *name, const float *dev, size_t n);
+
+  int device_ = 0, n_ctx_ = 0, max_batch_ = 0;
+  bool loaded_ = false;
+  cudaStream_t st_ = nullptr;
+  Config cfg_;
+  std::vector<LayerDev> layers_;
+  DevTensor output_;
+  float *output_norm_ = nullptr;
+  const uint8_t *embd_raw_ = nullptr;
+  int embd_type_ = 0;
+  size_t embd_row_bytes_ = 0;
+  int vocab_ = 0;
+  std::vector<uint32_t> eos_ids_;
+  size_t weight_bytes_ = 0, stream_bytes_ = 0, kv_bytes_ = 0;
+
+  // device allocations
+  uint8_t *d_weights_ = nullptr;
+  float *d_kcache_ = nullptr, *d_vcache_ = nullptr;
+  float *d_rope_cos_ = nullptr, *d_rope_sin_ = nullptr;
+  uint8_t *d_act_arena_ = nullptr;
+  float *x_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *attn_ = nullptr;
+  float *gate_ = nullptr, *up_ = nullptr, *h_ = nullptr, *logits_ = nullptr;
+  Q8Dev act_;
+  float *att_scores_ = nullptr, *att_cmax_ = nullptr, *att_csum_ = nullptr, *att_cacc_ = nullptr;
+  int att_nchunk_ = 0;
+  uint32_t *d_ids_ = nullptr, *d_tok_ = nullptr, *d_hist_ = nullptr;
+  int *d_pos_ = nullptr, *d_step_ = nullptr;
+  // pinned host staging
+  uint32_t *h_ids_ = nullptr, *h_tok_ = nullptr;
+  int *h_pos_ = nullptr;
+
+  // decode graphs: fwd1 = one b=1 forward with logits; step = argmax + advance + fwd1
+  cudaGraphExec_t g_fwd1_ = nullptr, g_step_ = nullptr;
+
+  // Engine::generate prefix-reuse state (model.rs:689-694)
+  std::vector<uint32_t> kv_tokens_;
+  size_t cached_prefill_len_ = 0;
+  int next_pos_ = 0;
+  bool have_logits_ = false;
+
+  bool dbg_on_ = false;
+  std::vector<std::pair<std::string, std::vector<float>>> dbg_;
+
+  // decode_profile: events around each launch of an eager b == 1 step
+  struct ProfMark {
+    std::string name;
+    double bytes;
+    cudaEvent_t start, stop;
+  };
+  std::vector<ProfMark> *prof_ = nullptr;
+  int prof_begin(const char *name, double bytes);
+  int prof_end();
+};
+
+}  // namespace pk

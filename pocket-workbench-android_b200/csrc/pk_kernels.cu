@@ -1,0 +1,965 @@
+// pk_kernels.cu -- sm_100a kernels for pocketinfer's decode and prefill path.
+//
+// Reference semantics (Aleinto97/pocket-workbench-android, rust/pocketinfer/src):
+//   Q8 activation quantiser       quant_int.rs:17-56
+//   int8 k-quant row dots         quant_int.rs:282-419 (lanes::*)
+//   dequant (embedding, norms)    quant.rs:102-359
+//   rmsnorm / rope / attention / swiglu / residual   model.rs:777-823, 905-1172
+//   greedy sampler                sampler.rs:21-36
+//
+// Exactness.  A row of a k-quant matvec is, in the reference, a sequential
+// float sum over per-sub-block terms such as
+//     acc += d*da*sc*dot - da*dmin*m*sa          (Q4_K, quant_int.rs:364)
+// The kernels below compute every integer dot with dp4a (exact), turn it into
+// the same float term with separately rounded multiplies/subtracts (exact),
+// park the terms in shared memory, and let one thread per row add them in
+// the reference's order.  The matvec output is therefore bit-identical to the
+// reference for identical Q8 inputs, not merely within tolerance.
+#include <float.h>
+#include <limits.h>
+#include <math.h>
+
+#include <algorithm>
+
+#include "pk_device.cuh"
+#include "pk_kernels.h"
+
+namespace pk {
+
+// ------------------------------------------------------------ type table
+bool type_block(int t, int *be, int *bb) {  // quant.rs:19-37
+  int e, b;
+  switch (t) {
+    case T_F32: e = 1; b = 4; break;
+    case T_F16: case T_BF16: e = 1; b = 2; break;
+    case T_Q4_0: e = 32; b = 18; break;
+    case T_Q4_1: e = 32; b = 20; break;
+    case T_Q5_0: e = 32; b = 22; break;
+    case T_Q5_1: e = 32; b = 24; break;
+    case T_Q8_0: e = 32; b = 34; break;
+    case T_Q8_1: e = 32; b = 36; break;
+    case T_Q2_K: e = 256; b = 84; break;
+    case T_Q3_K: e = 256; b = 110; break;
+    case T_Q4_K: e = 256; b = 144; break;
+    case T_Q5_K: e = 256; b = 176; break;
+    case T_Q6_K: e = 256; b = 210; break;
+    case T_Q8_K: e = 256; b = 292; break;
+    default: return false;
+  }
+  if (be) *be = e;
+  if (bb) *bb = b;
+  return true;
+}
+
+bool type_is_matvec(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q4_0 || t == T_Q8_0; }
+
+static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t packed_q_bytes(int t, int k, int rows) {
+  switch (t) {
+    case T_Q4_K: return (size_t)rows * (size_t)(k / 256) * 144;
+    case T_Q6_K: return (size_t)rows * (size_t)(k / 256) * 208;
+    case T_Q8_0: return (size_t)rows * (size_t)k;
+    case T_Q4_0: return (size_t)rows * (size_t)(k / 2);
+  }
+  return 0;
+}
+
+static size_t packed_d_bytes(int t, int k, int rows) {
+  switch (t) {
+    case T_Q6_K: return (size_t)rows * (size_t)(k / 256) * 2;
+    case T_Q8_0: case T_Q4_0: return (size_t)rows * (size_t)(k / 32) * 2;
+  }
+  return 0;
+}
+
+size_t packed_bytes(int t, int k, int rows) {
+  return align256(packed_q_bytes(t, k, rows)) + align256(packed_d_bytes(t, k, rows));
+}
+
+DevTensor packed_view(int t, int k, int rows, const void *packed) {
+  DevTensor w;
+  w.type = t;
+  w.k = k;
+  w.rows = rows;
+  w.q = (const uint8_t *)packed;
+  w.d = packed_d_bytes(t, k, rows) ? (const uint16_t *)((const uint8_t *)packed + align256(packed_q_bytes(t, k, rows)))
+                                    : nullptr;
+  return w;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n = v > 0 ? v : 148;
+  }
+  return n;
+}
+
+// ------------------------------------------------------------ packing
+__global__ void k_pack(int t, const uint8_t *__restrict__ raw, size_t row_bytes, int k, int rows,
+                       uint8_t *__restrict__ q, uint16_t *__restrict__ d) {
+  const int be = (t == T_Q4_K || t == T_Q6_K) ? 256 : 32;
+  const int nblk = k / be;
+  const long n = (long)rows * nblk;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / nblk;
+    const int b = (int)(i - r * nblk);
+    switch (t) {
+      case T_Q4_K: {
+        const uint8_t *s = raw + r * row_bytes + (size_t)b * 144;
+        uint8_t *o = q + i * 144;
+        for (int j = 0; j < 144; j++) o[j] = s[j];
+      } break;
+      case T_Q6_K: {
+        const uint8_t *s = raw + r * row_bytes + (size_t)b * 210;
+        uint8_t *o = q + i * 208;
+        for (int j = 0; j < 208; j++) o[j] = s[j];
+        d[i] = (uint16_t)(s[208] | (s[209] << 8));
+      } break;
+      case T_Q8_0: {
+        const uint8_t *s = raw + r * row_bytes + (size_t)b * 34;
+        uint8_t *o = q + r * (long)k + (long)b * 32;
+        for (int j = 0; j < 32; j++) o[j] = s[2 + j];
+        d[i] = (uint16_t)(s[0] | (s[1] << 8));
+      } break;
+      case T_Q4_0: {
+        const uint8_t *s = raw + r * row_bytes + (size_t)b * 18;
+        uint8_t *o = q + r * (long)(k / 2) + (long)b * 16;
+        for (int j = 0; j < 16; j++) o[j] = s[2 + j];
+        d[i] = (uint16_t)(s[0] | (s[1] << 8));
+      } break;
+    }
+  }
+}
+
+cudaError_t launch_pack(int t, const void *raw, size_t row_bytes, int k, int rows, void *packed, cudaStream_t st) {
+  if (!type_is_matvec(t)) return cudaErrorInvalidValue;
+  DevTensor w = packed_view(t, k, rows, packed);
+  int be = (t == T_Q4_K || t == T_Q6_K) ? 256 : 32;
+  long n = (long)rows * (k / be);
+  int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 16);
+  if (grid < 1) grid = 1;
+  k_pack<<<grid, 256, 0, st>>>(t, (const uint8_t *)raw, row_bytes, k, rows, (uint8_t *)w.q, (uint16_t *)w.d);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ dequant rows
+__device__ __forceinline__ uint16_t ld16u(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// One element of quant.rs:102-359 dequant_row, same expression per element.
+__device__ float dequant_elem(int t, const uint8_t *row, int j) {
+  switch (t) {
+    case T_F32: {
+      uint32_t b = (uint32_t)row[4 * j] | ((uint32_t)row[4 * j + 1] << 8) | ((uint32_t)row[4 * j + 2] << 16) |
+                   ((uint32_t)row[4 * j + 3] << 24);
+      return __uint_as_float(b);
+    }
+    case T_F16: return f16f(ld16u(row + 2 * j));
+    case T_BF16: return __uint_as_float((uint32_t)ld16u(row + 2 * j) << 16);
+    case T_Q4_0: {
+      const uint8_t *b = row + (j / 32) * 18;
+      int jj = j % 32;
+      uint8_t v = b[2 + (jj & 15)];
+      int nib = jj < 16 ? (v & 0xF) : (v >> 4);
+      return fmul(fsub((float)nib, 8.0f), f16f(ld16u(b)));
+    }
+    case T_Q4_1: {
+      const uint8_t *b = row + (j / 32) * 20;
+      int jj = j % 32;
+      uint8_t v = b[4 + (jj & 15)];
+      int nib = jj < 16 ? (v & 0xF) : (v >> 4);
+      return fadd(fmul((float)nib, f16f(ld16u(b))), f16f(ld16u(b + 2)));
+    }
+    case T_Q5_0: case T_Q5_1: {
+      const int bb = t == T_Q5_0 ? 22 : 24, qo = t == T_Q5_0 ? 2 : 4;
+      const uint8_t *b = row + (j / 32) * bb;
+      int jj = j % 32;
+      uint32_t qh = (uint32_t)b[qo] | ((uint32_t)b[qo + 1] << 8) | ((uint32_t)b[qo + 2] << 16) |
+                    ((uint32_t)b[qo + 3] << 24);
+      uint32_t q;
+      if (jj < 16) q = (uint32_t)(b[qo + 4 + jj] & 0xF) | (((qh >> jj) << 4) & 0x10u);
+      else q = (uint32_t)(b[qo + 4 + jj - 16] >> 4) | ((qh >> (jj - 16 + 12)) & 0x10u);
+      float d = f16f(ld16u(b));
+      if (t == T_Q5_0) return fmul(fsub((float)q, 16.0f), d);
+      return fadd(fmul((float)q, d), f16f(ld16u(b + 2)));
+    }
+    case T_Q8_0: {
+      const uint8_t *b = row + (j / 32) * 34;
+      return fmul((float)(int8_t)b[2 + (j % 32)], f16f(ld16u(b)));
+    }
+    case T_Q4_K: case T_Q5_K: {
+      const int bb = t == T_Q4_K ? 144 : 176;
+      const uint8_t *b = row + (j / 256) * bb;
+      int jj = j % 256, n64 = jj / 64, w = jj % 64, l = w % 32;
+      int is = 2 * n64 + (w >= 32 ? 1 : 0);
+      const uint8_t *scales = b + 4;
+      int sc, m;
+      if (is < 4) { sc = scales[is] & 63; m = scales[is + 4] & 63; }
+      else { sc = (scales[is + 4] & 0xF) | ((scales[is - 4] >> 6) << 4); m = (scales[is + 4] >> 4) | ((scales[is] >> 6) << 4); }
+      float d = f16f(ld16u(b)), dmin = f16f(ld16u(b + 2));
+      int q;
+      if (t == T_Q4_K) {
+        uint8_t v = b[16 + n64 * 32 + l];
+        q = w < 32 ? (v & 0xF) : (v >> 4);
+      } else {
+        const uint8_t *qh = b + 16, *ql = b + 48;
+        uint8_t v = ql[n64 * 32 + l];
+        uint8_t u = (uint8_t)((w < 32 ? 1 : 2) << (2 * n64));
+        q = (w < 32 ? (v & 0xF) : (v >> 4)) + ((qh[n64 * 32 + l] & u) ? 16 : 0);
+      }
+      return fsub(fmul(fmul(d, (float)sc), (float)q), fmul(dmin, (float)m));
+    }
+    case T_Q6_K: {
+      const uint8_t *b = row + (j / 256) * 210;
+      int jj = j % 256, half = jj / 128, w = jj % 128, quarter = w / 32, l = w % 32, is = l / 16;
+      const uint8_t *ql = b + half * 64, *qh = b + 128 + half * 32, *sc = b + 192 + half * 8;
+      int lo = (quarter & 1) ? ql[l + 32] : ql[l];
+      lo = (quarter & 2) ? (lo >> 4) : (lo & 0xF);
+      int q = (lo | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
+      float d = f16f(ld16u(b + 208));
+      return fmul(fmul(d, (float)(int8_t)sc[is + 2 * quarter]), (float)q);
+    }
+    case T_Q8_K: {
+      const uint8_t *b = row + (j / 256) * 292;
+      uint32_t db = (uint32_t)b[0] | ((uint32_t)b[1] << 8) | ((uint32_t)b[2] << 16) | ((uint32_t)b[3] << 24);
+      return fmul((float)(int8_t)b[4 + (j % 256)], __uint_as_float(db));
+    }
+  }
+  return 0.0f;
+}
+
+__global__ void k_dequant_rows(int t, const uint8_t *__restrict__ raw, size_t row_bytes, int k,
+                               const uint32_t *__restrict__ ids, float *__restrict__ out) {
+  const long r = ids ? (long)ids[blockIdx.x] : (long)blockIdx.x;
+  const uint8_t *row = raw + r * row_bytes;
+  for (int j = threadIdx.x; j < k; j += blockDim.x) out[(long)blockIdx.x * k + j] = dequant_elem(t, row, j);
+}
+
+cudaError_t launch_dequant_rows(int t, const void *raw, size_t row_bytes, int k, const uint32_t *ids, int n,
+                                float *out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_dequant_rows<<<n, 256, 0, st>>>(t, (const uint8_t *)raw, row_bytes, k, ids, out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ reductions
+// Deterministic block sum: per-warp trees, then warp partials in warp order.
+__device__ float block_sum(float v, float *red) {
+  v = warp_sum_f(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < nw; i++) s = fadd(s, red[i]);
+    red[32] = s;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ float block_max(float v, float *red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int i = 0; i < nw; i++) m = red[i] > m ? red[i] : m;
+    red[32] = m;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// ------------------------------------------------------------ Q8 quantiser
+__global__ void k_q8(const float *__restrict__ x, long xs_e, long xs_l, int k, int b, Q8Dev act) {
+  const int nb = k >> 5, lane = threadIdx.x & 31;
+  const long nwarp_total = (long)b * nb;
+  const long wstride = ((long)gridDim.x * blockDim.x) >> 5;
+  for (long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; w < nwarp_total; w += wstride) {
+    const int bi = (int)(w / nb), blk = (int)(w - (long)bi * nb);
+    float v = x[(long)(blk * 32 + lane) * xs_e + (long)bi * xs_l];
+    q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
+  }
+}
+
+cudaError_t launch_q8(const float *x, long xs_e, long xs_l, int k, int b, Q8Dev act, cudaStream_t st) {
+  long warps = (long)b * (k / 32);
+  int grid = (int)std::min<long>((warps * 32 + 255) / 256, (long)num_sms() * 8);
+  if (grid < 1) grid = 1;
+  k_q8<<<grid, 256, 0, st>>>(x, xs_e, xs_l, k, b, act);
+  return cudaGetLastError();
+}
+
+// RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.
+__global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
+                             float *__restrict__ xn) {
+  __shared__ float red[40];
+  const int bi = blockIdx.x;
+  const float *xr = x + (long)bi * k;
+  float part = 0.0f;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) part = fadd(part, fmul(xr[i], xr[i]));
+  const float ss = block_sum(part, red);
+  const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
+  const int nb = k >> 5, lane = threadIdx.x & 31;
+  for (int blk = threadIdx.x >> 5; blk < nb; blk += blockDim.x >> 5) {
+    const int i = blk * 32 + lane;
+    const float v = fmul(fmul(xr[i], s), nw[i]);
+    if (xn) xn[(long)bi * k + i] = v;
+    q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
+  }
+}
+
+cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
+                              cudaStream_t st) {
+  k_rmsnorm_q8<<<b, 256, 0, st>>>(x, nw, eps, k, act, xn);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ matvec core
+// A "group" is the unit one thread handles: 64 weights of Q4_K / Q6_K or a
+// 32-weight block of Q8_0 / Q4_0.  It yields TPG consecutive terms of the
+// row's reference accumulation order (term index = group * TPG + s).
+template <int T> struct Geo;
+template <> struct Geo<T_Q4_K> { static constexpr int GE = 64, TPG = 2; };
+template <> struct Geo<T_Q6_K> { static constexpr int GE = 64, TPG = 4; };
+template <> struct Geo<T_Q8_0> { static constexpr int GE = 32, TPG = 1; };
+template <> struct Geo<T_Q4_0> { static constexpr int GE = 32, TPG = 1; };
+
+struct ActRef {  // one lane's Q8 activation: q [k], d/s [k/32]
+  const int8_t *q;
+  const float *d;
+  const int32_t *s;
+};
+
+__device__ __forceinline__ int lo4(uint32_t w) { return (int)(w & 0x0F0F0F0Fu); }
+__device__ __forceinline__ int hi4(uint32_t w) { return (int)((w >> 4) & 0x0F0F0F0Fu); }
+
+template <int T> struct GroupW;
+
+template <> struct GroupW<T_Q4_K> {
+  uint4 hdr, w0, w1;
+  int blk, sb0;
+  __device__ __forceinline__ void load(const DevTensor &W, int row, int gi) {
+    const int nblk = W.k >> 8;
+    blk = gi >> 2;
+    const int g = gi & 3;
+    sb0 = 2 * g;
+    const uint8_t *base = W.q + ((size_t)row * nblk + blk) * 144;
+    hdr = ldw16(base);
+    w0 = ldw16(base + 16 + g * 32);
+    w1 = ldw16(base + 32 + g * 32);
+  }
+  // quant_int.rs:354-365: acc += d*da*s*dot - da*dmin*m*sa per sub-block.
+  __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+    const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 256 + sb0 * 32);
+    const int4 a00 = ap[0], a01 = ap[1], a10 = ap[2], a11 = ap[3];
+    int d0 = 0, d1 = 0;
+    d0 = __dp4a(lo4(w0.x), a00.x, d0); d0 = __dp4a(lo4(w0.y), a00.y, d0);
+    d0 = __dp4a(lo4(w0.z), a00.z, d0); d0 = __dp4a(lo4(w0.w), a00.w, d0);
+    d0 = __dp4a(lo4(w1.x), a01.x, d0); d0 = __dp4a(lo4(w1.y), a01.y, d0);
+    d0 = __dp4a(lo4(w1.z), a01.z, d0); d0 = __dp4a(lo4(w1.w), a01.w, d0);
+    d1 = __dp4a(hi4(w0.x), a10.x, d1); d1 = __dp4a(hi4(w0.y), a10.y, d1);
+    d1 = __dp4a(hi4(w0.z), a10.z, d1); d1 = __dp4a(hi4(w0.w), a10.w, d1);
+    d1 = __dp4a(hi4(w1.x), a11.x, d1); d1 = __dp4a(hi4(w1.y), a11.y, d1);
+    d1 = __dp4a(hi4(w1.z), a11.z, d1); d1 = __dp4a(hi4(w1.w), a11.w, d1);
+    const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
+    int sc0, m0, sc1, m1;
+    scale_min_k4(hdr, sb0, sc0, m0);
+    scale_min_k4(hdr, sb0 + 1, sc1, m1);
+    const int ai = blk * 8 + sb0;
+    const float da0 = A.d[ai], da1 = A.d[ai + 1];
+    const int sa0 = A.s[ai], sa1 = A.s[ai + 1];
+    t[0] = fsub(fmul(fmul(fmul(d, da0), (float)sc0), (float)d0), fmul(fmul(fmul(da0, dmin), (float)m0), (float)sa0));
+    t[1] = fsub(fmul(fmul(fmul(d, da1), (float)sc1), (float)d1), fmul(fmul(fmul(da1, dmin), (float)m1), (float)sa1));
+  }
+};
+
+template <> struct GroupW<T_Q6_K> {
+  int q[4][4];  // [s][word]: signed 6-bit weights minus 32, 16 per s
+  uint4 scv;
+  float d;
+  int blk, h, g;
+  __device__ __forceinline__ void load(const DevTensor &W, int row, int gi) {
+    const int nblk = W.k >> 8;
+    blk = gi >> 2;
+    h = (gi >> 1) & 1;
+    g = gi & 1;
+    const size_t bidx = (size_t)row * nblk + blk;
+    const uint8_t *base = W.q + bidx * 208;
+    const uint4 qa = ldw16(base + h * 64 + g * 16);
+    const uint4 qb = ldw16(base + h * 64 + 32 + g * 16);
+    const uint4 qh = ldw16(base + 128 + h * 32 + g * 16);
+    scv = ldw16(base + 192);
+    d = f16f(__ldg(W.d + bidx));
+#pragma unroll
+    for (int w = 0; w < 4; w++) {  // quant_int.rs:386-394 unpacking, four bytes at a time
+      const uint32_t a = word_of(qa, w), b = word_of(qb, w), hh = word_of(qh, w);
+      q[0][w] = (int)__vsub4((a & 0x0F0F0F0Fu) | ((hh << 4) & 0x30303030u), 0x20202020u);
+      q[1][w] = (int)__vsub4((b & 0x0F0F0F0Fu) | ((hh << 2) & 0x30303030u), 0x20202020u);
+      q[2][w] = (int)__vsub4(((a >> 4) & 0x0F0F0F0Fu) | (hh & 0x30303030u), 0x20202020u);
+      q[3][w] = (int)__vsub4(((b >> 4) & 0x0F0F0F0Fu) | ((hh >> 2) & 0x30303030u), 0x20202020u);
+    }
+  }
+  // quant_int.rs:397-413: acc += d*scale*da*dot per 16-element piece, order (half, g, s).
+  __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      const int4 a = *reinterpret_cast<const int4 *>(A.q + blk * 256 + (4 * h + s) * 32 + g * 16);
+      int dot = 0;
+      dot = __dp4a(q[s][0], a.x, dot);
+      dot = __dp4a(q[s][1], a.y, dot);
+      dot = __dp4a(q[s][2], a.z, dot);
+      dot = __dp4a(q[s][3], a.w, dot);
+      const float scale = (float)(int8_t)byte_of(scv, h * 8 + g + 2 * s);
+      const float da = A.d[blk * 8 + 4 * h + s];
+      t[s] = fmul(fmul(fmul(d, scale), da), (float)dot);
+    }
+  }
+};
+
+template <> struct GroupW<T_Q8_0> {
+  uint4 w0, w1;
+  float d;
+  int blk;
+  __device__ __forceinline__ void load(const DevTensor &W, int row, int gi) {
+    blk = gi;
+    const uint8_t *qs = W.q + (size_t)row * W.k + (size_t)gi * 32;
+    w0 = ldw16(qs);
+    w1 = ldw16(qs + 16);
+    d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
+  }
+  // quant_int.rs:291-296: acc += d*da*dot.
+  __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+    const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
+    const int4 a0 = ap[0], a1 = ap[1];
+    int dot = 0;
+    dot = __dp4a((int)w0.x, a0.x, dot); dot = __dp4a((int)w0.y, a0.y, dot);
+    dot = __dp4a((int)w0.z, a0.z, dot); dot = __dp4a((int)w0.w, a0.w, dot);
+    dot = __dp4a((int)w1.x, a1.x, dot); dot = __dp4a((int)w1.y, a1.y, dot);
+    dot = __dp4a((int)w1.z, a1.z, dot); dot = __dp4a((int)w1.w, a1.w, dot);
+    t[0] = fmul(fmul(d, A.d[blk]), (float)dot);
+  }
+};
+
+template <> struct GroupW<T_Q4_0> {
+  uint4 w;
+  float d;
+  int blk;
+  __device__ __forceinline__ void load(const DevTensor &W, int row, int gi) {
+    blk = gi;
+    w = ldw16(W.q + (size_t)row * (W.k >> 1) + (size_t)gi * 16);
+    d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
+  }
+  // quant_int.rs:316-323: acc += d*dq*(dot - 8*sq).
+  __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+    const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
+    const int4 a0 = ap[0], a1 = ap[1];
+    int dot = 0;
+    dot = __dp4a(lo4(w.x), a0.x, dot); dot = __dp4a(lo4(w.y), a0.y, dot);
+    dot = __dp4a(lo4(w.z), a0.z, dot); dot = __dp4a(lo4(w.w), a0.w, dot);
+    dot = __dp4a(hi4(w.x), a1.x, dot); dot = __dp4a(hi4(w.y), a1.y, dot);
+    dot = __dp4a(hi4(w.z), a1.z, dot); dot = __dp4a(hi4(w.w), a1.w, dot);
+    t[0] = fmul(fmul(d, A.d[blk]), fsub((float)dot, fmul(8.0f, (float)A.s[blk])));
+  }
+};
+
+// ------------------------------------------------------------ single-lane tile
+constexpr int B1_THREADS = 256;
+constexpr int B1_RT = 16;   // rows per tile
+constexpr int B1_TW = 256;  // terms per wave per row
+
+// Rows [r0, r0+nr) of W against one activation held in shared memory.
+// Returns the row's reference-ordered sum in threads [0, nr).
+template <int T>
+__device__ float tile_b1(const DevTensor &W, int r0, int nr, const ActRef &A, float *Tsm) {
+  constexpr int GE = Geo<T>::GE, TPG = Geo<T>::TPG, GW = B1_TW / TPG;
+  const int G = W.k / GE;
+  const int tid = threadIdx.x;
+  float acc = 0.0f;
+  for (int g0 = 0; g0 < G; g0 += GW) {
+    const int gw = min(GW, G - g0);
+    const int items = nr * gw;
+    for (int it = tid; it < items; it += B1_THREADS) {
+      const int rl = it / gw, gl = it - rl * gw;
+      GroupW<T> gwt;
+      gwt.load(W, r0 + rl, g0 + gl);
+      float t[TPG];
+      gwt.terms(A, t);
+#pragma unroll
+      for (int s = 0; s < TPG; s++) Tsm[(gl * TPG + s) * B1_RT + rl] = t[s];
+    }
+    __syncthreads();
+    if (tid < nr) {
+      const int nt = gw * TPG;
+#pragma unroll 8
+      for (int j = 0; j < nt; j++) acc = fadd(acc, Tsm[j * B1_RT + tid]);
+    }
+    __syncthreads();
+  }
+  return acc;
+}
+
+__device__ float tile_b1_any(const DevTensor &W, int r0, int nr, const ActRef &A, float *Tsm) {
+  switch (W.type) {
+    case T_Q4_K: return tile_b1<T_Q4_K>(W, r0, nr, A, Tsm);
+    case T_Q6_K: return tile_b1<T_Q6_K>(W, r0, nr, A, Tsm);
+    case T_Q8_0: return tile_b1<T_Q8_0>(W, r0, nr, A, Tsm);
+    default: return tile_b1<T_Q4_0>(W, r0, nr, A, Tsm);
+  }
+}
+
+struct B1Smem {
+  int8_t *q;
+  float *d;
+  int32_t *s;
+  float *T;
+  float *red;
+  float *xv;
+};
+
+static size_t b1_smem_bytes(int k) {
+  const size_t nb = (size_t)k / 32;
+  return ((size_t)k + 15) / 16 * 16 + nb * 4 + nb * 4 + (size_t)B1_TW * B1_RT * 4 + 40 * 4 + B1_RT * 4 * 2;
+}
+
+__device__ B1Smem b1_carve(uint8_t *base, int k) {
+  B1Smem m;
+  const int nb = k >> 5;
+  m.q = (int8_t *)base;
+  size_t off = ((size_t)k + 15) / 16 * 16;
+  m.d = (float *)(base + off);
+  off += (size_t)nb * 4;
+  m.s = (int32_t *)(base + off);
+  off += (size_t)nb * 4;
+  m.T = (float *)(base + off);
+  off += (size_t)B1_TW * B1_RT * 4;
+  m.red = (float *)(base + off);
+  off += 40 * 4;
+  m.xv = (float *)(base + off);
+  return m;
+}
+
+// Fill the CTA's shared Q8 activation from a float vector (optionally RMS
+// normalised, model.rs:795-809 / 812-822) or from a precomputed Q8Act.
+__device__ void act_prologue(const B1Src &src, int k, const B1Smem &m) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nb = k >> 5;
+  if (src.x == nullptr) {
+    const int4 *sq = reinterpret_cast<const int4 *>(src.act.q);
+    for (int i = tid; i < k / 16; i += blockDim.x) reinterpret_cast<int4 *>(m.q)[i] = sq[i];
+    for (int i = tid; i < nb; i += blockDim.x) {
+      m.d[i] = src.act.d[i];
+      m.s[i] = src.act.s[i];
+    }
+    __syncthreads();
+    return;
+  }
+  float scale = 1.0f;
+  if (src.nw) {
+    float part = 0.0f;
+    for (int i = tid; i < k; i += blockDim.x) {
+      const float v = src.x[i];
+      part = fadd(part, fmul(v, v));
+    }
+    const float ss = block_sum(part, m.red);
+    scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), src.eps)));
+  }
+  for (int blk = warp; blk < nb; blk += blockDim.x >> 5) {
+    float v = src.x[blk * 32 + lane];
+    if (src.nw) v = fmul(fmul(v, scale), src.nw[blk * 32 + lane]);
+    q8_block_lane(v, lane, m.q + blk * 32, m.d + blk, m.s + blk);
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(B1_THREADS) k_mv_b1(DevTensor W, B1Src src, float *__restrict__ out, int add) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const B1Smem m = b1_carve(smem_raw, W.k);
+  act_prologue(src, W.k, m);
+  const ActRef A{m.q, m.d, m.s};
+  const int tiles = (W.rows + B1_RT - 1) / B1_RT;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int r0 = t * B1_RT, nr = min(B1_RT, W.rows - r0);
+    const float acc = tile_b1_any(W, r0, nr, A, m.T);
+    if ((int)threadIdx.x < nr) {
+      const float v = fadd(0.0f, acc);  // Pool::matmul zero-fills, then out += acc
+      const int r = r0 + threadIdx.x;
+      out[r] = add ? fadd(out[r], v) : v;
+    }
+  }
+}
+
+static int b1_grid(int tiles, size_t smem) {
+  // Resident CTAs per SM bound by the 228 KB shared memory and 2048 threads.
+  int per_sm = (int)std::min<size_t>(8, std::max<size_t>(1, (227 * 1024) / std::max<size_t>(smem, 1)));
+  return std::max(1, std::min(tiles, num_sms() * per_sm));
+}
+
+template <typename K>
+static cudaError_t set_smem(K kernel, size_t smem) {
+  if (smem > 48 * 1024) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return cudaSuccess;
+}
+
+cudaError_t launch_mv_b1(const DevTensor &w, const B1Src &src, float *out, bool add, cudaStream_t st) {
+  if (!type_is_matvec(w.type)) return cudaErrorInvalidValue;
+  const size_t smem = b1_smem_bytes(w.k);
+  cudaError_t e = set_smem(k_mv_b1, smem);
+  if (e != cudaSuccess) return e;
+  const int tiles = (w.rows + B1_RT - 1) / B1_RT;
+  k_mv_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(w, src, out, add ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// q/k/v for one token + RoPE (model.rs:953-979) + KV write (model.rs:984-992).
+__global__ void __launch_bounds__(B1_THREADS) k_qkv_b1(QkvArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const B1Smem m = b1_carve(smem_raw, a.wq.k);
+  act_prologue(a.src, a.wq.k, m);
+  const ActRef A{m.q, m.d, m.s};
+  const int tq = (a.wq.rows + B1_RT - 1) / B1_RT, tk = (a.wk.rows + B1_RT - 1) / B1_RT,
+            tv = (a.wv.rows + B1_RT - 1) / B1_RT;
+  const int pos = *a.pos;
+  const int tid = threadIdx.x;
+  for (int t = blockIdx.x; t < tq + tk + tv; t += gridDim.x) {
+    const int seg = t < tq ? 0 : (t < tq + tk ? 1 : 2);
+    const int tt = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
+    const DevTensor &W = seg == 0 ? a.wq : (seg == 1 ? a.wk : a.wv);
+    const int r0 = tt * B1_RT, nr = min(B1_RT, W.rows - r0);
+    const float acc = tile_b1_any(W, r0, nr, A, m.T);
+    const float val = fadd(0.0f, acc);
+    if (tid < nr) m.xv[tid] = val;
+    __syncthreads();
+    if (tid < nr) {
+      const int r = r0 + tid, hd = r / a.dh, d = r - hd * a.dh;
+      float o = val;
+      if (seg < 2 && d < 2 * a.half) {
+        const int i = d >> 1;
+        const float c = a.rope_cos[(size_t)pos * a.half + i], s = a.rope_sin[(size_t)pos * a.half + i];
+        if ((d & 1) == 0) o = fsub(fmul(val, c), fmul(m.xv[tid + 1], s));
+        else o = fadd(fmul(m.xv[tid - 1], s), fmul(val, c));
+      }
+      if (seg == 0) a.qout[r] = o;
+      else if (seg == 1) a.kcache[((size_t)hd * a.n_ctx + pos) * a.dh + d] = o;
+      else a.vcache[((size_t)hd * a.n_ctx + pos) * a.dh + d] = o;
+    }
+    __syncthreads();
+  }
+}
+
+cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st) {
+  if (!type_is_matvec(a.wq.type) || !type_is_matvec(a.wk.type) || !type_is_matvec(a.wv.type)) return cudaErrorInvalidValue;
+  const size_t smem = b1_smem_bytes(a.wq.k);
+  cudaError_t e = set_smem(k_qkv_b1, smem);
+  if (e != cudaSuccess) return e;
+  const int tiles = (a.wq.rows + B1_RT - 1) / B1_RT + (a.wk.rows + B1_RT - 1) / B1_RT + (a.wv.rows + B1_RT - 1) / B1_RT;
+  k_qkv_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+// gate/up for one token + SwiGLU (model.rs:1105-1115).
+__global__ void __launch_bounds__(B1_THREADS) k_gateup_b1(DevTensor wg, DevTensor wu, B1Src src, float *__restrict__ h) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const B1Smem m = b1_carve(smem_raw, wg.k);
+  act_prologue(src, wg.k, m);
+  const ActRef A{m.q, m.d, m.s};
+  const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int r0 = t * B1_RT, nr = min(B1_RT, wg.rows - r0);
+    const float ag = tile_b1_any(wg, r0, nr, A, m.T);
+    const float au = tile_b1_any(wu, r0, nr, A, m.T);
+    if ((int)threadIdx.x < nr) {
+      const float g = fadd(0.0f, ag), u = fadd(0.0f, au);
+      const float s = fdiv(g, fadd(1.0f, expf_cr(-g)));
+      h[r0 + threadIdx.x] = fmul(s, u);
+    }
+  }
+}
+
+cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1Src &src, float *h, cudaStream_t st) {
+  if (!type_is_matvec(wg.type) || !type_is_matvec(wu.type) || wg.rows != wu.rows || wg.k != wu.k)
+    return cudaErrorInvalidValue;
+  const size_t smem = b1_smem_bytes(wg.k);
+  cudaError_t e = set_smem(k_gateup_b1, smem);
+  if (e != cudaSuccess) return e;
+  const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
+  k_gateup_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(wg, wu, src, h);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ multi-lane matvec
+constexpr int L_THREADS = 256;
+constexpr int L_RT = 8;    // rows per tile
+constexpr int L_LB = 32;   // lanes per pass
+constexpr int L_TW = 48;   // terms per wave per (row, lane)
+
+template <int T>
+__device__ void tile_lanes(const DevTensor &W, int r0, int nr, const Q8Dev &act, int l0, int nl, float *Tsm,
+                           float *out, long os_row, long os_lane, int add) {
+  constexpr int GE = Geo<T>::GE, TPG = Geo<T>::TPG, GW = L_TW / TPG;
+  const int G = W.k / GE, nb = W.k >> 5;
+  const int tid = threadIdx.x;
+  float acc = 0.0f;
+  for (int g0 = 0; g0 < G; g0 += GW) {
+    const int gw = min(GW, G - g0);
+    const int items = nr * gw;
+    for (int it = tid; it < items; it += L_THREADS) {
+      const int rl = it / gw, gl = it - rl * gw;
+      GroupW<T> gwt;
+      gwt.load(W, r0 + rl, g0 + gl);
+      for (int ln = 0; ln < nl; ln++) {
+        const int lane = l0 + ln;
+        const ActRef A{act.q + (long)lane * W.k, act.d + (long)lane * nb, act.s + (long)lane * nb};
+        float t[TPG];
+        gwt.terms(A, t);
+#pragma unroll
+        for (int s = 0; s < TPG; s++) Tsm[(gl * TPG + s) * (L_LB * L_RT) + ln * L_RT + rl] = t[s];
+      }
+    }
+    __syncthreads();
+    if (tid < nl * L_RT && (tid % L_RT) < nr) {
+      const int nt = gw * TPG;
+#pragma unroll 4
+      for (int j = 0; j < nt; j++) acc = fadd(acc, Tsm[j * (L_LB * L_RT) + tid]);
+    }
+    __syncthreads();
+  }
+  if (tid < nl * L_RT && (tid % L_RT) < nr) {
+    const int ln = tid / L_RT, rl = tid % L_RT;
+    const float v = fadd(0.0f, acc);
+    float *o = out + (long)(r0 + rl) * os_row + (long)(l0 + ln) * os_lane;
+    *o = add ? fadd(*o, v) : v;
+  }
+}
+
+__global__ void __launch_bounds__(L_THREADS) k_mv_lanes(DevTensor W, Q8Dev act, float *out, long os_row, long os_lane,
+                                                         int add) {
+  __shared__ float Tsm[L_TW * L_LB * L_RT];
+  const int tiles = (W.rows + L_RT - 1) / L_RT;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int r0 = t * L_RT, nr = min(L_RT, W.rows - r0);
+    for (int l0 = 0; l0 < act.b; l0 += L_LB) {
+      const int nl = min(L_LB, act.b - l0);
+      switch (W.type) {
+        case T_Q4_K: tile_lanes<T_Q4_K>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
+        case T_Q6_K: tile_lanes<T_Q6_K>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
+        case T_Q8_0: tile_lanes<T_Q8_0>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
+        default: tile_lanes<T_Q4_0>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
+      }
+    }
+  }
+}
+
+cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
+                            cudaStream_t st) {
+  if (!type_is_matvec(w.type) || act.k != w.k || act.b < 1) return cudaErrorInvalidValue;
+  const int tiles = (w.rows + L_RT - 1) / L_RT;
+  const int grid = std::max(1, std::min(tiles, num_sms() * 4));
+  k_mv_lanes<<<grid, L_THREADS, 0, st>>>(w, act, out, os_row, os_lane, add ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ RoPE + KV, SwiGLU
+__global__ void k_rope_kv(float *q, const float *k, const float *v, const int *pos, const float *rc, const float *rs,
+                          int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc) {
+  const int bi = blockIdx.x;
+  const int p = pos[bi];
+  const int qdim = n_head * dh, kdim = n_kv * dh;
+  float *qr = q + (long)bi * qdim;
+  for (int i = threadIdx.x; i < n_head * half; i += blockDim.x) {
+    const int h = i / half, j = i - h * half;
+    const int i0 = h * dh + 2 * j;
+    const float x0 = qr[i0], x1 = qr[i0 + 1];
+    const float c = rc[(size_t)p * half + j], s = rs[(size_t)p * half + j];
+    qr[i0] = fsub(fmul(x0, c), fmul(x1, s));
+    qr[i0 + 1] = fadd(fmul(x0, s), fmul(x1, c));
+  }
+  const float *kr = k + (long)bi * kdim, *vr = v + (long)bi * kdim;
+  for (int i = threadIdx.x; i < kdim; i += blockDim.x) {
+    const int h = i / dh, d = i - h * dh;
+    float o = kr[i];
+    if (d < 2 * half) {
+      const int j = d >> 1;
+      const float c = rc[(size_t)p * half + j], s = rs[(size_t)p * half + j];
+      if ((d & 1) == 0) o = fsub(fmul(kr[i], c), fmul(kr[i + 1], s));
+      else o = fadd(fmul(kr[i - 1], s), fmul(kr[i], c));
+    }
+    const size_t dst = ((size_t)h * n_ctx + p) * dh + d;
+    kc[dst] = o;
+    vc[dst] = vr[i];
+  }
+}
+
+cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rc,
+                           const float *rs, int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc,
+                           cudaStream_t st) {
+  k_rope_kv<<<b, 256, 0, st>>>(q, k, v, pos, rc, rs, half, dh, n_head, n_kv, n_ctx, kc, vc);
+  return cudaGetLastError();
+}
+
+__global__ void k_swiglu(const float *g, const float *u, float *h, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float gg = g[i];
+    h[i] = fmul(fdiv(gg, fadd(1.0f, expf_cr(-gg))), u[i]);
+  }
+}
+
+cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st) {
+  int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 8);
+  k_swiglu<<<std::max(grid, 1), 256, 0, st>>>(g, u, h, n);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ attention
+// Three passes over position chunks of ATTN_CHUNK:
+//   1. scores s_p = (q . k_p) * scale, a sequential dh-long dot per thread
+//      (bit-identical to model.rs:1015-1021), plus each chunk's maximum;
+//   2. e_p = exp(s_p - M) with the global maximum M (model.rs:1041-1044),
+//      chunk sums of e_p and chunk partials of sum_p e_p * v_p;
+//   3. combine chunks, out = acc * (1/sum) (model.rs:1046, 1078-1084).
+// Only the grouping of the two sums differs from the reference's single
+// sequential loop.
+__global__ void __launch_bounds__(ATTN_CHUNK) k_attn_scores(AttnArgs a) {
+  __shared__ float qs[256];
+  __shared__ float red[40];
+  const int group = a.n_head / a.n_kv, tid = threadIdx.x;
+  const long n_items = (long)a.b * a.n_head * a.n_chunk;
+  for (long it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const int c = (int)(it % a.n_chunk);
+    const long r = it / a.n_chunk;
+    const int h = (int)(r % a.n_head), bi = (int)(r / a.n_head);
+    const int pos = a.pos[bi];
+    if (c > pos / ATTN_CHUNK) continue;
+    __syncthreads();
+    for (int d = tid; d < a.dh; d += blockDim.x) qs[d] = a.q[((long)bi * a.n_head + h) * a.dh + d];
+    __syncthreads();
+    const int p = c * ATTN_CHUNK + tid;
+    float s = -INFINITY;
+    if (p <= pos) {
+      const float *kr = a.kcache + ((size_t)(h / group) * a.n_ctx + p) * a.dh;
+      float acc = 0.0f;
+      for (int d = 0; d < a.dh; d += 4) {
+        const float4 kv = *reinterpret_cast<const float4 *>(kr + d);
+        acc = fadd(acc, fmul(qs[d], kv.x));
+        acc = fadd(acc, fmul(qs[d + 1], kv.y));
+        acc = fadd(acc, fmul(qs[d + 2], kv.z));
+        acc = fadd(acc, fmul(qs[d + 3], kv.w));
+      }
+      s = fmul(acc, a.scale);
+      a.scores[((long)bi * a.n_head + h) * a.n_ctx + p] = s;
+    }
+    const float mx = block_max(s, red);
+    if (tid == 0) a.cmax[((long)bi * a.n_head + h) * a.n_chunk + c] = mx;
+  }
+}
+
+__global__ void __launch_bounds__(ATTN_CHUNK) k_attn_pv(AttnArgs a) {
+  __shared__ float e[ATTN_CHUNK];
+  __shared__ float red[40];
+  const int group = a.n_head / a.n_kv, tid = threadIdx.x;
+  const long n_items = (long)a.b * a.n_head * a.n_chunk;
+  for (long it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const int c = (int)(it % a.n_chunk);
+    const long r = it / a.n_chunk;
+    const int h = (int)(r % a.n_head), bi = (int)(r / a.n_head);
+    const int pos = a.pos[bi];
+    const int nc = pos / ATTN_CHUNK + 1;
+    if (c >= nc) continue;
+    const long hb = (long)bi * a.n_head + h;
+    float M = -INFINITY;
+    for (int j = 0; j < nc; j++) {
+      const float v = a.cmax[hb * a.n_chunk + j];
+      M = v > M ? v : M;
+    }
+    const int p = c * ATTN_CHUNK + tid;
+    float ev = 0.0f;
+    if (p <= pos) ev = expf_cr(fsub(a.scores[hb * a.n_ctx + p], M));
+    __syncthreads();
+    e[tid] = ev;
+    const float l = block_sum(ev, red);
+    if (tid == 0) a.csum[hb * a.n_chunk + c] = l;
+    const int np = min(ATTN_CHUNK, pos + 1 - c * ATTN_CHUNK);
+    for (int d = tid; d < a.dh; d += blockDim.x) {
+      const float *vr = a.vcache + ((size_t)(h / group) * a.n_ctx + (size_t)c * ATTN_CHUNK) * a.dh + d;
+      float acc = 0.0f;
+      for (int j = 0; j < np; j++) acc = fadd(acc, fmul(e[j], vr[(size_t)j * a.dh]));
+      a.cacc[(hb * a.n_chunk + c) * a.dh + d] = acc;
+    }
+  }
+}
+
+__global__ void k_attn_combine(AttnArgs a) {
+  const int h = blockIdx.x, bi = blockIdx.y;
+  const int nc = a.pos[bi] / ATTN_CHUNK + 1;
+  const long hb = (long)bi * a.n_head + h;
+  float sum = 0.0f;
+  for (int c = 0; c < nc; c++) sum = fadd(sum, a.csum[hb * a.n_chunk + c]);
+  const float inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+  for (int d = threadIdx.x; d < a.dh; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int c = 0; c < nc; c++) acc = fadd(acc, a.cacc[(hb * a.n_chunk + c) * a.dh + d]);
+    a.out[hb * a.dh + d] = fmul(acc, inv);
+  }
+}
+
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
+  if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
+  const long items = (long)a.b * a.n_head * a.n_chunk;
+  const int grid = (int)std::max<long>(1, std::min<long>(items, (long)num_sms() * 8));
+  k_attn_scores<<<grid, ATTN_CHUNK, 0, st>>>(a);
+  k_attn_pv<<<grid, ATTN_CHUNK, 0, st>>>(a);
+  k_attn_combine<<<dim3(a.n_head, a.b), std::min(a.dh, 256), 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ argmax / feedback
+__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, int n, uint32_t *out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+    *out = bi == INT_MAX ? 0u : (uint32_t)bi;  // nothing above -inf: the reference keeps index 0
+  }
+}
+
+cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st) {
+  k_argmax<<<1, 1024, 0, st>>>(x, n, out_idx);
+  return cudaGetLastError();
+}
+
+__global__ void k_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step) {
+  const uint32_t t = *tok;
+  ids[0] = t;
+  pos[0] += 1;
+  hist[*step] = t;
+  *step += 1;
+}
+
+cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st) {
+  k_advance<<<1, 1, 0, st>>>(tok, ids, pos, hist, step);
+  return cudaGetLastError();
+}
+
+}  // namespace pk

@@ -1,0 +1,112 @@
+// pk_kernels.h -- host-side view of the sm_100a kernels (launchers).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pk {
+
+// A weight matrix in the device layout (n_rows rows of k elements).
+//   Q4_K : q = raw GGUF blocks (144 B, already 16-byte aligned), d = nullptr
+//   Q6_K : q = [rows][nblk][208 B] (ql | qh | scales), d = [rows][nblk] f16
+//   Q8_0 : q = [rows][k] int8,                         d = [rows][k/32] f16
+//   Q4_0 : q = [rows][k/2] nibbles (GGUF order),      d = [rows][k/32] f16
+// The split keeps every per-thread load 16-byte aligned; the bytes are the
+// GGUF block bytes rearranged, so the arithmetic is unchanged.
+struct DevTensor {
+  int type = -1, k = 0, rows = 0;
+  const uint8_t *q = nullptr;
+  const uint16_t *d = nullptr;
+};
+
+// Q8Act in device memory: q [b][k], d/s [b][k/32].
+struct Q8Dev {
+  int8_t *q = nullptr;
+  float *d = nullptr;
+  int32_t *s = nullptr;
+  int k = 0, b = 0;
+};
+
+bool type_is_matvec(int type);
+bool type_block(int type, int *be, int *bb);
+size_t packed_q_bytes(int type, int k, int rows);
+size_t packed_bytes(int type, int k, int rows);
+DevTensor packed_view(int type, int k, int rows, const void *packed);
+
+// Raw GGUF rows (device) -> device layout.
+cudaError_t launch_pack(int type, const void *raw, size_t row_bytes, int k, int rows, void *packed,
+                        cudaStream_t st);
+// Dequantise rows of a raw GGUF tensor: out[i][k] = row ids[i] (ids on device, or
+// ids == nullptr for rows 0..n-1).  Used for the embedding and norm weights.
+cudaError_t launch_dequant_rows(int type, const void *raw, size_t row_bytes, int k, const uint32_t *ids,
+                                int n, float *out, cudaStream_t st);
+
+// Q8Act::prepare on x[i * xs_elem + bi * xs_lane].
+cudaError_t launch_q8(const float *x, long xs_elem, long xs_lane, int k, int b, Q8Dev act, cudaStream_t st);
+// RMSNorm (model.rs:812-822) + Q8 of token-major x [b][k]; xn (optional) gets the normed floats.
+cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
+                              cudaStream_t st);
+
+// Multi-lane matvec: out[r * os_row + lane * os_lane] (+)= row r . lane.
+cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane,
+                            bool add, cudaStream_t st);
+
+// Single-lane matvec with the activation quantised inside each CTA:
+// src = x (k floats, optionally RMS-normalised by nw) or a precomputed Q8 act.
+struct B1Src {
+  const float *x = nullptr;
+  const float *nw = nullptr;
+  float eps = 0.0f;
+  Q8Dev act;  // used when x == nullptr
+};
+cudaError_t launch_mv_b1(const DevTensor &w, const B1Src &src, float *out, bool add, cudaStream_t st);
+
+// Fused q/k/v matvecs + RoPE + KV write for one decode token.
+struct QkvArgs {
+  DevTensor wq, wk, wv;
+  B1Src src;
+  const int *pos = nullptr;          // device scalar: position of the token
+  const float *rope_cos = nullptr;   // [n_ctx][half]
+  const float *rope_sin = nullptr;
+  int half = 0, dh = 0, n_ctx = 0;
+  float *qout = nullptr;   // [n_head * dh]
+  float *kcache = nullptr; // this layer: [n_kv][n_ctx][dh]
+  float *vcache = nullptr;
+};
+cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st);
+// Fused gate/up matvecs + SwiGLU (model.rs:1105-1115) for one token.
+cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1Src &src, float *h,
+                             cudaStream_t st);
+
+// RoPE + KV write for b tokens (token-major q [b][qdim], k/v [b][kdim]).
+cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rope_cos,
+                           const float *rope_sin, int half, int dh, int n_head, int n_kv, int n_ctx, float *kcache,
+                           float *vcache, cudaStream_t st);
+// SwiGLU over [n] elements: h = g / (1 + exp(-g)) * u.
+cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st);
+
+// Causal GQA attention (model.rs:993-1087) for b tokens at positions pos[b].
+struct AttnArgs {
+  const float *q;      // [b][n_head * dh]
+  const float *kcache; // layer base [n_kv][n_ctx][dh]
+  const float *vcache;
+  const int *pos;      // [b] device
+  float *out;          // [b][n_head * dh]
+  int b, n_head, n_kv, dh, n_ctx;
+  float scale;
+  // scratch
+  float *scores;       // [b][n_head][n_ctx]
+  float *cmax;         // [b][n_head][n_chunk]
+  float *csum;         // [b][n_head][n_chunk]
+  float *cacc;         // [b][n_head][n_chunk][dh]
+  int n_chunk;         // ceil(n_ctx / ATTN_CHUNK)
+};
+constexpr int ATTN_CHUNK = 128;
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+
+// First index of the maximum (sampler.rs:26-36); NaNs never win.
+cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st);
+// Decode feedback on the device: ids[0] = *tok; pos[0] += 1; hist[*step] = *tok; *step += 1.
+cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st);
+
+}  // namespace pk
