@@ -1,0 +1,326 @@
+#!/usr/bin/env python3
+"""pocketinfer decode on B200: BASELINE config 3 (2.6B-class Q4_K_M, b = 1).
+
+A step is one greedy decode token of the synthetic M26 model (40 layers,
+d 2304, 36/36 heads x 64, FFN 5760, vocab 73448, Q4_K_M mix with a Q8_0
+ffn_down) after its 323-token seeded prompt.  Timed steps cycle over the
+BASELINE's decode positions 323..450 (the sequence is rewound every 128
+steps), so every step streams the full 1.83 GB of weights plus the KV of
+324..451 positions; weights are far larger than L2, so no flush is needed.
+
+  python bench.py [--gpus N --steps K --warmup W]           our CUDA arm
+  python bench.py --impl reference [--steps K --warmup W]   CPU restatement of
+                                                            the reference path
+
+Multi-GPU (launched by torchrun): b = 1 decode does not shard, so each rank
+runs an independent replica; value = all tokens / max-over-ranks device time.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "pocket-workbench-android_b200"), os.path.join(ROOT, "oracle")]
+
+PROMPT_LEN = 323
+CYCLE = 128
+METRIC = "decode tok/s (2.6B Q4_K_M, b=1)"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1024)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model-dir", default=os.environ.get("PK_MODEL_DIR", tempfile.gettempdir()))
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the bounded CPU baseline sample")
+    p.add_argument("--profile-window", action="store_true",
+                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.25)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        return summarize_clocks(self.lines)
+
+
+def summarize_clocks(lines):
+    sm, smax, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for ln in lines:
+        f = [x.strip() for x in ln.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            smax = float(f[2])
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower().startswith("active"):
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+            "samples": len(sm)}
+
+
+def cycle_steps(eng, n, state, timed):
+    """n decode steps on the device, rewinding to PROMPT_LEN every CYCLE tokens."""
+    total_ms, done = 0.0, 0
+    while done < n:
+        room = PROMPT_LEN + CYCLE - state["pos"]
+        if room <= 0:
+            eng.set_position(PROMPT_LEN)
+            state["pos"] = PROMPT_LEN
+            room = CYCLE
+        m = min(room, n - done)
+        _, ms = eng.decode_steps_device(m, return_ms=True)
+        total_ms += ms
+        state["pos"] += m
+        done += m
+    return total_ms
+
+
+def cpu_baseline_sample(path, prompt, budget_s):
+    """The CPU restatement (oracle) on this host: decode tok/s on a bounded sample."""
+    import pko
+
+    threads = os.cpu_count() or 1
+    o = pko.Engine(path, 512, threads)
+    short = prompt[:32]
+    probe = o.generate(short, 3)
+    per_tok = max(probe["gen_ms"] / 2.0, 1e-3) / 1000.0
+    s = int(max(4, min(64, budget_s / per_tok)))
+    r = o.generate(short, s + 1)
+    o.close()
+    return {"value": s / (r["gen_ms"] / 1000.0), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"M26 greedy decode, {s} tokens after a 32-token prompt (KV 32..{32 + s} positions), "
+                      f"C++ restatement of pocketinfer's CPU int8 lanes path, {threads} threads"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return
+    import numpy as np
+
+    import pko
+    from pocketinfer import synth
+
+    path = synth.m26_path(args.model_dir)
+    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.M26.n_vocab)
+    threads = os.cpu_count() or 1
+    o = pko.Engine(path, 512, threads)
+    o.generate(prompt, 1)  # prefill (Engine::generate's 32-token chunks), no decode step
+    pos = PROMPT_LEN
+
+    def step():
+        nonlocal pos
+        if pos >= PROMPT_LEN + CYCLE:
+            pos = PROMPT_LEN
+        tok = int(np.argmax(o.logits()))  # sampler.rs:26-36: first maximum
+        o.forward([tok], [pos], True)
+        pos += 1
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    budget = 150.0
+    timed = 0
+    while timed < args.steps:
+        step()
+        timed += 1
+        if time.perf_counter() - t0 > budget:
+            break
+    dt = time.perf_counter() - t0
+    value = timed / dt
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000.0 / timed, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32", "data": "synthetic",
+            "config": {"workload": "M26 (BASELINE config 3) greedy decode at positions 323..450", "model": "M26"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{timed} of {args.steps} decode steps timed (budget {budget:.0f} s), "
+                                       "C++ restatement of pocketinfer's CPU path (the Rust crate cannot be "
+                                       "built here)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import pocketinfer as pk
+    from pocketinfer import synth
+
+    if rank == 0:
+        path = synth.m26_path(args.model_dir)
+    if dist:
+        dist.barrier()
+    path = synth.m26_path(args.model_dir)
+    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.M26.n_vocab)
+    eng = pk.Engine(path, n_ctx=512, max_batch=32, device=local)
+    info = eng.info
+    # prefill through Engine::generate (32-token chunks); no decode step
+    pre = eng.generate(prompt, 1, stop_at_eog=False)
+    state = {"pos": PROMPT_LEN}
+    cycle_steps(eng, args.warmup, state, False)
+
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    clocks = ClockSampler(gpu_index)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    if args.profile_window:
+        torch.cuda.profiler.start()
+    total_ms = cycle_steps(eng, args.steps, state, True)
+    torch.cuda.synchronize()
+    if args.profile_window:
+        torch.cuda.profiler.stop()
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * args.steps / (max_ms / 1000.0)
+    ms_per_step = max_ms / args.steps
+
+    # per-kernel device times of one eager decode step (for the roofline)
+    eng.set_position(PROMPT_LEN + CYCLE // 2)
+    prof = eng.decode_profile()
+
+    # end to end through Engine::generate: host prompt in, one D2H token read
+    # and one H2D token/position write per decode step, host sync per step
+    n_e2e = min(args.steps, CYCLE)
+    eng.forward(prompt[:1], [0], False)  # public forward: drops the prefix cache
+    r = eng.generate(prompt, n_e2e + 1, stop_at_eog=False)
+    e2e_ms = torch.tensor([r["gen_ms"]], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * n_e2e / (float(e2e_ms.item()) / 1000.0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        eng.close()
+        cpu = cpu_baseline_sample(path, prompt, args.cpu_seconds)
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        dom = max(prof, key=lambda p: p["ms"])
+        achieved = dom["bytes"] / (dom["ms"] / 1000.0) / 1e9
+        step_bytes = info["stream_bytes"] + synth.M26.kv_bytes_per_position() * (PROMPT_LEN + 1 + CYCLE / 2)
+        step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+        launches_per_step = 1 + 1 + 1 + info["n_layer"] * (1 + 3 + 1 + 1 + 1) + 1  # argmax, advance, embed, layers, head
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8xint8->int32, f32", "data": "synthetic",
+            "config": {"workload": "M26 greedy decode b=1 (BASELINE config 3): 323-token prompt, positions "
+                                   "323..450 cycled", "model": "synthetic-2.6B-q4km (random blocks)",
+                       "global_batch": world, "seq_len": PROMPT_LEN + CYCLE,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "no flush: each step streams 1.83 GB of weights (> 126 MB L2)"},
+            "prefill_tok_s": pre["prefill_tokens"] / (pre["prefill_ms"] / 1000.0),
+            "decode_step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
+                                "frac": step_gbs / hbm, "peak": hbm, "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": f"of {peak_kind}", "traffic": None,
+                         "per_kernel": prof},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                    "path": "pk_generate (C ABI), host prompt, per-token host sync"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

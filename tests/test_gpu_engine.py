@@ -1,0 +1,172 @@
+"""Model-level parity of the device engine against the CPU oracle.
+
+Bars (from the path's parity requirements):
+  * identical greedy token ids for the generated sequence;
+  * logits within 1e-3 relative to the logit scale of the oracle's;
+  * Engine::generate prefix-reuse bookkeeping identical to the reference
+    (rust/pocketinfer/src/model.rs:1235-1352, tests/prefix_cache.rs:5-89).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from pocketinfer import synth
+
+pytestmark = pytest.mark.gpu
+THREADS = max(1, min(32, os.cpu_count() or 1))
+
+MODELS = {"tiny": synth.TINY, "q8down": synth.SMALL_Q8DOWN, "q40": synth.SMALL_Q40}
+
+
+@pytest.fixture(scope="module")
+def paths(tmp_path_factory):
+    d = tmp_path_factory.mktemp("models")
+    out = {}
+    for name, spec in MODELS.items():
+        out[name] = str(d / f"{name}.gguf")
+        synth.write_gguf(out[name], spec, seed=21)
+    return out
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / max(1e-6, float(np.std(b))))
+
+
+@pytest.mark.parametrize("name", list(MODELS))
+def test_prefill_logits_match_oracle(pk, oracle, paths, name):
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(5, 45, spec.n_vocab)
+    g = pk.Engine(paths[name], n_ctx=256)
+    o = oracle.Engine(paths[name], 256, THREADS)
+    for lo, hi in ((0, 32), (32, 45)):
+        g.forward(prompt[lo:hi], np.arange(lo, hi), True)
+        o.forward(prompt[lo:hi], np.arange(lo, hi), True)
+    lg, lo_ = g.logits(), o.logits()
+    assert rel_err(lg, lo_) < 1e-3
+    assert int(np.argmax(lg)) == int(np.argmax(lo_))
+    # one b == 1 step (the CUDA-graph decode path)
+    tok = int(np.argmax(lo_))
+    g.forward([tok], [45], True)
+    o.forward([tok], [45], True)
+    assert rel_err(g.logits(), o.logits()) < 1e-3
+
+
+@pytest.mark.parametrize("name", list(MODELS))
+def test_greedy_tokens_identical(pk, oracle, paths, name):
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(17, 70, spec.n_vocab)
+    g = pk.Engine(paths[name], n_ctx=256).generate(prompt, 128, stop_at_eog=False)
+    o = oracle.Engine(paths[name], 256, THREADS).generate(prompt, 128)
+    assert g["gen_ids"] == o["gen_ids"]
+    assert g["prefill_tokens"] == o["prefill_tokens"] == 70
+    assert g["stop"] == o["stop"] == "max_tokens"
+
+
+def test_device_decode_loop_matches_generate(pk, paths):
+    spec = MODELS["tiny"]
+    prompt = synth.prompt_ids(3, 33, spec.n_vocab)
+    ref = pk.Engine(paths["tiny"], n_ctx=256).generate(prompt, 40, stop_at_eog=False)["gen_ids"]
+    e = pk.Engine(paths["tiny"], n_ctx=256)
+    e.forward(prompt[:32], np.arange(32), False)
+    e.forward(prompt[32:], [32], True)
+    ids, ms = e.decode_steps_device(40, return_ms=True)
+    assert ids == ref and ms > 0
+    # rewind to the end of the prompt: the same positions are rewritten
+    e.set_position(34)
+    e.forward([ref[0]], [33], True)
+    assert e.decode_steps_device(39) == ref[1:]
+
+
+def test_decode_profile_reports_kernels(pk, paths):
+    spec = MODELS["q8down"]
+    e = pk.Engine(paths["q8down"], n_ctx=128)
+    e.forward(synth.prompt_ids(2, 20, spec.n_vocab), np.arange(20), True)
+    prof = {p["name"]: p for p in e.decode_profile()}
+    assert prof["k_qkv_b1"]["launches"] == spec.n_layer
+    assert prof["k_gateup_b1"]["launches"] == spec.n_layer
+    assert prof["k_mv_b1"]["launches"] == 2 * spec.n_layer + 1
+    assert all(p["ms"] > 0 and p["bytes"] > 0 for p in prof.values())
+
+
+def test_prefix_reuse_matches_fresh(pk, paths):
+    V = synth.TINY.n_vocab
+    base = synth.prompt_ids(1, 96, V).tolist()
+    extended = base + synth.prompt_ids(2, 9, V).tolist()
+    divergent = synth.prompt_ids(3, 7, V).tolist()
+    path = paths["tiny"]
+    eng = pk.Engine(path, n_ctx=512)
+    eng.generate(base, 2)
+    cached = eng.generate(extended, 2)
+    assert cached["prefill_cached_tokens"] == 96
+    assert cached["prefill_cached_tokens"] + cached["prefill_tokens"] == len(extended)
+    uncached = pk.Engine(path, n_ctx=512).generate(extended, 2)
+    assert cached["gen_ids"] == uncached["gen_ids"]
+    changed = eng.generate(divergent, 2)
+    assert changed["prefill_cached_tokens"] == 0
+    assert changed["gen_ids"] == pk.Engine(path, n_ctx=512).generate(divergent, 2)["gen_ids"]
+    eng.forward([divergent[0]], [0], False)  # public forward invalidates reuse
+    after = eng.generate(extended, 2)
+    assert after["prefill_cached_tokens"] == 0 and after["gen_ids"] == uncached["gen_ids"]
+    pk.request_stop()
+    try:
+        stopped = eng.generate(extended, 2)
+    finally:
+        pk.clear_stop()
+    assert stopped["stop"] == "user_stop"
+    again = eng.generate(extended, 2)
+    assert again["prefill_cached_tokens"] == 0 and again["gen_ids"] == uncached["gen_ids"]
+
+
+def test_prefix_reuse_counts_match_oracle(pk, oracle, paths):
+    V = synth.TINY.n_vocab
+    p1 = synth.prompt_ids(8, 50, V).tolist()
+    p2 = p1[:40] + synth.prompt_ids(9, 30, V).tolist()
+    g, o = pk.Engine(paths["tiny"], n_ctx=256), oracle.Engine(paths["tiny"], 256, THREADS)
+    for p in (p1, p2, p2, p1):
+        rg, ro = g.generate(p, 3), o.generate(p, 3)
+        for key in ("gen_ids", "prefill_tokens", "prefill_cached_tokens", "gen_tokens", "stop"):
+            assert rg[key] == ro[key], key
+
+
+def test_callback_abort(pk, paths):
+    e = pk.Engine(paths["tiny"], n_ctx=128)
+    seen = []
+    r = e.generate(synth.prompt_ids(4, 20, synth.TINY.n_vocab), 10,
+                   callback=lambda t: seen.append(t) or len(seen) < 3)
+    assert r["stop"] == "callback_error" and len(seen) == 3 and r["gen_tokens"] == 3
+
+
+def test_engine_errors(pk, paths, tmp_path):
+    with pytest.raises(pk.PkError) as e:
+        pk.Engine(str(tmp_path / "missing.gguf"))
+    assert e.value.code == 5
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUF\x09\x00\x00\x00" + b"\x00" * 32)
+    with pytest.raises(pk.PkError) as e:
+        pk.Engine(str(bad))
+    assert e.value.code == 5
+    eng = pk.Engine(paths["tiny"], n_ctx=16)
+    with pytest.raises(pk.PkError) as e:
+        eng.forward([synth.TINY.n_vocab], [0])
+    assert e.value.code == 1
+    with pytest.raises(pk.PkError) as e:
+        eng.forward([1], [16])
+    assert e.value.code == 6
+    r = eng.generate(synth.prompt_ids(4, 14, synth.TINY.n_vocab), 8)
+    assert r["stop"] == "context_full" and r["gen_tokens"] == 3
+    with pytest.raises(pk.PkError) as e:
+        eng.generate([1, 2, 3], 2, temp=0.7, top_p=0.9)
+    assert e.value.code == 2
+    with pytest.raises(pk.PkError) as e:
+        pk.Engine(paths["tiny"], n_ctx=16, max_batch=65)
+    assert e.value.code == 1
+
+
+def test_model_info(pk, paths):
+    e = pk.Engine(paths["q8down"], n_ctx=64)
+    i = e.info
+    s = synth.SMALL_Q8DOWN
+    assert (i["n_layer"], i["n_embd"], i["n_ff"], i["n_head"], i["n_rot"], i["n_vocab"]) == \
+        (s.n_layer, s.n_embd, s.n_ff, s.n_head, s.n_rot, s.n_vocab)
+    assert i["stream_bytes"] == s.streamed_bytes_per_token()
