@@ -218,7 +218,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     import pocketinfer as pk
-    from pocketinfer import synth
+    from pocketinfer import replicas, synth
 
     if rank == 0:
         path = synth.m26_path(args.model_dir)
@@ -254,11 +254,7 @@ def run_ours(args):
     clk = clocks.stop()
     if dist:
         dist.barrier()
-    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    value = world * args.steps / (max_ms / 1000.0)
+    value, max_ms = replicas.replica_throughput(args.steps, total_ms, world, dist, "cuda")
     ms_per_step = max_ms / args.steps
 
     # per-kernel device times of one eager decode step (for the roofline)
@@ -270,10 +266,7 @@ def run_ours(args):
     n_e2e = min(args.steps, CYCLE)
     eng.forward(prompt[:1], [0], False)  # public forward: drops the prefix cache
     r = eng.generate(prompt, n_e2e + 1, stop_at_eog=False)
-    e2e_ms = torch.tensor([r["gen_ms"]], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * n_e2e / (float(e2e_ms.item()) / 1000.0)
+    e2e_value, _ = replicas.replica_throughput(n_e2e, r["gen_ms"], world, dist, "cuda")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
