@@ -258,8 +258,9 @@ def run_ours(args):
     ms_per_step = max_ms / args.steps
 
     # per-kernel device times of one eager decode step (for the roofline)
-    eng.set_position(PROMPT_LEN + CYCLE // 2)
-    prof = eng.decode_profile()
+    eng.set_position(PROMPT_LEN)
+    cycle_steps(eng, CYCLE // 2, {"pos": PROMPT_LEN}, False)
+    prof = eng.decode_profile()  # one step at position PROMPT_LEN + CYCLE / 2
 
     # end to end through Engine::generate: host prompt in, one D2H token read
     # and one H2D token/position write per decode step, host sync per step

@@ -221,7 +221,7 @@ int Engine::load(const char *path) {
   auto upload_mat = [&](const TRef &t, DevTensor &dst) -> int {
     uint8_t *slot = d_weights_ + off;
     off += mat_bytes(t);
-    PK_CK(cudaMemcpy(staging, file + t.off, t.row_bytes * t.ne1, cudaMemcpyHostToDevice));
+    PK_CK(cudaMemcpyAsync(staging, file + t.off, t.row_bytes * t.ne1, cudaMemcpyHostToDevice, st_));
     PK_CK(launch_pack(t.type, staging, t.row_bytes, (int)t.ne0, (int)t.ne1, slot, st_));
     PK_CK(cudaStreamSynchronize(st_));
     dst = packed_view(t.type, (int)t.ne0, (int)t.ne1, slot);
@@ -230,7 +230,7 @@ int Engine::load(const char *path) {
   auto upload_norm = [&](const TRef &t, float **dst) -> int {
     float *slot = (float *)(d_weights_ + off);
     off += a256((size_t)c.n_embd * 4);
-    PK_CK(cudaMemcpy(staging, file + t.off, t.row_bytes, cudaMemcpyHostToDevice));
+    PK_CK(cudaMemcpyAsync(staging, file + t.off, t.row_bytes, cudaMemcpyHostToDevice, st_));
     PK_CK(launch_dequant_rows(t.type, staging, t.row_bytes, (int)t.ne0, nullptr, 1, slot, st_));
     PK_CK(cudaStreamSynchronize(st_));
     *dst = slot;
@@ -251,7 +251,7 @@ int Engine::load(const char *path) {
   cudaFree(staging);
   if (rc) return rc;
   embd_raw_ = d_weights_ + off;
-  PK_CK(cudaMemcpy((void *)embd_raw_, file + embd.off, embd.row_bytes * embd.ne1, cudaMemcpyHostToDevice));
+  PK_CK(cudaMemcpyAsync((void *)embd_raw_, file + embd.off, embd.row_bytes * embd.ne1, cudaMemcpyHostToDevice, st_));
   off += a256(embd.row_bytes * embd.ne1);
   embd_type_ = embd.type;
   embd_row_bytes_ = embd.row_bytes;
@@ -260,8 +260,8 @@ int Engine::load(const char *path) {
   kv_bytes_ = 2 * (size_t)c.n_layer * c.n_head_kv * n_ctx_ * c.head_dim * 4;
   PK_CK(cudaMalloc((void **)&d_kcache_, kv_bytes_ / 2));
   PK_CK(cudaMalloc((void **)&d_vcache_, kv_bytes_ / 2));
-  PK_CK(cudaMemset(d_kcache_, 0, kv_bytes_ / 2));
-  PK_CK(cudaMemset(d_vcache_, 0, kv_bytes_ / 2));
+  PK_CK(cudaMemsetAsync(d_kcache_, 0, kv_bytes_ / 2, st_));
+  PK_CK(cudaMemsetAsync(d_vcache_, 0, kv_bytes_ / 2, st_));
 
   // ---- RoPE tables, computed exactly like Scratch::new / ensure_rope
   // (model.rs:414-417, 452-457) with the C library's powf/cosf/sinf.
@@ -276,8 +276,8 @@ int Engine::load(const char *path) {
     }
   PK_CK(cudaMalloc((void **)&d_rope_cos_, std::max<size_t>(tc.size(), 1) * 4));
   PK_CK(cudaMalloc((void **)&d_rope_sin_, std::max<size_t>(ts.size(), 1) * 4));
-  PK_CK(cudaMemcpy(d_rope_cos_, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice));
-  PK_CK(cudaMemcpy(d_rope_sin_, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice));
+  PK_CK(cudaMemcpyAsync(d_rope_cos_, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(d_rope_sin_, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice, st_));
 
   // ---- activations and scratch (one arena)
   const size_t B = max_batch_, ne = c.n_embd, ff = c.n_ff;
@@ -293,7 +293,7 @@ int Engine::load(const char *path) {
   size_t arena = 0;
   for (size_t s : sizes) arena += a256(s);
   PK_CK(cudaMalloc((void **)&d_act_arena_, arena));
-  PK_CK(cudaMemset(d_act_arena_, 0, arena));
+  PK_CK(cudaMemsetAsync(d_act_arena_, 0, arena, st_));
   uint8_t *pa = d_act_arena_;
   size_t si = 0;
   auto take = [&]() {
@@ -336,7 +336,7 @@ void Engine::dump(const char *name, const float *dev, size_t n) {
   if (!dbg_on_) return;
   std::vector<float> h(n);
   cudaStreamSynchronize(st_);
-  cudaMemcpy(h.data(), dev, n * 4, cudaMemcpyDeviceToHost);
+  cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, st_);
   dbg_.emplace_back(name, std::move(h));
 }
 
@@ -718,7 +718,7 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
   if (rc) return rc;
   if (e != cudaSuccess) return cuda_error(e, "decode_profile");
   uint32_t tok = 0;
-  PK_CK(cudaMemcpy(&tok, d_tok_, 4, cudaMemcpyDeviceToHost));
+  PK_CK(cudaMemcpyAsync(&tok, d_tok_, 4, cudaMemcpyDeviceToHost, st_));
   kv_tokens_.push_back(tok);
   next_pos_ += 1;
   for (int i = 0; i < (int)agg.size() && i < cap; i++) out[i] = agg[i];

@@ -120,11 +120,10 @@ def test_config1_q4k_6144x2048(pk, oracle):
     want = oracle_matmul(oracle, synth.Q4_K, w, 2048, 6144, oracle.Q8Act(x, 2048, 1))
     got = pk.matmul(synth.Q4_K, dev(w), 2048, 6144, act_gpu).cpu().numpy()
     assert np.array_equal(bits(got), bits(want))
-    # and within the reference's own int8-vs-f32 tolerance of the x86 f32 path
+    # and close to the x86 f32 path (int8 activation rounding is the only difference)
     rb = oracle.row_bytes(synth.Q4_K, 2048)
-    for r in range(0, 6144, 512):
-        f = oracle.dot_row(synth.Q4_K, w[r * rb:(r + 1) * rb], 2048, x)
-        assert abs(got[r] - f) <= abs(f) * 0.02 + 0.05
+    f = np.array([oracle.dot_row(synth.Q4_K, w[r * rb:(r + 1) * rb], 2048, x) for r in range(0, 6144, 64)])
+    assert np.max(np.abs(got[::64] - f)) <= 0.02 * np.std(f)
 
 
 @pytest.mark.parametrize("t", [synth.Q6_K, synth.Q4_0, synth.Q8_0])
@@ -176,8 +175,10 @@ def test_backend_selftest_and_matvec(pk, oracle):
     be.selftest()
     assert be.supports(synth.Q4_K) and not be.supports(synth.F32)
     k, rows = 2304, 300
-    for t in TYPES:
+    keep = []  # the weight cache is keyed by (host pointer, length), as in opencl.rs:439-460,
+    for t in TYPES:  # so every host slice must stay alive while the backend can see it
         w = random_rows(t, k, rows, 555 + t)
+        keep.append(w)
         x = synth.normal_f32(556, k)
         got = be.matvec(t, w, k, x, rows)
         again = be.matvec(t, w, k, x, rows)  # served from the weight cache
