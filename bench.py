@@ -280,7 +280,7 @@ def run_ours(args):
         achieved = dom["bytes"] / (dom["ms"] / 1000.0) / 1e9
         step_bytes = info["stream_bytes"] + synth.M26.kv_bytes_per_position() * (PROMPT_LEN + 1 + CYCLE / 2)
         step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
-        launches_per_step = 1 + 1 + 1 + info["n_layer"] * (1 + 3 + 1 + 1 + 1) + 1  # argmax, advance, embed, layers, head
+        launches_per_step = 1 + 1 + 1 + info["n_layer"] * 5 + 1  # argmax, advance, embed, 5 per layer, head
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",

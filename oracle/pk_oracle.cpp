@@ -7,15 +7,20 @@
 // -ffp-contract=off and without fast-math, because Rust never contracts a
 // multiply and an add into an FMA and never reassociates.
 //
-// Which reference branch is restated:
-//   * matvecs use the aarch64 int8 lanes path (quant_int.rs:282-419); that is
-//     the path the north-star parity bar ("Q8 activations and integer block
-//     sums bit-exact") refers to;
-//   * rmsnorm / attention use the portable (non-aarch64) branches
-//     (model.rs:795-809, 1013-1026, 1028-1039, 1076-1085), which are the code
-//     the reference compiles on this ISA;
-//   * exp / pow / sin / cos come from the C library, which is what Rust's
-//     f32::{exp,powf,sin,cos} call on Linux.
+// Which reference branch is restated: the aarch64 build, the only build in
+// which the reference's int8 path exists (quant_int.rs:64-80).
+//   * matvecs: the int8 lanes path (quant_int.rs:282-419);
+//   * b == 1 rmsnorm: simd.rs:47-64 f32_sum_sq (two 4-lane FMA accumulators,
+//     added lane-wise, then a pairwise horizontal add), model.rs:791-810;
+//   * b == 1 attention scores: simd.rs:19-43 f32_dot (two 4-lane mul+add
+//     accumulators, each reduced pairwise), model.rs:998-1012;
+//   * b > 1 rmsnorm and scores: the scalar sequential loops (model.rs:812-822,
+//     1027-1039);
+//   * softmax sum and the V accumulation are sequential over positions in
+//     every build; the aarch64 V loop skips zero weights (model.rs:1047-1075).
+// Horizontal adds (vaddvq_f32) are taken as ((l0 + l1) + (l2 + l3)), the
+// FADDP pairwise reduction they compile to.  exp / pow / sin / cos come from
+// the C library (Rust's f32::{exp,powf,sin,cos} call libm).
 //
 // Parity pin: tests/test_oracle_kats.py re-runs the reference's own KATs
 // (tests/quant_layout.rs, simd_q8.rs:57-80, backend/opencl.rs:391-430).
@@ -662,6 +667,33 @@ void pool_matmul(Pool &pool, uint32_t t, const uint8_t *w, size_t row_bytes, siz
   pool.run(n_rows, fn);
 }
 
+// simd.rs:47-64 f32_sum_sq: acc0/acc1 = vfmaq(acc, x, x) over 8-element steps,
+// s = vaddvq(acc0 + acc1), then a scalar (unfused) tail.
+float sum_sq_neon(const float *x, size_t n) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8)
+    for (int l = 0; l < 8; l++) acc[l] = fmaf(x[i + l], x[i + l], acc[l]);
+  float c[4];
+  for (int l = 0; l < 4; l++) c[l] = acc[l] + acc[l + 4];
+  float s = (c[0] + c[1]) + (c[2] + c[3]);
+  for (; i < n; i++) s += x[i] * x[i];
+  return s;
+}
+
+// simd.rs:19-43 f32_dot: acc0/acc1 += a*b (unfused) over 8-element steps,
+// s = vaddvq(acc0) + vaddvq(acc1), then a scalar tail.
+float dot_neon(const float *a, const float *b, size_t n) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8)
+    for (int l = 0; l < 8; l++) acc[l] = acc[l] + a[i + l] * b[i + l];
+  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  s += (acc[4] + acc[5]) + (acc[6] + acc[7]);
+  for (; i < n; i++) s += a[i] * b[i];
+  return s;
+}
+
 bool int8_supported(uint32_t t) {  // quant_int.rs:75-80 with dotprod available
   return t == T_Q4_K || t == T_Q6_K || t == T_Q4_0 || t == T_Q8_0;
 }
@@ -972,7 +1004,7 @@ struct pko_engine {
     pool_matmul(*pool, w.ttype, ptr(w), w.row_bytes, w.ne0, xin, b, out, w.ne1, nullptr);
   }
 
-  // Engine::rmsnorm, portable branches (model.rs:777-823)
+  // Engine::rmsnorm (model.rs:777-823), aarch64 build
   void rmsnorm(const float *xin, const TRef &w, size_t b, float *out) {
     size_t ne = cfg.n_embd;
     float eps = cfg.rms_eps;
@@ -980,8 +1012,7 @@ struct pko_engine {
     dequant_row(w.ttype, ptr(w), ne, wbuf.data());
     const float *wp = wbuf.data();
     if (b == 1) {
-      float ss = 0.0f;
-      for (size_t i = 0; i < ne; i++) ss += xin[i] * xin[i];
+      float ss = sum_sq_neon(xin, ne);
       float s = 1.0f / sqrtf(ss / (float)ne + eps);
       for (size_t i = 0; i < ne; i++) out[i] = xin[i] * s * wp[i];
       return;
@@ -1071,7 +1102,7 @@ struct pko_engine {
             kv_v[base_k + d] = v[(h * dh + d) * b + bi];
           }
         }
-      for (size_t bi = 0; bi < b; bi++) {  // model.rs:993-1087 (portable branches)
+      for (size_t bi = 0; bi < b; bi++) {  // model.rs:993-1087 (aarch64 build)
         size_t pos = positions[bi];
         for (size_t h = 0; h < n_head; h++) {
           size_t kh = h / group;
@@ -1080,8 +1111,13 @@ struct pko_engine {
           const float *kbase = kv_k.data() + (l * n_kv + kh) * n_ctx * dh;
           const float *vbase = kv_v.data() + (l * n_kv + kh) * n_ctx * dh;
           for (size_t p = 0; p <= pos; p++) {
-            float s = 0.0f;
-            for (size_t d = 0; d < dh; d++) s += q[qbase + d * b] * kbase[p * dh + d];
+            float s;
+            if (b == 1) {
+              s = dot_neon(q.data() + qbase, kbase + p * dh, dh);
+            } else {
+              s = 0.0f;
+              for (size_t d = 0; d < dh; d++) s += q[qbase + d * b] * kbase[p * dh + d];
+            }
             s = s * scale;
             scores[p] = s;
             if (s > maxs) maxs = s;
@@ -1093,9 +1129,10 @@ struct pko_engine {
             sum += e;
           }
           float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
-          for (size_t d = 0; d < dh; d++) {
+          for (size_t d = 0; d < dh; d++) {  // f32_axpy per position, zero weights skipped
             float acc = 0.0f;
-            for (size_t p = 0; p <= pos; p++) acc += scores[p] * vbase[p * dh + d];
+            for (size_t p = 0; p <= pos; p++)
+              if (scores[p] != 0.0f) acc += scores[p] * vbase[p * dh + d];
             attn[(h * dh + d) * b + bi] = acc * inv;
           }
         }

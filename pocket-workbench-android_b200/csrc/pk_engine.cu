@@ -282,13 +282,12 @@ int Engine::load(const char *path) {
   // ---- activations and scratch (one arena)
   const size_t B = max_batch_, ne = c.n_embd, ff = c.n_ff;
   const size_t kmax = std::max(std::max(ne, ff), qdim);
-  att_nchunk_ = (n_ctx_ + ATTN_CHUNK - 1) / ATTN_CHUNK;
   const size_t H = c.n_head, dh = c.head_dim;
   const std::vector<size_t> sizes = {
       B * ne * 4, B * qdim * 4, B * kdim * 4, B * kdim * 4, B * qdim * 4,  // x q k v attn
       B * ff * 4, B * ff * 4, B * ff * 4, (size_t)vocab_ * 4,            // gate up h logits
       B * kmax, B * (kmax / 32) * 4, B * (kmax / 32) * 4,                  // act q d s
-      B * H * n_ctx_ * 4, B * H * att_nchunk_ * 4, B * H * att_nchunk_ * 4, B * H * att_nchunk_ * dh * 4,
+      B * H * n_ctx_ * 4,                                                  // attention scores
       64 * 4, 64 * 4, 16, (size_t)n_ctx_ * 4 + 16, 16};                 // ids pos tok hist step
   size_t arena = 0;
   for (size_t s : sizes) arena += a256(s);
@@ -304,7 +303,7 @@ int Engine::load(const char *path) {
   x_ = (float *)take(); q_ = (float *)take(); k_ = (float *)take(); v_ = (float *)take(); attn_ = (float *)take();
   gate_ = (float *)take(); up_ = (float *)take(); h_ = (float *)take(); logits_ = (float *)take();
   act_.q = (int8_t *)take(); act_.d = (float *)take(); act_.s = (int32_t *)take();
-  att_scores_ = (float *)take(); att_cmax_ = (float *)take(); att_csum_ = (float *)take(); att_cacc_ = (float *)take();
+  att_scores_ = (float *)take();
   d_ids_ = (uint32_t *)take(); d_pos_ = (int *)take(); d_tok_ = (uint32_t *)take(); d_hist_ = (uint32_t *)take();
   d_step_ = (int *)take();
 
@@ -384,7 +383,7 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable) {
   AttnArgs at{};
   at.q = q_; at.pos = d_pos_; at.out = attn_; at.b = b; at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh;
   at.n_ctx = n_ctx_; at.scale = 1.0f / sqrtf((float)dh);
-  at.scores = att_scores_; at.cmax = att_cmax_; at.csum = att_csum_; at.cacc = att_cacc_; at.n_chunk = att_nchunk_;
+  at.scores = att_scores_;
   for (int l = 0; l < c.n_layer; l++) {
     if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
     const LayerDev &L = layers_[l];
@@ -401,7 +400,7 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable) {
                            (qdim + 2 * kdim) * f4,
            launch_qkv_b1(qa, st_));
       if (l == 0) dump("Qrope-0", q_, (size_t)qdim);
-      PROF("attention(3 kernels)", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, st_));
+      PROF("k_attn", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, st_));
       B1Src so;
       so.x = attn_;
       PROF("k_mv_b1", mat_stream_bytes(L.o) + qdim * f4 + 2 * ne * f4, launch_mv_b1(L.o, so, x_, true, st_));

@@ -75,8 +75,7 @@ class Engine {
   float *x_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *attn_ = nullptr;
   float *gate_ = nullptr, *up_ = nullptr, *h_ = nullptr, *logits_ = nullptr;
   Q8Dev act_;
-  float *att_scores_ = nullptr, *att_cmax_ = nullptr, *att_csum_ = nullptr, *att_cacc_ = nullptr;
-  int att_nchunk_ = 0;
+  float *att_scores_ = nullptr;
   uint32_t *d_ids_ = nullptr, *d_tok_ = nullptr, *d_hist_ = nullptr;
   int *d_pos_ = nullptr, *d_step_ = nullptr;
   // pinned host staging

@@ -298,15 +298,49 @@ cudaError_t launch_q8(const float *x, long xs_e, long xs_l, int k, int b, Q8Dev 
   return cudaGetLastError();
 }
 
+// Sum of squares in the reference's b > 1 order (model.rs:813-817): one
+// sequential unfused chain.  Result broadcast through red[32].
+__device__ float sum_sq_seq(const float *__restrict__ x, int n, float *red) {
+  if (threadIdx.x == 0) {
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < n; i++) ss = fadd(ss, fmul(x[i], x[i]));
+    red[32] = ss;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Sum of squares in the reference's b == 1 order (simd.rs:47-64 f32_sum_sq):
+// eight FMA chains over x[8t + l], lanes l and l + 4 added, then a pairwise
+// horizontal add, then an unfused tail.
+__device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
+  const int tid = threadIdx.x, n8 = n / 8 * 8;
+  if (tid < 8) {
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int i = tid; i < n8; i += 8) acc = __fmaf_rn(x[i], x[i], acc);
+    red[tid] = acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const float c0 = fadd(red[0], red[4]), c1 = fadd(red[1], red[5]), c2 = fadd(red[2], red[6]),
+                c3 = fadd(red[3], red[7]);
+    float s = fadd(fadd(c0, c1), fadd(c2, c3));
+    for (int i = n8; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
+    red[32] = s;
+  }
+  __syncthreads();
+  return red[32];
+}
+
 // RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn) {
   __shared__ float red[40];
   const int bi = blockIdx.x;
   const float *xr = x + (long)bi * k;
-  float part = 0.0f;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) part = fadd(part, fmul(xr[i], xr[i]));
-  const float ss = block_sum(part, red);
+  const float ss = sum_sq_seq(xr, k, red);
   const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
   const int nb = k >> 5, lane = threadIdx.x & 31;
   for (int blk = threadIdx.x >> 5; blk < nb; blk += blockDim.x >> 5) {
@@ -562,13 +596,8 @@ __device__ void act_prologue(const B1Src &src, int k, const B1Smem &m) {
     return;
   }
   float scale = 1.0f;
-  if (src.nw) {
-    float part = 0.0f;
-    for (int i = tid; i < k; i += blockDim.x) {
-      const float v = src.x[i];
-      part = fadd(part, fmul(v, v));
-    }
-    const float ss = block_sum(part, m.red);
+  if (src.nw) {  // model.rs:791-810: the b == 1 rmsnorm
+    const float ss = sum_sq_neon(src.x, k, m.red);
     scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), src.eps)));
   }
   for (int blk = warp; blk < nb; blk += blockDim.x >> 5) {
@@ -818,104 +847,89 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cuda
 }
 
 // ------------------------------------------------------------ attention
-// Three passes over position chunks of ATTN_CHUNK:
-//   1. scores s_p = (q . k_p) * scale, a sequential dh-long dot per thread
-//      (bit-identical to model.rs:1015-1021), plus each chunk's maximum;
-//   2. e_p = exp(s_p - M) with the global maximum M (model.rs:1041-1044),
-//      chunk sums of e_p and chunk partials of sum_p e_p * v_p;
-//   3. combine chunks, out = acc * (1/sum) (model.rs:1046, 1078-1084).
-// Only the grouping of the two sums differs from the reference's single
-// sequential loop.
-__global__ void __launch_bounds__(ATTN_CHUNK) k_attn_scores(AttnArgs a) {
+// One CTA per (token, head), the reference's exact arithmetic
+// (model.rs:993-1087, aarch64 build):
+//   s_p = dot(q, k_p) * scale; for b == 1 the dot is f32_dot's order (two
+//         4-lane unfused accumulators reduced pairwise, simd.rs:19-43), for
+//         b > 1 one sequential chain (model.rs:1028-1033);
+//   M   = max_p s_p (order-free);  e_p = exp(s_p - M);
+//   sum = sequential over p;  inv = sum > 0 ? 1/sum : 0;
+//   out[d] = (sequential over p, zero weights skipped, of e_p * v_p[d]) * inv.
+// Every thread below dh owns one d and runs its chain over p; one more
+// thread runs the sum chain.  Scores live in the per-(token, head) scratch
+// row, so any context length fits.
+__global__ void k_attn(AttnArgs a, int dot8) {
   __shared__ float qs[256];
   __shared__ float red[40];
-  const int group = a.n_head / a.n_kv, tid = threadIdx.x;
-  const long n_items = (long)a.b * a.n_head * a.n_chunk;
-  for (long it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int c = (int)(it % a.n_chunk);
-    const long r = it / a.n_chunk;
-    const int h = (int)(r % a.n_head), bi = (int)(r / a.n_head);
-    const int pos = a.pos[bi];
-    if (c > pos / ATTN_CHUNK) continue;
-    __syncthreads();
-    for (int d = tid; d < a.dh; d += blockDim.x) qs[d] = a.q[((long)bi * a.n_head + h) * a.dh + d];
-    __syncthreads();
-    const int p = c * ATTN_CHUNK + tid;
-    float s = -INFINITY;
-    if (p <= pos) {
-      const float *kr = a.kcache + ((size_t)(h / group) * a.n_ctx + p) * a.dh;
-      float acc = 0.0f;
-      for (int d = 0; d < a.dh; d += 4) {
-        const float4 kv = *reinterpret_cast<const float4 *>(kr + d);
-        acc = fadd(acc, fmul(qs[d], kv.x));
-        acc = fadd(acc, fmul(qs[d + 1], kv.y));
-        acc = fadd(acc, fmul(qs[d + 2], kv.z));
-        acc = fadd(acc, fmul(qs[d + 3], kv.w));
-      }
-      s = fmul(acc, a.scale);
-      a.scores[((long)bi * a.n_head + h) * a.n_ctx + p] = s;
-    }
-    const float mx = block_max(s, red);
-    if (tid == 0) a.cmax[((long)bi * a.n_head + h) * a.n_chunk + c] = mx;
-  }
-}
-
-__global__ void __launch_bounds__(ATTN_CHUNK) k_attn_pv(AttnArgs a) {
-  __shared__ float e[ATTN_CHUNK];
-  __shared__ float red[40];
-  const int group = a.n_head / a.n_kv, tid = threadIdx.x;
-  const long n_items = (long)a.b * a.n_head * a.n_chunk;
-  for (long it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int c = (int)(it % a.n_chunk);
-    const long r = it / a.n_chunk;
-    const int h = (int)(r % a.n_head), bi = (int)(r / a.n_head);
-    const int pos = a.pos[bi];
-    const int nc = pos / ATTN_CHUNK + 1;
-    if (c >= nc) continue;
-    const long hb = (long)bi * a.n_head + h;
-    float M = -INFINITY;
-    for (int j = 0; j < nc; j++) {
-      const float v = a.cmax[hb * a.n_chunk + j];
-      M = v > M ? v : M;
-    }
-    const int p = c * ATTN_CHUNK + tid;
-    float ev = 0.0f;
-    if (p <= pos) ev = expf_cr(fsub(a.scores[hb * a.n_ctx + p], M));
-    __syncthreads();
-    e[tid] = ev;
-    const float l = block_sum(ev, red);
-    if (tid == 0) a.csum[hb * a.n_chunk + c] = l;
-    const int np = min(ATTN_CHUNK, pos + 1 - c * ATTN_CHUNK);
-    for (int d = tid; d < a.dh; d += blockDim.x) {
-      const float *vr = a.vcache + ((size_t)(h / group) * a.n_ctx + (size_t)c * ATTN_CHUNK) * a.dh + d;
-      float acc = 0.0f;
-      for (int j = 0; j < np; j++) acc = fadd(acc, fmul(e[j], vr[(size_t)j * a.dh]));
-      a.cacc[(hb * a.n_chunk + c) * a.dh + d] = acc;
-    }
-  }
-}
-
-__global__ void k_attn_combine(AttnArgs a) {
-  const int h = blockIdx.x, bi = blockIdx.y;
-  const int nc = a.pos[bi] / ATTN_CHUNK + 1;
+  __shared__ float s_inv;
+  const int h = blockIdx.x, bi = blockIdx.y, tid = threadIdx.x, dh = a.dh;
+  const int kh = h / (a.n_head / a.n_kv);
+  const int pos = a.pos[bi];
   const long hb = (long)bi * a.n_head + h;
-  float sum = 0.0f;
-  for (int c = 0; c < nc; c++) sum = fadd(sum, a.csum[hb * a.n_chunk + c]);
-  const float inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
-  for (int d = threadIdx.x; d < a.dh; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int c = 0; c < nc; c++) acc = fadd(acc, a.cacc[(hb * a.n_chunk + c) * a.dh + d]);
-    a.out[hb * a.dh + d] = fmul(acc, inv);
+  for (int d = tid; d < dh; d += blockDim.x) qs[d] = a.q[hb * dh + d];
+  __syncthreads();
+  const float *kb = a.kcache + (size_t)kh * a.n_ctx * dh;
+  const float *vb = a.vcache + (size_t)kh * a.n_ctx * dh;
+  float *sc = a.scores + hb * a.n_ctx;
+  float mx = -INFINITY;
+  for (int p = tid; p <= pos; p += blockDim.x) {
+    const float *kr = kb + (size_t)p * dh;
+    float s;
+    if (dot8) {
+      float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      int d = 0;
+      for (; d + 8 <= dh; d += 8) {
+        const float4 k0 = *reinterpret_cast<const float4 *>(kr + d);
+        const float4 k1 = *reinterpret_cast<const float4 *>(kr + d + 4);
+        c[0] = fadd(c[0], fmul(qs[d + 0], k0.x)); c[1] = fadd(c[1], fmul(qs[d + 1], k0.y));
+        c[2] = fadd(c[2], fmul(qs[d + 2], k0.z)); c[3] = fadd(c[3], fmul(qs[d + 3], k0.w));
+        c[4] = fadd(c[4], fmul(qs[d + 4], k1.x)); c[5] = fadd(c[5], fmul(qs[d + 5], k1.y));
+        c[6] = fadd(c[6], fmul(qs[d + 6], k1.z)); c[7] = fadd(c[7], fmul(qs[d + 7], k1.w));
+      }
+      s = fadd(fadd(c[0], c[1]), fadd(c[2], c[3]));
+      s = fadd(s, fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
+      for (; d < dh; d++) s = fadd(s, fmul(qs[d], kr[d]));
+    } else {
+      s = 0.0f;
+      for (int d = 0; d < dh; d += 4) {
+        const float4 kv = *reinterpret_cast<const float4 *>(kr + d);
+        s = fadd(s, fmul(qs[d], kv.x));
+        s = fadd(s, fmul(qs[d + 1], kv.y));
+        s = fadd(s, fmul(qs[d + 2], kv.z));
+        s = fadd(s, fmul(qs[d + 3], kv.w));
+      }
+    }
+    s = fmul(s, a.scale);
+    sc[p] = s;
+    mx = s > mx ? s : mx;
   }
+  const float M = block_max(mx, red);
+  for (int p = tid; p <= pos; p += blockDim.x) sc[p] = expf_cr(fsub(sc[p], M));
+  __syncthreads();
+  float acc = 0.0f;
+  if (tid < dh) {
+    const float *vr = vb + tid;
+#pragma unroll 8
+    for (int p = 0; p <= pos; p++) {
+      const float e = sc[p];
+      const float v = vr[(size_t)p * dh];
+      if (e != 0.0f) acc = fadd(acc, fmul(e, v));
+    }
+  }
+  if (tid == (dh < (int)blockDim.x ? dh : 0)) {
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int p = 0; p <= pos; p++) sum = fadd(sum, sc[p]);
+    s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+  }
+  __syncthreads();
+  if (tid < dh) a.out[hb * dh + tid] = fmul(acc, s_inv);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
-  const long items = (long)a.b * a.n_head * a.n_chunk;
-  const int grid = (int)std::max<long>(1, std::min<long>(items, (long)num_sms() * 8));
-  k_attn_scores<<<grid, ATTN_CHUNK, 0, st>>>(a);
-  k_attn_pv<<<grid, ATTN_CHUNK, 0, st>>>(a);
-  k_attn_combine<<<dim3(a.n_head, a.b), std::min(a.dh, 256), 0, st>>>(a);
+  const int threads = a.dh < 128 ? 128 : 256;
+  k_attn<<<dim3(a.n_head, a.b), threads, 0, st>>>(a, a.b == 1 ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -94,14 +94,8 @@ struct AttnArgs {
   float *out;          // [b][n_head * dh]
   int b, n_head, n_kv, dh, n_ctx;
   float scale;
-  // scratch
-  float *scores;       // [b][n_head][n_ctx]
-  float *cmax;         // [b][n_head][n_chunk]
-  float *csum;         // [b][n_head][n_chunk]
-  float *cacc;         // [b][n_head][n_chunk][dh]
-  int n_chunk;         // ceil(n_ctx / ATTN_CHUNK)
+  float *scores;       // scratch [b][n_head][n_ctx]
 };
-constexpr int ATTN_CHUNK = 128;
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 
 // First index of the maximum (sampler.rs:26-36); NaNs never win.
