@@ -66,6 +66,11 @@ int pk_supports(uint32_t ttype);
 
 /* ---------------------------------------------------------------- op level */
 
+/* The device exp used by softmax and SwiGLU: bit-identical to the C library's
+ * expf, which the reference's f32::exp calls (model.rs:1042, 1113). Exported
+ * so it can be verified.  x and out are device arrays of n floats. */
+int pk_expf(const float *x, float *out, int n, void *stream);
+
 /* Quantised activations, Q8Act layout (quant_int.rs:3-10), device memory:
  *   q   int8  [b][k]        (lane-major)
  *   d   float [b][k / 32]

@@ -1479,6 +1479,10 @@ int pko_generate(pko_engine *e, const uint32_t *prompt, size_t n, size_t max_tok
   return 0;
 }
 
+void pko_expf_batch(const float *x, float *out, size_t n) {
+  for (size_t i = 0; i < n; i++) out[i] = expf(x[i]);
+}
+
 void pko_request_stop(void) { g_stop.store(true); }
 void pko_clear_stop(void) { g_stop.store(false); }
 

@@ -110,6 +110,9 @@ size_t pko_engine_dump(pko_engine *e, const char *name, float *out, size_t cap);
 void pko_request_stop(void);
 void pko_clear_stop(void);
 
+/* The C library's expf over an array (f32::exp in the reference). */
+void pko_expf_batch(const float *x, float *out, size_t n);
+
 /* sampler.rs */
 uint32_t pko_sample(float *logits, size_t n, float temp, float top_p, uint64_t *rng_state);
 uint64_t pko_rng_new(uint64_t seed);

@@ -69,6 +69,7 @@ def lib():
         L.pko_engine_set_debug.argtypes = [P, C.c_int]
         L.pko_engine_dump.argtypes = [P, C.c_char_p, P, sz]
         L.pko_engine_dump.restype = sz
+        L.pko_expf_batch.argtypes = [P, P, sz]
         L.pko_sample.argtypes = [P, sz, C.c_float, C.c_float, C.POINTER(C.c_uint64)]
         L.pko_sample.restype = C.c_uint32
         L.pko_rng_new.argtypes = [C.c_uint64]
@@ -266,6 +267,13 @@ class Engine:
             "gen_ms": st.gen_ms,
             "stop": st.stop.decode(),
         }
+
+
+def expf_batch(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().pko_expf_batch(_p(x), _p(out), x.size)
+    return out
 
 
 def request_stop():

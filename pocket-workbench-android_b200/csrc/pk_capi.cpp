@@ -156,6 +156,13 @@ int pk_q8_quantize(const float *x, int k, int b, pk_q8act *act, void *stream) {
   return PK_OK;
 }
 
+int pk_expf(const float *x, float *out, int n, void *stream) {
+  if (!x || !out || n < 0) return set_error(PK_ERR_INVALID, "pk_expf: bad arguments");
+  if (n == 0) return PK_OK;
+  CK(launch_expf(x, out, n, (cudaStream_t)stream));
+  return PK_OK;
+}
+
 size_t pk_packed_bytes(uint32_t ttype, int k, int n_rows) {
   if (!type_is_matvec((int)ttype) || k <= 0 || n_rows <= 0) return 0;
   return packed_bytes((int)ttype, k, n_rows);

@@ -25,11 +25,45 @@ __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b)
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 
-// exp for the f32 paths: computed in double and rounded once, so it is the
-// correctly rounded expf except in vanishingly rare cases.  The reference's
-// f32::exp resolves to the C library's expf (< 0.51 ulp), so the two agree
-// on essentially every input.
-__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+// expf as the C library computes it (the function Rust's f32::exp calls):
+// the published table-driven method -- x * 32/ln2 = k + r with |r| <= 1/2,
+// 2^(k/32) from a 32-entry table, 2^(r/32) from a cubic, all in double with
+// fused multiply-adds, one rounding to float at the end.  The table is
+// 2^(i/32) correctly rounded (minus i << 47 in the bit pattern); the cubic's
+// coefficients are the method's minimax constants.  This evaluation returns
+// the same bits as the host C library for every non-NaN float (checked over
+// all 2^32 inputs), which the parity of softmax and SwiGLU depends on.
+static __constant__ unsigned long long kExp2Tab[32] = {
+    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
+    0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
+    0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
+    0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL,
+    0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL,
+    0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
+    0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
+    0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL,
+};
+
+__device__ __forceinline__ float expf_lib(float x) {
+  if (isnan(x)) return x + x;
+  if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);  // overflow
+  if (x < -0x1.9fe368p6f) return 0.0f;                       // underflow
+  const double kInvLn2N = 0x1.71547652b82fep+0 * 32.0, kShift = 0x1.8p+52;
+  const double kC0 = 0x1.c6af84b912394p-5 / 32768.0, kC1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
+               kC2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double xd = (double)x;
+  double kd = __fma_rn(kInvLn2N, xd, kShift);
+  const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+  kd = __dsub_rn(kd, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const double s = __longlong_as_double((long long)(kExp2Tab[ki & 31] + (ki << 47)));
+  const double z = __fma_rn(kC0, r, kC1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __fma_rn(kC2, r, 1.0);
+  y = __fma_rn(z, r2, y);
+  y = __dmul_rn(y, s);
+  return __double2float_rn(y);
+}
 
 // Streaming 16-byte load of weights (read once per token): no L1 allocation.
 __device__ __forceinline__ uint4 ldw16(const void *p) {
@@ -38,6 +72,20 @@ __device__ __forceinline__ uint4 ldw16(const void *p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
+}
+
+// Programmatic dependent launch.  Every kernel calls pdl_trigger() first (so
+// the next kernel in the stream may be scheduled once all of this grid's CTAs
+// are running) and pdl_wait() before it touches anything an earlier kernel
+// wrote.  griddepcontrol.wait returns once the preceding grids have completed
+// and their memory is visible; without a programmatic launch it is a no-op.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Hint: stream [p, p + bytes) from HBM into L2 (bytes a multiple of 16, p
+// 16-byte aligned, the range inside the allocation).
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  if (bytes >= 16) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {

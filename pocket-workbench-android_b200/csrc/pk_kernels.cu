@@ -99,9 +99,31 @@ static int num_sms() {
   return n;
 }
 
+
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while its predecessor in the stream still runs; every kernel here orders its
+// dependent reads with pdl_wait() (griddepcontrol.wait).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ------------------------------------------------------------ packing
 __global__ void k_pack(int t, const uint8_t *__restrict__ raw, size_t row_bytes, int k, int rows,
                        uint8_t *__restrict__ q, uint16_t *__restrict__ d) {
+  pdl_trigger();
+  pdl_wait();
   const int be = (t == T_Q4_K || t == T_Q6_K) ? 256 : 32;
   const int nblk = k / be;
   const long n = (long)rows * nblk;
@@ -143,8 +165,7 @@ cudaError_t launch_pack(int t, const void *raw, size_t row_bytes, int k, int row
   long n = (long)rows * (k / be);
   int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 16);
   if (grid < 1) grid = 1;
-  k_pack<<<grid, 256, 0, st>>>(t, (const uint8_t *)raw, row_bytes, k, rows, (uint8_t *)w.q, (uint16_t *)w.d);
-  return cudaGetLastError();
+  return launch(k_pack, dim3(grid), dim3(256), 0, st, t, (const uint8_t *)raw, row_bytes, k, rows, (uint8_t *)w.q, (uint16_t *)w.d);
 }
 
 // ------------------------------------------------------------ dequant rows
@@ -234,6 +255,8 @@ __device__ float dequant_elem(int t, const uint8_t *row, int j) {
 
 __global__ void k_dequant_rows(int t, const uint8_t *__restrict__ raw, size_t row_bytes, int k,
                                const uint32_t *__restrict__ ids, float *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const long r = ids ? (long)ids[blockIdx.x] : (long)blockIdx.x;
   const uint8_t *row = raw + r * row_bytes;
   for (int j = threadIdx.x; j < k; j += blockDim.x) out[(long)blockIdx.x * k + j] = dequant_elem(t, row, j);
@@ -242,8 +265,7 @@ __global__ void k_dequant_rows(int t, const uint8_t *__restrict__ raw, size_t ro
 cudaError_t launch_dequant_rows(int t, const void *raw, size_t row_bytes, int k, const uint32_t *ids, int n,
                                 float *out, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_dequant_rows<<<n, 256, 0, st>>>(t, (const uint8_t *)raw, row_bytes, k, ids, out);
-  return cudaGetLastError();
+  return launch(k_dequant_rows, dim3(n), dim3(256), 0, st, t, (const uint8_t *)raw, row_bytes, k, ids, out);
 }
 
 // ------------------------------------------------------------ reductions
@@ -280,6 +302,8 @@ __device__ float block_max(float v, float *red) {
 
 // ------------------------------------------------------------ Q8 quantiser
 __global__ void k_q8(const float *__restrict__ x, long xs_e, long xs_l, int k, int b, Q8Dev act) {
+  pdl_trigger();
+  pdl_wait();
   const int nb = k >> 5, lane = threadIdx.x & 31;
   const long nwarp_total = (long)b * nb;
   const long wstride = ((long)gridDim.x * blockDim.x) >> 5;
@@ -294,8 +318,7 @@ cudaError_t launch_q8(const float *x, long xs_e, long xs_l, int k, int b, Q8Dev 
   long warps = (long)b * (k / 32);
   int grid = (int)std::min<long>((warps * 32 + 255) / 256, (long)num_sms() * 8);
   if (grid < 1) grid = 1;
-  k_q8<<<grid, 256, 0, st>>>(x, xs_e, xs_l, k, b, act);
-  return cudaGetLastError();
+  return launch(k_q8, dim3(grid), dim3(256), 0, st, x, xs_e, xs_l, k, b, act);
 }
 
 // Sum of squares in the reference's b > 1 order (model.rs:813-817): one
@@ -338,6 +361,8 @@ __device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn) {
   __shared__ float red[40];
+  pdl_trigger();
+  pdl_wait();
   const int bi = blockIdx.x;
   const float *xr = x + (long)bi * k;
   const float ss = sum_sq_seq(xr, k, red);
@@ -353,8 +378,7 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st) {
-  k_rmsnorm_q8<<<b, 256, 0, st>>>(x, nw, eps, k, act, xn);
-  return cudaGetLastError();
+  return launch(k_rmsnorm_q8, dim3(b), dim3(256), 0, st, x, nw, eps, k, act, xn);
 }
 
 // ------------------------------------------------------------ matvec core
@@ -541,6 +565,25 @@ __device__ float tile_b1(const DevTensor &W, int r0, int nr, const ActRef &A, fl
   return acc;
 }
 
+// L2 prefetch of rows [r0, r0+nr) of W (quant bytes and per-block scales).
+// Tile byte ranges of the device layout start on 16-byte boundaries.
+__device__ void prefetch_rows(const DevTensor &W, int r0, int nr) {
+  size_t rq = 0, rd = 0;
+  switch (W.type) {
+    case T_Q4_K: rq = (size_t)(W.k >> 8) * 144; break;
+    case T_Q6_K: rq = (size_t)(W.k >> 8) * 208; rd = (size_t)(W.k >> 8) * 2; break;
+    case T_Q8_0: rq = (size_t)W.k; rd = (size_t)(W.k >> 5) * 2; break;
+    case T_Q4_0: rq = (size_t)(W.k >> 1); rd = (size_t)(W.k >> 5) * 2; break;
+    default: return;
+  }
+  const uint8_t *q = W.q + (size_t)r0 * rq;
+  if (((uintptr_t)q & 15) == 0) prefetch_l2(q, (uint32_t)(rq * nr));
+  if (rd) {
+    const uint8_t *d = reinterpret_cast<const uint8_t *>(W.d) + (size_t)r0 * rd;
+    if (((uintptr_t)d & 15) == 0) prefetch_l2(d, (uint32_t)(rd * nr));
+  }
+}
+
 __device__ float tile_b1_any(const DevTensor &W, int r0, int nr, const ActRef &A, float *Tsm) {
   switch (W.type) {
     case T_Q4_K: return tile_b1<T_Q4_K>(W, r0, nr, A, Tsm);
@@ -610,10 +653,15 @@ __device__ void act_prologue(const B1Src &src, int k, const B1Smem &m) {
 
 __global__ void __launch_bounds__(B1_THREADS) k_mv_b1(DevTensor W, B1Src src, float *__restrict__ out, int add) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int tiles = (W.rows + B1_RT - 1) / B1_RT;
+  if (threadIdx.x == 0)  // weights are constant: stream them in while the previous kernel runs
+    for (int t = blockIdx.x, i = 0; t < tiles && i < 2; t += gridDim.x, i++)
+      prefetch_rows(W, t * B1_RT, min(B1_RT, W.rows - t * B1_RT));
+  pdl_trigger();
+  pdl_wait();
   const B1Smem m = b1_carve(smem_raw, W.k);
   act_prologue(src, W.k, m);
   const ActRef A{m.q, m.d, m.s};
-  const int tiles = (W.rows + B1_RT - 1) / B1_RT;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = t * B1_RT, nr = min(B1_RT, W.rows - r0);
     const float acc = tile_b1_any(W, r0, nr, A, m.T);
@@ -643,18 +691,26 @@ cudaError_t launch_mv_b1(const DevTensor &w, const B1Src &src, float *out, bool 
   cudaError_t e = set_smem(k_mv_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (w.rows + B1_RT - 1) / B1_RT;
-  k_mv_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(w, src, out, add ? 1 : 0);
-  return cudaGetLastError();
+  return launch(k_mv_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, w, src, out, add ? 1 : 0);
 }
 
 // q/k/v for one token + RoPE (model.rs:953-979) + KV write (model.rs:984-992).
 __global__ void __launch_bounds__(B1_THREADS) k_qkv_b1(QkvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int tq = (a.wq.rows + B1_RT - 1) / B1_RT, tk = (a.wk.rows + B1_RT - 1) / B1_RT,
+            tv = (a.wv.rows + B1_RT - 1) / B1_RT;
+  if (threadIdx.x == 0)
+    for (int t = blockIdx.x, i = 0; t < tq + tk + tv && i < 2; t += gridDim.x, i++) {
+      const int seg = t < tq ? 0 : (t < tq + tk ? 1 : 2);
+      const int tt = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
+      const DevTensor &W = seg == 0 ? a.wq : (seg == 1 ? a.wk : a.wv);
+      prefetch_rows(W, tt * B1_RT, min(B1_RT, W.rows - tt * B1_RT));
+    }
+  pdl_trigger();
+  pdl_wait();
   const B1Smem m = b1_carve(smem_raw, a.wq.k);
   act_prologue(a.src, a.wq.k, m);
   const ActRef A{m.q, m.d, m.s};
-  const int tq = (a.wq.rows + B1_RT - 1) / B1_RT, tk = (a.wk.rows + B1_RT - 1) / B1_RT,
-            tv = (a.wv.rows + B1_RT - 1) / B1_RT;
   const int pos = *a.pos;
   const int tid = threadIdx.x;
   for (int t = blockIdx.x; t < tq + tk + tv; t += gridDim.x) {
@@ -689,24 +745,30 @@ cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st) {
   cudaError_t e = set_smem(k_qkv_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (a.wq.rows + B1_RT - 1) / B1_RT + (a.wk.rows + B1_RT - 1) / B1_RT + (a.wv.rows + B1_RT - 1) / B1_RT;
-  k_qkv_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch(k_qkv_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, a);
 }
 
 // gate/up for one token + SwiGLU (model.rs:1105-1115).
 __global__ void __launch_bounds__(B1_THREADS) k_gateup_b1(DevTensor wg, DevTensor wu, B1Src src, float *__restrict__ h) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
+  if (threadIdx.x == 0)
+    for (int t = blockIdx.x, i = 0; t < tiles && i < 2; t += gridDim.x, i++) {
+      prefetch_rows(wg, t * B1_RT, min(B1_RT, wg.rows - t * B1_RT));
+      prefetch_rows(wu, t * B1_RT, min(B1_RT, wu.rows - t * B1_RT));
+    }
+  pdl_trigger();
+  pdl_wait();
   const B1Smem m = b1_carve(smem_raw, wg.k);
   act_prologue(src, wg.k, m);
   const ActRef A{m.q, m.d, m.s};
-  const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = t * B1_RT, nr = min(B1_RT, wg.rows - r0);
     const float ag = tile_b1_any(wg, r0, nr, A, m.T);
     const float au = tile_b1_any(wu, r0, nr, A, m.T);
     if ((int)threadIdx.x < nr) {
       const float g = fadd(0.0f, ag), u = fadd(0.0f, au);
-      const float s = fdiv(g, fadd(1.0f, expf_cr(-g)));
+      const float s = fdiv(g, fadd(1.0f, expf_lib(-g)));
       h[r0 + threadIdx.x] = fmul(s, u);
     }
   }
@@ -719,8 +781,7 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
   cudaError_t e = set_smem(k_gateup_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
-  k_gateup_b1<<<b1_grid(tiles, smem), B1_THREADS, smem, st>>>(wg, wu, src, h);
-  return cudaGetLastError();
+  return launch(k_gateup_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, wg, wu, src, h);
 }
 
 // ------------------------------------------------------------ multi-lane matvec
@@ -772,6 +833,11 @@ __global__ void __launch_bounds__(L_THREADS) k_mv_lanes(DevTensor W, Q8Dev act, 
                                                          int add) {
   __shared__ float Tsm[L_TW * L_LB * L_RT];
   const int tiles = (W.rows + L_RT - 1) / L_RT;
+  if (threadIdx.x == 0)
+    for (int t = blockIdx.x, i = 0; t < tiles && i < 2; t += gridDim.x, i++)
+      prefetch_rows(W, t * L_RT, min(L_RT, W.rows - t * L_RT));
+  pdl_trigger();
+  pdl_wait();
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = t * L_RT, nr = min(L_RT, W.rows - r0);
     for (int l0 = 0; l0 < act.b; l0 += L_LB) {
@@ -791,13 +857,14 @@ cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, lo
   if (!type_is_matvec(w.type) || act.k != w.k || act.b < 1) return cudaErrorInvalidValue;
   const int tiles = (w.rows + L_RT - 1) / L_RT;
   const int grid = std::max(1, std::min(tiles, num_sms() * 4));
-  k_mv_lanes<<<grid, L_THREADS, 0, st>>>(w, act, out, os_row, os_lane, add ? 1 : 0);
-  return cudaGetLastError();
+  return launch(k_mv_lanes, dim3(grid), dim3(L_THREADS), 0, st, w, act, out, os_row, os_lane, add ? 1 : 0);
 }
 
 // ------------------------------------------------------------ RoPE + KV, SwiGLU
 __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *pos, const float *rc, const float *rs,
                           int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc) {
+  pdl_trigger();
+  pdl_wait();
   const int bi = blockIdx.x;
   const int p = pos[bi];
   const int qdim = n_head * dh, kdim = n_kv * dh;
@@ -829,21 +896,33 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rc,
                            const float *rs, int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc,
                            cudaStream_t st) {
-  k_rope_kv<<<b, 256, 0, st>>>(q, k, v, pos, rc, rs, half, dh, n_head, n_kv, n_ctx, kc, vc);
-  return cudaGetLastError();
+  return launch(k_rope_kv, dim3(b), dim3(256), 0, st, q, k, v, pos, rc, rs, half, dh, n_head, n_kv, n_ctx, kc, vc);
 }
 
 __global__ void k_swiglu(const float *g, const float *u, float *h, long n) {
+  pdl_trigger();
+  pdl_wait();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const float gg = g[i];
-    h[i] = fmul(fdiv(gg, fadd(1.0f, expf_cr(-gg))), u[i]);
+    h[i] = fmul(fdiv(gg, fadd(1.0f, expf_lib(-gg))), u[i]);
   }
+}
+
+__global__ void k_expf(const float *x, float *out, long n) {
+  pdl_trigger();
+  pdl_wait();
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    out[i] = expf_lib(x[i]);
+}
+
+cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st) {
+  int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 16);
+  return launch(k_expf, dim3(std::max(grid, 1)), dim3(256), 0, st, x, out, n);
 }
 
 cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st) {
   int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 8);
-  k_swiglu<<<std::max(grid, 1), 256, 0, st>>>(g, u, h, n);
-  return cudaGetLastError();
+  return launch(k_swiglu, dim3(std::max(grid, 1)), dim3(256), 0, st, g, u, h, n);
 }
 
 // ------------------------------------------------------------ attention
@@ -864,6 +943,8 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   __shared__ float s_inv;
   const int h = blockIdx.x, bi = blockIdx.y, tid = threadIdx.x, dh = a.dh;
   const int kh = h / (a.n_head / a.n_kv);
+  pdl_trigger();
+  pdl_wait();
   const int pos = a.pos[bi];
   const long hb = (long)bi * a.n_head + h;
   for (int d = tid; d < dh; d += blockDim.x) qs[d] = a.q[hb * dh + d];
@@ -904,7 +985,7 @@ __global__ void k_attn(AttnArgs a, int dot8) {
     mx = s > mx ? s : mx;
   }
   const float M = block_max(mx, red);
-  for (int p = tid; p <= pos; p += blockDim.x) sc[p] = expf_cr(fsub(sc[p], M));
+  for (int p = tid; p <= pos; p += blockDim.x) sc[p] = expf_lib(fsub(sc[p], M));
   __syncthreads();
   float acc = 0.0f;
   if (tid < dh) {
@@ -929,14 +1010,15 @@ __global__ void k_attn(AttnArgs a, int dot8) {
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
   const int threads = a.dh < 128 ? 128 : 256;
-  k_attn<<<dim3(a.n_head, a.b), threads, 0, st>>>(a, a.b == 1 ? 1 : 0);
-  return cudaGetLastError();
+  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, a.b == 1 ? 1 : 0);
 }
 
 // ------------------------------------------------------------ argmax / feedback
 __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, int n, uint32_t *out) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_trigger();
+  pdl_wait();
   float bv = -INFINITY;
   int bi = INT_MAX;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -959,11 +1041,12 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, in
 }
 
 cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st) {
-  k_argmax<<<1, 1024, 0, st>>>(x, n, out_idx);
-  return cudaGetLastError();
+  return launch(k_argmax, dim3(1), dim3(1024), 0, st, x, n, out_idx);
 }
 
 __global__ void k_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t t = *tok;
   ids[0] = t;
   pos[0] += 1;
@@ -972,8 +1055,7 @@ __global__ void k_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t
 }
 
 cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st) {
-  k_advance<<<1, 1, 0, st>>>(tok, ids, pos, hist, step);
-  return cudaGetLastError();
+  return launch(k_advance, dim3(1), dim3(1), 0, st, tok, ids, pos, hist, step);
 }
 
 }  // namespace pk

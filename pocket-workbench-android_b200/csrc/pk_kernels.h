@@ -82,6 +82,8 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rope_cos,
                            const float *rope_sin, int half, int dh, int n_head, int n_kv, int n_ctx, float *kcache,
                            float *vcache, cudaStream_t st);
+// out[i] = expf_lib(x[i]) (the C library's expf, bit for bit).
+cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st);
 // SwiGLU over [n] elements: h = g / (1 + exp(-g)) * u.
 cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st);
 

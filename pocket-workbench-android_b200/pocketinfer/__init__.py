@@ -31,7 +31,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34),
 
 # Every function include/pk.h declares (checked by tests/test_capi_symbols.py).
 SYMBOLS = [
-    "pk_last_error", "pk_version", "pk_supports", "pk_q8_quantize", "pk_matmul", "pk_packed_bytes",
+    "pk_last_error", "pk_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_packed_bytes",
     "pk_pack_weights", "pk_matmul_packed", "pk_backend_new", "pk_backend_free", "pk_backend_selftest",
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
     "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position",
@@ -91,7 +91,7 @@ def lib():
     P, I, U32, SZ = C.c_void_p, C.c_int, C.c_uint32, C.c_size_t
     sig = {
         "pk_last_error": ([], C.c_char_p), "pk_version": ([], I), "pk_supports": ([U32], I),
-        "pk_q8_quantize": ([P, I, I, C.POINTER(Q8ActC), P], I),
+        "pk_q8_quantize": ([P, I, I, C.POINTER(Q8ActC), P], I), "pk_expf": ([P, P, I, P], I),
         "pk_matmul": ([U32, P, SZ, I, I, C.POINTER(Q8ActC), P, P], I),
         "pk_packed_bytes": ([U32, I, I], SZ),
         "pk_pack_weights": ([U32, P, SZ, I, I, P, P], I),
@@ -158,6 +158,16 @@ class Q8Act:
         self.d = torch.empty(max(1, b * (k // 32)), dtype=torch.float32, device=device)
         self.sum = torch.empty(max(1, b * (k // 32)), dtype=torch.int32, device=device)
         self.c = Q8ActC(self.q.data_ptr(), self.d.data_ptr(), self.sum.data_ptr(), k, b)
+
+
+def expf(x, stream=None):
+    """The device exp of softmax and SwiGLU (bit-identical to the C library's expf)."""
+    import torch
+
+    assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+    out = torch.empty_like(x)
+    _check(lib().pk_expf(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
+    return out
 
 
 def q8_quantize(x, k: int, b: int, stream=None) -> Q8Act:

@@ -200,3 +200,16 @@ def test_op_errors(pk):
     with pytest.raises(pk.PkError) as e:
         pk.matmul(synth.Q4_K, dev(np.zeros(144, np.uint8)), 64, 1, act)  # k not a multiple of 256
     assert e.value.code == 1
+
+
+def test_device_expf_matches_c_library(pk, oracle):
+    """The softmax/SwiGLU exp returns the C library's expf bits (f32::exp in the reference)."""
+    bits_all = np.arange(0, 1 << 32, 61, dtype=np.uint64).astype(np.uint32)  # ~70M patterns
+    x = bits_all.view(np.float32)
+    x = x[~np.isnan(x)]
+    hard = np.array([0x1.04845ep+5, -0x1.f8cbb2p+5, 88.72283, -103.97208, -87.33655, 0.0, -0.0,
+                     np.inf, -np.inf], np.float32)
+    x = np.concatenate([hard, x])
+    got = pk.expf(dev(x)).cpu().numpy()
+    want = oracle.expf_batch(x)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
