@@ -207,8 +207,8 @@ def test_device_expf_matches_c_library(pk, oracle):
     bits_all = np.arange(0, 1 << 32, 61, dtype=np.uint64).astype(np.uint32)  # ~70M patterns
     x = bits_all.view(np.float32)
     x = x[~np.isnan(x)]
-    hard = np.array([0x1.04845ep+5, -0x1.f8cbb2p+5, 88.72283, -103.97208, -87.33655, 0.0, -0.0,
-                     np.inf, -np.inf], np.float32)
+    hard = np.array([float.fromhex("0x1.04845ep+5"), float.fromhex("-0x1.f8cbb2p+5"), 88.72283,
+                     -103.97208, -87.33655, 0.0, -0.0, np.inf, -np.inf], np.float32)
     x = np.concatenate([hard, x])
     got = pk.expf(dev(x)).cpu().numpy()
     want = oracle.expf_batch(x)
