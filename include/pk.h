@@ -97,6 +97,23 @@ int pk_q8_quantize(const float *x, int k, int b, pk_q8act *act, void *stream);
 int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows,
               const pk_q8act *act, float *out, void *stream);
 
+/* pk_matmul that allocates no device memory.  No counterpart in the
+ * reference, which has no device allocator to avoid.  Same arguments and
+ * result as pk_matmul; the rows that pk_matmul packs into a temporary are
+ * packed into one fixed scratch array inside this library's device image
+ * instead, so a call needing more than PK_NOALLOC_SCRATCH_BYTES of packed
+ * rows (pk_packed_bytes) fails with PK_ERR_INVALID before anything runs.
+ * 16-byte aligned Q4_K rows are used in place and have no size limit.
+ * The first call on each device looks up the scratch's address with that
+ * device current (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  There is one scratch per device: calls that overlap in
+ * time (other streams, other host threads) race on it and must be
+ * serialised by the caller.  Nothing in the scratch needs to start at zero:
+ * the pack kernel writes every byte the matvec then reads. */
+#define PK_NOALLOC_SCRATCH_BYTES (16u << 20)
+int pk_matmul_noalloc(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows,
+                      const pk_q8act *act, float *out, void *stream);
+
 /* Device weight layout: bytes needed for n_rows x k of ttype (>= raw size). */
 size_t pk_packed_bytes(uint32_t ttype, int k, int n_rows);
 /* Raw GGUF blocks (device) -> device layout (device, 16-byte aligned). */

@@ -212,6 +212,29 @@ int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows
   return rc;
 }
 
+int pk_matmul_noalloc(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows, const pk_q8act *act,
+                      float *out, void *stream) {
+  int rc = check_matvec_shape(ttype, k, n_rows);
+  if (rc) return rc;
+  if (!q8_ok(act, k)) return set_error(PK_ERR_INVALID, "activation does not match k");
+  int be, bb;
+  type_block((int)ttype, &be, &bb);
+  if (row_bytes != (size_t)(k / be) * bb) return set_error(PK_ERR_INVALID, "row_bytes does not match k for this type");
+  if (!w || !out) return set_error(PK_ERR_INVALID, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (ttype == PK_TYPE_Q4_K && ((uintptr_t)w & 15) == 0)  // used in place: no scratch
+    return matmul_packed(ttype, w, k, n_rows, act, out, st);
+  const size_t need = packed_bytes((int)ttype, k, n_rows);
+  if (need > PK_NOALLOC_SCRATCH_BYTES)
+    return set_error(PK_ERR_INVALID, "pk_matmul_noalloc: these rows need " + std::to_string(need) +
+                                         " bytes of scratch, the fixed scratch holds " +
+                                         std::to_string((size_t)PK_NOALLOC_SCRATCH_BYTES));
+  void *scratch = nullptr;
+  CK(noalloc_scratch(&scratch));
+  CK(launch_pack((int)ttype, w, row_bytes, k, n_rows, scratch, st));
+  return matmul_packed(ttype, scratch, k, n_rows, act, out, st);
+}
+
 int pk_backend_new(int device, pk_backend **out) {
   if (!out) return set_error(PK_ERR_INVALID, "null out");
   int n = 0;

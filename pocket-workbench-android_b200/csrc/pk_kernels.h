@@ -105,4 +105,8 @@ cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t
 // Decode feedback on the device: ids[0] = *tok; pos[0] += 1; hist[*step] = *tok; *step += 1.
 cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st);
 
+// Device address of pk_matmul_noalloc's fixed scratch on the current device
+// (pk_noalloc.cu); looked up once per device.
+cudaError_t noalloc_scratch(void **ptr);
+
 }  // namespace pk

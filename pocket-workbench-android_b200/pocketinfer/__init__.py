@@ -31,7 +31,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34),
 
 # Every function include/pk.h declares (checked by tests/test_capi_symbols.py).
 SYMBOLS = [
-    "pk_last_error", "pk_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_packed_bytes",
+    "pk_last_error", "pk_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_matmul_noalloc", "pk_packed_bytes",
     "pk_pack_weights", "pk_matmul_packed", "pk_backend_new", "pk_backend_free", "pk_backend_selftest",
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
     "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position",
@@ -93,6 +93,7 @@ def lib():
         "pk_last_error": ([], C.c_char_p), "pk_version": ([], I), "pk_supports": ([U32], I),
         "pk_q8_quantize": ([P, I, I, C.POINTER(Q8ActC), P], I), "pk_expf": ([P, P, I, P], I),
         "pk_matmul": ([U32, P, SZ, I, I, C.POINTER(Q8ActC), P, P], I),
+        "pk_matmul_noalloc": ([U32, P, SZ, I, I, C.POINTER(Q8ActC), P, P], I),
         "pk_packed_bytes": ([U32, I, I], SZ),
         "pk_pack_weights": ([U32, P, SZ, I, I, P, P], I),
         "pk_matmul_packed": ([U32, P, I, I, C.POINTER(Q8ActC), P, P], I),
@@ -199,6 +200,20 @@ def pack_weights(ttype: int, w, k: int, n_rows: int, stream=None):
     packed = torch.empty(packed_bytes(ttype, k, n_rows), dtype=torch.uint8, device=w.device)
     _check(lib().pk_pack_weights(ttype, _ptr(w), row_bytes(ttype, k), k, n_rows, _ptr(packed), _stream(stream)))
     return packed
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def matmul_noalloc(ttype: int, w, k: int, n_rows: int, act: Q8Act, out=None, stream=None):
+    """matmul() without a device allocation: packs into the library's fixed scratch."""
+    import torch
+
+    if out is None:
+        out = torch.empty(n_rows * act.b, dtype=torch.float32, device=w.device)
+    _check(lib().pk_matmul_noalloc(ttype, _ptr(w), row_bytes(ttype, k), k, n_rows, C.byref(act.c), _ptr(out),
+                                   _stream(stream)))
+    return out
 
 
 def matmul_packed(ttype: int, packed, k: int, n_rows: int, act: Q8Act, out=None, stream=None):
