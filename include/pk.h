@@ -150,6 +150,8 @@ typedef struct {
   size_t weight_bytes;      /* device weight bytes (packed layout) */
   size_t kv_bytes;          /* device KV cache bytes */
   size_t stream_bytes;      /* weight + norm + embedding-row bytes one decode token reads */
+  int decode_kernels;       /* kernel launches per b == 1 decode step: 1 when the persistent
+                               decode kernel runs this model, else the per-op sequence */
 } pk_model_info;
 
 typedef struct {

@@ -1,0 +1,910 @@
+// pk_decode.cu -- persistent single-token decode kernel for sm_100a.
+//
+// Reference semantics (Aleinto97/pocket-workbench-android, rust/pocketinfer/src):
+//   forward_inner, one token       model.rs:833-1170
+//   Q8Act::prepare                 quant_int.rs:17-56
+//   lanes::* row dots              quant_int.rs:282-419
+//   rmsnorm (b == 1, f32_sum_sq)   model.rs:791-810, simd.rs:47-64
+//   rope                           model.rs:953-979
+//   attention (b == 1, f32_dot)    model.rs:993-1087, simd.rs:19-43
+//   swiglu / residuals             model.rs:1095-1125
+//   greedy sample                  sampler.rs:26-36
+//
+// Work split.  The grid has one CTA per SM and every CTA owns a fixed slice
+// of rows of every matrix (host-built chunk list).  Per CTA:
+//   warp 0, lane 0   producer: walks the chunk list (plus the K/V history of
+//                    the attention heads this CTA owns) and bulk-copies each
+//                    chunk into the next free ring slot (mbarrier complete_tx);
+//   warps 2..15      term warps: integer dots + float terms of a chunk into a
+//                    term buffer (two buffers, alternating);
+//   warp 1           chain warp: one lane per row adds that row's terms in
+//                    the reference's order and runs the epilogue.
+// Between the phases of a layer (qkv | attention | o | gate+up | down) the
+// consumers meet at a grid barrier; the producer does not, so the weights of
+// the next phases keep streaming in while the barrier resolves.
+//
+// Every wait is bounded (2 s); a wait that runs out records PK_ERR_TIMEOUT in
+// the error word, the CTA stops at its next barrier, and the producer waits
+// for its own copies in flight before it returns.
+#include <float.h>
+#include <limits.h>
+#include <math.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "pk.h"
+#include "pk_decode.h"
+#include "pk_device.cuh"
+#include "pk_quant.cuh"
+
+namespace pk {
+namespace {
+
+constexpr int CONS = DK_THREADS - 32;    // consumer threads (warps 1..15)
+constexpr int TERM_T = DK_THREADS - 64;  // term threads (warps 2..15)
+constexpr int NB_CONS = 1, NB_FULLT = 2, NB_EMPTYT = 4, NB_V = 6;
+constexpr unsigned long long WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the completion of phase `parity`; false on timeout or abort.
+__device__ bool mbar_wait(uint64_t *b, uint32_t parity, const volatile int *abort) {
+  if (mbar_test(b, parity)) return true;
+  const unsigned long long t0 = gtime();
+  for (;;) {
+    if (mbar_test(b, parity)) return true;
+    if (abort && *abort) return false;
+    if (gtime() - t0 > WAIT_NS) return false;
+  }
+}
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completion counted on mbarrier b.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   saddr(dst)),
+               "l"(src), "r"(bytes), "r"(saddr(b))
+               : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ const uint8_t *align16_down(const uint8_t *p) {
+  return (const uint8_t *)((uintptr_t)p & ~(uintptr_t)15);
+}
+
+// Shared memory layout (host and device agree through dk_layout).
+struct Layout {
+  size_t ring, full, empty, aq, ad, as, u, qh, red, flag, total;
+  int kmax, uf;
+};
+
+__host__ __device__ inline size_t up16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+__host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int n_ctx) {
+  Layout L;
+  int km = n_embd > n_ff ? n_embd : n_ff;
+  km = km > qdim ? km : qdim;
+  L.kmax = (km + 15) / 16 * 16;
+  int uf = 2 * DK_TS;
+  uf = uf > km ? uf : km;
+  uf = uf > n_ctx ? uf : n_ctx;
+  L.uf = (uf + 3) / 4 * 4;
+  size_t o = 0;
+  L.ring = o; o += (size_t)DK_NS * DK_SLOT;
+  L.full = o; o += DK_NS * 8;
+  L.empty = o; o += DK_NS * 8;
+  o = up16(o);
+  L.aq = o; o += up16(L.kmax);
+  L.ad = o; o += up16((size_t)L.kmax / 32 * 4);
+  L.as = o; o += up16((size_t)L.kmax / 32 * 4);
+  L.u = o; o += (size_t)L.uf * 4;
+  L.qh = o; o += 256 * 4;
+  L.red = o; o += 64 * 4;
+  L.flag = o; o += 16;
+  L.total = o;
+  return L;
+}
+
+struct Smem {
+  uint8_t *ring;
+  uint64_t *full, *empty;
+  int8_t *aq;
+  float *ad;
+  int32_t *as;
+  float *u, *qh, *red;
+  volatile int *flag;  // [0] abort
+};
+
+__device__ Smem carve(uint8_t *base, const Layout &L) {
+  Smem s;
+  s.ring = base + L.ring;
+  s.full = (uint64_t *)(base + L.full);
+  s.empty = (uint64_t *)(base + L.empty);
+  s.aq = (int8_t *)(base + L.aq);
+  s.ad = (float *)(base + L.ad);
+  s.as = (int32_t *)(base + L.as);
+  s.u = (float *)(base + L.u);
+  s.qh = (float *)(base + L.qh);
+  s.red = (float *)(base + L.red);
+  s.flag = (volatile int *)(base + L.flag);
+  return s;
+}
+
+__host__ __device__ inline int dk_gpb(int t) { return (t == T_Q4_K || t == T_Q6_K) ? 4 : 1; }
+__host__ __device__ inline int dk_tpg(int t) { return t == T_Q4_K ? 2 : (t == T_Q6_K ? 4 : 1); }
+
+// Ring position shared by the producer and every consumer thread: both walk
+// the same sequence of transfers.
+struct Ring {
+  uint32_t slot = 0, par = 0;
+  __device__ void next() {
+    if (++slot == DK_NS) {
+      slot = 0;
+      par ^= 1u;
+    }
+  }
+};
+
+// ------------------------------------------------------------------ producer
+__device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChunk *ch, const int *ph) {
+  Ring rg;
+  uint32_t armed[DK_NS];
+  bool used[DK_NS];
+  for (int i = 0; i < DK_NS; i++) used[i] = false;
+  bool ok = true;
+  // Claim the next slot; false on abort / timeout.
+  auto claim = [&](uint32_t tx) -> uint8_t * {
+    if (!mbar_wait(&S.empty[rg.slot], rg.par ^ 1u, S.flag)) {
+      if (!*S.flag) atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+      S.flag[0] = 1;
+      ok = false;
+      return nullptr;
+    }
+    mbar_expect(&S.full[rg.slot], tx);
+    used[rg.slot] = true;
+    armed[rg.slot] = rg.par;
+    return S.ring + (size_t)rg.slot * DK_SLOT;
+  };
+  const int group = a.n_head / a.n_kv;
+  const int ppc = DK_SLOT / (a.dh * 4);
+  for (int p = 0; p < a.n_phase && ok; p++) {
+    for (int ci = ph[p]; ci < ph[p + 1] && ok; ci++) {
+      const DChunk &c = ch[ci];
+      const uint32_t dl = c.d ? c.d_len : 0u;
+      const uint32_t tx = c.full ? c.q_len + dl : (uint32_t)c.rows * (c.q_len + dl);
+      uint8_t *dst = claim(tx);
+      if (!dst) break;
+      uint64_t *fb = &S.full[rg.slot];
+      if (c.full) {
+        bulk_g2s(dst, c.q, c.q_len, fb);
+        if (c.d) bulk_g2s(dst + c.d_off, align16_down(c.d), c.d_len, fb);
+      } else {
+        for (int r = 0; r < c.rows; r++) {
+          bulk_g2s(dst + (size_t)r * c.q_len, c.q + (size_t)r * c.q_stride, c.q_len, fb);
+          if (c.d) bulk_g2s(dst + c.d_off + (size_t)r * c.d_len, align16_down(c.d + (size_t)r * c.d_stride), c.d_len, fb);
+        }
+      }
+      rg.next();
+    }
+    if ((p & 3) == 0 && p < 4 * a.n_layer && ok) {  // attention of layer p/4: K then V history of each owned head
+      const int L = p >> 2;
+      for (int h = blockIdx.x; h < a.n_head && ok; h += gridDim.x) {
+        const size_t base = ((size_t)L * a.n_kv + h / group) * a.n_ctx * a.dh;
+        for (int kv = 0; kv < 2 && ok; kv++) {
+          const float *src = (kv ? a.vcache : a.kcache) + base;
+          for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
+            const int n = min(ppc, pos - p0);
+            const uint32_t bytes = (uint32_t)n * a.dh * 4;
+            uint8_t *dst = claim(bytes);
+            if (!dst) break;
+            bulk_g2s(dst, src + (size_t)p0 * a.dh, bytes, &S.full[rg.slot]);
+            rg.next();
+          }
+        }
+      }
+    }
+  }
+  // Every copy this CTA issued lands before the CTA may exit.
+  for (int i = 0; i < DK_NS; i++)
+    if (used[i]) mbar_wait(&S.full[i], armed[i], nullptr);
+}
+
+// ------------------------------------------------------------------ consumers
+struct Cons {
+  const DecodeArgs &a;
+  const Smem &S;
+  const DChunk *ch;
+  const int *ph;
+  int pos, tid, ctid, cwarp, lane;
+  Ring rg;
+  int mv = 0, mv_total = 0;
+  unsigned gen = 0;
+  // chain-warp state
+  float acc = 0.0f, gval = 0.0f, best_v = -INFINITY;
+  int best_i = INT_MAX;
+
+  __device__ Cons(const DecodeArgs &a_, const Smem &S_, const DChunk *ch_, const int *ph_, int pos_)
+      : a(a_), S(S_), ch(ch_), ph(ph_), pos(pos_) {
+    tid = threadIdx.x;
+    ctid = tid - 32;
+    cwarp = ctid >> 5;
+    lane = tid & 31;
+    mv_total = ph[a.n_phase];
+  }
+
+  __device__ void wait_full() {
+    if (!mbar_wait(&S.full[rg.slot], rg.par, S.flag) && !*S.flag) {
+      atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+      S.flag[0] = 1;
+    }
+  }
+
+  __device__ void trace(int i) {
+    if (a.trace && ctid == 0 && i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = gtime();
+  }
+
+  // All consumers; true when the kernel is being abandoned.
+  __device__ bool grid_sync() {
+    bar_sync(NB_CONS, CONS);
+    if (ctid == 0) {
+      gen++;
+      const unsigned target = gen * gridDim.x;
+      __threadfence();
+      atomicAdd(a.sync, 1u);
+      const unsigned long long t0 = gtime();
+      while (ld_acquire(a.sync) < target) {
+        if (*(volatile int *)a.err) {
+          S.flag[0] = 1;
+          break;
+        }
+        if (gtime() - t0 > WAIT_NS) {
+          atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+          S.flag[0] = 1;
+          break;
+        }
+      }
+      __threadfence();
+      trace((int)gen);
+    }
+    bar_sync(NB_CONS, CONS);
+    return S.flag[0] != 0;
+  }
+
+  // x = dequant_row(token_embd, ids[0]) (model.rs:857-869): kept in the
+  // staging buffer for layer 0 and written to global x for the owned rows.
+  __device__ void embed() {
+    const uint32_t id = *a.ids;
+    const uint8_t *row = a.embd + (size_t)id * a.embd_row_bytes;
+    const int o0 = a.own[2 * blockIdx.x], o1 = a.own[2 * blockIdx.x + 1];
+    for (int j = ctid; j < a.n_embd; j += CONS) {
+      const float v = dequant_elem(a.embd_type, row, j);
+      S.u[j] = v;
+      if (j >= o0 && j < o1) a.x[j] = v;
+    }
+    bar_sync(NB_CONS, CONS);
+  }
+
+  __device__ void stage(const float *src, int k) {  // global (this launch's data) -> staging buffer
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *d4 = reinterpret_cast<float4 *>(S.u);
+    for (int i = ctid; i < k / 4; i += CONS) d4[i] = __ldcg(s4 + i);
+    bar_sync(NB_CONS, CONS);
+  }
+
+  // RMSNorm (b == 1 order, simd.rs:47-64) + Q8 of the staged vector.
+  __device__ void norm_q8(const float *nw, int k) {
+    float *xv = S.u;
+    const int n8 = k / 8 * 8;
+    if (ctid < 8) {
+      float c = 0.0f;
+#pragma unroll 8
+      for (int i = ctid; i < n8; i += 8) c = __fmaf_rn(xv[i], xv[i], c);
+      S.red[ctid] = c;
+    }
+    bar_sync(NB_CONS, CONS);
+    if (ctid == 0) {
+      const float c0 = fadd(S.red[0], S.red[4]), c1 = fadd(S.red[1], S.red[5]), c2 = fadd(S.red[2], S.red[6]),
+                  c3 = fadd(S.red[3], S.red[7]);
+      float s = fadd(fadd(c0, c1), fadd(c2, c3));
+      for (int i = n8; i < k; i++) s = fadd(s, fmul(xv[i], xv[i]));
+      S.red[32] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)k), a.eps)));
+    }
+    bar_sync(NB_CONS, CONS);
+    const float scale = S.red[32];
+    for (int blk = cwarp; blk < k / 32; blk += CONS / 32) {
+      const float v = fmul(fmul(xv[blk * 32 + lane], scale), __ldg(nw + blk * 32 + lane));
+      q8_block_lane(v, lane, S.aq + blk * 32, S.ad + blk, S.as + blk);
+    }
+    bar_sync(NB_CONS, CONS);
+  }
+
+  __device__ void q8(int k) {  // Q8 of the staged vector
+    for (int blk = cwarp; blk < k / 32; blk += CONS / 32)
+      q8_block_lane(S.u[blk * 32 + lane], lane, S.aq + blk * 32, S.ad + blk, S.as + blk);
+    bar_sync(NB_CONS, CONS);
+  }
+
+  template <int T>
+  __device__ void terms(const DChunk &c, const uint8_t *sl, float *Tb) {
+    constexpr int GPB = (T == T_Q4_K || T == T_Q6_K) ? 4 : 1, TPG = Geo<T>::TPG;
+    constexpr int QB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 208 : (T == T_Q8_0 ? 32 : 16));
+    const int R = c.rows, nbk = c.b1 - c.b0, G = nbk * GPB, items = R * G, rs = c.rs;
+    const int qrs = nbk * QB;
+    const ActRef A{S.aq, S.ad, S.as};
+    for (int it = tid - 64; it < items; it += TERM_T) {
+      int rl, gl;
+      if (GPB == 4) {  // lanes walk rows: one activation block per warp step
+        rl = it % R;
+        gl = it / R;
+      } else {
+        gl = it % G;
+        rl = it / G;
+      }
+      const uint8_t *rq = sl + rl * qrs;
+      const uint8_t *rd = nullptr;
+      if (T != T_Q4_K) {
+        const uintptr_t d0 = (uintptr_t)c.d;
+        rd = sl + c.d_off +
+             (c.full ? (d0 & 15) + (size_t)rl * c.d_stride : (size_t)rl * c.d_len + ((d0 + (size_t)rl * c.d_stride) & 15));
+      }
+      GroupW<T> g;
+      g.load_s(rq, rd, c.b0 * GPB + gl, c.b0);
+      float t[TPG];
+      g.terms(A, t);
+#pragma unroll
+      for (int s = 0; s < TPG; s++) Tb[(gl * TPG + s) * rs + rl] = t[s];
+    }
+  }
+
+  __device__ void epilogue(const DChunk &c) {
+    const float val = fadd(0.0f, acc);  // Pool::matmul: out zero-filled, then out += acc
+    const int r = c.row0 + lane;
+    const bool live = lane < c.rows;
+    switch (c.role) {
+      case DR_Q:
+      case DR_K: {  // model.rs:953-979
+        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+        const int hd = r / a.dh, d = r - hd * a.dh;
+        float o = val;
+        if (d < 2 * a.half) {
+          const int i = d >> 1;
+          const float cs = __ldg(a.rope_cos + (size_t)pos * a.half + i), sn = __ldg(a.rope_sin + (size_t)pos * a.half + i);
+          o = (d & 1) == 0 ? fsub(fmul(val, cs), fmul(partner, sn)) : fadd(fmul(partner, sn), fmul(val, cs));
+        }
+        if (live) {
+          if (c.role == DR_Q) a.q[r] = o;
+          else a.kcache[(((size_t)c.layer * a.n_kv + hd) * a.n_ctx + pos) * a.dh + d] = o;
+        }
+        break;
+      }
+      case DR_V:
+        if (live) {
+          const int hd = r / a.dh, d = r - hd * a.dh;
+          a.vcache[(((size_t)c.layer * a.n_kv + hd) * a.n_ctx + pos) * a.dh + d] = val;
+        }
+        break;
+      case DR_O:
+      case DR_DOWN:
+        if (live) a.x[r] = fadd(__ldcg(a.x + r), val);
+        break;
+      case DR_GATE:
+        gval = val;
+        break;
+      case DR_UP:  // model.rs:1111-1115
+        if (live) a.h[r] = fmul(fdiv(gval, fadd(1.0f, expf_lib(-gval))), val);
+        break;
+      case DR_HEAD: {
+        if (live) a.logits[r] = val;
+        float v = (live && !isnan(val)) ? val : -INFINITY;
+        int i = live ? r : INT_MAX;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+          if (ov > v || (ov == v && oi < i)) {
+            v = ov;
+            i = oi;
+          }
+        }
+        if (v > best_v) {  // row groups ascend: a strict > keeps the first maximum
+          best_v = v;
+          best_i = i;
+        }
+        break;
+      }
+    }
+  }
+
+  // The matvec chunks of phase p.
+  __device__ void run_mv(int p) {
+    const bool chain = cwarp == 0;
+    for (int ci = ph[p]; ci < ph[p + 1]; ci++) {
+      const DChunk &c = ch[ci];
+      const int buf = mv & 1;
+      float *Tb = S.u + buf * DK_TS;
+      if (!chain) {
+        if (mv >= 2) bar_sync(NB_EMPTYT + buf, CONS);
+        wait_full();
+        const uint8_t *sl = S.ring + (size_t)rg.slot * DK_SLOT;
+        switch (c.type) {
+          case T_Q4_K: terms<T_Q4_K>(c, sl, Tb); break;
+          case T_Q6_K: terms<T_Q6_K>(c, sl, Tb); break;
+          case T_Q8_0: terms<T_Q8_0>(c, sl, Tb); break;
+          default: terms<T_Q4_0>(c, sl, Tb); break;
+        }
+        bar_arrive(NB_FULLT + buf, CONS);
+      } else {
+        bar_sync(NB_FULLT + buf, CONS);
+        if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
+        if (c.flags & DF_FIRST) acc = 0.0f;
+        const int nt = (c.b1 - c.b0) * dk_gpb(c.type) * dk_tpg(c.type), rs = c.rs;
+        if (lane < c.rows) {
+          const float *tp = Tb + lane;
+#pragma unroll 8
+          for (int j = 0; j < nt; j++) acc = fadd(acc, tp[j * rs]);
+        }
+        if (c.flags & DF_LAST) epilogue(c);
+        if (mv < mv_total - 2) bar_arrive(NB_EMPTYT + buf, CONS);
+      }
+      rg.next();
+      mv++;
+    }
+  }
+
+  // Exact single-token attention for the heads this CTA owns (model.rs:993-1087).
+  __device__ void attention(int L) {
+    const int dh = a.dh, group = a.n_head / a.n_kv, ppc = DK_SLOT / (dh * 4);
+    float *sc = S.u;
+    const int grp = ctid >> 3, l = ctid & 7, ngrp = CONS / 8;
+    const int nvw = (dh + 31) / 32;  // value-chain warps
+    for (int h = blockIdx.x; h < a.n_head; h += gridDim.x) {
+      const int kh = h / group;
+      const size_t cur = (((size_t)L * a.n_kv + kh) * a.n_ctx + pos) * dh;
+      for (int d = ctid; d < dh; d += CONS) S.qh[d] = __ldcg(a.q + (size_t)h * dh + d);
+      bar_sync(NB_CONS, CONS);
+      float mx = -INFINITY;
+      // s_p = f32_dot(q, k_p) * scale: eight unfused chains over d = 8t + l,
+      // combined ((c0+c1)+(c2+c3)) + ((c4+c5)+(c6+c7)), then the tail.
+      auto score = [&](const float *kr, bool ld_global) -> float {
+        const int n8 = dh - (dh & 7);
+        float c = 0.0f;
+        for (int t = l; t < n8; t += 8) c = fadd(c, fmul(S.qh[t], ld_global ? __ldcg(kr + t) : kr[t]));
+        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 1));
+        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 2));
+        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 4));
+        for (int t = n8; t < dh; t++) c = fadd(c, fmul(S.qh[t], ld_global ? __ldcg(kr + t) : kr[t]));
+        return fmul(c, a.scale);
+      };
+      for (int p0 = 0; p0 < pos; p0 += ppc) {
+        const int n = min(ppc, pos - p0);
+        wait_full();
+        const float *kc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
+        for (int b = 0; b < n; b += ngrp) {
+          const int pi = b + grp;
+          const bool valid = pi < n;
+          const float s = score(kc + (size_t)(valid ? pi : 0) * dh, false);
+          if (valid) {
+            if (l == 0) sc[p0 + pi] = s;
+            mx = s > mx ? s : mx;
+          }
+        }
+        bar_sync(NB_CONS, CONS);
+        if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
+        rg.next();
+      }
+      if (cwarp == 0) {  // the position written by this step's qkv phase
+        const float s = score(a.kcache + cur, true);
+        if (grp == 0) {
+          if (l == 0) sc[pos] = s;
+          mx = s > mx ? s : mx;
+        }
+      }
+      mx = warp_max(mx);
+      if (lane == 0) S.red[cwarp] = mx;
+      bar_sync(NB_CONS, CONS);
+      if (ctid == 0) {
+        float m = -INFINITY;
+        for (int w = 0; w < CONS / 32; w++) m = S.red[w] > m ? S.red[w] : m;
+        S.red[32] = m;
+      }
+      bar_sync(NB_CONS, CONS);
+      const float M = S.red[32];
+      for (int p = ctid; p <= pos; p += CONS) sc[p] = expf_lib(fsub(sc[p], M));
+      bar_sync(NB_CONS, CONS);
+      // Weighted values: one chain per d over p (zero weights skipped); the
+      // softmax sum is one more chain.
+      const bool vw = cwarp < nvw;
+      float vacc = 0.0f;
+      if (ctid == nvw * 32) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int p = 0; p <= pos; p++) sum = fadd(sum, sc[p]);
+        S.red[33] = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+      }
+      for (int p0 = 0; p0 < pos; p0 += ppc) {
+        const int n = min(ppc, pos - p0);
+        if (vw) {
+          wait_full();
+          const float *vc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
+          if (ctid < dh) {
+#pragma unroll 8
+            for (int pi = 0; pi < n; pi++) {
+              const float e = sc[p0 + pi];
+              const float v = vc[(size_t)pi * dh + ctid];
+              if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
+            }
+          }
+          bar_sync(NB_V, nvw * 32);
+          if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
+        }
+        rg.next();
+      }
+      if (vw && ctid < dh) {
+        const float e = sc[pos];
+        const float v = __ldcg(a.vcache + cur + ctid);
+        if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
+      }
+      bar_sync(NB_CONS, CONS);
+      if (vw && ctid < dh) a.att[(size_t)h * dh + ctid] = fmul(vacc, S.red[33]);
+      bar_sync(NB_CONS, CONS);
+    }
+  }
+
+  __device__ void finish() {
+    if (cwarp == 0 && lane == 0) {
+      a.cand_v[blockIdx.x] = best_v;
+      a.cand_i[blockIdx.x] = best_i;
+    }
+    bar_sync(NB_CONS, CONS);
+    if (ctid == 0) {
+      trace(a.n_trace - 1);
+      __threadfence();
+      const unsigned prev = atomicAdd(a.sync + 1, 1u);
+      if (prev == gridDim.x - 1) {  // the last CTA: greedy pick over the per-CTA candidates
+        __threadfence();
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int c = 0; c < (int)gridDim.x; c++) {  // CTA row ranges ascend: strict > keeps the first maximum
+          const float v = __ldcg(a.cand_v + c);
+          if (v > bv) {
+            bv = v;
+            bi = __ldcg(a.cand_i + c);
+          }
+        }
+        const uint32_t t = bi == INT_MAX ? 0u : (uint32_t)bi;  // nothing above -inf: index 0
+        *a.tok = t;
+        if (a.mode == 1) {  // feed the token back: the next launch decodes it at pos + 1
+          a.ids[0] = t;
+          a.hist[*a.step] = t;
+          *a.step += 1;
+          *a.pos += 1;
+        }
+        a.sync[0] = 0u;
+        a.sync[1] = 0u;
+        __threadfence();
+      }
+    }
+  }
+
+  __device__ void run() {
+    trace(0);
+    embed();
+    const int qdim = a.n_head * a.dh;
+    for (int L = 0; L < a.n_layer; L++) {
+      const DecLayer &Ly = a.layers[L];
+      if (L > 0) stage(a.x, a.n_embd);
+      norm_q8(Ly.attn_norm, a.n_embd);
+      run_mv(4 * L);
+      if (grid_sync()) return;
+      attention(L);
+      if (grid_sync()) return;
+      stage(a.att, qdim);
+      q8(qdim);
+      run_mv(4 * L + 1);
+      if (grid_sync()) return;
+      stage(a.x, a.n_embd);
+      norm_q8(Ly.ffn_norm, a.n_embd);
+      run_mv(4 * L + 2);
+      if (grid_sync()) return;
+      stage(a.h, a.n_ff);
+      q8(a.n_ff);
+      run_mv(4 * L + 3);
+      if (grid_sync()) return;
+    }
+    stage(a.x, a.n_embd);
+    norm_q8(a.out_norm, a.n_embd);
+    run_mv(4 * a.n_layer);
+    finish();
+  }
+};
+
+__global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const Layout L = dk_layout(a.n_embd, a.n_ff, a.n_head * a.dh, a.n_ctx);
+  const Smem S = carve(smem_raw, L);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DK_NS; i++) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.empty[i], 1);
+    }
+    S.flag[0] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int pos = *a.pos;
+  const DChunk *ch = a.chunks + a.cta_chunk0[blockIdx.x];
+  const int *ph = a.phase0 + (size_t)blockIdx.x * (a.n_phase + 1);
+  if (threadIdx.x < 32) {
+    if (threadIdx.x == 0) producer(a, S, pos, ch, ph);
+    return;
+  }
+  Cons c(a, S, ch, ph, pos);
+  c.run();
+}
+
+}  // namespace
+
+size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh) {
+  if (dh <= 0 || dh > 256 || dh % 4 != 0 || DK_SLOT / (dh * 4) < 1) return 0;
+  const Layout L = dk_layout(n_embd, n_ff, qdim, n_ctx);
+  return L.total <= 227 * 1024 ? L.total : 0;
+}
+
+int decode_grid() {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v > 0 ? v : 148;
+}
+
+cudaError_t prepare_decode(size_t smem, int grid) {
+  cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, DK_THREADS, smem);
+  if (e != cudaSuccess) return e;
+  return per_sm >= 1 && grid <= per_sm * decode_grid() ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
+}
+
+cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(DK_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident at once, or the launch fails
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_decode, a);
+}
+
+
+// ------------------------------------------------------------------ host plan
+namespace {
+
+struct TypeGeo {
+  int be, qb, gpb, tpg;
+  bool has_d;
+};
+
+TypeGeo type_geo(int t) {
+  switch (t) {
+    case T_Q4_K: return {256, 144, 4, 2, false};
+    case T_Q6_K: return {256, 208, 4, 4, true};
+    case T_Q8_0: return {32, 32, 1, 1, true};
+    default: return {32, 16, 1, 1, true};
+  }
+}
+
+size_t up16h(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// [a, b) of n items split into `parts` near-equal pieces on multiples of 2.
+void split2(int n, int parts, int i, int &a, int &b) {
+  const long units = (n + 1) / 2;
+  a = (int)std::min<long>(n, 2 * (units * i / parts));
+  b = (int)std::min<long>(n, 2 * (units * (i + 1) / parts));
+}
+
+struct Builder {
+  std::vector<DChunk> &out;
+  std::string &why;
+
+  DChunk base(const DevTensor &W, uint8_t role, int layer, int r, int rows, int b0, int b1, bool full) {
+    const TypeGeo g = type_geo(W.type);
+    const int nblk = W.k / g.be;
+    const size_t row_q = (size_t)nblk * g.qb, row_d = g.has_d ? (size_t)nblk * 2 : 0;
+    DChunk c{};
+    c.type = (uint8_t)W.type;
+    c.role = role;
+    c.layer = layer;
+    c.row0 = r;
+    c.rows = (uint16_t)rows;
+    c.rs = (uint16_t)(rows | 1);
+    c.b0 = b0;
+    c.b1 = b1;
+    c.full = full ? 1 : 0;
+    c.q = W.q + (size_t)r * row_q + (size_t)b0 * g.qb;
+    c.q_stride = (uint32_t)row_q;
+    c.d_stride = (uint32_t)row_d;
+    if (full) {
+      c.q_len = (uint32_t)(rows * row_q);
+      c.d_off = c.q_len;
+    } else {
+      c.q_len = (uint32_t)((size_t)(b1 - b0) * g.qb);
+      c.d_off = (uint32_t)((size_t)rows * c.q_len);
+    }
+    if (g.has_d) {
+      c.d = reinterpret_cast<const uint8_t *>(W.d) + (size_t)r * row_d + (size_t)b0 * 2;
+      c.d_len = full ? (uint32_t)up16h(((uintptr_t)c.d & 15) + rows * row_d) : (uint32_t)up16h((size_t)(b1 - b0) * 2 + 15);
+    }
+    return c;
+  }
+
+  // Rows [r0, r1) of W (and, when W2 is given, the same rows of W2 right
+  // after each row group of W: gate then up).  Rows too long for a slot are
+  // split along k; the row chain carries across those chunks.
+  struct Mode {
+    TypeGeo g;
+    int nblk;
+    size_t row_q, row_d, terms_row;
+    bool full;
+    int rg;
+  };
+  Mode mode(const DevTensor &M, int own) {
+    Mode m;
+    m.g = type_geo(M.type);
+    m.nblk = M.k / m.g.be;
+    m.row_q = (size_t)m.nblk * m.g.qb;
+    m.row_d = m.g.has_d ? (size_t)m.nblk * 2 : 0;
+    m.terms_row = (size_t)m.nblk * m.g.gpb * m.g.tpg;
+    int rgf = 0;
+    for (int rg = std::min(DK_MAX_RG, own); rg >= 2; rg--)
+      if (full_fits(m, rg)) {
+        rgf = rg & ~1;
+        break;
+      }
+    m.full = rgf >= 2 && rgf >= std::min(8, own);
+    m.rg = m.full ? rgf : std::min(DK_MAX_RG, std::max(2, own)) & ~1;
+    return m;
+  }
+  static bool full_fits(const Mode &m, int rg) {
+    const size_t bytes = rg * m.row_q + (m.g.has_d ? up16h(15 + rg * m.row_d) : 0);
+    return bytes <= (size_t)DK_SLOT && (size_t)(rg | 1) * m.terms_row <= (size_t)DK_TS;
+  }
+
+  bool rows(const DevTensor &W, const DevTensor *W2, int r0, int r1, uint8_t role, uint8_t role2, int layer) {
+    if (r1 <= r0) return true;
+    if (!type_is_matvec(W.type) || (W2 && (!type_is_matvec(W2->type) || W2->k != W.k || W2->rows != W.rows))) {
+      why = "unsupported matrix pairing";
+      return false;
+    }
+    const int own = r1 - r0;
+    Mode md[2] = {mode(W, own), W2 ? mode(*W2, own) : mode(W, own)};
+    const int rg_max = std::max(2, std::min(md[0].rg, md[1].rg));
+    const int units = (own + 1) / 2, ng = (units + rg_max / 2 - 1) / (rg_max / 2);
+    for (int gi = 0; gi < ng; gi++) {
+      int a, b;
+      split2(own, ng, gi, a, b);
+      const int R = b - a;
+      if (R <= 0) continue;
+      for (int w = 0; w < (W2 ? 2 : 1); w++) {
+        const DevTensor &M = w ? *W2 : W;
+        const Mode &m = md[w];
+        const bool full = m.full && full_fits(m, R);
+        int nkc = 1;
+        if (!full) {
+          int nbmax = 0;
+          for (int nb = m.nblk; nb >= 1; nb--) {
+            const size_t bytes = (size_t)R * (nb * (size_t)m.g.qb + (m.g.has_d ? up16h((size_t)nb * 2 + 15) : 0));
+            if (bytes <= (size_t)DK_SLOT && (size_t)(R | 1) * nb * m.g.gpb * m.g.tpg <= (size_t)DK_TS) {
+              nbmax = nb;
+              break;
+            }
+          }
+          if (nbmax == 0) {
+            why = "a block of these rows does not fit a ring slot";
+            return false;
+          }
+          nkc = (m.nblk + nbmax - 1) / nbmax;
+        }
+        for (int j = 0; j < nkc; j++) {
+          const int b0 = full ? 0 : (int)((long)m.nblk * j / nkc), b1 = full ? m.nblk : (int)((long)m.nblk * (j + 1) / nkc);
+          DChunk c = base(M, w ? role2 : role, layer, r0 + a, R, b0, b1, full);
+          c.flags = (uint8_t)((j == 0 ? DF_FIRST : 0) | (j == nkc - 1 ? DF_LAST : 0));
+          out.push_back(c);
+        }
+      }
+    }
+    return true;
+  }
+};
+
+}  // namespace
+
+bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out, int n_embd, int n_ff, int n_head,
+                       int n_kv, int dh, int n_ctx, int grid, DecodePlan &plan, std::string &why) {
+  plan = DecodePlan{};
+  plan.grid = grid;
+  plan.smem = decode_smem_bytes(n_embd, n_ff, n_head * dh, n_ctx, dh);
+  if (!plan.smem) {
+    why = "model does not fit the persistent kernel's shared memory";
+    return false;
+  }
+  if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv) {
+    why = "unsupported dimensions";
+    return false;
+  }
+  const int nl = (int)layers.size();
+  plan.n_phase = 4 * nl + 1;
+  plan.cta_chunk0.assign(grid + 1, 0);
+  plan.phase0.assign((size_t)grid * (plan.n_phase + 1), 0);
+  plan.own.assign((size_t)grid * 2, 0);
+  for (int c = 0; c < grid; c++) {
+    plan.cta_chunk0[c] = (int)plan.chunks.size();
+    std::vector<DChunk> v;
+    Builder B{v, why};
+    int *ph = &plan.phase0[(size_t)c * (plan.n_phase + 1)];
+    int oa, ob;
+    split2(n_embd, grid, c, oa, ob);  // o / down rows, and the rows of x this CTA writes
+    plan.own[2 * c] = oa;
+    plan.own[2 * c + 1] = ob;
+    for (int L = 0; L < nl; L++) {
+      const DecLayer &Y = layers[L];
+      int a, b;
+      ph[4 * L] = (int)v.size();
+      split2(Y.q.rows, grid, c, a, b);
+      if (!B.rows(Y.q, nullptr, a, b, DR_Q, 0, L)) return false;
+      split2(Y.k.rows, grid, c, a, b);
+      if (!B.rows(Y.k, nullptr, a, b, DR_K, 0, L)) return false;
+      split2(Y.v.rows, grid, c, a, b);
+      if (!B.rows(Y.v, nullptr, a, b, DR_V, 0, L)) return false;
+      ph[4 * L + 1] = (int)v.size();
+      if (!B.rows(Y.o, nullptr, oa, ob, DR_O, 0, L)) return false;
+      ph[4 * L + 2] = (int)v.size();
+      split2(Y.gate.rows, grid, c, a, b);
+      if (!B.rows(Y.gate, &Y.up, a, b, DR_GATE, DR_UP, L)) return false;
+      ph[4 * L + 3] = (int)v.size();
+      if (!B.rows(Y.down, nullptr, oa, ob, DR_DOWN, 0, L)) return false;
+    }
+    ph[4 * nl] = (int)v.size();
+    int a, b;
+    split2(out.rows, grid, c, a, b);
+    if (!B.rows(out, nullptr, a, b, DR_HEAD, 0, nl)) return false;
+    ph[4 * nl + 1] = (int)v.size();
+    plan.chunks.insert(plan.chunks.end(), v.begin(), v.end());
+  }
+  plan.cta_chunk0[grid] = (int)plan.chunks.size();
+  return true;
+}
+
+}  // namespace pk

@@ -1,0 +1,100 @@
+// pk_decode.h -- the persistent single-token decode kernel (pk_decode.cu).
+//
+// One launch runs a whole b == 1 forward pass (model.rs:833-1170): the
+// embedding row, every layer, the final norm and the output head, and
+// optionally the greedy pick and the device-side token feedback.  One CTA
+// runs on each SM.  In each CTA one producer thread streams that CTA's share
+// of the weights (and, for the CTAs that own an attention head, the head's
+// K/V history) through a ring of shared-memory slots with bulk copies; the
+// consumer warps compute.  Weights never depend on activations, so the
+// producer runs ahead across the grid-wide dependency points.
+#pragma once
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "pk_kernels.h"
+
+namespace pk {
+
+constexpr int DK_THREADS = 512;     // warp 0 producer, warp 1 row chains, warps 2..15 terms
+constexpr int DK_NS = 5;            // ring slots
+constexpr int DK_SLOT = 32768;      // bytes per slot
+constexpr int DK_TS = 2560;         // floats per term buffer (two buffers)
+constexpr int DK_MAX_RG = 32;       // rows per row group (one chain lane each)
+
+enum : uint8_t { DR_Q = 0, DR_K, DR_V, DR_O, DR_GATE, DR_UP, DR_DOWN, DR_HEAD };
+enum : uint8_t { DF_FIRST = 1, DF_LAST = 2 };
+
+// One ring transfer: rows [row0, row0 + rows) x blocks [b0, b1) of one matrix.
+// full: the rows are whole and contiguous, one copy for q and one for d.
+// Otherwise one q copy and one d copy per row.  d copies start at the
+// 16-byte boundary at or below the row's first scale; the consumer recovers
+// the skew from the source address.
+struct DChunk {
+  const uint8_t *q;   // row 0's q bytes at block b0
+  const uint8_t *d;   // row 0's first f16 scale at block b0 (nullptr: scales inline)
+  uint32_t q_stride;  // bytes between rows' q parts in global memory
+  uint32_t d_stride;  // bytes between rows' scale arrays in global memory
+  uint32_t q_len;     // bytes per q copy
+  uint32_t d_len;     // bytes per d copy
+  uint32_t d_off;     // slot offset of the scale area
+  uint16_t rows, rs;  // rows; term-buffer row stride (odd)
+  uint8_t type, role, full, flags;
+  int row0, b0, b1, layer;
+};
+static_assert(sizeof(DChunk) == 64, "DChunk is one 64-byte record");
+
+struct DecLayer {
+  DevTensor q, k, v, o, gate, up, down;
+  const float *attn_norm, *ffn_norm;
+};
+
+struct DecodeArgs {
+  const DecLayer *layers;
+  DevTensor out;
+  const float *out_norm;
+  const uint8_t *embd;
+  uint32_t embd_row_bytes;
+  int embd_type;
+  int n_layer, n_embd, n_ff, n_head, n_kv, dh, half, n_ctx, n_vocab;
+  float eps, scale;
+  const float *rope_cos, *rope_sin;
+  float *kcache, *vcache;             // [L][n_kv][n_ctx][dh]
+  float *x, *q, *att, *h, *logits;    // activations
+  uint32_t *ids, *tok, *hist;
+  int *pos, *step;
+  const DChunk *chunks;
+  const int *cta_chunk0;              // [grid + 1]
+  const int *phase0;                  // [grid][n_phase + 1], relative to the CTA's first chunk
+  int n_phase;                        // 4 * n_layer + 1
+  const int *own;                     // [grid][2] rows of x written by this CTA
+  unsigned *sync;                     // [0] grid barrier arrivals, [1] finished CTAs
+  int *err;                           // 0 or a PK_ERR_* code
+  float *cand_v;
+  int *cand_i;                        // [grid]
+  int mode;                           // 1: greedy pick + token feedback after the head
+  unsigned long long *trace;          // optional [grid][n_trace] globaltimer stamps
+  int n_trace;
+};
+
+// Host-built work split: every CTA's chunk list in consumption order.
+struct DecodePlan {
+  std::vector<DChunk> chunks;
+  std::vector<int> cta_chunk0, phase0, own;
+  int grid = 0, n_phase = 0;
+  size_t smem = 0;
+};
+// false (with the reason) when this model cannot use the persistent kernel.
+bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out, int n_embd, int n_ff, int n_head,
+                       int n_kv, int dh, int n_ctx, int grid, DecodePlan &plan, std::string &why);
+
+// Shared memory the kernel needs for this model (0 if it does not fit).
+size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh);
+// Sets the kernel's shared-memory limit and checks that `grid` CTAs fit at once.
+cudaError_t prepare_decode(size_t smem, int grid);
+cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream_t st);
+int decode_grid();
+
+}  // namespace pk

@@ -11,6 +11,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "pk_engine.h"
@@ -36,6 +37,7 @@ Engine::~Engine() {
   cudaFree(d_rope_cos_);
   cudaFree(d_rope_sin_);
   cudaFree(d_act_arena_);
+  cudaFree(d_decode_);
   cudaFreeHost(h_ids_);
   cudaFreeHost(h_pos_);
   cudaFreeHost(h_tok_);
@@ -212,6 +214,7 @@ int Engine::load(const char *path) {
   total += mat_bytes(output) + a256(embd.row_bytes * embd.ne1) + a256((size_t)c.n_embd * 4);
   max_raw = std::max(max_raw, output.row_bytes * output.ne1);
   stream_bytes_ += output.row_bytes * output.ne1 + (size_t)c.n_embd * 4 + embd.row_bytes;
+  total += 256;  // the decode kernel's scale copies may read up to 30 bytes past a matrix
   PK_CK(cudaMalloc((void **)&d_weights_, total));
   weight_bytes_ = total;
   uint8_t *staging = nullptr;
@@ -319,7 +322,120 @@ int Engine::load(const char *path) {
   eos_ids_.erase(std::unique(eos_ids_.begin(), eos_ids_.end()), eos_ids_.end());
   PK_CK(cudaStreamSynchronize(st_));
   loaded_ = true;
+  return setup_decode();
+}
+
+// Plan and device tables of the persistent decode kernel.  A model it cannot
+// run (shared memory, shapes) keeps the per-op kernel sequence; the
+// environment variable PK_DECODE=ops selects that sequence as well.
+int Engine::setup_decode() {
+  use_decode_ = false;
+  const char *env = std::getenv("PK_DECODE");
+  if (env && std::strcmp(env, "ops") == 0) {
+    decode_why_ = "PK_DECODE=ops";
+    return PK_OK;
+  }
+  const Config &c = cfg_;
+  std::vector<DecLayer> dl(c.n_layer);
+  for (int i = 0; i < c.n_layer; i++) {
+    const LayerDev &L = layers_[i];
+    dl[i] = DecLayer{L.q, L.k, L.v, L.o, L.gate, L.up, L.down, L.attn_norm, L.ffn_norm};
+  }
+  const int grid = decode_grid();
+  if (!build_decode_plan(dl, output_, c.n_embd, c.n_ff, c.n_head, c.n_head_kv, c.head_dim, n_ctx_, grid, plan_,
+                         decode_why_))
+    return PK_OK;
+  // Every bulk copy must stay inside the weight arena.
+  const uintptr_t lo = (uintptr_t)d_weights_, hi = lo + weight_bytes_;
+  for (const DChunk &k : plan_.chunks) {
+    const size_t nq = k.full ? 1 : k.rows, qlen = k.q_len;
+    const uintptr_t q0 = (uintptr_t)k.q, q1 = q0 + (nq - 1) * (size_t)k.q_stride + qlen;
+    bool ok = (q0 & 15) == 0 && (qlen & 15) == 0 && q0 >= lo && q1 <= hi && (k.d_off & 15) == 0;
+    size_t tx = k.full ? qlen : (size_t)k.rows * qlen;
+    if (k.d) {
+      const uintptr_t d0 = (uintptr_t)k.d & ~(uintptr_t)15;
+      const uintptr_t d1 = k.full ? d0 + k.d_len : (((uintptr_t)k.d + (k.rows - 1) * (size_t)k.d_stride) & ~(uintptr_t)15) + k.d_len;
+      ok = ok && d0 >= lo && d1 <= hi && (k.d_len & 15) == 0;
+      tx += k.full ? k.d_len : (size_t)k.rows * k.d_len;
+    }
+    ok = ok && tx <= (size_t)DK_SLOT && k.rows >= 1 && k.rows <= DK_MAX_RG;
+    if (!ok) {
+      decode_why_ = "decode plan failed its bounds check";
+      return PK_OK;
+    }
+  }
+  if (prepare_decode(plan_.smem, plan_.grid) != cudaSuccess) {
+    cudaGetLastError();
+    decode_why_ = "the persistent kernel's grid does not fit the device at once";
+    return PK_OK;
+  }
+  const int n_trace = 5 * c.n_layer + 2;
+  const size_t n_ch = plan_.chunks.size() * sizeof(DChunk), n_c0 = plan_.cta_chunk0.size() * 4,
+               n_ph = plan_.phase0.size() * 4, n_own = plan_.own.size() * 4, n_ly = dl.size() * sizeof(DecLayer),
+               n_tr = (size_t)grid * n_trace * 8;
+  const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr};
+  size_t total = 0;
+  for (size_t z : sizes) total += a256(z);
+  PK_CK(cudaMalloc((void **)&d_decode_, total));
+  PK_CK(cudaMemsetAsync(d_decode_, 0, total, st_));
+  uint8_t *p = d_decode_;
+  size_t si = 0;
+  auto take = [&]() {
+    uint8_t *r = p;
+    p += a256(sizes[si++]);
+    return r;
+  };
+  DChunk *chunks = (DChunk *)take();
+  int *c0 = (int *)take(), *ph = (int *)take(), *own = (int *)take();
+  DecLayer *layers = (DecLayer *)take();
+  d_sync_ = (unsigned *)take();
+  d_err_ = (int *)take();
+  float *cv = (float *)take();
+  int *ci = (int *)take();
+  d_trace_ = (unsigned long long *)take();
+  PK_CK(cudaMemcpyAsync(chunks, plan_.chunks.data(), n_ch, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(c0, plan_.cta_chunk0.data(), n_c0, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(ph, plan_.phase0.data(), n_ph, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(own, plan_.own.data(), n_own, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(layers, dl.data(), n_ly, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  DecodeArgs &a = dargs_;
+  a = DecodeArgs{};
+  a.layers = layers;
+  a.out = output_;
+  a.out_norm = output_norm_;
+  a.embd = embd_raw_;
+  a.embd_row_bytes = (uint32_t)embd_row_bytes_;
+  a.embd_type = embd_type_;
+  a.n_layer = c.n_layer; a.n_embd = c.n_embd; a.n_ff = c.n_ff; a.n_head = c.n_head; a.n_kv = c.n_head_kv;
+  a.dh = c.head_dim; a.half = c.n_rot / 2; a.n_ctx = n_ctx_; a.n_vocab = vocab_;
+  a.eps = c.rms_eps;
+  a.scale = 1.0f / sqrtf((float)c.head_dim);
+  a.rope_cos = d_rope_cos_; a.rope_sin = d_rope_sin_;
+  a.kcache = d_kcache_; a.vcache = d_vcache_;
+  a.x = x_; a.q = q_; a.att = attn_; a.h = h_; a.logits = logits_;
+  a.ids = d_ids_; a.tok = d_tok_; a.hist = d_hist_; a.pos = d_pos_; a.step = d_step_;
+  a.chunks = chunks; a.cta_chunk0 = c0; a.phase0 = ph; a.n_phase = plan_.n_phase; a.own = own;
+  a.sync = d_sync_; a.err = d_err_; a.cand_v = cv; a.cand_i = ci;
+  a.mode = 0;
+  a.trace = nullptr;
+  a.n_trace = n_trace;
+  use_decode_ = true;
   return PK_OK;
+}
+
+// After a persistent-kernel launch: a bounded wait that ran out leaves an
+// error code; the barrier counters are reset so the next launch starts clean.
+int Engine::check_decode_error() {
+  if (!use_decode_) return PK_OK;
+  int err = 0;
+  PK_CK(cudaMemcpyAsync(&err, d_err_, 4, cudaMemcpyDeviceToHost, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  if (err == 0) return PK_OK;
+  PK_CK(cudaMemsetAsync(d_err_, 0, 4, st_));
+  PK_CK(cudaMemsetAsync(d_sync_, 0, 8, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  return set_error(err, "decode kernel: a bounded wait ran out (grid barrier or copy did not complete)");
 }
 
 int Engine::info(pk_model_info *o) const {
@@ -328,6 +444,7 @@ int Engine::info(pk_model_info *o) const {
   o->n_head_kv = cfg_.n_head_kv; o->head_dim = cfg_.head_dim; o->n_rot = cfg_.n_rot; o->n_vocab = vocab_;
   o->n_ctx = n_ctx_; o->rope_theta = cfg_.rope_theta; o->rms_eps = cfg_.rms_eps;
   o->weight_bytes = weight_bytes_; o->kv_bytes = kv_bytes_; o->stream_bytes = stream_bytes_;
+  o->decode_kernels = use_decode_ ? 1 : 3 + 5 * cfg_.n_layer + 1;
   return PK_OK;
 }
 
@@ -462,11 +579,17 @@ int Engine::ensure_graphs() {
     PK_CK(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
     int rc = PK_OK;
     cudaError_t e = cudaSuccess;
-    if (which == 1) {
-      e = launch_argmax(logits_, vocab_, d_tok_, st_);
-      if (e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
+    if (use_decode_) {
+      DecodeArgs a = dargs_;
+      a.mode = which;  // the step graph also picks the next token and feeds it back
+      e = launch_decode(a, plan_.grid, plan_.smem, st_);
+    } else {
+      if (which == 1) {
+        e = launch_argmax(logits_, vocab_, d_tok_, st_);
+        if (e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
+      }
+      if (e == cudaSuccess) rc = enqueue_forward(1, true, false);
     }
-    if (e == cudaSuccess) rc = enqueue_forward(1, true, false);
     cudaError_t ee = cudaStreamEndCapture(st_, &graph);
     if (e != cudaSuccess) {
       if (graph) cudaGraphDestroy(graph);
@@ -513,6 +636,10 @@ int Engine::forward_inner(const uint32_t *ids, const int *pos, int b, bool want_
   }
   PK_CK(cudaStreamSynchronize(st_));
   PK_CK(cudaGetLastError());
+  if (b == 1 && want_logits && !dbg_on_) {
+    const int rc = check_decode_error();
+    if (rc) return rc;
+  }
   next_pos_ = pos[b - 1] + 1;
   have_logits_ = want_logits;
   return PK_OK;
@@ -651,6 +778,10 @@ int Engine::decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms
   PK_CK(cudaEventCreate(&e0));
   PK_CK(cudaEventCreate(&e1));
   cudaError_t e = cudaEventRecord(e0, st_);
+  if (use_decode_ && e == cudaSuccess) {  // the first token comes from the logits already there
+    e = launch_argmax(logits_, vocab_, d_tok_, st_);
+    if (e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
+  }
   for (int i = 0; i < n_steps && e == cudaSuccess; i++) e = cudaGraphLaunch(g_step_, st_);
   if (e == cudaSuccess) e = cudaEventRecord(e1, st_);
   std::vector<uint32_t> hist(n_steps);
@@ -661,6 +792,8 @@ int Engine::decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   if (e != cudaSuccess) return cuda_error(e, "decode_steps_device");
+  rc = check_decode_error();
+  if (rc) return rc;
   if (device_ms) *device_ms = ms;
   if (out_ids) std::memcpy(out_ids, hist.data(), (size_t)n_steps * 4);
   kv_tokens_.insert(kv_tokens_.end(), hist.begin(), hist.end());
@@ -692,7 +825,18 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
     if (!rc) e = launch_argmax(logits_, vocab_, d_tok_, st_);
     if (!rc && e == cudaSuccess) rc = prof_end();
     if (!rc && e == cudaSuccess) e = launch_advance(d_tok_, d_ids_, d_pos_, d_hist_, d_step_, st_);
-    if (!rc && e == cudaSuccess) rc = enqueue_forward(1, true, false);
+    if (use_decode_) {
+      DecodeArgs a = dargs_;
+      a.mode = 1;
+      a.trace = d_trace_;
+      const Config &c = cfg_;
+      const double kv = 2.0 * c.n_layer * c.n_head_kv * c.head_dim * 4.0 * ((double)next_pos_ + 1.0);
+      if (!rc && e == cudaSuccess) rc = prof_begin("k_decode", (double)stream_bytes_ + kv);
+      if (!rc && e == cudaSuccess) e = launch_decode(a, plan_.grid, plan_.smem, st_);
+      if (!rc && e == cudaSuccess) rc = prof_end();
+    } else if (!rc && e == cudaSuccess) {
+      rc = enqueue_forward(1, true, false);
+    }
   }
   prof_ = nullptr;
   if (e == cudaSuccess) e = cudaStreamSynchronize(st_);
@@ -716,6 +860,47 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
   }
   if (rc) return rc;
   if (e != cudaSuccess) return cuda_error(e, "decode_profile");
+  if (use_decode_) {
+    if ((rc = check_decode_error())) return rc;
+    // Phase times inside the persistent kernel from its per-CTA timestamps:
+    // stamp 0 at the start, stamp g after grid barrier g, the last at the end.
+    const Config &c = cfg_;
+    const int nt = dargs_.n_trace, grid = plan_.grid;
+    std::vector<unsigned long long> tr((size_t)grid * nt);
+    PK_CK(cudaMemcpyAsync(tr.data(), d_trace_, tr.size() * 8, cudaMemcpyDeviceToHost, st_));
+    PK_CK(cudaStreamSynchronize(st_));
+    std::vector<double> T(nt);
+    for (int i = 0; i < nt; i++) {
+      unsigned long long v = tr[i];
+      for (int g = 1; g < grid; g++) {
+        const unsigned long long w = tr[(size_t)g * nt + i];
+        v = i == 0 ? std::min(v, w) : std::max(v, w);
+      }
+      T[i] = (double)v;
+    }
+    const char *names[6] = {"dk_qkv", "dk_attn", "dk_o", "dk_gateup", "dk_down", "dk_head"};
+    double ms[6] = {0, 0, 0, 0, 0, 0}, bytes[6] = {0, 0, 0, 0, 0, 0};
+    const double f4 = 4.0, kvp = (double)next_pos_ + 1.0;
+    for (int L = 0; L < c.n_layer; L++) {
+      const LayerDev &Y = layers_[L];
+      for (int j = 0; j < 5; j++) ms[j] += (T[5 * L + j + 1] - T[5 * L + j]) * 1e-6;
+      bytes[0] += mat_stream_bytes(Y.q) + mat_stream_bytes(Y.k) + mat_stream_bytes(Y.v) + c.n_embd * f4;
+      bytes[1] += 2.0 * c.n_head_kv * kvp * c.head_dim * f4;
+      bytes[2] += mat_stream_bytes(Y.o);
+      bytes[3] += mat_stream_bytes(Y.gate) + mat_stream_bytes(Y.up) + c.n_embd * f4;
+      bytes[4] += mat_stream_bytes(Y.down);
+    }
+    ms[5] = (T[nt - 1] - T[nt - 2]) * 1e-6;
+    bytes[5] = mat_stream_bytes(output_) + c.n_embd * f4 + embd_row_bytes_;
+    for (int j = 0; j < 6; j++) {
+      pk_kernel_stat st{};
+      std::snprintf(st.name, sizeof(st.name), "%s", names[j]);
+      st.launches = j == 5 ? 1 : c.n_layer;
+      st.ms = ms[j];
+      st.bytes = bytes[j];
+      agg.push_back(st);
+    }
+  }
   uint32_t tok = 0;
   PK_CK(cudaMemcpyAsync(&tok, d_tok_, 4, cudaMemcpyDeviceToHost, st_));
   kv_tokens_.push_back(tok);

@@ -8,6 +8,7 @@
 
 #include "pk.h"
 #include "pk_gguf.h"
+#include "pk_decode.h"
 #include "pk_kernels.h"
 
 namespace pk {
@@ -49,6 +50,8 @@ class Engine {
  private:
   int forward_inner(const uint32_t *ids, const int *pos, int b, bool want_logits, bool cancellable);
   int enqueue_forward(int b, bool want_logits, bool cancellable);
+  int setup_decode();
+  int check_decode_error();
   int ensure_graphs();
   void release_graphs();
   void dump(const char *name, const float *dev, size_t n);
@@ -81,6 +84,16 @@ class Engine {
   // pinned host staging
   uint32_t *h_ids_ = nullptr, *h_tok_ = nullptr;
   int *h_pos_ = nullptr;
+
+  // persistent decode kernel (pk_decode.cu): plan, device tables and args
+  bool use_decode_ = false;
+  std::string decode_why_;
+  DecodePlan plan_;
+  DecodeArgs dargs_{};
+  uint8_t *d_decode_ = nullptr;
+  int *d_err_ = nullptr;
+  unsigned *d_sync_ = nullptr;
+  unsigned long long *d_trace_ = nullptr;
 
   // decode graphs: fwd1 = one b=1 forward with logits; step = argmax + advance + fwd1
   cudaGraphExec_t g_fwd1_ = nullptr, g_step_ = nullptr;

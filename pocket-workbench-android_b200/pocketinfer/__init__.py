@@ -53,7 +53,7 @@ class ModelInfo(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_rot",
                                        "n_vocab", "n_ctx")] + \
                [("rope_theta", C.c_float), ("rms_eps", C.c_float), ("weight_bytes", C.c_size_t),
-                ("kv_bytes", C.c_size_t), ("stream_bytes", C.c_size_t)]
+                ("kv_bytes", C.c_size_t), ("stream_bytes", C.c_size_t), ("decode_kernels", C.c_int)]
 
 
 class GenOpts(C.Structure):

@@ -78,15 +78,53 @@ def test_device_decode_loop_matches_generate(pk, paths):
     assert e.decode_steps_device(39) == ref[1:]
 
 
+def ops_engine(pk, path, **kw):
+    """An engine on the per-op kernel sequence (PK_DECODE=ops is read at load)."""
+    old = os.environ.get("PK_DECODE")
+    os.environ["PK_DECODE"] = "ops"
+    try:
+        return pk.Engine(path, **kw)
+    finally:
+        if old is None:
+            del os.environ["PK_DECODE"]
+        else:
+            os.environ["PK_DECODE"] = old
+
+
 def test_decode_profile_reports_kernels(pk, paths):
     spec = MODELS["q8down"]
     e = pk.Engine(paths["q8down"], n_ctx=128)
+    assert e.info["decode_kernels"] == 1
     e.forward(synth.prompt_ids(2, 20, spec.n_vocab), np.arange(20), True)
     prof = {p["name"]: p for p in e.decode_profile()}
+    assert prof["k_decode"]["launches"] == 1
+    for name in ("dk_qkv", "dk_attn", "dk_o", "dk_gateup", "dk_down"):
+        assert prof[name]["launches"] == spec.n_layer
+    assert sum(prof[n]["ms"] for n in prof if n.startswith("dk_")) <= prof["k_decode"]["ms"] * 1.05
+    assert all(p["ms"] > 0 and p["bytes"] > 0 for p in prof.values())
+    o = ops_engine(pk, paths["q8down"], n_ctx=128)
+    assert o.info["decode_kernels"] == 3 + 5 * spec.n_layer + 1
+    o.forward(synth.prompt_ids(2, 20, spec.n_vocab), np.arange(20), True)
+    prof = {p["name"]: p for p in o.decode_profile()}
     assert prof["k_qkv_b1"]["launches"] == spec.n_layer
     assert prof["k_gateup_b1"]["launches"] == spec.n_layer
     assert prof["k_mv_b1"]["launches"] == 2 * spec.n_layer + 1
     assert all(p["ms"] > 0 and p["bytes"] > 0 for p in prof.values())
+
+
+@pytest.mark.parametrize("name", list(MODELS))
+def test_persistent_kernel_equals_op_sequence(pk, paths, name):
+    """The persistent decode kernel and the per-op kernels give the same bits."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(9, 40, spec.n_vocab)
+    a, b = pk.Engine(paths[name], n_ctx=256), ops_engine(pk, paths[name], n_ctx=256)
+    for e in (a, b):
+        e.forward(prompt[:32], np.arange(32), False)
+        e.forward(prompt[32:39], np.arange(32, 39), False)
+        e.forward(prompt[39:], [39], True)  # b == 1 forward with logits
+    assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
+    assert a.decode_steps_device(24) == b.decode_steps_device(24)
+    assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
 
 
 def test_prefix_reuse_matches_fresh(pk, paths):
