@@ -15,7 +15,7 @@
 //   warp 0, lane 0   producer: walks the chunk list (plus the K/V history of
 //                    the attention heads this CTA owns) and bulk-copies each
 //                    chunk into the next free ring slot (mbarrier complete_tx);
-//   warps 2..15      term warps: integer dots + float terms of a chunk into a
+//   warps 2..11      term warps: integer dots + float terms of a chunk into a
 //                    term buffer (two buffers, alternating);
 //   warp 1           chain warp: one lane per row adds that row's terms in
 //                    the reference's order and runs the epilogue.
@@ -42,8 +42,8 @@
 namespace pk {
 namespace {
 
-constexpr int CONS = DK_THREADS - 32;    // consumer threads (warps 1..15)
-constexpr int TERM_T = DK_THREADS - 64;  // term threads (warps 2..15)
+constexpr int CONS = DK_THREADS - 32;    // consumer threads (warps 1..11)
+constexpr int TERM_T = DK_THREADS - 64;  // term threads (warps 2..11)
 constexpr int NB_CONS = 1, NB_FULLT = 2, NB_EMPTYT = 4, NB_V = 6;
 constexpr unsigned long long WAIT_NS = 2000000000ull;
 
@@ -73,12 +73,24 @@ __device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Like mbar_test, but the thread may sleep up to `ns` in the hardware until the
+// phase completes (it wakes as soon as it does).
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t *b, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the completion of phase `parity`; false on timeout or abort.
-__device__ bool mbar_wait(uint64_t *b, uint32_t parity, const volatile int *abort) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, const volatile int *abort,
+                                          uint32_t sleep_ns = 0) {
   if (mbar_test(b, parity)) return true;
   const unsigned long long t0 = gtime();
   for (;;) {
-    if (mbar_test(b, parity)) return true;
+    if (sleep_ns ? mbar_test_sleep(b, parity, sleep_ns) : mbar_test(b, parity)) return true;
     if (abort && *abort) return false;
     if (gtime() - t0 > WAIT_NS) return false;
   }
@@ -96,19 +108,23 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ const uint8_t *align16_down(const uint8_t *p) {
   return (const uint8_t *)((uintptr_t)p & ~(uintptr_t)15);
 }
 
 // Shared memory layout (host and device agree through dk_layout).
 struct Layout {
-  size_t ring, full, empty, aq, ad, as, u, qh, red, flag, total;
+  size_t ring, full, empty, desc, aq, ad, as, u, qh, rope, xo, ph, nw, red, flag, prof, total;
   int kmax, uf;
 };
+constexpr int DK_XO = 256;  // owned rows of x kept in shared memory
 
 __host__ __device__ inline size_t up16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-__host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int n_ctx) {
+__host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int n_ctx, int n_layer) {
   Layout L;
   int km = n_embd > n_ff ? n_embd : n_ff;
   km = km > qdim ? km : qdim;
@@ -122,13 +138,19 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
   L.full = o; o += DK_NS * 8;
   L.empty = o; o += DK_NS * 8;
   o = up16(o);
+  L.desc = o; o += DK_NS * sizeof(DChunk);
   L.aq = o; o += up16(L.kmax);
   L.ad = o; o += up16((size_t)L.kmax / 32 * 4);
   L.as = o; o += up16((size_t)L.kmax / 32 * 4);
   L.u = o; o += (size_t)L.uf * 4;
-  L.qh = o; o += 256 * 4;
+  L.qh = o; o += 3 * 256 * 4;  // q, current k, current v of one head
+  L.rope = o; o += 2 * 128 * 4;  // cos, sin of this step's position
+  L.xo = o; o += DK_XO * 4;
+  L.ph = o; o += up16((size_t)(4 * n_layer + 2) * 4);
+  L.nw = o; o += up16((size_t)n_embd * 4);  // the next RMSNorm's weights
   L.red = o; o += 64 * 4;
-  L.flag = o; o += 16;
+  L.flag = o; o += 16;  // [0] abort
+  L.prof = o; o += 8 * 8;  // profile cycle accumulators
   L.total = o;
   return L;
 }
@@ -136,18 +158,27 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
 struct Smem {
   uint8_t *ring;
   uint64_t *full, *empty;
+  DChunk *desc;
+  float *rope, *xo, *nw;
+  int *ph;
   int8_t *aq;
   float *ad;
   int32_t *as;
   float *u, *qh, *red;
   volatile int *flag;  // [0] abort
+  unsigned long long *prof;
 };
 
-__device__ Smem carve(uint8_t *base, const Layout &L) {
+__device__ __forceinline__ Smem carve(uint8_t *base, const Layout &L) {
   Smem s;
   s.ring = base + L.ring;
   s.full = (uint64_t *)(base + L.full);
   s.empty = (uint64_t *)(base + L.empty);
+  s.desc = (DChunk *)(base + L.desc);
+  s.rope = (float *)(base + L.rope);
+  s.xo = (float *)(base + L.xo);
+  s.nw = (float *)(base + L.nw);
+  s.ph = (int *)(base + L.ph);
   s.aq = (int8_t *)(base + L.aq);
   s.ad = (float *)(base + L.ad);
   s.as = (int32_t *)(base + L.as);
@@ -155,11 +186,137 @@ __device__ Smem carve(uint8_t *base, const Layout &L) {
   s.qh = (float *)(base + L.qh);
   s.red = (float *)(base + L.red);
   s.flag = (volatile int *)(base + L.flag);
+  s.prof = (unsigned long long *)(base + L.prof);
   return s;
 }
 
 __host__ __device__ inline int dk_gpb(int t) { return (t == T_Q4_K || t == T_Q6_K) ? 4 : 1; }
 __host__ __device__ inline int dk_tpg(int t) { return t == T_Q4_K ? 2 : (t == T_Q6_K ? 4 : 1); }
+
+// Q8Act::prepare (quant_int.rs:36-53) of one 32-block held four elements per
+// lane in an aligned group of 8 lanes: amax of |x| ignoring NaN, d = amax/127,
+// inv = 1/d (0 if d == 0), q = clamp(round_half_away(x*inv), +-127), NaN -> 0.
+// All 32 lanes of the warp must call it (the group reductions shuffle).
+__device__ __forceinline__ void q8_block8(const float4 v, int l8, bool store, int8_t *q, float *d, int32_t *sum) {
+  auto ab = [](float x) {
+    const float a = fabsf(x);
+    return a > 0.0f ? a : 0.0f;
+  };
+  float amax = ab(v.x), t;
+  t = ab(v.y); amax = t > amax ? t : amax;
+  t = ab(v.z); amax = t > amax ? t : amax;
+  t = ab(v.w); amax = t > amax ? t : amax;
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    t = __shfl_xor_sync(0xffffffffu, amax, o);
+    amax = t > amax ? t : amax;
+  }
+  const float dd = fdiv(amax, 127.0f);
+  const float inv = dd > 0.0f ? fdiv(1.0f, dd) : 0.0f;
+  auto qz = [&](float x) {
+    float r = roundf(fmul(x, inv));
+    r = r < -127.0f ? -127.0f : r;
+    r = r > 127.0f ? 127.0f : r;
+    return isnan(r) ? 0 : (int)r;
+  };
+  const int q0 = qz(v.x), q1 = qz(v.y), q2 = qz(v.z), q3 = qz(v.w);
+  int sm = q0 + q1 + q2 + q3;
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+  if (store) {
+    *reinterpret_cast<uint32_t *>(q + 4 * l8) =
+        (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) | ((uint32_t)(q3 & 0xFF) << 24);
+    if (l8 == 0) {
+      *d = dd;
+      *sum = sm;
+    }
+  }
+}
+
+// Sequential float chains.  The reference adds terms one at a time, so only
+// the add itself may sit on the dependency path: operands are loaded a batch
+// of eight ahead of the adds that consume them.
+//   acc + p[0] + p[s] + ... + p[(n-1)s], in that order.
+__device__ __forceinline__ float chain_add(float acc, const float *p, int s, int n) {
+  int j = 0;
+  if (n >= 8) {
+    float cur[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) cur[u] = p[u * s];
+    for (j = 8; j + 8 <= n; j += 8) {
+      float nxt[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) nxt[u] = p[(j + u) * s];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = fadd(acc, cur[u]);
+#pragma unroll
+      for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = fadd(acc, cur[u]);
+  }
+  for (; j < n; j++) acc = fadd(acc, p[j * s]);
+  return acc;
+}
+
+// fma(p[(n-1)s], p[(n-1)s], ... fma(p[0], p[0], acc)): one f32_sum_sq lane.
+__device__ __forceinline__ float chain_sq(float acc, const float *p, int s, int n) {
+  int j = 0;
+  if (n >= 8) {
+    float cur[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) cur[u] = p[u * s];
+    for (j = 8; j + 8 <= n; j += 8) {
+      float nxt[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) nxt[u] = p[(j + u) * s];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = __fmaf_rn(cur[u], cur[u], acc);
+#pragma unroll
+      for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = __fmaf_rn(cur[u], cur[u], acc);
+  }
+  for (; j < n; j++) acc = __fmaf_rn(p[j * s], p[j * s], acc);
+  return acc;
+}
+
+// acc + e_0*v_0 + e_1*v_1 + ... with the terms of zero weights skipped
+// (model.rs:1076-1085).  A skipped term adds -0.0, which leaves every float
+// (signed zeros and NaN included) unchanged, so the product and the choice
+// stay off the dependency path.
+__device__ __forceinline__ float chain_wv(float acc, const float *e, const float *v, int vs, int n) {
+  auto term = [](float ew, float vv) { return ew != 0.0f ? fmul(ew, vv) : -0.0f; };
+  int j = 0;
+  if (n >= 8) {
+    float ce[8], cv[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      ce[u] = e[u];
+      cv[u] = v[u * vs];
+    }
+    for (j = 8; j + 8 <= n; j += 8) {
+      float ne[8], nv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        ne[u] = e[j + u];
+        nv[u] = v[(j + u) * vs];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = fadd(acc, term(ce[u], cv[u]));
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        ce[u] = ne[u];
+        cv[u] = nv[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = fadd(acc, term(ce[u], cv[u]));
+  }
+  for (; j < n; j++) acc = fadd(acc, term(e[j], v[j * vs]));
+  return acc;
+}
 
 // Ring position shared by the producer and every consumer thread: both walk
 // the same sequence of transfers.
@@ -174,21 +331,32 @@ struct Ring {
 };
 
 // ------------------------------------------------------------------ producer
+template <bool TRACE>
 __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChunk *ch, const int *ph) {
   Ring rg;
   uint32_t armed[DK_NS];
   bool used[DK_NS];
   for (int i = 0; i < DK_NS; i++) used[i] = false;
   bool ok = true;
+  unsigned long long pst = 0;  // SM cycles spent waiting for a free slot (profile trace)
+  auto note = [&](int layer) {
+    if ((TRACE && a.trace)) {
+      const int i = 1 + 8 * 5 * a.n_layer + 2 + layer;
+      if (i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = pst;
+      pst = 0;
+    }
+  };
   // Claim the next slot; false on abort / timeout.
   auto claim = [&](uint32_t tx) -> uint8_t * {
-    if (!mbar_wait(&S.empty[rg.slot], rg.par ^ 1u, S.flag)) {
+    const long long t0 = (TRACE && a.trace) ? clock64() : 0;
+    const bool got = mbar_wait(&S.empty[rg.slot], rg.par ^ 1u, S.flag, 20000u);
+    if ((TRACE && a.trace)) pst += (unsigned long long)(clock64() - t0);
+    if (!got) {
       if (!*S.flag) atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
       S.flag[0] = 1;
       ok = false;
       return nullptr;
     }
-    mbar_expect(&S.full[rg.slot], tx);
     used[rg.slot] = true;
     armed[rg.slot] = rg.par;
     return S.ring + (size_t)rg.slot * DK_SLOT;
@@ -196,13 +364,17 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
   const int group = a.n_head / a.n_kv;
   const int ppc = DK_SLOT / (a.dh * 4);
   for (int p = 0; p < a.n_phase && ok; p++) {
+    if (p > 0 && (p & 3) == 0) note(p / 4 - 1);
     for (int ci = ph[p]; ci < ph[p + 1] && ok; ci++) {
-      const DChunk &c = ch[ci];
+      const DChunk c = ch[ci];
       const uint32_t dl = c.d ? c.d_len : 0u;
       const uint32_t tx = c.full ? c.q_len + dl : (uint32_t)c.rows * (c.q_len + dl);
       uint8_t *dst = claim(tx);
       if (!dst) break;
       uint64_t *fb = &S.full[rg.slot];
+      S.desc[rg.slot] = c;  // made visible to the consumers by the full barrier's completion
+      mbar_expect(fb, tx);
+      if (ci + 1 < ph[p + 1]) prefetch_l1(ch + ci + 1);
       if (c.full) {
         bulk_g2s(dst, c.q, c.q_len, fb);
         if (c.d) bulk_g2s(dst + c.d_off, align16_down(c.d), c.d_len, fb);
@@ -225,6 +397,7 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
             const uint32_t bytes = (uint32_t)n * a.dh * 4;
             uint8_t *dst = claim(bytes);
             if (!dst) break;
+            mbar_expect(&S.full[rg.slot], bytes);
             bulk_g2s(dst, src + (size_t)p0 * a.dh, bytes, &S.full[rg.slot]);
             rg.next();
           }
@@ -232,18 +405,20 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
       }
     }
   }
+  note(a.n_layer);
   // Every copy this CTA issued lands before the CTA may exit.
   for (int i = 0; i < DK_NS; i++)
     if (used[i]) mbar_wait(&S.full[i], armed[i], nullptr);
 }
 
 // ------------------------------------------------------------------ consumers
+template <bool TRACE>
 struct Cons {
   const DecodeArgs &a;
   const Smem &S;
   const DChunk *ch;
   const int *ph;
-  int pos, tid, ctid, cwarp, lane;
+  int pos, tid, ctid, cwarp, lane, own0;
   Ring rg;
   int mv = 0, mv_total = 0;
   unsigned gen = 0;
@@ -257,22 +432,50 @@ struct Cons {
     ctid = tid - 32;
     cwarp = ctid >> 5;
     lane = tid & 31;
-    mv_total = ph[a.n_phase];
+    mv_total = ph[a.n_phase];  // ph is the shared-memory copy
+    own0 = a.own[2 * blockIdx.x];
   }
 
-  __device__ void wait_full() {
-    if (!mbar_wait(&S.full[rg.slot], rg.par, S.flag) && !*S.flag) {
+  __device__ __forceinline__ void wait_full() {
+    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == 32);
+    const long long t0 = timed ? clock64() : 0;
+    const bool ok = mbar_wait(&S.full[rg.slot], rg.par, S.flag);
+    if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
+    if (!ok && !*S.flag) {
       atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
       S.flag[0] = 1;
     }
   }
 
-  __device__ void trace(int i) {
-    if (a.trace && ctid == 0 && i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = gtime();
+  // Profile trace (only when (TRACE && a.trace) is set), per CTA:
+  //   [0] start (ns); phase q = 5L + {qkv, attn, o, gate/up, down}, base
+  //   1 + 8q: [+0] prologue end, [+1] compute end, [+2] barrier exit (ns);
+  //   SM cycles: [+3] waiting for ring data, [+4] term warps waiting for a
+  //   term buffer, [+5] term computation, [+6] chain warp waiting for terms,
+  //   [+7] chain + epilogue; head: [1 + 40L + 0] prologue end, [+1] end (ns);
+  //   [1 + 40L + 2 + layer] SM cycles the producer waited for a free slot.
+  // Accumulators live in shared memory: S.prof[0] data wait of thread 0,
+  // [1] of thread 32, [2..5] the term / chain figures.
+  __device__ __forceinline__ void pacc(int i, long long c) {
+    if ((TRACE && a.trace)) S.prof[i] += (unsigned long long)c;
+  }
+  __device__ __forceinline__ void stamp(int i, unsigned long long v) {
+    if ((TRACE && a.trace) && i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = v;
+  }
+  __device__ __forceinline__ void mark(int q, int j) {
+    if ((TRACE && a.trace) && ctid == 0) stamp(1 + 8 * q + j, gtime());
   }
 
   // All consumers; true when the kernel is being abandoned.
   __device__ bool grid_sync() {
+    const int q = (int)gen;  // the phase this barrier closes
+    mark(q, 1);
+    if ((TRACE && a.trace)) bar_sync(NB_CONS, CONS);  // every accumulator of this phase is final
+    if ((TRACE && a.trace) && ctid == 0) {
+      stamp(1 + 8 * q + 3, S.prof[q % 5 == 1 ? 0 : 1]);
+      for (int i = 2; i < 6; i++) stamp(1 + 8 * q + 2 + i, S.prof[i]);
+      for (int i = 0; i < 6; i++) S.prof[i] = 0ull;
+    }
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {
       gen++;
@@ -292,7 +495,7 @@ struct Cons {
         }
       }
       __threadfence();
-      trace((int)gen);
+      mark(q, 2);
     }
     bar_sync(NB_CONS, CONS);
     return S.flag[0] != 0;
@@ -307,7 +510,10 @@ struct Cons {
     for (int j = ctid; j < a.n_embd; j += CONS) {
       const float v = dequant_elem(a.embd_type, row, j);
       S.u[j] = v;
-      if (j >= o0 && j < o1) a.x[j] = v;
+      if (j >= o0 && j < o1) {
+        a.x[j] = v;
+        S.xo[j - o0] = v;
+      }
     }
     bar_sync(NB_CONS, CONS);
   }
@@ -315,20 +521,58 @@ struct Cons {
   __device__ void stage(const float *src, int k) {  // global (this launch's data) -> staging buffer
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     float4 *d4 = reinterpret_cast<float4 *>(S.u);
-    for (int i = ctid; i < k / 4; i += CONS) d4[i] = __ldcg(s4 + i);
+    const int n4 = k >> 2;
+    for (int base = 0; base < n4; base += 4 * CONS) {  // every load in flight before the first store
+      float4 r[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = base + ctid + j * CONS;
+        if (i < n4) r[j] = __ldcg(s4 + i);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = base + ctid + j * CONS;
+        if (i < n4) d4[i] = r[j];
+      }
+    }
     bar_sync(NB_CONS, CONS);
   }
 
-  // RMSNorm (b == 1 order, simd.rs:47-64) + Q8 of the staged vector.
-  __device__ void norm_q8(const float *nw, int k) {
+  // The next RMSNorm's weights go to shared memory with asynchronous copies
+  // issued one phase ahead; norm_q8 waits for them.
+  __device__ void prefetch_norm(const float *nw, int k) {
+    for (int i = ctid; i < k / 4; i += CONS)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(S.nw + 4 * i)), "l"(nw + 4 * i) : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
+  // Q8 of the staged vector (optionally v = (x * scale) * w first, w in the
+  // shared norm buffer), eight lanes per 32-block.
+  __device__ void quant(int k, bool norm, float scale) {
+    const int nb = k >> 5, gi = ctid >> 3, l8 = ctid & 7;
+    const float4 *x4 = reinterpret_cast<const float4 *>(S.u);
+    const float4 *w4 = reinterpret_cast<const float4 *>(S.nw);
+    for (int base = 0; base < nb; base += CONS / 8) {
+      const int b = base + gi;
+      const bool ok = b < nb;
+      float4 v = ok ? x4[b * 8 + l8] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (norm && ok) {
+        const float4 w = w4[b * 8 + l8];
+        v = make_float4(fmul(fmul(v.x, scale), w.x), fmul(fmul(v.y, scale), w.y), fmul(fmul(v.z, scale), w.z),
+                        fmul(fmul(v.w, scale), w.w));
+      }
+      q8_block8(v, l8, ok, S.aq + b * 32, S.ad + b, S.as + b);
+    }
+    bar_sync(NB_CONS, CONS);
+  }
+
+  // RMSNorm (b == 1 order, simd.rs:47-64) + Q8 of the staged vector; the
+  // weights were requested with prefetch_norm.
+  __device__ void norm_q8(int k) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
     float *xv = S.u;
     const int n8 = k / 8 * 8;
-    if (ctid < 8) {
-      float c = 0.0f;
-#pragma unroll 8
-      for (int i = ctid; i < n8; i += 8) c = __fmaf_rn(xv[i], xv[i], c);
-      S.red[ctid] = c;
-    }
+    if (ctid < 8) S.red[ctid] = chain_sq(0.0f, xv + ctid, 8, n8 / 8);
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {
       const float c0 = fadd(S.red[0], S.red[4]), c1 = fadd(S.red[1], S.red[5]), c2 = fadd(S.red[2], S.red[6]),
@@ -338,19 +582,10 @@ struct Cons {
       S.red[32] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)k), a.eps)));
     }
     bar_sync(NB_CONS, CONS);
-    const float scale = S.red[32];
-    for (int blk = cwarp; blk < k / 32; blk += CONS / 32) {
-      const float v = fmul(fmul(xv[blk * 32 + lane], scale), __ldg(nw + blk * 32 + lane));
-      q8_block_lane(v, lane, S.aq + blk * 32, S.ad + blk, S.as + blk);
-    }
-    bar_sync(NB_CONS, CONS);
+    quant(k, true, S.red[32]);
   }
 
-  __device__ void q8(int k) {  // Q8 of the staged vector
-    for (int blk = cwarp; blk < k / 32; blk += CONS / 32)
-      q8_block_lane(S.u[blk * 32 + lane], lane, S.aq + blk * 32, S.ad + blk, S.as + blk);
-    bar_sync(NB_CONS, CONS);
-  }
+  __device__ void q8(int k) { quant(k, false, 1.0f); }
 
   template <int T>
   __device__ void terms(const DChunk &c, const uint8_t *sl, float *Tb) {
@@ -359,32 +594,67 @@ struct Cons {
     const int R = c.rows, nbk = c.b1 - c.b0, G = nbk * GPB, items = R * G, rs = c.rs;
     const int qrs = nbk * QB;
     const ActRef A{S.aq, S.ad, S.as};
-    for (int it = tid - 64; it < items; it += TERM_T) {
-      int rl, gl;
-      if (GPB == 4) {  // lanes walk rows: one activation block per warp step
-        rl = it % R;
-        gl = it / R;
-      } else {
-        gl = it % G;
-        rl = it / G;
+    // Item (row, group): rows fastest for the k-quants (lanes of a warp share
+    // one activation block), groups fastest for Q8_0/Q4_0 (contiguous bytes).
+    // Each thread keeps two items in flight.
+    const int M = GPB == 4 ? R : G, df = TERM_T % M, ds = TERM_T / M;
+    int t = tid - 64, f = t % M, sl_ = t / M;
+    auto adv = [&](int &a, int &b) {
+      a += df;
+      b += ds;
+      if (a >= M) {
+        a -= M;
+        b++;
       }
-      const uint8_t *rq = sl + rl * qrs;
-      const uint8_t *rd = nullptr;
-      if (T != T_Q4_K) {
-        const uintptr_t d0 = (uintptr_t)c.d;
+    };
+    const uintptr_t d0 = (uintptr_t)c.d;
+    auto ptrs = [&](int rl, const uint8_t *&rq, const uint8_t *&rd) {
+      rq = sl + rl * qrs;
+      rd = nullptr;
+      if (T != T_Q4_K)
         rd = sl + c.d_off +
              (c.full ? (d0 & 15) + (size_t)rl * c.d_stride : (size_t)rl * c.d_len + ((d0 + (size_t)rl * c.d_stride) & 15));
+    };
+    constexpr bool kTwo = true;  // two items in flight per thread
+    for (; t < items; t += (kTwo ? 2 : 1) * TERM_T) {
+      int f2 = f, s2 = sl_;
+      adv(f2, s2);
+      const bool two = kTwo && t + TERM_T < items;
+      const int rl1 = GPB == 4 ? f : sl_, gl1 = GPB == 4 ? sl_ : f;
+      const int rl2 = two ? (GPB == 4 ? f2 : s2) : rl1, gl2 = two ? (GPB == 4 ? s2 : f2) : gl1;
+      const uint8_t *rq1, *rd1, *rq2, *rd2;
+      ptrs(rl1, rq1, rd1);
+      ptrs(rl2, rq2, rd2);
+      float t1[TPG], t2[TPG];
+      {
+        GroupW<T> g1;
+        g1.load_s(rq1, rd1, c.b0 * GPB + gl1, c.b0);
+        if (kTwo) {
+          GroupW<T> g2;
+          g2.load_s(rq2, rd2, c.b0 * GPB + gl2, c.b0);
+          g1.terms(A, t1);
+          g2.terms(A, t2);
+        } else {
+          g1.terms(A, t1);
+        }
       }
-      GroupW<T> g;
-      g.load_s(rq, rd, c.b0 * GPB + gl, c.b0);
-      float t[TPG];
-      g.terms(A, t);
 #pragma unroll
-      for (int s = 0; s < TPG; s++) Tb[(gl * TPG + s) * rs + rl] = t[s];
+      for (int s = 0; s < TPG; s++) Tb[(gl1 * TPG + s) * rs + rl1] = t1[s];
+      if (two) {
+#pragma unroll
+        for (int s = 0; s < TPG; s++) Tb[(gl2 * TPG + s) * rs + rl2] = t2[s];
+      }
+      if (kTwo) adv(f2, s2);
+      f = f2;
+      sl_ = s2;
     }
   }
 
-  __device__ void epilogue(const DChunk &c) {
+  struct ChainInfo {
+    int row0, rows, role, layer, flags, nt, rs;
+  };
+
+  __device__ void epilogue(const ChainInfo &c) {
     const float val = fadd(0.0f, acc);  // Pool::matmul: out zero-filled, then out += acc
     const int r = c.row0 + lane;
     const bool live = lane < c.rows;
@@ -396,7 +666,7 @@ struct Cons {
         float o = val;
         if (d < 2 * a.half) {
           const int i = d >> 1;
-          const float cs = __ldg(a.rope_cos + (size_t)pos * a.half + i), sn = __ldg(a.rope_sin + (size_t)pos * a.half + i);
+          const float cs = S.rope[i], sn = S.rope[128 + i];
           o = (d & 1) == 0 ? fsub(fmul(val, cs), fmul(partner, sn)) : fadd(fmul(partner, sn), fmul(val, cs));
         }
         if (live) {
@@ -413,7 +683,12 @@ struct Cons {
         break;
       case DR_O:
       case DR_DOWN:
-        if (live) a.x[r] = fadd(__ldcg(a.x + r), val);
+        if (live) {
+          float *xr = S.xo + (r - own0);
+          const float nx = fadd(*xr, val);
+          *xr = nx;
+          a.x[r] = nx;
+        }
         break;
       case DR_GATE:
         gval = val;
@@ -447,12 +722,16 @@ struct Cons {
   __device__ void run_mv(int p) {
     const bool chain = cwarp == 0;
     for (int ci = ph[p]; ci < ph[p + 1]; ci++) {
-      const DChunk &c = ch[ci];
       const int buf = mv & 1;
       float *Tb = S.u + buf * DK_TS;
       if (!chain) {
+        const bool tp = (TRACE && a.trace) && ctid == 32;
+        long long c0 = tp ? clock64() : 0;
         if (mv >= 2) bar_sync(NB_EMPTYT + buf, CONS);
+        if (tp) pacc(2, clock64() - c0);
         wait_full();
+        if (tp) c0 = clock64();
+        const DChunk &c = S.desc[rg.slot];
         const uint8_t *sl = S.ring + (size_t)rg.slot * DK_SLOT;
         switch (c.type) {
           case T_Q4_K: terms<T_Q4_K>(c, sl, Tb); break;
@@ -460,18 +739,36 @@ struct Cons {
           case T_Q8_0: terms<T_Q8_0>(c, sl, Tb); break;
           default: terms<T_Q4_0>(c, sl, Tb); break;
         }
+        if (tp) pacc(3, clock64() - c0);
         bar_arrive(NB_FULLT + buf, CONS);
       } else {
+        const bool tp = (TRACE && a.trace) && ctid == 0;
+        long long c0 = tp ? clock64() : 0;
         bar_sync(NB_FULLT + buf, CONS);
+        if (tp) {
+          const long long c1 = clock64();
+          pacc(4, c1 - c0);
+          c0 = c1;
+        }
+        // what the chain needs, copied before the slot is handed back
+        ChainInfo c;
+        {
+          const DChunk &d = S.desc[rg.slot];
+          c.row0 = d.row0;
+          c.rows = d.rows;
+          c.role = d.role;
+          c.layer = d.layer;
+          c.flags = d.flags;
+          c.nt = (d.b1 - d.b0) * dk_gpb(d.type) * dk_tpg(d.type);
+          c.rs = d.rs;
+        }
+        __syncwarp();
         if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
         if (c.flags & DF_FIRST) acc = 0.0f;
-        const int nt = (c.b1 - c.b0) * dk_gpb(c.type) * dk_tpg(c.type), rs = c.rs;
-        if (lane < c.rows) {
-          const float *tp = Tb + lane;
-#pragma unroll 8
-          for (int j = 0; j < nt; j++) acc = fadd(acc, tp[j * rs]);
-        }
+        const int nt = c.nt, rs = c.rs;
+        if (lane < c.rows) acc = chain_add(acc, Tb + lane, rs, nt);
         if (c.flags & DF_LAST) epilogue(c);
+        if (tp) pacc(5, clock64() - c0);
         if (mv < mv_total - 2) bar_arrive(NB_EMPTYT + buf, CONS);
       }
       rg.next();
@@ -488,32 +785,55 @@ struct Cons {
     for (int h = blockIdx.x; h < a.n_head; h += gridDim.x) {
       const int kh = h / group;
       const size_t cur = (((size_t)L * a.n_kv + kh) * a.n_ctx + pos) * dh;
-      for (int d = ctid; d < dh; d += CONS) S.qh[d] = __ldcg(a.q + (size_t)h * dh + d);
+      float *kcur = S.qh + 256, *vcur = S.qh + 512;
+      for (int d = ctid; d < dh; d += CONS) {  // one round trip for q, this step's k and v
+        const float qv = __ldcg(a.q + (size_t)h * dh + d), kv = __ldcg(a.kcache + cur + d), vv = __ldcg(a.vcache + cur + d);
+        S.qh[d] = qv;
+        kcur[d] = kv;
+        vcur[d] = vv;
+      }
       bar_sync(NB_CONS, CONS);
       float mx = -INFINITY;
       // s_p = f32_dot(q, k_p) * scale: eight unfused chains over d = 8t + l,
       // combined ((c0+c1)+(c2+c3)) + ((c4+c5)+(c6+c7)), then the tail.
-      auto score = [&](const float *kr, bool ld_global) -> float {
+      // Two positions per group at once (two independent chain sets).
+      auto score2 = [&](const float *k1, const float *k2, float &s1, float &s2) {  // rows in shared memory
         const int n8 = dh - (dh & 7);
-        float c = 0.0f;
-        for (int t = l; t < n8; t += 8) c = fadd(c, fmul(S.qh[t], ld_global ? __ldcg(kr + t) : kr[t]));
-        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 1));
-        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 2));
-        c = fadd(c, __shfl_xor_sync(0xffffffffu, c, 4));
-        for (int t = n8; t < dh; t++) c = fadd(c, fmul(S.qh[t], ld_global ? __ldcg(kr + t) : kr[t]));
-        return fmul(c, a.scale);
+        float c1 = 0.0f, c2 = 0.0f;
+#pragma unroll 4
+        for (int t = l; t < n8; t += 8) {
+          const float qv = S.qh[t];
+          c1 = fadd(c1, fmul(qv, k1[t]));
+          c2 = fadd(c2, fmul(qv, k2[t]));
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          c1 = fadd(c1, __shfl_xor_sync(0xffffffffu, c1, o));
+          c2 = fadd(c2, __shfl_xor_sync(0xffffffffu, c2, o));
+        }
+        for (int t = n8; t < dh; t++) {
+          c1 = fadd(c1, fmul(S.qh[t], k1[t]));
+          c2 = fadd(c2, fmul(S.qh[t], k2[t]));
+        }
+        s1 = fmul(c1, a.scale);
+        s2 = fmul(c2, a.scale);
       };
       for (int p0 = 0; p0 < pos; p0 += ppc) {
         const int n = min(ppc, pos - p0);
         wait_full();
         const float *kc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
-        for (int b = 0; b < n; b += ngrp) {
-          const int pi = b + grp;
-          const bool valid = pi < n;
-          const float s = score(kc + (size_t)(valid ? pi : 0) * dh, false);
-          if (valid) {
-            if (l == 0) sc[p0 + pi] = s;
-            mx = s > mx ? s : mx;
+        for (int b = 0; b < n; b += 2 * ngrp) {
+          const int p1 = b + grp, p2 = b + ngrp + grp;
+          const bool v1 = p1 < n, v2 = p2 < n;
+          float s1, s2;
+          score2(kc + (size_t)(v1 ? p1 : 0) * dh, kc + (size_t)(v2 ? p2 : 0) * dh, s1, s2);
+          if (v1) {
+            if (l == 0) sc[p0 + p1] = s1;
+            mx = s1 > mx ? s1 : mx;
+          }
+          if (v2) {
+            if (l == 0) sc[p0 + p2] = s2;
+            mx = s2 > mx ? s2 : mx;
           }
         }
         bar_sync(NB_CONS, CONS);
@@ -521,12 +841,16 @@ struct Cons {
         rg.next();
       }
       if (cwarp == 0) {  // the position written by this step's qkv phase
-        const float s = score(a.kcache + cur, true);
+        float s, s_unused;
+        score2(kcur, kcur, s, s_unused);
         if (grp == 0) {
           if (l == 0) sc[pos] = s;
           mx = s > mx ? s : mx;
         }
       }
+      if (h == (int)blockIdx.x) mark(5 * L + 1, 0);
+      const bool tp = TRACE && a.trace && h == (int)blockIdx.x;
+      long long c0 = (tp && ctid == 0) ? clock64() : 0;
       mx = warp_max(mx);
       if (lane == 0) S.red[cwarp] = mx;
       bar_sync(NB_CONS, CONS);
@@ -539,29 +863,27 @@ struct Cons {
       const float M = S.red[32];
       for (int p = ctid; p <= pos; p += CONS) sc[p] = expf_lib(fsub(sc[p], M));
       bar_sync(NB_CONS, CONS);
+      if (tp && ctid == 0) {  // profile: max + exp
+        const long long c1 = clock64();
+        pacc(2, c1 - c0);
+        c0 = c1;
+      }
       // Weighted values: one chain per d over p (zero weights skipped); the
       // softmax sum is one more chain.
       const bool vw = cwarp < nvw;
       float vacc = 0.0f;
       if (ctid == nvw * 32) {
-        float sum = 0.0f;
-#pragma unroll 8
-        for (int p = 0; p <= pos; p++) sum = fadd(sum, sc[p]);
+        const long long s0 = tp ? clock64() : 0;
+        const float sum = chain_add(0.0f, sc, 1, pos + 1);
         S.red[33] = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+        if (tp) pacc(4, clock64() - s0);  // profile: softmax sum chain
       }
       for (int p0 = 0; p0 < pos; p0 += ppc) {
         const int n = min(ppc, pos - p0);
         if (vw) {
           wait_full();
           const float *vc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
-          if (ctid < dh) {
-#pragma unroll 8
-            for (int pi = 0; pi < n; pi++) {
-              const float e = sc[p0 + pi];
-              const float v = vc[(size_t)pi * dh + ctid];
-              if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
-            }
-          }
+          if (ctid < dh) vacc = chain_wv(vacc, sc + p0, vc + ctid, dh, n);
           bar_sync(NB_V, nvw * 32);
           if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
         }
@@ -569,12 +891,18 @@ struct Cons {
       }
       if (vw && ctid < dh) {
         const float e = sc[pos];
-        const float v = __ldcg(a.vcache + cur + ctid);
+        const float v = vcur[ctid];
         if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
+      }
+      if (tp && ctid == 0) {  // profile: value chains
+        const long long c1 = clock64();
+        pacc(3, c1 - c0);
+        c0 = c1;
       }
       bar_sync(NB_CONS, CONS);
       if (vw && ctid < dh) a.att[(size_t)h * dh + ctid] = fmul(vacc, S.red[33]);
       bar_sync(NB_CONS, CONS);
+      if (tp && ctid == 0) pacc(5, clock64() - c0);  // profile: output
     }
   }
 
@@ -585,7 +913,7 @@ struct Cons {
     }
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {
-      trace(a.n_trace - 1);
+      mark(5 * a.n_layer, 1);  // 1 + 40L + 1
       __threadfence();
       const unsigned prev = atomicAdd(a.sync + 1, 1u);
       if (prev == gridDim.x - 1) {  // the last CTA: greedy pick over the per-CTA candidates
@@ -615,66 +943,83 @@ struct Cons {
   }
 
   __device__ void run() {
-    trace(0);
+    if ((TRACE && a.trace) && ctid == 0) stamp(0, gtime());
+    prefetch_norm(a.layers[0].attn_norm, a.n_embd);
     embed();
     const int qdim = a.n_head * a.dh;
     for (int L = 0; L < a.n_layer; L++) {
       const DecLayer &Ly = a.layers[L];
       if (L > 0) stage(a.x, a.n_embd);
-      norm_q8(Ly.attn_norm, a.n_embd);
+      norm_q8(a.n_embd);
+      mark(5 * L, 0);
       run_mv(4 * L);
       if (grid_sync()) return;
       attention(L);
       if (grid_sync()) return;
+      prefetch_norm(Ly.ffn_norm, a.n_embd);  // the qkv norm is done with the buffer
       stage(a.att, qdim);
       q8(qdim);
+      mark(5 * L + 2, 0);
       run_mv(4 * L + 1);
       if (grid_sync()) return;
       stage(a.x, a.n_embd);
-      norm_q8(Ly.ffn_norm, a.n_embd);
+      norm_q8(a.n_embd);
+      mark(5 * L + 3, 0);
       run_mv(4 * L + 2);
       if (grid_sync()) return;
+      prefetch_norm(L + 1 < a.n_layer ? a.layers[L + 1].attn_norm : a.out_norm, a.n_embd);
       stage(a.h, a.n_ff);
       q8(a.n_ff);
+      mark(5 * L + 4, 0);
       run_mv(4 * L + 3);
       if (grid_sync()) return;
     }
     stage(a.x, a.n_embd);
-    norm_q8(a.out_norm, a.n_embd);
+    norm_q8(a.n_embd);
+    mark(5 * a.n_layer, 0);
     run_mv(4 * a.n_layer);
     finish();
   }
 };
 
+template <bool TRACE>
 __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  const Layout L = dk_layout(a.n_embd, a.n_ff, a.n_head * a.dh, a.n_ctx);
+  const Layout L = dk_layout(a.n_embd, a.n_ff, a.n_head * a.dh, a.n_ctx, a.n_layer);
   const Smem S = carve(smem_raw, L);
   if (threadIdx.x == 0) {
     for (int i = 0; i < DK_NS; i++) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.empty[i], 1);
     }
-    S.flag[0] = 0;
+    for (int i = 0; i < 4; i++) S.flag[i] = 0;
+    for (int i = 0; i < 8; i++) S.prof[i] = 0ull;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   const int pos = *a.pos;
   const DChunk *ch = a.chunks + a.cta_chunk0[blockIdx.x];
-  const int *ph = a.phase0 + (size_t)blockIdx.x * (a.n_phase + 1);
+  const int *ph_g = a.phase0 + (size_t)blockIdx.x * (a.n_phase + 1);
+  for (int i = threadIdx.x; i <= a.n_phase; i += DK_THREADS) S.ph[i] = ph_g[i];
+  for (int i = threadIdx.x; i < a.half; i += DK_THREADS) {
+    S.rope[i] = a.rope_cos[(size_t)pos * a.half + i];
+    S.rope[128 + i] = a.rope_sin[(size_t)pos * a.half + i];
+  }
+  __syncthreads();
+  const int *ph = S.ph;
   if (threadIdx.x < 32) {
-    if (threadIdx.x == 0) producer(a, S, pos, ch, ph);
+    if (threadIdx.x == 0) producer<TRACE>(a, S, pos, ch, ph);
     return;
   }
-  Cons c(a, S, ch, ph, pos);
+  Cons<TRACE> c(a, S, ch, ph, pos);
   c.run();
 }
 
 }  // namespace
 
-size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh) {
+size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh, int n_layer) {
   if (dh <= 0 || dh > 256 || dh % 4 != 0 || DK_SLOT / (dh * 4) < 1) return 0;
-  const Layout L = dk_layout(n_embd, n_ff, qdim, n_ctx);
+  const Layout L = dk_layout(n_embd, n_ff, qdim, n_ctx, n_layer);
   return L.total <= 227 * 1024 ? L.total : 0;
 }
 
@@ -686,10 +1031,11 @@ int decode_grid() {
 }
 
 cudaError_t prepare_decode(size_t smem, int grid) {
-  cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(k_decode<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_decode<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, DK_THREADS, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<false>, DK_THREADS, smem);
   if (e != cudaSuccess) return e;
   return per_sm >= 1 && grid <= per_sm * decode_grid() ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
 }
@@ -705,7 +1051,7 @@ cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_decode, a);
+  return a.trace ? cudaLaunchKernelEx(&cfg, k_decode<true>, a) : cudaLaunchKernelEx(&cfg, k_decode<false>, a);
 }
 
 
@@ -855,12 +1201,12 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
                        int n_kv, int dh, int n_ctx, int grid, DecodePlan &plan, std::string &why) {
   plan = DecodePlan{};
   plan.grid = grid;
-  plan.smem = decode_smem_bytes(n_embd, n_ff, n_head * dh, n_ctx, dh);
+  plan.smem = decode_smem_bytes(n_embd, n_ff, n_head * dh, n_ctx, dh, (int)layers.size());
   if (!plan.smem) {
     why = "model does not fit the persistent kernel's shared memory";
     return false;
   }
-  if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv) {
+  if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv || 2 * ((n_embd / 2 + grid - 1) / grid) > DK_XO) {
     why = "unsupported dimensions";
     return false;
   }

@@ -18,7 +18,7 @@
 
 namespace pk {
 
-constexpr int DK_THREADS = 512;     // warp 0 producer, warp 1 row chains, warps 2..15 terms
+constexpr int DK_THREADS = 384;     // warp 0 producer, warp 1 row chains, warps 2..11 terms
 constexpr int DK_NS = 5;            // ring slots
 constexpr int DK_SLOT = 32768;      // bytes per slot
 constexpr int DK_TS = 2560;         // floats per term buffer (two buffers)
@@ -91,7 +91,7 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
                        int n_kv, int dh, int n_ctx, int grid, DecodePlan &plan, std::string &why);
 
 // Shared memory the kernel needs for this model (0 if it does not fit).
-size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh);
+size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh, int n_layer);
 // Sets the kernel's shared-memory limit and checks that `grid` CTAs fit at once.
 cudaError_t prepare_decode(size_t smem, int grid);
 cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream_t st);

@@ -369,7 +369,7 @@ int Engine::setup_decode() {
     decode_why_ = "the persistent kernel's grid does not fit the device at once";
     return PK_OK;
   }
-  const int n_trace = 5 * c.n_layer + 2;
+  const int n_trace = 1 + 40 * c.n_layer + 2 + c.n_layer + 1;
   const size_t n_ch = plan_.chunks.size() * sizeof(DChunk), n_c0 = plan_.cta_chunk0.size() * 4,
                n_ph = plan_.phase0.size() * 4, n_own = plan_.own.size() * 4, n_ly = dl.size() * sizeof(DecLayer),
                n_tr = (size_t)grid * n_trace * 8;
@@ -862,44 +862,72 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
   if (e != cudaSuccess) return cuda_error(e, "decode_profile");
   if (use_decode_) {
     if ((rc = check_decode_error())) return rc;
-    // Phase times inside the persistent kernel from its per-CTA timestamps:
-    // stamp 0 at the start, stamp g after grid barrier g, the last at the end.
+    // Phase times inside the persistent kernel from its per-CTA trace (layout
+    // in pk_decode.cu): wall time per phase from the barrier exits, and per
+    // CTA averages of prologue, compute, barrier wait and ring-data stall.
     const Config &c = cfg_;
-    const int nt = dargs_.n_trace, grid = plan_.grid;
+    const int nt = dargs_.n_trace, grid = plan_.grid, nl = c.n_layer;
     std::vector<unsigned long long> tr((size_t)grid * nt);
     PK_CK(cudaMemcpyAsync(tr.data(), d_trace_, tr.size() * 8, cudaMemcpyDeviceToHost, st_));
     PK_CK(cudaStreamSynchronize(st_));
-    std::vector<double> T(nt);
-    for (int i = 0; i < nt; i++) {
-      unsigned long long v = tr[i];
-      for (int g = 1; g < grid; g++) {
-        const unsigned long long w = tr[(size_t)g * nt + i];
-        v = i == 0 ? std::min(v, w) : std::max(v, w);
-      }
-      T[i] = (double)v;
-    }
+    auto at = [&](int g, int i) { return (double)tr[(size_t)g * nt + i]; };
+    int khz = 0;
+    PK_CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device_));
+    const double cyc_ms = 1.0 / std::max(1.0, (double)khz);  // SM cycles -> ms at the rated clock
+    auto exit_of = [&](int g, int q) { return q < 0 ? at(g, 0) : at(g, 1 + 8 * q + 2); };
+    auto max_exit = [&](int q) {
+      double v = 0;
+      for (int g = 0; g < grid; g++) v = std::max(v, exit_of(g, q));
+      return v;
+    };
     const char *names[6] = {"dk_qkv", "dk_attn", "dk_o", "dk_gateup", "dk_down", "dk_head"};
-    double ms[6] = {0, 0, 0, 0, 0, 0}, bytes[6] = {0, 0, 0, 0, 0, 0};
+    const char *subs[7] = {"prologue", "compute", "barrier", "data_wait", "term_bufwait", "term_work", "chain_wait"};
+    double wall[6] = {0}, sub[6][8] = {{0}}, bytes[6] = {0};
     const double f4 = 4.0, kvp = (double)next_pos_ + 1.0;
-    for (int L = 0; L < c.n_layer; L++) {
+    for (int q = 0; q < 5 * nl; q++) {
+      const int j = q % 5;
+      wall[j] += (max_exit(q) - max_exit(q - 1)) * 1e-6;
+      // attention sub-phases: only the CTAs that own a head stamp them
+      const int ng = j == 1 ? std::min(grid, c.n_head) : grid;
+      for (int g = 0; g < ng; g++) {
+        const int b0 = 1 + 8 * q;
+        sub[j][0] += (at(g, b0) - exit_of(g, q - 1)) * 1e-6 / ng;
+        sub[j][1] += (at(g, b0 + 1) - at(g, b0)) * 1e-6 / ng;
+        sub[j][2] += (at(g, b0 + 2) - at(g, b0 + 1)) * 1e-6 / ng;
+        for (int i = 3; i < 8; i++) sub[j][i] += at(g, b0 + i) * cyc_ms / ng;
+      }
+    }
+    double head_end = 0, prod = 0;
+    for (int g = 0; g < grid; g++) {
+      head_end = std::max(head_end, at(g, 1 + 40 * nl + 1));
+      sub[5][0] += (at(g, 1 + 40 * nl) - exit_of(g, 5 * nl - 1)) * 1e-6 / grid;
+      sub[5][1] += (at(g, 1 + 40 * nl + 1) - at(g, 1 + 40 * nl)) * 1e-6 / grid;
+      for (int L = 0; L <= nl; L++) prod += at(g, 1 + 40 * nl + 2 + L) * cyc_ms / grid;
+    }
+    wall[5] = (head_end - max_exit(5 * nl - 1)) * 1e-6;
+    for (int L = 0; L < nl; L++) {
       const LayerDev &Y = layers_[L];
-      for (int j = 0; j < 5; j++) ms[j] += (T[5 * L + j + 1] - T[5 * L + j]) * 1e-6;
       bytes[0] += mat_stream_bytes(Y.q) + mat_stream_bytes(Y.k) + mat_stream_bytes(Y.v) + c.n_embd * f4;
       bytes[1] += 2.0 * c.n_head_kv * kvp * c.head_dim * f4;
       bytes[2] += mat_stream_bytes(Y.o);
       bytes[3] += mat_stream_bytes(Y.gate) + mat_stream_bytes(Y.up) + c.n_embd * f4;
       bytes[4] += mat_stream_bytes(Y.down);
     }
-    ms[5] = (T[nt - 1] - T[nt - 2]) * 1e-6;
     bytes[5] = mat_stream_bytes(output_) + c.n_embd * f4 + embd_row_bytes_;
-    for (int j = 0; j < 6; j++) {
+    auto add = [&](const std::string &n, int launches, double ms, double by) {
       pk_kernel_stat st{};
-      std::snprintf(st.name, sizeof(st.name), "%s", names[j]);
-      st.launches = j == 5 ? 1 : c.n_layer;
-      st.ms = ms[j];
-      st.bytes = bytes[j];
+      std::snprintf(st.name, sizeof(st.name), "%s", n.c_str());
+      st.launches = launches;
+      st.ms = ms;
+      st.bytes = by;
       agg.push_back(st);
-    }
+    };
+    for (int j = 0; j < 6; j++) add(names[j], j == 5 ? 1 : nl, wall[j], bytes[j]);
+    // Sub-phase averages over CTAs (bytes 0: not kernels of their own).
+    for (int j = 0; j < 6; j++)
+      for (int i = 0; i < (j == 5 ? 2 : 8); i++)
+        add(std::string(names[j]) + "/" + (i < 7 ? subs[i] : "chain_work"), j == 5 ? 1 : nl, sub[j][i], 0.0);
+    add("dk_producer/slot_wait", 1, prod, 0.0);
   }
   uint32_t tok = 0;
   PK_CK(cudaMemcpyAsync(&tok, d_tok_, 4, cudaMemcpyDeviceToHost, st_));

@@ -146,19 +146,33 @@ template <> struct GroupW<T_Q4_K> {
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 256 + sb0 * 32);
     const int4 a00 = ap[0], a01 = ap[1], a10 = ap[2], a11 = ap[3];
-    int d0 = 0, d1 = 0;
-    d0 = __dp4a(lo4(w0.x), a00.x, d0); d0 = __dp4a(lo4(w0.y), a00.y, d0);
-    d0 = __dp4a(lo4(w0.z), a00.z, d0); d0 = __dp4a(lo4(w0.w), a00.w, d0);
-    d0 = __dp4a(lo4(w1.x), a01.x, d0); d0 = __dp4a(lo4(w1.y), a01.y, d0);
-    d0 = __dp4a(lo4(w1.z), a01.z, d0); d0 = __dp4a(lo4(w1.w), a01.w, d0);
-    d1 = __dp4a(hi4(w0.x), a10.x, d1); d1 = __dp4a(hi4(w0.y), a10.y, d1);
-    d1 = __dp4a(hi4(w0.z), a10.z, d1); d1 = __dp4a(hi4(w0.w), a10.w, d1);
-    d1 = __dp4a(hi4(w1.x), a11.x, d1); d1 = __dp4a(hi4(w1.y), a11.y, d1);
-    d1 = __dp4a(hi4(w1.z), a11.z, d1); d1 = __dp4a(hi4(w1.w), a11.w, d1);
+    // integer sums are exact in any order: two partial chains each
+    int d0a = 0, d0b = 0, d1a = 0, d1b = 0;
+    d0a = __dp4a(lo4(w0.x), a00.x, d0a); d0b = __dp4a(lo4(w0.y), a00.y, d0b);
+    d0a = __dp4a(lo4(w0.z), a00.z, d0a); d0b = __dp4a(lo4(w0.w), a00.w, d0b);
+    d0a = __dp4a(lo4(w1.x), a01.x, d0a); d0b = __dp4a(lo4(w1.y), a01.y, d0b);
+    d0a = __dp4a(lo4(w1.z), a01.z, d0a); d0b = __dp4a(lo4(w1.w), a01.w, d0b);
+    d1a = __dp4a(hi4(w0.x), a10.x, d1a); d1b = __dp4a(hi4(w0.y), a10.y, d1b);
+    d1a = __dp4a(hi4(w0.z), a10.z, d1a); d1b = __dp4a(hi4(w0.w), a10.w, d1b);
+    d1a = __dp4a(hi4(w1.x), a11.x, d1a); d1b = __dp4a(hi4(w1.y), a11.y, d1b);
+    d1a = __dp4a(hi4(w1.z), a11.z, d1a); d1b = __dp4a(hi4(w1.w), a11.w, d1b);
+    const int d0 = d0a + d0b, d1 = d1a + d1b;
     const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
+    // get_scale_min_k4 (quant.rs:80-86) for sub-blocks sb0 and sb0 + 1; the
+    // 12 scale bytes are hdr.y | hdr.z | hdr.w.
+    const int sh = (sb0 & 3) * 8;
     int sc0, m0, sc1, m1;
-    scale_min_k4(hdr, sb0, sc0, m0);
-    scale_min_k4(hdr, sb0 + 1, sc1, m1);
+    if (sb0 < 4) {
+      sc0 = (int)((hdr.y >> sh) & 63u);
+      m0 = (int)((hdr.z >> sh) & 63u);
+      sc1 = (int)((hdr.y >> (sh + 8)) & 63u);
+      m1 = (int)((hdr.z >> (sh + 8)) & 63u);
+    } else {
+      sc0 = (int)(((hdr.w >> sh) & 0xFu) | ((hdr.y >> (sh + 2)) & 0x30u));
+      m0 = (int)(((hdr.w >> (sh + 4)) & 0xFu) | ((hdr.z >> (sh + 2)) & 0x30u));
+      sc1 = (int)(((hdr.w >> (sh + 8)) & 0xFu) | ((hdr.y >> (sh + 10)) & 0x30u));
+      m1 = (int)(((hdr.w >> (sh + 12)) & 0xFu) | ((hdr.z >> (sh + 10)) & 0x30u));
+    }
     const int ai = blk * 8 + sb0;
     const float da0 = A.d[ai], da1 = A.d[ai + 1];
     const int sa0 = A.s[ai], sa1 = A.s[ai + 1];
@@ -204,15 +218,18 @@ template <> struct GroupW<T_Q6_K> {
   }
   // quant_int.rs:397-413: acc += d*scale*da*dot per 16-element piece, order (half, g, s).
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+    // scales of this half: bytes h*8 .. h*8+7 of the 16 scale bytes
+    const unsigned long long sw = h ? ((unsigned long long)scv.w << 32 | scv.z) : ((unsigned long long)scv.y << 32 | scv.x);
 #pragma unroll
     for (int s = 0; s < 4; s++) {
       const int4 a = *reinterpret_cast<const int4 *>(A.q + blk * 256 + (4 * h + s) * 32 + g * 16);
-      int dot = 0;
-      dot = __dp4a(q[s][0], a.x, dot);
-      dot = __dp4a(q[s][1], a.y, dot);
-      dot = __dp4a(q[s][2], a.z, dot);
-      dot = __dp4a(q[s][3], a.w, dot);
-      const float scale = (float)(int8_t)byte_of(scv, h * 8 + g + 2 * s);
+      int pa = 0, pb = 0;
+      pa = __dp4a(q[s][0], a.x, pa);
+      pb = __dp4a(q[s][1], a.y, pb);
+      pa = __dp4a(q[s][2], a.z, pa);
+      pb = __dp4a(q[s][3], a.w, pb);
+      const int dot = pa + pb;
+      const float scale = (float)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s)));
       const float da = A.d[blk * 8 + 4 * h + s];
       t[s] = fmul(fmul(fmul(d, scale), da), (float)dot);
     }
@@ -240,11 +257,12 @@ template <> struct GroupW<T_Q8_0> {
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
     const int4 a0 = ap[0], a1 = ap[1];
-    int dot = 0;
-    dot = __dp4a((int)w0.x, a0.x, dot); dot = __dp4a((int)w0.y, a0.y, dot);
-    dot = __dp4a((int)w0.z, a0.z, dot); dot = __dp4a((int)w0.w, a0.w, dot);
-    dot = __dp4a((int)w1.x, a1.x, dot); dot = __dp4a((int)w1.y, a1.y, dot);
-    dot = __dp4a((int)w1.z, a1.z, dot); dot = __dp4a((int)w1.w, a1.w, dot);
+    int da = 0, db = 0;
+    da = __dp4a((int)w0.x, a0.x, da); db = __dp4a((int)w0.y, a0.y, db);
+    da = __dp4a((int)w0.z, a0.z, da); db = __dp4a((int)w0.w, a0.w, db);
+    da = __dp4a((int)w1.x, a1.x, da); db = __dp4a((int)w1.y, a1.y, db);
+    da = __dp4a((int)w1.z, a1.z, da); db = __dp4a((int)w1.w, a1.w, db);
+    const int dot = da + db;
     t[0] = fmul(fmul(d, A.d[blk]), (float)dot);
   }
 };
@@ -267,11 +285,12 @@ template <> struct GroupW<T_Q4_0> {
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
     const int4 a0 = ap[0], a1 = ap[1];
-    int dot = 0;
-    dot = __dp4a(lo4(w.x), a0.x, dot); dot = __dp4a(lo4(w.y), a0.y, dot);
-    dot = __dp4a(lo4(w.z), a0.z, dot); dot = __dp4a(lo4(w.w), a0.w, dot);
-    dot = __dp4a(hi4(w.x), a1.x, dot); dot = __dp4a(hi4(w.y), a1.y, dot);
-    dot = __dp4a(hi4(w.z), a1.z, dot); dot = __dp4a(hi4(w.w), a1.w, dot);
+    int da = 0, db = 0;
+    da = __dp4a(lo4(w.x), a0.x, da); db = __dp4a(lo4(w.y), a0.y, db);
+    da = __dp4a(lo4(w.z), a0.z, da); db = __dp4a(lo4(w.w), a0.w, db);
+    da = __dp4a(hi4(w.x), a1.x, da); db = __dp4a(hi4(w.y), a1.y, db);
+    da = __dp4a(hi4(w.z), a1.z, da); db = __dp4a(hi4(w.w), a1.w, db);
+    const int dot = da + db;
     t[0] = fmul(fmul(d, A.d[blk]), fsub((float)dot, fmul(8.0f, (float)A.s[blk])));
   }
 };
