@@ -42,6 +42,9 @@ def parse_args():
     p.add_argument("--model-dir", default=os.environ.get("PK_MODEL_DIR", tempfile.gettempdir()))
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the bounded CPU baseline sample")
+    p.add_argument("--layers", type=int, default=None,
+                   help="M26-shaped model with this many layers (the small case for detailed ncu captures)")
+    p.add_argument("--vocab", type=int, default=None, help="vocabulary of that model (default M26's)")
     p.add_argument("--profile-window", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return p.parse_args()
@@ -165,8 +168,8 @@ def run_reference(args):
     import pko
     from pocketinfer import synth
 
-    path = synth.m26_path(args.model_dir)
-    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.M26.n_vocab)
+    path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
+    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.m26_spec(args.layers, args.vocab).n_vocab)
     threads = os.cpu_count() or 1
     o = pko.Engine(path, 512, threads)
     o.generate(prompt, 1)  # prefill (Engine::generate's 32-token chunks), no decode step
@@ -221,11 +224,11 @@ def run_ours(args):
     from pocketinfer import replicas, synth
 
     if rank == 0:
-        path = synth.m26_path(args.model_dir)
+        path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
     if dist:
         dist.barrier()
-    path = synth.m26_path(args.model_dir)
-    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.M26.n_vocab)
+    path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
+    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.m26_spec(args.layers, args.vocab).n_vocab)
     eng = pk.Engine(path, n_ctx=512, max_batch=32, device=local)
     info = eng.info
     # prefill through Engine::generate (32-token chunks); no decode step
@@ -278,7 +281,7 @@ def run_ours(args):
         hbm, peak_kind = peaks()
         dom = max(prof, key=lambda p: p["ms"])
         achieved = dom["bytes"] / (dom["ms"] / 1000.0) / 1e9
-        step_bytes = info["stream_bytes"] + synth.M26.kv_bytes_per_position() * (PROMPT_LEN + 1 + CYCLE / 2)
+        step_bytes = info["stream_bytes"] + synth.m26_spec(args.layers, args.vocab).kv_bytes_per_position() * (PROMPT_LEN + 1 + CYCLE / 2)
         step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
         # persistent kernel: one launch per step, plus argmax + advance once per decode_steps_device call
         calls = -(-args.steps // CYCLE) + 1
@@ -287,8 +290,10 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8xint8->int32, f32", "data": "synthetic",
-            "config": {"workload": "M26 greedy decode b=1 (BASELINE config 3): 323-token prompt, positions "
-                                   "323..450 cycled", "model": "synthetic-2.6B-q4km (random blocks)",
+            "config": {"workload": ("M26 greedy decode b=1 (BASELINE config 3): 323-token prompt, positions "
+                                    "323..450 cycled") if args.layers is None and args.vocab is None else
+                       f"reduced M26-shaped model {synth.m26_spec(args.layers, args.vocab).name} (profiling case, "
+                       "not the BASELINE workload)", "model": "synthetic-2.6B-q4km (random blocks)",
                        "global_batch": world, "seq_len": PROMPT_LEN + CYCLE,
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "no flush: each step streams 1.83 GB of weights (> 126 MB L2)"},

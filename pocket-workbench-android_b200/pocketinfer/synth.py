@@ -295,13 +295,27 @@ def config2_inputs(ttype: int, k: int, rows: int, seed: int = 0):
     return w, x
 
 
-def m26_path(directory: str, seed: int = 0) -> str:
-    """Path of the cached M26 GGUF in ``directory``, writing it on first use."""
+def m26_spec(n_layer: int | None = None, n_vocab: int | None = None) -> ModelSpec:
+    """M26, or an M26-shaped model with fewer layers / a smaller vocabulary
+    (same per-layer matrices: the small case used for detailed profiles)."""
+    import dataclasses
+
+    if n_layer is None and n_vocab is None:
+        return M26
+    return dataclasses.replace(M26, name=f"m26-{n_layer or M26.n_layer}l-{n_vocab or M26.n_vocab}v",
+                               n_layer=n_layer or M26.n_layer, n_vocab=n_vocab or M26.n_vocab)
+
+
+def m26_path(directory: str, seed: int = 0, spec: ModelSpec | None = None) -> str:
+    """Path of the cached M26 (or ``spec``) GGUF in ``directory``, written on first use."""
     import os
 
-    p = os.path.join(directory, f"pk_m26_seed{seed}.gguf")
+    spec = spec or M26
+    tag = "m26" if spec is M26 else spec.name
+    os.makedirs(directory, exist_ok=True)
+    p = os.path.join(directory, f"pk_{tag}_seed{seed}.gguf")
     if not os.path.exists(p):
         tmp = f"{p}.{os.getpid()}.tmp"
-        write_gguf(tmp, M26, seed=seed)
+        write_gguf(tmp, spec, seed=seed)
         os.replace(tmp, p)
     return p
