@@ -15,10 +15,11 @@
 //   warp 0, lane 0   producer: walks the chunk list (plus the K/V history of
 //                    the attention heads this CTA owns) and bulk-copies each
 //                    chunk into the next free ring slot (mbarrier complete_tx);
-//   warps 2..11      term warps: integer dots + float terms of a chunk into a
-//                    term buffer (two buffers, alternating);
-//   warp 1           chain warp: one lane per row adds that row's terms in
-//                    the reference's order and runs the epilogue.
+//   warps 3..11      term warps: integer dots + float terms of a chunk into a
+//                    term buffer (DK_NB buffers, in turn);
+//   warps 1, 2       chain warps: one lane per row adds that row's terms in
+//                    the reference's order and runs the epilogue; each row
+//                    group is assigned to one of them by the plan.
 // Between the phases of a layer (qkv | attention | o | gate+up | down) the
 // consumers meet at a grid barrier; the producer does not, so the weights of
 // the next phases keep streaming in while the barrier resolves.
@@ -42,9 +43,14 @@
 namespace pk {
 namespace {
 
-constexpr int CONS = DK_THREADS - 32;    // consumer threads (warps 1..11)
-constexpr int TERM_T = DK_THREADS - 64;  // term threads (warps 2..11)
-constexpr int NB_CONS = 1, NB_FULLT = 2, NB_EMPTYT = 4, NB_V = 6;
+constexpr int CONS = DK_THREADS - 32;                        // consumer threads (warps 1..11)
+constexpr int TERM_T = DK_THREADS - 32 - 32 * DK_CHAINS;     // term threads (warps 3..11)
+// Named barriers: all consumers; per (term buffer, chain warp) "terms ready"
+// and "buffer free" pairs (a barrier id is only ever shared by the term warps
+// and ONE chain warp, so generations cannot mix); the value-chain warps.
+constexpr int NB_CONS = 1, NB_FULLT = 2, NB_EMPTYT = 2 + DK_NB * DK_CHAINS, NB_V = 2 + 2 * DK_NB * DK_CHAINS;
+static_assert(NB_V < 16, "named barrier ids");
+constexpr int NB_PAIR = TERM_T + 32;                         // term threads + one chain warp
 constexpr unsigned long long WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -117,10 +123,11 @@ __device__ __forceinline__ const uint8_t *align16_down(const uint8_t *p) {
 
 // Shared memory layout (host and device agree through dk_layout).
 struct Layout {
-  size_t ring, full, empty, desc, aq, ad, as, u, qh, rope, xo, ph, nw, red, flag, prof, total;
+  size_t ring, full, empty, desc, aq, ad, as, u, qh, rope, xo, ph, nw, cwb, red, flag, prof, total;
   int kmax, uf;
 };
-constexpr int DK_XO = 256;  // owned rows of x kept in shared memory
+constexpr int DK_XO = 256;   // owned rows of x kept in shared memory
+constexpr int DK_CWW = 64;   // words of chain-warp bits (chunks per CTA < 32 * DK_CWW - 31)
 
 __host__ __device__ inline size_t up16(size_t x) { return (x + 15) & ~(size_t)15; }
 
@@ -129,7 +136,7 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
   int km = n_embd > n_ff ? n_embd : n_ff;
   km = km > qdim ? km : qdim;
   L.kmax = (km + 15) / 16 * 16;
-  int uf = 2 * DK_TS;
+  int uf = DK_NB * DK_TS;
   uf = uf > km ? uf : km;
   uf = uf > n_ctx ? uf : n_ctx;
   L.uf = (uf + 3) / 4 * 4;
@@ -148,6 +155,7 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
   L.xo = o; o += DK_XO * 4;
   L.ph = o; o += up16((size_t)(4 * n_layer + 2) * 4);
   L.nw = o; o += up16((size_t)n_embd * 4);  // the next RMSNorm's weights
+  L.cwb = o; o += DK_CWW * 4;               // chain-warp bit per chunk of this CTA
   L.red = o; o += 64 * 4;
   L.flag = o; o += 16;  // [0] abort
   L.prof = o; o += 8 * 8;  // profile cycle accumulators
@@ -161,6 +169,7 @@ struct Smem {
   DChunk *desc;
   float *rope, *xo, *nw;
   int *ph;
+  uint32_t *cwb;
   int8_t *aq;
   float *ad;
   int32_t *as;
@@ -179,6 +188,7 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const Layout &L) {
   s.xo = (float *)(base + L.xo);
   s.nw = (float *)(base + L.nw);
   s.ph = (int *)(base + L.ph);
+  s.cwb = (uint32_t *)(base + L.cwb);
   s.aq = (int8_t *)(base + L.aq);
   s.ad = (float *)(base + L.ad);
   s.as = (int32_t *)(base + L.as);
@@ -233,20 +243,22 @@ __device__ __forceinline__ void q8_block8(const float4 v, int l8, bool store, in
   }
 }
 
-// Sequential float chains.  The reference adds terms one at a time, so only
-// the add itself may sit on the dependency path: operands are loaded a batch
-// of eight ahead of the adds that consume them.
+// Sequential float chains over shared memory (shared addresses, byte
+// strides).  The reference adds terms one at a time, so only the add itself
+// may sit on the dependency path: operands are loaded a batch of eight ahead
+// of the adds that consume them.
 //   acc + p[0] + p[s] + ... + p[(n-1)s], in that order.
-__device__ __forceinline__ float chain_add(float acc, const float *p, int s, int n) {
+__device__ __forceinline__ float chain_add(float acc, uint32_t p, uint32_t s, int n) {
   int j = 0;
   if (n >= 8) {
     float cur[8];
 #pragma unroll
-    for (int u = 0; u < 8; u++) cur[u] = p[u * s];
+    for (int u = 0; u < 8; u++) cur[u] = sld_f(p + u * s);
     for (j = 8; j + 8 <= n; j += 8) {
       float nxt[8];
+      const uint32_t q = p + (uint32_t)j * s;
 #pragma unroll
-      for (int u = 0; u < 8; u++) nxt[u] = p[(j + u) * s];
+      for (int u = 0; u < 8; u++) nxt[u] = sld_f(q + u * s);
 #pragma unroll
       for (int u = 0; u < 8; u++) acc = fadd(acc, cur[u]);
 #pragma unroll
@@ -255,21 +267,22 @@ __device__ __forceinline__ float chain_add(float acc, const float *p, int s, int
 #pragma unroll
     for (int u = 0; u < 8; u++) acc = fadd(acc, cur[u]);
   }
-  for (; j < n; j++) acc = fadd(acc, p[j * s]);
+  for (; j < n; j++) acc = fadd(acc, sld_f(p + (uint32_t)j * s));
   return acc;
 }
 
 // fma(p[(n-1)s], p[(n-1)s], ... fma(p[0], p[0], acc)): one f32_sum_sq lane.
-__device__ __forceinline__ float chain_sq(float acc, const float *p, int s, int n) {
+__device__ __forceinline__ float chain_sq(float acc, uint32_t p, uint32_t s, int n) {
   int j = 0;
   if (n >= 8) {
     float cur[8];
 #pragma unroll
-    for (int u = 0; u < 8; u++) cur[u] = p[u * s];
+    for (int u = 0; u < 8; u++) cur[u] = sld_f(p + u * s);
     for (j = 8; j + 8 <= n; j += 8) {
       float nxt[8];
+      const uint32_t q = p + (uint32_t)j * s;
 #pragma unroll
-      for (int u = 0; u < 8; u++) nxt[u] = p[(j + u) * s];
+      for (int u = 0; u < 8; u++) nxt[u] = sld_f(q + u * s);
 #pragma unroll
       for (int u = 0; u < 8; u++) acc = __fmaf_rn(cur[u], cur[u], acc);
 #pragma unroll
@@ -278,50 +291,65 @@ __device__ __forceinline__ float chain_sq(float acc, const float *p, int s, int 
 #pragma unroll
     for (int u = 0; u < 8; u++) acc = __fmaf_rn(cur[u], cur[u], acc);
   }
-  for (; j < n; j++) acc = __fmaf_rn(p[j * s], p[j * s], acc);
+  for (; j < n; j++) {
+    const float x = sld_f(p + (uint32_t)j * s);
+    acc = __fmaf_rn(x, x, acc);
+  }
   return acc;
 }
 
 // acc + e_0*v_0 + e_1*v_1 + ... with the terms of zero weights skipped
 // (model.rs:1076-1085).  A skipped term adds -0.0, which leaves every float
 // (signed zeros and NaN included) unchanged, so the product and the choice
-// stay off the dependency path.
-__device__ __forceinline__ float chain_wv(float acc, const float *e, const float *v, int vs, int n) {
+// stay off the dependency path.  e: 4-byte stride, v: byte stride vs.
+__device__ __forceinline__ float chain_wv(float acc, uint32_t e, uint32_t v, uint32_t vs, int n) {
+  // e is 16-byte aligned: the weights of eight positions come in two vector loads
   auto term = [](float ew, float vv) { return ew != 0.0f ? fmul(ew, vv) : -0.0f; };
   int j = 0;
   if (n >= 8) {
-    float ce[8], cv[8];
+    float4 ca = sld_v4f(e), cb = sld_v4f(e + 16);
+    float cv[8];
 #pragma unroll
-    for (int u = 0; u < 8; u++) {
-      ce[u] = e[u];
-      cv[u] = v[u * vs];
-    }
+    for (int u = 0; u < 8; u++) cv[u] = sld_f(v + u * vs);
     for (j = 8; j + 8 <= n; j += 8) {
-      float ne[8], nv[8];
+      const float4 na = sld_v4f(e + 4 * j), nb = sld_v4f(e + 4 * j + 16);
+      float nv[8];
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        ne[u] = e[j + u];
-        nv[u] = v[(j + u) * vs];
-      }
+      for (int u = 0; u < 8; u++) nv[u] = sld_f(v + (uint32_t)(j + u) * vs);
+      const float ce[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
       for (int u = 0; u < 8; u++) acc = fadd(acc, term(ce[u], cv[u]));
+      ca = na;
+      cb = nb;
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        ce[u] = ne[u];
-        cv[u] = nv[u];
-      }
+      for (int u = 0; u < 8; u++) cv[u] = nv[u];
     }
+    const float ce[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
     for (int u = 0; u < 8; u++) acc = fadd(acc, term(ce[u], cv[u]));
   }
-  for (; j < n; j++) acc = fadd(acc, term(e[j], v[j * vs]));
+  for (; j < n; j++) acc = fadd(acc, term(sld_f(e + 4 * j), sld_f(v + (uint32_t)j * vs)));
   return acc;
+}
+
+// A chunk descriptor copied from shared memory into registers.
+__device__ __forceinline__ DChunk load_desc(uint32_t a) {
+  DChunk c;
+  uint4 *w = reinterpret_cast<uint4 *>(&c);
+  w[0] = sld_v4(a);
+  w[1] = sld_v4(a + 16);
+  w[2] = sld_v4(a + 32);
+  w[3] = sld_v4(a + 48);
+  return c;
 }
 
 // Ring position shared by the producer and every consumer thread: both walk
 // the same sequence of transfers.
 struct Ring {
   uint32_t slot = 0, par = 0;
+  // slot and phase parity of the transfer j places ahead
+  __device__ uint32_t slot_at(int j) const { return (slot + j) % DK_NS; }
+  __device__ uint32_t par_at(int j) const { return par ^ (((slot + j) / DK_NS) & 1u); }
   __device__ void next() {
     if (++slot == DK_NS) {
       slot = 0;
@@ -331,8 +359,13 @@ struct Ring {
 };
 
 // ------------------------------------------------------------------ producer
+// The whole of warp 0: lane 0 claims each slot (bounded wait on its empty
+// barrier), writes the descriptor and arms the full barrier with the byte
+// count; then the lanes share out the copies (one per row of a split chunk,
+// one per dimension of a K chunk).
 template <bool TRACE>
 __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChunk *ch, const int *ph) {
+  const int lane = threadIdx.x & 31;
   Ring rg;
   uint32_t armed[DK_NS];
   bool used[DK_NS];
@@ -340,26 +373,33 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
   bool ok = true;
   unsigned long long pst = 0;  // SM cycles spent waiting for a free slot (profile trace)
   auto note = [&](int layer) {
-    if ((TRACE && a.trace)) {
-      const int i = 1 + 8 * 5 * a.n_layer + 2 + layer;
+    if ((TRACE && a.trace) && lane == 0) {
+      const int i = 1 + DK_TRW * (5 * a.n_layer + 1) + layer;
       if (i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = pst;
       pst = 0;
     }
   };
-  // Claim the next slot; false on abort / timeout.
-  auto claim = [&](uint32_t tx) -> uint8_t * {
-    const long long t0 = (TRACE && a.trace) ? clock64() : 0;
-    const bool got = mbar_wait(&S.empty[rg.slot], rg.par ^ 1u, S.flag, 20000u);
-    if ((TRACE && a.trace)) pst += (unsigned long long)(clock64() - t0);
-    if (!got) {
-      if (!*S.flag) atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
-      S.flag[0] = 1;
-      ok = false;
-      return nullptr;
+  // Claim the next slot for tx bytes (desc: the chunk descriptor, or null);
+  // false on abort / timeout, on every lane.
+  auto claim = [&](uint32_t tx, const DChunk *desc) -> bool {
+    int got = 1;
+    if (lane == 0) {
+      const long long t0 = (TRACE && a.trace) ? clock64() : 0;
+      got = mbar_wait(&S.empty[rg.slot], rg.par ^ 1u, S.flag, 20000u) ? 1 : 0;
+      if ((TRACE && a.trace)) pst += (unsigned long long)(clock64() - t0);
+      if (!got) {
+        if (!*S.flag) atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+        S.flag[0] = 1;
+      } else {
+        used[rg.slot] = true;
+        armed[rg.slot] = rg.par;
+        if (desc) S.desc[rg.slot] = *desc;  // visible to the consumers once the full barrier completes
+        mbar_expect(&S.full[rg.slot], tx);
+      }
     }
-    used[rg.slot] = true;
-    armed[rg.slot] = rg.par;
-    return S.ring + (size_t)rg.slot * DK_SLOT;
+    got = __shfl_sync(0xffffffffu, got, 0);
+    ok = got != 0;
+    return ok;
   };
   const int group = a.n_head / a.n_kv;
   const int ppc = DK_SLOT / (a.dh * 4);
@@ -369,17 +409,17 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
       const DChunk c = ch[ci];
       const uint32_t dl = c.d ? c.d_len : 0u;
       const uint32_t tx = c.full ? c.q_len + dl : (uint32_t)c.rows * (c.q_len + dl);
-      uint8_t *dst = claim(tx);
-      if (!dst) break;
+      if (!claim(tx, &c)) break;
+      uint8_t *dst = S.ring + (size_t)rg.slot * DK_SLOT;
       uint64_t *fb = &S.full[rg.slot];
-      S.desc[rg.slot] = c;  // made visible to the consumers by the full barrier's completion
-      mbar_expect(fb, tx);
-      if (ci + 1 < ph[p + 1]) prefetch_l1(ch + ci + 1);
+      if (lane == 0 && ci + 1 < ph[p + 1]) prefetch_l1(ch + ci + 1);
       if (c.full) {
-        bulk_g2s(dst, c.q, c.q_len, fb);
-        if (c.d) bulk_g2s(dst + c.d_off, align16_down(c.d), c.d_len, fb);
+        if (lane == 0) {
+          bulk_g2s(dst, c.q, c.q_len, fb);
+          if (c.d) bulk_g2s(dst + c.d_off, align16_down(c.d), c.d_len, fb);
+        }
       } else {
-        for (int r = 0; r < c.rows; r++) {
+        for (int r = lane; r < c.rows; r += 32) {
           bulk_g2s(dst + (size_t)r * c.q_len, c.q + (size_t)r * c.q_stride, c.q_len, fb);
           if (c.d) bulk_g2s(dst + c.d_off + (size_t)r * c.d_len, align16_down(c.d + (size_t)r * c.d_stride), c.d_len, fb);
         }
@@ -390,25 +430,33 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
       const int L = p >> 2;
       for (int h = blockIdx.x; h < a.n_head && ok; h += gridDim.x) {
         const size_t base = ((size_t)L * a.n_kv + h / group) * a.n_ctx * a.dh;
-        for (int kv = 0; kv < 2 && ok; kv++) {
-          const float *src = (kv ? a.vcache : a.kcache) + base;
-          for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
-            const int n = min(ppc, pos - p0);
-            const uint32_t bytes = (uint32_t)n * a.dh * 4;
-            uint8_t *dst = claim(bytes);
-            if (!dst) break;
-            mbar_expect(&S.full[rg.slot], bytes);
-            bulk_g2s(dst, src + (size_t)p0 * a.dh, bytes, &S.full[rg.slot]);
-            rg.next();
-          }
+        // K (d-major): one run of positions per dimension, rounded up to a
+        // multiple of 4 positions (the slot's extra entries are not read).
+        for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
+          const int n4 = (min(ppc, pos - p0) + 3) & ~3;
+          if (!claim((uint32_t)(a.dh * n4 * 4), nullptr)) break;
+          uint8_t *dst = S.ring + (size_t)rg.slot * DK_SLOT;
+          for (int d = lane; d < a.dh; d += 32)
+            bulk_g2s(dst + (size_t)d * ppc * 4, a.kcache + base + (size_t)d * a.n_ctx + p0, (uint32_t)n4 * 4,
+                     &S.full[rg.slot]);
+          rg.next();
+        }
+        // V (position-major): one contiguous run
+        for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
+          const uint32_t bytes = (uint32_t)min(ppc, pos - p0) * a.dh * 4;
+          if (!claim(bytes, nullptr)) break;
+          if (lane == 0) bulk_g2s(S.ring + (size_t)rg.slot * DK_SLOT, a.vcache + base + (size_t)p0 * a.dh, bytes, &S.full[rg.slot]);
+          rg.next();
         }
       }
     }
   }
   note(a.n_layer);
   // Every copy this CTA issued lands before the CTA may exit.
-  for (int i = 0; i < DK_NS; i++)
-    if (used[i]) mbar_wait(&S.full[i], armed[i], nullptr);
+  if (lane == 0)
+    for (int i = 0; i < DK_NS; i++)
+      if (used[i]) mbar_wait(&S.full[i], armed[i], nullptr);
+  __syncwarp();
 }
 
 // ------------------------------------------------------------------ consumers
@@ -418,7 +466,9 @@ struct Cons {
   const Smem &S;
   const DChunk *ch;
   const int *ph;
-  int pos, tid, ctid, cwarp, lane, own0;
+  int pos, tid, ctid, cwarp, lane, own0, cw_base;
+  uint32_t ring_a, u_a, desc_a;
+  SAct act_a;
   Ring rg;
   int mv = 0, mv_total = 0;
   unsigned gen = 0;
@@ -434,8 +484,23 @@ struct Cons {
     lane = tid & 31;
     mv_total = ph[a.n_phase];  // ph is the shared-memory copy
     own0 = a.own[2 * blockIdx.x];
+    cw_base = a.cta_chunk0[blockIdx.x] & 31;  // S.cwb[0] holds the word with this CTA's first chunk
+    ring_a = shaddr(S.ring);
+    u_a = shaddr(S.u);
+    desc_a = shaddr(S.desc);
+    act_a = SAct{shaddr(S.aq), shaddr(S.ad), shaddr(S.as)};
   }
 
+  __device__ __forceinline__ void wait_full_at(int j) {  // the transfer j places ahead
+    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == 32);
+    const long long t0 = timed ? clock64() : 0;
+    const bool ok = mbar_wait(&S.full[rg.slot_at(j)], rg.par_at(j), S.flag);
+    if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
+    if (!ok && !*S.flag) {
+      atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+      S.flag[0] = 1;
+    }
+  }
   __device__ __forceinline__ void wait_full() {
     const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == 32);
     const long long t0 = timed ? clock64() : 0;
@@ -463,7 +528,11 @@ struct Cons {
     if ((TRACE && a.trace) && i < a.n_trace) a.trace[(size_t)blockIdx.x * a.n_trace + i] = v;
   }
   __device__ __forceinline__ void mark(int q, int j) {
-    if ((TRACE && a.trace) && ctid == 0) stamp(1 + 8 * q + j, gtime());
+    if ((TRACE && a.trace) && ctid == 0) stamp(1 + DK_TRW * q + j, gtime());
+  }
+  // fine-grained stamp i (< 8) inside the current phase
+  __device__ __forceinline__ void fine(int i) {
+    if ((TRACE && a.trace) && ctid == 0) stamp(1 + DK_TRW * (int)gen + 8 + i, gtime());
   }
 
   // All consumers; true when the kernel is being abandoned.
@@ -472,8 +541,8 @@ struct Cons {
     mark(q, 1);
     if ((TRACE && a.trace)) bar_sync(NB_CONS, CONS);  // every accumulator of this phase is final
     if ((TRACE && a.trace) && ctid == 0) {
-      stamp(1 + 8 * q + 3, S.prof[q % 5 == 1 ? 0 : 1]);
-      for (int i = 2; i < 6; i++) stamp(1 + 8 * q + 2 + i, S.prof[i]);
+      stamp(1 + DK_TRW * q + 3, S.prof[q % 5 == 1 ? 0 : 1]);
+      for (int i = 2; i < 6; i++) stamp(1 + DK_TRW * q + 2 + i, S.prof[i]);
       for (int i = 0; i < 6; i++) S.prof[i] = 0ull;
     }
     bar_sync(NB_CONS, CONS);
@@ -536,6 +605,7 @@ struct Cons {
       }
     }
     bar_sync(NB_CONS, CONS);
+    fine(0);
   }
 
   // The next RMSNorm's weights go to shared memory with asynchronous copies
@@ -572,7 +642,7 @@ struct Cons {
     asm volatile("cp.async.wait_all;" ::: "memory");
     float *xv = S.u;
     const int n8 = k / 8 * 8;
-    if (ctid < 8) S.red[ctid] = chain_sq(0.0f, xv + ctid, 8, n8 / 8);
+    if (ctid < 8) S.red[ctid] = chain_sq(0.0f, u_a + 4 * ctid, 32u, n8 / 8);
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {
       const float c0 = fadd(S.red[0], S.red[4]), c1 = fadd(S.red[1], S.red[5]), c2 = fadd(S.red[2], S.red[6]),
@@ -582,23 +652,23 @@ struct Cons {
       S.red[32] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)k), a.eps)));
     }
     bar_sync(NB_CONS, CONS);
+    fine(1);
     quant(k, true, S.red[32]);
   }
 
   __device__ void q8(int k) { quant(k, false, 1.0f); }
 
   template <int T>
-  __device__ void terms(const DChunk &c, const uint8_t *sl, float *Tb) {
+  __device__ void terms(const DChunk &c, uint32_t sl, uint32_t Tb) {
     constexpr int GPB = (T == T_Q4_K || T == T_Q6_K) ? 4 : 1, TPG = Geo<T>::TPG;
     constexpr int QB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 208 : (T == T_Q8_0 ? 32 : 16));
     const int R = c.rows, nbk = c.b1 - c.b0, G = nbk * GPB, items = R * G, rs = c.rs;
     const int qrs = nbk * QB;
-    const ActRef A{S.aq, S.ad, S.as};
     // Item (row, group): rows fastest for the k-quants (lanes of a warp share
     // one activation block), groups fastest for Q8_0/Q4_0 (contiguous bytes).
     // Each thread keeps two items in flight.
     const int M = GPB == 4 ? R : G, df = TERM_T % M, ds = TERM_T / M;
-    int t = tid - 64, f = t % M, sl_ = t / M;
+    int t = tid - 32 - 32 * DK_CHAINS, f = t % M, sl_ = t / M;
     auto adv = [&](int &a, int &b) {
       a += df;
       b += ds;
@@ -608,41 +678,42 @@ struct Cons {
       }
     };
     const uintptr_t d0 = (uintptr_t)c.d;
-    auto ptrs = [&](int rl, const uint8_t *&rq, const uint8_t *&rd) {
-      rq = sl + rl * qrs;
-      rd = nullptr;
+    auto ptrs = [&](int rl, uint32_t &rq, uint32_t &rd) {
+      rq = sl + (uint32_t)(rl * qrs);
+      rd = 0u;
       if (T != T_Q4_K)
         rd = sl + c.d_off +
-             (c.full ? (d0 & 15) + (size_t)rl * c.d_stride : (size_t)rl * c.d_len + ((d0 + (size_t)rl * c.d_stride) & 15));
+             (uint32_t)(c.full ? (d0 & 15) + (size_t)rl * c.d_stride
+                               : (size_t)rl * c.d_len + ((d0 + (size_t)rl * c.d_stride) & 15));
     };
-    constexpr bool kTwo = true;  // two items in flight per thread
+    constexpr bool kTwo = false;  // one item per step measured faster than two in the full kernel
     for (; t < items; t += (kTwo ? 2 : 1) * TERM_T) {
       int f2 = f, s2 = sl_;
       adv(f2, s2);
       const bool two = kTwo && t + TERM_T < items;
       const int rl1 = GPB == 4 ? f : sl_, gl1 = GPB == 4 ? sl_ : f;
       const int rl2 = two ? (GPB == 4 ? f2 : s2) : rl1, gl2 = two ? (GPB == 4 ? s2 : f2) : gl1;
-      const uint8_t *rq1, *rd1, *rq2, *rd2;
+      uint32_t rq1, rd1, rq2, rd2;
       ptrs(rl1, rq1, rd1);
       ptrs(rl2, rq2, rd2);
       float t1[TPG], t2[TPG];
       {
         GroupW<T> g1;
-        g1.load_s(rq1, rd1, c.b0 * GPB + gl1, c.b0);
+        g1.load_sa(rq1, rd1, c.b0 * GPB + gl1, c.b0);
         if (kTwo) {
           GroupW<T> g2;
-          g2.load_s(rq2, rd2, c.b0 * GPB + gl2, c.b0);
-          g1.terms(A, t1);
-          g2.terms(A, t2);
+          g2.load_sa(rq2, rd2, c.b0 * GPB + gl2, c.b0);
+          g1.terms_sa(act_a, t1);
+          g2.terms_sa(act_a, t2);
         } else {
-          g1.terms(A, t1);
+          g1.terms_sa(act_a, t1);
         }
       }
 #pragma unroll
-      for (int s = 0; s < TPG; s++) Tb[(gl1 * TPG + s) * rs + rl1] = t1[s];
+      for (int s = 0; s < TPG; s++) sst_f(Tb + 4u * (uint32_t)((gl1 * TPG + s) * rs + rl1), t1[s]);
       if (two) {
 #pragma unroll
-        for (int s = 0; s < TPG; s++) Tb[(gl2 * TPG + s) * rs + rl2] = t2[s];
+        for (int s = 0; s < TPG; s++) sst_f(Tb + 4u * (uint32_t)((gl2 * TPG + s) * rs + rl2), t2[s]);
       }
       if (kTwo) adv(f2, s2);
       f = f2;
@@ -671,7 +742,7 @@ struct Cons {
         }
         if (live) {
           if (c.role == DR_Q) a.q[r] = o;
-          else a.kcache[(((size_t)c.layer * a.n_kv + hd) * a.n_ctx + pos) * a.dh + d] = o;
+          else a.kcache[(((size_t)c.layer * a.n_kv + hd) * a.dh + d) * a.n_ctx + pos] = o;  // K is d-major
         }
         break;
       }
@@ -719,20 +790,26 @@ struct Cons {
   }
 
   // The matvec chunks of phase p.
+  // Chain warp that sums chunk ci of this CTA (plan bit list in shared memory).
+  __device__ __forceinline__ int owner(int ci) const {
+    const int bi = cw_base + ci;
+    return (int)((S.cwb[bi >> 5] >> (bi & 31)) & 1u);
+  }
+
   __device__ void run_mv(int p) {
-    const bool chain = cwarp == 0;
+    const bool chain = cwarp < DK_CHAINS;
     for (int ci = ph[p]; ci < ph[p + 1]; ci++) {
-      const int buf = mv & 1;
-      float *Tb = S.u + buf * DK_TS;
+      const int buf = mv % DK_NB;
+      const uint32_t Tb = u_a + 4u * (uint32_t)(buf * DK_TS);
       if (!chain) {
-        const bool tp = (TRACE && a.trace) && ctid == 32;
+        const bool tp = (TRACE && a.trace) && ctid == 32 * DK_CHAINS;
         long long c0 = tp ? clock64() : 0;
-        if (mv >= 2) bar_sync(NB_EMPTYT + buf, CONS);
+        if (mv >= DK_NB) bar_sync(NB_EMPTYT + buf * DK_CHAINS + owner(ci - DK_NB), NB_PAIR);
         if (tp) pacc(2, clock64() - c0);
         wait_full();
         if (tp) c0 = clock64();
-        const DChunk &c = S.desc[rg.slot];
-        const uint8_t *sl = S.ring + (size_t)rg.slot * DK_SLOT;
+        const DChunk c = load_desc(desc_a + rg.slot * (uint32_t)sizeof(DChunk));
+        const uint32_t sl = ring_a + rg.slot * (uint32_t)DK_SLOT;
         switch (c.type) {
           case T_Q4_K: terms<T_Q4_K>(c, sl, Tb); break;
           case T_Q6_K: terms<T_Q6_K>(c, sl, Tb); break;
@@ -740,36 +817,39 @@ struct Cons {
           default: terms<T_Q4_0>(c, sl, Tb); break;
         }
         if (tp) pacc(3, clock64() - c0);
-        bar_arrive(NB_FULLT + buf, CONS);
+        bar_arrive(NB_FULLT + buf * DK_CHAINS + owner(ci), NB_PAIR);
       } else {
+        // Ownership comes from the plan's bit list (the descriptor may only be
+        // read by the owner, before it hands the slot back).
         const bool tp = (TRACE && a.trace) && ctid == 0;
-        long long c0 = tp ? clock64() : 0;
-        bar_sync(NB_FULLT + buf, CONS);
-        if (tp) {
-          const long long c1 = clock64();
-          pacc(4, c1 - c0);
-          c0 = c1;
+        if (owner(ci) == cwarp) {
+          long long c0 = tp ? clock64() : 0;
+          bar_sync(NB_FULLT + buf * DK_CHAINS + cwarp, NB_PAIR);
+          if (ci == ph[p]) fine(3);  // first chunk's terms are in
+          if (tp) {
+            const long long c1 = clock64();
+            pacc(4, c1 - c0);
+            c0 = c1;
+          }
+          const DChunk d0 = load_desc(desc_a + rg.slot * (uint32_t)sizeof(DChunk));
+          ChainInfo c;
+          c.row0 = d0.row0;
+          c.rows = d0.rows;
+          c.role = d0.role;
+          c.layer = d0.layer;
+          c.flags = d0.flags;
+          c.nt = (d0.b1 - d0.b0) * dk_gpb(d0.type) * dk_tpg(d0.type);
+          c.rs = d0.rs;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
+          if (c.flags & DF_FIRST) acc = 0.0f;
+          if (lane < c.rows) acc = chain_add(acc, Tb + 4u * lane, 4u * (uint32_t)c.rs, c.nt);
+          __syncwarp();
+          if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cwarp, NB_PAIR);  // the term buffer is free again
+          if (c.flags & DF_LAST) epilogue(c);
+          if (tp) pacc(5, clock64() - c0);
+          if (ci == ph[p]) fine(4);  // first chunk chained
         }
-        // what the chain needs, copied before the slot is handed back
-        ChainInfo c;
-        {
-          const DChunk &d = S.desc[rg.slot];
-          c.row0 = d.row0;
-          c.rows = d.rows;
-          c.role = d.role;
-          c.layer = d.layer;
-          c.flags = d.flags;
-          c.nt = (d.b1 - d.b0) * dk_gpb(d.type) * dk_tpg(d.type);
-          c.rs = d.rs;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
-        if (c.flags & DF_FIRST) acc = 0.0f;
-        const int nt = c.nt, rs = c.rs;
-        if (lane < c.rows) acc = chain_add(acc, Tb + lane, rs, nt);
-        if (c.flags & DF_LAST) epilogue(c);
-        if (tp) pacc(5, clock64() - c0);
-        if (mv < mv_total - 2) bar_arrive(NB_EMPTYT + buf, CONS);
       }
       rg.next();
       mv++;
@@ -780,75 +860,65 @@ struct Cons {
   __device__ void attention(int L) {
     const int dh = a.dh, group = a.n_head / a.n_kv, ppc = DK_SLOT / (dh * 4);
     float *sc = S.u;
-    const int grp = ctid >> 3, l = ctid & 7, ngrp = CONS / 8;
     const int nvw = (dh + 31) / 32;  // value-chain warps
     for (int h = blockIdx.x; h < a.n_head; h += gridDim.x) {
       const int kh = h / group;
-      const size_t cur = (((size_t)L * a.n_kv + kh) * a.n_ctx + pos) * dh;
+      const size_t kbase = ((size_t)L * a.n_kv + kh) * a.n_ctx * dh;  // K d-major, V position-major
       float *kcur = S.qh + 256, *vcur = S.qh + 512;
       for (int d = ctid; d < dh; d += CONS) {  // one round trip for q, this step's k and v
-        const float qv = __ldcg(a.q + (size_t)h * dh + d), kv = __ldcg(a.kcache + cur + d), vv = __ldcg(a.vcache + cur + d);
+        const float qv = __ldcg(a.q + (size_t)h * dh + d), kv = __ldcg(a.kcache + kbase + (size_t)d * a.n_ctx + pos),
+                    vv = __ldcg(a.vcache + kbase + (size_t)pos * dh + d);
         S.qh[d] = qv;
         kcur[d] = kv;
         vcur[d] = vv;
       }
       bar_sync(NB_CONS, CONS);
+      if (h == (int)blockIdx.x) fine(0);
       float mx = -INFINITY;
       // s_p = f32_dot(q, k_p) * scale: eight unfused chains over d = 8t + l,
-      // combined ((c0+c1)+(c2+c3)) + ((c4+c5)+(c6+c7)), then the tail.
-      // Two positions per group at once (two independent chain sets).
-      auto score2 = [&](const float *k1, const float *k2, float &s1, float &s2) {  // rows in shared memory
+      // combined ((c0+c1)+(c2+c3)) + ((c4+c5)+(c6+c7)), then the tail.  One
+      // thread per position; k_p[d] sits at kp + d * ks (bytes).
+      const uint32_t qh_a = shaddr(S.qh);
+      auto score = [&](uint32_t kp, uint32_t ks) -> float {
         const int n8 = dh - (dh & 7);
-        float c1 = 0.0f, c2 = 0.0f;
-#pragma unroll 4
-        for (int t = l; t < n8; t += 8) {
-          const float qv = S.qh[t];
-          c1 = fadd(c1, fmul(qv, k1[t]));
-          c2 = fadd(c2, fmul(qv, k2[t]));
-        }
+        float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        for (int t = 0; t < n8; t += 8) {
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-          c1 = fadd(c1, __shfl_xor_sync(0xffffffffu, c1, o));
-          c2 = fadd(c2, __shfl_xor_sync(0xffffffffu, c2, o));
+          for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(sld_f(qh_a + 4u * (t + u)), sld_f(kp + (uint32_t)(t + u) * ks)));
         }
-        for (int t = n8; t < dh; t++) {
-          c1 = fadd(c1, fmul(S.qh[t], k1[t]));
-          c2 = fadd(c2, fmul(S.qh[t], k2[t]));
-        }
-        s1 = fmul(c1, a.scale);
-        s2 = fmul(c2, a.scale);
+        float r = fadd(fadd(fadd(c[0], c[1]), fadd(c[2], c[3])), fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
+        for (int t = n8; t < dh; t++) r = fadd(r, fmul(sld_f(qh_a + 4u * t), sld_f(kp + (uint32_t)t * ks)));
+        return fmul(r, a.scale);
       };
-      for (int p0 = 0; p0 < pos; p0 += ppc) {
-        const int n = min(ppc, pos - p0);
-        wait_full();
-        const float *kc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
-        for (int b = 0; b < n; b += 2 * ngrp) {
-          const int p1 = b + grp, p2 = b + ngrp + grp;
-          const bool v1 = p1 < n, v2 = p2 < n;
-          float s1, s2;
-          score2(kc + (size_t)(v1 ? p1 : 0) * dh, kc + (size_t)(v2 ? p2 : 0) * dh, s1, s2);
-          if (v1) {
-            if (l == 0) sc[p0 + p1] = s1;
-            mx = s1 > mx ? s1 : mx;
-          }
-          if (v2) {
-            if (l == 0) sc[p0 + p2] = s2;
-            mx = s2 > mx ? s2 : mx;
-          }
+      // K chunks are scored up to KG at a time (all consumer threads, one
+      // position each); chunk j of the group is the j-th next ring transfer.
+      constexpr int KG = 3;
+      const int nk = (pos + ppc - 1) / ppc;
+      for (int k0 = 0; k0 < nk; k0 += KG) {
+        const int g = min(KG, nk - k0), np = min(g * ppc, pos - k0 * ppc);
+        for (int j = 0; j < g; j++) wait_full_at(j);
+        for (int pi = ctid; pi < np; pi += CONS) {
+          const int j = pi / ppc, pj = pi - j * ppc;
+          const uint32_t kc = ring_a + rg.slot_at(j) * (uint32_t)DK_SLOT;  // [dh][ppc] floats
+          const float sv = score(kc + 4u * pj, 4u * ppc);
+          sc[k0 * ppc + pi] = sv;
+          mx = sv > mx ? sv : mx;
         }
         bar_sync(NB_CONS, CONS);
-        if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
-        rg.next();
+        if (ctid == 0)
+          for (int j = 0; j < g; j++) mbar_arrive(&S.empty[rg.slot_at(j)]);
+        for (int j = 0; j < g; j++) rg.next();
+        if (h == (int)blockIdx.x && k0 == 0) fine(1);
       }
-      if (cwarp == 0) {  // the position written by this step's qkv phase
-        float s, s_unused;
-        score2(kcur, kcur, s, s_unused);
-        if (grp == 0) {
-          if (l == 0) sc[pos] = s;
-          mx = s > mx ? s : mx;
-        }
+      if (h == (int)blockIdx.x) {
+        fine(2);
+        mark(5 * L + 1, 0);
       }
-      if (h == (int)blockIdx.x) mark(5 * L + 1, 0);
+      if (ctid == 0) {  // the position written by this step's qkv phase
+        const float sv = score(shaddr(kcur), 4u);
+        sc[pos] = sv;
+        mx = sv > mx ? sv : mx;
+      }
       const bool tp = TRACE && a.trace && h == (int)blockIdx.x;
       long long c0 = (tp && ctid == 0) ? clock64() : 0;
       mx = warp_max(mx);
@@ -860,9 +930,11 @@ struct Cons {
         S.red[32] = m;
       }
       bar_sync(NB_CONS, CONS);
+      if (h == (int)blockIdx.x) fine(3);
       const float M = S.red[32];
       for (int p = ctid; p <= pos; p += CONS) sc[p] = expf_lib(fsub(sc[p], M));
       bar_sync(NB_CONS, CONS);
+      if (h == (int)blockIdx.x) fine(4);
       if (tp && ctid == 0) {  // profile: max + exp
         const long long c1 = clock64();
         pacc(2, c1 - c0);
@@ -874,7 +946,7 @@ struct Cons {
       float vacc = 0.0f;
       if (ctid == nvw * 32) {
         const long long s0 = tp ? clock64() : 0;
-        const float sum = chain_add(0.0f, sc, 1, pos + 1);
+        const float sum = chain_add(0.0f, u_a, 4u, pos + 1);
         S.red[33] = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
         if (tp) pacc(4, clock64() - s0);  // profile: softmax sum chain
       }
@@ -883,7 +955,7 @@ struct Cons {
         if (vw) {
           wait_full();
           const float *vc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
-          if (ctid < dh) vacc = chain_wv(vacc, sc + p0, vc + ctid, dh, n);
+          if (ctid < dh) vacc = chain_wv(vacc, u_a + 4u * p0, shaddr(vc) + 4u * ctid, 4u * dh, n);
           bar_sync(NB_V, nvw * 32);
           if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
         }
@@ -894,6 +966,7 @@ struct Cons {
         const float v = vcur[ctid];
         if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
       }
+      if (h == (int)blockIdx.x) fine(5);
       if (tp && ctid == 0) {  // profile: value chains
         const long long c1 = clock64();
         pacc(3, c1 - c0);
@@ -907,13 +980,28 @@ struct Cons {
   }
 
   __device__ void finish() {
-    if (cwarp == 0 && lane == 0) {
-      a.cand_v[blockIdx.x] = best_v;
-      a.cand_i[blockIdx.x] = best_i;
+    if (cwarp < DK_CHAINS && lane == 0) {  // each chain warp's first maximum over its row groups
+      S.red[40 + cwarp] = best_v;
+      reinterpret_cast<volatile int *>(S.red)[48 + cwarp] = best_i;
+    }
+    bar_sync(NB_CONS, CONS);
+    if (ctid == 0) {  // larger value wins; equal values: the lower row index (first maximum)
+      float bv = S.red[40];
+      int bi = reinterpret_cast<volatile int *>(S.red)[48];
+      for (int w = 1; w < DK_CHAINS; w++) {
+        const float v = S.red[40 + w];
+        const int i = reinterpret_cast<volatile int *>(S.red)[48 + w];
+        if (v > bv || (v == bv && i < bi)) {
+          bv = v;
+          bi = i;
+        }
+      }
+      a.cand_v[blockIdx.x] = bv;
+      a.cand_i[blockIdx.x] = bi;
     }
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {
-      mark(5 * a.n_layer, 1);  // 1 + 40L + 1
+      mark(5 * a.n_layer, 1);
       __threadfence();
       const unsigned prev = atomicAdd(a.sync + 1, 1u);
       if (prev == gridDim.x - 1) {  // the last CTA: greedy pick over the per-CTA candidates
@@ -942,42 +1030,34 @@ struct Cons {
     }
   }
 
+  // One loop over the phases so that every large step has a single call site
+  // (the kernel's code stays small enough for the instruction caches).
+  //   q = 5L + 0 qkv | 1 attention | 2 o | 3 gate+up | 4 down;  q = 5n: head
   __device__ void run() {
     if ((TRACE && a.trace) && ctid == 0) stamp(0, gtime());
     prefetch_norm(a.layers[0].attn_norm, a.n_embd);
     embed();
-    const int qdim = a.n_head * a.dh;
-    for (int L = 0; L < a.n_layer; L++) {
-      const DecLayer &Ly = a.layers[L];
-      if (L > 0) stage(a.x, a.n_embd);
-      norm_q8(a.n_embd);
-      mark(5 * L, 0);
-      run_mv(4 * L);
-      if (grid_sync()) return;
-      attention(L);
-      if (grid_sync()) return;
-      prefetch_norm(Ly.ffn_norm, a.n_embd);  // the qkv norm is done with the buffer
-      stage(a.att, qdim);
-      q8(qdim);
-      mark(5 * L + 2, 0);
-      run_mv(4 * L + 1);
-      if (grid_sync()) return;
-      stage(a.x, a.n_embd);
-      norm_q8(a.n_embd);
-      mark(5 * L + 3, 0);
-      run_mv(4 * L + 2);
-      if (grid_sync()) return;
-      prefetch_norm(L + 1 < a.n_layer ? a.layers[L + 1].attn_norm : a.out_norm, a.n_embd);
-      stage(a.h, a.n_ff);
-      q8(a.n_ff);
-      mark(5 * L + 4, 0);
-      run_mv(4 * L + 3);
+    const int qdim = a.n_head * a.dh, nq = 5 * a.n_layer;
+    for (int q = 0; q <= nq; q++) {
+      const int L = q / 5, kind = q == nq ? 5 : q % 5;
+      if (kind == 1) {
+        attention(L);
+      } else {
+        // prologue: stage the input vector, then RMSNorm + Q8 or Q8 alone
+        if (kind == 2) prefetch_norm(a.layers[L].ffn_norm, a.n_embd);  // the qkv norm is done with the buffer
+        if (kind == 4) prefetch_norm(L + 1 < a.n_layer ? a.layers[L + 1].attn_norm : a.out_norm, a.n_embd);
+        const bool norm = kind == 0 || kind == 3 || kind == 5;
+        const float *src = kind == 2 ? a.att : kind == 4 ? a.h : a.x;
+        const int k = kind == 2 ? qdim : kind == 4 ? a.n_ff : a.n_embd;
+        if (q > 0) stage(src, k);
+        if (norm) norm_q8(k);
+        else q8(k);
+        mark(q, 0);
+        run_mv(kind == 5 ? 4 * a.n_layer : 4 * L + (kind == 0 ? 0 : kind - 1));
+      }
+      if (kind == 5) break;
       if (grid_sync()) return;
     }
-    stage(a.x, a.n_embd);
-    norm_q8(a.n_embd);
-    mark(5 * a.n_layer, 0);
-    run_mv(4 * a.n_layer);
     finish();
   }
 };
@@ -1001,6 +1081,11 @@ __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant_
   const DChunk *ch = a.chunks + a.cta_chunk0[blockIdx.x];
   const int *ph_g = a.phase0 + (size_t)blockIdx.x * (a.n_phase + 1);
   for (int i = threadIdx.x; i <= a.n_phase; i += DK_THREADS) S.ph[i] = ph_g[i];
+  {
+    const int c0 = a.cta_chunk0[blockIdx.x], c1 = a.cta_chunk0[blockIdx.x + 1];
+    const int w0 = c0 >> 5, nw = ((c1 + 31) >> 5) - w0;
+    for (int i = threadIdx.x; i < nw && i < DK_CWW; i += DK_THREADS) S.cwb[i] = a.cwbits[w0 + i];
+  }
   for (int i = threadIdx.x; i < a.half; i += DK_THREADS) {
     S.rope[i] = a.rope_cos[(size_t)pos * a.half + i];
     S.rope[128 + i] = a.rope_sin[(size_t)pos * a.half + i];
@@ -1008,7 +1093,7 @@ __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant_
   __syncthreads();
   const int *ph = S.ph;
   if (threadIdx.x < 32) {
-    if (threadIdx.x == 0) producer<TRACE>(a, S, pos, ch, ph);
+    producer<TRACE>(a, S, pos, ch, ph);
     return;
   }
   Cons<TRACE> c(a, S, ch, ph, pos);
@@ -1084,6 +1169,10 @@ void split2(int n, int parts, int i, int &a, int &b) {
 struct Builder {
   std::vector<DChunk> &out;
   std::string &why;
+  long load[DK_CHAINS] = {};  // chain terms given to each chain warp in this phase
+  void new_phase() {
+    for (long &l : load) l = 0;
+  }
 
   DChunk base(const DevTensor &W, uint8_t role, int layer, int r, int rows, int b0, int b1, bool full) {
     const TypeGeo g = type_geo(W.type);
@@ -1163,6 +1252,11 @@ struct Builder {
       split2(own, ng, gi, a, b);
       const int R = b - a;
       if (R <= 0) continue;
+      // the chain warp with the least work so far sums this group (and its pair)
+      int cw = 0;
+      for (int w = 1; w < DK_CHAINS; w++)
+        if (load[w] < load[cw]) cw = w;
+      load[cw] += (long)md[0].terms_row + (W2 ? (long)md[1].terms_row : 0L);
       for (int w = 0; w < (W2 ? 2 : 1); w++) {
         const DevTensor &M = w ? *W2 : W;
         const Mode &m = md[w];
@@ -1187,6 +1281,7 @@ struct Builder {
           const int b0 = full ? 0 : (int)((long)m.nblk * j / nkc), b1 = full ? m.nblk : (int)((long)m.nblk * (j + 1) / nkc);
           DChunk c = base(M, w ? role2 : role, layer, r0 + a, R, b0, b1, full);
           c.flags = (uint8_t)((j == 0 ? DF_FIRST : 0) | (j == nkc - 1 ? DF_LAST : 0));
+          c.cw = (uint8_t)cw;
           out.push_back(c);
         }
       }
@@ -1206,7 +1301,8 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
     why = "model does not fit the persistent kernel's shared memory";
     return false;
   }
-  if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv || 2 * ((n_embd / 2 + grid - 1) / grid) > DK_XO) {
+  if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv || 2 * ((n_embd / 2 + grid - 1) / grid) > DK_XO ||
+      n_ctx % 4) {  // K chunks copy whole groups of 4 positions
     why = "unsupported dimensions";
     return false;
   }
@@ -1228,21 +1324,26 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
       const DecLayer &Y = layers[L];
       int a, b;
       ph[4 * L] = (int)v.size();
+      B.new_phase();  // v first: its Q6_K rows have the longest chains
+      split2(Y.v.rows, grid, c, a, b);
+      if (!B.rows(Y.v, nullptr, a, b, DR_V, 0, L)) return false;
       split2(Y.q.rows, grid, c, a, b);
       if (!B.rows(Y.q, nullptr, a, b, DR_Q, 0, L)) return false;
       split2(Y.k.rows, grid, c, a, b);
       if (!B.rows(Y.k, nullptr, a, b, DR_K, 0, L)) return false;
-      split2(Y.v.rows, grid, c, a, b);
-      if (!B.rows(Y.v, nullptr, a, b, DR_V, 0, L)) return false;
       ph[4 * L + 1] = (int)v.size();
+      B.new_phase();
       if (!B.rows(Y.o, nullptr, oa, ob, DR_O, 0, L)) return false;
       ph[4 * L + 2] = (int)v.size();
+      B.new_phase();
       split2(Y.gate.rows, grid, c, a, b);
       if (!B.rows(Y.gate, &Y.up, a, b, DR_GATE, DR_UP, L)) return false;
       ph[4 * L + 3] = (int)v.size();
+      B.new_phase();
       if (!B.rows(Y.down, nullptr, oa, ob, DR_DOWN, 0, L)) return false;
     }
     ph[4 * nl] = (int)v.size();
+    B.new_phase();
     int a, b;
     split2(out.rows, grid, c, a, b);
     if (!B.rows(out, nullptr, a, b, DR_HEAD, 0, nl)) return false;
@@ -1250,6 +1351,14 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
     plan.chunks.insert(plan.chunks.end(), v.begin(), v.end());
   }
   plan.cta_chunk0[grid] = (int)plan.chunks.size();
+  plan.cwbits.assign((plan.chunks.size() + 31) / 32 + 1, 0u);
+  for (size_t i = 0; i < plan.chunks.size(); i++)
+    if (plan.chunks[i].cw) plan.cwbits[i / 32] |= 1u << (i % 32);
+  for (int c = 0; c < grid; c++)
+    if (plan.cta_chunk0[c + 1] - plan.cta_chunk0[c] > 32 * DK_CWW - 31) {
+      why = "too many chunks per CTA for the chain-warp bit list";
+      return false;
+    }
   return true;
 }
 

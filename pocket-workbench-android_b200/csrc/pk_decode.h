@@ -18,11 +18,14 @@
 
 namespace pk {
 
-constexpr int DK_THREADS = 384;     // warp 0 producer, warp 1 row chains, warps 2..11 terms
+constexpr int DK_THREADS = 384;     // warp 0 producer, warps 1-2 row chains, warps 3..11 terms
+constexpr int DK_CHAINS = 2;        // chain warps
+constexpr int DK_NB = 3;            // term buffers
 constexpr int DK_NS = 5;            // ring slots
 constexpr int DK_SLOT = 32768;      // bytes per slot
-constexpr int DK_TS = 2560;         // floats per term buffer (two buffers)
+constexpr int DK_TS = 2560;         // floats per term buffer
 constexpr int DK_MAX_RG = 32;       // rows per row group (one chain lane each)
+constexpr int DK_TRW = 16;          // profile-trace words per phase
 
 enum : uint8_t { DR_Q = 0, DR_K, DR_V, DR_O, DR_GATE, DR_UP, DR_DOWN, DR_HEAD };
 enum : uint8_t { DF_FIRST = 1, DF_LAST = 2 };
@@ -43,6 +46,7 @@ struct DChunk {
   uint16_t rows, rs;  // rows; term-buffer row stride (odd)
   uint8_t type, role, full, flags;
   int row0, b0, b1, layer;
+  uint8_t cw, pad_[3];  // chain warp that sums these rows
 };
 static_assert(sizeof(DChunk) == 64, "DChunk is one 64-byte record");
 
@@ -70,6 +74,7 @@ struct DecodeArgs {
   const int *phase0;                  // [grid][n_phase + 1], relative to the CTA's first chunk
   int n_phase;                        // 4 * n_layer + 1
   const int *own;                     // [grid][2] rows of x written by this CTA
+  const uint32_t *cwbits;             // bit per chunk: which chain warp sums it
   unsigned *sync;                     // [0] grid barrier arrivals, [1] finished CTAs
   int *err;                           // 0 or a PK_ERR_* code
   float *cand_v;
@@ -83,6 +88,7 @@ struct DecodeArgs {
 struct DecodePlan {
   std::vector<DChunk> chunks;
   std::vector<int> cta_chunk0, phase0, own;
+  std::vector<uint32_t> cwbits;  // bit i: chain warp of chunk i
   int grid = 0, n_phase = 0;
   size_t smem = 0;
 };

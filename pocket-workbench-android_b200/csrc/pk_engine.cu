@@ -259,7 +259,9 @@ int Engine::load(const char *path) {
   embd_type_ = embd.type;
   embd_row_bytes_ = embd.row_bytes;
 
-  // ---- KV cache (model.rs:352-387): [layer][kv_head][n_ctx][dh] f32
+  // ---- KV cache (model.rs:352-387), f32: V as the reference lays it out,
+  // [layer][kv_head][n_ctx][dh]; K d-major, [layer][kv_head][dh][n_ctx], so a
+  // run of positions of one dimension is contiguous for the score pass.
   kv_bytes_ = 2 * (size_t)c.n_layer * c.n_head_kv * n_ctx_ * c.head_dim * 4;
   PK_CK(cudaMalloc((void **)&d_kcache_, kv_bytes_ / 2));
   PK_CK(cudaMalloc((void **)&d_vcache_, kv_bytes_ / 2));
@@ -369,11 +371,12 @@ int Engine::setup_decode() {
     decode_why_ = "the persistent kernel's grid does not fit the device at once";
     return PK_OK;
   }
-  const int n_trace = 1 + 40 * c.n_layer + 2 + c.n_layer + 1;
+  const int n_trace = 1 + DK_TRW * (5 * c.n_layer + 1) + c.n_layer + 1;
   const size_t n_ch = plan_.chunks.size() * sizeof(DChunk), n_c0 = plan_.cta_chunk0.size() * 4,
                n_ph = plan_.phase0.size() * 4, n_own = plan_.own.size() * 4, n_ly = dl.size() * sizeof(DecLayer),
+               n_cw = plan_.cwbits.size() * 4,
                n_tr = (size_t)grid * n_trace * 8;
-  const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr};
+  const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr, n_cw};
   size_t total = 0;
   for (size_t z : sizes) total += a256(z);
   PK_CK(cudaMalloc((void **)&d_decode_, total));
@@ -393,11 +396,13 @@ int Engine::setup_decode() {
   float *cv = (float *)take();
   int *ci = (int *)take();
   d_trace_ = (unsigned long long *)take();
+  uint32_t *cwb = (uint32_t *)take();
   PK_CK(cudaMemcpyAsync(chunks, plan_.chunks.data(), n_ch, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(c0, plan_.cta_chunk0.data(), n_c0, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(ph, plan_.phase0.data(), n_ph, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(own, plan_.own.data(), n_own, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(layers, dl.data(), n_ly, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(cwb, plan_.cwbits.data(), n_cw, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaStreamSynchronize(st_));
   DecodeArgs &a = dargs_;
   a = DecodeArgs{};
@@ -415,7 +420,7 @@ int Engine::setup_decode() {
   a.kcache = d_kcache_; a.vcache = d_vcache_;
   a.x = x_; a.q = q_; a.att = attn_; a.h = h_; a.logits = logits_;
   a.ids = d_ids_; a.tok = d_tok_; a.hist = d_hist_; a.pos = d_pos_; a.step = d_step_;
-  a.chunks = chunks; a.cta_chunk0 = c0; a.phase0 = ph; a.n_phase = plan_.n_phase; a.own = own;
+  a.chunks = chunks; a.cta_chunk0 = c0; a.phase0 = ph; a.n_phase = plan_.n_phase; a.own = own; a.cwbits = cwb;
   a.sync = d_sync_; a.err = d_err_; a.cand_v = cv; a.cand_i = ci;
   a.mode = 0;
   a.trace = nullptr;
@@ -874,7 +879,7 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
     int khz = 0;
     PK_CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device_));
     const double cyc_ms = 1.0 / std::max(1.0, (double)khz);  // SM cycles -> ms at the rated clock
-    auto exit_of = [&](int g, int q) { return q < 0 ? at(g, 0) : at(g, 1 + 8 * q + 2); };
+    auto exit_of = [&](int g, int q) { return q < 0 ? at(g, 0) : at(g, 1 + DK_TRW * q + 2); };
     auto max_exit = [&](int q) {
       double v = 0;
       for (int g = 0; g < grid; g++) v = std::max(v, exit_of(g, q));
@@ -890,19 +895,36 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
       // attention sub-phases: only the CTAs that own a head stamp them
       const int ng = j == 1 ? std::min(grid, c.n_head) : grid;
       for (int g = 0; g < ng; g++) {
-        const int b0 = 1 + 8 * q;
+        const int b0 = 1 + DK_TRW * q;
         sub[j][0] += (at(g, b0) - exit_of(g, q - 1)) * 1e-6 / ng;
         sub[j][1] += (at(g, b0 + 1) - at(g, b0)) * 1e-6 / ng;
         sub[j][2] += (at(g, b0 + 2) - at(g, b0 + 1)) * 1e-6 / ng;
         for (int i = 3; i < 8; i++) sub[j][i] += at(g, b0 + i) * cyc_ms / ng;
       }
     }
+    // fine stamps: average offset from the phase start, summed over layers
+    double fine_ms[5][8] = {{0}};
+    for (int q = 0; q < 5 * nl; q++) {
+      const int j = q % 5;
+      for (int i = 0; i < 8; i++) {
+        double sum = 0;
+        int cnt = 0;
+        for (int g = 0; g < grid; g++) {
+          const double v = at(g, 1 + DK_TRW * q + 8 + i);
+          if (v > 0) {
+            sum += (v - exit_of(g, q - 1)) * 1e-6;
+            cnt++;
+          }
+        }
+        if (cnt) fine_ms[j][i] += sum / cnt;
+      }
+    }
     double head_end = 0, prod = 0;
     for (int g = 0; g < grid; g++) {
-      head_end = std::max(head_end, at(g, 1 + 40 * nl + 1));
-      sub[5][0] += (at(g, 1 + 40 * nl) - exit_of(g, 5 * nl - 1)) * 1e-6 / grid;
-      sub[5][1] += (at(g, 1 + 40 * nl + 1) - at(g, 1 + 40 * nl)) * 1e-6 / grid;
-      for (int L = 0; L <= nl; L++) prod += at(g, 1 + 40 * nl + 2 + L) * cyc_ms / grid;
+      head_end = std::max(head_end, at(g, 1 + DK_TRW * 5 * nl + 1));
+      sub[5][0] += (at(g, 1 + DK_TRW * 5 * nl) - exit_of(g, 5 * nl - 1)) * 1e-6 / grid;
+      sub[5][1] += (at(g, 1 + DK_TRW * 5 * nl + 1) - at(g, 1 + DK_TRW * 5 * nl)) * 1e-6 / grid;
+      for (int L = 0; L <= nl; L++) prod += at(g, 1 + DK_TRW * (5 * nl + 1) + L) * cyc_ms / grid;
     }
     wall[5] = (head_end - max_exit(5 * nl - 1)) * 1e-6;
     for (int L = 0; L < nl; L++) {
@@ -928,6 +950,9 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
       for (int i = 0; i < (j == 5 ? 2 : 8); i++)
         add(std::string(names[j]) + "/" + (i < 7 ? subs[i] : "chain_work"), j == 5 ? 1 : nl, sub[j][i], 0.0);
     add("dk_producer/slot_wait", 1, prod, 0.0);
+    for (int j = 0; j < 5; j++)
+      for (int i = 0; i < 8; i++)
+        if (fine_ms[j][i] > 0) add(std::string(names[j]) + "/at" + std::to_string(i), nl, fine_ms[j][i], 0.0);
   }
   uint32_t tok = 0;
   PK_CK(cudaMemcpyAsync(&tok, d_tok_, 4, cudaMemcpyDeviceToHost, st_));

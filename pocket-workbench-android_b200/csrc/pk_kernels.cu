@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(B1_THREADS) k_qkv_b1(QkvArgs a) {
         else o = fadd(fmul(m.xv[tid - 1], s), fmul(val, c));
       }
       if (seg == 0) a.qout[r] = o;
-      else if (seg == 1) a.kcache[((size_t)hd * a.n_ctx + pos) * a.dh + d] = o;
+      else if (seg == 1) a.kcache[((size_t)hd * a.dh + d) * a.n_ctx + pos] = o;  // K is d-major
       else a.vcache[((size_t)hd * a.n_ctx + pos) * a.dh + d] = o;
     }
     __syncthreads();
@@ -660,9 +660,8 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
       if ((d & 1) == 0) o = fsub(fmul(kr[i], c), fmul(kr[i + 1], s));
       else o = fadd(fmul(kr[i - 1], s), fmul(kr[i], c));
     }
-    const size_t dst = ((size_t)h * n_ctx + p) * dh + d;
-    kc[dst] = o;
-    vc[dst] = vr[i];
+    kc[((size_t)h * dh + d) * n_ctx + p] = o;  // K is d-major: [kv head][d][position]
+    vc[((size_t)h * n_ctx + p) * dh + d] = vr[i];
   }
 }
 
@@ -726,32 +725,23 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   const float *vb = a.vcache + (size_t)kh * a.n_ctx * dh;
   float *sc = a.scores + hb * a.n_ctx;
   float mx = -INFINITY;
+  const size_t nc = (size_t)a.n_ctx;
   for (int p = tid; p <= pos; p += blockDim.x) {
-    const float *kr = kb + (size_t)p * dh;
+    const float *kcol = kb + p;  // K is d-major: element d of position p at kcol[d * n_ctx]
     float s;
     if (dot8) {
       float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       int d = 0;
       for (; d + 8 <= dh; d += 8) {
-        const float4 k0 = *reinterpret_cast<const float4 *>(kr + d);
-        const float4 k1 = *reinterpret_cast<const float4 *>(kr + d + 4);
-        c[0] = fadd(c[0], fmul(qs[d + 0], k0.x)); c[1] = fadd(c[1], fmul(qs[d + 1], k0.y));
-        c[2] = fadd(c[2], fmul(qs[d + 2], k0.z)); c[3] = fadd(c[3], fmul(qs[d + 3], k0.w));
-        c[4] = fadd(c[4], fmul(qs[d + 4], k1.x)); c[5] = fadd(c[5], fmul(qs[d + 5], k1.y));
-        c[6] = fadd(c[6], fmul(qs[d + 6], k1.z)); c[7] = fadd(c[7], fmul(qs[d + 7], k1.w));
+#pragma unroll
+        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], kcol[(size_t)(d + u) * nc]));
       }
       s = fadd(fadd(c[0], c[1]), fadd(c[2], c[3]));
       s = fadd(s, fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
-      for (; d < dh; d++) s = fadd(s, fmul(qs[d], kr[d]));
+      for (; d < dh; d++) s = fadd(s, fmul(qs[d], kcol[(size_t)d * nc]));
     } else {
       s = 0.0f;
-      for (int d = 0; d < dh; d += 4) {
-        const float4 kv = *reinterpret_cast<const float4 *>(kr + d);
-        s = fadd(s, fmul(qs[d], kv.x));
-        s = fadd(s, fmul(qs[d + 1], kv.y));
-        s = fadd(s, fmul(qs[d + 2], kv.z));
-        s = fadd(s, fmul(qs[d + 3], kv.w));
-      }
+      for (int d = 0; d < dh; d++) s = fadd(s, fmul(qs[d], kcol[(size_t)d * nc]));
     }
     s = fmul(s, a.scale);
     sc[p] = s;

@@ -70,7 +70,7 @@ struct QkvArgs {
   const float *rope_sin = nullptr;
   int half = 0, dh = 0, n_ctx = 0;
   float *qout = nullptr;   // [n_head * dh]
-  float *kcache = nullptr; // this layer: [n_kv][n_ctx][dh]
+  float *kcache = nullptr; // this layer: K d-major [n_kv][dh][n_ctx]
   float *vcache = nullptr;
 };
 cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st);
@@ -90,7 +90,7 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cuda
 // Causal GQA attention (model.rs:993-1087) for b tokens at positions pos[b].
 struct AttnArgs {
   const float *q;      // [b][n_head * dh]
-  const float *kcache; // layer base [n_kv][n_ctx][dh]
+  const float *kcache; // layer base, K d-major [n_kv][dh][n_ctx]
   const float *vcache;
   const int *pos;      // [b] device
   float *out;          // [b][n_head * dh]

@@ -111,14 +111,18 @@ struct ActRef {  // one lane's Q8 activation: q [k], d/s [k/32]
 __device__ __forceinline__ int lo4(uint32_t w) { return (int)(w & 0x0F0F0F0Fu); }
 __device__ __forceinline__ int hi4(uint32_t w) { return (int)((w >> 4) & 0x0F0F0F0Fu); }
 
-__device__ __forceinline__ uint4 lds16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
-__device__ __forceinline__ uint16_t lds2(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
-
 // A group of one row's blocks.  load() reads the device layout in global
-// memory; load_s() reads a staged copy of one row's blocks [b0, ...) in
-// shared memory: rq = that row's first staged block, rd = its first staged
-// f16 scale (the types that keep d apart).  gi is always the global group.
+// memory; load_s()/load_sa() read a staged copy of one row's blocks [b0, ...)
+// in shared memory (by pointer / by shared address): rq = that row's first
+// staged block, rd = its first staged f16 scale (the types that keep d
+// apart).  gi is always the global group.  terms() takes the activation by
+// pointer, terms_sa() by shared address; both end in the same finish().
 template <int T> struct GroupW;
+
+// A Q8 activation in shared memory by shared address: q [k] i8, d/s [k/32].
+struct SAct {
+  uint32_t q, d, s;
+};
 
 template <> struct GroupW<T_Q4_K> {
   uint4 hdr, w0, w1;
@@ -134,18 +138,31 @@ template <> struct GroupW<T_Q4_K> {
     w1 = ldw16(base + 32 + g * 32);
   }
   __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *, int gi, int b0) {
+    load_sa(shaddr(rq), 0u, gi, b0);
+  }
+  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t, int gi, int b0) {
     blk = gi >> 2;
     const int g = gi & 3;
     sb0 = 2 * g;
-    const uint8_t *base = rq + (blk - b0) * 144;
-    hdr = lds16(base);
-    w0 = lds16(base + 16 + g * 32);
-    w1 = lds16(base + 32 + g * 32);
+    const uint32_t base = rq + (uint32_t)(blk - b0) * 144u;
+    hdr = sld_v4(base);
+    w0 = sld_v4(base + 16 + g * 32);
+    w1 = sld_v4(base + 32 + g * 32);
   }
-  // quant_int.rs:354-365: acc += d*da*s*dot - da*dmin*m*sa per sub-block.
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 256 + sb0 * 32);
-    const int4 a00 = ap[0], a01 = ap[1], a10 = ap[2], a11 = ap[3];
+    const int ai = blk * 8 + sb0;
+    finish(ap[0], ap[1], ap[2], ap[3], A.d[ai], A.d[ai + 1], A.s[ai], A.s[ai + 1], t);
+  }
+  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
+    const uint32_t ap = A.q + (uint32_t)(blk * 256 + sb0 * 32);
+    const uint32_t ai = (uint32_t)(blk * 8 + sb0) * 4u;
+    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_v4i(ap + 32), sld_v4i(ap + 48), sld_f(A.d + ai), sld_f(A.d + ai + 4),
+           sld_i(A.s + ai), sld_i(A.s + ai + 4), t);
+  }
+  // quant_int.rs:354-365: acc += d*da*s*dot - da*dmin*m*sa per sub-block.
+  __device__ __forceinline__ void finish(const int4 a00, const int4 a01, const int4 a10, const int4 a11, float da0,
+                                         float da1, int sa0, int sa1, float *t) const {
     // integer sums are exact in any order: two partial chains each
     int d0a = 0, d0b = 0, d1a = 0, d1b = 0;
     d0a = __dp4a(lo4(w0.x), a00.x, d0a); d0b = __dp4a(lo4(w0.y), a00.y, d0b);
@@ -173,9 +190,6 @@ template <> struct GroupW<T_Q4_K> {
       sc1 = (int)(((hdr.w >> (sh + 8)) & 0xFu) | ((hdr.y >> (sh + 10)) & 0x30u));
       m1 = (int)(((hdr.w >> (sh + 12)) & 0xFu) | ((hdr.z >> (sh + 10)) & 0x30u));
     }
-    const int ai = blk * 8 + sb0;
-    const float da0 = A.d[ai], da1 = A.d[ai + 1];
-    const int sa0 = A.s[ai], sa1 = A.s[ai + 1];
     t[0] = fsub(fmul(fmul(fmul(d, da0), (float)sc0), (float)d0), fmul(fmul(fmul(da0, dmin), (float)m0), (float)sa0));
     t[1] = fsub(fmul(fmul(fmul(d, da1), (float)sc1), (float)d1), fmul(fmul(fmul(da1, dmin), (float)m1), (float)sa1));
   }
@@ -198,13 +212,16 @@ template <> struct GroupW<T_Q6_K> {
     unpack(ldw16(base + h * 64 + g * 16), ldw16(base + h * 64 + 32 + g * 16), ldw16(base + 128 + h * 32 + g * 16));
   }
   __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
+    load_sa(shaddr(rq), shaddr(rd), gi, b0);
+  }
+  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
     blk = gi >> 2;
     h = (gi >> 1) & 1;
     g = gi & 1;
-    const uint8_t *base = rq + (blk - b0) * 208;
-    scv = lds16(base + 192);
-    d = f16f(lds2(rd + (blk - b0) * 2));
-    unpack(lds16(base + h * 64 + g * 16), lds16(base + h * 64 + 32 + g * 16), lds16(base + 128 + h * 32 + g * 16));
+    const uint32_t base = rq + (uint32_t)(blk - b0) * 208u;
+    scv = sld_v4(base + 192);
+    d = f16f(sld_u16(rd + (uint32_t)(blk - b0) * 2u));
+    unpack(sld_v4(base + h * 64 + g * 16), sld_v4(base + h * 64 + 32 + g * 16), sld_v4(base + 128 + h * 32 + g * 16));
   }
   __device__ __forceinline__ void unpack(const uint4 &qa, const uint4 &qb, const uint4 &qh) {
 #pragma unroll
@@ -216,22 +233,40 @@ template <> struct GroupW<T_Q6_K> {
       q[3][w] = (int)__vsub4(((b >> 4) & 0x0F0F0F0Fu) | ((hh >> 2) & 0x30303030u), 0x20202020u);
     }
   }
-  // quant_int.rs:397-413: acc += d*scale*da*dot per 16-element piece, order (half, g, s).
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
+    int4 a[4];
+    float da[4];
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      a[s] = *reinterpret_cast<const int4 *>(A.q + blk * 256 + (4 * h + s) * 32 + g * 16);
+      da[s] = A.d[blk * 8 + 4 * h + s];
+    }
+    finish(a, da, t);
+  }
+  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
+    int4 a[4];
+    float da[4];
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      a[s] = sld_v4i(A.q + (uint32_t)(blk * 256 + (4 * h + s) * 32 + g * 16));
+      da[s] = sld_f(A.d + (uint32_t)(blk * 8 + 4 * h + s) * 4u);
+    }
+    finish(a, da, t);
+  }
+  // quant_int.rs:397-413: acc += d*scale*da*dot per 16-element piece, order (half, g, s).
+  __device__ __forceinline__ void finish(const int4 *a, const float *da, float *t) const {
     // scales of this half: bytes h*8 .. h*8+7 of the 16 scale bytes
     const unsigned long long sw = h ? ((unsigned long long)scv.w << 32 | scv.z) : ((unsigned long long)scv.y << 32 | scv.x);
 #pragma unroll
     for (int s = 0; s < 4; s++) {
-      const int4 a = *reinterpret_cast<const int4 *>(A.q + blk * 256 + (4 * h + s) * 32 + g * 16);
       int pa = 0, pb = 0;
-      pa = __dp4a(q[s][0], a.x, pa);
-      pb = __dp4a(q[s][1], a.y, pb);
-      pa = __dp4a(q[s][2], a.z, pa);
-      pb = __dp4a(q[s][3], a.w, pb);
+      pa = __dp4a(q[s][0], a[s].x, pa);
+      pb = __dp4a(q[s][1], a[s].y, pb);
+      pa = __dp4a(q[s][2], a[s].z, pa);
+      pb = __dp4a(q[s][3], a[s].w, pb);
       const int dot = pa + pb;
       const float scale = (float)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s)));
-      const float da = A.d[blk * 8 + 4 * h + s];
-      t[s] = fmul(fmul(fmul(d, scale), da), (float)dot);
+      t[s] = fmul(fmul(fmul(d, scale), da[s]), (float)dot);
     }
   }
 };
@@ -248,22 +283,31 @@ template <> struct GroupW<T_Q8_0> {
     d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
   }
   __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
-    blk = gi;
-    w0 = lds16(rq + (gi - b0) * 32);
-    w1 = lds16(rq + (gi - b0) * 32 + 16);
-    d = f16f(lds2(rd + (gi - b0) * 2));
+    load_sa(shaddr(rq), shaddr(rd), gi, b0);
   }
-  // quant_int.rs:291-296: acc += d*da*dot.
+  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
+    blk = gi;
+    w0 = sld_v4(rq + (uint32_t)(gi - b0) * 32u);
+    w1 = sld_v4(rq + (uint32_t)(gi - b0) * 32u + 16u);
+    d = f16f(sld_u16(rd + (uint32_t)(gi - b0) * 2u));
+  }
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
-    const int4 a0 = ap[0], a1 = ap[1];
+    finish(ap[0], ap[1], A.d[blk], t);
+  }
+  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
+    const uint32_t ap = A.q + (uint32_t)blk * 32u;
+    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_f(A.d + (uint32_t)blk * 4u), t);
+  }
+  // quant_int.rs:291-296: acc += d*da*dot.
+  __device__ __forceinline__ void finish(const int4 a0, const int4 a1, float da_, float *t) const {
     int da = 0, db = 0;
     da = __dp4a((int)w0.x, a0.x, da); db = __dp4a((int)w0.y, a0.y, db);
     da = __dp4a((int)w0.z, a0.z, da); db = __dp4a((int)w0.w, a0.w, db);
     da = __dp4a((int)w1.x, a1.x, da); db = __dp4a((int)w1.y, a1.y, db);
     da = __dp4a((int)w1.z, a1.z, da); db = __dp4a((int)w1.w, a1.w, db);
     const int dot = da + db;
-    t[0] = fmul(fmul(d, A.d[blk]), (float)dot);
+    t[0] = fmul(fmul(d, da_), (float)dot);
   }
 };
 
@@ -277,21 +321,30 @@ template <> struct GroupW<T_Q4_0> {
     d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
   }
   __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
-    blk = gi;
-    w = lds16(rq + (gi - b0) * 16);
-    d = f16f(lds2(rd + (gi - b0) * 2));
+    load_sa(shaddr(rq), shaddr(rd), gi, b0);
   }
-  // quant_int.rs:316-323: acc += d*dq*(dot - 8*sq).
+  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
+    blk = gi;
+    w = sld_v4(rq + (uint32_t)(gi - b0) * 16u);
+    d = f16f(sld_u16(rd + (uint32_t)(gi - b0) * 2u));
+  }
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
-    const int4 a0 = ap[0], a1 = ap[1];
+    finish(ap[0], ap[1], A.d[blk], A.s[blk], t);
+  }
+  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
+    const uint32_t ap = A.q + (uint32_t)blk * 32u;
+    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_f(A.d + (uint32_t)blk * 4u), sld_i(A.s + (uint32_t)blk * 4u), t);
+  }
+  // quant_int.rs:316-323: acc += d*dq*(dot - 8*sq).
+  __device__ __forceinline__ void finish(const int4 a0, const int4 a1, float da_, int sa, float *t) const {
     int da = 0, db = 0;
     da = __dp4a(lo4(w.x), a0.x, da); db = __dp4a(lo4(w.y), a0.y, db);
     da = __dp4a(lo4(w.z), a0.z, da); db = __dp4a(lo4(w.w), a0.w, db);
     da = __dp4a(hi4(w.x), a1.x, da); db = __dp4a(hi4(w.y), a1.y, db);
     da = __dp4a(hi4(w.z), a1.z, da); db = __dp4a(hi4(w.w), a1.w, db);
     const int dot = da + db;
-    t[0] = fmul(fmul(d, A.d[blk]), fsub((float)dot, fmul(8.0f, (float)A.s[blk])));
+    t[0] = fmul(fmul(d, da_), fsub((float)dot, fmul(8.0f, (float)sa)));
   }
 };
 

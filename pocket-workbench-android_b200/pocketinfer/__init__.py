@@ -336,9 +336,9 @@ class Engine:
         _check(lib().pk_set_position(self.h, pos))
 
     def decode_profile(self) -> list:
-        stats = (KernelStat * 64)()
+        stats = (KernelStat * 128)()
         n = C.c_int()
-        _check(lib().pk_decode_profile(self.h, stats, 64, C.byref(n)))
+        _check(lib().pk_decode_profile(self.h, stats, 128, C.byref(n)))
         return [{"name": s.name.decode(), "launches": s.launches, "ms": s.ms, "bytes": s.bytes}
                 for s in stats[: n.value]]
 
