@@ -123,7 +123,7 @@ __device__ __forceinline__ const uint8_t *align16_down(const uint8_t *p) {
 
 // Shared memory layout (host and device agree through dk_layout).
 struct Layout {
-  size_t ring, full, empty, desc, aq, ad, as, u, qh, rope, xo, ph, nw, cwb, red, flag, prof, total;
+  size_t ring, full, empty, desc, aq, ad, as, as16, u, qh, rope, xo, ph, nw, cwb, red, flag, prof, total;
   int kmax, uf;
 };
 constexpr int DK_XO = 256;   // owned rows of x kept in shared memory
@@ -149,6 +149,7 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
   L.aq = o; o += up16(L.kmax);
   L.ad = o; o += up16((size_t)L.kmax / 32 * 4);
   L.as = o; o += up16((size_t)L.kmax / 32 * 4);
+  L.as16 = o; o += up16((size_t)L.kmax / 16 * 4);
   L.u = o; o += (size_t)L.uf * 4;
   L.qh = o; o += 3 * 256 * 4;  // q, current k, current v of one head
   L.rope = o; o += 2 * 128 * 4;  // cos, sin of this step's position
@@ -172,7 +173,8 @@ struct Smem {
   uint32_t *cwb;
   int8_t *aq;
   float *ad;
-  int32_t *as;
+  float *as;     // per 32-block sum of q, as a float (exact)
+  int32_t *as16;  // per 16-element sum of q
   float *u, *qh, *red;
   volatile int *flag;  // [0] abort
   unsigned long long *prof;
@@ -191,7 +193,8 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const Layout &L) {
   s.cwb = (uint32_t *)(base + L.cwb);
   s.aq = (int8_t *)(base + L.aq);
   s.ad = (float *)(base + L.ad);
-  s.as = (int32_t *)(base + L.as);
+  s.as = (float *)(base + L.as);
+  s.as16 = (int32_t *)(base + L.as16);
   s.u = (float *)(base + L.u);
   s.qh = (float *)(base + L.qh);
   s.red = (float *)(base + L.red);
@@ -203,42 +206,80 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const Layout &L) {
 __host__ __device__ inline int dk_gpb(int t) { return (t == T_Q4_K || t == T_Q6_K) ? 4 : 1; }
 __host__ __device__ inline int dk_tpg(int t) { return t == T_Q4_K ? 2 : (t == T_Q6_K ? 4 : 1); }
 
-// Q8Act::prepare (quant_int.rs:36-53) of one 32-block held four elements per
-// lane in an aligned group of 8 lanes: amax of |x| ignoring NaN, d = amax/127,
-// inv = 1/d (0 if d == 0), q = clamp(round_half_away(x*inv), +-127), NaN -> 0.
-// All 32 lanes of the warp must call it (the group reductions shuffle).
-__device__ __forceinline__ void q8_block8(const float4 v, int l8, bool store, int8_t *q, float *d, int32_t *sum) {
-  auto ab = [](float x) {
-    const float a = fabsf(x);
-    return a > 0.0f ? a : 0.0f;
-  };
-  float amax = ab(v.x), t;
-  t = ab(v.y); amax = t > amax ? t : amax;
-  t = ab(v.z); amax = t > amax ? t : amax;
-  t = ab(v.w); amax = t > amax ? t : amax;
+__device__ __forceinline__ void sst_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sst_v2(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void sst_i(uint32_t a, int v) { asm volatile("st.shared.s32 [%0], %1;" ::"r"(a), "r"(v) : "memory"); }
+
+// The Q8 activation in shared memory, by shared address: q [k] i8, d [k/32]
+// f32, s [k/32] f32 block sums, s16 [k/16] i32 half-block sums.
+struct DAct {
+  uint32_t q, d, s, s16;
+};
+
+// Q8Act::prepare (quant_int.rs:36-53) of one 32-block held E = 32 / L
+// elements per lane in an aligned group of L lanes: amax of |x| ignoring NaN,
+// d = amax/127, inv = 1/d (0 if d == 0), q = clamp(round_half_away(x*inv),
+// +-127), NaN -> 0.  Besides q and d it stores the sum of q as a float
+// (exact: |sum| <= 4064) and the sums of q over each 16-element half.  With
+// L > 1 all 32 lanes of the warp must call it (the group reductions
+// shuffle).  q_sa: this lane's E bytes; b: the block.
+template <int L>
+__device__ __forceinline__ void q8_lanes(const float (&v)[32 / L], bool store, int l, uint32_t q_sa, const DAct &A,
+                                         int b) {
+  constexpr int E = 32 / L;
+  float amax = 0.0f;  // every |x| below is >= 0, so starting at 0 leaves the maximum unchanged
 #pragma unroll
-  for (int o = 1; o < 8; o <<= 1) {
-    t = __shfl_xor_sync(0xffffffffu, amax, o);
+  for (int i = 0; i < E; i++) {
+    const float a = fabsf(v[i]);
+    const float t = a > 0.0f ? a : 0.0f;  // NaN -> 0
+    amax = t > amax ? t : amax;
+  }
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, amax, o);
     amax = t > amax ? t : amax;
   }
   const float dd = fdiv(amax, 127.0f);
   const float inv = dd > 0.0f ? fdiv(1.0f, dd) : 0.0f;
-  auto qz = [&](float x) {
-    float r = roundf(fmul(x, inv));
-    r = r < -127.0f ? -127.0f : r;
-    r = r > 127.0f ? 127.0f : r;
-    return isnan(r) ? 0 : (int)r;
-  };
-  const int q0 = qz(v.x), q1 = qz(v.y), q2 = qz(v.z), q3 = qz(v.w);
-  int sm = q0 + q1 + q2 + q3;
+  uint32_t w[E / 4];
+  int sh[2] = {0, 0};  // sums over this lane's elements of each 16-element half
 #pragma unroll
-  for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+  for (int j = 0; j < E / 4; j++) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      float r = roundf(fmul(v[4 * j + u], inv));
+      r = r < -127.0f ? -127.0f : r;
+      r = r > 127.0f ? 127.0f : r;
+      const int qi = isnan(r) ? 0 : (int)r;
+      sh[j * 4 >= 16 ? 1 : 0] += qi;
+      word |= (uint32_t)(qi & 0xFF) << (8 * u);
+    }
+    w[j] = word;
+  }
+  static_assert(L == 1 || L == 4, "4 or 1 lanes per block");
+  int h0 = sh[0], h1 = sh[1];
+  if (L == 4) {  // lanes 0-1 hold the first half, lanes 2-3 the second
+    const int pair = sh[0] + __shfl_xor_sync(0xffffffffu, sh[0], 1);
+    const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
+    h0 = (l & 2) ? other : pair;
+    h1 = (l & 2) ? pair : other;
+  }
   if (store) {
-    *reinterpret_cast<uint32_t *>(q + 4 * l8) =
-        (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) | ((uint32_t)(q3 & 0xFF) << 24);
-    if (l8 == 0) {
-      *d = dd;
-      *sum = sm;
+    if constexpr (E == 32) {
+      sst_v4(q_sa, w[0], w[1], w[2], w[3]);
+      sst_v4(q_sa + 16, w[4], w[5], w[6], w[7]);
+    } else {
+      sst_v2(q_sa, w[0], w[1]);
+    }
+    if (l == 0) {
+      sst_f(A.d + 4u * (uint32_t)b, dd);
+      sst_f(A.s + 4u * (uint32_t)b, (float)(h0 + h1));
+      sst_v2(A.s16 + 8u * (uint32_t)b, (uint32_t)h0, (uint32_t)h1);
     }
   }
 }
@@ -332,6 +373,123 @@ __device__ __forceinline__ float chain_wv(float acc, uint32_t e, uint32_t v, uin
   return acc;
 }
 
+// ---------------------------------------------------------------- term items
+// The reference's row dots (quant_int.rs:282-419, lanes::*) add one float
+// term per (sub-)block to the row's accumulator.  An item computes the terms
+// of one staged block (Q8_0, Q4_0) or superblock (Q4_K: 8 terms, Q6_K: 16) of
+// one row and stores them at t_a + i * ts (term i).  Integer dots are exact
+// in any order; every float expression keeps the reference's operand order.
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {  // unsigned bytes of a times signed bytes of b
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// lanes::q4_k (quant_int.rs:354-365): term_j = (d*da_j)*sc_j*dot_j - (da_j*dmin)*m_j*sa_j.
+__device__ __forceinline__ void item_q4k(uint32_t w_a, int blk, const DAct &A, uint32_t t_a, uint32_t ts) {
+  const uint4 hdr = sld_v4(w_a);
+  const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
+  // get_scale_min_k4 (quant.rs:80-86) for all eight sub-blocks, a byte each:
+  // the 12 scale bytes are hdr.y | hdr.z | hdr.w.
+  const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
+  const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+  const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+  const uint32_t xq = A.q + (uint32_t)blk * 256u, xf = (uint32_t)blk * 32u;
+#pragma unroll
+  for (int p = 0; p < 4; p++) {  // sub-blocks 2p (low nibbles) and 2p + 1 (high nibbles)
+    const uint4 w0 = sld_v4(w_a + 16 + 32 * p), w1 = sld_v4(w_a + 32 + 32 * p);
+    const uint32_t xa = xq + 64u * p;
+    const int4 x0 = sld_v4i(xa), x1 = sld_v4i(xa + 16), x2 = sld_v4i(xa + 32), x3 = sld_v4i(xa + 48);
+    const float da0 = sld_f(A.d + xf + 8u * p), da1 = sld_f(A.d + xf + 8u * p + 4u);
+    const float sa0 = sld_f(A.s + xf + 8u * p), sa1 = sld_f(A.s + xf + 8u * p + 4u);
+    const uint32_t M = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+    int d0a = 0, d0b = 0, d1a = 0, d1b = 0;
+    d0a = __dp4a((int)(w0.x & M), x0.x, d0a); d0b = __dp4a((int)(w0.y & M), x0.y, d0b);
+    d0a = __dp4a((int)(w0.z & M), x0.z, d0a); d0b = __dp4a((int)(w0.w & M), x0.w, d0b);
+    d0a = __dp4a((int)(w1.x & M), x1.x, d0a); d0b = __dp4a((int)(w1.y & M), x1.y, d0b);
+    d0a = __dp4a((int)(w1.z & M), x1.z, d0a); d0b = __dp4a((int)(w1.w & M), x1.w, d0b);
+    // high nibbles in place: 16 * dot, divided back exactly
+    d1a = dp4a_us(w0.x & H, x2.x, d1a); d1b = dp4a_us(w0.y & H, x2.y, d1b);
+    d1a = dp4a_us(w0.z & H, x2.z, d1a); d1b = dp4a_us(w0.w & H, x2.w, d1b);
+    d1a = dp4a_us(w1.x & H, x3.x, d1a); d1b = dp4a_us(w1.y & H, x3.y, d1b);
+    d1a = dp4a_us(w1.z & H, x3.z, d1a); d1b = dp4a_us(w1.w & H, x3.w, d1b);
+    const int dot0 = d0a + d0b, dot1 = (d1a + d1b) >> 4;
+    const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
+    const int sh = (2 * p & 3) * 8;
+    const float sc0 = (float)((scw >> sh) & 0xFFu), m0 = (float)((mw >> sh) & 0xFFu);
+    const float sc1 = (float)((scw >> (sh + 8)) & 0xFFu), m1 = (float)((mw >> (sh + 8)) & 0xFFu);
+    sst_f(t_a + ts * (uint32_t)(2 * p), fsub(fmul(fmul(fmul(d, da0), sc0), (float)dot0), fmul(fmul(fmul(da0, dmin), m0), sa0)));
+    sst_f(t_a + ts * (uint32_t)(2 * p + 1),
+          fsub(fmul(fmul(fmul(d, da1), sc1), (float)dot1), fmul(fmul(fmul(da1, dmin), m1), sa1)));
+  }
+}
+
+// lanes::q6_k (quant_int.rs:386-413) for half h of a superblock: per
+// 16-element piece, order (g, s), term = ((d*scale)*da)*dot with
+// dot = sum((q - 32) a), computed as sum(q a) - 32 sum(a).  Term i of the
+// half is the superblock's term 8h + i.
+__device__ __forceinline__ void item_q6k(uint32_t w_a, uint32_t d_a, int blk, int h, const DAct &A, uint32_t t_a,
+                                         uint32_t ts) {
+  const uint2 scw = sld_v2(w_a + 192 + 8 * h);  // this half's eight scales
+  const float d = f16f(sld_u16(d_a));
+  {
+    const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+      const uint4 qa = sld_v4(w_a + h * 64 + g * 16), qb = sld_v4(w_a + h * 64 + 32 + g * 16),
+                  qh = sld_v4(w_a + 128 + h * 32 + g * 16);
+#pragma unroll
+      for (int s = 0; s < 4; s++) {
+        const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);  // activation block
+        const int4 x = sld_v4i(A.q + ab * 32u + g * 16);
+        const float da = sld_f(A.d + ab * 4u);
+        const int s16 = sld_i(A.s16 + (ab * 2u + g) * 4u);
+        int pa = 0, pb = 0;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {  // quant_int.rs:386-394 unpacking, four bytes at a time (0..63)
+          const uint32_t lo = word_of(s & 1 ? qb : qa, w), hh = word_of(qh, w);
+          const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) | ((s == 0 ? hh << 4 : s == 1 ? hh << 2 : s == 2 ? hh : hh >> 2) & 0x30303030u);
+          const int xw = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
+          if (w & 1) pb = __dp4a((int)q, xw, pb);
+          else pa = __dp4a((int)q, xw, pa);
+        }
+        const int dot = pa + pb - 32 * s16;
+        const float scale = (float)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s)));
+        sst_f(t_a + ts * (uint32_t)(g * 4 + s), fmul(fmul(fmul(d, scale), da), (float)dot));
+      }
+    }
+  }
+}
+
+// lanes::q8_0 (quant_int.rs:291-296): term = (d*da)*dot.
+__device__ __forceinline__ void item_q80(uint32_t w_a, uint32_t d_a, int blk, const DAct &A, uint32_t t_a) {
+  const uint4 w0 = sld_v4(w_a), w1 = sld_v4(w_a + 16);
+  const uint32_t xa = A.q + (uint32_t)blk * 32u;
+  const int4 x0 = sld_v4i(xa), x1 = sld_v4i(xa + 16);
+  const float d = f16f(sld_u16(d_a)), da = sld_f(A.d + (uint32_t)blk * 4u);
+  int pa = 0, pb = 0;
+  pa = __dp4a((int)w0.x, x0.x, pa); pb = __dp4a((int)w0.y, x0.y, pb);
+  pa = __dp4a((int)w0.z, x0.z, pa); pb = __dp4a((int)w0.w, x0.w, pb);
+  pa = __dp4a((int)w1.x, x1.x, pa); pb = __dp4a((int)w1.y, x1.y, pb);
+  pa = __dp4a((int)w1.z, x1.z, pa); pb = __dp4a((int)w1.w, x1.w, pb);
+  sst_f(t_a, fmul(fmul(d, da), (float)(pa + pb)));
+}
+
+// lanes::q4_0 (quant_int.rs:316-323): term = (d*da)*(dot - 8*sa).
+__device__ __forceinline__ void item_q40(uint32_t w_a, uint32_t d_a, int blk, const DAct &A, uint32_t t_a) {
+  const uint4 w = sld_v4(w_a);
+  const uint32_t xa = A.q + (uint32_t)blk * 32u;
+  const int4 x0 = sld_v4i(xa), x1 = sld_v4i(xa + 16);
+  const float d = f16f(sld_u16(d_a)), da = sld_f(A.d + (uint32_t)blk * 4u), sa = sld_f(A.s + (uint32_t)blk * 4u);
+  int pa = 0, pb = 0;
+  pa = __dp4a(lo4(w.x), x0.x, pa); pb = __dp4a(lo4(w.y), x0.y, pb);
+  pa = __dp4a(lo4(w.z), x0.z, pa); pb = __dp4a(lo4(w.w), x0.w, pb);
+  pa = __dp4a(hi4(w.x), x1.x, pa); pb = __dp4a(hi4(w.y), x1.y, pb);
+  pa = __dp4a(hi4(w.z), x1.z, pa); pb = __dp4a(hi4(w.w), x1.w, pb);
+  sst_f(t_a, fmul(fmul(d, da), fsub((float)(pa + pb), fmul(8.0f, sa))));
+}
+
 // A chunk descriptor copied from shared memory into registers.
 __device__ __forceinline__ DChunk load_desc(uint32_t a) {
   DChunk c;
@@ -419,8 +577,9 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
           if (c.d) bulk_g2s(dst + c.d_off, align16_down(c.d), c.d_len, fb);
         }
       } else {
+        const uint32_t pitch = c.q_len + 16u * c.qpad;
         for (int r = lane; r < c.rows; r += 32) {
-          bulk_g2s(dst + (size_t)r * c.q_len, c.q + (size_t)r * c.q_stride, c.q_len, fb);
+          bulk_g2s(dst + (size_t)r * pitch, c.q + (size_t)r * c.q_stride, c.q_len, fb);
           if (c.d) bulk_g2s(dst + c.d_off + (size_t)r * c.d_len, align16_down(c.d + (size_t)r * c.d_stride), c.d_len, fb);
         }
       }
@@ -467,8 +626,8 @@ struct Cons {
   const DChunk *ch;
   const int *ph;
   int pos, tid, ctid, cwarp, lane, own0, cw_base;
-  uint32_t ring_a, u_a, desc_a;
-  SAct act_a;
+  uint32_t ring_a, u_a, desc_a, nw_a;
+  DAct act_a;
   Ring rg;
   int mv = 0, mv_total = 0;
   unsigned gen = 0;
@@ -488,11 +647,15 @@ struct Cons {
     ring_a = shaddr(S.ring);
     u_a = shaddr(S.u);
     desc_a = shaddr(S.desc);
-    act_a = SAct{shaddr(S.aq), shaddr(S.ad), shaddr(S.as)};
+    nw_a = shaddr(S.nw);
+    act_a = DAct{shaddr(S.aq), shaddr(S.ad), shaddr(S.as), shaddr(S.as16)};
   }
 
+  // Ring-data stalls are timed for consumer thread 0 (attention) and the
+  // first term thread (matvec phases).
+  static constexpr int TT0 = 32 * DK_CHAINS;
   __device__ __forceinline__ void wait_full_at(int j) {  // the transfer j places ahead
-    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == 32);
+    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == TT0);
     const long long t0 = timed ? clock64() : 0;
     const bool ok = mbar_wait(&S.full[rg.slot_at(j)], rg.par_at(j), S.flag);
     if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
@@ -502,7 +665,7 @@ struct Cons {
     }
   }
   __device__ __forceinline__ void wait_full() {
-    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == 32);
+    const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == TT0);
     const long long t0 = timed ? clock64() : 0;
     const bool ok = mbar_wait(&S.full[rg.slot], rg.par, S.flag);
     if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
@@ -513,14 +676,15 @@ struct Cons {
   }
 
   // Profile trace (only when (TRACE && a.trace) is set), per CTA:
-  //   [0] start (ns); phase q = 5L + {qkv, attn, o, gate/up, down}, base
-  //   1 + 8q: [+0] prologue end, [+1] compute end, [+2] barrier exit (ns);
-  //   SM cycles: [+3] waiting for ring data, [+4] term warps waiting for a
-  //   term buffer, [+5] term computation, [+6] chain warp waiting for terms,
-  //   [+7] chain + epilogue; head: [1 + 40L + 0] prologue end, [+1] end (ns);
-  //   [1 + 40L + 2 + layer] SM cycles the producer waited for a free slot.
-  // Accumulators live in shared memory: S.prof[0] data wait of thread 0,
-  // [1] of thread 32, [2..5] the term / chain figures.
+  //   [0] start (ns); phase q = 5L + {qkv, attn, o, gate/up, down} (q = 5n:
+  //   the head), base 1 + DK_TRW q: [+0] prologue end, [+1] compute end,
+  //   [+2] barrier exit (ns); SM cycles: [+3] waiting for ring data, [+4]
+  //   term warps waiting for a term buffer, [+5] term computation, [+6]
+  //   chain warp 0 waiting for terms, [+7] chain warp 0 sums + epilogue;
+  //   [+8 .. +15] fine stamps (ns) inside the phase;
+  //   [1 + DK_TRW (5n + 1) + layer] SM cycles the producer waited for a slot.
+  // Accumulators live in shared memory: S.prof[0] data wait of consumer
+  // thread 0, [1] of the first term thread, [2..5] the term / chain figures.
   __device__ __forceinline__ void pacc(int i, long long c) {
     if ((TRACE && a.trace)) S.prof[i] += (unsigned long long)c;
   }
@@ -616,24 +780,52 @@ struct Cons {
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
 
-  // Q8 of the staged vector (optionally v = (x * scale) * w first, w in the
-  // shared norm buffer), eight lanes per 32-block.
-  __device__ void quant(int k, bool norm, float scale) {
-    const int nb = k >> 5, gi = ctid >> 3, l8 = ctid & 7;
-    const float4 *x4 = reinterpret_cast<const float4 *>(S.u);
-    const float4 *w4 = reinterpret_cast<const float4 *>(S.nw);
-    for (int base = 0; base < nb; base += CONS / 8) {
-      const int b = base + gi;
+  // Q8 of a k-vector, L lanes per 32-block.  FROM_G: read it from global
+  // memory (this launch's data, through L2); otherwise from the staging
+  // buffer, optionally as v = (x * scale) * w with w in the norm buffer.
+  template <int L, bool FROM_G>
+  __device__ void quant_l(const float *src, int k, bool norm, float scale) {
+    constexpr int E = 32 / L;
+    const int nb = k >> 5, per = CONS / L, l = ctid % L;
+    for (int base = 0; base < nb; base += per) {  // the same trip count on every consumer thread
+      const int b = base + ctid / L;
       const bool ok = b < nb;
-      float4 v = ok ? x4[b * 8 + l8] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (norm && ok) {
-        const float4 w = w4[b * 8 + l8];
-        v = make_float4(fmul(fmul(v.x, scale), w.x), fmul(fmul(v.y, scale), w.y), fmul(fmul(v.z, scale), w.z),
-                        fmul(fmul(v.w, scale), w.w));
+      const int e0 = b * 32 + l * E;  // first element of this lane
+      float v[E];
+#pragma unroll
+      for (int j = 0; j < E / 4; j++) {
+        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (ok) {
+          if (FROM_G) {
+            x = __ldcg(reinterpret_cast<const float4 *>(src + e0) + j);
+          } else {
+            x = sld_v4f(u_a + 4u * (uint32_t)(e0 + 4 * j));
+            if (norm) {
+              const float4 w = sld_v4f(nw_a + 4u * (uint32_t)(e0 + 4 * j));
+              x = make_float4(fmul(fmul(x.x, scale), w.x), fmul(fmul(x.y, scale), w.y), fmul(fmul(x.z, scale), w.z),
+                              fmul(fmul(x.w, scale), w.w));
+            }
+          }
+        }
+        v[4 * j] = x.x;
+        v[4 * j + 1] = x.y;
+        v[4 * j + 2] = x.z;
+        v[4 * j + 3] = x.w;
       }
-      q8_block8(v, l8, ok, S.aq + b * 32, S.ad + b, S.as + b);
+      q8_lanes<L>(v, ok, l, act_a.q + (uint32_t)e0, act_a, b);
     }
     bar_sync(NB_CONS, CONS);
+  }
+  // One round where the consumers allow: four lanes per block when every
+  // block fits, else one.
+  __device__ void quant(const float *src, int k, bool norm, float scale, bool from_g) {
+    if ((k >> 5) * 4 <= CONS) {
+      if (from_g) quant_l<4, true>(src, k, norm, scale);
+      else quant_l<4, false>(src, k, norm, scale);
+    } else {
+      if (from_g) quant_l<1, true>(src, k, norm, scale);
+      else quant_l<1, false>(src, k, norm, scale);
+    }
   }
 
   // RMSNorm (b == 1 order, simd.rs:47-64) + Q8 of the staged vector; the
@@ -653,71 +845,43 @@ struct Cons {
     }
     bar_sync(NB_CONS, CONS);
     fine(1);
-    quant(k, true, S.red[32]);
+    quant(nullptr, k, true, S.red[32], false);
   }
 
-  __device__ void q8(int k) { quant(k, false, 1.0f); }
-
+  // The terms of one staged chunk: one item per (row, block or superblock),
+  // rows fastest, so the lanes of a warp share activation blocks and read
+  // the weights of different rows (staged row pitches are odd multiples of
+  // 16 bytes: conflict-free 16-byte loads).
   template <int T>
   __device__ void terms(const DChunk &c, uint32_t sl, uint32_t Tb) {
-    constexpr int GPB = (T == T_Q4_K || T == T_Q6_K) ? 4 : 1, TPG = Geo<T>::TPG;
+    // terms per item; Q6_K items are half superblocks (j = 2 superblock + half)
+    constexpr int TPI = T == T_Q4_K ? 8 : (T == T_Q6_K ? 8 : 1), IPB = T == T_Q6_K ? 2 : 1;
     constexpr int QB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 208 : (T == T_Q8_0 ? 32 : 16));
-    const int R = c.rows, nbk = c.b1 - c.b0, G = nbk * GPB, items = R * G, rs = c.rs;
-    const int qrs = nbk * QB;
-    // Item (row, group): rows fastest for the k-quants (lanes of a warp share
-    // one activation block), groups fastest for Q8_0/Q4_0 (contiguous bytes).
-    // Each thread keeps two items in flight.
-    const int M = GPB == 4 ? R : G, df = TERM_T % M, ds = TERM_T / M;
-    int t = tid - 32 - 32 * DK_CHAINS, f = t % M, sl_ = t / M;
-    auto adv = [&](int &a, int &b) {
-      a += df;
-      b += ds;
-      if (a >= M) {
-        a -= M;
-        b++;
-      }
-    };
+    const int R = c.rows, items = R * (c.b1 - c.b0) * IPB, rs = c.rs;
+    const uint32_t pitch = c.full ? c.q_stride : c.q_len + 16u * c.qpad;
     const uintptr_t d0 = (uintptr_t)c.d;
-    auto ptrs = [&](int rl, uint32_t &rq, uint32_t &rd) {
-      rq = sl + (uint32_t)(rl * qrs);
-      rd = 0u;
+    const int dr = TERM_T % R, dj = TERM_T / R;
+    int t = tid - 32 - 32 * DK_CHAINS, r = t % R, j = t / R;
+    for (; t < items; t += TERM_T) {
+      const int jb = j / IPB;  // block or superblock within the staged row
+      const uint32_t w_a = sl + (uint32_t)r * pitch + (uint32_t)(jb * QB);
+      const uint32_t t_a = Tb + 4u * (uint32_t)(j * TPI * rs + r), ts = 4u * (uint32_t)rs;
+      uint32_t d_a = 0u;
       if (T != T_Q4_K)
-        rd = sl + c.d_off +
-             (uint32_t)(c.full ? (d0 & 15) + (size_t)rl * c.d_stride
-                               : (size_t)rl * c.d_len + ((d0 + (size_t)rl * c.d_stride) & 15));
-    };
-    constexpr bool kTwo = false;  // one item per step measured faster than two in the full kernel
-    for (; t < items; t += (kTwo ? 2 : 1) * TERM_T) {
-      int f2 = f, s2 = sl_;
-      adv(f2, s2);
-      const bool two = kTwo && t + TERM_T < items;
-      const int rl1 = GPB == 4 ? f : sl_, gl1 = GPB == 4 ? sl_ : f;
-      const int rl2 = two ? (GPB == 4 ? f2 : s2) : rl1, gl2 = two ? (GPB == 4 ? s2 : f2) : gl1;
-      uint32_t rq1, rd1, rq2, rd2;
-      ptrs(rl1, rq1, rd1);
-      ptrs(rl2, rq2, rd2);
-      float t1[TPG], t2[TPG];
-      {
-        GroupW<T> g1;
-        g1.load_sa(rq1, rd1, c.b0 * GPB + gl1, c.b0);
-        if (kTwo) {
-          GroupW<T> g2;
-          g2.load_sa(rq2, rd2, c.b0 * GPB + gl2, c.b0);
-          g1.terms_sa(act_a, t1);
-          g2.terms_sa(act_a, t2);
-        } else {
-          g1.terms_sa(act_a, t1);
-        }
+        d_a = sl + c.d_off + 2u * (uint32_t)jb +
+              (uint32_t)(c.full ? (d0 & 15) + (size_t)r * c.d_stride
+                                : (size_t)r * c.d_len + ((d0 + (size_t)r * c.d_stride) & 15));
+      const int blk = c.b0 + jb;
+      if (T == T_Q4_K) item_q4k(w_a, blk, act_a, t_a, ts);
+      else if (T == T_Q6_K) item_q6k(w_a, d_a, blk, j & 1, act_a, t_a, ts);
+      else if (T == T_Q8_0) item_q80(w_a, d_a, blk, act_a, t_a);
+      else item_q40(w_a, d_a, blk, act_a, t_a);
+      r += dr;
+      j += dj;
+      if (r >= R) {
+        r -= R;
+        j++;
       }
-#pragma unroll
-      for (int s = 0; s < TPG; s++) sst_f(Tb + 4u * (uint32_t)((gl1 * TPG + s) * rs + rl1), t1[s]);
-      if (two) {
-#pragma unroll
-        for (int s = 0; s < TPG; s++) sst_f(Tb + 4u * (uint32_t)((gl2 * TPG + s) * rs + rl2), t2[s]);
-      }
-      if (kTwo) adv(f2, s2);
-      f = f2;
-      sl_ = s2;
     }
   }
 
@@ -1049,9 +1213,12 @@ struct Cons {
         const bool norm = kind == 0 || kind == 3 || kind == 5;
         const float *src = kind == 2 ? a.att : kind == 4 ? a.h : a.x;
         const int k = kind == 2 ? qdim : kind == 4 ? a.n_ff : a.n_embd;
-        if (q > 0) stage(src, k);
-        if (norm) norm_q8(k);
-        else q8(k);
+        if (norm) {
+          if (q > 0) stage(src, k);  // layer 0's input was staged by embed()
+          norm_q8(k);
+        } else {
+          quant(src, k, false, 1.0f, true);  // attention output / SwiGLU: straight from L2
+        }
         mark(q, 0);
         run_mv(kind == 5 ? 4 * a.n_layer : 4 * L + (kind == 0 ? 0 : kind - 1));
       }
@@ -1196,7 +1363,8 @@ struct Builder {
       c.d_off = c.q_len;
     } else {
       c.q_len = (uint32_t)((size_t)(b1 - b0) * g.qb);
-      c.d_off = (uint32_t)((size_t)rows * c.q_len);
+      c.qpad = (uint8_t)(((c.q_len >> 4) & 1u) ? 0 : 1);  // odd pitch / 16: rows land on distinct banks
+      c.d_off = (uint32_t)((size_t)rows * (c.q_len + 16u * c.qpad));
     }
     if (g.has_d) {
       c.d = reinterpret_cast<const uint8_t *>(W.d) + (size_t)r * row_d + (size_t)b0 * 2;
@@ -1265,7 +1433,7 @@ struct Builder {
         if (!full) {
           int nbmax = 0;
           for (int nb = m.nblk; nb >= 1; nb--) {
-            const size_t bytes = (size_t)R * (nb * (size_t)m.g.qb + (m.g.has_d ? up16h((size_t)nb * 2 + 15) : 0));
+            const size_t bytes = (size_t)R * (nb * (size_t)m.g.qb + 16 + (m.g.has_d ? up16h((size_t)nb * 2 + 15) : 0));
             if (bytes <= (size_t)DK_SLOT && (size_t)(R | 1) * nb * m.g.gpb * m.g.tpg <= (size_t)DK_TS) {
               nbmax = nb;
               break;

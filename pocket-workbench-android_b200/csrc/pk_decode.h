@@ -32,9 +32,10 @@ enum : uint8_t { DF_FIRST = 1, DF_LAST = 2 };
 
 // One ring transfer: rows [row0, row0 + rows) x blocks [b0, b1) of one matrix.
 // full: the rows are whole and contiguous, one copy for q and one for d.
-// Otherwise one q copy and one d copy per row.  d copies start at the
-// 16-byte boundary at or below the row's first scale; the consumer recovers
-// the skew from the source address.
+// Otherwise one q copy and one d copy per row, the staged rows q_len +
+// 16 qpad bytes apart.  d copies start at the 16-byte boundary at or below
+// the row's first scale; the consumer recovers the skew from the source
+// address.
 struct DChunk {
   const uint8_t *q;   // row 0's q bytes at block b0
   const uint8_t *d;   // row 0's first f16 scale at block b0 (nullptr: scales inline)
@@ -46,7 +47,9 @@ struct DChunk {
   uint16_t rows, rs;  // rows; term-buffer row stride (odd)
   uint8_t type, role, full, flags;
   int row0, b0, b1, layer;
-  uint8_t cw, pad_[3];  // chain warp that sums these rows
+  uint8_t cw;          // chain warp that sums these rows
+  uint8_t qpad;        // not full: extra 16-byte units after each staged row (odd row pitch / 16)
+  uint8_t pad_[2];
 };
 static_assert(sizeof(DChunk) == 64, "DChunk is one 64-byte record");
 

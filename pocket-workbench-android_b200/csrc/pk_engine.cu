@@ -875,6 +875,12 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
     std::vector<unsigned long long> tr((size_t)grid * nt);
     PK_CK(cudaMemcpyAsync(tr.data(), d_trace_, tr.size() * 8, cudaMemcpyDeviceToHost, st_));
     PK_CK(cudaStreamSynchronize(st_));
+    if (const char *dump = std::getenv("PK_TRACE_DUMP")) {  // raw per-CTA trace: grid x n_trace u64 words
+      if (FILE *f = std::fopen(dump, "wb")) {
+        std::fwrite(tr.data(), 8, tr.size(), f);
+        std::fclose(f);
+      }
+    }
     auto at = [&](int g, int i) { return (double)tr[(size_t)g * nt + i]; };
     int khz = 0;
     PK_CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device_));

@@ -111,18 +111,10 @@ struct ActRef {  // one lane's Q8 activation: q [k], d/s [k/32]
 __device__ __forceinline__ int lo4(uint32_t w) { return (int)(w & 0x0F0F0F0Fu); }
 __device__ __forceinline__ int hi4(uint32_t w) { return (int)((w >> 4) & 0x0F0F0F0Fu); }
 
-// A group of one row's blocks.  load() reads the device layout in global
-// memory; load_s()/load_sa() read a staged copy of one row's blocks [b0, ...)
-// in shared memory (by pointer / by shared address): rq = that row's first
-// staged block, rd = its first staged f16 scale (the types that keep d
-// apart).  gi is always the global group.  terms() takes the activation by
-// pointer, terms_sa() by shared address; both end in the same finish().
+// A group of one row's blocks, read from the device layout in global memory
+// (load), combined with a Q8 activation (terms -> finish).  gi is the
+// group's index within the row.
 template <int T> struct GroupW;
-
-// A Q8 activation in shared memory by shared address: q [k] i8, d/s [k/32].
-struct SAct {
-  uint32_t q, d, s;
-};
 
 template <> struct GroupW<T_Q4_K> {
   uint4 hdr, w0, w1;
@@ -137,28 +129,10 @@ template <> struct GroupW<T_Q4_K> {
     w0 = ldw16(base + 16 + g * 32);
     w1 = ldw16(base + 32 + g * 32);
   }
-  __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *, int gi, int b0) {
-    load_sa(shaddr(rq), 0u, gi, b0);
-  }
-  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t, int gi, int b0) {
-    blk = gi >> 2;
-    const int g = gi & 3;
-    sb0 = 2 * g;
-    const uint32_t base = rq + (uint32_t)(blk - b0) * 144u;
-    hdr = sld_v4(base);
-    w0 = sld_v4(base + 16 + g * 32);
-    w1 = sld_v4(base + 32 + g * 32);
-  }
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 256 + sb0 * 32);
     const int ai = blk * 8 + sb0;
     finish(ap[0], ap[1], ap[2], ap[3], A.d[ai], A.d[ai + 1], A.s[ai], A.s[ai + 1], t);
-  }
-  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
-    const uint32_t ap = A.q + (uint32_t)(blk * 256 + sb0 * 32);
-    const uint32_t ai = (uint32_t)(blk * 8 + sb0) * 4u;
-    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_v4i(ap + 32), sld_v4i(ap + 48), sld_f(A.d + ai), sld_f(A.d + ai + 4),
-           sld_i(A.s + ai), sld_i(A.s + ai + 4), t);
   }
   // quant_int.rs:354-365: acc += d*da*s*dot - da*dmin*m*sa per sub-block.
   __device__ __forceinline__ void finish(const int4 a00, const int4 a01, const int4 a10, const int4 a11, float da0,
@@ -211,18 +185,6 @@ template <> struct GroupW<T_Q6_K> {
     d = f16f(__ldg(W.d + bidx));
     unpack(ldw16(base + h * 64 + g * 16), ldw16(base + h * 64 + 32 + g * 16), ldw16(base + 128 + h * 32 + g * 16));
   }
-  __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
-    load_sa(shaddr(rq), shaddr(rd), gi, b0);
-  }
-  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
-    blk = gi >> 2;
-    h = (gi >> 1) & 1;
-    g = gi & 1;
-    const uint32_t base = rq + (uint32_t)(blk - b0) * 208u;
-    scv = sld_v4(base + 192);
-    d = f16f(sld_u16(rd + (uint32_t)(blk - b0) * 2u));
-    unpack(sld_v4(base + h * 64 + g * 16), sld_v4(base + h * 64 + 32 + g * 16), sld_v4(base + 128 + h * 32 + g * 16));
-  }
   __device__ __forceinline__ void unpack(const uint4 &qa, const uint4 &qb, const uint4 &qh) {
 #pragma unroll
     for (int w = 0; w < 4; w++) {  // quant_int.rs:386-394 unpacking, four bytes at a time
@@ -240,16 +202,6 @@ template <> struct GroupW<T_Q6_K> {
     for (int s = 0; s < 4; s++) {
       a[s] = *reinterpret_cast<const int4 *>(A.q + blk * 256 + (4 * h + s) * 32 + g * 16);
       da[s] = A.d[blk * 8 + 4 * h + s];
-    }
-    finish(a, da, t);
-  }
-  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
-    int4 a[4];
-    float da[4];
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      a[s] = sld_v4i(A.q + (uint32_t)(blk * 256 + (4 * h + s) * 32 + g * 16));
-      da[s] = sld_f(A.d + (uint32_t)(blk * 8 + 4 * h + s) * 4u);
     }
     finish(a, da, t);
   }
@@ -282,22 +234,9 @@ template <> struct GroupW<T_Q8_0> {
     w1 = ldw16(qs + 16);
     d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
   }
-  __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
-    load_sa(shaddr(rq), shaddr(rd), gi, b0);
-  }
-  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
-    blk = gi;
-    w0 = sld_v4(rq + (uint32_t)(gi - b0) * 32u);
-    w1 = sld_v4(rq + (uint32_t)(gi - b0) * 32u + 16u);
-    d = f16f(sld_u16(rd + (uint32_t)(gi - b0) * 2u));
-  }
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
     finish(ap[0], ap[1], A.d[blk], t);
-  }
-  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
-    const uint32_t ap = A.q + (uint32_t)blk * 32u;
-    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_f(A.d + (uint32_t)blk * 4u), t);
   }
   // quant_int.rs:291-296: acc += d*da*dot.
   __device__ __forceinline__ void finish(const int4 a0, const int4 a1, float da_, float *t) const {
@@ -320,21 +259,9 @@ template <> struct GroupW<T_Q4_0> {
     w = ldw16(W.q + (size_t)row * (W.k >> 1) + (size_t)gi * 16);
     d = f16f(__ldg(W.d + (size_t)row * (W.k >> 5) + gi));
   }
-  __device__ __forceinline__ void load_s(const uint8_t *rq, const uint8_t *rd, int gi, int b0) {
-    load_sa(shaddr(rq), shaddr(rd), gi, b0);
-  }
-  __device__ __forceinline__ void load_sa(uint32_t rq, uint32_t rd, int gi, int b0) {
-    blk = gi;
-    w = sld_v4(rq + (uint32_t)(gi - b0) * 16u);
-    d = f16f(sld_u16(rd + (uint32_t)(gi - b0) * 2u));
-  }
   __device__ __forceinline__ void terms(const ActRef &A, float *t) const {
     const int4 *ap = reinterpret_cast<const int4 *>(A.q + blk * 32);
     finish(ap[0], ap[1], A.d[blk], A.s[blk], t);
-  }
-  __device__ __forceinline__ void terms_sa(const SAct &A, float *t) const {
-    const uint32_t ap = A.q + (uint32_t)blk * 32u;
-    finish(sld_v4i(ap), sld_v4i(ap + 16), sld_f(A.d + (uint32_t)blk * 4u), sld_i(A.s + (uint32_t)blk * 4u), t);
   }
   // quant_int.rs:316-323: acc += d*dq*(dot - 8*sq).
   __device__ __forceinline__ void finish(const int4 a0, const int4 a1, float da_, int sa, float *t) const {
