@@ -10,9 +10,10 @@
 //   swiglu / residuals             model.rs:1095-1125
 //   greedy sample                  sampler.rs:26-36
 //
-// Work split.  The grid has one CTA per SM and every CTA owns a fixed slice
-// of rows of every matrix (host-built chunk list).  Per CTA:
-//   warp 0, lane 0   producer: walks the chunk list (plus the K/V history of
+// Work split.  The grid has one CTA per SM (fewer for small models: every
+// CTA owns rows of every matrix) and every CTA owns a fixed slice of rows of
+// every matrix (host-built chunk list).  Per CTA:
+//   warp 0           producer: walks the chunk list (plus the K/V history of
 //                    the attention heads this CTA owns) and bulk-copies each
 //                    chunk into the next free ring slot (mbarrier complete_tx);
 //   warps 3..11      term warps: integer dots + float terms of a chunk into a
@@ -20,13 +21,18 @@
 //   warps 1, 2       chain warps: one lane per row adds that row's terms in
 //                    the reference's order and runs the epilogue; each row
 //                    group is assigned to one of them by the plan.
-// Between the phases of a layer (qkv | attention | o | gate+up | down) the
-// consumers meet at a grid barrier; the producer does not, so the weights of
-// the next phases keep streaming in while the barrier resolves.
+// Phase hand-off (qkv | attention | o | gate+up | down): the epilogues
+// publish their rows as tagged 8-byte words (value + epoch/phase tag) and
+// the next phase's readers poll the words they need until every tag is the
+// previous phase's, so no grid barrier separates the phases.  No CTA can get
+// two phases ahead of another: each phase reads all of the previous phase's
+// output (attention reads its heads' q/k/v, and the o phase then reads every
+// head), and every CTA writes rows of every phase; the residual alternates
+// between two buffers.  The producer streams on regardless.
 //
 // Every wait is bounded (2 s); a wait that runs out records PK_ERR_TIMEOUT in
-// the error word, the CTA stops at its next barrier, and the producer waits
-// for its own copies in flight before it returns.
+// the error word, the CTA's consumers stop together at the end of the phase,
+// and the producer waits for its own copies in flight before it returns.
 #include <float.h>
 #include <limits.h>
 #include <math.h>
@@ -61,6 +67,17 @@ __device__ __forceinline__ unsigned long long gtime() {
 }
 __device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// Named barrier that also ORs a predicate over the participating threads:
+// every thread gets the same answer (a decision to stop cannot diverge).
+__device__ __forceinline__ bool bar_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t n) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
 }
@@ -114,6 +131,20 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Tagged words (see DecodeArgs): single-copy atomic 8-byte accesses at GPU
+// scope, so a reader sees a value together with the tag it was written with.
+__device__ __forceinline__ void st_ll(unsigned long long *p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ bool ll_ok(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
 __device__ __forceinline__ void prefetch_l1(const void *p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
@@ -631,6 +662,7 @@ struct Cons {
   Ring rg;
   int mv = 0, mv_total = 0;
   unsigned gen = 0;
+  uint32_t epoch = 0;  // this launch's tag epoch
   // chain-warp state
   float acc = 0.0f, gval = 0.0f, best_v = -INFINITY;
   int best_i = INT_MAX;
@@ -642,6 +674,7 @@ struct Cons {
     cwarp = ctid >> 5;
     lane = tid & 31;
     mv_total = ph[a.n_phase];  // ph is the shared-memory copy
+    epoch = *(volatile const unsigned *)(a.sync + 2);
     own0 = a.own[2 * blockIdx.x];
     cw_base = a.cta_chunk0[blockIdx.x] & 31;  // S.cwb[0] holds the word with this CTA's first chunk
     ring_a = shaddr(S.ring);
@@ -699,9 +732,27 @@ struct Cons {
     if ((TRACE && a.trace) && ctid == 0) stamp(1 + DK_TRW * (int)gen + 8 + i, gtime());
   }
 
-  // All consumers; true when the kernel is being abandoned.
-  __device__ bool grid_sync() {
-    const int q = (int)gen;  // the phase this barrier closes
+  __device__ __forceinline__ uint32_t tag_of(int q) const { return (epoch << 10) | (uint32_t)q; }
+
+  // Bounded poll: false (with the error recorded) once the wait has run out
+  // or another CTA has failed.  `it` counts the caller's polls.
+  __device__ __forceinline__ bool poll_ok(unsigned long long t0, unsigned it) {
+    if ((it & 63u) == 63u && *(volatile int *)a.err) {
+      S.flag[0] = 1;
+      return false;
+    }
+    if (gtime() - t0 > WAIT_NS) {
+      atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
+      S.flag[0] = 1;
+      return false;
+    }
+    return true;
+  }
+
+  // The end of a phase for this CTA (no grid-wide wait: the next phase's
+  // readers poll the tagged words).  True when the kernel is being abandoned.
+  __device__ bool phase_end() {
+    const int q = (int)gen;
     mark(q, 1);
     if ((TRACE && a.trace)) bar_sync(NB_CONS, CONS);  // every accumulator of this phase is final
     if ((TRACE && a.trace) && ctid == 0) {
@@ -709,33 +760,15 @@ struct Cons {
       for (int i = 2; i < 6; i++) stamp(1 + DK_TRW * q + 2 + i, S.prof[i]);
       for (int i = 0; i < 6; i++) S.prof[i] = 0ull;
     }
-    bar_sync(NB_CONS, CONS);
-    if (ctid == 0) {
-      gen++;
-      const unsigned target = gen * gridDim.x;
-      __threadfence();
-      atomicAdd(a.sync, 1u);
-      const unsigned long long t0 = gtime();
-      while (ld_acquire(a.sync) < target) {
-        if (*(volatile int *)a.err) {
-          S.flag[0] = 1;
-          break;
-        }
-        if (gtime() - t0 > WAIT_NS) {
-          atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
-          S.flag[0] = 1;
-          break;
-        }
-      }
-      __threadfence();
-      mark(q, 2);
-    }
-    bar_sync(NB_CONS, CONS);
-    return S.flag[0] != 0;
+    // every consumer is done with this phase's shared buffers; stop together
+    const bool stop = bar_or(NB_CONS, CONS, S.flag[0] != 0);
+    gen++;
+    mark(q, 2);
+    return stop;
   }
 
   // x = dequant_row(token_embd, ids[0]) (model.rs:857-869): kept in the
-  // staging buffer for layer 0 and written to global x for the owned rows.
+  // staging buffer for layer 0 and, for the owned rows, in the residual rows.
   __device__ void embed() {
     const uint32_t id = *a.ids;
     const uint8_t *row = a.embd + (size_t)id * a.embd_row_bytes;
@@ -743,33 +776,46 @@ struct Cons {
     for (int j = ctid; j < a.n_embd; j += CONS) {
       const float v = dequant_elem(a.embd_type, row, j);
       S.u[j] = v;
-      if (j >= o0 && j < o1) {
-        a.x[j] = v;
-        S.xo[j - o0] = v;
-      }
+      if (j >= o0 && j < o1) S.xo[j - o0] = v;
     }
     bar_sync(NB_CONS, CONS);
   }
 
-  __device__ void stage(const float *src, int k) {  // global (this launch's data) -> staging buffer
-    const float4 *s4 = reinterpret_cast<const float4 *>(src);
-    float4 *d4 = reinterpret_cast<float4 *>(S.u);
-    const int n4 = k >> 2;
-    for (int base = 0; base < n4; base += 4 * CONS) {  // every load in flight before the first store
-      float4 r[4];
+  // The previous phase's k-vector (tagged words) -> staging buffer.  Each
+  // consumer thread reads its words coalesced, re-reads the ones whose tag is
+  // not yet `tag` (their writer has not finished), then stores the values.
+  // True (on every consumer) when a wait ran out and the kernel stops.
+  __device__ bool stage_ll(const unsigned long long *src, int k, uint32_t tag) {
+    constexpr int NW = 8;  // words in flight per thread
+    const unsigned long long t0 = gtime();
+    unsigned it = 0;
+    for (int base = 0; base < k; base += NW * CONS) {  // the same trip count on every consumer thread
+      unsigned long long w[NW];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < NW; j++) {
         const int i = base + ctid + j * CONS;
-        if (i < n4) r[j] = __ldcg(s4 + i);
+        w[j] = i < k ? ld_ll(src + i) : ((unsigned long long)tag << 32);
+      }
+      for (;;) {
+        bool all = true;
+#pragma unroll
+        for (int j = 0; j < NW; j++) all = all && ll_ok(w[j], tag);
+        if (all || !poll_ok(t0, ++it)) break;
+#pragma unroll
+        for (int j = 0; j < NW; j++) {
+          const int i = base + ctid + j * CONS;
+          if (!ll_ok(w[j], tag)) w[j] = ld_ll(src + i);
+        }
       }
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < NW; j++) {
         const int i = base + ctid + j * CONS;
-        if (i < n4) d4[i] = r[j];
+        if (i < k) S.u[i] = ll_val(w[j]);
       }
     }
-    bar_sync(NB_CONS, CONS);
+    const bool stop = bar_or(NB_CONS, CONS, S.flag[0] != 0);
     fine(0);
+    return stop;
   }
 
   // The next RMSNorm's weights go to shared memory with asynchronous copies
@@ -905,8 +951,12 @@ struct Cons {
           o = (d & 1) == 0 ? fsub(fmul(val, cs), fmul(partner, sn)) : fadd(fmul(partner, sn), fmul(val, cs));
         }
         if (live) {
-          if (c.role == DR_Q) a.q[r] = o;
-          else a.kcache[(((size_t)c.layer * a.n_kv + hd) * a.dh + d) * a.n_ctx + pos] = o;  // K is d-major
+          if (c.role == DR_Q) {
+            st_ll(a.q_ll + r, o, tag_of(5 * c.layer));
+          } else {
+            a.kcache[(((size_t)c.layer * a.n_kv + hd) * a.dh + d) * a.n_ctx + pos] = o;  // K is d-major
+            st_ll(a.kv_ll + r, o, tag_of(5 * c.layer));
+          }
         }
         break;
       }
@@ -914,6 +964,7 @@ struct Cons {
         if (live) {
           const int hd = r / a.dh, d = r - hd * a.dh;
           a.vcache[(((size_t)c.layer * a.n_kv + hd) * a.n_ctx + pos) * a.dh + d] = val;
+          st_ll(a.kv_ll + (size_t)a.n_kv * a.dh + r, val, tag_of(5 * c.layer));
         }
         break;
       case DR_O:
@@ -922,14 +973,15 @@ struct Cons {
           float *xr = S.xo + (r - own0);
           const float nx = fadd(*xr, val);
           *xr = nx;
-          a.x[r] = nx;
+          if (c.role == DR_O) st_ll(a.x_ll + r, nx, tag_of(5 * c.layer + 2));
+          else st_ll(a.x_ll + a.n_embd + r, nx, tag_of(5 * c.layer + 4));
         }
         break;
       case DR_GATE:
         gval = val;
         break;
       case DR_UP:  // model.rs:1111-1115
-        if (live) a.h[r] = fmul(fdiv(gval, fadd(1.0f, expf_lib(-gval))), val);
+        if (live) st_ll(a.h_ll + r, fmul(fdiv(gval, fadd(1.0f, expf_lib(-gval))), val), tag_of(5 * c.layer + 3));
         break;
       case DR_HEAD: {
         if (live) a.logits[r] = val;
@@ -1027,14 +1079,24 @@ struct Cons {
     const int nvw = (dh + 31) / 32;  // value-chain warps
     for (int h = blockIdx.x; h < a.n_head; h += gridDim.x) {
       const int kh = h / group;
-      const size_t kbase = ((size_t)L * a.n_kv + kh) * a.n_ctx * dh;  // K d-major, V position-major
       float *kcur = S.qh + 256, *vcur = S.qh + 512;
-      for (int d = ctid; d < dh; d += CONS) {  // one round trip for q, this step's k and v
-        const float qv = __ldcg(a.q + (size_t)h * dh + d), kv = __ldcg(a.kcache + kbase + (size_t)d * a.n_ctx + pos),
-                    vv = __ldcg(a.vcache + kbase + (size_t)pos * dh + d);
-        S.qh[d] = qv;
-        kcur[d] = kv;
-        vcur[d] = vv;
+      {  // q and this position's k, v: tagged words of the qkv phase
+        const uint32_t tag = tag_of(5 * L);
+        const unsigned long long t0 = gtime();
+        unsigned it = 0;
+        for (int d = ctid; d < dh; d += CONS) {
+          const unsigned long long *pq = a.q_ll + (size_t)h * dh + d, *pk = a.kv_ll + (size_t)kh * dh + d,
+                                   *pv = a.kv_ll + (size_t)(a.n_kv + kh) * dh + d;
+          unsigned long long wq = ld_ll(pq), wk = ld_ll(pk), wv = ld_ll(pv);
+          while (!(ll_ok(wq, tag) && ll_ok(wk, tag) && ll_ok(wv, tag)) && poll_ok(t0, ++it)) {
+            if (!ll_ok(wq, tag)) wq = ld_ll(pq);
+            if (!ll_ok(wk, tag)) wk = ld_ll(pk);
+            if (!ll_ok(wv, tag)) wv = ld_ll(pv);
+          }
+          S.qh[d] = ll_val(wq);
+          kcur[d] = ll_val(wk);
+          vcur[d] = ll_val(wv);
+        }
       }
       bar_sync(NB_CONS, CONS);
       if (h == (int)blockIdx.x) fine(0);
@@ -1137,7 +1199,7 @@ struct Cons {
         c0 = c1;
       }
       bar_sync(NB_CONS, CONS);
-      if (vw && ctid < dh) a.att[(size_t)h * dh + ctid] = fmul(vacc, S.red[33]);
+      if (vw && ctid < dh) st_ll(a.att_ll + (size_t)h * dh + ctid, fmul(vacc, S.red[33]), tag_of(5 * L + 1));
       bar_sync(NB_CONS, CONS);
       if (tp && ctid == 0) pacc(5, clock64() - c0);  // profile: output
     }
@@ -1187,8 +1249,8 @@ struct Cons {
           *a.step += 1;
           *a.pos += 1;
         }
-        a.sync[0] = 0u;
         a.sync[1] = 0u;
+        a.sync[2] = epoch + 1u > (1u << 22) - 1u ? 1u : epoch + 1u;  // every CTA read the epoch at its start
         __threadfence();
       }
     }
@@ -1211,19 +1273,18 @@ struct Cons {
         if (kind == 2) prefetch_norm(a.layers[L].ffn_norm, a.n_embd);  // the qkv norm is done with the buffer
         if (kind == 4) prefetch_norm(L + 1 < a.n_layer ? a.layers[L + 1].attn_norm : a.out_norm, a.n_embd);
         const bool norm = kind == 0 || kind == 3 || kind == 5;
-        const float *src = kind == 2 ? a.att : kind == 4 ? a.h : a.x;
+        // the previous phase's output: residual after down (qkv, head), attention
+        // output (o), residual after o (gate+up), SwiGLU output (down)
+        const unsigned long long *src = kind == 2 ? a.att_ll : kind == 4 ? a.h_ll : kind == 3 ? a.x_ll : a.x_ll + a.n_embd;
         const int k = kind == 2 ? qdim : kind == 4 ? a.n_ff : a.n_embd;
-        if (norm) {
-          if (q > 0) stage(src, k);  // layer 0's input was staged by embed()
-          norm_q8(k);
-        } else {
-          quant(src, k, false, 1.0f, true);  // attention output / SwiGLU: straight from L2
-        }
+        if (q > 0 && stage_ll(src, k, tag_of(q - 1))) return;  // layer 0's input was staged by embed()
+        if (norm) norm_q8(k);
+        else quant(nullptr, k, false, 1.0f, false);
         mark(q, 0);
         run_mv(kind == 5 ? 4 * a.n_layer : 4 * L + (kind == 0 ? 0 : kind - 1));
       }
       if (kind == 5) break;
-      if (grid_sync()) return;
+      if (phase_end()) return;
     }
     finish();
   }
@@ -1273,6 +1334,16 @@ size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh, int 
   if (dh <= 0 || dh > 256 || dh % 4 != 0 || DK_SLOT / (dh * 4) < 1) return 0;
   const Layout L = dk_layout(n_embd, n_ff, qdim, n_ctx, n_layer);
   return L.total <= 227 * 1024 ? L.total : 0;
+}
+
+int decode_grid_for(const std::vector<DecLayer> &layers, const DevTensor &out, int sms) {
+  long units = sms;
+  auto lim = [&](int rows) { units = std::min<long>(units, rows / 2); };  // whole row pairs per CTA
+  for (const DecLayer &L : layers) {
+    lim(L.q.rows); lim(L.k.rows); lim(L.v.rows); lim(L.o.rows); lim(L.gate.rows); lim(L.down.rows);
+  }
+  lim(out.rows);
+  return (int)std::max<long>(1, units);
 }
 
 int decode_grid() {
@@ -1472,6 +1543,10 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
   if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv || 2 * ((n_embd / 2 + grid - 1) / grid) > DK_XO ||
       n_ctx % 4) {  // K chunks copy whole groups of 4 positions
     why = "unsupported dimensions";
+    return false;
+  }
+  if (decode_grid_for(layers, out, grid) < grid) {  // the tagged hand-off needs rows of every matrix on every CTA
+    why = "more CTAs than row pairs of some matrix";
     return false;
   }
   const int nl = (int)layers.size();

@@ -68,8 +68,17 @@ struct DecodeArgs {
   int n_layer, n_embd, n_ff, n_head, n_kv, dh, half, n_ctx, n_vocab;
   float eps, scale;
   const float *rope_cos, *rope_sin;
-  float *kcache, *vcache;             // [L][n_kv][n_ctx][dh]
-  float *x, *q, *att, *h, *logits;    // activations
+  float *kcache, *vcache;             // K [L][n_kv][dh][n_ctx] (d-major), V [L][n_kv][n_ctx][dh]
+  float *logits;
+  // Vectors passed between CTAs, one 8-byte word per element: the f32 value
+  // in the low half, in the high half the tag (epoch << 10 | phase) of the
+  // phase that wrote it.  A reader polls until every word it needs carries
+  // the previous phase's tag, so no grid barrier separates the phases.
+  unsigned long long *x_ll;           // [2][n_embd] residual after o (0) and after down (1)
+  unsigned long long *att_ll;         // [n_head * dh] attention output
+  unsigned long long *h_ll;           // [n_ff] SwiGLU output
+  unsigned long long *q_ll;           // [n_head * dh] roped q
+  unsigned long long *kv_ll;          // [2][n_kv * dh] this position's roped k (0) and v (1)
   uint32_t *ids, *tok, *hist;
   int *pos, *step;
   const DChunk *chunks;
@@ -78,7 +87,7 @@ struct DecodeArgs {
   int n_phase;                        // 4 * n_layer + 1
   const int *own;                     // [grid][2] rows of x written by this CTA
   const uint32_t *cwbits;             // bit per chunk: which chain warp sums it
-  unsigned *sync;                     // [0] grid barrier arrivals, [1] finished CTAs
+  unsigned *sync;                     // [1] finished CTAs, [2] launch epoch (>= 1; the last CTA advances it)
   int *err;                           // 0 or a PK_ERR_* code
   float *cand_v;
   int *cand_i;                        // [grid]
@@ -98,6 +107,10 @@ struct DecodePlan {
 // false (with the reason) when this model cannot use the persistent kernel.
 bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out, int n_embd, int n_ff, int n_head,
                        int n_kv, int dh, int n_ctx, int grid, DecodePlan &plan, std::string &why);
+
+// Largest grid for which every CTA owns rows of every matrix (the tagged
+// phase hand-off relies on it), at most `sms`.
+int decode_grid_for(const std::vector<DecLayer> &layers, const DevTensor &out, int sms);
 
 // Shared memory the kernel needs for this model (0 if it does not fit).
 size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh, int n_layer);

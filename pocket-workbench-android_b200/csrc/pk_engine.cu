@@ -343,7 +343,7 @@ int Engine::setup_decode() {
     const LayerDev &L = layers_[i];
     dl[i] = DecLayer{L.q, L.k, L.v, L.o, L.gate, L.up, L.down, L.attn_norm, L.ffn_norm};
   }
-  const int grid = decode_grid();
+  const int grid = decode_grid_for(dl, output_, decode_grid());
   if (!build_decode_plan(dl, output_, c.n_embd, c.n_ff, c.n_head, c.n_head_kv, c.head_dim, n_ctx_, grid, plan_,
                          decode_why_))
     return PK_OK;
@@ -376,7 +376,9 @@ int Engine::setup_decode() {
                n_ph = plan_.phase0.size() * 4, n_own = plan_.own.size() * 4, n_ly = dl.size() * sizeof(DecLayer),
                n_cw = plan_.cwbits.size() * 4,
                n_tr = (size_t)grid * n_trace * 8;
-  const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr, n_cw};
+  const size_t qdim = (size_t)c.n_head * c.head_dim, kdim = (size_t)c.n_head_kv * c.head_dim;
+  const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr, n_cw,
+                                     2 * (size_t)c.n_embd * 8, qdim * 8, (size_t)c.n_ff * 8, qdim * 8, 2 * kdim * 8};
   size_t total = 0;
   for (size_t z : sizes) total += a256(z);
   PK_CK(cudaMalloc((void **)&d_decode_, total));
@@ -397,12 +399,17 @@ int Engine::setup_decode() {
   int *ci = (int *)take();
   d_trace_ = (unsigned long long *)take();
   uint32_t *cwb = (uint32_t *)take();
+  unsigned long long *x_ll = (unsigned long long *)take(), *att_ll = (unsigned long long *)take(),
+                     *h_ll = (unsigned long long *)take(), *q_ll = (unsigned long long *)take(),
+                     *kv_ll = (unsigned long long *)take();
   PK_CK(cudaMemcpyAsync(chunks, plan_.chunks.data(), n_ch, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(c0, plan_.cta_chunk0.data(), n_c0, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(ph, plan_.phase0.data(), n_ph, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(own, plan_.own.data(), n_own, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(layers, dl.data(), n_ly, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(cwb, plan_.cwbits.data(), n_cw, cudaMemcpyHostToDevice, st_));
+  const unsigned epoch0 = 1;  // tags of zeroed words (epoch 0) never match
+  PK_CK(cudaMemcpyAsync(d_sync_ + 2, &epoch0, 4, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaStreamSynchronize(st_));
   DecodeArgs &a = dargs_;
   a = DecodeArgs{};
@@ -418,7 +425,8 @@ int Engine::setup_decode() {
   a.scale = 1.0f / sqrtf((float)c.head_dim);
   a.rope_cos = d_rope_cos_; a.rope_sin = d_rope_sin_;
   a.kcache = d_kcache_; a.vcache = d_vcache_;
-  a.x = x_; a.q = q_; a.att = attn_; a.h = h_; a.logits = logits_;
+  a.logits = logits_;
+  a.x_ll = x_ll; a.att_ll = att_ll; a.h_ll = h_ll; a.q_ll = q_ll; a.kv_ll = kv_ll;
   a.ids = d_ids_; a.tok = d_tok_; a.hist = d_hist_; a.pos = d_pos_; a.step = d_step_;
   a.chunks = chunks; a.cta_chunk0 = c0; a.phase0 = ph; a.n_phase = plan_.n_phase; a.own = own; a.cwbits = cwb;
   a.sync = d_sync_; a.err = d_err_; a.cand_v = cv; a.cand_i = ci;
@@ -430,17 +438,25 @@ int Engine::setup_decode() {
 }
 
 // After a persistent-kernel launch: a bounded wait that ran out leaves an
-// error code; the barrier counters are reset so the next launch starts clean.
+// error code.  The finish counter is reset and the tag epoch advanced (the
+// stopped launch did not advance it), so words that launch left behind can
+// never match the next launch's tags.
 int Engine::check_decode_error() {
   if (!use_decode_) return PK_OK;
   int err = 0;
   PK_CK(cudaMemcpyAsync(&err, d_err_, 4, cudaMemcpyDeviceToHost, st_));
   PK_CK(cudaStreamSynchronize(st_));
   if (err == 0) return PK_OK;
-  PK_CK(cudaMemsetAsync(d_err_, 0, 4, st_));
-  PK_CK(cudaMemsetAsync(d_sync_, 0, 8, st_));
+  unsigned sync[4] = {0, 0, 0, 0};
+  PK_CK(cudaMemcpyAsync(sync, d_sync_, 16, cudaMemcpyDeviceToHost, st_));
   PK_CK(cudaStreamSynchronize(st_));
-  return set_error(err, "decode kernel: a bounded wait ran out (grid barrier or copy did not complete)");
+  sync[0] = 0;
+  sync[1] = 0;
+  sync[2] = sync[2] + 1 > (1u << 22) - 1 ? 1 : sync[2] + 1;
+  PK_CK(cudaMemsetAsync(d_err_, 0, 4, st_));
+  PK_CK(cudaMemcpyAsync(d_sync_, sync, 16, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  return set_error(err, "decode kernel: a bounded wait ran out (a phase input or a copy did not arrive)");
 }
 
 int Engine::info(pk_model_info *o) const {
