@@ -213,6 +213,13 @@ typedef struct {
 } pk_kernel_stat;
 int pk_decode_profile(pk_engine *eng, pk_kernel_stat *out, int cap, int *n_out);
 
+/* Test hook (no reference counterpart): one persistent decode launch in which
+ * the readers of one phase wait for a tag nothing writes, so every bounded
+ * wait in the kernel runs out.  *status receives the launch's status
+ * (PK_ERR_TIMEOUT expected); the engine stays usable and the sequence is
+ * unchanged.  PK_ERR_UNSUPPORTED when the persistent kernel is not in use. */
+int pk_selftest_bounded_wait(pk_engine *eng, int *status);
+
 /* Records layer-0 intermediates for parity bisection (Engine.dbg). */
 int pk_set_debug(pk_engine *eng, int on);
 /* Copies the named layer-0 dump (token-major [b][dim]); returns elements via n_out. */

@@ -419,6 +419,11 @@ int pk_decode_profile(pk_engine *e, pk_kernel_stat *out, int cap, int *n_out) {
   return e->eng.decode_profile(out, cap, n_out);
 }
 
+int pk_selftest_bounded_wait(pk_engine *e, int *status) {
+  if (!e || !status) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.selftest_bounded_wait(status);
+}
+
 int pk_set_debug(pk_engine *e, int on) {
   if (!e) return set_error(PK_ERR_INVALID, "null engine");
   return e->eng.set_debug(on != 0);

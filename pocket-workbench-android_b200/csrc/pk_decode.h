@@ -92,6 +92,7 @@ struct DecodeArgs {
   float *cand_v;
   int *cand_i;                        // [grid]
   int mode;                           // 1: greedy pick + token feedback after the head
+  int poison;                         // > 0 (test hook): phase `poison` waits for a tag no phase writes
   unsigned long long *trace;          // optional [grid][n_trace] globaltimer stamps
   int n_trace;
 };

@@ -831,6 +831,26 @@ int Engine::set_position(int pos) {
   return PK_OK;
 }
 
+// One persistent-kernel launch whose o-phase readers (layer 0) wait for a tag
+// that no phase writes: every CTA's bounded wait runs out, the launch stops
+// with PK_ERR_TIMEOUT in the error word and returns, and the engine recovers
+// (the error path resets the counters and advances the tag epoch).  The
+// launch does not feed a token back, so the sequence is unchanged.
+int Engine::selftest_bounded_wait(int *status) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (!use_decode_) return set_error(PK_ERR_UNSUPPORTED, "the persistent decode kernel is not in use");
+  if (next_pos_ + 1 > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+  h_pos_[0] = next_pos_;
+  PK_CK(cudaMemcpyAsync(d_pos_, h_pos_, sizeof(int), cudaMemcpyHostToDevice, st_));
+  DecodeArgs a = dargs_;
+  a.mode = 0;
+  a.poison = 2;  // phase 2: layer 0's o phase reads the attention output
+  PK_CK(launch_decode(a, plan_.grid, plan_.smem, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  *status = check_decode_error();  // its message stays in pk_last_error()
+  return PK_OK;
+}
+
 int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
   if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
   if (!have_logits_) return set_error(PK_ERR_INVALID, "no logits: run a forward pass with want_logits first");

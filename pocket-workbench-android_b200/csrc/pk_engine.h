@@ -44,6 +44,7 @@ class Engine {
   int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
   int set_position(int pos);
   int decode_profile(pk_kernel_stat *out, int cap, int *n_out);
+  int selftest_bounded_wait(int *status);
   int set_debug(bool on);
   int get_dump(const char *name, float *out, int cap, int *n_out);
 

@@ -35,7 +35,8 @@ SYMBOLS = [
     "pk_pack_weights", "pk_matmul_packed", "pk_backend_new", "pk_backend_free", "pk_backend_selftest",
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
     "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position",
-    "pk_decode_profile", "pk_set_debug", "pk_get_dump", "pk_request_stop", "pk_clear_stop",
+    "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
+    "pk_clear_stop",
 ]
 
 
@@ -107,6 +108,7 @@ def lib():
         "pk_generate": ([P, P, I, C.POINTER(GenOpts), TOKEN_CB, P, P, I, C.POINTER(I), C.POINTER(GenStats)], I),
         "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_position": ([P, I], I),
         "pk_decode_profile": ([P, C.POINTER(KernelStat), I, C.POINTER(I)], I), "pk_set_debug": ([P, I], I),
+        "pk_selftest_bounded_wait": ([P, C.POINTER(I)], I),
         "pk_get_dump": ([P, C.c_char_p, P, I, C.POINTER(I)], I),
         "pk_request_stop": ([], None), "pk_clear_stop": ([], None),
     }
@@ -341,6 +343,13 @@ class Engine:
         _check(lib().pk_decode_profile(self.h, stats, 128, C.byref(n)))
         return [{"name": s.name.decode(), "launches": s.launches, "ms": s.ms, "bytes": s.bytes}
                 for s in stats[: n.value]]
+
+    def selftest_bounded_wait(self) -> int:
+        """One persistent-kernel launch whose bounded waits are made to run out;
+        returns the status that launch produced (PK_ERR_TIMEOUT = 8 expected)."""
+        st = C.c_int()
+        _check(lib().pk_selftest_bounded_wait(self.h, C.byref(st)))
+        return st.value
 
     def set_debug(self, on: bool):
         _check(lib().pk_set_debug(self.h, int(on)))

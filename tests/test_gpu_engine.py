@@ -129,6 +129,29 @@ def test_persistent_kernel_equals_op_sequence(pk, paths, name):
     assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
 
 
+def test_bounded_wait_runs_out_and_engine_recovers(pk, paths):
+    """Failure detection without a GPU fault: one persistent-kernel launch
+    whose phase inputs never arrive (its readers wait for a tag nothing
+    writes) stops with PK_ERR_TIMEOUT inside the wait bound, the context
+    stays usable, and decoding afterwards is bit-identical to a clean engine."""
+    import time
+
+    spec = MODELS["q8down"]
+    prompt = synth.prompt_ids(5, 33, spec.n_vocab)
+    ref, e = pk.Engine(paths["q8down"], n_ctx=256), pk.Engine(paths["q8down"], n_ctx=256)
+    assert e.info["decode_kernels"] == 1  # the persistent kernel is in use
+    for eng in (ref, e):
+        eng.forward(prompt[:32], np.arange(32), False)
+        eng.forward(prompt[32:], [32], True)
+    t0 = time.time()
+    status = e.selftest_bounded_wait()
+    assert status == 8  # PK_ERR_TIMEOUT
+    assert time.time() - t0 < 30.0
+    assert np.array_equal(e.logits().view(np.uint32), ref.logits().view(np.uint32))
+    assert e.decode_steps_device(16) == ref.decode_steps_device(16)
+    assert np.array_equal(e.logits().view(np.uint32), ref.logits().view(np.uint32))
+
+
 def test_prefix_reuse_matches_fresh(pk, paths):
     V = synth.TINY.n_vocab
     base = synth.prompt_ids(1, 96, V).tolist()
