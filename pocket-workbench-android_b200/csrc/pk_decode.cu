@@ -343,6 +343,26 @@ __device__ __forceinline__ float chain_add(float acc, uint32_t p, uint32_t s, in
   return acc;
 }
 
+//   acc + p[0] + p[1] + ... + p[n-1] over contiguous floats (p 16-byte
+// aligned): 128-bit loads, eight terms a batch ahead of the adds.
+__device__ __forceinline__ float chain_add_v(float acc, uint32_t p, int n) {
+  int j = 0;
+  if (n >= 8) {
+    float4 a = sld_v4f(p), b = sld_v4f(p + 16);
+    for (j = 8; j + 8 <= n; j += 8) {
+      const float4 na = sld_v4f(p + 4u * j), nb = sld_v4f(p + 4u * j + 16u);
+      acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
+      acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
+      a = na;
+      b = nb;
+    }
+    acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
+    acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
+  }
+  for (; j < n; j++) acc = fadd(acc, sld_f(p + 4u * j));
+  return acc;
+}
+
 // fma(p[(n-1)s], p[(n-1)s], ... fma(p[0], p[0], acc)): one f32_sum_sq lane.
 __device__ __forceinline__ float chain_sq(float acc, uint32_t p, uint32_t s, int n) {
   int j = 0;
@@ -408,7 +428,8 @@ __device__ __forceinline__ float chain_wv(float acc, uint32_t e, uint32_t v, uin
 // The reference's row dots (quant_int.rs:282-419, lanes::*) add one float
 // term per (sub-)block to the row's accumulator.  An item computes the terms
 // of one staged block (Q8_0, Q4_0) or superblock (Q4_K: 8 terms, Q6_K: 16) of
-// one row and stores them at t_a + i * ts (term i).  Integer dots are exact
+// one row and stores them contiguously at t_a (term i at t_a + 4i; 16-byte
+// aligned for the 8-term items).  Integer dots are exact
 // in any order; every float expression keeps the reference's operand order.
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {  // unsigned bytes of a times signed bytes of b
@@ -417,30 +438,47 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {  // unsigned 
   return d;
 }
 
+// Shared-memory loads and stores are volatile asm, which keeps them in
+// program order: every item issues all its loads first, computes, and stores
+// its terms last, so the loads' latencies overlap instead of adding up.
+
 // lanes::q4_k (quant_int.rs:354-365): term_j = (d*da_j)*sc_j*dot_j - (da_j*dmin)*m_j*sa_j.
-__device__ __forceinline__ void item_q4k(uint32_t w_a, int blk, const DAct &A, uint32_t t_a, uint32_t ts) {
+__device__ __forceinline__ void sst_v4f(uint32_t a, float x, float y, float z, float w) {
+  asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+
+__device__ __forceinline__ void item_q4k(uint32_t w_a, int blk, const DAct &A, uint32_t t_a) {
+  const uint32_t xq = A.q + (uint32_t)blk * 256u, xf = (uint32_t)blk * 32u;
   const uint4 hdr = sld_v4(w_a);
+  uint4 w[8];
+  int4 x[16];
+  float da[8], sa[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) w[i] = sld_v4(w_a + 16 + 16 * i);  // pair p: w[2p] (lo16), w[2p+1]
+#pragma unroll
+  for (int i = 0; i < 16; i++) x[i] = sld_v4i(xq + 16u * i);  // sub-block j: x[2j], x[2j+1]
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    da[j] = sld_f(A.d + xf + 4u * j);
+    sa[j] = sld_f(A.s + xf + 4u * j);
+  }
   const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
   // get_scale_min_k4 (quant.rs:80-86) for all eight sub-blocks, a byte each:
   // the 12 scale bytes are hdr.y | hdr.z | hdr.w.
   const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
   const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
   const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-  const uint32_t xq = A.q + (uint32_t)blk * 256u, xf = (uint32_t)blk * 32u;
+  const uint32_t M = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+  float t[8];
 #pragma unroll
-  for (int p = 0; p < 4; p++) {  // sub-blocks 2p (low nibbles) and 2p + 1 (high nibbles)
-    const uint4 w0 = sld_v4(w_a + 16 + 32 * p), w1 = sld_v4(w_a + 32 + 32 * p);
-    const uint32_t xa = xq + 64u * p;
-    const int4 x0 = sld_v4i(xa), x1 = sld_v4i(xa + 16), x2 = sld_v4i(xa + 32), x3 = sld_v4i(xa + 48);
-    const float da0 = sld_f(A.d + xf + 8u * p), da1 = sld_f(A.d + xf + 8u * p + 4u);
-    const float sa0 = sld_f(A.s + xf + 8u * p), sa1 = sld_f(A.s + xf + 8u * p + 4u);
-    const uint32_t M = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+  for (int p = 0; p < 4; p++) {  // sub-blocks 2p (low nibbles) and 2p + 1 (high nibbles, dotted in place: 16x)
+    const uint4 w0 = w[2 * p], w1 = w[2 * p + 1];
+    const int4 x0 = x[4 * p], x1 = x[4 * p + 1], x2 = x[4 * p + 2], x3 = x[4 * p + 3];
     int d0a = 0, d0b = 0, d1a = 0, d1b = 0;
     d0a = __dp4a((int)(w0.x & M), x0.x, d0a); d0b = __dp4a((int)(w0.y & M), x0.y, d0b);
     d0a = __dp4a((int)(w0.z & M), x0.z, d0a); d0b = __dp4a((int)(w0.w & M), x0.w, d0b);
     d0a = __dp4a((int)(w1.x & M), x1.x, d0a); d0b = __dp4a((int)(w1.y & M), x1.y, d0b);
     d0a = __dp4a((int)(w1.z & M), x1.z, d0a); d0b = __dp4a((int)(w1.w & M), x1.w, d0b);
-    // high nibbles in place: 16 * dot, divided back exactly
     d1a = dp4a_us(w0.x & H, x2.x, d1a); d1b = dp4a_us(w0.y & H, x2.y, d1b);
     d1a = dp4a_us(w0.z & H, x2.z, d1a); d1b = dp4a_us(w0.w & H, x2.w, d1b);
     d1a = dp4a_us(w1.x & H, x3.x, d1a); d1b = dp4a_us(w1.y & H, x3.y, d1b);
@@ -450,47 +488,65 @@ __device__ __forceinline__ void item_q4k(uint32_t w_a, int blk, const DAct &A, u
     const int sh = (2 * p & 3) * 8;
     const float sc0 = (float)((scw >> sh) & 0xFFu), m0 = (float)((mw >> sh) & 0xFFu);
     const float sc1 = (float)((scw >> (sh + 8)) & 0xFFu), m1 = (float)((mw >> (sh + 8)) & 0xFFu);
-    sst_f(t_a + ts * (uint32_t)(2 * p), fsub(fmul(fmul(fmul(d, da0), sc0), (float)dot0), fmul(fmul(fmul(da0, dmin), m0), sa0)));
-    sst_f(t_a + ts * (uint32_t)(2 * p + 1),
-          fsub(fmul(fmul(fmul(d, da1), sc1), (float)dot1), fmul(fmul(fmul(da1, dmin), m1), sa1)));
+    t[2 * p] = fsub(fmul(fmul(fmul(d, da[2 * p]), sc0), (float)dot0), fmul(fmul(fmul(da[2 * p], dmin), m0), sa[2 * p]));
+    t[2 * p + 1] =
+        fsub(fmul(fmul(fmul(d, da[2 * p + 1]), sc1), (float)dot1), fmul(fmul(fmul(da[2 * p + 1], dmin), m1), sa[2 * p + 1]));
   }
+  sst_v4f(t_a, t[0], t[1], t[2], t[3]);
+  sst_v4f(t_a + 16, t[4], t[5], t[6], t[7]);
 }
 
 // lanes::q6_k (quant_int.rs:386-413) for half h of a superblock: per
 // 16-element piece, order (g, s), term = ((d*scale)*da)*dot with
 // dot = sum((q - 32) a), computed as sum(q a) - 32 sum(a).  Term i of the
 // half is the superblock's term 8h + i.
-__device__ __forceinline__ void item_q6k(uint32_t w_a, uint32_t d_a, int blk, int h, const DAct &A, uint32_t t_a,
-                                         uint32_t ts) {
+__device__ __forceinline__ void item_q6k(uint32_t w_a, uint32_t d_a, int blk, int h, const DAct &A, uint32_t t_a) {
   const uint2 scw = sld_v2(w_a + 192 + 8 * h);  // this half's eight scales
-  const float d = f16f(sld_u16(d_a));
-  {
-    const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
+  const uint16_t dbits = sld_u16(d_a);
+  uint4 qa[2], qb[2], qh[2];
+  int4 x[8];
+  float da[4];
+  int s16[8];
 #pragma unroll
-    for (int g = 0; g < 2; g++) {
-      const uint4 qa = sld_v4(w_a + h * 64 + g * 16), qb = sld_v4(w_a + h * 64 + 32 + g * 16),
-                  qh = sld_v4(w_a + 128 + h * 32 + g * 16);
+  for (int g = 0; g < 2; g++) {
+    qa[g] = sld_v4(w_a + h * 64 + g * 16);
+    qb[g] = sld_v4(w_a + h * 64 + 32 + g * 16);
+    qh[g] = sld_v4(w_a + 128 + h * 32 + g * 16);
+  }
 #pragma unroll
-      for (int s = 0; s < 4; s++) {
-        const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);  // activation block
-        const int4 x = sld_v4i(A.q + ab * 32u + g * 16);
-        const float da = sld_f(A.d + ab * 4u);
-        const int s16 = sld_i(A.s16 + (ab * 2u + g) * 4u);
-        int pa = 0, pb = 0;
+  for (int s = 0; s < 4; s++) {
+    const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);  // activation block
+    x[2 * s] = sld_v4i(A.q + ab * 32u);
+    x[2 * s + 1] = sld_v4i(A.q + ab * 32u + 16u);
+    da[s] = sld_f(A.d + ab * 4u);
+    const uint2 hs = sld_v2(A.s16 + ab * 8u);
+    s16[2 * s] = (int)hs.x;
+    s16[2 * s + 1] = (int)hs.y;
+  }
+  const float d = f16f(dbits);
+  const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
+  float t[8];
 #pragma unroll
-        for (int w = 0; w < 4; w++) {  // quant_int.rs:386-394 unpacking, four bytes at a time (0..63)
-          const uint32_t lo = word_of(s & 1 ? qb : qa, w), hh = word_of(qh, w);
-          const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) | ((s == 0 ? hh << 4 : s == 1 ? hh << 2 : s == 2 ? hh : hh >> 2) & 0x30303030u);
-          const int xw = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
-          if (w & 1) pb = __dp4a((int)q, xw, pb);
-          else pa = __dp4a((int)q, xw, pa);
-        }
-        const int dot = pa + pb - 32 * s16;
-        const float scale = (float)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s)));
-        sst_f(t_a + ts * (uint32_t)(g * 4 + s), fmul(fmul(fmul(d, scale), da), (float)dot));
+  for (int g = 0; g < 2; g++) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      const int4 xs = x[2 * s + g];
+      int pa = 0, pb = 0;
+#pragma unroll
+      for (int w = 0; w < 4; w++) {  // quant_int.rs:386-394 unpacking, four bytes at a time (0..63)
+        const uint32_t lo = word_of(s & 1 ? qb[g] : qa[g], w), hh = word_of(qh[g], w);
+        const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) | ((s == 0 ? hh << 4 : s == 1 ? hh << 2 : s == 2 ? hh : hh >> 2) & 0x30303030u);
+        const int xw = w == 0 ? xs.x : w == 1 ? xs.y : w == 2 ? xs.z : xs.w;
+        if (w & 1) pb = __dp4a((int)q, xw, pb);
+        else pa = __dp4a((int)q, xw, pa);
       }
+      const int dot = pa + pb - 32 * s16[2 * s + g];
+      const float scale = (float)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s)));
+      t[g * 4 + s] = fmul(fmul(fmul(d, scale), da[s]), (float)dot);
     }
   }
+  sst_v4f(t_a, t[0], t[1], t[2], t[3]);
+  sst_v4f(t_a + 16, t[4], t[5], t[6], t[7]);
 }
 
 // lanes::q8_0 (quant_int.rs:291-296): term = (d*da)*dot.
@@ -911,15 +967,15 @@ struct Cons {
     for (; t < items; t += TERM_T) {
       const int jb = j / IPB;  // block or superblock within the staged row
       const uint32_t w_a = sl + (uint32_t)r * pitch + (uint32_t)(jb * QB);
-      const uint32_t t_a = Tb + 4u * (uint32_t)(j * TPI * rs + r), ts = 4u * (uint32_t)rs;
+      const uint32_t t_a = Tb + 4u * (uint32_t)(r * rs + j * TPI);  // [row][term], rs: the row pitch
       uint32_t d_a = 0u;
       if (T != T_Q4_K)
         d_a = sl + c.d_off + 2u * (uint32_t)jb +
               (uint32_t)(c.full ? (d0 & 15) + (size_t)r * c.d_stride
                                 : (size_t)r * c.d_len + ((d0 + (size_t)r * c.d_stride) & 15));
       const int blk = c.b0 + jb;
-      if (T == T_Q4_K) item_q4k(w_a, blk, act_a, t_a, ts);
-      else if (T == T_Q6_K) item_q6k(w_a, d_a, blk, j & 1, act_a, t_a, ts);
+      if (T == T_Q4_K) item_q4k(w_a, blk, act_a, t_a);
+      else if (T == T_Q6_K) item_q6k(w_a, d_a, blk, j & 1, act_a, t_a);
       else if (T == T_Q8_0) item_q80(w_a, d_a, blk, act_a, t_a);
       else item_q40(w_a, d_a, blk, act_a, t_a);
       r += dr;
@@ -1059,7 +1115,7 @@ struct Cons {
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
           if (c.flags & DF_FIRST) acc = 0.0f;
-          if (lane < c.rows) acc = chain_add(acc, Tb + 4u * lane, 4u * (uint32_t)c.rs, c.nt);
+          if (lane < c.rows) acc = chain_add_v(acc, Tb + 16u * (uint32_t)(lane * (c.rs >> 2)), c.nt);
           __syncwarp();
           if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cwarp, NB_PAIR);  // the term buffer is free again
           if (c.flags & DF_LAST) epilogue(c);
@@ -1398,6 +1454,12 @@ TypeGeo type_geo(int t) {
 }
 
 size_t up16h(size_t x) { return (x + 15) & ~(size_t)15; }
+// Floats between rows of a term buffer: at least nt, an odd multiple of 4
+// (rows start on distinct 16-byte bank groups: conflict-free 128-bit accesses).
+int term_pitch(int nt) {
+  const int q = (nt + 3) / 4;
+  return 4 * (q | 1);
+}
 
 // [a, b) of n items split into `parts` near-equal pieces on multiples of 2.
 void split2(int n, int parts, int i, int &a, int &b) {
@@ -1424,7 +1486,7 @@ struct Builder {
     c.layer = layer;
     c.row0 = r;
     c.rows = (uint16_t)rows;
-    c.rs = (uint16_t)(rows | 1);
+    c.rs = (uint16_t)term_pitch((b1 - b0) * g.gpb * g.tpg);
     c.b0 = b0;
     c.b1 = b1;
     c.full = full ? 1 : 0;
@@ -1475,7 +1537,7 @@ struct Builder {
   }
   static bool full_fits(const Mode &m, int rg) {
     const size_t bytes = rg * m.row_q + (m.g.has_d ? up16h(15 + rg * m.row_d) : 0);
-    return bytes <= (size_t)DK_SLOT && (size_t)(rg | 1) * m.terms_row <= (size_t)DK_TS;
+    return bytes <= (size_t)DK_SLOT && (size_t)rg * term_pitch((int)m.terms_row) <= (size_t)DK_TS;
   }
 
   bool rows(const DevTensor &W, const DevTensor *W2, int r0, int r1, uint8_t role, uint8_t role2, int layer) {
@@ -1507,7 +1569,7 @@ struct Builder {
           int nbmax = 0;
           for (int nb = m.nblk; nb >= 1; nb--) {
             const size_t bytes = (size_t)R * (nb * (size_t)m.g.qb + 16 + (m.g.has_d ? up16h((size_t)nb * 2 + 15) : 0));
-            if (bytes <= (size_t)DK_SLOT && (size_t)(R | 1) * nb * m.g.gpb * m.g.tpg <= (size_t)DK_TS) {
+            if (bytes <= (size_t)DK_SLOT && (size_t)R * term_pitch(nb * m.g.gpb * m.g.tpg) <= (size_t)DK_TS) {
               nbmax = nb;
               break;
             }

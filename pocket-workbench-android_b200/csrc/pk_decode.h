@@ -44,7 +44,7 @@ struct DChunk {
   uint32_t q_len;     // bytes per q copy
   uint32_t d_len;     // bytes per d copy
   uint32_t d_off;     // slot offset of the scale area
-  uint16_t rows, rs;  // rows; term-buffer row stride (odd)
+  uint16_t rows, rs;  // rows; term-buffer row pitch in floats (terms of a row contiguous; an odd multiple of 4)
   uint8_t type, role, full, flags;
   int row0, b0, b1, layer;
   uint8_t cw;          // chain warp that sums these rows
