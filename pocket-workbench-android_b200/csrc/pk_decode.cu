@@ -56,7 +56,12 @@ constexpr int TERM_T = DK_THREADS - 32 - 32 * DK_CHAINS;     // term threads (wa
 // and ONE chain warp, so generations cannot mix); the value-chain warps.
 constexpr int NB_CONS = 1, NB_FULLT = 2, NB_EMPTYT = 2 + DK_NB * DK_CHAINS, NB_V = 2 + 2 * DK_NB * DK_CHAINS;
 static_assert(NB_V < 16, "named barrier ids");
-constexpr int NB_PAIR = TERM_T + 32;                         // term threads + one chain warp
+// The term warps form two groups that take alternate chunks (chunk mv: group
+// mv & 1), so two chunks' items are in flight at once.
+constexpr int TG0 = 32 * ((TERM_T / 32 + 1) / 2), TG1 = TERM_T - TG0;  // threads per group
+static_assert(TG1 > 0 && TG0 % 32 == 0 && TG1 % 32 == 0, "two whole-warp term groups");
+// A term-buffer barrier's participants: the chunk's group and one chain warp.
+__host__ __device__ constexpr int nb_pair(int mv) { return ((mv & 1) ? TG1 : TG0) + 32; }
 constexpr unsigned long long WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -955,16 +960,16 @@ struct Cons {
   // the weights of different rows (staged row pitches are odd multiples of
   // 16 bytes: conflict-free 16-byte loads).
   template <int T>
-  __device__ void terms(const DChunk &c, uint32_t sl, uint32_t Tb) {
+  __device__ void terms(const DChunk &c, uint32_t sl, uint32_t Tb, int gt, int ng) {  // thread gt of a group of ng
     // terms per item; Q6_K items are half superblocks (j = 2 superblock + half)
     constexpr int TPI = T == T_Q4_K ? 8 : (T == T_Q6_K ? 8 : 1), IPB = T == T_Q6_K ? 2 : 1;
     constexpr int QB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 208 : (T == T_Q8_0 ? 32 : 16));
     const int R = c.rows, items = R * (c.b1 - c.b0) * IPB, rs = c.rs;
     const uint32_t pitch = c.full ? c.q_stride : c.q_len + 16u * c.qpad;
     const uintptr_t d0 = (uintptr_t)c.d;
-    const int dr = TERM_T % R, dj = TERM_T / R;
-    int t = tid - 32 - 32 * DK_CHAINS, r = t % R, j = t / R;
-    for (; t < items; t += TERM_T) {
+    const int dr = ng % R, dj = ng / R;
+    int t = gt, r = t % R, j = t / R;
+    for (; t < items; t += ng) {
       const int jb = j / IPB;  // block or superblock within the staged row
       const uint32_t w_a = sl + (uint32_t)r * pitch + (uint32_t)(jb * QB);
       const uint32_t t_a = Tb + 4u * (uint32_t)(r * rs + j * TPI);  // [row][term], rs: the row pitch
@@ -1068,35 +1073,43 @@ struct Cons {
     return (int)((S.cwb[bi >> 5] >> (bi & 31)) & 1u);
   }
 
+  // Barrier protocol per term buffer b and chain warp w: FULLT(b, w) and
+  // EMPTYT(b, w) are used by one chunk at a time (chunk mv uses buffer
+  // mv % DK_NB, and its group waits for the release of chunk mv - DK_NB before
+  // it writes), and each use has exactly the chunk's group and its chain warp,
+  // nb_pair(mv) threads.
   __device__ void run_mv(int p) {
     const bool chain = cwarp < DK_CHAINS;
+    const int ti = tid - 32 - 32 * DK_CHAINS;           // term thread index
+    const int grp = ti < TG0 ? 0 : 1, gt = grp ? ti - TG0 : ti;
     for (int ci = ph[p]; ci < ph[p + 1]; ci++) {
       const int buf = mv % DK_NB;
       const uint32_t Tb = u_a + 4u * (uint32_t)(buf * DK_TS);
-      if (!chain) {
+      if (!chain && (mv & 1) == grp) {
         const bool tp = (TRACE && a.trace) && ctid == 32 * DK_CHAINS;
         long long c0 = tp ? clock64() : 0;
-        if (mv >= DK_NB) bar_sync(NB_EMPTYT + buf * DK_CHAINS + owner(ci - DK_NB), NB_PAIR);
+        if (mv >= DK_NB) bar_sync(NB_EMPTYT + buf * DK_CHAINS + owner(ci - DK_NB), nb_pair(mv));
         if (tp) pacc(2, clock64() - c0);
         wait_full();
         if (tp) c0 = clock64();
         const DChunk c = load_desc(desc_a + rg.slot * (uint32_t)sizeof(DChunk));
         const uint32_t sl = ring_a + rg.slot * (uint32_t)DK_SLOT;
+        const int ng = grp ? TG1 : TG0;
         switch (c.type) {
-          case T_Q4_K: terms<T_Q4_K>(c, sl, Tb); break;
-          case T_Q6_K: terms<T_Q6_K>(c, sl, Tb); break;
-          case T_Q8_0: terms<T_Q8_0>(c, sl, Tb); break;
-          default: terms<T_Q4_0>(c, sl, Tb); break;
+          case T_Q4_K: terms<T_Q4_K>(c, sl, Tb, gt, ng); break;
+          case T_Q6_K: terms<T_Q6_K>(c, sl, Tb, gt, ng); break;
+          case T_Q8_0: terms<T_Q8_0>(c, sl, Tb, gt, ng); break;
+          default: terms<T_Q4_0>(c, sl, Tb, gt, ng); break;
         }
         if (tp) pacc(3, clock64() - c0);
-        bar_arrive(NB_FULLT + buf * DK_CHAINS + owner(ci), NB_PAIR);
-      } else {
+        bar_arrive(NB_FULLT + buf * DK_CHAINS + owner(ci), nb_pair(mv));
+      } else if (chain) {
         // Ownership comes from the plan's bit list (the descriptor may only be
         // read by the owner, before it hands the slot back).
         const bool tp = (TRACE && a.trace) && ctid == 0;
         if (owner(ci) == cwarp) {
           long long c0 = tp ? clock64() : 0;
-          bar_sync(NB_FULLT + buf * DK_CHAINS + cwarp, NB_PAIR);
+          bar_sync(NB_FULLT + buf * DK_CHAINS + cwarp, nb_pair(mv));
           if (ci == ph[p]) fine(3);  // first chunk's terms are in
           if (tp) {
             const long long c1 = clock64();
@@ -1117,7 +1130,8 @@ struct Cons {
           if (c.flags & DF_FIRST) acc = 0.0f;
           if (lane < c.rows) acc = chain_add_v(acc, Tb + 16u * (uint32_t)(lane * (c.rs >> 2)), c.nt);
           __syncwarp();
-          if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cwarp, NB_PAIR);  // the term buffer is free again
+          // the term buffer is free again, for chunk mv + DK_NB and its group
+          if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cwarp, nb_pair(mv + DK_NB));
           if (c.flags & DF_LAST) epilogue(c);
           if (tp) pacc(5, clock64() - c0);
           if (ci == ph[p]) fine(4);  // first chunk chained
