@@ -348,24 +348,31 @@ __device__ __forceinline__ float chain_add(float acc, uint32_t p, uint32_t s, in
   return acc;
 }
 
-//   acc + p[0] + p[1] + ... + p[n-1] over contiguous floats (p 16-byte
-// aligned): 128-bit loads, eight terms a batch ahead of the adds.
-__device__ __forceinline__ float chain_add_v(float acc, uint32_t p, int n) {
-  int j = 0;
-  if (n >= 8) {
-    float4 a = sld_v4f(p), b = sld_v4f(p + 16);
-    for (j = 8; j + 8 <= n; j += 8) {
-      const float4 na = sld_v4f(p + 4u * j), nb = sld_v4f(p + 4u * j + 16u);
-      acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
-      acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
-      a = na;
-      b = nb;
-    }
-    acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
-    acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
-  }
-  for (; j < n; j++) acc = fadd(acc, sld_f(p + 4u * j));
+__device__ __forceinline__ float add8(float acc, const float4 a, const float4 b) {
+  acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
+  acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
   return acc;
+}
+
+//   acc + p[0] + p[1] + ... + p[n-1] over contiguous floats (p 16-byte
+// aligned, readable up to the next multiple of eight): 128-bit loads a batch
+// of eight ahead of the adds, no scalar tail.  The last batch's slots past n
+// add +0.0, an exact identity here: the sum starts at +0.0 and, rounding to
+// nearest, never becomes -0.0.
+__device__ __forceinline__ float chain_add_v(float acc, uint32_t p, int n) {
+  const int nb = (n + 7) >> 3;
+  if (nb == 0) return acc;
+  float4 a = sld_v4f(p), b = sld_v4f(p + 16);
+  for (int i = 1; i < nb; i++) {
+    const float4 na = sld_v4f(p + 32u * i), nb8 = sld_v4f(p + 32u * i + 16u);
+    acc = add8(acc, a, b);
+    a = na;
+    b = nb8;
+  }
+  const int r = n - 8 * (nb - 1);  // live slots of the last batch, 1..8
+  const float4 za = make_float4(a.x, r > 1 ? a.y : 0.0f, r > 2 ? a.z : 0.0f, r > 3 ? a.w : 0.0f);
+  const float4 zb = make_float4(r > 4 ? b.x : 0.0f, r > 5 ? b.y : 0.0f, r > 6 ? b.z : 0.0f, r > 7 ? b.w : 0.0f);
+  return add8(acc, za, zb);
 }
 
 // fma(p[(n-1)s], p[(n-1)s], ... fma(p[0], p[0], acc)): one f32_sum_sq lane.
@@ -1468,11 +1475,12 @@ TypeGeo type_geo(int t) {
 }
 
 size_t up16h(size_t x) { return (x + 15) & ~(size_t)15; }
-// Floats between rows of a term buffer: at least nt, an odd multiple of 4
+// Floats between rows of a term buffer: at least nt rounded up to a multiple
+// of 8 (the row chains read whole batches of eight), and an odd multiple of 4
 // (rows start on distinct 16-byte bank groups: conflict-free 128-bit accesses).
 int term_pitch(int nt) {
-  const int q = (nt + 3) / 4;
-  return 4 * (q | 1);
+  const int q = ((nt + 7) / 8) * 2;
+  return 4 * (q + 1);
 }
 
 // [a, b) of n items split into `parts` near-equal pieces on multiples of 2.
