@@ -217,6 +217,12 @@ __device__ float block_max(float v, float *red) {
   return red[32];
 }
 
+template <typename K>
+static cudaError_t set_smem(K kernel, size_t smem) {
+  if (smem > 48 * 1024) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return cudaSuccess;
+}
+
 // ------------------------------------------------------------ Q8 quantiser
 __global__ void k_q8(const float *__restrict__ x, long xs_e, long xs_l, int k, int b, Q8Dev act) {
   pdl_trigger();
@@ -236,19 +242,6 @@ cudaError_t launch_q8(const float *x, long xs_e, long xs_l, int k, int b, Q8Dev 
   int grid = (int)std::min<long>((warps * 32 + 255) / 256, (long)num_sms() * 8);
   if (grid < 1) grid = 1;
   return launch(k_q8, dim3(grid), dim3(256), 0, st, x, xs_e, xs_l, k, b, act);
-}
-
-// Sum of squares in the reference's b > 1 order (model.rs:813-817): one
-// sequential unfused chain.  Result broadcast through red[32].
-__device__ float sum_sq_seq(const float *__restrict__ x, int n, float *red) {
-  if (threadIdx.x == 0) {
-    float ss = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < n; i++) ss = fadd(ss, fmul(x[i], x[i]));
-    red[32] = ss;
-  }
-  __syncthreads();
-  return red[32];
 }
 
 // Sum of squares in the reference's b == 1 order (simd.rs:47-64 f32_sum_sq):
@@ -274,20 +267,55 @@ __device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
   return red[32];
 }
 
-// RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.
+// Sum of squares in the reference's b > 1 order (model.rs:813-817), over a
+// row staged in shared memory: one sequential unfused chain, with the squares
+// of the next eight elements formed while the current eight are added.
+// Result broadcast through red[32].
+__device__ float sum_sq_seq_smem(const float *xs, int n, float *red) {
+  if (threadIdx.x == 0) {
+    float ss = 0.0f;
+    int i = 0;
+    if (n >= 8) {
+      float cur[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) cur[u] = fmul(xs[u], xs[u]);
+      for (i = 8; i + 8 <= n; i += 8) {
+        float nxt[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) nxt[u] = fmul(xs[i + u], xs[i + u]);
+#pragma unroll
+        for (int u = 0; u < 8; u++) ss = fadd(ss, cur[u]);
+#pragma unroll
+        for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) ss = fadd(ss, cur[u]);
+    }
+    for (; i < n; i++) ss = fadd(ss, fmul(xs[i], xs[i]));
+    red[32] = ss;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.  The
+// token's row is staged in shared memory (dynamic, k floats) first.
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn) {
+  extern __shared__ float xs[];
   __shared__ float red[40];
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
   const float *xr = x + (long)bi * k;
-  const float ss = sum_sq_seq(xr, k, red);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = xr[i];
+  __syncthreads();
+  const float ss = sum_sq_seq_smem(xs, k, red);
   const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
   const int nb = k >> 5, lane = threadIdx.x & 31;
   for (int blk = threadIdx.x >> 5; blk < nb; blk += blockDim.x >> 5) {
     const int i = blk * 32 + lane;
-    const float v = fmul(fmul(xr[i], s), nw[i]);
+    const float v = fmul(fmul(xs[i], s), nw[i]);
     if (xn) xn[(long)bi * k + i] = v;
     q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
   }
@@ -295,7 +323,10 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st) {
-  return launch(k_rmsnorm_q8, dim3(b), dim3(256), 0, st, x, nw, eps, k, act, xn);
+  const size_t smem = (size_t)k * 4;
+  cudaError_t e = set_smem(k_rmsnorm_q8, smem);
+  if (e != cudaSuccess) return e;
+  return launch(k_rmsnorm_q8, dim3(b), dim3(256), smem, st, x, nw, eps, k, act, xn);
 }
 
 // ------------------------------------------------------------ matvec core
@@ -450,12 +481,6 @@ static int b1_grid(int tiles, size_t smem) {
   // Resident CTAs per SM bound by the 228 KB shared memory and 2048 threads.
   int per_sm = (int)std::min<size_t>(8, std::max<size_t>(1, (227 * 1024) / std::max<size_t>(smem, 1)));
   return std::max(1, std::min(tiles, num_sms() * per_sm));
-}
-
-template <typename K>
-static cudaError_t set_smem(K kernel, size_t smem) {
-  if (smem > 48 * 1024) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return cudaSuccess;
 }
 
 cudaError_t launch_mv_b1(const DevTensor &w, const B1Src &src, float *out, bool add, cudaStream_t st) {
