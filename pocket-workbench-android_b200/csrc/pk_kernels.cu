@@ -650,12 +650,239 @@ __global__ void __launch_bounds__(L_THREADS) k_mv_lanes(DevTensor W, Q8Dev act, 
   }
 }
 
+// ------------------------------------------------- multi-lane matvec, tensor cores
+// b > 1 (prefill chunks, Pool::matmul with several lanes).  The reference adds
+// one float term per (row, lane, sub-block) in sub-block order
+// (quant_int.rs:282-419).  Each sub-block's integer dot is one element of an
+// int8 mma.sync tile (m16n8k32 per 32-element sub-block, m16n8k16 per
+// 16-element Q6_K piece), exact in int32 with a zero accumulator; every thread
+// turns its four tile elements into the reference's float terms (operand
+// order as in the scalar path) and adds them to four register accumulators,
+// sub-block after sub-block.  CTA: 4 warps, tile 16 rows x 32 lanes (warp w
+// takes lanes 8w .. 8w+7); the tile's rows and the lanes' activation scales
+// are staged in shared memory one k-chunk at a time.
+constexpr int MM_WARPS = 4;
+constexpr int MM_ROWS = 16;
+constexpr int MM_LANES = 8 * MM_WARPS;
+constexpr int MM_WBYTES = 40 * 1024;  // staged weight bytes per chunk (at most)
+
+__device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+__device__ __forceinline__ uint32_t ldg_u32(const int8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+
+template <int T> struct MmGeo;
+template <> struct MmGeo<T_Q4_K> { static constexpr int BE = 256, QB = 144; static constexpr bool D = false; };
+template <> struct MmGeo<T_Q6_K> { static constexpr int BE = 256, QB = 208; static constexpr bool D = true; };
+template <> struct MmGeo<T_Q8_0> { static constexpr int BE = 32, QB = 32; static constexpr bool D = true; };
+template <> struct MmGeo<T_Q4_0> { static constexpr int BE = 32, QB = 16; static constexpr bool D = true; };
+
+// Storage blocks per staged chunk.
+template <int T>
+__host__ __device__ constexpr int mm_chunk_blocks() {
+  return MM_WBYTES / (MM_ROWS * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)));
+}
+
+template <int T>
+__global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act, float *out, long os_row, long os_lane,
+                                                           int add) {
+  using G = MmGeo<T>;
+  constexpr int NBC = mm_chunk_blocks<T>();            // storage blocks per chunk
+  constexpr int SBC = NBC * G::BE / 32;                // 32-element activation blocks per chunk
+  extern __shared__ __align__(16) uint8_t mm_smem[];
+  uint8_t *wq = mm_smem;                                // [16 rows][NBC][QB]
+  float *wd = (float *)(mm_smem + MM_ROWS * NBC * G::QB);  // [16 rows][NBC] (types with a separate d)
+  float2 *as = (float2 *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][SBC] {da, sa}
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int r0 = blockIdx.x * MM_ROWS, nr = min(MM_ROWS, W.rows - r0);
+  const int L0 = blockIdx.y * MM_LANES, nl = min(MM_LANES, act.b - L0);
+  const int k = W.k, nblk = k / G::BE, nb32 = k >> 5;
+  const int lb = L0 + 8 * w + g;                       // lane of this thread's B fragment loads
+  const int lbc = min(lb, act.b - 1);
+  const int lc0 = 8 * w + 2 * t, lc1 = lc0 + 1;         // local lanes of this thread's accumulators
+  const int8_t *aq = act.q + (long)lbc * k;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};             // (row g, lc0), (g, lc1), (g + 8, lc0), (g + 8, lc1)
+  const size_t row_q = (size_t)nblk * G::QB;
+  for (int c0 = 0; c0 < nblk; c0 += NBC) {
+    const int nbc = min(NBC, nblk - c0);
+    __syncthreads();  // the previous chunk is consumed
+    // stage: the tile's rows (16-byte vectors), their scales, the lanes' activation scales
+    const int v16 = nbc * G::QB / 16;
+    for (int i = tid; i < nr * v16; i += 32 * MM_WARPS) {
+      const int r = i / v16, j = i - r * v16;
+      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB) + j);
+      *reinterpret_cast<uint4 *>(wq + (size_t)r * NBC * G::QB + 16 * j) = v;
+    }
+    if (G::D)
+      for (int i = tid; i < nr * nbc; i += 32 * MM_WARPS) {
+        const int r = i / nbc, j = i - r * nbc;
+        wd[r * NBC + j] = f16f(__ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j));
+      }
+    const int s0 = c0 * (G::BE / 32), nsb = nbc * (G::BE / 32);
+    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS) {
+      const int l = i / nsb, j = i - l * nsb;
+      const long o = (long)(L0 + l) * nb32 + s0 + j;
+      as[l * SBC + j] = make_float2(__ldg(act.d + o), (float)__ldg(act.s + o));
+    }
+    __syncthreads();
+    if (8 * w >= nl) continue;  // no lanes for this warp (it still meets every barrier)
+    const uint8_t *qa = wq + (size_t)g * NBC * G::QB, *qb = wq + (size_t)(g + 8) * NBC * G::QB;
+    const float2 *a0s = as + lc0 * SBC, *a1s = as + lc1 * SBC;
+    for (int i = 0; i < nbc; i++) {
+      const int blk = c0 + i;  // storage block
+      if (T == T_Q4_K) {
+        const uint4 ha = *reinterpret_cast<const uint4 *>(qa + i * 144), hb = *reinterpret_cast<const uint4 *>(qb + i * 144);
+        const float da_r = f16f((uint16_t)(ha.x & 0xFFFFu)), dm_r = f16f((uint16_t)(ha.x >> 16));
+        const float db_r = f16f((uint16_t)(hb.x & 0xFFFFu)), dmb_r = f16f((uint16_t)(hb.x >> 16));
+        // get_scale_min_k4 (quant.rs:80-86), a byte per sub-block
+        const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
+        const uint32_t sca_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+        const uint32_t ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+        const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
+        const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+        const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          const uint32_t wa0 = *reinterpret_cast<const uint32_t *>(qa + i * 144 + 16 + 32 * p + 4 * t);
+          const uint32_t wa1 = *reinterpret_cast<const uint32_t *>(qa + i * 144 + 32 + 32 * p + 4 * t);
+          const uint32_t wb0 = *reinterpret_cast<const uint32_t *>(qb + i * 144 + 16 + 32 * p + 4 * t);
+          const uint32_t wb1 = *reinterpret_cast<const uint32_t *>(qb + i * 144 + 32 + 32 * p + 4 * t);
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const int j = 2 * p + h, sb = blk * 8 + j, sl = (i * 8 + j);
+            const uint32_t M = 0x0F0F0F0Fu;
+            const uint32_t x0 = h ? (wa0 >> 4) & M : wa0 & M, x1 = h ? (wb0 >> 4) & M : wb0 & M;
+            const uint32_t x2 = h ? (wa1 >> 4) & M : wa1 & M, x3 = h ? (wb1 >> 4) & M : wb1 & M;
+            int dot[4];
+            mma_k32(dot, x0, x1, x2, x3, ldg_u32(aq + sb * 32 + 4 * t), ldg_u32(aq + sb * 32 + 16 + 4 * t));
+            const float2 a0 = a0s[sl], a1 = a1s[sl];
+            const int sh = (j & 3) * 8;
+            const uint32_t sa_w = j < 4 ? sca_lo : sca_hi, ma_w = j < 4 ? ma_lo : ma_hi;
+            const uint32_t sb_w = j < 4 ? scb_lo : scb_hi, mb_w = j < 4 ? mb_lo : mb_hi;
+            const float sca = (float)((sa_w >> sh) & 0xFFu), mma_ = (float)((ma_w >> sh) & 0xFFu);
+            const float scb = (float)((sb_w >> sh) & 0xFFu), mmb = (float)((mb_w >> sh) & 0xFFu);
+            acc[0] = fadd(acc[0], fsub(fmul(fmul(fmul(da_r, a0.x), sca), (float)dot[0]), fmul(fmul(fmul(a0.x, dm_r), mma_), a0.y)));
+            acc[1] = fadd(acc[1], fsub(fmul(fmul(fmul(da_r, a1.x), sca), (float)dot[1]), fmul(fmul(fmul(a1.x, dm_r), mma_), a1.y)));
+            acc[2] = fadd(acc[2], fsub(fmul(fmul(fmul(db_r, a0.x), scb), (float)dot[2]), fmul(fmul(fmul(a0.x, dmb_r), mmb), a0.y)));
+            acc[3] = fadd(acc[3], fsub(fmul(fmul(fmul(db_r, a1.x), scb), (float)dot[3]), fmul(fmul(fmul(a1.x, dmb_r), mmb), a1.y)));
+          }
+        }
+      } else if (T == T_Q6_K) {
+        const float dra = wd[g * NBC + i], drb = wd[(g + 8) * NBC + i];
+        const uint8_t *ba = qa + i * 208, *bb = qb + i * 208;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const uint2 sa2 = *reinterpret_cast<const uint2 *>(ba + 192 + 8 * h);
+          const uint2 sb2 = *reinterpret_cast<const uint2 *>(bb + 192 + 8 * h);
+          const unsigned long long swa = (unsigned long long)sa2.y << 32 | sa2.x;
+          const unsigned long long swb = (unsigned long long)sb2.y << 32 | sb2.x;
+#pragma unroll
+          for (int g2 = 0; g2 < 2; g2++) {
+            const uint32_t la0 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + g2 * 16 + 4 * t);
+            const uint32_t la1 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + 32 + g2 * 16 + 4 * t);
+            const uint32_t lha = *reinterpret_cast<const uint32_t *>(ba + 128 + h * 32 + g2 * 16 + 4 * t);
+            const uint32_t lb0 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + g2 * 16 + 4 * t);
+            const uint32_t lb1 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + 32 + g2 * 16 + 4 * t);
+            const uint32_t lhb = *reinterpret_cast<const uint32_t *>(bb + 128 + h * 32 + g2 * 16 + 4 * t);
+#pragma unroll
+            for (int s = 0; s < 4; s++) {
+              // quant_int.rs:386-394 unpacking, four bytes at a time, minus 32
+              auto unpack = [&](uint32_t l0w, uint32_t l1w, uint32_t hw) {
+                const uint32_t lo = s & 1 ? l1w : l0w;
+                const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) |
+                                   ((s == 0 ? hw << 4 : s == 1 ? hw << 2 : s == 2 ? hw : hw >> 2) & 0x30303030u);
+                return __vsub4(q, 0x20202020u);
+              };
+              const int sbk = blk * 8 + 4 * h + s;  // activation block
+              int dot[4];
+              mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), ldg_u32(aq + sbk * 32 + g2 * 16 + 4 * t));
+              const float2 a0 = a0s[i * 8 + 4 * h + s], a1 = a1s[i * 8 + 4 * h + s];
+              const float sca = (float)(int8_t)(uint8_t)(swa >> (8 * (g2 + 2 * s)));
+              const float scb = (float)(int8_t)(uint8_t)(swb >> (8 * (g2 + 2 * s)));
+              acc[0] = fadd(acc[0], fmul(fmul(fmul(dra, sca), a0.x), (float)dot[0]));
+              acc[1] = fadd(acc[1], fmul(fmul(fmul(dra, sca), a1.x), (float)dot[1]));
+              acc[2] = fadd(acc[2], fmul(fmul(fmul(drb, scb), a0.x), (float)dot[2]));
+              acc[3] = fadd(acc[3], fmul(fmul(fmul(drb, scb), a1.x), (float)dot[3]));
+            }
+          }
+        }
+      } else {  // Q8_0 / Q4_0: one 32-element block per storage block
+        const float dra = wd[g * NBC + i], drb = wd[(g + 8) * NBC + i];
+        uint32_t x0, x1, x2, x3;
+        if (T == T_Q8_0) {
+          x0 = *reinterpret_cast<const uint32_t *>(qa + i * 32 + 4 * t);
+          x2 = *reinterpret_cast<const uint32_t *>(qa + i * 32 + 16 + 4 * t);
+          x1 = *reinterpret_cast<const uint32_t *>(qb + i * 32 + 4 * t);
+          x3 = *reinterpret_cast<const uint32_t *>(qb + i * 32 + 16 + 4 * t);
+        } else {  // low nibbles = elements 0-15, high = 16-31
+          const uint32_t wa = *reinterpret_cast<const uint32_t *>(qa + i * 16 + 4 * t);
+          const uint32_t wb = *reinterpret_cast<const uint32_t *>(qb + i * 16 + 4 * t);
+          x0 = wa & 0x0F0F0F0Fu;
+          x2 = (wa >> 4) & 0x0F0F0F0Fu;
+          x1 = wb & 0x0F0F0F0Fu;
+          x3 = (wb >> 4) & 0x0F0F0F0Fu;
+        }
+        int dot[4];
+        mma_k32(dot, x0, x1, x2, x3, ldg_u32(aq + blk * 32 + 4 * t), ldg_u32(aq + blk * 32 + 16 + 4 * t));
+        const float2 a0 = a0s[i], a1 = a1s[i];
+        if (T == T_Q8_0) {  // quant_int.rs:291-296
+          acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), (float)dot[0]));
+          acc[1] = fadd(acc[1], fmul(fmul(dra, a1.x), (float)dot[1]));
+          acc[2] = fadd(acc[2], fmul(fmul(drb, a0.x), (float)dot[2]));
+          acc[3] = fadd(acc[3], fmul(fmul(drb, a1.x), (float)dot[3]));
+        } else {  // quant_int.rs:316-323
+          acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), fsub((float)dot[0], fmul(8.0f, a0.y))));
+          acc[1] = fadd(acc[1], fmul(fmul(dra, a1.x), fsub((float)dot[1], fmul(8.0f, a1.y))));
+          acc[2] = fadd(acc[2], fmul(fmul(drb, a0.x), fsub((float)dot[2], fmul(8.0f, a0.y))));
+          acc[3] = fadd(acc[3], fmul(fmul(drb, a1.x), fsub((float)dot[3], fmul(8.0f, a1.y))));
+        }
+      }
+    }
+  }
+  // out = 0.0 + acc (Pool::matmul zero-fills, then adds), or x += that
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int r = g + (e >> 1) * 8, l = (e & 1) ? lc1 : lc0;
+    if (r < nr && l < nl) {
+      float *o = out + (long)(r0 + r) * os_row + (long)(L0 + l) * os_lane;
+      const float v = fadd(0.0f, acc[e]);
+      *o = add ? fadd(*o, v) : v;
+    }
+  }
+}
+
+template <int T>
+static cudaError_t launch_mv_mma_t(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
+                                   cudaStream_t st) {
+  constexpr int NBC = mm_chunk_blocks<T>();
+  const size_t smem = (size_t)MM_ROWS * NBC * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)) +
+                      (size_t)MM_LANES * (NBC * MmGeo<T>::BE / 32) * sizeof(float2);
+  cudaError_t e = set_smem(k_mv_mma<T>, smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((w.rows + MM_ROWS - 1) / MM_ROWS, (act.b + MM_LANES - 1) / MM_LANES);
+  return launch(k_mv_mma<T>, grid, dim3(32 * MM_WARPS), smem, st, w, act, out, os_row, os_lane, add ? 1 : 0);
+}
+
 cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
                             cudaStream_t st) {
   if (!type_is_matvec(w.type) || act.k != w.k || act.b < 1) return cudaErrorInvalidValue;
-  const int tiles = (w.rows + L_RT - 1) / L_RT;
-  const int grid = std::max(1, std::min(tiles, num_sms() * 4));
-  return launch(k_mv_lanes, dim3(grid), dim3(L_THREADS), 0, st, w, act, out, os_row, os_lane, add ? 1 : 0);
+  switch (w.type) {
+    case T_Q4_K: return launch_mv_mma_t<T_Q4_K>(w, act, out, os_row, os_lane, add, st);
+    case T_Q6_K: return launch_mv_mma_t<T_Q6_K>(w, act, out, os_row, os_lane, add, st);
+    case T_Q8_0: return launch_mv_mma_t<T_Q8_0>(w, act, out, os_row, os_lane, add, st);
+    default: return launch_mv_mma_t<T_Q4_0>(w, act, out, os_row, os_lane, add, st);
+  }
 }
 
 // ------------------------------------------------------------ RoPE + KV, SwiGLU
