@@ -668,13 +668,12 @@ constexpr int MM_WBYTES = 40 * 1024;  // staged weight bytes per chunk (at most)
 
 __device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
                : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
@@ -739,7 +738,32 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
     if (8 * w >= nl) continue;  // no lanes for this warp (it still meets every barrier)
     const uint8_t *qa = wq + (size_t)g * NBC * G::QB, *qb = wq + (size_t)(g + 8) * NBC * G::QB;
     const float2 *a0s = as + lc0 * SBC, *a1s = as + lc1 * SBC;
-    for (int i = 0; i < nbc; i++) {
+    // The activation fragments of one group (a K-quant superblock, or eight
+    // Q8_0/Q4_0 blocks: 16 words) are loaded one group ahead of their use.
+    constexpr int GB = G::BE == 256 ? 1 : 8;  // storage blocks per group
+    const int ngrp = (nbc + GB - 1) / GB;
+    auto load_b = [&](int gi, uint32_t (&bw)[16]) {
+      const int8_t *ap = aq + (size_t)(c0 + gi * GB) * G::BE;
+      if (T == T_Q6_K) {
+#pragma unroll
+        for (int e = 0; e < 16; e++) bw[e] = ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t);  // piece (4h+s, g2)
+      } else if (T == T_Q4_K) {
+#pragma unroll
+        for (int e = 0; e < 16; e++) bw[e] = ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t);  // sub-block e/2
+      } else {
+        const int nv = min(GB, nbc - gi * GB);
+#pragma unroll
+        for (int e = 0; e < 16; e++) bw[e] = (e >> 1) < nv ? ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t) : 0u;
+      }
+    };
+    uint32_t bc[16], bn[16];
+    load_b(0, bc);
+    for (int gi = 0; gi < ngrp; gi++) {
+      if (gi + 1 < ngrp) load_b(gi + 1, bn);
+#pragma unroll
+    for (int ig = 0; ig < GB; ig++) {
+      const int i = gi * GB + ig;
+      if (i >= nbc) break;
       const int blk = c0 + i;  // storage block
       if (T == T_Q4_K) {
         const uint4 ha = *reinterpret_cast<const uint4 *>(qa + i * 144), hb = *reinterpret_cast<const uint4 *>(qb + i * 144);
@@ -760,12 +784,12 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
           const uint32_t wb1 = *reinterpret_cast<const uint32_t *>(qb + i * 144 + 32 + 32 * p + 4 * t);
 #pragma unroll
           for (int h = 0; h < 2; h++) {
-            const int j = 2 * p + h, sb = blk * 8 + j, sl = (i * 8 + j);
+            const int j = 2 * p + h, sl = i * 8 + j;
             const uint32_t M = 0x0F0F0F0Fu;
             const uint32_t x0 = h ? (wa0 >> 4) & M : wa0 & M, x1 = h ? (wb0 >> 4) & M : wb0 & M;
             const uint32_t x2 = h ? (wa1 >> 4) & M : wa1 & M, x3 = h ? (wb1 >> 4) & M : wb1 & M;
             int dot[4];
-            mma_k32(dot, x0, x1, x2, x3, ldg_u32(aq + sb * 32 + 4 * t), ldg_u32(aq + sb * 32 + 16 + 4 * t));
+            mma_k32(dot, x0, x1, x2, x3, bc[2 * j], bc[2 * j + 1]);
             const float2 a0 = a0s[sl], a1 = a1s[sl];
             const int sh = (j & 3) * 8;
             const uint32_t sa_w = j < 4 ? sca_lo : sca_hi, ma_w = j < 4 ? ma_lo : ma_hi;
@@ -804,9 +828,8 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
                                    ((s == 0 ? hw << 4 : s == 1 ? hw << 2 : s == 2 ? hw : hw >> 2) & 0x30303030u);
                 return __vsub4(q, 0x20202020u);
               };
-              const int sbk = blk * 8 + 4 * h + s;  // activation block
               int dot[4];
-              mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), ldg_u32(aq + sbk * 32 + g2 * 16 + 4 * t));
+              mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), bc[2 * (4 * h + s) + g2]);
               const float2 a0 = a0s[i * 8 + 4 * h + s], a1 = a1s[i * 8 + 4 * h + s];
               const float sca = (float)(int8_t)(uint8_t)(swa >> (8 * (g2 + 2 * s)));
               const float scb = (float)(int8_t)(uint8_t)(swb >> (8 * (g2 + 2 * s)));
@@ -834,7 +857,7 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
           x3 = (wb >> 4) & 0x0F0F0F0Fu;
         }
         int dot[4];
-        mma_k32(dot, x0, x1, x2, x3, ldg_u32(aq + blk * 32 + 4 * t), ldg_u32(aq + blk * 32 + 16 + 4 * t));
+        mma_k32(dot, x0, x1, x2, x3, bc[2 * ig], bc[2 * ig + 1]);
         const float2 a0 = a0s[i], a1 = a1s[i];
         if (T == T_Q8_0) {  // quant_int.rs:291-296
           acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), (float)dot[0]));
@@ -848,6 +871,9 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
           acc[3] = fadd(acc[3], fmul(fmul(drb, a1.x), fsub((float)dot[3], fmul(8.0f, a1.y))));
         }
       }
+    }
+#pragma unroll
+      for (int e = 0; e < 16; e++) bc[e] = bn[e];
     }
   }
   // out = 0.0 + acc (Pool::matmul zero-fills, then adds), or x += that
