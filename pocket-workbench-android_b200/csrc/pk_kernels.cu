@@ -678,6 +678,18 @@ __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, u
                : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 __device__ __forceinline__ uint32_t ldg_u32(const int8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+// Asynchronous global -> shared copies (completed by cp_async_wait_all).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+}
 
 template <int T> struct MmGeo;
 template <> struct MmGeo<T_Q4_K> { static constexpr int BE = 256, QB = 144; static constexpr bool D = false; };
@@ -700,7 +712,8 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
   extern __shared__ __align__(16) uint8_t mm_smem[];
   uint8_t *wq = mm_smem;                                // [16 rows][NBC][QB]
   float *wd = (float *)(mm_smem + MM_ROWS * NBC * G::QB);  // [16 rows][NBC] (types with a separate d)
-  float2 *as = (float2 *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][SBC] {da, sa}
+  float *asd = (float *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][SBC] da
+  int *ass = (int *)(asd + MM_LANES * SBC);                                         // [32 lanes][SBC] sa
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
@@ -716,28 +729,44 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
   for (int c0 = 0; c0 < nblk; c0 += NBC) {
     const int nbc = min(NBC, nblk - c0);
     __syncthreads();  // the previous chunk is consumed
-    // stage: the tile's rows (16-byte vectors), their scales, the lanes' activation scales
+    // stage: the tile's rows and the lanes' activation scales by asynchronous
+    // copies (every copy in flight at once), the f16 row scales four loads at a time
     const int v16 = nbc * G::QB / 16;
     for (int i = tid; i < nr * v16; i += 32 * MM_WARPS) {
       const int r = i / v16, j = i - r * v16;
-      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB) + j);
-      *reinterpret_cast<uint4 *>(wq + (size_t)r * NBC * G::QB + 16 * j) = v;
+      cp_async16(wq + (size_t)r * NBC * G::QB + 16 * j, W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB + 16 * j);
     }
-    if (G::D)
-      for (int i = tid; i < nr * nbc; i += 32 * MM_WARPS) {
-        const int r = i / nbc, j = i - r * nbc;
-        wd[r * NBC + j] = f16f(__ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j));
-      }
     const int s0 = c0 * (G::BE / 32), nsb = nbc * (G::BE / 32);
     for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS) {
       const int l = i / nsb, j = i - l * nsb;
       const long o = (long)(L0 + l) * nb32 + s0 + j;
-      as[l * SBC + j] = make_float2(__ldg(act.d + o), (float)__ldg(act.s + o));
+      cp_async4(asd + l * SBC + j, act.d + o);
+      cp_async4(ass + l * SBC + j, act.s + o);
     }
+    if (G::D)
+      for (int i0 = tid; i0 < nr * nbc; i0 += 4 * 32 * MM_WARPS) {
+        uint16_t hv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int i = i0 + u * 32 * MM_WARPS, r = i / nbc, j = i - r * nbc;
+          hv[u] = i < nr * nbc ? __ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j) : (uint16_t)0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int i = i0 + u * 32 * MM_WARPS, r = i / nbc, j = i - r * nbc;
+          if (i < nr * nbc) wd[r * NBC + j] = f16f(hv[u]);
+        }
+      }
+    cp_async_wait_all();
     __syncthreads();
     if (8 * w >= nl) continue;  // no lanes for this warp (it still meets every barrier)
     const uint8_t *qa = wq + (size_t)g * NBC * G::QB, *qb = wq + (size_t)(g + 8) * NBC * G::QB;
-    const float2 *a0s = as + lc0 * SBC, *a1s = as + lc1 * SBC;
+    const float *d0s = asd + lc0 * SBC, *d1s = asd + lc1 * SBC;
+    const int *s0s = ass + lc0 * SBC, *s1s = ass + lc1 * SBC;
+    auto ascale = [&](int sl, float2 &a0, float2 &a1) {  // {da, sa} of this thread's two lanes
+      a0 = make_float2(d0s[sl], (float)s0s[sl]);
+      a1 = make_float2(d1s[sl], (float)s1s[sl]);
+    };
     // The activation fragments of one group (a K-quant superblock, or eight
     // Q8_0/Q4_0 blocks: 16 words) are loaded one group ahead of their use.
     constexpr int GB = G::BE == 256 ? 1 : 8;  // storage blocks per group
@@ -790,7 +819,8 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
             const uint32_t x2 = h ? (wa1 >> 4) & M : wa1 & M, x3 = h ? (wb1 >> 4) & M : wb1 & M;
             int dot[4];
             mma_k32(dot, x0, x1, x2, x3, bc[2 * j], bc[2 * j + 1]);
-            const float2 a0 = a0s[sl], a1 = a1s[sl];
+            float2 a0, a1;
+            ascale(sl, a0, a1);
             const int sh = (j & 3) * 8;
             const uint32_t sa_w = j < 4 ? sca_lo : sca_hi, ma_w = j < 4 ? ma_lo : ma_hi;
             const uint32_t sb_w = j < 4 ? scb_lo : scb_hi, mb_w = j < 4 ? mb_lo : mb_hi;
@@ -830,7 +860,8 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
               };
               int dot[4];
               mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), bc[2 * (4 * h + s) + g2]);
-              const float2 a0 = a0s[i * 8 + 4 * h + s], a1 = a1s[i * 8 + 4 * h + s];
+              float2 a0, a1;
+              ascale(i * 8 + 4 * h + s, a0, a1);
               const float sca = (float)(int8_t)(uint8_t)(swa >> (8 * (g2 + 2 * s)));
               const float scb = (float)(int8_t)(uint8_t)(swb >> (8 * (g2 + 2 * s)));
               acc[0] = fadd(acc[0], fmul(fmul(fmul(dra, sca), a0.x), (float)dot[0]));
@@ -858,7 +889,8 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
         }
         int dot[4];
         mma_k32(dot, x0, x1, x2, x3, bc[2 * ig], bc[2 * ig + 1]);
-        const float2 a0 = a0s[i], a1 = a1s[i];
+        float2 a0, a1;
+        ascale(i, a0, a1);
         if (T == T_Q8_0) {  // quant_int.rs:291-296
           acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), (float)dot[0]));
           acc[1] = fadd(acc[1], fmul(fmul(dra, a1.x), (float)dot[1]));
@@ -893,7 +925,7 @@ static cudaError_t launch_mv_mma_t(const DevTensor &w, const Q8Dev &act, float *
                                    cudaStream_t st) {
   constexpr int NBC = mm_chunk_blocks<T>();
   const size_t smem = (size_t)MM_ROWS * NBC * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)) +
-                      (size_t)MM_LANES * (NBC * MmGeo<T>::BE / 32) * sizeof(float2);
+                      (size_t)MM_LANES * (NBC * MmGeo<T>::BE / 32) * 8;
   cudaError_t e = set_smem(k_mv_mma<T>, smem);
   if (e != cudaSuccess) return e;
   const dim3 grid((w.rows + MM_ROWS - 1) / MM_ROWS, (act.b + MM_LANES - 1) / MM_LANES);
