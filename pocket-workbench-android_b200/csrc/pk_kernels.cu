@@ -944,41 +944,46 @@ cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, lo
 }
 
 // ------------------------------------------------------------ RoPE + KV, SwiGLU
+// One thread per element: threads [0, n_head*half) rotate one q pair in
+// place; the rest write one K element (rotated) and one V element to the
+// cache.  grid = (b, element blocks).
 __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *pos, const float *rc, const float *rs,
                           int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc) {
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;
+  const int nq = n_head * half, kdim = n_kv * dh;
+  if (i >= nq + kdim) return;
   const int p = pos[bi];
-  const int qdim = n_head * dh, kdim = n_kv * dh;
-  float *qr = q + (long)bi * qdim;
-  for (int i = threadIdx.x; i < n_head * half; i += blockDim.x) {
+  if (i < nq) {
     const int h = i / half, j = i - h * half;
-    const int i0 = h * dh + 2 * j;
-    const float x0 = qr[i0], x1 = qr[i0 + 1];
+    float *qr = q + (long)bi * n_head * dh + h * dh + 2 * j;
+    const float x0 = qr[0], x1 = qr[1];
     const float c = rc[(size_t)p * half + j], s = rs[(size_t)p * half + j];
-    qr[i0] = fsub(fmul(x0, c), fmul(x1, s));
-    qr[i0 + 1] = fadd(fmul(x0, s), fmul(x1, c));
+    qr[0] = fsub(fmul(x0, c), fmul(x1, s));
+    qr[1] = fadd(fmul(x0, s), fmul(x1, c));
+    return;
   }
-  const float *kr = k + (long)bi * kdim, *vr = v + (long)bi * kdim;
-  for (int i = threadIdx.x; i < kdim; i += blockDim.x) {
-    const int h = i / dh, d = i - h * dh;
-    float o = kr[i];
-    if (d < 2 * half) {
-      const int j = d >> 1;
-      const float c = rc[(size_t)p * half + j], s = rs[(size_t)p * half + j];
-      if ((d & 1) == 0) o = fsub(fmul(kr[i], c), fmul(kr[i + 1], s));
-      else o = fadd(fmul(kr[i - 1], s), fmul(kr[i], c));
-    }
-    kc[((size_t)h * dh + d) * n_ctx + p] = o;  // K is d-major: [kv head][d][position]
-    vc[((size_t)h * n_ctx + p) * dh + d] = vr[i];
+  const int e = i - nq, h = e / dh, d = e - h * dh;
+  const float *kr = k + (long)bi * kdim;
+  float o = kr[e];
+  if (d < 2 * half) {
+    const int j = d >> 1;
+    const float c = rc[(size_t)p * half + j], s = rs[(size_t)p * half + j];
+    if ((d & 1) == 0) o = fsub(fmul(kr[e], c), fmul(kr[e + 1], s));
+    else o = fadd(fmul(kr[e - 1], s), fmul(kr[e], c));
   }
+  kc[((size_t)h * dh + d) * n_ctx + p] = o;  // K is d-major: [kv head][d][position]
+  vc[((size_t)h * n_ctx + p) * dh + d] = v[(long)bi * kdim + e];
 }
 
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rc,
                            const float *rs, int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc,
                            cudaStream_t st) {
-  return launch(k_rope_kv, dim3(b), dim3(256), 0, st, q, k, v, pos, rc, rs, half, dh, n_head, n_kv, n_ctx, kc, vc);
+  const int total = n_head * half + n_kv * dh;
+  return launch(k_rope_kv, dim3(b, (total + 127) / 128), dim3(128), 0, st, q, k, v, pos, rc, rs, half, dh, n_head,
+                n_kv, n_ctx, kc, vc);
 }
 
 __global__ void k_swiglu(const float *g, const float *u, float *h, long n) {
@@ -1080,8 +1085,163 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   if (tid < dh) a.out[hb * dh + tid] = fmul(acc, s_inv);
 }
 
+// Chunk attention (b > 1): the same arithmetic as k_attn's b > 1 branch, one
+// CTA per (group of AC_G tokens, head), the head's K and V brought into
+// shared memory tile by tile (AC_P positions, double-buffered asynchronous
+// copies) and shared by the group's tokens.
+//   pass 1: thread (token, 4 positions) runs four score chains over d
+//           (sequential, unfused) against the K tile [d][position];
+//   pass 2: the tile's weights e = exp(s - M) (0 past the token's position,
+//           which the V chain skips and which adds +0.0 exactly to a sum that
+//           starts at +0.0), then thread (token, 2 dims) runs two V chains
+//           and the token's sum chain over the tile in position order.
+constexpr int AC_THREADS = 256;
+__host__ __device__ inline int ac_group(int dh) { return 512 / dh < 8 ? 512 / dh : 8; }
+__host__ __device__ inline int ac_tile(int dh) { return dh <= 64 ? 128 : 64; }
+static size_t ac_smem(int dh) {
+  const int G = ac_group(dh), P = ac_tile(dh);
+  return sizeof(float) * ((size_t)2 * P * dh + (size_t)G * (P + 4) + (size_t)G * dh + AC_THREADS + 16);
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+__global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
+  extern __shared__ __align__(16) float acs[];
+  const int dh = a.dh, G = ac_group(dh), P = ac_tile(dh), QP = P / 4, tid = threadIdx.x;
+  const int h = blockIdx.y, kh = h / (a.n_head / a.n_kv), t0 = blockIdx.x * G;
+  float *buf0 = acs, *buf1 = acs + P * dh, *E = buf1 + P * dh, *qs = E + G * (P + 4), *red = qs + G * dh;
+  float *Ms = red + AC_THREADS;
+  int *posv = (int *)(Ms + 8);
+  pdl_trigger();
+  pdl_wait();
+  if (tid < G) {
+    const int bi = t0 + tid;
+    posv[tid] = bi < a.b ? min(a.pos[bi], a.n_ctx - 1) : -1;
+  }
+  for (int i = tid; i < G * dh; i += AC_THREADS) {
+    const int t = i / dh, bi = t0 + t;
+    qs[i] = bi < a.b ? a.q[((long)bi * a.n_head + h) * dh + (i - t * dh)] : 0.0f;
+  }
+  __syncthreads();
+  int maxpos = -1;
+  for (int t = 0; t < G; t++) maxpos = max(maxpos, posv[t]);
+  if (maxpos < 0) return;
+  const int nt = maxpos / P + 1;
+  const float *kc = a.kcache + (size_t)kh * dh * a.n_ctx, *vc = a.vcache + (size_t)kh * a.n_ctx * dh;
+  auto stage_k = [&](int i, float *dst) {
+    const int p0 = i * P, nq = (min(P, maxpos + 1 - p0) + 3) >> 2;
+    for (int c = tid; c < dh * nq; c += AC_THREADS) {
+      const int d = c / nq, j = c - d * nq;
+      cp_async16(dst + d * P + 4 * j, kc + (size_t)d * a.n_ctx + p0 + 4 * j);
+    }
+  };
+  auto stage_v = [&](int i, float *dst) {
+    const int p0 = i * P, nq = min(P, maxpos + 1 - p0) * dh / 4;
+    for (int c = tid; c < nq; c += AC_THREADS) cp_async16(dst + 4 * c, vc + (size_t)p0 * dh + 4 * c);
+  };
+  // ---- pass 1: scores
+  const int st = tid / QP, sq = tid - st * QP;
+  const int spos = st < G ? posv[st] : -1;
+  float *sc = a.scores + ((long)(t0 + st) * a.n_head + h) * a.n_ctx;
+  float mx = -INFINITY;
+  stage_k(0, buf0);
+  cp_async_commit();
+  for (int i = 0; i < nt; i++) {
+    if (i + 1 < nt) stage_k(i + 1, (i & 1) ? buf0 : buf1);
+    else stage_v(0, (i & 1) ? buf0 : buf1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();
+    const int p = i * P + 4 * sq;
+    if (p <= spos) {
+      const float4 *kt = (const float4 *)((i & 1) ? buf1 : buf0) + sq;
+      const float *qv = qs + st * dh;
+      float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+#pragma unroll 4
+      for (int d = 0; d < dh; d++) {
+        const float4 k = kt[d * QP];
+        const float qq = qv[d];
+        c0 = fadd(c0, fmul(qq, k.x));
+        c1 = fadd(c1, fmul(qq, k.y));
+        c2 = fadd(c2, fmul(qq, k.z));
+        c3 = fadd(c3, fmul(qq, k.w));
+      }
+      const float sv[4] = {fmul(c0, a.scale), fmul(c1, a.scale), fmul(c2, a.scale), fmul(c3, a.scale)};
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (p + u <= spos) {
+          sc[p + u] = sv[u];
+          mx = sv[u] > mx ? sv[u] : mx;
+        }
+    }
+    __syncthreads();
+  }
+  red[tid] = mx;
+  __syncthreads();
+  if (tid < G) {
+    float m = -INFINITY;
+    for (int i = 0; i < QP; i++) m = red[tid * QP + i] > m ? red[tid * QP + i] : m;
+    Ms[tid] = m;
+  }
+  __syncthreads();
+  // ---- pass 2: weights, V chains and sum chains
+  const int H2 = dh / 2, vt = tid / H2, vd = tid - vt * H2;
+  const bool vact = vt < G;
+  const float *Et = E + (vact ? vt : 0) * (P + 4);
+  float acc0 = 0.0f, acc1 = 0.0f, sum = 0.0f;
+  for (int j = 0; j < nt; j++) {
+    const float *vb = ((nt + j) & 1) ? buf1 : buf0;
+    if (j + 1 < nt) stage_v(j + 1, ((nt + j) & 1) ? buf0 : buf1);
+    cp_async_commit();
+    const int p0 = j * P;
+    for (int i = tid; i < G * P; i += AC_THREADS) {
+      const int t = i / P, pl = i - t * P, p = p0 + pl;
+      float e = 0.0f;
+      if (p <= posv[t]) {
+        const float *srow = a.scores + ((long)(t0 + t) * a.n_head + h) * a.n_ctx;
+        e = expf_lib(fsub(srow[p], Ms[t]));
+      }
+      E[t * (P + 4) + pl] = e;
+    }
+    cp_async_wait1();
+    __syncthreads();
+    if (vact) {
+      const int npr = (min(P, maxpos + 1 - p0) + 3) & ~3;
+      const float2 *vv = (const float2 *)vb + vd;
+      for (int pl = 0; pl < npr; pl += 4) {
+        const float4 e4 = *(const float4 *)(Et + pl);
+        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const float2 v = vv[(pl + u) * H2];
+          if (ev[u] != 0.0f) {
+            acc0 = fadd(acc0, fmul(ev[u], v.x));
+            acc1 = fadd(acc1, fmul(ev[u], v.y));
+          }
+          sum = fadd(sum, ev[u]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (vact && t0 + vt < a.b) {
+    const float inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+    float *o = a.out + ((long)(t0 + vt) * a.n_head + h) * dh + 2 * vd;
+    o[0] = fmul(acc0, inv);
+    o[1] = fmul(acc1, inv);
+  }
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
+  if (a.b > 1 && a.n_ctx % 4 == 0 && (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
+    const size_t smem = ac_smem(a.dh);
+    cudaError_t e = set_smem(k_attn_chunk, smem);
+    if (e != cudaSuccess) return e;
+    const int G = ac_group(a.dh);
+    return launch(k_attn_chunk, dim3((a.b + G - 1) / G, a.n_head), dim3(AC_THREADS), smem, st, a);
+  }
   const int threads = a.dh < 128 ? 128 : 256;
   return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, a.b == 1 ? 1 : 0);
 }

@@ -129,6 +129,21 @@ def test_persistent_kernel_equals_op_sequence(pk, paths, name):
     assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
 
 
+@pytest.mark.parametrize("name", ["tiny", "q40"])
+def test_chunk_attention_equals_per_token_kernel(pk, paths, name):
+    """Prefill attention over K/V tiles in shared memory (n_ctx a multiple of
+    4) gives the same bits as the one-CTA-per-token kernel (n_ctx = 254 takes
+    that path), across chunks whose positions span several tiles."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(13, 200, spec.n_vocab)
+    a, b = pk.Engine(paths[name], n_ctx=256), pk.Engine(paths[name], n_ctx=254)
+    for e in (a, b):
+        for lo in range(0, 192, 32):
+            e.forward(prompt[lo:lo + 32], np.arange(lo, lo + 32), False)
+        e.forward(prompt[192:199], np.arange(192, 199), True)
+    assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
+
+
 def test_bounded_wait_runs_out_and_engine_recovers(pk, paths):
     """Failure detection without a GPU fault: one persistent-kernel launch
     whose phase inputs never arrive (its readers wait for a tag nothing
