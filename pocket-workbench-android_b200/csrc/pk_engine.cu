@@ -41,6 +41,15 @@ Engine::~Engine() {
   cudaFreeHost(h_ids_);
   cudaFreeHost(h_pos_);
   cudaFreeHost(h_tok_);
+  if (lane_[1].st) cudaStreamSynchronize(lane_[1].st);
+  cudaFree(d_lane1_arena_);
+  cudaFreeHost(h_pids_);
+  cudaFreeHost(h_ppos_);
+  for (auto &v : kv_ev_)
+    for (cudaEvent_t e : v) cudaEventDestroy(e);
+  if (fork_ev_) cudaEventDestroy(fork_ev_);
+  if (join_ev_) cudaEventDestroy(join_ev_);
+  if (lane_[1].st) cudaStreamDestroy(lane_[1].st);
   if (st_) cudaStreamDestroy(st_);
 }
 
@@ -312,6 +321,43 @@ int Engine::load(const char *path) {
   d_ids_ = (uint32_t *)take(); d_pos_ = (int *)take(); d_tok_ = (uint32_t *)take(); d_hist_ = (uint32_t *)take();
   d_step_ = (int *)take();
 
+  // prefill lanes (lane 1: a second set of per-chunk scratch and a stream)
+  lane_[0].st = st_;
+  lane_[0].x = x_; lane_[0].q = q_; lane_[0].k = k_; lane_[0].v = v_; lane_[0].attn = attn_;
+  lane_[0].gate = gate_; lane_[0].up = up_; lane_[0].h = h_; lane_[0].scores = att_scores_;
+  lane_[0].act = act_; lane_[0].ids = d_ids_; lane_[0].pos = d_pos_;
+  {
+    const std::vector<size_t> s1 = {B * ne * 4, B * qdim * 4, B * kdim * 4, B * kdim * 4, B * qdim * 4,
+                                    B * ff * 4, B * ff * 4, B * ff * 4, B * kmax, B * (kmax / 32) * 4,
+                                    B * (kmax / 32) * 4, B * H * n_ctx_ * 4, 64 * 4, 64 * 4};
+    size_t a1 = 0;
+    for (size_t v : s1) a1 += a256(v);
+    PK_CK(cudaMalloc((void **)&d_lane1_arena_, a1));
+    PK_CK(cudaMemsetAsync(d_lane1_arena_, 0, a1, st_));
+    uint8_t *p1 = d_lane1_arena_;
+    size_t i1 = 0;
+    auto take1 = [&]() {
+      uint8_t *r = p1;
+      p1 += a256(s1[i1++]);
+      return r;
+    };
+    Lane &L = lane_[1];
+    L.x = (float *)take1(); L.q = (float *)take1(); L.k = (float *)take1(); L.v = (float *)take1();
+    L.attn = (float *)take1(); L.gate = (float *)take1(); L.up = (float *)take1(); L.h = (float *)take1();
+    L.act = act_;
+    L.act.q = (int8_t *)take1(); L.act.d = (float *)take1(); L.act.s = (int32_t *)take1();
+    L.scores = (float *)take1(); L.ids = (uint32_t *)take1(); L.pos = (int *)take1();
+    PK_CK(cudaStreamCreateWithFlags(&L.st, cudaStreamNonBlocking));
+    for (auto &v : kv_ev_) {
+      v.resize(c.n_layer);
+      for (auto &e : v) PK_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    PK_CK(cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming));
+    PK_CK(cudaEventCreateWithFlags(&join_ev_, cudaEventDisableTiming));
+    PK_CK(cudaHostAlloc((void **)&h_pids_, (size_t)n_ctx_ * sizeof(uint32_t), cudaHostAllocDefault));
+    PK_CK(cudaHostAlloc((void **)&h_ppos_, (size_t)n_ctx_ * sizeof(int), cudaHostAllocDefault));
+  }
+
   // Tokenizer::from_gguf end-of-generation ids (tokenizer.rs:82-92)
   uint64_t eos;
   if (g.get_u64("tokenizer.ggml.eos_token_id", &eos)) eos_ids_.push_back((uint32_t)eos);
@@ -508,20 +554,24 @@ static double mat_stream_bytes(const DevTensor &w) {
     if ((_rc = prof_end())) return _rc;           \
   } while (0)
 
-// The per-token kernel sequence (model.rs:857-1170).  Reads ids/positions
-// from d_ids_/d_pos_ so a b == 1 pass can be captured once as a CUDA graph.
-int Engine::enqueue_forward(int b, bool want_logits, bool cancellable) {
+// The per-token kernel sequence (model.rs:857-1170) on prefill lane li.
+// Reads ids/positions from the lane's device buffers, so a b == 1 pass
+// (lane 0) can be captured once as a CUDA graph.  kv & KV_RECORD: record
+// kv_ev_[li][l] once layer l's K/V are written; kv & KV_WAIT: layer l's
+// attention first waits for the other lane's kv_ev_ of layer l.
+int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, int kv) {
+  const Lane &S = lane_[li];
   const Config &c = cfg_;
   const int ne = c.n_embd, dh = c.head_dim, qdim = c.n_head * dh, kdim = c.n_head_kv * dh, ff = c.n_ff;
   const size_t layer_kv = (size_t)c.n_head_kv * n_ctx_ * dh;
   const double f4 = 4.0, kv_pos = (double)next_pos_ + 1.0;  // positions attended in a profiled decode step
   PROF("k_dequant_rows", embd_row_bytes_ + ne * f4,
-       launch_dequant_rows(embd_type_, embd_raw_, embd_row_bytes_, ne, d_ids_, b, x_, st_));
-  dump("embd", x_, (size_t)b * ne);
+       launch_dequant_rows(embd_type_, embd_raw_, embd_row_bytes_, ne, S.ids, b, S.x, S.st));
+  dump("embd", S.x, (size_t)b * ne);
   AttnArgs at{};
-  at.q = q_; at.pos = d_pos_; at.out = attn_; at.b = b; at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh;
+  at.q = S.q; at.pos = S.pos; at.out = S.attn; at.b = b; at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh;
   at.n_ctx = n_ctx_; at.scale = 1.0f / sqrtf((float)dh);
-  at.scores = att_scores_;
+  at.scores = S.scores;
   for (int l = 0; l < c.n_layer; l++) {
     if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
     const LayerDev &L = layers_[l];
@@ -530,63 +580,67 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable) {
     if (b == 1) {
       QkvArgs qa;
       qa.wq = L.q; qa.wk = L.k; qa.wv = L.v;
-      qa.src.x = x_; qa.src.nw = L.attn_norm; qa.src.eps = c.rms_eps;
-      qa.pos = d_pos_; qa.rope_cos = d_rope_cos_; qa.rope_sin = d_rope_sin_;
+      qa.src.x = S.x; qa.src.nw = L.attn_norm; qa.src.eps = c.rms_eps;
+      qa.pos = S.pos; qa.rope_cos = d_rope_cos_; qa.rope_sin = d_rope_sin_;
       qa.half = c.n_rot / 2; qa.dh = dh; qa.n_ctx = n_ctx_;
-      qa.qout = q_; qa.kcache = kc; qa.vcache = vc;
+      qa.qout = S.q; qa.kcache = kc; qa.vcache = vc;
       PROF("k_qkv_b1", mat_stream_bytes(L.q) + mat_stream_bytes(L.k) + mat_stream_bytes(L.v) + 2 * ne * f4 +
                            (qdim + 2 * kdim) * f4,
-           launch_qkv_b1(qa, st_));
-      if (l == 0) dump("Qrope-0", q_, (size_t)qdim);
-      PROF("k_attn", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, st_));
+           launch_qkv_b1(qa, S.st));
+      if (l == 0) dump("Qrope-0", S.q, (size_t)qdim);
+      if (kv & KV_RECORD) PK_CK(cudaEventRecord(kv_ev_[li][l], S.st));
+      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(S.st, kv_ev_[1 - li][l], 0));
+      PROF("k_attn", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, S.st));
       B1Src so;
-      so.x = attn_;
-      PROF("k_mv_b1", mat_stream_bytes(L.o) + qdim * f4 + 2 * ne * f4, launch_mv_b1(L.o, so, x_, true, st_));
-      if (l == 0) dump("ffn_inp-0", x_, (size_t)ne);
+      so.x = S.attn;
+      PROF("k_mv_b1", mat_stream_bytes(L.o) + qdim * f4 + 2 * ne * f4, launch_mv_b1(L.o, so, S.x, true, S.st));
+      if (l == 0) dump("ffn_inp-0", S.x, (size_t)ne);
       B1Src sf;
-      sf.x = x_; sf.nw = L.ffn_norm; sf.eps = c.rms_eps;
+      sf.x = S.x; sf.nw = L.ffn_norm; sf.eps = c.rms_eps;
       PROF("k_gateup_b1", mat_stream_bytes(L.gate) + mat_stream_bytes(L.up) + 2 * ne * f4 + ff * f4,
-           launch_gateup_b1(L.gate, L.up, sf, h_, st_));
+           launch_gateup_b1(L.gate, L.up, sf, S.h, S.st));
       B1Src sd;
-      sd.x = h_;
-      PROF("k_mv_b1", mat_stream_bytes(L.down) + ff * f4 + 2 * ne * f4, launch_mv_b1(L.down, sd, x_, true, st_));
+      sd.x = S.h;
+      PROF("k_mv_b1", mat_stream_bytes(L.down) + ff * f4 + 2 * ne * f4, launch_mv_b1(L.down, sd, S.x, true, S.st));
     } else {
-      Q8Dev a = act_;
+      const cudaStream_t st = S.st;
+      Q8Dev a = S.act;
       a.k = ne; a.b = b;
-      PK_CK(launch_rmsnorm_q8(x_, L.attn_norm, c.rms_eps, ne, b, a, nullptr, st_));
-      PK_CK(launch_mv_lanes(L.q, a, q_, 1, qdim, false, st_));
-      PK_CK(launch_mv_lanes(L.k, a, k_, 1, kdim, false, st_));
-      PK_CK(launch_mv_lanes(L.v, a, v_, 1, kdim, false, st_));
-      if (l == 0) { dump("Qcur-0", q_, (size_t)b * qdim); dump("Kcur-0", k_, (size_t)b * kdim); dump("Vcur-0", v_, (size_t)b * kdim); }
-      PK_CK(launch_rope_kv(q_, k_, v_, b, d_pos_, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
-                           n_ctx_, kc, vc, st_));
-      if (l == 0) dump("Qrope-0", q_, (size_t)b * qdim);
-      PK_CK(launch_attention(at, st_));
+      PK_CK(launch_rmsnorm_q8(S.x, L.attn_norm, c.rms_eps, ne, b, a, nullptr, st));
+      const MvOut qkv[3] = {{L.q, S.q, 1, qdim, false}, {L.k, S.k, 1, kdim, false}, {L.v, S.v, 1, kdim, false}};
+      PK_CK(launch_mv_multi(3, qkv, a, st));
+      if (l == 0) { dump("Qcur-0", S.q, (size_t)b * qdim); dump("Kcur-0", S.k, (size_t)b * kdim); dump("Vcur-0", S.v, (size_t)b * kdim); }
+      PK_CK(launch_rope_kv(S.q, S.k, S.v, b, S.pos, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
+                           n_ctx_, kc, vc, st));
+      if (kv & KV_RECORD) PK_CK(cudaEventRecord(kv_ev_[li][l], st));
+      if (l == 0) dump("Qrope-0", S.q, (size_t)b * qdim);
+      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(st, kv_ev_[1 - li][l], 0));
       a.k = qdim;
-      PK_CK(launch_q8(attn_, 1, qdim, qdim, b, a, st_));
-      PK_CK(launch_mv_lanes(L.o, a, x_, 1, ne, true, st_));
-      if (l == 0) dump("ffn_inp-0", x_, (size_t)b * ne);
+      AttnArgs atq = at;
+      atq.q8 = a;  // the attention kernel also writes Q8 of its output
+      PK_CK(launch_attention(atq, st));
+      PK_CK(launch_mv_lanes(L.o, a, S.x, 1, ne, true, st));
+      if (l == 0) dump("ffn_inp-0", S.x, (size_t)b * ne);
       a.k = ne;
-      PK_CK(launch_rmsnorm_q8(x_, L.ffn_norm, c.rms_eps, ne, b, a, nullptr, st_));
-      PK_CK(launch_mv_lanes(L.gate, a, gate_, 1, ff, false, st_));
-      PK_CK(launch_mv_lanes(L.up, a, up_, 1, ff, false, st_));
-      PK_CK(launch_swiglu(gate_, up_, h_, (long)b * ff, st_));
+      PK_CK(launch_rmsnorm_q8(S.x, L.ffn_norm, c.rms_eps, ne, b, a, nullptr, st));
+      const MvOut gu[2] = {{L.gate, S.gate, 1, ff, false}, {L.up, S.up, 1, ff, false}};
+      PK_CK(launch_mv_multi(2, gu, a, st));
       a.k = ff;
-      PK_CK(launch_q8(h_, 1, ff, ff, b, a, st_));
-      PK_CK(launch_mv_lanes(L.down, a, x_, 1, ne, true, st_));
+      PK_CK(launch_swiglu_q8(S.gate, S.up, ff, b, a, S.h, st));
+      PK_CK(launch_mv_lanes(L.down, a, S.x, 1, ne, true, st));
     }
     if (l == 0) {
-      dump("kqv_out-0", attn_, (size_t)b * qdim);
-      dump("ffn_swiglu-0", h_, (size_t)b * ff);
-      dump("l_out-0", x_, (size_t)b * ne);
+      dump("kqv_out-0", S.attn, (size_t)b * qdim);
+      dump("ffn_swiglu-0", S.h, (size_t)b * ff);
+      dump("l_out-0", S.x, (size_t)b * ne);
     }
   }
   if (want_logits) {
     if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
     B1Src sh;
-    sh.x = x_ + (size_t)(b - 1) * ne; sh.nw = output_norm_; sh.eps = c.rms_eps;
+    sh.x = S.x + (size_t)(b - 1) * ne; sh.nw = output_norm_; sh.eps = c.rms_eps;
     PROF("k_mv_b1", mat_stream_bytes(output_) + 2 * ne * f4 + (double)vocab_ * f4,
-         launch_mv_b1(output_, sh, logits_, false, st_));
+         launch_mv_b1(output_, sh, logits_, false, S.st));
     dump("result_output", logits_, (size_t)vocab_);
   }
   return PK_OK;
@@ -690,6 +744,53 @@ int Engine::argmax(uint32_t *tok) {
   return PK_OK;
 }
 
+// The prompt's chunks [off, n) (chunk tokens each) on alternate prefill
+// lanes: chunk c + 1 runs its layer l while chunk c is still in later
+// layers, waiting only for chunk c's K/V of layer l before its attention.
+// Every kernel sees the same inputs as in chunk order, so the results are
+// the same bits.  Returns with both lanes idle.
+int Engine::prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, bool *stopped) {
+  if (n > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+  for (int i = off; i < n; i++)
+    if (prompt[i] >= (uint32_t)vocab_) return set_error(PK_ERR_INVALID, "token " + std::to_string(prompt[i]) + " out of vocab");
+  PK_CK(cudaSetDevice(device_));
+  for (int i = off; i < n; i++) {
+    h_pids_[i] = prompt[i];
+    h_ppos_[i] = i;
+  }
+  have_logits_ = false;
+  PK_CK(cudaEventRecord(fork_ev_, st_));
+  PK_CK(cudaStreamWaitEvent(lane_[1].st, fork_ev_, 0));
+  int rc = PK_OK;
+  cudaError_t e = cudaSuccess;
+  for (int o = off, c = 0; o < n; o += chunk, c++) {
+    if (g_stop.load()) {
+      *stopped = true;
+      break;
+    }
+    const int m = std::min(chunk, n - o), li = c & 1;
+    const Lane &L = lane_[li];
+    e = cudaMemcpyAsync(L.ids, h_pids_ + o, m * sizeof(uint32_t), cudaMemcpyHostToDevice, L.st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(L.pos, h_ppos_ + o, m * sizeof(int), cudaMemcpyHostToDevice, L.st);
+    if (e != cudaSuccess) break;
+    if ((rc = enqueue_forward(m, o + m >= n, true, li, KV_RECORD | (c > 0 ? KV_WAIT : 0)))) break;
+  }
+  // lane 1 joins lane 0, then both are drained
+  cudaError_t ej = cudaEventRecord(join_ev_, lane_[1].st);
+  if (ej == cudaSuccess) ej = cudaStreamWaitEvent(st_, join_ev_, 0);
+  const cudaError_t es = cudaStreamSynchronize(st_);
+  cudaStreamSynchronize(lane_[1].st);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync (prefill ids)");
+  if (ej != cudaSuccess) return cuda_error(ej, "prefill lane join");
+  if (es != cudaSuccess) return cuda_error(es, "prefill");
+  PK_CK(cudaGetLastError());
+  if (*stopped) return PK_OK;
+  next_pos_ = n;
+  have_logits_ = true;
+  return PK_OK;
+}
+
 // Engine::generate (model.rs:1235-1352).  The device engine is this
 // process's only engine, so prefix reuse follows the reference's CPU rules
 // (cpu_only == true): full 32-token prefill chunks of an exactly matching
@@ -720,7 +821,21 @@ int Engine::generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_
   int off = (int)reused;
   bool user_stop = false;
   std::vector<int> positions(chunk);
-  while (off < n) {
+  if (!dbg_on_ && n - off > chunk) {  // two or more chunks: alternate lanes
+    bool stopped = false;
+    const int rc = prefill_lanes(prompt, n, off, chunk, &stopped);
+    if (rc && !g_stop.load()) {
+      kv_tokens_.clear();
+      return finish(rc);
+    }
+    if (rc || stopped) {
+      user_stop = true;
+    } else {
+      kv_tokens_.insert(kv_tokens_.end(), prompt + off, prompt + n);
+      off = n;
+    }
+  }
+  while (off < n && !user_stop) {
     if (g_stop.load()) { user_stop = true; break; }
     const int m = std::min(chunk, n - off);
     for (int i = 0; i < m; i++) positions[i] = off + i;

@@ -50,7 +50,9 @@ class Engine {
 
  private:
   int forward_inner(const uint32_t *ids, const int *pos, int b, bool want_logits, bool cancellable);
-  int enqueue_forward(int b, bool want_logits, bool cancellable);
+  enum { KV_RECORD = 1, KV_WAIT = 2 };
+  int enqueue_forward(int b, bool want_logits, bool cancellable, int li = 0, int kv = 0);
+  int prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, bool *stopped);
   int setup_decode();
   int check_decode_error();
   int ensure_graphs();
@@ -85,6 +87,25 @@ class Engine {
   // pinned host staging
   uint32_t *h_ids_ = nullptr, *h_tok_ = nullptr;
   int *h_pos_ = nullptr;
+
+  // Prefill lanes: the scratch of one chunk's forward pass and the stream it
+  // runs on.  Lane 0 is the buffers above and st_; lane 1 has its own, so
+  // consecutive chunks of a prompt run on alternate lanes, chunk c + 1's
+  // layer l waiting only for chunk c's K/V of layer l (kv_ev_).
+  struct Lane {
+    cudaStream_t st = nullptr;
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *gate = nullptr, *up = nullptr, *h = nullptr, *scores = nullptr;
+    Q8Dev act;
+    uint32_t *ids = nullptr;
+    int *pos = nullptr;
+  };
+  Lane lane_[2];
+  uint8_t *d_lane1_arena_ = nullptr;
+  std::vector<cudaEvent_t> kv_ev_[2];
+  cudaEvent_t fork_ev_ = nullptr, join_ev_ = nullptr;
+  uint32_t *h_pids_ = nullptr;  // pinned prompt ids / positions, n_ctx each
+  int *h_ppos_ = nullptr;
 
   // persistent decode kernel (pk_decode.cu): plan, device tables and args
   bool use_decode_ = false;

@@ -267,31 +267,30 @@ __device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
   return red[32];
 }
 
-// Sum of squares in the reference's b > 1 order (model.rs:813-817), over a
-// row staged in shared memory: one sequential unfused chain, with the squares
-// of the next eight elements formed while the current eight are added.
-// Result broadcast through red[32].
-__device__ float sum_sq_seq_smem(const float *xs, int n, float *red) {
+// Sum of squares in the reference's b > 1 order (model.rs:813-817): one
+// sequential unfused chain.  The squares are formed by every thread into
+// sq[] (zero-padded to a multiple of 16); thread 0 then adds them in order,
+// loading the next sixteen while it adds the current sixteen.  The padding
+// adds +0.0, exact for a sum that starts at +0.0.  Result broadcast through
+// red[32].
+__device__ float sum_sq_seq_smem(const float *xs, float *sq, int n, float *red) {
+  const int n16 = (n + 15) & ~15;
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) sq[i] = i < n ? fmul(xs[i], xs[i]) : 0.0f;
+  __syncthreads();
   if (threadIdx.x == 0) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(sq);
+    const int g = n16 / 16;
     float ss = 0.0f;
-    int i = 0;
-    if (n >= 8) {
-      float cur[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) cur[u] = fmul(xs[u], xs[u]);
-      for (i = 8; i + 8 <= n; i += 8) {
-        float nxt[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) nxt[u] = fmul(xs[i + u], xs[i + u]);
-#pragma unroll
-        for (int u = 0; u < 8; u++) ss = fadd(ss, cur[u]);
-#pragma unroll
-        for (int u = 0; u < 8; u++) cur[u] = nxt[u];
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) ss = fadd(ss, cur[u]);
+    float4 c0 = s4[0], c1 = s4[1], c2 = s4[2], c3 = s4[3];
+    for (int i = 0; i < g; i++) {
+      const int nx = i + 1 < g ? 4 * (i + 1) : 4 * i;
+      const float4 n0 = s4[nx], n1 = s4[nx + 1], n2 = s4[nx + 2], n3 = s4[nx + 3];
+      ss = fadd(ss, c0.x); ss = fadd(ss, c0.y); ss = fadd(ss, c0.z); ss = fadd(ss, c0.w);
+      ss = fadd(ss, c1.x); ss = fadd(ss, c1.y); ss = fadd(ss, c1.z); ss = fadd(ss, c1.w);
+      ss = fadd(ss, c2.x); ss = fadd(ss, c2.y); ss = fadd(ss, c2.z); ss = fadd(ss, c2.w);
+      ss = fadd(ss, c3.x); ss = fadd(ss, c3.y); ss = fadd(ss, c3.z); ss = fadd(ss, c3.w);
+      c0 = n0; c1 = n1; c2 = n2; c3 = n3;
     }
-    for (; i < n; i++) ss = fadd(ss, fmul(xs[i], xs[i]));
     red[32] = ss;
   }
   __syncthreads();
@@ -299,23 +298,28 @@ __device__ float sum_sq_seq_smem(const float *xs, int n, float *red) {
 }
 
 // RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.  The
-// token's row is staged in shared memory (dynamic, k floats) first.
+// token's row and the norm weights are staged in shared memory first
+// (dynamic: x, w and the padded squares, 3 x k floats).
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn) {
-  extern __shared__ float xs[];
+  extern __shared__ __align__(16) float xs[];
   __shared__ float red[40];
+  float *ws = xs + ((k + 15) & ~15), *sq = ws + ((k + 15) & ~15);
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
   const float *xr = x + (long)bi * k;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = xr[i];
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    xs[i] = xr[i];
+    ws[i] = nw[i];
+  }
   __syncthreads();
-  const float ss = sum_sq_seq_smem(xs, k, red);
+  const float ss = sum_sq_seq_smem(xs, sq, k, red);
   const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
   const int nb = k >> 5, lane = threadIdx.x & 31;
   for (int blk = threadIdx.x >> 5; blk < nb; blk += blockDim.x >> 5) {
     const int i = blk * 32 + lane;
-    const float v = fmul(fmul(xs[i], s), nw[i]);
+    const float v = fmul(fmul(xs[i], s), ws[i]);
     if (xn) xn[(long)bi * k + i] = v;
     q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
   }
@@ -323,10 +327,36 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st) {
-  const size_t smem = (size_t)k * 4;
+  const size_t smem = (size_t)3 * ((k + 15) & ~15) * 4;
   cudaError_t e = set_smem(k_rmsnorm_q8, smem);
   if (e != cudaSuccess) return e;
   return launch(k_rmsnorm_q8, dim3(b), dim3(256), smem, st, x, nw, eps, k, act, xn);
+}
+
+// SwiGLU (model.rs:1105-1115: h = g / (1 + exp(-g)) * u) of token-major g, u [b][k], then Q8 of
+// the product; h (optional) gets the floats.  One warp per 32-element block.
+__global__ void k_swiglu_q8(const float *__restrict__ g, const float *__restrict__ u, int k, int b, Q8Dev act,
+                            float *__restrict__ h) {
+  pdl_trigger();
+  pdl_wait();
+  const int nb = k >> 5, lane = threadIdx.x & 31;
+  const long nwarp_total = (long)b * nb;
+  const long wstride = ((long)gridDim.x * blockDim.x) >> 5;
+  for (long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; w < nwarp_total; w += wstride) {
+    const int bi = (int)(w / nb), blk = (int)(w - (long)bi * nb);
+    const long i = (long)bi * k + blk * 32 + lane;
+    const float gg = g[i];
+    const float v = fmul(fdiv(gg, fadd(1.0f, expf_lib(-gg))), u[i]);
+    if (h) h[i] = v;
+    q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
+  }
+}
+
+cudaError_t launch_swiglu_q8(const float *g, const float *u, int k, int b, Q8Dev act, float *h, cudaStream_t st) {
+  if (k % 32 != 0 || b < 1) return cudaErrorInvalidValue;
+  long warps = (long)b * (k / 32);
+  int grid = (int)std::min<long>((warps * 32 + 255) / 256, (long)num_sms() * 8);
+  return launch(k_swiglu_q8, dim3(std::max(grid, 1)), dim3(256), 0, st, g, u, k, b, act, h);
 }
 
 // ------------------------------------------------------------ matvec core
@@ -664,18 +694,22 @@ __global__ void __launch_bounds__(L_THREADS) k_mv_lanes(DevTensor W, Q8Dev act, 
 constexpr int MM_WARPS = 4;
 constexpr int MM_ROWS = 16;
 constexpr int MM_LANES = 8 * MM_WARPS;
-constexpr int MM_WBYTES = 40 * 1024;  // staged weight bytes per chunk (at most)
 
+// Integer tile products.  The accumulator starts at DOT_BIAS, the bit
+// pattern of 1.5 * 2^23, so each result is the float 12582912 + dot exactly
+// (|dot| < 2^20 here) and unbias() turns it into the float dot.
+constexpr int DOT_BIAS = 0x4B400000;
+__device__ __forceinline__ float unbias(int d) { return fsub(__int_as_float(d), 12582912.0f); }
 __device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(DOT_BIAS));
 }
 __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
   asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
-               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(DOT_BIAS));
 }
 __device__ __forceinline__ uint32_t ldg_u32(const int8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
 // Asynchronous global -> shared copies (completed by cp_async_wait_all).
@@ -697,32 +731,91 @@ template <> struct MmGeo<T_Q6_K> { static constexpr int BE = 256, QB = 208; stat
 template <> struct MmGeo<T_Q8_0> { static constexpr int BE = 32, QB = 32; static constexpr bool D = true; };
 template <> struct MmGeo<T_Q4_0> { static constexpr int BE = 32, QB = 16; static constexpr bool D = true; };
 
-// Storage blocks per staged chunk.
+// Lane stride (in float2) of the staged activation scales: odd, so the four
+// lane pairs a warp reads at once fall in different banks.
+__host__ __device__ inline int mm_lane_stride(int sbc) { return sbc | 1; }
+constexpr int MM_RELAY_BYTES = 4 * 32 * 16;  // one float4 per thread of each lane group
+// Storage blocks per staged chunk of a matrix of nblk blocks, so that the
+// chunk's rows and lane scales fit in smem_bytes of shared memory; Q8_0 /
+// Q4_0 chunks hold whole 8-block units.
 template <int T>
-__host__ __device__ constexpr int mm_chunk_blocks() {
-  return MM_WBYTES / (MM_ROWS * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)));
+__host__ __device__ inline int mm_nbc(int nblk, int smem_bytes) {
+  const int per_block = MM_ROWS * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)) + MM_LANES * (MmGeo<T>::BE / 32) * 8;
+  int n = (smem_bytes - MM_RELAY_BYTES - MM_LANES * 8) / per_block;
+  if (MmGeo<T>::BE == 32) n &= ~7;
+  return nblk < n ? nblk : n;
+}
+template <int T>
+__host__ __device__ inline size_t mm_smem_bytes(int nbc) {
+  return (size_t)MM_ROWS * nbc * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)) +
+         (size_t)MM_LANES * mm_lane_stride(nbc * MmGeo<T>::BE / 32) * 8 + MM_RELAY_BYTES;
 }
 
-template <int T>
-__global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act, float *out, long os_row, long os_lane,
-                                                           int add) {
+// Exact int -> float conversions on the integer/FP32 pipes: x + 1.5*2^23 as
+// a float bit pattern is exact for |x| < 2^22, and a byte placed under the
+// exponent of 2^23 is 2^23 + byte.
+__device__ __forceinline__ float dotf(int x) { return fsub(__int_as_float(x + 0x4B400000), 12582912.0f); }
+template <int B>
+__device__ __forceinline__ float bytef(uint32_t w) {  // byte B of w (a value below 256)
+  return fsub(__int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u + B)), 8388608.0f);
+}
+__device__ __forceinline__ uint2 ldg_u2(const int8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+// Named barriers 1 + s (s < 4) with immediate ids, so the kernel holds only
+// the barriers it uses.
+__device__ __forceinline__ void mm_bar_sync(int s, int n) {
+  switch (s) {
+    case 0: asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); break;
+    case 1: asm volatile("bar.sync 2, %0;" ::"r"(n) : "memory"); break;
+    case 2: asm volatile("bar.sync 3, %0;" ::"r"(n) : "memory"); break;
+    default: asm volatile("bar.sync 4, %0;" ::"r"(n) : "memory"); break;
+  }
+}
+__device__ __forceinline__ void mm_bar_arrive(int s, int n) {
+  switch (s) {
+    case 0: asm volatile("bar.arrive 1, %0;" ::"r"(n) : "memory"); break;
+    case 1: asm volatile("bar.arrive 2, %0;" ::"r"(n) : "memory"); break;
+    case 2: asm volatile("bar.arrive 3, %0;" ::"r"(n) : "memory"); break;
+    default: asm volatile("bar.arrive 4, %0;" ::"r"(n) : "memory"); break;
+  }
+}
+
+// One 16-row x 32-lane tile (row tile bx, lane tile blockIdx.y) of out = W * act.
+//
+// Work unit: eight consecutive float terms of every (row, lane) of the tile
+// (a Q4_K superblock, half a Q6_K superblock, eight Q8_0 / Q4_0 blocks).
+// Warp w is lane group lw = w % 4 (lanes 8lw .. 8lw+7) and k slice
+// ks = w / 4 of KS: units are dealt to the slices round robin, each slice
+// forms its unit's terms in registers, then adds them to the running sums
+// of the (row, lane) pairs, which pass from slice to slice through shared
+// memory (named barrier 1 + s is the hand-off into slice s).  So every sum
+// is still the reference's sequential one, term after term.
+//
+// Integer dots are independent of the order of the 32 products, so for
+// Q4_K / Q8_0 the k slots of a sub-block are permuted: thread t's A and B
+// fragment slots 4t..4t+3 and 16+4t..16+4t+3 carry elements 8t..8t+7 of
+// the weight row and of the activation lane (one 64-bit load each).
+template <int T, int KS>
+__device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, float *out, long os_row, long os_lane,
+                                        int add, int bx, int NBC, uint8_t *mm_smem) {
   using G = MmGeo<T>;
-  constexpr int NBC = mm_chunk_blocks<T>();            // storage blocks per chunk
-  constexpr int SBC = NBC * G::BE / 32;                // 32-element activation blocks per chunk
-  extern __shared__ __align__(16) uint8_t mm_smem[];
+  constexpr int UPB = T == T_Q6_K ? 2 : 1;             // units per storage block (K-quants)
+  constexpr bool KQ = G::BE == 256;
+  const int SBC = NBC * G::BE / 32;                     // 32-element activation blocks per chunk
+  const int LS = mm_lane_stride(SBC);
   uint8_t *wq = mm_smem;                                // [16 rows][NBC][QB]
   float *wd = (float *)(mm_smem + MM_ROWS * NBC * G::QB);  // [16 rows][NBC] (types with a separate d)
-  float *asd = (float *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][SBC] da
-  int *ass = (int *)(asd + MM_LANES * SBC);                                         // [32 lanes][SBC] sa
-  pdl_trigger();
-  pdl_wait();
+  float2 *asf = (float2 *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][LS] {da, sa}
+  float4 *relay = (float4 *)(asf + MM_LANES * LS);     // [4 lane groups][32]
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
-  const int r0 = blockIdx.x * MM_ROWS, nr = min(MM_ROWS, W.rows - r0);
+  const int lw = w & 3, ks = w >> 2;
+  const int r0 = bx * MM_ROWS, nr = min(MM_ROWS, W.rows - r0);
   const int L0 = blockIdx.y * MM_LANES, nl = min(MM_LANES, act.b - L0);
+  const int nact = (nl + 7) >> 3;                      // lane groups with lanes
+  const bool active = lw < nact;
   const int k = W.k, nblk = k / G::BE, nb32 = k >> 5;
-  const int lb = L0 + 8 * w + g;                       // lane of this thread's B fragment loads
-  const int lbc = min(lb, act.b - 1);
-  const int lc0 = 8 * w + 2 * t, lc1 = lc0 + 1;         // local lanes of this thread's accumulators
+  const int units = KQ ? nblk * UPB : (nblk + 7) >> 3;  // units of the whole row
+  const int lbc = min(L0 + 8 * lw + g, act.b - 1);     // lane of this thread's B fragment loads
+  const int lc0 = 8 * lw + 2 * t, lc1 = lc0 + 1;        // local lanes of this thread's accumulators
   const int8_t *aq = act.q + (long)lbc * k;
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};             // (row g, lc0), (g, lc1), (g + 8, lc0), (g + 8, lc1)
   const size_t row_q = (size_t)nblk * G::QB;
@@ -732,69 +825,78 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
     // stage: the tile's rows and the lanes' activation scales by asynchronous
     // copies (every copy in flight at once), the f16 row scales four loads at a time
     const int v16 = nbc * G::QB / 16;
-    for (int i = tid; i < nr * v16; i += 32 * MM_WARPS) {
+    for (int i = tid; i < nr * v16; i += 32 * MM_WARPS * KS) {
       const int r = i / v16, j = i - r * v16;
       cp_async16(wq + (size_t)r * NBC * G::QB + 16 * j, W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB + 16 * j);
     }
     const int s0 = c0 * (G::BE / 32), nsb = nbc * (G::BE / 32);
-    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS) {
+    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS * KS) {
       const int l = i / nsb, j = i - l * nsb;
       const long o = (long)(L0 + l) * nb32 + s0 + j;
-      cp_async4(asd + l * SBC + j, act.d + o);
-      cp_async4(ass + l * SBC + j, act.s + o);
+      cp_async4(&asf[l * LS + j].x, act.d + o);
+      cp_async4(&asf[l * LS + j].y, act.s + o);
     }
     if (G::D)
-      for (int i0 = tid; i0 < nr * nbc; i0 += 4 * 32 * MM_WARPS) {
+      for (int i0 = tid; i0 < nr * nbc; i0 += 4 * 32 * MM_WARPS * KS) {
         uint16_t hv[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          const int i = i0 + u * 32 * MM_WARPS, r = i / nbc, j = i - r * nbc;
+          const int i = i0 + u * 32 * MM_WARPS * KS, r = i / nbc, j = i - r * nbc;
           hv[u] = i < nr * nbc ? __ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j) : (uint16_t)0;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          const int i = i0 + u * 32 * MM_WARPS, r = i / nbc, j = i - r * nbc;
+          const int i = i0 + u * 32 * MM_WARPS * KS, r = i / nbc, j = i - r * nbc;
           if (i < nr * nbc) wd[r * NBC + j] = f16f(hv[u]);
         }
       }
     cp_async_wait_all();
+    // the block sums as floats (each thread converts the entries it copied)
+    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS * KS) {
+      const int l = i / nsb, j = i - l * nsb;
+      float *sp = &asf[l * LS + j].y;
+      *sp = (float)__float_as_int(*sp);
+    }
     __syncthreads();
-    if (8 * w >= nl) continue;  // no lanes for this warp (it still meets every barrier)
+    if (!active) continue;  // no lanes for this warp (it still meets every __syncthreads)
     const uint8_t *qa = wq + (size_t)g * NBC * G::QB, *qb = wq + (size_t)(g + 8) * NBC * G::QB;
-    const float *d0s = asd + lc0 * SBC, *d1s = asd + lc1 * SBC;
-    const int *s0s = ass + lc0 * SBC, *s1s = ass + lc1 * SBC;
-    auto ascale = [&](int sl, float2 &a0, float2 &a1) {  // {da, sa} of this thread's two lanes
-      a0 = make_float2(d0s[sl], (float)s0s[sl]);
-      a1 = make_float2(d1s[sl], (float)s1s[sl]);
-    };
-    // The activation fragments of one group (a K-quant superblock, or eight
-    // Q8_0/Q4_0 blocks: 16 words) are loaded one group ahead of their use.
-    constexpr int GB = G::BE == 256 ? 1 : 8;  // storage blocks per group
-    const int ngrp = (nbc + GB - 1) / GB;
-    auto load_b = [&](int gi, uint32_t (&bw)[16]) {
-      const int8_t *ap = aq + (size_t)(c0 + gi * GB) * G::BE;
+    const float2 *as0 = asf + lc0 * LS, *as1 = asf + lc1 * LS;
+    const int ubase = KQ ? c0 * UPB : c0 >> 3;            // global index of the chunk's first unit
+    const int nu = KQ ? nbc * UPB : (nbc + 7) >> 3;       // units in this chunk
+    // B fragments of unit u of this chunk (16 words; 8 for a Q6_K half)
+    auto load_b = [&](int u, uint32_t (&bw)[16]) {
       if (T == T_Q6_K) {
+        const int8_t *ap = aq + (size_t)(c0 + (u >> 1)) * 256 + (u & 1) * 128;
 #pragma unroll
-        for (int e = 0; e < 16; e++) bw[e] = ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t);  // piece (4h+s, g2)
+        for (int e = 0; e < 8; e++) bw[e] = ldg_u32(ap + (e & 3) * 32 + (e >> 2) * 16 + 4 * t);  // piece (4h+s, g2), e = 4 g2 + s
       } else if (T == T_Q4_K) {
+        const int8_t *ap = aq + (size_t)(c0 + u) * 256;
 #pragma unroll
-        for (int e = 0; e < 16; e++) bw[e] = ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t);  // sub-block e/2
+        for (int e = 0; e < 8; e++) {  // sub-block e, permuted slots
+          const uint2 v = ldg_u2(ap + e * 32 + 8 * t);
+          bw[2 * e] = v.x;
+          bw[2 * e + 1] = v.y;
+        }
       } else {
-        const int nv = min(GB, nbc - gi * GB);
+        const int8_t *ap = aq + (size_t)(c0 + 8 * u) * 32;
+        const int nv = min(8, nbc - 8 * u);
 #pragma unroll
-        for (int e = 0; e < 16; e++) bw[e] = (e >> 1) < nv ? ldg_u32(ap + (e >> 1) * 32 + (e & 1) * 16 + 4 * t) : 0u;
+        for (int e = 0; e < 8; e++) {
+          if (T == T_Q8_0) {
+            const uint2 v = e < nv ? ldg_u2(ap + e * 32 + 8 * t) : make_uint2(0u, 0u);
+            bw[2 * e] = v.x;
+            bw[2 * e + 1] = v.y;
+          } else {
+            bw[2 * e] = e < nv ? ldg_u32(ap + e * 32 + 4 * t) : 0u;
+            bw[2 * e + 1] = e < nv ? ldg_u32(ap + e * 32 + 16 + 4 * t) : 0u;
+          }
+        }
       }
     };
-    uint32_t bc[16], bn[16];
-    load_b(0, bc);
-    for (int gi = 0; gi < ngrp; gi++) {
-      if (gi + 1 < ngrp) load_b(gi + 1, bn);
-#pragma unroll
-    for (int ig = 0; ig < GB; ig++) {
-      const int i = gi * GB + ig;
-      if (i >= nbc) break;
-      const int blk = c0 + i;  // storage block
+    // the eight terms of unit u for this thread's four (row, lane) pairs
+    auto unit_terms = [&](int u, const uint32_t (&bc)[16], float (&tm)[8][4]) {
       if (T == T_Q4_K) {
+        const int i = u;
         const uint4 ha = *reinterpret_cast<const uint4 *>(qa + i * 144), hb = *reinterpret_cast<const uint4 *>(qb + i * 144);
         const float da_r = f16f((uint16_t)(ha.x & 0xFFFFu)), dm_r = f16f((uint16_t)(ha.x >> 16));
         const float db_r = f16f((uint16_t)(hb.x & 0xFFFFu)), dmb_r = f16f((uint16_t)(hb.x >> 16));
@@ -807,108 +909,151 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
         const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
 #pragma unroll
         for (int p = 0; p < 4; p++) {
-          const uint32_t wa0 = *reinterpret_cast<const uint32_t *>(qa + i * 144 + 16 + 32 * p + 4 * t);
-          const uint32_t wa1 = *reinterpret_cast<const uint32_t *>(qa + i * 144 + 32 + 32 * p + 4 * t);
-          const uint32_t wb0 = *reinterpret_cast<const uint32_t *>(qb + i * 144 + 16 + 32 * p + 4 * t);
-          const uint32_t wb1 = *reinterpret_cast<const uint32_t *>(qb + i * 144 + 32 + 32 * p + 4 * t);
+          const uint2 wa = *reinterpret_cast<const uint2 *>(qa + i * 144 + 16 + 32 * p + 8 * t);
+          const uint2 wb = *reinterpret_cast<const uint2 *>(qb + i * 144 + 16 + 32 * p + 8 * t);
 #pragma unroll
           for (int h = 0; h < 2; h++) {
             const int j = 2 * p + h, sl = i * 8 + j;
             const uint32_t M = 0x0F0F0F0Fu;
-            const uint32_t x0 = h ? (wa0 >> 4) & M : wa0 & M, x1 = h ? (wb0 >> 4) & M : wb0 & M;
-            const uint32_t x2 = h ? (wa1 >> 4) & M : wa1 & M, x3 = h ? (wb1 >> 4) & M : wb1 & M;
+            const uint32_t x0 = h ? (wa.x >> 4) & M : wa.x & M, x1 = h ? (wb.x >> 4) & M : wb.x & M;
+            const uint32_t x2 = h ? (wa.y >> 4) & M : wa.y & M, x3 = h ? (wb.y >> 4) & M : wb.y & M;
             int dot[4];
             mma_k32(dot, x0, x1, x2, x3, bc[2 * j], bc[2 * j + 1]);
-            float2 a0, a1;
-            ascale(sl, a0, a1);
-            const int sh = (j & 3) * 8;
+            const float2 a0 = as0[sl], a1 = as1[sl];
             const uint32_t sa_w = j < 4 ? sca_lo : sca_hi, ma_w = j < 4 ? ma_lo : ma_hi;
             const uint32_t sb_w = j < 4 ? scb_lo : scb_hi, mb_w = j < 4 ? mb_lo : mb_hi;
-            const float sca = (float)((sa_w >> sh) & 0xFFu), mma_ = (float)((ma_w >> sh) & 0xFFu);
-            const float scb = (float)((sb_w >> sh) & 0xFFu), mmb = (float)((mb_w >> sh) & 0xFFu);
-            acc[0] = fadd(acc[0], fsub(fmul(fmul(fmul(da_r, a0.x), sca), (float)dot[0]), fmul(fmul(fmul(a0.x, dm_r), mma_), a0.y)));
-            acc[1] = fadd(acc[1], fsub(fmul(fmul(fmul(da_r, a1.x), sca), (float)dot[1]), fmul(fmul(fmul(a1.x, dm_r), mma_), a1.y)));
-            acc[2] = fadd(acc[2], fsub(fmul(fmul(fmul(db_r, a0.x), scb), (float)dot[2]), fmul(fmul(fmul(a0.x, dmb_r), mmb), a0.y)));
-            acc[3] = fadd(acc[3], fsub(fmul(fmul(fmul(db_r, a1.x), scb), (float)dot[3]), fmul(fmul(fmul(a1.x, dmb_r), mmb), a1.y)));
+            float sca, mma_, scb, mmb;
+            switch (j & 3) {
+              case 0: sca = bytef<0>(sa_w); mma_ = bytef<0>(ma_w); scb = bytef<0>(sb_w); mmb = bytef<0>(mb_w); break;
+              case 1: sca = bytef<1>(sa_w); mma_ = bytef<1>(ma_w); scb = bytef<1>(sb_w); mmb = bytef<1>(mb_w); break;
+              case 2: sca = bytef<2>(sa_w); mma_ = bytef<2>(ma_w); scb = bytef<2>(sb_w); mmb = bytef<2>(mb_w); break;
+              default: sca = bytef<3>(sa_w); mma_ = bytef<3>(ma_w); scb = bytef<3>(sb_w); mmb = bytef<3>(mb_w); break;
+            }
+            tm[j][0] = fsub(fmul(fmul(fmul(da_r, a0.x), sca), unbias(dot[0])), fmul(fmul(fmul(a0.x, dm_r), mma_), a0.y));
+            tm[j][1] = fsub(fmul(fmul(fmul(da_r, a1.x), sca), unbias(dot[1])), fmul(fmul(fmul(a1.x, dm_r), mma_), a1.y));
+            tm[j][2] = fsub(fmul(fmul(fmul(db_r, a0.x), scb), unbias(dot[2])), fmul(fmul(fmul(a0.x, dmb_r), mmb), a0.y));
+            tm[j][3] = fsub(fmul(fmul(fmul(db_r, a1.x), scb), unbias(dot[3])), fmul(fmul(fmul(a1.x, dmb_r), mmb), a1.y));
           }
         }
       } else if (T == T_Q6_K) {
+        // half h of superblock i: pieces (sub-block 4h+s, 16-half g2) in the
+        // reference's order g2 = 0, 1, then s = 0..3 (quant_int.rs:380-405)
+        const int i = u >> 1, h = u & 1;
         const float dra = wd[g * NBC + i], drb = wd[(g + 8) * NBC + i];
         const uint8_t *ba = qa + i * 208, *bb = qb + i * 208;
+        const uint2 sa2 = *reinterpret_cast<const uint2 *>(ba + 192 + 8 * h);
+        const uint2 sb2 = *reinterpret_cast<const uint2 *>(bb + 192 + 8 * h);
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const uint2 sa2 = *reinterpret_cast<const uint2 *>(ba + 192 + 8 * h);
-          const uint2 sb2 = *reinterpret_cast<const uint2 *>(bb + 192 + 8 * h);
-          const unsigned long long swa = (unsigned long long)sa2.y << 32 | sa2.x;
-          const unsigned long long swb = (unsigned long long)sb2.y << 32 | sb2.x;
+        for (int g2 = 0; g2 < 2; g2++) {
+          const uint32_t la0 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + g2 * 16 + 4 * t);
+          const uint32_t la1 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + 32 + g2 * 16 + 4 * t);
+          const uint32_t lha = *reinterpret_cast<const uint32_t *>(ba + 128 + h * 32 + g2 * 16 + 4 * t);
+          const uint32_t lb0 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + g2 * 16 + 4 * t);
+          const uint32_t lb1 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + 32 + g2 * 16 + 4 * t);
+          const uint32_t lhb = *reinterpret_cast<const uint32_t *>(bb + 128 + h * 32 + g2 * 16 + 4 * t);
 #pragma unroll
-          for (int g2 = 0; g2 < 2; g2++) {
-            const uint32_t la0 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + g2 * 16 + 4 * t);
-            const uint32_t la1 = *reinterpret_cast<const uint32_t *>(ba + h * 64 + 32 + g2 * 16 + 4 * t);
-            const uint32_t lha = *reinterpret_cast<const uint32_t *>(ba + 128 + h * 32 + g2 * 16 + 4 * t);
-            const uint32_t lb0 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + g2 * 16 + 4 * t);
-            const uint32_t lb1 = *reinterpret_cast<const uint32_t *>(bb + h * 64 + 32 + g2 * 16 + 4 * t);
-            const uint32_t lhb = *reinterpret_cast<const uint32_t *>(bb + 128 + h * 32 + g2 * 16 + 4 * t);
-#pragma unroll
-            for (int s = 0; s < 4; s++) {
-              // quant_int.rs:386-394 unpacking, four bytes at a time, minus 32
-              auto unpack = [&](uint32_t l0w, uint32_t l1w, uint32_t hw) {
-                const uint32_t lo = s & 1 ? l1w : l0w;
-                const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) |
-                                   ((s == 0 ? hw << 4 : s == 1 ? hw << 2 : s == 2 ? hw : hw >> 2) & 0x30303030u);
-                return __vsub4(q, 0x20202020u);
-              };
-              int dot[4];
-              mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), bc[2 * (4 * h + s) + g2]);
-              float2 a0, a1;
-              ascale(i * 8 + 4 * h + s, a0, a1);
-              const float sca = (float)(int8_t)(uint8_t)(swa >> (8 * (g2 + 2 * s)));
-              const float scb = (float)(int8_t)(uint8_t)(swb >> (8 * (g2 + 2 * s)));
-              acc[0] = fadd(acc[0], fmul(fmul(fmul(dra, sca), a0.x), (float)dot[0]));
-              acc[1] = fadd(acc[1], fmul(fmul(fmul(dra, sca), a1.x), (float)dot[1]));
-              acc[2] = fadd(acc[2], fmul(fmul(fmul(drb, scb), a0.x), (float)dot[2]));
-              acc[3] = fadd(acc[3], fmul(fmul(fmul(drb, scb), a1.x), (float)dot[3]));
-            }
+          for (int s = 0; s < 4; s++) {
+            // quant_int.rs:386-394 unpacking, four bytes at a time, minus 32
+            auto unpack = [&](uint32_t l0w, uint32_t l1w, uint32_t hw) {
+              const uint32_t lo = s & 1 ? l1w : l0w;
+              const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) |
+                                 ((s == 0 ? hw << 4 : s == 1 ? hw << 2 : s == 2 ? hw : hw >> 2) & 0x30303030u);
+              return __vsub4(q, 0x20202020u);
+            };
+            int dot[4];
+            mma_k16(dot, unpack(la0, la1, lha), unpack(lb0, lb1, lhb), bc[4 * g2 + s]);
+            const float2 a0 = as0[i * 8 + 4 * h + s], a1 = as1[i * 8 + 4 * h + s];
+            // the signed scale byte (g2 + 2s) of this half, exactly, on the integer pipe
+            const int sh = 8 * (g2 + 2 * s);
+            const uint32_t swa = sh < 32 ? sa2.x : sa2.y, swb = sh < 32 ? sb2.x : sb2.y;
+            const float sca = dotf((int)(int8_t)(uint8_t)(swa >> (sh & 31)));
+            const float scb = dotf((int)(int8_t)(uint8_t)(swb >> (sh & 31)));
+            tm[4 * g2 + s][0] = fmul(fmul(fmul(dra, sca), a0.x), unbias(dot[0]));
+            tm[4 * g2 + s][1] = fmul(fmul(fmul(dra, sca), a1.x), unbias(dot[1]));
+            tm[4 * g2 + s][2] = fmul(fmul(fmul(drb, scb), a0.x), unbias(dot[2]));
+            tm[4 * g2 + s][3] = fmul(fmul(fmul(drb, scb), a1.x), unbias(dot[3]));
           }
         }
-      } else {  // Q8_0 / Q4_0: one 32-element block per storage block
-        const float dra = wd[g * NBC + i], drb = wd[(g + 8) * NBC + i];
-        uint32_t x0, x1, x2, x3;
-        if (T == T_Q8_0) {
-          x0 = *reinterpret_cast<const uint32_t *>(qa + i * 32 + 4 * t);
-          x2 = *reinterpret_cast<const uint32_t *>(qa + i * 32 + 16 + 4 * t);
-          x1 = *reinterpret_cast<const uint32_t *>(qb + i * 32 + 4 * t);
-          x3 = *reinterpret_cast<const uint32_t *>(qb + i * 32 + 16 + 4 * t);
-        } else {  // low nibbles = elements 0-15, high = 16-31
-          const uint32_t wa = *reinterpret_cast<const uint32_t *>(qa + i * 16 + 4 * t);
-          const uint32_t wb = *reinterpret_cast<const uint32_t *>(qb + i * 16 + 4 * t);
-          x0 = wa & 0x0F0F0F0Fu;
-          x2 = (wa >> 4) & 0x0F0F0F0Fu;
-          x1 = wb & 0x0F0F0F0Fu;
-          x3 = (wb >> 4) & 0x0F0F0F0Fu;
-        }
-        int dot[4];
-        mma_k32(dot, x0, x1, x2, x3, bc[2 * ig], bc[2 * ig + 1]);
-        float2 a0, a1;
-        ascale(i, a0, a1);
-        if (T == T_Q8_0) {  // quant_int.rs:291-296
-          acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), (float)dot[0]));
-          acc[1] = fadd(acc[1], fmul(fmul(dra, a1.x), (float)dot[1]));
-          acc[2] = fadd(acc[2], fmul(fmul(drb, a0.x), (float)dot[2]));
-          acc[3] = fadd(acc[3], fmul(fmul(drb, a1.x), (float)dot[3]));
-        } else {  // quant_int.rs:316-323
-          acc[0] = fadd(acc[0], fmul(fmul(dra, a0.x), fsub((float)dot[0], fmul(8.0f, a0.y))));
-          acc[1] = fadd(acc[1], fmul(fmul(dra, a1.x), fsub((float)dot[1], fmul(8.0f, a1.y))));
-          acc[2] = fadd(acc[2], fmul(fmul(drb, a0.x), fsub((float)dot[2], fmul(8.0f, a0.y))));
-          acc[3] = fadd(acc[3], fmul(fmul(drb, a1.x), fsub((float)dot[3], fmul(8.0f, a1.y))));
+      } else {  // Q8_0 / Q4_0: one 32-element block per term
+        const int nv = min(8, nbc - 8 * u);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          if (e >= nv) {  // past the row's last block: +0.0 terms (adding them is exact)
+            tm[e][0] = tm[e][1] = tm[e][2] = tm[e][3] = 0.0f;
+            continue;
+          }
+          const int i = 8 * u + e;
+          const float dra = wd[g * NBC + i], drb = wd[(g + 8) * NBC + i];
+          uint32_t x0, x1, x2, x3;
+          if (T == T_Q8_0) {  // permuted slots: elements 8t..8t+7
+            const uint2 wa = *reinterpret_cast<const uint2 *>(qa + i * 32 + 8 * t);
+            const uint2 wb = *reinterpret_cast<const uint2 *>(qb + i * 32 + 8 * t);
+            x0 = wa.x;
+            x2 = wa.y;
+            x1 = wb.x;
+            x3 = wb.y;
+          } else {  // low nibbles = elements 0-15, high = 16-31
+            const uint32_t wa = *reinterpret_cast<const uint32_t *>(qa + i * 16 + 4 * t);
+            const uint32_t wb = *reinterpret_cast<const uint32_t *>(qb + i * 16 + 4 * t);
+            x0 = wa & 0x0F0F0F0Fu;
+            x2 = (wa >> 4) & 0x0F0F0F0Fu;
+            x1 = wb & 0x0F0F0F0Fu;
+            x3 = (wb >> 4) & 0x0F0F0F0Fu;
+          }
+          int dot[4];
+          mma_k32(dot, x0, x1, x2, x3, bc[2 * e], bc[2 * e + 1]);
+          const float2 a0 = as0[i], a1 = as1[i];
+          if (T == T_Q8_0) {  // quant_int.rs:291-296
+            tm[e][0] = fmul(fmul(dra, a0.x), unbias(dot[0]));
+            tm[e][1] = fmul(fmul(dra, a1.x), unbias(dot[1]));
+            tm[e][2] = fmul(fmul(drb, a0.x), unbias(dot[2]));
+            tm[e][3] = fmul(fmul(drb, a1.x), unbias(dot[3]));
+          } else {  // quant_int.rs:316-323
+            tm[e][0] = fmul(fmul(dra, a0.x), fsub(unbias(dot[0]), fmul(8.0f, a0.y)));
+            tm[e][1] = fmul(fmul(dra, a1.x), fsub(unbias(dot[1]), fmul(8.0f, a1.y)));
+            tm[e][2] = fmul(fmul(drb, a0.x), fsub(unbias(dot[2]), fmul(8.0f, a0.y)));
+            tm[e][3] = fmul(fmul(drb, a1.x), fsub(unbias(dot[3]), fmul(8.0f, a1.y)));
+          }
         }
       }
-    }
+    };
+    const int nbar = 64 * nact;  // one hand-off: the active lane groups' sender and receiver warps
+    int u = ((ks - ubase) % KS + KS) % KS;  // this slice's first unit of the chunk
+    // With four slices (one CTA per SM, registers to spare) each unit's B
+    // fragments are loaded one unit ahead; with fewer, the other resident
+    // warps cover the load.
+    constexpr bool AHEAD = KS == 4;
+    uint32_t bc[16], bn[16];
+    if (AHEAD && u < nu) load_b(u, bc);
+    for (; u < nu; u += KS) {
+      if (AHEAD && u + KS < nu) load_b(u + KS, bn);
+      if (!AHEAD) load_b(u, bc);
+      float tm[8][4];
+      unit_terms(u, bc, tm);
+      const int gu = ubase + u;
+      if (KS > 1 && gu > 0) {  // take the running sums from the previous unit's slice
+        mm_bar_sync(ks, nbar);
+        const float4 r = relay[lw * 32 + lane];
+        acc[0] = r.x; acc[1] = r.y; acc[2] = r.z; acc[3] = r.w;
+      }
 #pragma unroll
-      for (int e = 0; e < 16; e++) bc[e] = bn[e];
+      for (int j = 0; j < 8; j++) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[e] = fadd(acc[e], tm[j][e]);
+      }
+      if (KS > 1 && gu + 1 < units) {  // and hand them to the next unit's slice
+        relay[lw * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        mm_bar_arrive((ks + 1) % KS, nbar);
+      }
+      if (AHEAD) {
+#pragma unroll
+        for (int e = 0; e < 16; e++) bc[e] = bn[e];
+      }
     }
   }
+  // the slice of the last unit holds the final sums:
   // out = 0.0 + acc (Pool::matmul zero-fills, then adds), or x += that
+  if (!active || ks != (units - 1) % KS) return;
 #pragma unroll
   for (int e = 0; e < 4; e++) {
     const int r = g + (e >> 1) * 8, l = (e & 1) ? lc1 : lc0;
@@ -920,27 +1065,96 @@ __global__ void __launch_bounds__(32 * MM_WARPS) k_mv_mma(DevTensor W, Q8Dev act
   }
 }
 
-template <int T>
-static cudaError_t launch_mv_mma_t(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
-                                   cudaStream_t st) {
-  constexpr int NBC = mm_chunk_blocks<T>();
-  const size_t smem = (size_t)MM_ROWS * NBC * (MmGeo<T>::QB + (MmGeo<T>::D ? 4 : 0)) +
-                      (size_t)MM_LANES * (NBC * MmGeo<T>::BE / 32) * 8;
-  cudaError_t e = set_smem(k_mv_mma<T>, smem);
-  if (e != cudaSuccess) return e;
-  const dim3 grid((w.rows + MM_ROWS - 1) / MM_ROWS, (act.b + MM_LANES - 1) / MM_LANES);
-  return launch(k_mv_mma<T>, grid, dim3(32 * MM_WARPS), smem, st, w, act, out, os_row, os_lane, add ? 1 : 0);
+// Up to three matrices against one activation in one launch (q/k/v,
+// gate/up): CTA x-index ranges [cta0, next cta0) belong to segment s.
+struct MvSeg {
+  DevTensor W;
+  float *out;
+  long os_row, os_lane;
+  int add, cta0, nbc;
+};
+constexpr int MV_MAX_SEGS = 3;
+struct MvSegs {
+  MvSeg s[MV_MAX_SEGS];
+  int n;
+};
+
+template <int KS>
+__global__ void __launch_bounds__(32 * MM_WARPS * KS, KS == 1 ? 5 : 1) k_mv_mma(MvSegs ss, Q8Dev act) {
+  extern __shared__ __align__(16) uint8_t mm_smem[];
+  pdl_trigger();
+  pdl_wait();
+  const int bx = blockIdx.x;
+  const MvSeg &S = (ss.n > 2 && bx >= ss.s[2].cta0) ? ss.s[2] : (ss.n > 1 && bx >= ss.s[1].cta0) ? ss.s[1] : ss.s[0];
+  const int tb = bx - S.cta0;
+  switch (S.W.type) {
+    case T_Q4_K: mv_tile<T_Q4_K, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    case T_Q6_K: mv_tile<T_Q6_K, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    case T_Q8_0: mv_tile<T_Q8_0, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    default: mv_tile<T_Q4_0, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+  }
+}
+
+// Blocks per chunk and shared memory of one matrix for a weight budget.
+static int mv_seg_nbc(const DevTensor &w, int wbytes) {
+  switch (w.type) {
+    case T_Q4_K: return mm_nbc<T_Q4_K>(w.k / 256, wbytes);
+    case T_Q6_K: return mm_nbc<T_Q6_K>(w.k / 256, wbytes);
+    case T_Q8_0: return mm_nbc<T_Q8_0>(w.k / 32, wbytes);
+    default: return mm_nbc<T_Q4_0>(w.k / 32, wbytes);
+  }
+}
+static size_t mv_seg_smem(const DevTensor &w, int nbc) {
+  switch (w.type) {
+    case T_Q4_K: return mm_smem_bytes<T_Q4_K>(nbc);
+    case T_Q6_K: return mm_smem_bytes<T_Q6_K>(nbc);
+    case T_Q8_0: return mm_smem_bytes<T_Q8_0>(nbc);
+    default: return mm_smem_bytes<T_Q4_0>(nbc);
+  }
+}
+
+// Slices per tile: four when the tiles are at most one per SM (a 16-warp CTA
+// per SM with a larger staged chunk), else plain 4-warp tiles.
+cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st) {
+  if (n < 1 || n > MV_MAX_SEGS || act.b < 1) return cudaErrorInvalidValue;
+  int tiles = 0;
+  for (int i = 0; i < n; i++) {
+    const MvOut &o = outs[i];
+    if (!type_is_matvec(o.w.type) || act.k != o.w.k || o.w.rows < 1) return cudaErrorInvalidValue;
+    tiles += (o.w.rows + MM_ROWS - 1) / MM_ROWS;
+  }
+  const int lane_tiles = (act.b + MM_LANES - 1) / MM_LANES, sms = num_sms();
+  const long ctas = (long)tiles * lane_tiles;
+  const int KS = ctas <= sms ? 4 : 1;
+  // shared memory per CTA: one CTA per SM (KS 4), five (KS 1)
+  const int wbytes = KS == 4 ? 200 * 1024 : 44 * 1024;
+  MvSegs ss{};
+  ss.n = n;
+  int cta = 0;
+  size_t smem = 0;
+  for (int i = 0; i < n; i++) {
+    const MvOut &o = outs[i];
+    const int nbc = mv_seg_nbc(o.w, wbytes);
+    ss.s[i] = MvSeg{o.w, o.out, o.os_row, o.os_lane, o.add ? 1 : 0, cta, nbc};
+    cta += (o.w.rows + MM_ROWS - 1) / MM_ROWS;
+    smem = std::max(smem, mv_seg_smem(o.w, nbc));
+  }
+  const dim3 grid(tiles, lane_tiles);
+  cudaError_t e;
+  switch (KS) {
+    case 4:
+      if ((e = set_smem(k_mv_mma<4>, smem)) != cudaSuccess) return e;
+      return launch(k_mv_mma<4>, grid, dim3(32 * MM_WARPS * 4), smem, st, ss, act);
+    default:
+      if ((e = set_smem(k_mv_mma<1>, smem)) != cudaSuccess) return e;
+      return launch(k_mv_mma<1>, grid, dim3(32 * MM_WARPS), smem, st, ss, act);
+  }
 }
 
 cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
                             cudaStream_t st) {
-  if (!type_is_matvec(w.type) || act.k != w.k || act.b < 1) return cudaErrorInvalidValue;
-  switch (w.type) {
-    case T_Q4_K: return launch_mv_mma_t<T_Q4_K>(w, act, out, os_row, os_lane, add, st);
-    case T_Q6_K: return launch_mv_mma_t<T_Q6_K>(w, act, out, os_row, os_lane, add, st);
-    case T_Q8_0: return launch_mv_mma_t<T_Q8_0>(w, act, out, os_row, os_lane, add, st);
-    default: return launch_mv_mma_t<T_Q4_0>(w, act, out, os_row, os_lane, add, st);
-  }
+  const MvOut o{w, out, os_row, os_lane, add};
+  return launch_mv_multi(1, &o, act, st);
 }
 
 // ------------------------------------------------------------ RoPE + KV, SwiGLU
@@ -1082,7 +1296,15 @@ __global__ void k_attn(AttnArgs a, int dot8) {
     s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
   }
   __syncthreads();
-  if (tid < dh) a.out[hb * dh + tid] = fmul(acc, s_inv);
+  if (tid < dh) {
+    const float o = fmul(acc, s_inv);
+    a.out[hb * dh + tid] = o;
+    if (a.q8.q) {  // dh % 32 == 0: warp w holds block (h * dh + 32 w) / 32 of the token's row
+      const int qk = a.n_head * dh, blk = (h * dh + tid) >> 5;
+      q8_block_lane(o, tid & 31, a.q8.q + (long)bi * qk + blk * 32, a.q8.d + (long)bi * (qk >> 5) + blk,
+                    a.q8.s + (long)bi * (qk >> 5) + blk);
+    }
+  }
 }
 
 // Chunk attention (b > 1): the same arithmetic as k_attn's b > 1 branch, one
@@ -1225,16 +1447,42 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
     }
     __syncthreads();
   }
-  if (vact && t0 + vt < a.b) {
+  const bool valid = vact && t0 + vt < a.b;
+  const long bi = t0 + vt;
+  float o0 = 0.0f, o1 = 0.0f;
+  if (valid) {
     const float inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
-    float *o = a.out + ((long)(t0 + vt) * a.n_head + h) * dh + 2 * vd;
-    o[0] = fmul(acc0, inv);
-    o[1] = fmul(acc1, inv);
+    float *o = a.out + (bi * a.n_head + h) * dh + 2 * vd;
+    o0 = fmul(acc0, inv);
+    o1 = fmul(acc1, inv);
+    o[0] = o0;
+    o[1] = o1;
+  }
+  if (a.q8.q) {
+    // dh % 32 == 0, so each half warp holds one 32-element block of one
+    // token's row, or no valid token at all (it still takes part in the
+    // shuffles, which stay inside the half warp, and stores nothing).
+    const int qk = a.n_head * dh, blk = (h * dh + 2 * vd) >> 5;
+    const long qo = valid ? bi * qk + blk * 32 : 0, so = valid ? bi * (qk >> 5) + blk : 0;
+    q8_block_pair(o0, o1, tid & 15, valid, a.q8.q + qo, a.q8.d + so, a.q8.s + so);
   }
 }
 
+static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
+  if (a.q8.q && a.dh % 32 != 0) {  // quantise separately
+    AttnArgs b = a;
+    b.q8 = Q8Dev{};
+    cudaError_t e = launch_attention_k(b, st);
+    if (e != cudaSuccess) return e;
+    return launch_q8(a.out, 1, (long)a.n_head * a.dh, a.n_head * a.dh, a.b, a.q8, st);
+  }
+  return launch_attention_k(a, st);
+}
+
+static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
   if (a.b > 1 && a.n_ctx % 4 == 0 && (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
     const size_t smem = ac_smem(a.dh);
     cudaError_t e = set_smem(k_attn_chunk, smem);

@@ -47,9 +47,20 @@ cudaError_t launch_q8(const float *x, long xs_elem, long xs_lane, int k, int b, 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st);
 
+// SwiGLU + Q8 of token-major g, u [b][k]; h (optional) gets the floats.
+cudaError_t launch_swiglu_q8(const float *g, const float *u, int k, int b, Q8Dev act, float *h, cudaStream_t st);
+
 // Multi-lane matvec: out[r * os_row + lane * os_lane] (+)= row r . lane.
 cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane,
                             bool add, cudaStream_t st);
+// Several matrices (at most three) against the same activation in one launch.
+struct MvOut {
+  DevTensor w;
+  float *out;
+  long os_row, os_lane;
+  bool add;
+};
+cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st);
 
 // Single-lane matvec with the activation quantised inside each CTA:
 // src = x (k floats, optionally RMS-normalised by nw) or a precomputed Q8 act.
@@ -97,6 +108,7 @@ struct AttnArgs {
   int b, n_head, n_kv, dh, n_ctx;
   float scale;
   float *scores;       // scratch [b][n_head][n_ctx]
+  Q8Dev q8{};          // optional (q8.q != nullptr): Q8 of out, k = n_head * dh
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 

@@ -144,6 +144,26 @@ def test_chunk_attention_equals_per_token_kernel(pk, paths, name):
     assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
 
 
+@pytest.mark.parametrize("name,n", [("tiny", 150), ("q8down", 129), ("q40", 97)])
+def test_prefill_lanes_equal_chunk_order(pk, paths, name, n):
+    """generate() runs a prompt's chunks on two alternating lanes (chunk c + 1
+    waiting only for chunk c's K/V of each layer); the prefill logits are the
+    same bits as forward() over the chunks one after another (n = 129 ends
+    with a one-token chunk)."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(29, n, spec.n_vocab)
+    a = pk.Engine(paths[name], n_ctx=256)
+    r = a.generate(prompt, 0, stop_at_eog=False)
+    assert r["prefill_tokens"] == n and r["gen_tokens"] == 0
+    b = pk.Engine(paths[name], n_ctx=256)
+    for lo in range(0, n, 32):
+        hi = min(n, lo + 32)
+        b.forward(prompt[lo:hi], np.arange(lo, hi), hi == n)
+    assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
+    # and the decode that follows is unchanged
+    assert a.decode_steps_device(8) == b.decode_steps_device(8)
+
+
 def test_bounded_wait_runs_out_and_engine_recovers(pk, paths):
     """Failure detection without a GPU fault: one persistent-kernel launch
     whose phase inputs never arrive (its readers wait for a tag nothing

@@ -95,6 +95,20 @@ def test_matvec_bitexact(pk, oracle, t, b):
 
 
 @pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("k,rows,b", [(16384, 96, 32), (4096, 3072, 32), (4096, 8192, 20)])
+def test_matvec_lanes_slices_and_chunks(pk, oracle, t, k, rows, b):
+    """Multi-lane matvec with each tile's k range split over four warps
+    (few tiles) or kept in one (many tiles), rows staged in one or several
+    chunks: bit-identical to the reference order in every case."""
+    w = random_rows(t, k, rows, 3000 + t + rows)
+    x = synth.normal_f32(4000 + k, k * b)
+    act_gpu, *_ = gpu_q8(pk, x, k, b)
+    want = oracle_matmul(oracle, t, w, k, rows, oracle.Q8Act(x, k, b))
+    got = pk.matmul(t, dev(w), k, rows, act_gpu).cpu().numpy()
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("t", TYPES)
 def test_matvec_fully_random_bytes(pk, oracle, t):
     """Every byte random (scales included), as in tests/quant_layout.rs:242-286."""
     k, rows, b = 512, 64, 4
