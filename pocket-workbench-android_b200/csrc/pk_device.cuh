@@ -189,6 +189,54 @@ __device__ __forceinline__ void q8_block_lane(float v, int lane, int8_t *q, floa
   }
 }
 
+// q8_block_lane for N independent blocks at once (one value per lane of
+// each), their shuffles interleaved so the latencies overlap.  ok[j] must be
+// the same on every lane (a block the warp skips still takes part in the
+// shuffles and stores nothing).
+template <int N>
+__device__ __forceinline__ void q8_blocks_lane(const float (&v)[N], const bool (&ok)[N], int lane, int8_t *const (&q)[N],
+                                               float *const (&d)[N], int32_t *const (&sum)[N]) {
+  float amax[N];
+#pragma unroll
+  for (int j = 0; j < N; j++) {
+    const float a = fabsf(v[j]);
+    amax[j] = a > 0.0f ? a : 0.0f;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+      const float w = __shfl_xor_sync(0xffffffffu, amax[j], o);
+      amax[j] = w > amax[j] ? w : amax[j];
+    }
+  }
+  int iv[N];
+  float dd[N];
+#pragma unroll
+  for (int j = 0; j < N; j++) {
+    dd[j] = fdiv(amax[j], 127.0f);
+    const float inv = dd[j] > 0.0f ? fdiv(1.0f, dd[j]) : 0.0f;
+    float r = roundf(fmul(v[j], inv));
+    r = r < -127.0f ? -127.0f : r;
+    r = r > 127.0f ? 127.0f : r;
+    iv[j] = isnan(r) ? 0 : (int)r;
+    if (ok[j]) q[j][lane] = (int8_t)iv[j];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int j = 0; j < N; j++) iv[j] += __shfl_xor_sync(0xffffffffu, iv[j], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if (ok[j]) {
+        *d[j] = dd[j];
+        *sum[j] = iv[j];
+      }
+  }
+}
+
 // q8_block_lane for a 32-element block held two values per lane by the
 // sixteen lanes of a half warp (l16 = lane within the half; both halves of
 // the warp run it together, each on its own block): value 2*l16 + e is

@@ -41,15 +41,19 @@ Engine::~Engine() {
   cudaFreeHost(h_ids_);
   cudaFreeHost(h_pos_);
   cudaFreeHost(h_tok_);
-  if (lane_[1].st) cudaStreamSynchronize(lane_[1].st);
-  cudaFree(d_lane1_arena_);
+  for (int i = 1; i < NLANES; i++) {
+    if (lane_[i].st) cudaStreamSynchronize(lane_[i].st);
+    cudaFree(d_lane_arena_[i]);
+  }
   cudaFreeHost(h_pids_);
   cudaFreeHost(h_ppos_);
   for (auto &v : kv_ev_)
     for (cudaEvent_t e : v) cudaEventDestroy(e);
   if (fork_ev_) cudaEventDestroy(fork_ev_);
-  if (join_ev_) cudaEventDestroy(join_ev_);
-  if (lane_[1].st) cudaStreamDestroy(lane_[1].st);
+  for (cudaEvent_t e : join_ev_)
+    if (e) cudaEventDestroy(e);
+  for (int i = 1; i < NLANES; i++)
+    if (lane_[i].st) cudaStreamDestroy(lane_[i].st);
   if (st_) cudaStreamDestroy(st_);
 }
 
@@ -321,7 +325,7 @@ int Engine::load(const char *path) {
   d_ids_ = (uint32_t *)take(); d_pos_ = (int *)take(); d_tok_ = (uint32_t *)take(); d_hist_ = (uint32_t *)take();
   d_step_ = (int *)take();
 
-  // prefill lanes (lane 1: a second set of per-chunk scratch and a stream)
+  // prefill lanes (lanes 1.. : their own per-chunk scratch and stream)
   lane_[0].st = st_;
   lane_[0].x = x_; lane_[0].q = q_; lane_[0].k = k_; lane_[0].v = v_; lane_[0].attn = attn_;
   lane_[0].gate = gate_; lane_[0].up = up_; lane_[0].h = h_; lane_[0].scores = att_scores_;
@@ -332,28 +336,30 @@ int Engine::load(const char *path) {
                                     B * (kmax / 32) * 4, B * H * n_ctx_ * 4, 64 * 4, 64 * 4};
     size_t a1 = 0;
     for (size_t v : s1) a1 += a256(v);
-    PK_CK(cudaMalloc((void **)&d_lane1_arena_, a1));
-    PK_CK(cudaMemsetAsync(d_lane1_arena_, 0, a1, st_));
-    uint8_t *p1 = d_lane1_arena_;
-    size_t i1 = 0;
-    auto take1 = [&]() {
-      uint8_t *r = p1;
-      p1 += a256(s1[i1++]);
-      return r;
-    };
-    Lane &L = lane_[1];
-    L.x = (float *)take1(); L.q = (float *)take1(); L.k = (float *)take1(); L.v = (float *)take1();
-    L.attn = (float *)take1(); L.gate = (float *)take1(); L.up = (float *)take1(); L.h = (float *)take1();
-    L.act = act_;
-    L.act.q = (int8_t *)take1(); L.act.d = (float *)take1(); L.act.s = (int32_t *)take1();
-    L.scores = (float *)take1(); L.ids = (uint32_t *)take1(); L.pos = (int *)take1();
-    PK_CK(cudaStreamCreateWithFlags(&L.st, cudaStreamNonBlocking));
+    for (int li = 1; li < NLANES; li++) {
+      PK_CK(cudaMalloc((void **)&d_lane_arena_[li], a1));
+      PK_CK(cudaMemsetAsync(d_lane_arena_[li], 0, a1, st_));
+      uint8_t *p1 = d_lane_arena_[li];
+      size_t i1 = 0;
+      auto take1 = [&]() {
+        uint8_t *r = p1;
+        p1 += a256(s1[i1++]);
+        return r;
+      };
+      Lane &L = lane_[li];
+      L.x = (float *)take1(); L.q = (float *)take1(); L.k = (float *)take1(); L.v = (float *)take1();
+      L.attn = (float *)take1(); L.gate = (float *)take1(); L.up = (float *)take1(); L.h = (float *)take1();
+      L.act = act_;
+      L.act.q = (int8_t *)take1(); L.act.d = (float *)take1(); L.act.s = (int32_t *)take1();
+      L.scores = (float *)take1(); L.ids = (uint32_t *)take1(); L.pos = (int *)take1();
+      PK_CK(cudaStreamCreateWithFlags(&L.st, cudaStreamNonBlocking));
+    }
     for (auto &v : kv_ev_) {
       v.resize(c.n_layer);
       for (auto &e : v) PK_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
     PK_CK(cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming));
-    PK_CK(cudaEventCreateWithFlags(&join_ev_, cudaEventDisableTiming));
+    for (auto &e : join_ev_) PK_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     PK_CK(cudaHostAlloc((void **)&h_pids_, (size_t)n_ctx_ * sizeof(uint32_t), cudaHostAllocDefault));
     PK_CK(cudaHostAlloc((void **)&h_ppos_, (size_t)n_ctx_ * sizeof(int), cudaHostAllocDefault));
   }
@@ -558,7 +564,7 @@ static double mat_stream_bytes(const DevTensor &w) {
 // Reads ids/positions from the lane's device buffers, so a b == 1 pass
 // (lane 0) can be captured once as a CUDA graph.  kv & KV_RECORD: record
 // kv_ev_[li][l] once layer l's K/V are written; kv & KV_WAIT: layer l's
-// attention first waits for the other lane's kv_ev_ of layer l.
+// attention first waits for the previous lane's kv_ev_ of layer l.
 int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, int kv) {
   const Lane &S = lane_[li];
   const Config &c = cfg_;
@@ -589,7 +595,7 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, i
            launch_qkv_b1(qa, S.st));
       if (l == 0) dump("Qrope-0", S.q, (size_t)qdim);
       if (kv & KV_RECORD) PK_CK(cudaEventRecord(kv_ev_[li][l], S.st));
-      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(S.st, kv_ev_[1 - li][l], 0));
+      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(S.st, kv_ev_[(li + NLANES - 1) % NLANES][l], 0));
       PROF("k_attn", 2.0 * c.n_head_kv * kv_pos * dh * f4 + 2 * qdim * f4, launch_attention(at, S.st));
       B1Src so;
       so.x = S.attn;
@@ -614,7 +620,7 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, i
                            n_ctx_, kc, vc, st));
       if (kv & KV_RECORD) PK_CK(cudaEventRecord(kv_ev_[li][l], st));
       if (l == 0) dump("Qrope-0", S.q, (size_t)b * qdim);
-      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(st, kv_ev_[1 - li][l], 0));
+      if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(st, kv_ev_[(li + NLANES - 1) % NLANES][l], 0));
       a.k = qdim;
       AttnArgs atq = at;
       atq.q8 = a;  // the attention kernel also writes Q8 of its output
@@ -744,9 +750,9 @@ int Engine::argmax(uint32_t *tok) {
   return PK_OK;
 }
 
-// The prompt's chunks [off, n) (chunk tokens each) on alternate prefill
-// lanes: chunk c + 1 runs its layer l while chunk c is still in later
-// layers, waiting only for chunk c's K/V of layer l before its attention.
+// The prompt's chunks [off, n) (chunk tokens each) on the prefill lanes in
+// turn: chunk c + 1 runs its layer l while chunk c is still in later layers,
+// waiting only for chunk c's K/V of layer l before its attention.
 // Every kernel sees the same inputs as in chunk order, so the results are
 // the same bits.  Returns with both lanes idle.
 int Engine::prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, bool *stopped) {
@@ -760,7 +766,7 @@ int Engine::prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, boo
   }
   have_logits_ = false;
   PK_CK(cudaEventRecord(fork_ev_, st_));
-  PK_CK(cudaStreamWaitEvent(lane_[1].st, fork_ev_, 0));
+  for (int i = 1; i < NLANES; i++) PK_CK(cudaStreamWaitEvent(lane_[i].st, fork_ev_, 0));
   int rc = PK_OK;
   cudaError_t e = cudaSuccess;
   for (int o = off, c = 0; o < n; o += chunk, c++) {
@@ -768,18 +774,21 @@ int Engine::prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, boo
       *stopped = true;
       break;
     }
-    const int m = std::min(chunk, n - o), li = c & 1;
+    const int m = std::min(chunk, n - o), li = c % NLANES;
     const Lane &L = lane_[li];
     e = cudaMemcpyAsync(L.ids, h_pids_ + o, m * sizeof(uint32_t), cudaMemcpyHostToDevice, L.st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(L.pos, h_ppos_ + o, m * sizeof(int), cudaMemcpyHostToDevice, L.st);
     if (e != cudaSuccess) break;
     if ((rc = enqueue_forward(m, o + m >= n, true, li, KV_RECORD | (c > 0 ? KV_WAIT : 0)))) break;
   }
-  // lane 1 joins lane 0, then both are drained
-  cudaError_t ej = cudaEventRecord(join_ev_, lane_[1].st);
-  if (ej == cudaSuccess) ej = cudaStreamWaitEvent(st_, join_ev_, 0);
+  // the other lanes join lane 0, then all are drained
+  cudaError_t ej = cudaSuccess;
+  for (int i = 1; i < NLANES; i++) {
+    if (ej == cudaSuccess) ej = cudaEventRecord(join_ev_[i], lane_[i].st);
+    if (ej == cudaSuccess) ej = cudaStreamWaitEvent(st_, join_ev_[i], 0);
+  }
   const cudaError_t es = cudaStreamSynchronize(st_);
-  cudaStreamSynchronize(lane_[1].st);
+  for (int i = 1; i < NLANES; i++) cudaStreamSynchronize(lane_[i].st);
   if (rc) return rc;
   if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync (prefill ids)");
   if (ej != cudaSuccess) return cuda_error(ej, "prefill lane join");
@@ -821,7 +830,7 @@ int Engine::generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_
   int off = (int)reused;
   bool user_stop = false;
   std::vector<int> positions(chunk);
-  if (!dbg_on_ && n - off > chunk) {  // two or more chunks: alternate lanes
+  if (!dbg_on_ && n - off > chunk) {  // two or more chunks: lanes in turn
     bool stopped = false;
     const int rc = prefill_lanes(prompt, n, off, chunk, &stopped);
     if (rc && !g_stop.load()) {

@@ -89,8 +89,8 @@ class Engine {
   int *h_pos_ = nullptr;
 
   // Prefill lanes: the scratch of one chunk's forward pass and the stream it
-  // runs on.  Lane 0 is the buffers above and st_; lane 1 has its own, so
-  // consecutive chunks of a prompt run on alternate lanes, chunk c + 1's
+  // runs on.  Lane 0 is the buffers above and st_; the others have their
+  // own, so consecutive chunks of a prompt run on lanes in turn, chunk c + 1's
   // layer l waiting only for chunk c's K/V of layer l (kv_ev_).
   struct Lane {
     cudaStream_t st = nullptr;
@@ -100,10 +100,11 @@ class Engine {
     uint32_t *ids = nullptr;
     int *pos = nullptr;
   };
-  Lane lane_[2];
-  uint8_t *d_lane1_arena_ = nullptr;
-  std::vector<cudaEvent_t> kv_ev_[2];
-  cudaEvent_t fork_ev_ = nullptr, join_ev_ = nullptr;
+  static constexpr int NLANES = 3;
+  Lane lane_[NLANES];
+  uint8_t *d_lane_arena_[NLANES] = {};
+  std::vector<cudaEvent_t> kv_ev_[NLANES];
+  cudaEvent_t fork_ev_ = nullptr, join_ev_[NLANES] = {};
   uint32_t *h_pids_ = nullptr;  // pinned prompt ids / positions, n_ctx each
   int *h_ppos_ = nullptr;
 

@@ -268,15 +268,13 @@ __device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
 }
 
 // Sum of squares in the reference's b > 1 order (model.rs:813-817): one
-// sequential unfused chain.  The squares are formed by every thread into
-// sq[] (zero-padded to a multiple of 16); thread 0 then adds them in order,
-// loading the next sixteen while it adds the current sixteen.  The padding
-// adds +0.0, exact for a sum that starts at +0.0.  Result broadcast through
+// sequential unfused chain over the squares sq[] (formed by every thread,
+// zero-padded to a multiple of 16).  Thread 0 adds them in order, loading
+// the next sixteen while it adds the current sixteen; the padding adds
+// +0.0, exact for a sum that starts at +0.0.  Result broadcast through
 // red[32].
-__device__ float sum_sq_seq_smem(const float *xs, float *sq, int n, float *red) {
+__device__ float sum_sq_chain(const float *sq, int n, float *red) {
   const int n16 = (n + 15) & ~15;
-  for (int i = threadIdx.x; i < n16; i += blockDim.x) sq[i] = i < n ? fmul(xs[i], xs[i]) : 0.0f;
-  __syncthreads();
   if (threadIdx.x == 0) {
     const float4 *s4 = reinterpret_cast<const float4 *>(sq);
     const int g = n16 / 16;
@@ -298,35 +296,56 @@ __device__ float sum_sq_seq_smem(const float *xs, float *sq, int n, float *red) 
 }
 
 // RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.  The
-// token's row and the norm weights are staged in shared memory first
-// (dynamic: x, w and the padded squares, 3 x k floats).
+// token's row, the norm weights and the squares are staged in shared
+// memory (dynamic, 3 x k floats, k a multiple of 32); each warp then
+// quantises its blocks three at a time.
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[40];
-  float *ws = xs + ((k + 15) & ~15), *sq = ws + ((k + 15) & ~15);
+  const int n16 = (k + 15) & ~15;
+  float *ws = xs + n16, *sq = ws + n16;
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
-  const float *xr = x + (long)bi * k;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    xs[i] = xr[i];
-    ws[i] = nw[i];
+  const float4 *x4 = reinterpret_cast<const float4 *>(x + (long)bi * k), *w4 = reinterpret_cast<const float4 *>(nw);
+  for (int i = threadIdx.x; i < n16 / 4; i += blockDim.x) {
+    const bool in = 4 * i < k;
+    const float4 v = in ? x4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (in) {
+      reinterpret_cast<float4 *>(xs)[i] = v;
+      reinterpret_cast<float4 *>(ws)[i] = w4[i];
+    }
+    reinterpret_cast<float4 *>(sq)[i] = make_float4(fmul(v.x, v.x), fmul(v.y, v.y), fmul(v.z, v.z), fmul(v.w, v.w));
   }
   __syncthreads();
-  const float ss = sum_sq_seq_smem(xs, sq, k, red);
+  const float ss = sum_sq_chain(sq, k, red);
   const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
-  const int nb = k >> 5, lane = threadIdx.x & 31;
-  for (int blk = threadIdx.x >> 5; blk < nb; blk += blockDim.x >> 5) {
-    const int i = blk * 32 + lane;
-    const float v = fmul(fmul(xs[i], s), ws[i]);
-    if (xn) xn[(long)bi * k + i] = v;
-    q8_block_lane(v, lane, act.q + (long)bi * k + blk * 32, act.d + (long)bi * nb + blk, act.s + (long)bi * nb + blk);
+  const int nb = k >> 5, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw_ = blockDim.x >> 5;
+  for (int b0 = w; b0 < nb; b0 += 3 * nw_) {
+    float v[3];
+    bool ok[3];
+    int8_t *qp[3];
+    float *dp[3];
+    int32_t *sp[3];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+      const int blk = b0 + j * nw_;
+      ok[j] = blk < nb;
+      const int bc = ok[j] ? blk : 0, i = bc * 32 + lane;
+      v[j] = fmul(fmul(xs[i], s), ws[i]);
+      if (ok[j] && xn) xn[(long)bi * k + i] = v[j];
+      qp[j] = act.q + (long)bi * k + bc * 32;
+      dp[j] = act.d + (long)bi * nb + bc;
+      sp[j] = act.s + (long)bi * nb + bc;
+    }
+    q8_blocks_lane<3>(v, ok, lane, qp, dp, sp);
   }
 }
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st) {
+  if (k % 32 != 0 || ((uintptr_t)x | (uintptr_t)nw) % 16 != 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)3 * ((k + 15) & ~15) * 4;
   cudaError_t e = set_smem(k_rmsnorm_q8, smem);
   if (e != cudaSuccess) return e;

@@ -146,7 +146,7 @@ def test_chunk_attention_equals_per_token_kernel(pk, paths, name):
 
 @pytest.mark.parametrize("name,n", [("tiny", 150), ("q8down", 129), ("q40", 97)])
 def test_prefill_lanes_equal_chunk_order(pk, paths, name, n):
-    """generate() runs a prompt's chunks on two alternating lanes (chunk c + 1
+    """generate() runs a prompt's chunks on stream lanes in turn (chunk c + 1
     waiting only for chunk c's K/V of each layer); the prefill logits are the
     same bits as forward() over the chunks one after another (n = 129 ends
     with a one-token chunk)."""
