@@ -45,6 +45,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="M26-shaped model with this many layers (the small case for detailed ncu captures)")
     p.add_argument("--vocab", type=int, default=None, help="vocabulary of that model (default M26's)")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
     p.add_argument("--profile-window", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return p.parse_args()
@@ -145,6 +147,32 @@ def prefill_summary(pre, spec, stream_bytes, hbm):
             "weight_stream_gbs": gbs, "hbm_frac": gbs / hbm,
             "note": "32-token chunks on three stream lanes in turn; exact reference-order f32 accumulation "
                     "of per-sub-block int8 dots (mma.sync tiles) bounds it, not the tensor pipe or HBM"}
+
+
+def prefill_config4(pk, path, spec, device):
+    """BASELINE config 4 on the device: a 4096-token prompt prefilled in 32-token
+    chunks, and the 323 -> 379 extension, whose second call reuses the 320
+    tokens of full chunks it shares with the first (model.rs:1251-1295)."""
+    eng = pk.Engine(path, n_ctx=4096 + 64, max_batch=32, device=device)
+    warm = synth_prompt(spec, 7, 96)
+    eng.generate(warm, 0, stop_at_eog=False)
+    long_prompt = synth_prompt(spec, 4096, 4096)
+    r = eng.generate(long_prompt, 0, stop_at_eog=False)
+    out = {"prefill_4096": {"tokens": r["prefill_tokens"], "ms": r["prefill_ms"],
+                            "tok_s": r["prefill_tokens"] / (r["prefill_ms"] / 1000.0)}}
+    ext = synth_prompt(spec, 379, 379)
+    first = eng.generate(ext[:323], 0, stop_at_eog=False)
+    second = eng.generate(ext, 0, stop_at_eog=False)
+    out["extension_323_379"] = {"fresh_323_ms": first["prefill_ms"], "cached_tokens": second["prefill_cached_tokens"],
+                                "prefill_tokens": second["prefill_tokens"], "ms": second["prefill_ms"]}
+    del eng
+    return out
+
+
+def synth_prompt(spec, seed, n):
+    from pocketinfer import synth
+
+    return synth.prompt_ids(seed, n, spec.n_vocab)
 
 
 def cycle_steps(eng, n, state, timed):
@@ -259,6 +287,15 @@ def run_ours(args):
     warm = [(t + 1) % synth.m26_spec(args.layers, args.vocab).n_vocab for t in prompt[:96]]
     eng.generate(warm, 0, stop_at_eog=False)
     pre = eng.generate(prompt, 1, stop_at_eog=False)
+    spec = synth.m26_spec(args.layers, args.vocab)
+    if args.prefill_only:
+        summary = prefill_summary(pre, spec, info["stream_bytes"], peaks()[0])
+        summary.update(prefill_config4(pk, path, spec, local))
+        if rank == 0:
+            print(json.dumps({"prefill": summary}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     state = {"pos": PROMPT_LEN}
     cycle_steps(eng, args.warmup, state, False)
 
@@ -299,9 +336,12 @@ def run_ours(args):
     e2e_value, _ = replicas.replica_throughput(n_e2e, r["gen_ms"], world, dist, "cuda")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    c4 = None
+    if rank == 0 and world == 1:
         eng.close()
-        cpu = cpu_baseline_sample(path, prompt, args.cpu_seconds)
+        c4 = prefill_config4(pk, path, spec, local)  # BASELINE config 4, outside the timed region
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline_sample(path, prompt, args.cpu_seconds)
 
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -333,7 +373,7 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "no flush: each step streams 1.83 GB of weights (> 126 MB L2)"},
             "prefill_tok_s": pre["prefill_tokens"] / (pre["prefill_ms"] / 1000.0),
-            "prefill": prefill_summary(pre, synth.m26_spec(args.layers, args.vocab), info["stream_bytes"], hbm),
+            "prefill": dict(prefill_summary(pre, spec, info["stream_bytes"], hbm), **(c4 or {})),
             "decode_step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                                 "frac": step_gbs / hbm, "peak": hbm, "peak_kind": peak_kind},
             "roofline": {"bound": "hbm", "kernel": "k_decode", "achieved": achieved, "peak": hbm, "unit": "GB/s",

@@ -237,38 +237,44 @@ __device__ __forceinline__ void q8_blocks_lane(const float (&v)[N], const bool (
   }
 }
 
-// q8_block_lane for a 32-element block held two values per lane by the
-// sixteen lanes of a half warp (l16 = lane within the half; both halves of
-// the warp run it together, each on its own block): value 2*l16 + e is
-// (v0, v1)[e].  Same arithmetic, same results.  Every lane of the warp calls
-// it; lanes with store == false (a half warp without a block) store nothing.
-__device__ __forceinline__ void q8_block_pair(float v0, float v1, int l16, bool store, int8_t *q, float *d,
-                                              int32_t *sum) {
-  const float a0 = fabsf(v0), a1 = fabsf(v1);
-  float amax = a0 > 0.0f ? a0 : 0.0f;
-  amax = a1 > amax ? a1 : amax;
+// q8_block_lane for a 32-element block held V values per lane by a group of
+// L = 32 / V consecutive lanes (l = lane within the group; every group of
+// the warp runs it together, each on its own block): value V * l + e is
+// v[e].  Same arithmetic, same results.  Every lane of the warp calls it;
+// a group with store == false stores nothing.
+template <int L, int V>
+__device__ __forceinline__ void q8_block_group(const float (&v)[V], int l, bool store, int8_t *q, float *d,
+                                               int32_t *sum) {
+  static_assert(L * V == 32, "one 32-element block per group");
+  float amax = 0.0f;
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) {
+  for (int e = 0; e < V; e++) {
+    const float a = fabsf(v[e]);
+    amax = a > amax ? a : amax;  // NaN never wins, as in q8_block_lane
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) {
     const float t = __shfl_xor_sync(0xFFFFFFFFu, amax, o);
     amax = t > amax ? t : amax;
   }
   const float dd = fdiv(amax, 127.0f);
   const float inv = dd > 0.0f ? fdiv(1.0f, dd) : 0.0f;
-  auto qv = [&](float v) {
-    float r = roundf(fmul(v, inv));
+  int s = 0, iv[V];
+#pragma unroll
+  for (int e = 0; e < V; e++) {
+    float r = roundf(fmul(v[e], inv));
     r = r < -127.0f ? -127.0f : r;
     r = r > 127.0f ? 127.0f : r;
-    return isnan(r) ? 0 : (int)r;
-  };
-  const int i0 = qv(v0), i1 = qv(v1);
-  if (store) {
-    q[2 * l16] = (int8_t)i0;
-    q[2 * l16 + 1] = (int8_t)i1;
+    iv[e] = isnan(r) ? 0 : (int)r;
+    s += iv[e];
   }
-  int s = i0 + i1;
+  if (store) {
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-  if (store && l16 == 0) {
+    for (int e = 0; e < V; e++) q[V * l + e] = (int8_t)iv[e];
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  if (store && l == 0) {
     *d = dd;
     *sum = s;
   }

@@ -631,85 +631,17 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
   return launch(k_gateup_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, wg, wu, src, h);
 }
 
-// ------------------------------------------------------------ multi-lane matvec
-constexpr int L_THREADS = 256;
-constexpr int L_RT = 8;    // rows per tile
-constexpr int L_LB = 32;   // lanes per pass
-constexpr int L_TW = 48;   // terms per wave per (row, lane)
-
-template <int T>
-__device__ void tile_lanes(const DevTensor &W, int r0, int nr, const Q8Dev &act, int l0, int nl, float *Tsm,
-                           float *out, long os_row, long os_lane, int add) {
-  constexpr int GE = Geo<T>::GE, TPG = Geo<T>::TPG, GW = L_TW / TPG;
-  const int G = W.k / GE, nb = W.k >> 5;
-  const int tid = threadIdx.x;
-  float acc = 0.0f;
-  for (int g0 = 0; g0 < G; g0 += GW) {
-    const int gw = min(GW, G - g0);
-    const int items = nr * gw;
-    for (int it = tid; it < items; it += L_THREADS) {
-      const int rl = it / gw, gl = it - rl * gw;
-      GroupW<T> gwt;
-      gwt.load(W, r0 + rl, g0 + gl);
-      for (int ln = 0; ln < nl; ln++) {
-        const int lane = l0 + ln;
-        const ActRef A{act.q + (long)lane * W.k, act.d + (long)lane * nb, act.s + (long)lane * nb};
-        float t[TPG];
-        gwt.terms(A, t);
-#pragma unroll
-        for (int s = 0; s < TPG; s++) Tsm[(gl * TPG + s) * (L_LB * L_RT) + ln * L_RT + rl] = t[s];
-      }
-    }
-    __syncthreads();
-    if (tid < nl * L_RT && (tid % L_RT) < nr) {
-      const int nt = gw * TPG;
-#pragma unroll 4
-      for (int j = 0; j < nt; j++) acc = fadd(acc, Tsm[j * (L_LB * L_RT) + tid]);
-    }
-    __syncthreads();
-  }
-  if (tid < nl * L_RT && (tid % L_RT) < nr) {
-    const int ln = tid / L_RT, rl = tid % L_RT;
-    const float v = fadd(0.0f, acc);
-    float *o = out + (long)(r0 + rl) * os_row + (long)(l0 + ln) * os_lane;
-    *o = add ? fadd(*o, v) : v;
-  }
-}
-
-__global__ void __launch_bounds__(L_THREADS) k_mv_lanes(DevTensor W, Q8Dev act, float *out, long os_row, long os_lane,
-                                                         int add) {
-  __shared__ float Tsm[L_TW * L_LB * L_RT];
-  const int tiles = (W.rows + L_RT - 1) / L_RT;
-  if (threadIdx.x == 0)
-    for (int t = blockIdx.x, i = 0; t < tiles && i < 2; t += gridDim.x, i++)
-      prefetch_rows(W, t * L_RT, min(L_RT, W.rows - t * L_RT));
-  pdl_trigger();
-  pdl_wait();
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int r0 = t * L_RT, nr = min(L_RT, W.rows - r0);
-    for (int l0 = 0; l0 < act.b; l0 += L_LB) {
-      const int nl = min(L_LB, act.b - l0);
-      switch (W.type) {
-        case T_Q4_K: tile_lanes<T_Q4_K>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
-        case T_Q6_K: tile_lanes<T_Q6_K>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
-        case T_Q8_0: tile_lanes<T_Q8_0>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
-        default: tile_lanes<T_Q4_0>(W, r0, nr, act, l0, nl, Tsm, out, os_row, os_lane, add); break;
-      }
-    }
-  }
-}
-
 // ------------------------------------------------- multi-lane matvec, tensor cores
 // b > 1 (prefill chunks, Pool::matmul with several lanes).  The reference adds
 // one float term per (row, lane, sub-block) in sub-block order
 // (quant_int.rs:282-419).  Each sub-block's integer dot is one element of an
 // int8 mma.sync tile (m16n8k32 per 32-element sub-block, m16n8k16 per
-// 16-element Q6_K piece), exact in int32 with a zero accumulator; every thread
-// turns its four tile elements into the reference's float terms (operand
-// order as in the scalar path) and adds them to four register accumulators,
-// sub-block after sub-block.  CTA: 4 warps, tile 16 rows x 32 lanes (warp w
-// takes lanes 8w .. 8w+7); the tile's rows and the lanes' activation scales
-// are staged in shared memory one k-chunk at a time.
+// 16-element Q6_K piece), exact in int32; every thread turns its four tile
+// elements into the reference's float terms (operand order as in the scalar
+// path) and adds them, sub-block after sub-block, to the running sums.  A
+// tile is 16 rows x 32 lanes (four lane groups of 8); the tile's rows and
+// the lanes' activation scales are staged in shared memory one k-chunk at a
+// time.  mv_tile below has the details.
 constexpr int MM_WARPS = 4;
 constexpr int MM_ROWS = 16;
 constexpr int MM_LANES = 8 * MM_WARPS;
@@ -1219,15 +1151,6 @@ cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, cons
                 n_kv, n_ctx, kc, vc);
 }
 
-__global__ void k_swiglu(const float *g, const float *u, float *h, long n) {
-  pdl_trigger();
-  pdl_wait();
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float gg = g[i];
-    h[i] = fmul(fdiv(gg, fadd(1.0f, expf_lib(-gg))), u[i]);
-  }
-}
-
 __global__ void k_expf(const float *x, float *out, long n) {
   pdl_trigger();
   pdl_wait();
@@ -1240,10 +1163,6 @@ cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st) {
   return launch(k_expf, dim3(std::max(grid, 1)), dim3(256), 0, st, x, out, n);
 }
 
-cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st) {
-  int grid = (int)std::min<long>((n + 255) / 256, (long)num_sms() * 8);
-  return launch(k_swiglu, dim3(std::max(grid, 1)), dim3(256), 0, st, g, u, h, n);
-}
 
 // ------------------------------------------------------------ attention
 // One CTA per (token, head), the reference's exact arithmetic
@@ -1334,7 +1253,7 @@ __global__ void k_attn(AttnArgs a, int dot8) {
 //           (sequential, unfused) against the K tile [d][position];
 //   pass 2: the tile's weights e = exp(s - M) (0 past the token's position,
 //           which the V chain skips and which adds +0.0 exactly to a sum that
-//           starts at +0.0), then thread (token, 2 dims) runs two V chains
+//           starts at +0.0), then thread (token, 4 dims) runs four V chains
 //           and the token's sum chain over the tile in position order.
 constexpr int AC_THREADS = 256;
 __host__ __device__ inline int ac_group(int dh) { return 512 / dh < 8 ? 512 / dh : 8; }
@@ -1426,11 +1345,11 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
     Ms[tid] = m;
   }
   __syncthreads();
-  // ---- pass 2: weights, V chains and sum chains
-  const int H2 = dh / 2, vt = tid / H2, vd = tid - vt * H2;
+  // ---- pass 2: weights, V chains and sum chains (thread: token vt, dims 4 vd .. 4 vd + 3)
+  const int H4 = dh / 4, vt = tid / H4, vd = tid - vt * H4;
   const bool vact = vt < G;
   const float *Et = E + (vact ? vt : 0) * (P + 4);
-  float acc0 = 0.0f, acc1 = 0.0f, sum = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sum = 0.0f;
   for (int j = 0; j < nt; j++) {
     const float *vb = ((nt + j) & 1) ? buf1 : buf0;
     if (j + 1 < nt) stage_v(j + 1, ((nt + j) & 1) ? buf0 : buf1);
@@ -1449,16 +1368,18 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
     __syncthreads();
     if (vact) {
       const int npr = (min(P, maxpos + 1 - p0) + 3) & ~3;
-      const float2 *vv = (const float2 *)vb + vd;
+      const float4 *vv = (const float4 *)vb + vd;
       for (int pl = 0; pl < npr; pl += 4) {
         const float4 e4 = *(const float4 *)(Et + pl);
         const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          const float2 v = vv[(pl + u) * H2];
+          const float4 v = vv[(pl + u) * H4];
           if (ev[u] != 0.0f) {
-            acc0 = fadd(acc0, fmul(ev[u], v.x));
-            acc1 = fadd(acc1, fmul(ev[u], v.y));
+            acc[0] = fadd(acc[0], fmul(ev[u], v.x));
+            acc[1] = fadd(acc[1], fmul(ev[u], v.y));
+            acc[2] = fadd(acc[2], fmul(ev[u], v.z));
+            acc[3] = fadd(acc[3], fmul(ev[u], v.w));
           }
           sum = fadd(sum, ev[u]);
         }
@@ -1468,22 +1389,21 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   }
   const bool valid = vact && t0 + vt < a.b;
   const long bi = t0 + vt;
-  float o0 = 0.0f, o1 = 0.0f;
+  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (valid) {
     const float inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
-    float *o = a.out + (bi * a.n_head + h) * dh + 2 * vd;
-    o0 = fmul(acc0, inv);
-    o1 = fmul(acc1, inv);
-    o[0] = o0;
-    o[1] = o1;
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[e] = fmul(acc[e], inv);
+    *(float4 *)(a.out + (bi * a.n_head + h) * dh + 4 * vd) = make_float4(o[0], o[1], o[2], o[3]);
   }
-  if (a.q8.q) {
-    // dh % 32 == 0, so each half warp holds one 32-element block of one
-    // token's row, or no valid token at all (it still takes part in the
-    // shuffles, which stay inside the half warp, and stores nothing).
-    const int qk = a.n_head * dh, blk = (h * dh + 2 * vd) >> 5;
+  if (a.q8.q && tid < ((G * H4 + 31) & ~31)) {
+    // dh % 32 == 0, so H4 is a multiple of 8 and each group of eight threads
+    // holds one 32-element block of one token's row, or no valid token at
+    // all (it still takes part in the shuffles, which stay inside the group,
+    // and stores nothing).  Whole warps take part.
+    const int qk = a.n_head * dh, blk = (h * dh + 4 * vd) >> 5;
     const long qo = valid ? bi * qk + blk * 32 : 0, so = valid ? bi * (qk >> 5) + blk : 0;
-    q8_block_pair(o0, o1, tid & 15, valid, a.q8.q + qo, a.q8.d + so, a.q8.s + so);
+    q8_block_group<8, 4>(o, tid & 7, valid, a.q8.q + qo, a.q8.d + so, a.q8.s + so);
   }
 }
 

@@ -95,8 +95,6 @@ cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, cons
                            float *vcache, cudaStream_t st);
 // out[i] = expf_lib(x[i]) (the C library's expf, bit for bit).
 cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st);
-// SwiGLU over [n] elements: h = g / (1 + exp(-g)) * u.
-cudaError_t launch_swiglu(const float *g, const float *u, float *h, long n, cudaStream_t st);
 
 // Causal GQA attention (model.rs:993-1087) for b tokens at positions pos[b].
 struct AttnArgs {
