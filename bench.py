@@ -45,6 +45,10 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="M26-shaped model with this many layers (the small case for detailed ncu captures)")
     p.add_argument("--vocab", type=int, default=None, help="vocabulary of that model (default M26's)")
+    p.add_argument("--tp70", action="store_true",
+                   help="tensor-parallel decode of the 70B-shaped stack (BASELINE config 5), one rank per GPU "
+                        "(world = the torchrun world size); prints its own JSON line")
+    p.add_argument("--tp-layers", type=int, default=None, help="layers of that stack (default 80)")
     p.add_argument("--prefill-only", action="store_true",
                    help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
     p.add_argument("--profile-window", action="store_true",
@@ -397,10 +401,79 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_tp70(args):
+    """BASELINE config 5, tensor-parallel half: the 70B-shaped stack split over
+    the torchrun world (1, 2, 4 or 8 GPUs), synthetic weights generated on each
+    device, greedy b = 1 decode.  The time is the max over ranks of the CUDA-event
+    time of the decode steps; HBM fraction per rank from its shard's bytes."""
+    import datetime
+
+    import torch
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    import torch.distributed as dist
+
+    if world == 1:  # a plain single-process run still gets a (one-rank) group for the handle exchange
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29517")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600))
+    from pocketinfer import tp
+
+    model = dict(tp.M70)
+    if args.tp_layers:
+        model["n_layer"] = args.tp_layers
+    n_ctx = 8 + max(args.warmup, 3) + args.steps + 16
+    eng = tp.TpEngine(rank, world, device=local, n_ctx=n_ctx)
+    t0 = time.time()
+    eng.load_synthetic(model, seed=70)
+    load_s = time.time() - t0
+    eng.connect()
+    info = eng.info
+    prompt = [(7 * i + 3) % model["n_vocab"] for i in range(8)]
+    eng.prefill(prompt)
+    eng.decode(max(args.warmup, 3))
+    gpu_index = local
+    clocks = ClockSampler(gpu_index)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    _, ms = eng.decode(args.steps, return_ms=True)  # args.steps steps, each one token through the model
+    clk = clocks.stop()
+    t = torch.tensor([ms], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_step = max_ms / args.steps
+    hbm, peak_kind = peaks()
+    gbs = info["stream_bytes"] / (ms_step / 1000.0) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "decode tok/s (70B-shaped Q4_K stack, b=1, tensor-parallel)", "value": 1000.0 / ms_step,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8xint8->int32, f32", "data": "synthetic (weights generated on each device)",
+            "config": {"workload": "BASELINE config 5 TP: 80 L, d 8192, 64/8 heads x 128, FFN 28672, vocab 128256"
+                       if not args.tp_layers else f"70B-shaped stack cut to {model['n_layer']} layers",
+                       "parallelism": f"tp{world}", "prompt": len(prompt),
+                       "collectives_per_token": info["collectives_per_token"],
+                       "exchange": "partial row sums (n_embd f32) pushed to every rank's peer buffer, added in "
+                                   "rank order; own push/sum kernels over NVLink peer memory"},
+            "per_rank": {"stream_bytes": info["stream_bytes"], "achieved_gbs": gbs, "hbm_frac": gbs / hbm,
+                         "peak": hbm, "peak_kind": peak_kind, "weight_bytes": info["weight_bytes"],
+                         "load_s": load_s},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp70:
+        run_tp70(args)
     else:
         run_ours(args)
 

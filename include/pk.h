@@ -228,6 +228,57 @@ int pk_get_dump(pk_engine *eng, const char *name, float *out, int cap, int *n_ou
 void pk_request_stop(void);
 void pk_clear_stop(void);
 
+/* ------------------------------------------------- tensor-parallel decode
+ * No reference counterpart: the reference runs one engine per process on the
+ * CPU.  This splits a llama stack over T GPUs, one process per GPU (the
+ * 70B-shaped configuration), for b = 1 decode:
+ *   q/k/v rows of whole heads, o and down k ranges, gate/up rows, output
+ *   vocabulary rows; after o and after down the ranks' partial row sums are
+ *   added in rank order through peer memory (cudaIpc handles exchanged by
+ *   the caller); the token is the first maximum over the vocabulary shards.
+ * Every rank makes the same calls in the same order.  With T = 1 a step is
+ * the single-GPU b = 1 op sequence bit for bit. */
+typedef struct pk_tp pk_tp;
+
+typedef struct {
+  int rank, world, n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab;
+  int local_heads, local_kv_heads, local_ff, vocab0, local_vocab;
+  size_t weight_bytes;       /* this rank's device weight bytes */
+  size_t stream_bytes;       /* bytes this rank's weights stream per token */
+  int collectives_per_token; /* 2 per layer + the token pick */
+} pk_tp_info;
+
+/* A synthetic llama stack (Q4_K q/k/o/gate/up/down, Q6_K v/output, Q4_K
+ * embedding) generated on the device, each rank its own shard. */
+typedef struct {
+  int n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab, n_rot;
+  float rope_theta, rms_eps;
+} pk_tp_model;
+
+int pk_tp_create(int device, int n_ctx, int rank, int world, pk_tp **out);
+void pk_tp_destroy(pk_tp *tp);
+int pk_tp_load_gguf(pk_tp *tp, const char *path);
+int pk_tp_load_synthetic(pk_tp *tp, const pk_tp_model *model, uint64_t seed);
+/* Bytes of one peer-memory handle (a cudaIpcMemHandle_t). */
+int pk_tp_handle_bytes(void);
+/* This rank's handle (after a load); then every rank passes all T handles in rank order. */
+int pk_tp_ipc_handle(pk_tp *tp, void *out);
+int pk_tp_open_peers(pk_tp *tp, const void *handles);
+/* The prompt as b = 1 steps; the last step picks the first generated token. */
+int pk_tp_prefill(pk_tp *tp, const uint32_t *prompt, int n);
+/* n_steps tokens as pk_decode_steps_device: the token picked last, then the next n_steps - 1; the
+ * n_steps steps also pick the token the next call starts with (device time in *device_ms). */
+int pk_tp_decode(pk_tp *tp, int n_steps, uint32_t *out_ids, float *device_ms);
+/* This rank's logits of the last step with the head: rows [vocab0, vocab0 + n_local). */
+int pk_tp_logits(pk_tp *tp, float *out, int n, int *n_local, int *vocab0);
+int pk_tp_info_get(pk_tp *tp, pk_tp_info *info);
+/* Host restatements for tests: the shard of rank r of T (out = {local heads,
+ * local kv heads, local ffn rows, vocab0, local vocab}), and the pick over
+ * the shards' {value, global index or -1}. */
+int pk_tp_split(int n_head, int n_head_kv, int head_dim, int n_ff, int n_vocab, int rank, int world, int o_block,
+                int down_block, int out[5]);
+uint32_t pk_tp_pick(const float *vals, const int *idx, int world);
+
 #ifdef __cplusplus
 }
 #endif

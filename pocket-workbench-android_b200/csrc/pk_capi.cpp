@@ -10,6 +10,7 @@
 
 #include "pk.h"
 #include "pk_engine.h"
+#include "pk_tp.h"
 
 namespace pk {
 
@@ -436,5 +437,104 @@ int pk_get_dump(pk_engine *e, const char *name, float *out, int cap, int *n_out)
 
 void pk_request_stop(void) { g_stop.store(true); }
 void pk_clear_stop(void) { g_stop.store(false); }
+
+// ---- tensor-parallel decode
+struct pk_tp {
+  pk::TpEngine eng;
+};
+
+int pk_tp_create(int device, int n_ctx, int rank, int world, pk_tp **out) {
+  if (!out) return set_error(PK_ERR_INVALID, "null argument");
+  *out = nullptr;
+  pk_tp *t = new (std::nothrow) pk_tp;
+  if (!t) return set_error(PK_ERR_OOM, "out of host memory");
+  const int rc = t->eng.create(device, n_ctx, rank, world);
+  if (rc) {
+    delete t;
+    return rc;
+  }
+  *out = t;
+  return PK_OK;
+}
+
+void pk_tp_destroy(pk_tp *t) { delete t; }
+
+int pk_tp_load_gguf(pk_tp *t, const char *path) {
+  if (!t || !path) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.load(path);
+}
+
+int pk_tp_load_synthetic(pk_tp *t, const pk_tp_model *m, uint64_t seed) {
+  if (!t || !m) return set_error(PK_ERR_INVALID, "null argument");
+  pk::Config c;
+  c.arch = "llama";
+  c.n_layer = m->n_layer;
+  c.n_embd = m->n_embd;
+  c.n_head = m->n_head;
+  c.n_head_kv = m->n_head_kv;
+  c.head_dim = m->head_dim;
+  c.n_ff = m->n_ff;
+  c.n_vocab = m->n_vocab;
+  c.n_rot = m->n_rot;
+  c.rope_theta = m->rope_theta;
+  c.rms_eps = m->rms_eps;
+  return t->eng.load_synthetic(c, m->n_vocab, seed);
+}
+
+int pk_tp_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int pk_tp_ipc_handle(pk_tp *t, void *out) {
+  if (!t || !out) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.ipc_handle(out);
+}
+
+int pk_tp_open_peers(pk_tp *t, const void *handles) {
+  if (!t || !handles) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.open_peers(handles);
+}
+
+int pk_tp_prefill(pk_tp *t, const uint32_t *prompt, int n) {
+  if (!t || !prompt) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.prefill(prompt, n);
+}
+
+int pk_tp_decode(pk_tp *t, int n_steps, uint32_t *out_ids, float *device_ms) {
+  if (!t) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.decode(n_steps, out_ids, device_ms);
+}
+
+int pk_tp_logits(pk_tp *t, float *out, int n, int *n_local, int *vocab0) {
+  if (!t || (!out && n > 0)) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.logits(out, n, n_local, vocab0);
+}
+
+int pk_tp_info_get(pk_tp *t, pk_tp_info *info) {
+  if (!t || !info) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.info(info);
+}
+
+int pk_tp_split(int n_head, int n_head_kv, int head_dim, int n_ff, int n_vocab, int rank, int world, int o_block,
+                int down_block, int out[5]) {
+  if (!out) return set_error(PK_ERR_INVALID, "null argument");
+  pk::Config c;
+  c.n_head = n_head;
+  c.n_head_kv = n_head_kv;
+  c.head_dim = head_dim;
+  c.n_ff = n_ff;
+  pk::TpSplit s;
+  std::string why;
+  if (!pk::tp_split(c, n_vocab, rank, world, o_block, down_block, s, why)) return set_error(PK_ERR_UNSUPPORTED, why);
+  out[0] = s.nh;
+  out[1] = s.nkv;
+  out[2] = s.ff;
+  out[3] = s.vocab0;
+  out[4] = s.nvocab;
+  return PK_OK;
+}
+
+uint32_t pk_tp_pick(const float *vals, const int *idx, int world) {
+  if (!vals || !idx || world < 1 || world > pk::TP_MAX) return 0;
+  return pk::tp_pick(vals, idx, world);
+}
 
 }  // extern "C"

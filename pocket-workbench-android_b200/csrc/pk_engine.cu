@@ -80,8 +80,6 @@ int Engine::create(int device, int n_ctx, int max_batch) {
   return PK_OK;
 }
 
-namespace {
-
 // Config::from_gguf (model.rs:32-97)
 int config_from_gguf(const Gguf &g, Config &c) {
   const std::string arch = g.get_str("general.architecture");
@@ -120,12 +118,6 @@ int config_from_gguf(const Gguf &g, Config &c) {
   return PK_OK;
 }
 
-struct TRef {
-  std::string name;
-  int type = 0;
-  size_t ne0 = 0, ne1 = 0, row_bytes = 0, off = 0;
-};
-
 // Model::load find (model.rs:494-523)
 int find_tensor(const Gguf &g, const std::string &name, TRef &out) {
   const GgufTensor *t = g.tensor(name);
@@ -156,8 +148,6 @@ int check_shape(const TRef &t, size_t cols, size_t rows) {  // model.rs:650-655
                                          std::to_string(rows));
   return PK_OK;
 }
-
-}  // namespace
 
 int Engine::load(const char *path) {
   if (!st_) return set_error(PK_ERR_INVALID, "engine not created");

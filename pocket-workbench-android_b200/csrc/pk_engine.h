@@ -24,6 +24,16 @@ struct Config {
   float rope_theta = 10000.0f, rms_eps = 1e-5f;
 };
 
+// A GGUF tensor: type, shape (ne0 = row length) and file offset.
+struct TRef {
+  std::string name;
+  int type = 0;
+  size_t ne0 = 0, ne1 = 0, row_bytes = 0, off = 0;
+};
+int config_from_gguf(const Gguf &g, Config &c);
+int find_tensor(const Gguf &g, const std::string &name, TRef &out);
+int check_shape(const TRef &t, size_t cols, size_t rows);
+
 struct LayerDev {
   DevTensor q, k, v, o, gate, up, down;
   float *attn_norm = nullptr, *ffn_norm = nullptr;

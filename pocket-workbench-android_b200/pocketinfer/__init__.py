@@ -36,7 +36,9 @@ SYMBOLS = [
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
     "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position",
     "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
-    "pk_clear_stop",
+    "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
+    "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
+    "pk_tp_info_get", "pk_tp_split", "pk_tp_pick",
 ]
 
 
@@ -69,6 +71,18 @@ class GenStats(C.Structure):
 
 class KernelStat(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_int), ("ms", C.c_double), ("bytes", C.c_double)]
+
+
+class TpInfo(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("rank", "world", "n_layer", "n_embd", "n_head", "n_head_kv", "head_dim",
+                                       "n_ff", "n_vocab", "local_heads", "local_kv_heads", "local_ff", "vocab0",
+                                       "local_vocab")] + \
+               [("weight_bytes", C.c_size_t), ("stream_bytes", C.c_size_t), ("collectives_per_token", C.c_int)]
+
+
+class TpModel(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_ff", "n_vocab",
+                                       "n_rot")] + [("rope_theta", C.c_float), ("rms_eps", C.c_float)]
 
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_uint32, C.c_void_p)
@@ -111,6 +125,12 @@ def lib():
         "pk_selftest_bounded_wait": ([P, C.POINTER(I)], I),
         "pk_get_dump": ([P, C.c_char_p, P, I, C.POINTER(I)], I),
         "pk_request_stop": ([], None), "pk_clear_stop": ([], None),
+        "pk_tp_create": ([I, I, I, I, C.POINTER(P)], I), "pk_tp_destroy": ([P], None),
+        "pk_tp_load_gguf": ([P, C.c_char_p], I), "pk_tp_load_synthetic": ([P, C.POINTER(TpModel), C.c_uint64], I),
+        "pk_tp_handle_bytes": ([], I), "pk_tp_ipc_handle": ([P, P], I), "pk_tp_open_peers": ([P, P], I),
+        "pk_tp_prefill": ([P, P, I], I), "pk_tp_decode": ([P, I, P, C.POINTER(C.c_float)], I),
+        "pk_tp_logits": ([P, P, I, C.POINTER(I), C.POINTER(I)], I), "pk_tp_info_get": ([P, C.POINTER(TpInfo)], I),
+        "pk_tp_split": ([I, I, I, I, I, I, I, I, I, P], I), "pk_tp_pick": ([P, P, I], U32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
