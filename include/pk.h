@@ -187,6 +187,15 @@ int pk_forward(pk_engine *eng, const uint32_t *ids, const int *positions, int n,
 int pk_logits(pk_engine *eng, float *out, int n);
 /* Greedy sample of the current logits on the device (first maximum wins). */
 int pk_argmax(pk_engine *eng, uint32_t *token);
+/* sampler.rs:21-92 with temp > 0 (temperature, then top-p when 0 < top_p < 1) on device
+ * logits[n]: the token into *tok (device), *rng_state (device, the splitmix64 state
+ * Rng::new(seed) holds: seed + 0x9E3779B97F4A7C15) advanced when a draw happens.  Same
+ * arithmetic and order as the reference; equal probabilities in the top-p sort are ordered by
+ * index.  scratch: pk_sample_scratch_bytes(n) bytes of device memory, 256-byte aligned.
+ * pk_generate uses it when pk_gen_opts.temp > 0. */
+size_t pk_sample_scratch_bytes(int n);
+int pk_sample(const float *logits, int n, float temp, float top_p, uint64_t *rng_state, void *scratch,
+              uint32_t *tok, void *stream);
 /* Engine::generate.  out_ids receives up to out_cap generated ids. */
 int pk_generate(pk_engine *eng, const uint32_t *prompt, int n, const pk_gen_opts *opts,
                 pk_token_cb cb, void *user, uint32_t *out_ids, int out_cap, int *n_out,

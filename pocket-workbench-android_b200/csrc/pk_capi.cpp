@@ -438,6 +438,17 @@ int pk_get_dump(pk_engine *e, const char *name, float *out, int cap, int *n_out)
 void pk_request_stop(void) { g_stop.store(true); }
 void pk_clear_stop(void) { g_stop.store(false); }
 
+size_t pk_sample_scratch_bytes(int n) { return n > 0 ? sample_scratch_bytes(n) : 0; }
+
+int pk_sample(const float *logits, int n, float temp, float top_p, uint64_t *rng_state, void *scratch,
+              uint32_t *tok, void *stream) {
+  if (!logits || !rng_state || !scratch || !tok || n < 1 || !(temp > 0.0f))
+    return set_error(PK_ERR_INVALID, "pk_sample: null pointer, n < 1 or temp <= 0");
+  if (((uintptr_t)scratch) & 255) return set_error(PK_ERR_INVALID, "pk_sample: scratch must be 256-byte aligned");
+  CK(launch_sample(logits, n, temp, top_p, (unsigned long long *)rng_state, scratch, tok, (cudaStream_t)stream));
+  return PK_OK;
+}
+
 // ---- tensor-parallel decode
 struct pk_tp {
   pk::TpEngine eng;

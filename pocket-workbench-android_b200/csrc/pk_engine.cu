@@ -38,6 +38,8 @@ Engine::~Engine() {
   cudaFree(d_rope_sin_);
   cudaFree(d_act_arena_);
   cudaFree(d_decode_);
+  cudaFree(d_rng_);
+  cudaFree(d_sample_scratch_);
   cudaFreeHost(h_ids_);
   cudaFreeHost(h_pos_);
   cudaFreeHost(h_tok_);
@@ -740,6 +742,17 @@ int Engine::argmax(uint32_t *tok) {
   return PK_OK;
 }
 
+// sampler.rs:21-92 with temp > 0 on the current logits (the device Rng
+// state advances when a draw happens).
+int Engine::sample(float temp, float top_p, uint32_t *tok) {
+  if (!loaded_ || !d_rng_) return set_error(PK_ERR_INVALID, "no model loaded or no sampler state");
+  PK_CK(launch_sample(logits_, vocab_, temp, top_p, d_rng_, d_sample_scratch_, d_tok_, st_));
+  PK_CK(cudaMemcpyAsync(h_tok_, d_tok_, 4, cudaMemcpyDeviceToHost, st_));
+  PK_CK(cudaStreamSynchronize(st_));
+  *tok = h_tok_[0];
+  return PK_OK;
+}
+
 // The prompt's chunks [off, n) (chunk tokens each) on the prefill lanes in
 // turn: chunk c + 1 runs its layer l while chunk c is still in later layers,
 // waiting only for chunk c's K/V of layer l before its attention.
@@ -807,8 +820,15 @@ int Engine::generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_
   };
   if (!loaded_) return finish(set_error(PK_ERR_INVALID, "no model loaded"));
   if (n <= 0) return finish(set_error(PK_ERR_INVALID, "empty prompt"));
-  if (opts.temp > 0.0f)
-    return finish(set_error(PK_ERR_UNSUPPORTED, "temperature sampling is not implemented on the device; use temp <= 0"));
+  const bool sampling = opts.temp > 0.0f;
+  if (sampling) {  // Rng::new(seed) (sampler.rs:6-8) for this call, on the device
+    if (!d_rng_) {
+      PK_CK(cudaMalloc((void **)&d_rng_, 256));
+      PK_CK(cudaMalloc((void **)&d_sample_scratch_, sample_scratch_bytes(vocab_)));
+    }
+    h_rng_ = opts.seed + 0x9E3779B97F4A7C15ULL;
+    PK_CK(cudaMemcpyAsync(d_rng_, &h_rng_, 8, cudaMemcpyHostToDevice, st_));
+  }
   const auto t0 = std::chrono::steady_clock::now();
   const int chunk = std::min(max_batch_, 32);
   size_t common = 0;
@@ -861,7 +881,7 @@ int Engine::generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_
   for (int i = 0; i < opts.max_tokens; i++) {
     if (g_stop.load()) { std::snprintf(s.stop, sizeof(s.stop), "user_stop"); break; }
     uint32_t tok = 0;
-    int rc = argmax(&tok);
+    int rc = sampling ? sample(opts.temp, opts.top_p, &tok) : argmax(&tok);
     if (rc) return finish(rc);
     if (opts.stop_at_eog && std::binary_search(eos_ids_.begin(), eos_ids_.end(), tok)) {
       std::snprintf(s.stop, sizeof(s.stop), "eog");

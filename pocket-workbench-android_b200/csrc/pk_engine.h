@@ -49,6 +49,7 @@ class Engine {
   int forward(const uint32_t *ids, const int *pos, int n, bool want_logits);
   int logits(float *out, int n);
   int argmax(uint32_t *tok);
+  int sample(float temp, float top_p, uint32_t *tok);
   int generate(const uint32_t *prompt, int n, const pk_gen_opts &opts, pk_token_cb cb, void *user,
                uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats);
   int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
@@ -97,6 +98,9 @@ class Engine {
   // pinned host staging
   uint32_t *h_ids_ = nullptr, *h_tok_ = nullptr;
   int *h_pos_ = nullptr;
+  // temperature / top-p sampling: the Rng state and the sampler's scratch
+  unsigned long long *d_rng_ = nullptr, h_rng_ = 0;
+  uint8_t *d_sample_scratch_ = nullptr;
 
   // Prefill lanes: the scratch of one chunk's forward pass and the stream it
   // runs on.  Lane 0 is the buffers above and st_; the others have their

@@ -1433,6 +1433,155 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
   return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, a.b == 1 ? 1 : 0);
 }
 
+// ------------------------------------------------------------ temperature / top-p sampling
+// sampler.rs:21-92 for temp > 0, on one CTA of 1024 threads, with the
+// reference's arithmetic and order:
+//   M = max (strict '>', NaN never wins); e_i = exp((l_i - M) * (1 / temp));
+//   sum = sequential over i; 0 (no draw) unless sum > 0;
+//   top_p in (0, 1): indices sorted by e descending, equal e by index (the
+//   oracle's tie order; Rust's sort_unstable leaves it open), acc += e / sum
+//   in that order until acc >= top_p; e of the others set to 0 and
+//   sum = sequential over the kept ones in index order;
+//   r = rng.next_f32() * sum, the first i whose running sum of e reaches r
+//   (n - 1 if none).
+// Elementwise steps run on all threads; each sum is one thread's sequential
+// chain.  The sort is a bitonic network on 64-bit keys (~bits(e) << 32 | i)
+// in the scratch buffer.
+constexpr int SMP_THREADS = 1024;
+static int smp_pow2(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+size_t sample_scratch_bytes(int n) {
+  const size_t a = ((size_t)n * 4 + 255) & ~(size_t)255;
+  return 2 * a + (size_t)smp_pow2(n) * 8 + (((size_t)n + 255) & ~(size_t)255);
+}
+
+__device__ float rng_next_f32(unsigned long long *state) {  // sampler.rs:6-19 (splitmix64)
+  unsigned long long z = *state + 0x9E3779B97F4A7C15ULL;
+  *state = z;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  z ^= z >> 31;
+  return (float)(unsigned)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+__global__ void __launch_bounds__(SMP_THREADS) k_sample(const float *__restrict__ logits, int n, int p2, float temp,
+                                                        float top_p, unsigned long long *rng, uint8_t *scratch,
+                                                        uint32_t *tok) {
+  __shared__ float redf[32];
+  __shared__ float s_val;
+  __shared__ int s_cut;
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const size_t fa = ((size_t)n * 4 + 255) & ~(size_t)255;
+  float *E = (float *)scratch, *P = (float *)(scratch + fa);
+  unsigned long long *K = (unsigned long long *)(scratch + 2 * fa);
+  uint8_t *keep = scratch + 2 * fa + (size_t)p2 * 8;
+  // the maximum (order-free: NaN never wins)
+  float mx = -INFINITY;
+  for (int i = tid; i < n; i += SMP_THREADS) {
+    const float v = logits[i];
+    mx = v > mx ? v : mx;
+  }
+  mx = warp_max(mx);
+  if (lane == 0) redf[w] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = -INFINITY;
+    for (int i = 0; i < SMP_THREADS / 32; i++) m = redf[i] > m ? redf[i] : m;
+    s_val = m;
+  }
+  __syncthreads();
+  const float M = s_val, inv = fdiv(1.0f, temp);
+  for (int i = tid; i < n; i += SMP_THREADS) E[i] = expf_lib(fmul(fsub(logits[i], M), inv));
+  __syncthreads();
+  if (tid == 0) {
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < n; i++) sum = fadd(sum, E[i]);
+    s_val = sum;
+  }
+  __syncthreads();
+  float sum = s_val;
+  if (!(sum > 0.0f)) {
+    if (tid == 0) *tok = 0u;
+    return;
+  }
+  if (top_p > 0.0f && top_p < 1.0f) {
+    for (int i = tid; i < p2; i += SMP_THREADS)
+      K[i] = i < n ? ((unsigned long long)(~__float_as_uint(E[i])) << 32) | (unsigned)i : ~0ULL;
+    __syncthreads();
+    for (int k = 2; k <= p2; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < p2; i += SMP_THREADS) {
+          const int l = i ^ j;
+          if (l > i) {
+            const unsigned long long a = K[i], b = K[l];
+            if ((a > b) == ((i & k) == 0)) {
+              K[i] = b;
+              K[l] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    for (int k = tid; k < n; k += SMP_THREADS) {
+      P[k] = fdiv(E[(unsigned)(K[k] & 0xFFFFFFFFULL)], sum);
+      keep[k] = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float acc = 0.0f;
+      int cut = n;
+      for (int k = 0; k < n; k++) {
+        acc = fadd(acc, P[k]);
+        if (acc >= top_p) {
+          cut = k + 1;
+          break;
+        }
+      }
+      s_cut = cut;
+    }
+    __syncthreads();
+    for (int k = tid; k < s_cut; k += SMP_THREADS) keep[(unsigned)(K[k] & 0xFFFFFFFFULL)] = 1;
+    __syncthreads();
+    for (int i = tid; i < n; i += SMP_THREADS)
+      if (!keep[i]) E[i] = 0.0f;
+    __syncthreads();
+    if (tid == 0) {
+      float ns = 0.0f;
+      for (int i = 0; i < n; i++)
+        if (keep[i]) ns = fadd(ns, E[i]);
+      s_val = ns;
+    }
+    __syncthreads();
+    sum = s_val;
+  }
+  if (tid == 0) {
+    const float r = fmul(rng_next_f32(rng), sum);
+    float acc = 0.0f;
+    unsigned t = (unsigned)(n - 1);
+    for (int i = 0; i < n; i++) {
+      acc = fadd(acc, E[i]);
+      if (acc >= r) {
+        t = (unsigned)i;
+        break;
+      }
+    }
+    *tok = t;
+  }
+}
+
+cudaError_t launch_sample(const float *logits, int n, float temp, float top_p, unsigned long long *rng, void *scratch,
+                          uint32_t *tok, cudaStream_t st) {
+  if (n < 1 || !(temp > 0.0f) || (((uintptr_t)scratch) & 255)) return cudaErrorInvalidValue;
+  return launch(k_sample, dim3(1), dim3(SMP_THREADS), 0, st, logits, n, smp_pow2(n), temp, top_p, rng,
+                (uint8_t *)scratch, tok);
+}
+
 // ------------------------------------------------------------ argmax / feedback
 __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, int n, uint32_t *out) {
   __shared__ float sv[32];

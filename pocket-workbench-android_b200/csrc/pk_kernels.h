@@ -110,6 +110,13 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 
+// sampler.rs:21-92 for temp > 0 (temperature + top-p) on the device: the
+// token into *tok, rng (the splitmix64 state, device memory) advanced when
+// a draw happens.  scratch: sample_scratch_bytes(n) bytes, 256-aligned.
+size_t sample_scratch_bytes(int n);
+cudaError_t launch_sample(const float *logits, int n, float temp, float top_p, unsigned long long *rng, void *scratch,
+                          uint32_t *tok, cudaStream_t st);
+
 // First index of the maximum (sampler.rs:26-36); NaNs never win.
 cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st);
 // Decode feedback on the device: ids[0] = *tok; pos[0] += 1; hist[*step] = *tok; *step += 1.

@@ -38,7 +38,7 @@ SYMBOLS = [
     "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
     "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
     "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
-    "pk_tp_info_get", "pk_tp_split", "pk_tp_pick",
+    "pk_tp_info_get", "pk_tp_split", "pk_tp_pick", "pk_sample_scratch_bytes", "pk_sample",
 ]
 
 
@@ -131,6 +131,8 @@ def lib():
         "pk_tp_prefill": ([P, P, I], I), "pk_tp_decode": ([P, I, P, C.POINTER(C.c_float)], I),
         "pk_tp_logits": ([P, P, I, C.POINTER(I), C.POINTER(I)], I), "pk_tp_info_get": ([P, C.POINTER(TpInfo)], I),
         "pk_tp_split": ([I, I, I, I, I, I, I, I, I, P], I), "pk_tp_pick": ([P, P, I], U32),
+        "pk_sample_scratch_bytes": ([I], SZ),
+        "pk_sample": ([P, I, C.c_float, C.c_float, P, P, P, P], I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -191,6 +193,22 @@ def expf(x, stream=None):
     out = torch.empty_like(x)
     _check(lib().pk_expf(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
     return out
+
+
+def sample(logits, temp: float, top_p: float, rng_state: int, stream=None):
+    """sampler.rs:21-92 (temp > 0) on a device float32 vector; returns (token, new rng state)."""
+    import torch
+
+    assert logits.is_cuda and logits.dtype == torch.float32 and logits.is_contiguous()
+    n = logits.numel()
+    scratch = torch.empty(lib().pk_sample_scratch_bytes(n) + 256, dtype=torch.uint8, device=logits.device)
+    base = (scratch.data_ptr() + 255) // 256 * 256
+    r = rng_state & 0xFFFFFFFFFFFFFFFF
+    st = torch.tensor([r - (1 << 64) if r >= 1 << 63 else r], dtype=torch.int64, device=logits.device)
+    tok = torch.zeros(1, dtype=torch.int32, device=logits.device)
+    _check(lib().pk_sample(_ptr(logits), n, temp, top_p, _ptr(st), C.c_void_p(base), _ptr(tok), _stream(stream)))
+    torch.cuda.synchronize(logits.device)
+    return int(tok.item()) & 0xFFFFFFFF, int(st.item()) & 0xFFFFFFFFFFFFFFFF
 
 
 def q8_quantize(x, k: int, b: int, stream=None) -> Q8Act:

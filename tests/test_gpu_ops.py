@@ -227,3 +227,32 @@ def test_device_expf_matches_c_library(pk, oracle):
     got = pk.expf(dev(x)).cpu().numpy()
     want = oracle.expf_batch(x)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,temp,top_p", [(1000, 0.7, 0.9), (73448, 1.0, 0.9), (73448, 0.8, 1.0), (5000, 1.3, 0.5),
+                                          (5000, 1.0, 0.0), (3000, 0.5, 0.999), (1, 1.0, 0.9)])
+def test_sample_matches_reference(pk, oracle, n, temp, top_p):
+    """sampler.rs:21-92 with temp > 0 on the device: the same token and the same
+    Rng state as the reference's sampler on the same logits (ties in the top-p
+    sort included)."""
+    r = oracle.Rng(7 + n)
+    for trial in range(4):
+        x = synth.normal_f32(100 + trial + n, n) * np.float32(3.0)
+        if trial == 1 and n > 8:
+            x[::7] = x[3]  # many equal probabilities
+        before = r.s.value
+        want = oracle.sample(x.copy(), temp, top_p, r)
+        got, after = pk.sample(dev(x), temp, top_p, before)
+        assert got == want and after == r.s.value
+
+
+def test_sample_nonfinite_logits(pk, oracle):
+    """A NaN or +inf logit makes the sum NaN: token 0 and no draw (sampler.rs:45-47)."""
+    for bad in (np.nan, np.inf):
+        x = synth.normal_f32(5, 500)
+        x[17] = bad
+        r = oracle.Rng(3)
+        before = r.s.value
+        want = oracle.sample(x.copy(), 1.0, 0.9, r)
+        got, after = pk.sample(dev(x), 1.0, 0.9, before)
+        assert got == want == 0 and after == before == r.s.value
