@@ -1256,8 +1256,8 @@ __global__ void k_attn(AttnArgs a, int dot8) {
 //           starts at +0.0), then thread (token, 4 dims) runs four V chains
 //           and the token's sum chain over the tile in position order.
 constexpr int AC_THREADS = 256;
-__host__ __device__ inline int ac_group(int dh) { return 512 / dh < 8 ? 512 / dh : 8; }
-__host__ __device__ inline int ac_tile(int dh) { return dh <= 64 ? 128 : 64; }
+__host__ __device__ constexpr int ac_group(int dh) { return 512 / dh < 8 ? 512 / dh : 8; }
+__host__ __device__ constexpr int ac_tile(int dh) { return dh <= 64 ? 128 : 64; }
 static size_t ac_smem(int dh) {
   const int G = ac_group(dh), P = ac_tile(dh);
   return sizeof(float) * ((size_t)2 * P * dh + (size_t)G * (P + 4) + (size_t)G * dh + AC_THREADS + 16);
@@ -1266,9 +1266,11 @@ static size_t ac_smem(int dh) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
+// DHC: the head dimension as a compile-time constant (64, 128), or 0 for any.
+template <int DHC>
 __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   extern __shared__ __align__(16) float acs[];
-  const int dh = a.dh, G = ac_group(dh), P = ac_tile(dh), QP = P / 4, tid = threadIdx.x;
+  const int dh = DHC ? DHC : a.dh, G = ac_group(dh), P = ac_tile(dh), QP = P / 4, tid = threadIdx.x;
   const int h = blockIdx.y, kh = h / (a.n_head / a.n_kv), t0 = blockIdx.x * G;
   float *buf0 = acs, *buf1 = acs + P * dh, *E = buf1 + P * dh, *qs = E + G * (P + 4), *red = qs + G * dh;
   float *Ms = red + AC_THREADS;
@@ -1291,9 +1293,9 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   const float *kc = a.kcache + (size_t)kh * dh * a.n_ctx, *vc = a.vcache + (size_t)kh * a.n_ctx * dh;
   auto stage_k = [&](int i, float *dst) {
     const int p0 = i * P, nq = (min(P, maxpos + 1 - p0) + 3) >> 2;
-    for (int c = tid; c < dh * nq; c += AC_THREADS) {
-      const int d = c / nq, j = c - d * nq;
-      cp_async16(dst + d * P + 4 * j, kc + (size_t)d * a.n_ctx + p0 + 4 * j);
+    for (int c = tid; c < dh * QP; c += AC_THREADS) {
+      const int d = c / QP, j = c - d * QP;
+      if (j < nq) cp_async16(dst + d * P + 4 * j, kc + (size_t)d * a.n_ctx + p0 + 4 * j);
     }
   };
   auto stage_v = [&](int i, float *dst) {
@@ -1318,7 +1320,7 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
       const float4 *kt = (const float4 *)((i & 1) ? buf1 : buf0) + sq;
       const float *qv = qs + st * dh;
       float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
       for (int d = 0; d < dh; d++) {
         const float4 k = kt[d * QP];
         const float qq = qv[d];
@@ -1424,10 +1426,12 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
   if (a.b > 1 && a.n_ctx % 4 == 0 && (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
     const size_t smem = ac_smem(a.dh);
-    cudaError_t e = set_smem(k_attn_chunk, smem);
-    if (e != cudaSuccess) return e;
     const int G = ac_group(a.dh);
-    return launch(k_attn_chunk, dim3((a.b + G - 1) / G, a.n_head), dim3(AC_THREADS), smem, st, a);
+    const dim3 grid((a.b + G - 1) / G, a.n_head);
+    void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_chunk<64> : a.dh == 128 ? k_attn_chunk<128> : k_attn_chunk<0>;
+    cudaError_t e = set_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, grid, dim3(AC_THREADS), smem, st, a);
   }
   const int threads = a.dh < 128 ? 128 : 256;
   return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, a.b == 1 ? 1 : 0);
