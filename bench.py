@@ -149,7 +149,7 @@ def prefill_summary(pre, spec, stream_bytes, hbm):
             "int8_ops_per_token": ops_per_token, "int8_tops": tops, "int8_peak_tops": INT8_DENSE_TOPS_NOMINAL,
             "int8_frac": tops / INT8_DENSE_TOPS_NOMINAL, "int8_peak_kind": "nominal",
             "weight_stream_gbs": gbs, "hbm_frac": gbs / hbm,
-            "note": "32-token chunks on three stream lanes in turn; exact reference-order f32 accumulation "
+            "note": "32-token chunks on six stream lanes in turn; exact reference-order f32 accumulation "
                     "of per-sub-block int8 dots (mma.sync tiles) bounds it, not the tensor pipe or HBM"}
 
 

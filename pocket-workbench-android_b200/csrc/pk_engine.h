@@ -114,7 +114,7 @@ class Engine {
     uint32_t *ids = nullptr;
     int *pos = nullptr;
   };
-  static constexpr int NLANES = 3;
+  static constexpr int NLANES = 6;
   Lane lane_[NLANES];
   uint8_t *d_lane_arena_[NLANES] = {};
   std::vector<cudaEvent_t> kv_ev_[NLANES];
