@@ -774,40 +774,31 @@ __device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, fl
     const int nbc = min(NBC, nblk - c0);
     __syncthreads();  // the previous chunk is consumed
     // stage: the tile's rows and the lanes' activation scales by asynchronous
-    // copies (every copy in flight at once), the f16 row scales four loads at a time
+    // copies (every copy in flight at once), the f16 row scales by plain loads;
+    // warps take rows (lanes), lanes take pieces, so no index is divided
+    constexpr int NW = MM_WARPS * KS;
     const int v16 = nbc * G::QB / 16;
-    for (int i = tid; i < nr * v16; i += 32 * MM_WARPS * KS) {
-      const int r = i / v16, j = i - r * v16;
-      cp_async16(wq + (size_t)r * NBC * G::QB + 16 * j, W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB + 16 * j);
-    }
+    for (int r = w; r < nr; r += NW)
+      for (int j = lane; j < v16; j += 32)
+        cp_async16(wq + (size_t)r * NBC * G::QB + 16 * j, W.q + (size_t)(r0 + r) * row_q + (size_t)c0 * G::QB + 16 * j);
     const int s0 = c0 * (G::BE / 32), nsb = nbc * (G::BE / 32);
-    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS * KS) {
-      const int l = i / nsb, j = i - l * nsb;
-      const long o = (long)(L0 + l) * nb32 + s0 + j;
-      cp_async4(&asf[l * LS + j].x, act.d + o);
-      cp_async4(&asf[l * LS + j].y, act.s + o);
+    for (int l = w; l < nl; l += NW) {
+      const long o = (long)(L0 + l) * nb32 + s0;
+      for (int j = lane; j < nsb; j += 32) {
+        cp_async4(&asf[l * LS + j].x, act.d + o + j);
+        cp_async4(&asf[l * LS + j].y, act.s + o + j);
+      }
     }
     if (G::D)
-      for (int i0 = tid; i0 < nr * nbc; i0 += 4 * 32 * MM_WARPS * KS) {
-        uint16_t hv[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int i = i0 + u * 32 * MM_WARPS * KS, r = i / nbc, j = i - r * nbc;
-          hv[u] = i < nr * nbc ? __ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j) : (uint16_t)0;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int i = i0 + u * 32 * MM_WARPS * KS, r = i / nbc, j = i - r * nbc;
-          if (i < nr * nbc) wd[r * NBC + j] = f16f(hv[u]);
-        }
-      }
+      for (int r = w; r < nr; r += NW)
+        for (int j = lane; j < nbc; j += 32) wd[r * NBC + j] = f16f(__ldg(W.d + (size_t)(r0 + r) * nblk + c0 + j));
     cp_async_wait_all();
     // the block sums as floats (each thread converts the entries it copied)
-    for (int i = tid; i < nl * nsb; i += 32 * MM_WARPS * KS) {
-      const int l = i / nsb, j = i - l * nsb;
-      float *sp = &asf[l * LS + j].y;
-      *sp = (float)__float_as_int(*sp);
-    }
+    for (int l = w; l < nl; l += NW)
+      for (int j = lane; j < nsb; j += 32) {
+        float *sp = &asf[l * LS + j].y;
+        *sp = (float)__float_as_int(*sp);
+      }
     __syncthreads();
     if (!active) continue;  // no lanes for this warp (it still meets every __syncthreads)
     const uint8_t *qa = wq + (size_t)g * NBC * G::QB, *qb = wq + (size_t)(g + 8) * NBC * G::QB;
