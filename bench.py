@@ -49,6 +49,9 @@ def parse_args():
                    help="tensor-parallel decode of the 70B-shaped stack (BASELINE config 5), one rank per GPU "
                         "(world = the torchrun world size); prints its own JSON line")
     p.add_argument("--tp-layers", type=int, default=None, help="layers of that stack (default 80)")
+    p.add_argument("--streams", type=int, default=0,
+                   help="independent M26 streams per GPU decoded together (the data-parallel streams case)")
+    p.add_argument("--stream-ctx", type=int, default=512, help="KV positions of each stream")
     p.add_argument("--prefill-only", action="store_true",
                    help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
     p.add_argument("--profile-window", action="store_true",
@@ -468,10 +471,106 @@ def run_tp70(args):
     dist.destroy_process_group()
 
 
+def run_streams(args):
+    """Data-parallel streams: every rank decodes ``--streams`` independent M26
+    sequences (its share of streams * world, dealt round-robin), one batched
+    step per token of every stream, each stream at its own position over its
+    own KV cache.  Weak scaling; the time is the max over ranks of the CUDA-event
+    time of the steps."""
+    import torch
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import pocketinfer as pk
+    from pocketinfer import replicas, synth
+
+    spec = synth.m26_spec(args.layers, args.vocab)
+    if rank == 0:
+        synth.m26_path(args.model_dir, spec=spec)
+    if dist:
+        dist.barrier()
+    path = synth.m26_path(args.model_dir, spec=spec)
+    mine = replicas.assign_streams(args.streams * world, rank, world)
+    n_ctx = args.stream_ctx
+    if PROMPT_LEN + CYCLE > n_ctx:
+        raise SystemExit(f"--stream-ctx must be at least {PROMPT_LEN + CYCLE}")
+    eng = pk.Engine(path, n_ctx=n_ctx, max_batch=max(32, len(mine)), device=local)
+    info = eng.info
+    eng.streams_begin(len(mine))
+    for s, sid in enumerate(mine):  # every stream its own prompt, prefilled into its own cache
+        eng.stream_prefill(s, synth.prompt_ids(1000 + sid, PROMPT_LEN, spec.n_vocab))
+
+    def cycle(n):
+        total, done, pos = 0.0, 0, PROMPT_LEN
+        while done < n:
+            m = min(CYCLE, n - done)
+            if pos + m > PROMPT_LEN + CYCLE:
+                eng.streams_set_position(PROMPT_LEN)
+                pos = PROMPT_LEN
+            _, ms = eng.streams_decode(m, return_ms=True)
+            total, done, pos = total + ms, done + m, pos + m
+        return total
+
+    cycle(max(args.warmup, 3))
+    eng.streams_set_position(PROMPT_LEN)
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    clocks = ClockSampler(gpu_index)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    total_ms = cycle(args.steps)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    value, max_ms = replicas.replica_throughput(args.steps * len(mine), total_ms, world, dist, "cuda")
+    ms_step = max_ms / args.steps
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        mean_pos = PROMPT_LEN + 1 + min(args.steps, CYCLE) / 2
+        step_bytes = info["stream_bytes"] + len(mine) * spec.kv_bytes_per_position() * mean_pos
+        gbs = step_bytes / (ms_step / 1000.0) / 1e9
+        line = {
+            "metric": f"decode tok/s (2.6B Q4_K_M, {len(mine)} streams per GPU, batched)", "value": value,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xint8->int32, f32", "data": "synthetic",
+            "config": {"workload": f"M26, {args.streams * world} independent greedy streams, {len(mine)} per GPU, "
+                                   f"{PROMPT_LEN}-token prompts, positions {PROMPT_LEN}..{PROMPT_LEN + CYCLE} "
+                                   f"(rewound every {CYCLE} tokens), n_ctx {n_ctx} per stream",
+                       "model": spec.name, "parallelism": f"dp{world} (streams)",
+                       "l2": "weights (1.5 GB) and caches exceed L2"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_kind": peak_kind, "bytes_per_step": step_bytes},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.streams:
+        run_streams(args)
     elif args.tp70:
         run_tp70(args)
     else:

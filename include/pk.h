@@ -212,6 +212,22 @@ int pk_decode_steps_device(pk_engine *eng, int n_steps, uint32_t *out_ids, float
  * before they are read again.  Invalidates prefix reuse beyond pos. */
 int pk_set_position(pk_engine *eng, int pos);
 
+/* Independent greedy streams on one engine, decoded together (no reference
+ * counterpart: the reference's engine holds one sequence, engine.rs; these
+ * serve many sequences per GPU).  Each stream has its own KV cache of n_ctx
+ * positions; one step decodes one token of every stream with the weights read
+ * once.  Every stream's tokens equal those pk_generate gives it alone.
+ * pk_streams_begin allocates n_streams caches (1 <= n_streams <= max_batch,
+ * at most 64, once per engine); pk_stream_prefill runs a prompt into stream
+ * s's cache and picks its next token (the engine's own sequence and prefix
+ * reuse are reset); pk_streams_decode writes [n_steps][n_streams] ids, as
+ * pk_decode_steps_device per stream; pk_streams_set_position rewinds every
+ * stream to pos (timing). */
+int pk_streams_begin(pk_engine *eng, int n_streams);
+int pk_stream_prefill(pk_engine *eng, int s, const uint32_t *prompt, int n);
+int pk_streams_decode(pk_engine *eng, int n_steps, uint32_t *out_ids, float *device_ms);
+int pk_streams_set_position(pk_engine *eng, int pos);
+
 /* One decode step run eagerly with CUDA events around every kernel: per
  * kernel name the launch count, device time and algorithmic bytes. */
 typedef struct {

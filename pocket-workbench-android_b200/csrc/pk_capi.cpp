@@ -415,6 +415,26 @@ int pk_set_position(pk_engine *e, int pos) {
   return e->eng.set_position(pos);
 }
 
+int pk_streams_begin(pk_engine *e, int n_streams) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.streams_begin(n_streams);
+}
+
+int pk_stream_prefill(pk_engine *e, int s, const uint32_t *prompt, int n) {
+  if (!e || !prompt) return set_error(PK_ERR_INVALID, "null argument");
+  return e->eng.stream_prefill(s, prompt, n);
+}
+
+int pk_streams_decode(pk_engine *e, int n_steps, uint32_t *out_ids, float *device_ms) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.streams_decode(n_steps, out_ids, device_ms);
+}
+
+int pk_streams_set_position(pk_engine *e, int pos) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.streams_set_position(pos);
+}
+
 int pk_decode_profile(pk_engine *e, pk_kernel_stat *out, int cap, int *n_out) {
   if (!e || (!out && cap > 0)) return set_error(PK_ERR_INVALID, "null argument");
   return e->eng.decode_profile(out, cap, n_out);

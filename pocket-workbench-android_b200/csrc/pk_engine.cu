@@ -40,6 +40,9 @@ Engine::~Engine() {
   cudaFree(d_decode_);
   cudaFree(d_rng_);
   cudaFree(d_sample_scratch_);
+  cudaFree(d_sk_);
+  cudaFree(d_sv_);
+  cudaFree(d_slogits_);
   cudaFreeHost(h_ids_);
   cudaFreeHost(h_pos_);
   cudaFreeHost(h_tok_);
@@ -962,6 +965,185 @@ int Engine::set_position(int pos) {
   next_pos_ = pos;
   if (kv_tokens_.size() > (size_t)pos) kv_tokens_.resize(pos);
   cached_prefill_len_ = std::min(cached_prefill_len_, (size_t)pos);
+  return PK_OK;
+}
+
+// ---- independent streams (no reference counterpart: the reference keeps one
+// sequence per engine).  Each stream has its own KV cache; a step decodes one
+// token of every stream in one batch, the weights read once for all.  The
+// step uses the b == 1 arithmetic for every stream (the sum of squares in
+// the f32_sum_sq order, scores in the f32_dot order, one attention CTA per
+// stream and head), and the lanes matvec equals the single-lane one bit for
+// bit, so each stream's tokens are those it gets decoded alone.
+int Engine::streams_begin(int n) {
+  if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
+  if (n < 1 || n > max_batch_ || n > 64) return set_error(PK_ERR_INVALID, "streams: 1..max_batch streams");
+  if (n_streams_) return set_error(PK_ERR_INVALID, "streams already begun");
+  PK_CK(cudaSetDevice(device_));
+  const size_t half = kv_bytes_ / 2;
+  PK_CK(cudaMalloc((void **)&d_sk_, half * n));
+  PK_CK(cudaMalloc((void **)&d_sv_, half * n));
+  PK_CK(cudaMemsetAsync(d_sk_, 0, half * n, st_));
+  PK_CK(cudaMemsetAsync(d_sv_, 0, half * n, st_));
+  const size_t aux = (size_t)n * vocab_ * 4 + 256 + (size_t)n * 4 * 4 + (size_t)n * n_ctx_ * 4;
+  PK_CK(cudaMalloc((void **)&d_slogits_, aux));
+  uint8_t *p = (uint8_t *)d_slogits_ + (size_t)n * vocab_ * 4 + 256 - (((size_t)n * vocab_ * 4) & 255);
+  d_sids_ = (uint32_t *)p;
+  d_stok_ = d_sids_ + n;
+  d_spos_ = (int *)(d_stok_ + n);
+  d_sstep_ = d_spos_ + n;
+  d_shist_ = (uint32_t *)(d_sstep_ + n);
+  PK_CK(cudaStreamSynchronize(st_));
+  n_streams_ = n;
+  spos_.assign(n, 0);
+  stok_.assign(n, 0);
+  sready_.assign(n, 0);
+  return PK_OK;
+}
+
+// The prompt into stream s's cache: the engine's prefill (32-token chunks,
+// lanes for two or more) with stream s's cache in place of the engine's; the
+// greedy pick of its last logits is the stream's next token.
+int Engine::stream_prefill(int s, const uint32_t *prompt, int n) {
+  if (s < 0 || s >= n_streams_) return set_error(PK_ERR_INVALID, "no such stream");
+  if (n <= 0 || n > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "prompt empty or longer than n_ctx");
+  for (int i = 0; i < n; i++)
+    if (prompt[i] >= (uint32_t)vocab_) return set_error(PK_ERR_INVALID, "token out of vocab");
+  PK_CK(cudaSetDevice(device_));
+  const size_t per = kv_bytes_ / 2 / 4;  // floats of one cache
+  float *k0 = d_kcache_, *v0 = d_vcache_;
+  d_kcache_ = d_sk_ + (size_t)s * per;
+  d_vcache_ = d_sv_ + (size_t)s * per;
+  kv_tokens_.clear();
+  cached_prefill_len_ = 0;
+  int rc = PK_OK;
+  const int chunk = std::min(max_batch_, 32);
+  if (n > chunk) {
+    bool stopped = false;
+    rc = prefill_lanes(prompt, n, 0, chunk, &stopped);
+    if (!rc && stopped) rc = set_error(PK_ERR_STOPPED, "generation stopped");
+  } else {
+    for (int i = 0; i < n; i++) {
+      h_ids_[i] = prompt[i];
+      h_pos_[i] = i;
+    }
+    cudaError_t e = cudaMemcpyAsync(d_ids_, h_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st_);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_pos_, h_pos_, n * sizeof(int), cudaMemcpyHostToDevice, st_);
+    rc = e != cudaSuccess ? cuda_error(e, "stream prefill ids") : enqueue_forward(n, true, false);
+    const cudaError_t es = cudaStreamSynchronize(st_);
+    if (!rc && es != cudaSuccess) rc = cuda_error(es, "stream prefill");
+  }
+  uint32_t tok = 0;
+  if (!rc) rc = argmax(&tok);
+  d_kcache_ = k0;
+  d_vcache_ = v0;
+  have_logits_ = false;  // the engine's own sequence is not what the logits belong to
+  next_pos_ = 0;
+  if (rc) return rc;
+  spos_[s] = n;
+  stok_[s] = tok;
+  sready_[s] = 1;
+  return PK_OK;
+}
+
+int Engine::enqueue_streams_step() {
+  const Config &c = cfg_;
+  const int S = n_streams_, ne = c.n_embd, dh = c.head_dim, qdim = c.n_head * dh, kdim = c.n_head_kv * dh, ff = c.n_ff;
+  const size_t layer_kv = (size_t)c.n_head_kv * n_ctx_ * dh, stride = (size_t)c.n_layer * layer_kv;
+  PK_CK(launch_dequant_rows(embd_type_, embd_raw_, embd_row_bytes_, ne, d_sids_, S, x_, st_));
+  for (int l = 0; l < c.n_layer; l++) {
+    const LayerDev &L = layers_[l];
+    float *kc = d_sk_ + l * layer_kv, *vc = d_sv_ + l * layer_kv;
+    Q8Dev a = act_;
+    a.k = ne; a.b = S;
+    PK_CK(launch_rmsnorm_q8(x_, L.attn_norm, c.rms_eps, ne, S, a, nullptr, st_, true));
+    const MvOut qkv[3] = {{L.q, q_, 1, qdim, false}, {L.k, k_, 1, kdim, false}, {L.v, v_, 1, kdim, false}};
+    PK_CK(launch_mv_multi(3, qkv, a, st_));
+    PK_CK(launch_rope_kv(q_, k_, v_, S, d_spos_, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
+                         n_ctx_, kc, vc, st_, stride));
+    AttnArgs at{};
+    at.q = q_; at.kcache = kc; at.vcache = vc; at.pos = d_spos_; at.out = attn_; at.b = S;
+    at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh; at.n_ctx = n_ctx_;
+    at.scale = 1.0f / sqrtf((float)dh); at.scores = att_scores_;
+    at.lane_stride = stride; at.b1_order = 1;
+    a.k = qdim;
+    at.q8 = a;
+    PK_CK(launch_attention(at, st_));
+    PK_CK(launch_mv_lanes(L.o, a, x_, 1, ne, true, st_));
+    a.k = ne;
+    PK_CK(launch_rmsnorm_q8(x_, L.ffn_norm, c.rms_eps, ne, S, a, nullptr, st_, true));
+    const MvOut gu[2] = {{L.gate, gate_, 1, ff, false}, {L.up, up_, 1, ff, false}};
+    PK_CK(launch_mv_multi(2, gu, a, st_));
+    a.k = ff;
+    PK_CK(launch_swiglu_q8(gate_, up_, ff, S, a, h_, st_));
+    PK_CK(launch_mv_lanes(L.down, a, x_, 1, ne, true, st_));
+  }
+  Q8Dev a = act_;
+  a.k = ne; a.b = S;
+  PK_CK(launch_rmsnorm_q8(x_, output_norm_, c.rms_eps, ne, S, a, nullptr, st_, true));
+  PK_CK(launch_mv_lanes(output_, a, d_slogits_, 1, vocab_, false, st_));
+  for (int s = 0; s < S; s++) {
+    PK_CK(launch_argmax(d_slogits_ + (size_t)s * vocab_, vocab_, d_stok_ + s, st_));
+    PK_CK(launch_advance(d_stok_ + s, d_sids_ + s, d_spos_ + s, d_shist_ + (size_t)s * n_ctx_, d_sstep_ + s, st_));
+  }
+  return PK_OK;
+}
+
+// n_steps tokens of every stream, as decode_steps_device: the token picked
+// last, then the next n_steps - 1 (the n_steps steps also pick the token the
+// next call starts with).  out_ids: [n_steps][n_streams].
+int Engine::streams_decode(int n_steps, uint32_t *out_ids, float *device_ms) {
+  if (!n_streams_) return set_error(PK_ERR_INVALID, "no streams");
+  if (n_steps < 1) return set_error(PK_ERR_INVALID, "n_steps must be >= 1");
+  const int S = n_streams_;
+  for (int s = 0; s < S; s++) {
+    if (!sready_[s]) return set_error(PK_ERR_INVALID, "stream " + std::to_string(s) + " has no prefill");
+    if (spos_[s] + n_steps > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
+  }
+  PK_CK(cudaSetDevice(device_));
+  std::vector<int> zero(S, 0);
+  PK_CK(cudaMemcpyAsync(d_sids_, stok_.data(), S * 4, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(d_spos_, spos_.data(), S * 4, cudaMemcpyHostToDevice, st_));
+  PK_CK(cudaMemcpyAsync(d_sstep_, zero.data(), S * 4, cudaMemcpyHostToDevice, st_));
+  cudaEvent_t e0, e1;
+  PK_CK(cudaEventCreate(&e0));
+  PK_CK(cudaEventCreate(&e1));
+  cudaError_t e = cudaEventRecord(e0, st_);
+  int rc = PK_OK;
+  for (int i = 0; i < n_steps && e == cudaSuccess && !rc; i++) rc = enqueue_streams_step();
+  if (e == cudaSuccess) e = cudaEventRecord(e1, st_);
+  std::vector<uint32_t> hist((size_t)S * n_ctx_);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(hist.data(), d_shist_, hist.size() * 4, cudaMemcpyDeviceToHost, st_);
+  const cudaError_t es = cudaStreamSynchronize(st_);
+  float ms = 0.0f;
+  if (e == cudaSuccess && es == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_error(e, "streams decode");
+  if (es != cudaSuccess) return cuda_error(es, "streams decode");
+  for (int s = 0; s < S; s++) {
+    const uint32_t *hs = hist.data() + (size_t)s * n_ctx_;
+    if (out_ids) {
+      out_ids[s] = stok_[s];
+      for (int i = 1; i < n_steps; i++) out_ids[(size_t)i * S + s] = hs[i - 1];
+    }
+    stok_[s] = hs[n_steps - 1];
+    spos_[s] += n_steps;
+  }
+  if (device_ms) *device_ms = ms;
+  return PK_OK;
+}
+
+// Every stream's position set to pos (<= each stream's length): the next
+// step decodes at pos, over the cache entries already there (timing runs).
+int Engine::streams_set_position(int pos) {
+  if (!n_streams_) return set_error(PK_ERR_INVALID, "no streams");
+  if (pos < 1 || pos >= n_ctx_) return set_error(PK_ERR_INVALID, "position must be in 1..n_ctx-1");
+  for (int s = 0; s < n_streams_; s++) {
+    if (!sready_[s]) return set_error(PK_ERR_INVALID, "stream " + std::to_string(s) + " has no prefill");
+    spos_[s] = pos;
+  }
   return PK_OK;
 }
 

@@ -54,6 +54,11 @@ class Engine {
                uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats);
   int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
   int set_position(int pos);
+  // Independent streams, each with its own KV cache, decoded together.
+  int streams_begin(int n_streams);
+  int stream_prefill(int s, const uint32_t *prompt, int n);
+  int streams_decode(int n_steps, uint32_t *out_ids, float *device_ms);
+  int streams_set_position(int pos);
   int decode_profile(pk_kernel_stat *out, int cap, int *n_out);
   int selftest_bounded_wait(int *status);
   int set_debug(bool on);
@@ -64,6 +69,7 @@ class Engine {
   enum { KV_RECORD = 1, KV_WAIT = 2 };
   int enqueue_forward(int b, bool want_logits, bool cancellable, int li = 0, int kv = 0);
   int prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, bool *stopped);
+  int enqueue_streams_step();
   int setup_decode();
   int check_decode_error();
   int ensure_graphs();
@@ -98,6 +104,16 @@ class Engine {
   // pinned host staging
   uint32_t *h_ids_ = nullptr, *h_tok_ = nullptr;
   int *h_pos_ = nullptr;
+  // streams: one KV cache each ([stream][layer][...] as the engine's own), the
+  // batch's token ids / positions / picks on the device, each stream's
+  // history of picks, and the host view of every stream
+  int n_streams_ = 0;
+  float *d_sk_ = nullptr, *d_sv_ = nullptr, *d_slogits_ = nullptr;
+  uint32_t *d_sids_ = nullptr, *d_stok_ = nullptr, *d_shist_ = nullptr;
+  int *d_spos_ = nullptr, *d_sstep_ = nullptr;
+  std::vector<int> spos_;
+  std::vector<uint32_t> stok_;
+  std::vector<char> sready_;
   // temperature / top-p sampling: the Rng state and the sampler's scratch
   unsigned long long *d_rng_ = nullptr, h_rng_ = 0;
   uint8_t *d_sample_scratch_ = nullptr;

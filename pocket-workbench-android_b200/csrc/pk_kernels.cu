@@ -300,7 +300,7 @@ __device__ float sum_sq_chain(const float *sq, int n, float *red) {
 // memory (dynamic, 3 x k floats, k a multiple of 32); each warp then
 // quantises its blocks three at a time.
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
-                             float *__restrict__ xn) {
+                             float *__restrict__ xn, int neon) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[40];
   const int n16 = (k + 15) & ~15;
@@ -319,7 +319,7 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
     reinterpret_cast<float4 *>(sq)[i] = make_float4(fmul(v.x, v.x), fmul(v.y, v.y), fmul(v.z, v.z), fmul(v.w, v.w));
   }
   __syncthreads();
-  const float ss = sum_sq_chain(sq, k, red);
+  const float ss = neon ? sum_sq_neon(xs, k, red) : sum_sq_chain(sq, k, red);
   const float s = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)k), eps)));
   const int nb = k >> 5, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw_ = blockDim.x >> 5;
   for (int b0 = w; b0 < nb; b0 += 3 * nw_) {
@@ -344,12 +344,12 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
 }
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
-                              cudaStream_t st) {
+                              cudaStream_t st, bool neon) {
   if (k % 32 != 0 || ((uintptr_t)x | (uintptr_t)nw) % 16 != 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)3 * ((k + 15) & ~15) * 4;
   cudaError_t e = set_smem(k_rmsnorm_q8, smem);
   if (e != cudaSuccess) return e;
-  return launch(k_rmsnorm_q8, dim3(b), dim3(256), smem, st, x, nw, eps, k, act, xn);
+  return launch(k_rmsnorm_q8, dim3(b), dim3(256), smem, st, x, nw, eps, k, act, xn, neon ? 1 : 0);
 }
 
 // SwiGLU (model.rs:1105-1115: h = g / (1 + exp(-g)) * u) of token-major g, u [b][k], then Q8 of
@@ -1104,7 +1104,7 @@ cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, lo
 // place; the rest write one K element (rotated) and one V element to the
 // cache.  grid = (b, element blocks).
 __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *pos, const float *rc, const float *rs,
-                          int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc) {
+                          int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc, size_t lane_stride) {
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
@@ -1122,6 +1122,8 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
     return;
   }
   const int e = i - nq, h = e / dh, d = e - h * dh;
+  kc += (size_t)bi * lane_stride;  // this token's own cache when every token has one
+  vc += (size_t)bi * lane_stride;
   const float *kr = k + (long)bi * kdim;
   float o = kr[e];
   if (d < 2 * half) {
@@ -1136,10 +1138,10 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
 
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rc,
                            const float *rs, int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc,
-                           cudaStream_t st) {
+                           cudaStream_t st, size_t lane_stride) {
   const int total = n_head * half + n_kv * dh;
   return launch(k_rope_kv, dim3(b, (total + 127) / 128), dim3(128), 0, st, q, k, v, pos, rc, rs, half, dh, n_head,
-                n_kv, n_ctx, kc, vc);
+                n_kv, n_ctx, kc, vc, lane_stride);
 }
 
 __global__ void k_expf(const float *x, float *out, long n) {
@@ -1179,8 +1181,8 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   const long hb = (long)bi * a.n_head + h;
   for (int d = tid; d < dh; d += blockDim.x) qs[d] = a.q[hb * dh + d];
   __syncthreads();
-  const float *kb = a.kcache + (size_t)kh * a.n_ctx * dh;
-  const float *vb = a.vcache + (size_t)kh * a.n_ctx * dh;
+  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * dh;
+  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * dh;
   float *sc = a.scores + hb * a.n_ctx;
   float mx = -INFINITY;
   const size_t nc = (size_t)a.n_ctx;
@@ -1415,7 +1417,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 }
 
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
-  if (a.b > 1 && a.n_ctx % 4 == 0 && (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
+  if (a.b > 1 && !a.b1_order && a.lane_stride == 0 && a.n_ctx % 4 == 0 &&
+      (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
     const size_t smem = ac_smem(a.dh);
     const int G = ac_group(a.dh);
     const dim3 grid((a.b + G - 1) / G, a.n_head);
@@ -1425,7 +1428,7 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
     return launch(kern, grid, dim3(AC_THREADS), smem, st, a);
   }
   const int threads = a.dh < 128 ? 128 : 256;
-  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, a.b == 1 ? 1 : 0);
+  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, (a.b == 1 || a.b1_order) ? 1 : 0);
 }
 
 // ------------------------------------------------------------ temperature / top-p sampling

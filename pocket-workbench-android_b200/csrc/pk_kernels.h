@@ -44,8 +44,10 @@ cudaError_t launch_dequant_rows(int type, const void *raw, size_t row_bytes, int
 // Q8Act::prepare on x[i * xs_elem + bi * xs_lane].
 cudaError_t launch_q8(const float *x, long xs_elem, long xs_lane, int k, int b, Q8Dev act, cudaStream_t st);
 // RMSNorm (model.rs:812-822) + Q8 of token-major x [b][k]; xn (optional) gets the normed floats.
+// neon: the sum of squares in the reference's b == 1 order (simd.rs:47-64)
+// for every row, instead of the b > 1 sequential chain.
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
-                              cudaStream_t st);
+                              cudaStream_t st, bool neon = false);
 
 // SwiGLU + Q8 of token-major g, u [b][k]; h (optional) gets the floats.
 cudaError_t launch_swiglu_q8(const float *g, const float *u, int k, int b, Q8Dev act, float *h, cudaStream_t st);
@@ -92,7 +94,7 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
 // RoPE + KV write for b tokens (token-major q [b][qdim], k/v [b][kdim]).
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rope_cos,
                            const float *rope_sin, int half, int dh, int n_head, int n_kv, int n_ctx, float *kcache,
-                           float *vcache, cudaStream_t st);
+                           float *vcache, cudaStream_t st, size_t lane_stride = 0);
 // out[i] = expf_lib(x[i]) (the C library's expf, bit for bit).
 cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st);
 
@@ -107,6 +109,8 @@ struct AttnArgs {
   float scale;
   float *scores;       // scratch [b][n_head][n_ctx]
   Q8Dev q8{};          // optional (q8.q != nullptr): Q8 of out, k = n_head * dh
+  size_t lane_stride = 0;  // floats from token i's K/V cache to token i + 1's (0: one shared cache)
+  int b1_order = 0;        // 1: every token scored in the b == 1 order (simd.rs:19-43), one CTA each
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 

@@ -39,6 +39,7 @@ SYMBOLS = [
     "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
     "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
     "pk_tp_info_get", "pk_tp_split", "pk_tp_pick", "pk_sample_scratch_bytes", "pk_sample",
+    "pk_streams_begin", "pk_stream_prefill", "pk_streams_decode", "pk_streams_set_position",
 ]
 
 
@@ -121,6 +122,8 @@ def lib():
         "pk_argmax": ([P, C.POINTER(U32)], I),
         "pk_generate": ([P, P, I, C.POINTER(GenOpts), TOKEN_CB, P, P, I, C.POINTER(I), C.POINTER(GenStats)], I),
         "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_position": ([P, I], I),
+        "pk_streams_begin": ([P, I], I), "pk_stream_prefill": ([P, I, P, I], I),
+        "pk_streams_decode": ([P, I, P, C.POINTER(C.c_float)], I), "pk_streams_set_position": ([P, I], I),
         "pk_decode_profile": ([P, C.POINTER(KernelStat), I, C.POINTER(I)], I), "pk_set_debug": ([P, I], I),
         "pk_selftest_bounded_wait": ([P, C.POINTER(I)], I),
         "pk_get_dump": ([P, C.c_char_p, P, I, C.POINTER(I)], I),
@@ -374,6 +377,30 @@ class Engine:
 
     def set_position(self, pos: int):
         _check(lib().pk_set_position(self.h, pos))
+
+    def streams_begin(self, n_streams: int):
+        """n_streams independent sequences, each with its own KV cache, decoded together."""
+        _check(lib().pk_streams_begin(self.h, n_streams))
+        self.n_streams = n_streams
+
+    def stream_prefill(self, s: int, prompt):
+        import numpy as np
+
+        p = np.ascontiguousarray(prompt, np.uint32)
+        _check(lib().pk_stream_prefill(self.h, s, p.ctypes.data_as(C.c_void_p), len(p)))
+
+    def streams_decode(self, n_steps: int, return_ms: bool = False):
+        """n_steps greedy tokens of every stream: a list per stream (optionally the device time, ms)."""
+        import numpy as np
+
+        out = np.zeros((max(n_steps, 1), self.n_streams), np.uint32)
+        ms = C.c_float()
+        _check(lib().pk_streams_decode(self.h, n_steps, out.ctypes.data_as(C.c_void_p), C.byref(ms)))
+        ids = [out[:n_steps, s].tolist() for s in range(self.n_streams)]
+        return (ids, ms.value) if return_ms else ids
+
+    def streams_set_position(self, pos: int):
+        _check(lib().pk_streams_set_position(self.h, pos))
 
     def decode_profile(self) -> list:
         stats = (KernelStat * 128)()

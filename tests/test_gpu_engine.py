@@ -175,6 +175,31 @@ def test_prefill_lanes_equal_chunk_order(pk, paths, name, n):
     assert a.decode_steps_device(8) == b.decode_steps_device(8)
 
 
+@pytest.mark.parametrize("name", list(MODELS))
+def test_streams_equal_each_stream_alone(pk, paths, name):
+    """Independent streams decoded together (one batched step per token, every
+    stream at its own position over its own KV cache) give every stream the
+    greedy tokens generate() gives it alone: prompts of 1 token (the b == 1
+    prefill), 20 (one chunk) and 45 / 70 (stream lanes), decoded in two calls."""
+    spec = MODELS[name]
+    prompts = [synth.prompt_ids(31 + i, n, spec.n_vocab) for i, n in enumerate((1, 20, 45, 70))]
+    want = [pk.Engine(paths[name], n_ctx=256).generate(p, 48, stop_at_eog=False)["gen_ids"] for p in prompts]
+    e = pk.Engine(paths[name], n_ctx=256)
+    e.streams_begin(len(prompts))
+    with pytest.raises(pk.PkError):
+        e.streams_decode(4)  # no stream has a prompt yet
+    for s, p in enumerate(prompts):
+        e.stream_prefill(s, p)
+    first = e.streams_decode(20)
+    rest = e.streams_decode(28)
+    for s in range(len(prompts)):
+        assert first[s] + rest[s] == want[s]
+    with pytest.raises(pk.PkError):
+        e.stream_prefill(len(prompts), prompts[0])
+    with pytest.raises(pk.PkError):
+        e.streams_begin(2)
+
+
 def test_bounded_wait_runs_out_and_engine_recovers(pk, paths):
     """Failure detection without a GPU fault: one persistent-kernel launch
     whose phase inputs never arrive (its readers wait for a tag nothing
