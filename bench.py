@@ -533,8 +533,12 @@ def run_streams(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    if args.profile_window:
+        torch.cuda.profiler.start()
     total_ms = cycle(args.steps)
     torch.cuda.synchronize()
+    if args.profile_window:
+        torch.cuda.profiler.stop()
     clk = clocks.stop()
     if dist:
         dist.barrier()

@@ -31,6 +31,7 @@ static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 Engine::~Engine() {
   if (st_) cudaStreamSynchronize(st_);
   release_graphs();
+  if (g_streams_) cudaGraphExecDestroy(g_streams_);
   cudaFree(d_weights_);
   cudaFree(d_kcache_);
   cudaFree(d_vcache_);
@@ -1082,10 +1083,8 @@ int Engine::enqueue_streams_step() {
   a.k = ne; a.b = S;
   PK_CK(launch_rmsnorm_q8(x_, output_norm_, c.rms_eps, ne, S, a, nullptr, st_, true));
   PK_CK(launch_mv_lanes(output_, a, d_slogits_, 1, vocab_, false, st_));
-  for (int s = 0; s < S; s++) {
-    PK_CK(launch_argmax(d_slogits_ + (size_t)s * vocab_, vocab_, d_stok_ + s, st_));
-    PK_CK(launch_advance(d_stok_ + s, d_sids_ + s, d_spos_ + s, d_shist_ + (size_t)s * n_ctx_, d_sstep_ + s, st_));
-  }
+  PK_CK(launch_argmax(d_slogits_, vocab_, d_stok_, st_, S));
+  PK_CK(launch_advance(d_stok_, d_sids_, d_spos_, d_shist_, d_sstep_, st_, S, (size_t)n_ctx_));
   return PK_OK;
 }
 
@@ -1101,6 +1100,22 @@ int Engine::streams_decode(int n_steps, uint32_t *out_ids, float *device_ms) {
     if (spos_[s] + n_steps > n_ctx_) return set_error(PK_ERR_CONTEXT_FULL, "context full");
   }
   PK_CK(cudaSetDevice(device_));
+  if (!g_streams_) {  // every pointer of the step is fixed once the streams exist: one graph, replayed
+    cudaGraph_t graph = nullptr;
+    PK_CK(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_streams_step();
+    const cudaError_t ee = cudaStreamEndCapture(st_, &graph);
+    if (rc || ee != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc ? rc : cuda_error(ee, "streams graph capture");
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&g_streams_, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      g_streams_ = nullptr;
+      return cuda_error(ei, "streams graph instantiate");
+    }
+  }
   std::vector<int> zero(S, 0);
   PK_CK(cudaMemcpyAsync(d_sids_, stok_.data(), S * 4, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(d_spos_, spos_.data(), S * 4, cudaMemcpyHostToDevice, st_));
@@ -1109,8 +1124,7 @@ int Engine::streams_decode(int n_steps, uint32_t *out_ids, float *device_ms) {
   PK_CK(cudaEventCreate(&e0));
   PK_CK(cudaEventCreate(&e1));
   cudaError_t e = cudaEventRecord(e0, st_);
-  int rc = PK_OK;
-  for (int i = 0; i < n_steps && e == cudaSuccess && !rc; i++) rc = enqueue_streams_step();
+  for (int i = 0; i < n_steps && e == cudaSuccess; i++) e = cudaGraphLaunch(g_streams_, st_);
   if (e == cudaSuccess) e = cudaEventRecord(e1, st_);
   std::vector<uint32_t> hist((size_t)S * n_ctx_);
   if (e == cudaSuccess) e = cudaMemcpyAsync(hist.data(), d_shist_, hist.size() * 4, cudaMemcpyDeviceToHost, st_);
@@ -1119,7 +1133,6 @@ int Engine::streams_decode(int n_steps, uint32_t *out_ids, float *device_ms) {
   if (e == cudaSuccess && es == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
-  if (rc) return rc;
   if (e != cudaSuccess) return cuda_error(e, "streams decode");
   if (es != cudaSuccess) return cuda_error(es, "streams decode");
   for (int s = 0; s < S; s++) {

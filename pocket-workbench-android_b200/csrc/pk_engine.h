@@ -150,6 +150,7 @@ class Engine {
 
   // decode graphs: fwd1 = one b=1 forward with logits; step = argmax + advance + fwd1
   cudaGraphExec_t g_fwd1_ = nullptr, g_step_ = nullptr;
+  cudaGraphExec_t g_streams_ = nullptr;  // one batched streams step (its state lives on the device)
 
   // Engine::generate prefix-reuse state (model.rs:689-694)
   std::vector<uint32_t> kv_tokens_;

@@ -1404,6 +1404,122 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
 
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 
+// b == 1 order attention (k_attn with dot8) for one token per CTA with the
+// head's K and V brought through shared memory in 128-position tiles
+// (double-buffered cp.async), so the score dots and the per-d chains read
+// shared memory instead of waiting on global loads:
+//   pass 1: thread t scores position p0 + t of the tile: eight chains over d
+//           (d = 8j + u in chain u), reduced ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7));
+//   pass 2: the tile's V rows and e_p; thread d < DH runs its chain over the
+//           tile's positions in order (zero weights skipped), thread DH the
+//           sum chain.
+// Same operations in the same order as k_attn, so the same bits.  Needs
+// n_ctx % 4 == 0 and 16-byte aligned K, V and score rows.
+template <int DH>
+__global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
+  constexpr int P = 128, NT = DH == 64 ? 128 : 256, TILE = DH * P;
+  extern __shared__ __align__(16) float at_sm[];
+  float *const es = at_sm + 2 * TILE;  // two tiles of TILE floats, then e: [2][P]
+  __shared__ float qs[DH];
+  __shared__ float red[40];
+  __shared__ float s_inv;
+  const int h = blockIdx.x, bi = blockIdx.y, tid = threadIdx.x;
+  const int kh = h / (a.n_head / a.n_kv);
+  pdl_trigger();
+  pdl_wait();
+  const int pos = a.pos[bi], n = pos + 1, nt = (n + P - 1) / P;
+  const long hb = (long)bi * a.n_head + h;
+  if (tid < DH) qs[tid] = a.q[hb * DH + tid];
+  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  float *sc = a.scores + hb * a.n_ctx;
+  // K tile t: [d][P] from the d-major cache, 16-byte chunks holding a position <= pos
+  auto load_k = [&](int t, float *dst) {
+    const int p0 = t * P, nq = (min(P, n - p0) + 3) >> 2;
+    for (int c = tid; c < DH * (P / 4); c += NT) {
+      const int d = c >> 5, j = c & 31;
+      if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+    }
+  };
+  load_k(0, at_sm);
+  cp_async_commit();
+  float mx = -INFINITY;
+  for (int t = 0; t < nt; t++) {
+    const float *cur = at_sm + (t & 1) * TILE;
+    if (t + 1 < nt) {
+      load_k(t + 1, at_sm + ((t + 1) & 1) * TILE);
+      cp_async_commit();
+      cp_async_wait1();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    const int p = t * P + tid;
+    if (tid < P && p <= pos) {
+      float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int d = 0; d < DH; d += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], cur[(d + u) * P + tid]));
+      }
+      float sv = fadd(fadd(c[0], c[1]), fadd(c[2], c[3]));
+      sv = fadd(sv, fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
+      sv = fmul(sv, a.scale);
+      sc[p] = sv;
+      mx = sv > mx ? sv : mx;
+    }
+    __syncthreads();
+  }
+  const float M = block_max(mx, red);
+  for (int p = tid; p <= pos; p += NT) sc[p] = expf_lib(fsub(sc[p], M));
+  __syncthreads();
+  // V tile t: P rows of DH floats (contiguous), and e of its positions
+  auto load_v = [&](int t, float *dst, float *edst) {
+    const int p0 = t * P, nv = min(P, n - p0);
+    const float *src = vb + (size_t)p0 * DH;
+    for (int c = tid; c < nv * (DH / 4); c += NT) cp_async16(dst + 4 * c, src + 4 * c);
+    if (tid < ((nv + 3) >> 2)) cp_async16(edst + 4 * tid, sc + p0 + 4 * tid);
+  };
+  load_v(0, at_sm, es);
+  cp_async_commit();
+  float acc = 0.0f, sum = 0.0f;
+  for (int t = 0; t < nt; t++) {
+    const float *cur = at_sm + (t & 1) * TILE, *ec = es + (t & 1) * P;
+    if (t + 1 < nt) {
+      load_v(t + 1, at_sm + ((t + 1) & 1) * TILE, es + ((t + 1) & 1) * P);
+      cp_async_commit();
+      cp_async_wait1();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    const int nv = min(P, n - t * P);
+    if (tid < DH) {
+#pragma unroll 8
+      for (int j = 0; j < nv; j++) {
+        const float e = ec[j];
+        const float v = cur[j * DH + tid];
+        if (e != 0.0f) acc = fadd(acc, fmul(e, v));
+      }
+    } else if (tid == DH) {
+#pragma unroll 8
+      for (int j = 0; j < nv; j++) sum = fadd(sum, ec[j]);
+    }
+    __syncthreads();
+  }
+  if (tid == DH) s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+  __syncthreads();
+  if (tid < DH) {
+    const float o = fmul(acc, s_inv);
+    a.out[hb * DH + tid] = o;
+    if (a.q8.q) {  // warp w holds block (h * DH + 32 w) / 32 of the token's row
+      const int qk = a.n_head * DH, blk = (h * DH + tid) >> 5;
+      q8_block_lane(o, tid & 31, a.q8.q + (long)bi * qk + blk * 32, a.q8.d + (long)bi * (qk >> 5) + blk,
+                    a.q8.s + (long)bi * (qk >> 5) + blk);
+    }
+  }
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.dh > 256 || a.dh % 4 != 0 || a.n_head % a.n_kv != 0) return cudaErrorInvalidValue;
   if (a.q8.q && a.dh % 32 != 0) {  // quantise separately
@@ -1427,8 +1543,17 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     return launch(kern, grid, dim3(AC_THREADS), smem, st, a);
   }
+  const bool dot8 = a.b == 1 || a.b1_order;
+  if (dot8 && (a.dh == 64 || a.dh == 128) && a.n_ctx % 4 == 0 && a.lane_stride % 4 == 0 &&
+      (((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.scores) & 15) == 0) {
+    const size_t smem = (size_t)(2 * a.dh * 128 + 2 * 128) * 4;
+    void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_b1t<64> : k_attn_b1t<128>;
+    cudaError_t e = set_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, dim3(a.n_head, a.b), dim3(a.dh == 64 ? 128 : 256), smem, st, a);
+  }
   const int threads = a.dh < 128 ? 128 : 256;
-  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, (a.b == 1 || a.b1_order) ? 1 : 0);
+  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, dot8 ? 1 : 0);
 }
 
 // ------------------------------------------------------------ temperature / top-p sampling
@@ -1586,11 +1711,18 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, in
   __shared__ int si[32];
   pdl_trigger();
   pdl_wait();
+  x += (size_t)blockIdx.x * n;  // one row per CTA
+  out += blockIdx.x;
   float bv = -INFINITY;
   int bi = INT_MAX;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = x[i];
-    if (v > bv) { bv = v; bi = i; }
+  const int nt = blockDim.x;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * nt) {  // eight loads in flight, then compared in index order
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = i0 + u * nt < n ? x[i0 + u * nt] : -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (v[u] > bv) { bv = v[u]; bi = i0 + u * nt; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -1607,22 +1739,30 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, in
   }
 }
 
-cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st) {
-  return launch(k_argmax, dim3(1), dim3(1024), 0, st, x, n, out_idx);
+cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st, int rows) {
+  if (rows < 1) return cudaErrorInvalidValue;
+  return launch(k_argmax, dim3(rows), dim3(1024), 0, st, x, n, out_idx);
 }
 
-__global__ void k_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step) {
+// Row r: ids[r] = tok[r], pos[r] += 1, hist[r * hist_stride + step[r]] = tok[r], step[r] += 1.
+__global__ void k_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, int rows,
+                          size_t hist_stride) {
   pdl_trigger();
   pdl_wait();
-  const uint32_t t = *tok;
-  ids[0] = t;
-  pos[0] += 1;
-  hist[*step] = t;
-  *step += 1;
+  const int r = threadIdx.x;
+  if (r >= rows) return;
+  const uint32_t t = tok[r];
+  ids[r] = t;
+  pos[r] += 1;
+  hist[(size_t)r * hist_stride + step[r]] = t;
+  step[r] += 1;
 }
 
-cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st) {
-  return launch(k_advance, dim3(1), dim3(1), 0, st, tok, ids, pos, hist, step);
+cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st,
+                           int rows, size_t hist_stride) {
+  if (rows < 1 || rows > 1024) return cudaErrorInvalidValue;
+  return launch(k_advance, dim3(1), dim3(rows <= 32 ? 32 : (rows + 31) & ~31), 0, st, tok, ids, pos, hist, step,
+                rows, hist_stride);
 }
 
 }  // namespace pk

@@ -122,9 +122,12 @@ cudaError_t launch_sample(const float *logits, int n, float temp, float top_p, u
                           uint32_t *tok, cudaStream_t st);
 
 // First index of the maximum (sampler.rs:26-36); NaNs never win.
-cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st);
-// Decode feedback on the device: ids[0] = *tok; pos[0] += 1; hist[*step] = *tok; *step += 1.
-cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st);
+// rows > 1: one index per row of x [rows][n] into out_idx[row].
+cudaError_t launch_argmax(const float *x, int n, uint32_t *out_idx, cudaStream_t st, int rows = 1);
+// Decode feedback on the device, per row r < rows: ids[r] = tok[r]; pos[r] += 1;
+// hist[r * hist_stride + step[r]] = tok[r]; step[r] += 1.
+cudaError_t launch_advance(const uint32_t *tok, uint32_t *ids, int *pos, uint32_t *hist, int *step, cudaStream_t st,
+                           int rows = 1, size_t hist_stride = 0);
 
 // Device address of pk_matmul_noalloc's fixed scratch on the current device
 // (pk_noalloc.cu); looked up once per device.
