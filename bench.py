@@ -52,6 +52,9 @@ def parse_args():
     p.add_argument("--streams", type=int, default=0,
                    help="independent M26 streams per GPU decoded together (the data-parallel streams case)")
     p.add_argument("--stream-ctx", type=int, default=512, help="KV positions of each stream")
+    p.add_argument("--stream-pos", type=int, default=None,
+                   help="decode the streams at this position (past the prompt: zero-filled cache entries; "
+                        "the long-context timing case)")
     p.add_argument("--prefill-only", action="store_true",
                    help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
     p.add_argument("--profile-window", action="store_true",
@@ -500,8 +503,9 @@ def run_streams(args):
     path = synth.m26_path(args.model_dir, spec=spec)
     mine = replicas.assign_streams(args.streams * world, rank, world)
     n_ctx = args.stream_ctx
-    if PROMPT_LEN + CYCLE > n_ctx:
-        raise SystemExit(f"--stream-ctx must be at least {PROMPT_LEN + CYCLE}")
+    p0 = args.stream_pos or PROMPT_LEN
+    if p0 < PROMPT_LEN or p0 + CYCLE > n_ctx:
+        raise SystemExit(f"need {PROMPT_LEN} <= --stream-pos and --stream-pos + {CYCLE} <= --stream-ctx")
     eng = pk.Engine(path, n_ctx=n_ctx, max_batch=max(32, len(mine)), device=local)
     info = eng.info
     eng.streams_begin(len(mine))
@@ -509,18 +513,19 @@ def run_streams(args):
         eng.stream_prefill(s, synth.prompt_ids(1000 + sid, PROMPT_LEN, spec.n_vocab))
 
     def cycle(n):
-        total, done, pos = 0.0, 0, PROMPT_LEN
+        total, done, pos = 0.0, 0, p0
         while done < n:
             m = min(CYCLE, n - done)
-            if pos + m > PROMPT_LEN + CYCLE:
-                eng.streams_set_position(PROMPT_LEN)
-                pos = PROMPT_LEN
+            if pos + m > p0 + CYCLE:
+                eng.streams_set_position(p0)
+                pos = p0
             _, ms = eng.streams_decode(m, return_ms=True)
             total, done, pos = total + ms, done + m, pos + m
         return total
 
+    eng.streams_set_position(p0)
     cycle(max(args.warmup, 3))
-    eng.streams_set_position(PROMPT_LEN)
+    eng.streams_set_position(p0)
     gpu_index = local
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -546,7 +551,7 @@ def run_streams(args):
     ms_step = max_ms / args.steps
     if rank == 0:
         hbm, peak_kind = peaks()
-        mean_pos = PROMPT_LEN + 1 + min(args.steps, CYCLE) / 2
+        mean_pos = p0 + 1 + min(args.steps, CYCLE) / 2
         step_bytes = info["stream_bytes"] + len(mine) * spec.kv_bytes_per_position() * mean_pos
         gbs = step_bytes / (ms_step / 1000.0) / 1e9
         line = {
@@ -555,8 +560,10 @@ def run_streams(args):
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xint8->int32, f32", "data": "synthetic",
             "config": {"workload": f"M26, {args.streams * world} independent greedy streams, {len(mine)} per GPU, "
-                                   f"{PROMPT_LEN}-token prompts, positions {PROMPT_LEN}..{PROMPT_LEN + CYCLE} "
-                                   f"(rewound every {CYCLE} tokens), n_ctx {n_ctx} per stream",
+                                   f"{PROMPT_LEN}-token prompts, positions {p0}..{p0 + CYCLE} "
+                                   f"(rewound every {CYCLE} tokens), n_ctx {n_ctx} per stream"
+                                   + ("" if p0 == PROMPT_LEN else
+                                      f"; cache entries {PROMPT_LEN}..{p0 - 1} zero-filled (timing case)"),
                        "model": spec.name, "parallelism": f"dp{world} (streams)",
                        "l2": "weights (1.5 GB) and caches exceed L2"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,

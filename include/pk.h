@@ -221,8 +221,9 @@ int pk_set_position(pk_engine *eng, int pos);
  * at most 64, once per engine); pk_stream_prefill runs a prompt into stream
  * s's cache and picks its next token (the engine's own sequence and prefix
  * reuse are reset); pk_streams_decode writes [n_steps][n_streams] ids, as
- * pk_decode_steps_device per stream; pk_streams_set_position rewinds every
- * stream to pos (timing). */
+ * pk_decode_steps_device per stream; pk_streams_set_position moves every
+ * stream to pos (a pos past a stream's tokens attends zero-filled cache
+ * entries: for timing long contexts only). */
 int pk_streams_begin(pk_engine *eng, int n_streams);
 int pk_stream_prefill(pk_engine *eng, int s, const uint32_t *prompt, int n);
 int pk_streams_decode(pk_engine *eng, int n_steps, uint32_t *out_ids, float *device_ms);

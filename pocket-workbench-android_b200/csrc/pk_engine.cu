@@ -1148,8 +1148,10 @@ int Engine::streams_decode(int n_steps, uint32_t *out_ids, float *device_ms) {
   return PK_OK;
 }
 
-// Every stream's position set to pos (<= each stream's length): the next
-// step decodes at pos, over the cache entries already there (timing runs).
+// Every stream's position set to pos: the next step decodes at pos over the
+// cache entries 0..pos - 1 as they are.  Entries past a stream's own tokens
+// hold zeros (or an earlier run's values), so a pos beyond a stream's length
+// is for timing long-context steps only; the tokens then are not a sequence.
 int Engine::streams_set_position(int pos) {
   if (!n_streams_) return set_error(PK_ERR_INVALID, "no streams");
   if (pos < 1 || pos >= n_ctx_) return set_error(PK_ERR_INVALID, "position must be in 1..n_ctx-1");
