@@ -1258,6 +1258,8 @@ static size_t ac_smem(int dh) {
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_ns() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // DHC: the head dimension as a compile-time constant (64, 128), or 0 for any.
 template <int DHC>
@@ -1405,9 +1407,10 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 
 // b == 1 order attention (k_attn with dot8) for one token per CTA with the
-// head's K and V brought through shared memory in 128-position tiles
-// (double-buffered cp.async), so the score dots and the per-d chains read
-// shared memory instead of waiting on global loads:
+// head's K and V brought through shared memory in 128-position tiles, three
+// stages of cp.async (two tiles in flight while one is used), so the score
+// dots and the per-d chains read shared memory instead of waiting on global
+// loads:
 //   pass 1: thread t scores position p0 + t of the tile: eight chains over d
 //           (d = 8j + u in chain u), reduced ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7));
 //   pass 2: the tile's V rows and e_p; thread d < DH runs its chain over the
@@ -1415,11 +1418,14 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 //           sum chain.
 // Same operations in the same order as k_attn, so the same bits.  Needs
 // n_ctx % 4 == 0 and 16-byte aligned K, V and score rows.
+constexpr int AB_P = 128, AB_NS = 3;
+__host__ __device__ constexpr size_t ab_smem(int dh) { return (size_t)AB_NS * (dh * AB_P + AB_P) * 4; }
+
 template <int DH>
 __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
-  constexpr int P = 128, NT = DH == 64 ? 128 : 256, TILE = DH * P;
+  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P;
   extern __shared__ __align__(16) float at_sm[];
-  float *const es = at_sm + 2 * TILE;  // two tiles of TILE floats, then e: [2][P]
+  float *const es = at_sm + NS * TILE;  // NS tiles of TILE floats, then e: [NS][P]
   __shared__ float qs[DH];
   __shared__ float red[40];
   __shared__ float s_inv;
@@ -1433,27 +1439,27 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
   const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
   const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
   float *sc = a.scores + hb * a.n_ctx;
-  // K tile t: [d][P] from the d-major cache, 16-byte chunks holding a position <= pos
-  auto load_k = [&](int t, float *dst) {
-    const int p0 = t * P, nq = (min(P, n - p0) + 3) >> 2;
-    for (int c = tid; c < DH * (P / 4); c += NT) {
-      const int d = c >> 5, j = c & 31;
-      if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+  // K tile t into stage t % NS: [d][P] from the d-major cache, 16-byte chunks
+  // holding a position <= pos.  Every call commits one group (empty past the
+  // last tile), so "wait until NS - 1 groups are pending" completes tile t.
+  auto load_k = [&](int t) {
+    if (t < nt) {
+      float *dst = at_sm + (t % NS) * TILE;
+      const int p0 = t * P, nq = (min(P, n - p0) + 3) >> 2;
+      for (int c = tid; c < DH * (P / 4); c += NT) {
+        const int d = c >> 5, j = c & 31;
+        if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+      }
     }
+    cp_async_commit();
   };
-  load_k(0, at_sm);
-  cp_async_commit();
+  for (int t = 0; t < NS - 1; t++) load_k(t);
   float mx = -INFINITY;
   for (int t = 0; t < nt; t++) {
-    const float *cur = at_sm + (t & 1) * TILE;
-    if (t + 1 < nt) {
-      load_k(t + 1, at_sm + ((t + 1) & 1) * TILE);
-      cp_async_commit();
-      cp_async_wait1();
-    } else {
-      cp_async_wait_all();
-    }
+    load_k(t + NS - 1);
+    cp_async_wait_ns<NS - 1>();
     __syncthreads();
+    const float *cur = at_sm + (t % NS) * TILE;
     const int p = t * P + tid;
     if (tid < P && p <= pos) {
       float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -1470,29 +1476,28 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     }
     __syncthreads();
   }
+  cp_async_wait_all();  // only empty groups are left
   const float M = block_max(mx, red);
   for (int p = tid; p <= pos; p += NT) sc[p] = expf_lib(fsub(sc[p], M));
   __syncthreads();
-  // V tile t: P rows of DH floats (contiguous), and e of its positions
-  auto load_v = [&](int t, float *dst, float *edst) {
-    const int p0 = t * P, nv = min(P, n - p0);
-    const float *src = vb + (size_t)p0 * DH;
-    for (int c = tid; c < nv * (DH / 4); c += NT) cp_async16(dst + 4 * c, src + 4 * c);
-    if (tid < ((nv + 3) >> 2)) cp_async16(edst + 4 * tid, sc + p0 + 4 * tid);
+  // V tile t into stage t % NS: P rows of DH floats (contiguous), and e of its positions
+  auto load_v = [&](int t) {
+    if (t < nt) {
+      float *dst = at_sm + (t % NS) * TILE, *edst = es + (t % NS) * P;
+      const int p0 = t * P, nv = min(P, n - p0);
+      const float *src = vb + (size_t)p0 * DH;
+      for (int c = tid; c < nv * (DH / 4); c += NT) cp_async16(dst + 4 * c, src + 4 * c);
+      if (tid < ((nv + 3) >> 2)) cp_async16(edst + 4 * tid, sc + p0 + 4 * tid);
+    }
+    cp_async_commit();
   };
-  load_v(0, at_sm, es);
-  cp_async_commit();
+  for (int t = 0; t < NS - 1; t++) load_v(t);
   float acc = 0.0f, sum = 0.0f;
   for (int t = 0; t < nt; t++) {
-    const float *cur = at_sm + (t & 1) * TILE, *ec = es + (t & 1) * P;
-    if (t + 1 < nt) {
-      load_v(t + 1, at_sm + ((t + 1) & 1) * TILE, es + ((t + 1) & 1) * P);
-      cp_async_commit();
-      cp_async_wait1();
-    } else {
-      cp_async_wait_all();
-    }
+    load_v(t + NS - 1);
+    cp_async_wait_ns<NS - 1>();
     __syncthreads();
+    const float *cur = at_sm + (t % NS) * TILE, *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
     if (tid < DH) {
 #pragma unroll 8
@@ -1507,6 +1512,7 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     }
     __syncthreads();
   }
+  cp_async_wait_all();
   if (tid == DH) s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
   __syncthreads();
   if (tid < DH) {
@@ -1546,7 +1552,7 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
   const bool dot8 = a.b == 1 || a.b1_order;
   if (dot8 && (a.dh == 64 || a.dh == 128) && a.n_ctx % 4 == 0 && a.lane_stride % 4 == 0 &&
       (((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.scores) & 15) == 0) {
-    const size_t smem = (size_t)(2 * a.dh * 128 + 2 * 128) * 4;
+    const size_t smem = ab_smem(a.dh);
     void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_b1t<64> : k_attn_b1t<128>;
     cudaError_t e = set_smem(kern, smem);
     if (e != cudaSuccess) return e;
