@@ -21,6 +21,11 @@
  *   pk_generate            model.rs:1235-1352 Engine::generate (prefix-KV reuse included)
  *   pk_request_stop        util.rs:274-282 request_stop / STOP_REQUESTED
  *   pk_set_debug/get_dump  model.rs:870-872,942-1168 Engine.dbg intermediates
+ *   pk_tokenizer_load, pk_tokenize, pk_token_bytes, pk_token_is_eog
+ *                          tokenizer.rs:38-110 from_gguf, :187-224 encode, :226-250 decode_token,
+ *                          :252-254 is_eog (pre-tokenizer patterns: regexlite.rs)
+ *   pk_chat_apply etc.     chat.rs:16-18 is_minicpm5, :20-97 apply_minicpm5 / apply_generic,
+ *                          :99-109 the thinking / direct suffixes
  *
  * Threading: one engine per host thread; calls on one engine are serialised
  * by the caller (the reference serialises with a global Mutex, jni.rs:211).
@@ -304,6 +309,53 @@ int pk_tp_info_get(pk_tp *tp, pk_tp_info *info);
 int pk_tp_split(int n_head, int n_head_kv, int head_dim, int n_ff, int n_vocab, int rank, int world, int o_block,
                 int down_block, int out[5]);
 uint32_t pk_tp_pick(const float *vals, const int *idx, int world);
+
+/* ---- Prompt text (host code): the GGUF's byte-level BPE tokenizer and the chat template. */
+typedef struct pk_tokenizer pk_tokenizer;
+typedef struct {
+  int32_t n_vocab;
+  int32_t n_eos;         /* end-of-generation ids (eos_token_id and the <|im_end|>-like specials) */
+  int64_t bos_id;        /* -1: the GGUF names none */
+  uint32_t eos_ids[16];  /* the first min(n_eos, 16), ascending */
+  int32_t ignore_merges; /* 1 when tokenizer.ggml.pre is "minicpm5" */
+  char pre[64];          /* tokenizer.ggml.pre (truncated, NUL-terminated) */
+} pk_tokenizer_info;
+
+/* Reads tokenizer.ggml.{tokens, token_type, merges, pre, bos_token_id, eos_token_id};
+ * PK_ERR_IO when the file does not parse or has no token list. */
+int pk_tokenizer_load(const char *gguf_path, pk_tokenizer **out);
+void pk_tokenizer_free(pk_tokenizer *tok);
+int pk_tokenizer_info_get(const pk_tokenizer *tok, pk_tokenizer_info *out);
+/* UTF-8 text of len bytes -> token ids (parse_special: special-token texts become their ids).
+ * Writes min(cap, n) ids and *n_out = n; PK_ERR_INVALID for malformed UTF-8 or n > cap. */
+int pk_tokenize(const pk_tokenizer *tok, const char *text, size_t len, int parse_special, uint32_t *out,
+                size_t cap, size_t *n_out);
+/* The bytes one token stands for (special tokens: their text).  Unknown ids give 0 bytes.
+ * Writes min(cap, n) bytes and *n_out = n; PK_ERR_INVALID for n > cap. */
+int pk_token_bytes(const pk_tokenizer *tok, uint32_t id, uint8_t *out, size_t cap, size_t *n_out);
+/* 1 when id ends generation, else 0. */
+int pk_token_is_eog(const pk_tokenizer *tok, uint32_t id);
+/* Host restatement for tests: the matches of a pre-tokenizer pattern (UTF-8, plen bytes) over a
+ * UTF-8 text, as (start, end) code-point offsets, two entries per match.  Writes min(cap, n)
+ * entries and *n_out = n; PK_ERR_INVALID for malformed UTF-8 or n > cap. */
+int pk_text_find(const char *pattern, size_t plen, const char *text, size_t tlen, uint32_t *bounds, size_t cap,
+                 size_t *n_out);
+
+typedef struct {
+  const char *role;    /* "system", "user", "assistant", "tool" (other roles are dropped) */
+  const char *content; /* UTF-8, NUL-terminated */
+} pk_chat_message;
+/* The prompt text of a conversation: minicpm5 != 0 the MiniCPM5 template, else generic
+ * <|im_start|>role turns; add_generation_prompt appends the assistant header.  Writes min(cap, n)
+ * bytes (no terminator) and *n_out = n; PK_ERR_INVALID for n > cap. */
+int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add_generation_prompt, char *out,
+                  size_t cap, size_t *n_out);
+/* 1 when the tokenizer's pre name or the model name selects the MiniCPM5 template. */
+int pk_chat_is_minicpm5(const char *pre, const char *name);
+/* Suffixes a host appends after the generation prompt: a direct answer (empty reasoning block)
+ * or an open reasoning block. */
+const char *pk_chat_direct_suffix(void);
+const char *pk_chat_thinking_suffix(void);
 
 #ifdef __cplusplus
 }

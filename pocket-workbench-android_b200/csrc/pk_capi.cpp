@@ -2,6 +2,8 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <map>
 #include <new>
@@ -10,6 +12,8 @@
 
 #include "pk.h"
 #include "pk_engine.h"
+#include "pk_gguf.h"
+#include "pk_text.h"
 #include "pk_tp.h"
 
 namespace pk {
@@ -567,5 +571,110 @@ uint32_t pk_tp_pick(const float *vals, const int *idx, int world) {
   if (!vals || !idx || world < 1 || world > pk::TP_MAX) return 0;
   return pk::tp_pick(vals, idx, world);
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- prompt text
+struct pk_tokenizer {
+  pk::text::Tokenizer tok;
+};
+
+namespace {
+
+template <class T>
+int copy_out(const T *src, size_t n, T *out, size_t cap, size_t *n_out, const char *what) {
+  if (n_out) *n_out = n;
+  if (out && cap) std::memcpy(out, src, std::min(n, cap) * sizeof(T));
+  if (n > cap) return set_error(PK_ERR_INVALID, std::string(what) + ": output needs " + std::to_string(n) + " entries");
+  return PK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pk_tokenizer_load(const char *path, pk_tokenizer **out) {
+  if (!path || !out) return set_error(PK_ERR_INVALID, "null argument");
+  *out = nullptr;
+  pk::Gguf g;
+  std::string err;
+  if (!g.open(path, err)) return set_error(PK_ERR_IO, err);
+  pk_tokenizer *t = new (std::nothrow) pk_tokenizer;
+  if (!t) return set_error(PK_ERR_OOM, "tokenizer allocation");
+  if (!t->tok.load(g, err)) {
+    delete t;
+    return set_error(PK_ERR_IO, err);
+  }
+  *out = t;
+  return PK_OK;
+}
+
+void pk_tokenizer_free(pk_tokenizer *t) { delete t; }
+
+int pk_tokenizer_info_get(const pk_tokenizer *t, pk_tokenizer_info *o) {
+  if (!t || !o) return set_error(PK_ERR_INVALID, "null argument");
+  std::memset(o, 0, sizeof(*o));
+  o->n_vocab = (int32_t)t->tok.n_vocab();
+  o->bos_id = t->tok.bos_id();
+  const auto &e = t->tok.eos_ids();
+  o->n_eos = (int32_t)e.size();
+  for (size_t i = 0; i < e.size() && i < 16; i++) o->eos_ids[i] = e[i];
+  o->ignore_merges = t->tok.ignore_merges() ? 1 : 0;
+  std::snprintf(o->pre, sizeof(o->pre), "%s", t->tok.pre().c_str());
+  return PK_OK;
+}
+
+int pk_tokenize(const pk_tokenizer *t, const char *text, size_t len, int parse_special, uint32_t *out, size_t cap,
+                size_t *n_out) {
+  if (!t || (!text && len) || (!out && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  std::u32string check;
+  if (!pk::text::utf8_decode(text, len, &check)) return set_error(PK_ERR_INVALID, "text is not valid UTF-8");
+  const std::vector<uint32_t> ids = t->tok.encode(std::string(text ? text : "", len), parse_special != 0);
+  return copy_out(ids.data(), ids.size(), out, cap, n_out, "pk_tokenize");
+}
+
+int pk_token_bytes(const pk_tokenizer *t, uint32_t id, uint8_t *out, size_t cap, size_t *n_out) {
+  if (!t || (!out && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  const std::string b = t->tok.token_bytes(id);
+  return copy_out(reinterpret_cast<const uint8_t *>(b.data()), b.size(), out, cap, n_out, "pk_token_bytes");
+}
+
+int pk_token_is_eog(const pk_tokenizer *t, uint32_t id) { return t && t->tok.is_eog(id) ? 1 : 0; }
+
+int pk_text_find(const char *pattern, size_t plen, const char *text, size_t tlen, uint32_t *bounds, size_t cap,
+                 size_t *n_out) {
+  if ((!pattern && plen) || (!text && tlen) || (!bounds && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  std::u32string p, t;
+  if (!pk::text::utf8_decode(pattern, plen, &p) || !pk::text::utf8_decode(text, tlen, &t))
+    return set_error(PK_ERR_INVALID, "pattern or text is not valid UTF-8");
+  const pk::text::Pattern pat(p);
+  std::vector<uint32_t> b;
+  for (const auto &m : pat.find(t)) {
+    b.push_back((uint32_t)m.first);
+    b.push_back((uint32_t)m.second);
+  }
+  return copy_out(b.data(), b.size(), bounds, cap, n_out, "pk_text_find");
+}
+
+int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add_generation_prompt, char *out,
+                  size_t cap, size_t *n_out) {
+  if ((!msgs && n_msgs) || n_msgs < 0 || (!out && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  std::vector<pk::text::Message> m((size_t)n_msgs);
+  for (int i = 0; i < n_msgs; i++) {
+    if (!msgs[i].role || !msgs[i].content) return set_error(PK_ERR_INVALID, "message with a null role or content");
+    m[i].role = msgs[i].role;
+    m[i].content = msgs[i].content;
+  }
+  const std::string s = minicpm5 ? pk::text::apply_minicpm5(m, add_generation_prompt != 0)
+                                 : pk::text::apply_generic(m, add_generation_prompt != 0);
+  return copy_out(s.data(), s.size(), out, cap, n_out, "pk_chat_apply");
+}
+
+int pk_chat_is_minicpm5(const char *pre, const char *name) {
+  return pk::text::is_minicpm5(pre ? pre : "", name ? name : "") ? 1 : 0;
+}
+
+const char *pk_chat_direct_suffix(void) { return pk::text::direct_suffix(); }
+const char *pk_chat_thinking_suffix(void) { return pk::text::thinking_on_suffix(); }
 
 }  // extern "C"

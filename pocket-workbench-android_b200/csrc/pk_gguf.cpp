@@ -42,13 +42,18 @@ struct Cursor {
 };
 
 // gguf.rs:345-375 skip_array (with string capture for tokenizer arrays).
-bool skip_array(Cursor &c, uint32_t et, uint64_t count, std::vector<std::string> *strs, int depth) {
+bool skip_array(Cursor &c, uint32_t et, uint64_t count, std::vector<std::string> *strs, int depth,
+                std::vector<int32_t> *i32s = nullptr) {
   if (depth > 4) return false;
   for (uint64_t i = 0; i < count && c.ok; i++) {
     switch (et) {
       case 0: case 1: case 7: c.uint(1); break;
       case 2: case 3: c.uint(2); break;
-      case 4: case 5: case 6: c.uint(4); break;
+      case 4: case 6: c.uint(4); break;
+      case 5: {
+        const uint32_t v = (uint32_t)c.uint(4);
+        if (i32s) i32s->push_back((int32_t)v);
+      } break;
       case 10: case 11: case 12: c.uint(8); break;
       case 8: {
         std::string s = c.str();
@@ -135,7 +140,8 @@ bool Gguf::open(const char *path, std::string &err) {
       case 9:
         v.arr_type = (uint32_t)c.uint(4);
         v.arr_count = c.uint(8);
-        if (!skip_array(c, v.arr_type, v.arr_count, v.arr_type == 8 ? &v.arr_str : nullptr, 0)) {
+        if (!skip_array(c, v.arr_type, v.arr_count, v.arr_type == 8 ? &v.arr_str : nullptr, 0,
+                        v.arr_type == 5 ? &v.arr_i32 : nullptr)) {
           err = "bad metadata array for key " + key;
           return false;
         }

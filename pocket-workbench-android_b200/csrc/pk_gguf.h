@@ -27,6 +27,7 @@ struct GgufValue {
   uint32_t arr_type = 0;  // array element type
   uint64_t arr_count = 0;
   std::vector<std::string> arr_str;
+  std::vector<int32_t> arr_i32;  // elements of an i32 array (tokenizer.ggml.token_type)
 };
 
 class Gguf {

@@ -226,6 +226,35 @@ def _kv_f32(key, val):
     return _s(key) + struct.pack("<I", 6) + struct.pack("<f", val)
 
 
+def _kv_arr_str(key, vals):
+    body = b"".join(struct.pack("<Q", len(v)) + v for v in (x if isinstance(x, bytes) else x.encode() for x in vals))
+    return _s(key) + struct.pack("<IIQ", 9, 8, len(vals)) + body
+
+
+def _kv_arr_i32(key, vals):
+    return _s(key) + struct.pack("<IIQ", 9, 5, len(vals)) + b"".join(struct.pack("<i", int(v)) for v in vals)
+
+
+def write_tokenizer_gguf(path: str, tokens, token_types=None, merges=None, pre=None, bos=None, eos=None,
+                         name="synthetic-tokenizer") -> None:
+    """A GGUF v3 file holding only tokenizer metadata (tokenizer.ggml.*) and no tensors."""
+    kvs = [_kv_str("general.architecture", "llama"), _kv_str("general.name", name),
+           _kv_arr_str("tokenizer.ggml.tokens", tokens)]
+    if token_types is not None:
+        kvs.append(_kv_arr_i32("tokenizer.ggml.token_type", token_types))
+    if merges is not None:
+        kvs.append(_kv_arr_str("tokenizer.ggml.merges", merges))
+    if pre is not None:
+        kvs.append(_kv_str("tokenizer.ggml.pre", pre))
+    if bos is not None:
+        kvs.append(_kv_u32("tokenizer.ggml.bos_token_id", bos))
+    if eos is not None:
+        kvs.append(_kv_u32("tokenizer.ggml.eos_token_id", eos))
+    header = struct.pack("<IIQQ", 0x46554747, 3, 0, len(kvs)) + b"".join(kvs)
+    with open(path, "wb") as f:
+        f.write(header + b"\x00" * ((-len(header)) % 32))
+
+
 def write_gguf(path: str, spec: ModelSpec, seed: int = 0, alignment: int = 32) -> dict:
     """Writes ``spec`` as a GGUF v3 file; returns a summary dict."""
     tensors = spec.tensor_specs()
