@@ -986,7 +986,12 @@ int Engine::streams_begin(int n) {
   PK_CK(cudaMalloc((void **)&d_sv_, half * n));
   PK_CK(cudaMemsetAsync(d_sk_, 0, half * n, st_));
   PK_CK(cudaMemsetAsync(d_sv_, 0, half * n, st_));
-  const size_t aux = (size_t)n * vocab_ * 4 + 256 + (size_t)n * 4 * 4 + (size_t)n * n_ctx_ * 4;
+  // histories above 1024 positions: the attention's scores are split over
+  // chunks of 512 (1024 above 8192) positions, whose maxima need scratch
+  spchunk_ = n_ctx_ > 1024 ? (n_ctx_ > 8192 ? 1024 : 512) : 0;
+  const size_t nch = spchunk_ ? (size_t)(n_ctx_ + spchunk_ - 1) / spchunk_ : 0;
+  const size_t aux = (size_t)n * vocab_ * 4 + 256 + (size_t)n * 4 * 4 + (size_t)n * n_ctx_ * 4 +
+                     (size_t)n * cfg_.n_head * nch * 4;
   PK_CK(cudaMalloc((void **)&d_slogits_, aux));
   uint8_t *p = (uint8_t *)d_slogits_ + (size_t)n * vocab_ * 4 + 256 - (((size_t)n * vocab_ * 4) & 255);
   d_sids_ = (uint32_t *)p;
@@ -994,6 +999,7 @@ int Engine::streams_begin(int n) {
   d_spos_ = (int *)(d_stok_ + n);
   d_sstep_ = d_spos_ + n;
   d_shist_ = (uint32_t *)(d_sstep_ + n);
+  d_spmax_ = spchunk_ ? (float *)(d_shist_ + (size_t)n * n_ctx_) : nullptr;
   PK_CK(cudaStreamSynchronize(st_));
   n_streams_ = n;
   spos_.assign(n, 0);
@@ -1067,6 +1073,7 @@ int Engine::enqueue_streams_step() {
     at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh; at.n_ctx = n_ctx_;
     at.scale = 1.0f / sqrtf((float)dh); at.scores = att_scores_;
     at.lane_stride = stride; at.b1_order = 1;
+    at.pmax = d_spmax_; at.pchunk = spchunk_;
     a.k = qdim;
     at.q8 = a;
     PK_CK(launch_attention(at, st_));

@@ -111,6 +111,8 @@ class Engine {
   float *d_sk_ = nullptr, *d_sv_ = nullptr, *d_slogits_ = nullptr;
   uint32_t *d_sids_ = nullptr, *d_stok_ = nullptr, *d_shist_ = nullptr;
   int *d_spos_ = nullptr, *d_sstep_ = nullptr;
+  float *d_spmax_ = nullptr;  // long histories: per-chunk score maxima of the split attention
+  int spchunk_ = 0;
   std::vector<int> spos_;
   std::vector<uint32_t> stok_;
   std::vector<char> sready_;

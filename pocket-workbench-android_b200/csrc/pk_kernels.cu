@@ -711,14 +711,18 @@ __device__ __forceinline__ float bytef(uint32_t w) {  // byte B of w (a value be
   return fsub(__int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u + B)), 8388608.0f);
 }
 __device__ __forceinline__ uint2 ldg_u2(const int8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
-// Named barriers 1 + s (s < 4) with immediate ids, so the kernel holds only
+// Named barriers 1 + s (s < 8) with immediate ids, so the kernel holds only
 // the barriers it uses.
 __device__ __forceinline__ void mm_bar_sync(int s, int n) {
   switch (s) {
     case 0: asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); break;
     case 1: asm volatile("bar.sync 2, %0;" ::"r"(n) : "memory"); break;
     case 2: asm volatile("bar.sync 3, %0;" ::"r"(n) : "memory"); break;
-    default: asm volatile("bar.sync 4, %0;" ::"r"(n) : "memory"); break;
+    case 3: asm volatile("bar.sync 4, %0;" ::"r"(n) : "memory"); break;
+    case 4: asm volatile("bar.sync 5, %0;" ::"r"(n) : "memory"); break;
+    case 5: asm volatile("bar.sync 6, %0;" ::"r"(n) : "memory"); break;
+    case 6: asm volatile("bar.sync 7, %0;" ::"r"(n) : "memory"); break;
+    default: asm volatile("bar.sync 8, %0;" ::"r"(n) : "memory"); break;
   }
 }
 __device__ __forceinline__ void mm_bar_arrive(int s, int n) {
@@ -726,16 +730,20 @@ __device__ __forceinline__ void mm_bar_arrive(int s, int n) {
     case 0: asm volatile("bar.arrive 1, %0;" ::"r"(n) : "memory"); break;
     case 1: asm volatile("bar.arrive 2, %0;" ::"r"(n) : "memory"); break;
     case 2: asm volatile("bar.arrive 3, %0;" ::"r"(n) : "memory"); break;
-    default: asm volatile("bar.arrive 4, %0;" ::"r"(n) : "memory"); break;
+    case 3: asm volatile("bar.arrive 4, %0;" ::"r"(n) : "memory"); break;
+    case 4: asm volatile("bar.arrive 5, %0;" ::"r"(n) : "memory"); break;
+    case 5: asm volatile("bar.arrive 6, %0;" ::"r"(n) : "memory"); break;
+    case 6: asm volatile("bar.arrive 7, %0;" ::"r"(n) : "memory"); break;
+    default: asm volatile("bar.arrive 8, %0;" ::"r"(n) : "memory"); break;
   }
 }
 
-// One 16-row x 32-lane tile (row tile bx, lane tile blockIdx.y) of out = W * act.
+// One 16-row x 8LG-lane tile (row tile bx, lane tile blockIdx.y) of out = W * act.
 //
 // Work unit: eight consecutive float terms of every (row, lane) of the tile
 // (a Q4_K superblock, half a Q6_K superblock, eight Q8_0 / Q4_0 blocks).
-// Warp w is lane group lw = w % 4 (lanes 8lw .. 8lw+7) and k slice
-// ks = w / 4 of KS: units are dealt to the slices round robin, each slice
+// Warp w is lane group lw = w % LG (lanes 8lw .. 8lw+7) and k slice
+// ks = w / LG of KS: units are dealt to the slices round robin, each slice
 // forms its unit's terms in registers, then adds them to the running sums
 // of the (row, lane) pairs, which pass from slice to slice through shared
 // memory (named barrier 1 + s is the hand-off into slice s).  So every sum
@@ -745,7 +753,7 @@ __device__ __forceinline__ void mm_bar_arrive(int s, int n) {
 // Q4_K / Q8_0 the k slots of a sub-block are permuted: thread t's A and B
 // fragment slots 4t..4t+3 and 16+4t..16+4t+3 carry elements 8t..8t+7 of
 // the weight row and of the activation lane (one 64-bit load each).
-template <int T, int KS>
+template <int T, int KS, int LG>
 __device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, float *out, long os_row, long os_lane,
                                         int add, int bx, int NBC, uint8_t *mm_smem) {
   using G = MmGeo<T>;
@@ -756,11 +764,11 @@ __device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, fl
   uint8_t *wq = mm_smem;                                // [16 rows][NBC][QB]
   float *wd = (float *)(mm_smem + MM_ROWS * NBC * G::QB);  // [16 rows][NBC] (types with a separate d)
   float2 *asf = (float2 *)(mm_smem + MM_ROWS * NBC * (G::QB + (G::D ? 4 : 0)));  // [32 lanes][LS] {da, sa}
-  float4 *relay = (float4 *)(asf + MM_LANES * LS);     // [4 lane groups][32]
+  float4 *relay = (float4 *)(asf + MM_LANES * LS);     // [lane groups][32]
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
-  const int lw = w & 3, ks = w >> 2;
+  const int lw = w % LG, ks = w / LG;
   const int r0 = bx * MM_ROWS, nr = min(MM_ROWS, W.rows - r0);
-  const int L0 = blockIdx.y * MM_LANES, nl = min(MM_LANES, act.b - L0);
+  const int L0 = blockIdx.y * 8 * LG, nl = min(8 * LG, act.b - L0);
   const int nact = (nl + 7) >> 3;                      // lane groups with lanes
   const bool active = lw < nact;
   const int k = W.k, nblk = k / G::BE, nb32 = k >> 5;
@@ -776,7 +784,7 @@ __device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, fl
     // stage: the tile's rows and the lanes' activation scales by asynchronous
     // copies (every copy in flight at once), the f16 row scales by plain loads;
     // warps take rows (lanes), lanes take pieces, so no index is divided
-    constexpr int NW = MM_WARPS * KS;
+    constexpr int NW = LG * KS;
     const int v16 = nbc * G::QB / 16;
     for (int r = w; r < nr; r += NW)
       for (int j = lane; j < v16; j += 32)
@@ -961,10 +969,9 @@ __device__ __forceinline__ void mv_tile(const DevTensor &W, const Q8Dev &act, fl
     };
     const int nbar = 64 * nact;  // one hand-off: the active lane groups' sender and receiver warps
     int u = ((ks - ubase) % KS + KS) % KS;  // this slice's first unit of the chunk
-    // With four slices (one CTA per SM, registers to spare) each unit's B
-    // fragments are loaded one unit ahead; with fewer, the other resident
-    // warps cover the load.
-    constexpr bool AHEAD = KS == 4;
+    // With four or more slices each unit's B fragments are loaded one unit
+    // ahead; with one, the other resident warps cover the load.
+    constexpr bool AHEAD = KS >= 4;
     uint32_t bc[16], bn[16];
     if (AHEAD && u < nu) load_b(u, bc);
     for (; u < nu; u += KS) {
@@ -1021,8 +1028,11 @@ struct MvSegs {
   int n;
 };
 
-template <int KS>
-__global__ void __launch_bounds__(32 * MM_WARPS * KS, KS == 1 ? 5 : 1) k_mv_mma(MvSegs ss, Q8Dev act) {
+// KS k slices of LG lane groups: (1, 4) and (4, 4) for b > 8, (4, 1) and
+// (8, 1) for b <= 8, where one lane group holds every lane and the slices
+// keep all warps busy.
+template <int KS, int LG>
+__global__ void __launch_bounds__(32 * LG * KS, KS == 1 ? 5 : KS * LG == 4 ? 4 : 1) k_mv_mma(MvSegs ss, Q8Dev act) {
   extern __shared__ __align__(16) uint8_t mm_smem[];
   pdl_trigger();
   pdl_wait();
@@ -1030,10 +1040,10 @@ __global__ void __launch_bounds__(32 * MM_WARPS * KS, KS == 1 ? 5 : 1) k_mv_mma(
   const MvSeg &S = (ss.n > 2 && bx >= ss.s[2].cta0) ? ss.s[2] : (ss.n > 1 && bx >= ss.s[1].cta0) ? ss.s[1] : ss.s[0];
   const int tb = bx - S.cta0;
   switch (S.W.type) {
-    case T_Q4_K: mv_tile<T_Q4_K, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
-    case T_Q6_K: mv_tile<T_Q6_K, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
-    case T_Q8_0: mv_tile<T_Q8_0, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
-    default: mv_tile<T_Q4_0, KS>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    case T_Q4_K: mv_tile<T_Q4_K, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    case T_Q6_K: mv_tile<T_Q6_K, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    case T_Q8_0: mv_tile<T_Q8_0, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
+    default: mv_tile<T_Q4_0, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
   }
 }
 
@@ -1055,8 +1065,10 @@ static size_t mv_seg_smem(const DevTensor &w, int nbc) {
   }
 }
 
-// Slices per tile: four when the tiles are at most one per SM (a 16-warp CTA
-// per SM with a larger staged chunk), else plain 4-warp tiles.
+// Tile shape: b > 8 uses four lane groups (32 lanes a tile) with four k
+// slices when the tiles are at most one per SM (a 16-warp CTA per SM with a
+// larger staged chunk), else one; b <= 8 uses one lane group with eight
+// slices (at most one tile per SM) or four.
 cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st) {
   if (n < 1 || n > MV_MAX_SEGS || act.b < 1) return cudaErrorInvalidValue;
   int tiles = 0;
@@ -1065,11 +1077,13 @@ cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStre
     if (!type_is_matvec(o.w.type) || act.k != o.w.k || o.w.rows < 1) return cudaErrorInvalidValue;
     tiles += (o.w.rows + MM_ROWS - 1) / MM_ROWS;
   }
-  const int lane_tiles = (act.b + MM_LANES - 1) / MM_LANES, sms = num_sms();
+  const int LG = act.b <= 8 ? 1 : 4;
+  const int lane_tiles = (act.b + 8 * LG - 1) / (8 * LG), sms = num_sms();
   const long ctas = (long)tiles * lane_tiles;
-  const int KS = ctas <= sms ? 4 : 1;
-  // shared memory per CTA: one CTA per SM (KS 4), five (KS 1)
-  const int wbytes = KS == 4 ? 200 * 1024 : 44 * 1024;
+  const bool big = ctas <= sms;  // at most one tile per SM: one wide CTA each
+  const int KS = LG == 4 ? (big ? 4 : 1) : (big ? 8 : 4);
+  // shared memory per CTA: one CTA per SM (wide), else up to five
+  const int wbytes = big ? 200 * 1024 : 44 * 1024;
   MvSegs ss{};
   ss.n = n;
   int cta = 0;
@@ -1083,14 +1097,10 @@ cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStre
   }
   const dim3 grid(tiles, lane_tiles);
   cudaError_t e;
-  switch (KS) {
-    case 4:
-      if ((e = set_smem(k_mv_mma<4>, smem)) != cudaSuccess) return e;
-      return launch(k_mv_mma<4>, grid, dim3(32 * MM_WARPS * 4), smem, st, ss, act);
-    default:
-      if ((e = set_smem(k_mv_mma<1>, smem)) != cudaSuccess) return e;
-      return launch(k_mv_mma<1>, grid, dim3(32 * MM_WARPS), smem, st, ss, act);
-  }
+  void (*kern)(MvSegs, Q8Dev) = LG == 4 ? (KS == 4 ? k_mv_mma<4, 4> : k_mv_mma<1, 4>)
+                                        : (KS == 8 ? k_mv_mma<8, 1> : k_mv_mma<4, 1>);
+  if ((e = set_smem(kern, smem)) != cudaSuccess) return e;
+  return launch(kern, grid, dim3(32 * LG * KS), smem, st, ss, act);
 }
 
 cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, long os_row, long os_lane, bool add,
@@ -1413,9 +1423,10 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 // loads:
 //   pass 1: thread t scores position p0 + t of the tile: eight chains over d
 //           (d = 8j + u in chain u), reduced ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7));
-//   pass 2: the tile's V rows and e_p; thread d < DH runs its chain over the
-//           tile's positions in order (zero weights skipped), thread DH the
-//           sum chain.
+//   pass 2: the tile's V rows and scores; thread p turns score p into
+//           e_p = exp(s_p - M) in shared memory, then thread d < DH runs its
+//           chain over the tile's positions in order (zero weights skipped)
+//           and thread DH the sum chain.
 // Same operations in the same order as k_attn, so the same bits.  Needs
 // n_ctx % 4 == 0 and 16-byte aligned K, V and score rows.
 constexpr int AB_P = 128, AB_NS = 3;
@@ -1477,10 +1488,8 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     __syncthreads();
   }
   cp_async_wait_all();  // only empty groups are left
-  const float M = block_max(mx, red);
-  for (int p = tid; p <= pos; p += NT) sc[p] = expf_lib(fsub(sc[p], M));
-  __syncthreads();
-  // V tile t into stage t % NS: P rows of DH floats (contiguous), and e of its positions
+  const float M = block_max(mx, red);  // (its barriers also order the score stores before pass 2)
+  // V tile t into stage t % NS: P rows of DH floats (contiguous), and the scores of its positions
   auto load_v = [&](int t) {
     if (t < nt) {
       float *dst = at_sm + (t % NS) * TILE, *edst = es + (t % NS) * P;
@@ -1497,8 +1506,11 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     load_v(t + NS - 1);
     cp_async_wait_ns<NS - 1>();
     __syncthreads();
-    const float *cur = at_sm + (t % NS) * TILE, *ec = es + (t % NS) * P;
+    const float *cur = at_sm + (t % NS) * TILE;
+    float *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
+    if (tid < nv) ec[tid] = expf_lib(fsub(ec[tid], M));
+    __syncthreads();
     if (tid < DH) {
 #pragma unroll 8
       for (int j = 0; j < nv; j++) {
@@ -1538,6 +1550,151 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   return launch_attention_k(a, st);
 }
 
+// The b == 1 order for long histories, split so that many more CTAs
+// stream K and V (same values, same order, so the same bits as k_attn_b1t):
+//   k_attn_sc: CTA (head, token, c) scores positions [c * pchunk, ...) as
+//              k_attn_b1t's pass 1 and writes their maximum (-inf if none);
+//   k_attn_pv: CTA (head, token, part) takes M as the maximum of those
+//              (order-free), turns each 128-position tile's scores into e_p
+//              in shared memory and runs the chains of d = 32 part .. +31
+//              over V's matching 128-byte row pieces, plus its own copy of
+//              the sum chain; its 32 outputs are one Q8 block.
+template <int DH>
+__global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
+  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P;
+  extern __shared__ __align__(16) float at_sm[];
+  __shared__ float qs[DH];
+  __shared__ float red[40];
+  const int h = blockIdx.x, bi = blockIdx.y, c = blockIdx.z, tid = threadIdx.x;
+  const int kh = h / (a.n_head / a.n_kv);
+  pdl_trigger();
+  pdl_wait();
+  const int pos = a.pos[bi];
+  const long hb = (long)bi * a.n_head + h;
+  const int p_lo = c * a.pchunk, p_hi = min(p_lo + a.pchunk, pos + 1);
+  float *pm = a.pmax + hb * gridDim.z + c;
+  if (p_lo >= p_hi) {  // the whole CTA: no position of this token in the chunk
+    if (tid == 0) *pm = -INFINITY;
+    return;
+  }
+  if (tid < DH) qs[tid] = a.q[hb * DH + tid];
+  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  float *sc = a.scores + hb * a.n_ctx;
+  const int nt = (p_hi - p_lo + P - 1) / P;
+  auto load_k = [&](int t) {
+    if (t < nt) {
+      float *dst = at_sm + (t % NS) * TILE;
+      const int p0 = p_lo + t * P, nq = (min(P, p_hi - p0) + 3) >> 2;
+      for (int i = tid; i < DH * (P / 4); i += NT) {
+        const int d = i >> 5, j = i & 31;
+        if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int t = 0; t < NS - 1; t++) load_k(t);
+  float mx = -INFINITY;
+  for (int t = 0; t < nt; t++) {
+    load_k(t + NS - 1);
+    cp_async_wait_ns<NS - 1>();
+    __syncthreads();
+    const float *cur = at_sm + (t % NS) * TILE;
+    const int p = p_lo + t * P + tid;
+    if (tid < P && p < p_hi) {
+      float cc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int d = 0; d < DH; d += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) cc[u] = fadd(cc[u], fmul(qs[d + u], cur[(d + u) * P + tid]));
+      }
+      float sv = fadd(fadd(cc[0], cc[1]), fadd(cc[2], cc[3]));
+      sv = fadd(sv, fadd(fadd(cc[4], cc[5]), fadd(cc[6], cc[7])));
+      sv = fmul(sv, a.scale);
+      sc[p] = sv;
+      mx = sv > mx ? sv : mx;
+    }
+    __syncthreads();
+  }
+  cp_async_wait_all();
+  const float M = block_max(mx, red);
+  if (tid == 0) *pm = M;
+}
+
+constexpr int PV_P = 128, PV_NS = 3, PV_W = 32, PV_NT = 64;
+constexpr size_t pv_smem() { return (size_t)PV_NS * (PV_P * PV_W + PV_P) * 4; }
+
+template <int DH>
+__global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
+  constexpr int P = PV_P, NS = PV_NS, W = PV_W, NT = PV_NT;
+  extern __shared__ __align__(16) float pv_sm[];
+  float *const es = pv_sm + NS * P * W;  // NS V pieces of P x W floats, then e: [NS][P]
+  __shared__ float s_m, s_inv;
+  const int h = blockIdx.x, bi = blockIdx.y, part = blockIdx.z, tid = threadIdx.x;
+  const int kh = h / (a.n_head / a.n_kv);
+  pdl_trigger();
+  pdl_wait();
+  const int pos = a.pos[bi], n = pos + 1, nt = (n + P - 1) / P;
+  const long hb = (long)bi * a.n_head + h;
+  if (tid == 0) {
+    const float *pm = a.pmax + hb * nch;
+    float m = -INFINITY;
+    for (int c = 0; c < nch; c++) m = pm[c] > m ? pm[c] : m;
+    s_m = m;
+  }
+  __syncthreads();
+  const float M = s_m;
+  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH + part * W;
+  const float *sc = a.scores + hb * a.n_ctx;
+  auto load = [&](int t) {
+    if (t < nt) {
+      float *dst = pv_sm + (t % NS) * P * W, *edst = es + (t % NS) * P;
+      const int p0 = t * P, nv = min(P, n - p0);
+      for (int i = tid; i < nv * (W / 4); i += NT) {
+        const int r = i >> 3, j = i & 7;
+        cp_async16(dst + r * W + 4 * j, vb + (size_t)(p0 + r) * DH + 4 * j);
+      }
+      for (int i = tid; i < ((nv + 3) >> 2); i += NT) cp_async16(edst + 4 * i, sc + p0 + 4 * i);
+    }
+    cp_async_commit();
+  };
+  for (int t = 0; t < NS - 1; t++) load(t);
+  float acc = 0.0f, sum = 0.0f;
+  for (int t = 0; t < nt; t++) {
+    load(t + NS - 1);
+    cp_async_wait_ns<NS - 1>();
+    __syncthreads();
+    const float *cur = pv_sm + (t % NS) * P * W;
+    float *ec = es + (t % NS) * P;
+    const int nv = min(P, n - t * P);
+    for (int j = tid; j < nv; j += NT) ec[j] = expf_lib(fsub(ec[j], M));
+    __syncthreads();
+    if (tid < W) {
+#pragma unroll 8
+      for (int j = 0; j < nv; j++) {
+        const float e = ec[j];
+        const float v = cur[j * W + tid];
+        if (e != 0.0f) acc = fadd(acc, fmul(e, v));
+      }
+    } else if (tid == W) {
+#pragma unroll 8
+      for (int j = 0; j < nv; j++) sum = fadd(sum, ec[j]);
+    }
+    __syncthreads();
+  }
+  cp_async_wait_all();
+  if (tid == W) s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+  __syncthreads();
+  if (tid < W) {
+    const float o = fmul(acc, s_inv);
+    a.out[hb * DH + part * W + tid] = o;
+    if (a.q8.q) {
+      const int qk = a.n_head * DH, blk = (h * DH + part * W) >> 5;
+      q8_block_lane(o, tid, a.q8.q + (long)bi * qk + blk * 32, a.q8.d + (long)bi * (qk >> 5) + blk,
+                    a.q8.s + (long)bi * (qk >> 5) + blk);
+    }
+  }
+}
+
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
   if (a.b > 1 && !a.b1_order && a.lane_stride == 0 && a.n_ctx % 4 == 0 &&
       (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
@@ -1550,8 +1707,22 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
     return launch(kern, grid, dim3(AC_THREADS), smem, st, a);
   }
   const bool dot8 = a.b == 1 || a.b1_order;
-  if (dot8 && (a.dh == 64 || a.dh == 128) && a.n_ctx % 4 == 0 && a.lane_stride % 4 == 0 &&
-      (((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.scores) & 15) == 0) {
+  const bool tiles = dot8 && (a.dh == 64 || a.dh == 128) && a.n_ctx % 4 == 0 && a.lane_stride % 4 == 0 &&
+                     (((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.scores) & 15) == 0;
+  if (tiles && a.pmax && a.pchunk > 0) {
+    if (a.pchunk % AB_P != 0) return cudaErrorInvalidValue;
+    const int nch = (a.n_ctx + a.pchunk - 1) / a.pchunk;
+    void (*ks)(AttnArgs) = a.dh == 64 ? k_attn_sc<64> : k_attn_sc<128>;
+    void (*kv)(AttnArgs, int) = a.dh == 64 ? k_attn_pv<64> : k_attn_pv<128>;
+    const size_t s1 = (size_t)AB_NS * a.dh * AB_P * 4;
+    cudaError_t e = set_smem(ks, s1);
+    if (e == cudaSuccess) e = set_smem(kv, pv_smem());
+    if (e == cudaSuccess)
+      e = launch(ks, dim3(a.n_head, a.b, nch), dim3(a.dh == 64 ? 128 : 256), s1, st, a);
+    if (e != cudaSuccess) return e;
+    return launch(kv, dim3(a.n_head, a.b, a.dh / PV_W), dim3(PV_NT), pv_smem(), st, a, nch);
+  }
+  if (tiles) {
     const size_t smem = ab_smem(a.dh);
     void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_b1t<64> : k_attn_b1t<128>;
     cudaError_t e = set_smem(kern, smem);

@@ -111,6 +111,11 @@ struct AttnArgs {
   Q8Dev q8{};          // optional (q8.q != nullptr): Q8 of out, k = n_head * dh
   size_t lane_stride = 0;  // floats from token i's K/V cache to token i + 1's (0: one shared cache)
   int b1_order = 0;        // 1: every token scored in the b == 1 order (simd.rs:19-43), one CTA each
+  // b == 1 order over long histories: pchunk positions per scoring CTA (a
+  // multiple of 128) and pmax scratch [b][n_head][ceil(n_ctx / pchunk)] for
+  // their maxima; then the value pass runs one CTA per (token, head, 32 d).
+  float *pmax = nullptr;
+  int pchunk = 0;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 

@@ -200,6 +200,23 @@ def test_streams_equal_each_stream_alone(pk, paths, name):
         e.streams_begin(2)
 
 
+@pytest.mark.parametrize("name", ["tiny", "q8down"])
+def test_streams_long_history_split_attention(pk, paths, name):
+    """Above 1024 positions of context the streams' attention is split (scores
+    over 512-position chunks on many CTAs, then the value chains per 32 d);
+    the tokens still equal each stream decoded alone, across chunk edges."""
+    spec = MODELS[name]
+    prompts = [synth.prompt_ids(41 + i, n, spec.n_vocab) for i, n in enumerate((3, 530, 1100))]
+    want = [pk.Engine(paths[name], n_ctx=1536).generate(p, 24, stop_at_eog=False)["gen_ids"] for p in prompts]
+    e = pk.Engine(paths[name], n_ctx=1536)
+    e.streams_begin(len(prompts))
+    for s, p in enumerate(prompts):
+        e.stream_prefill(s, p)
+    first, rest = e.streams_decode(9), e.streams_decode(15)
+    for s in range(len(prompts)):
+        assert first[s] + rest[s] == want[s]
+
+
 def test_bounded_wait_runs_out_and_engine_recovers(pk, paths):
     """Failure detection without a GPU fault: one persistent-kernel launch
     whose phase inputs never arrive (its readers wait for a tag nothing
