@@ -347,9 +347,14 @@ def run_ours(args):
 
     cpu = None
     c4 = None
+    streams = None
     if rank == 0 and world == 1:
         eng.close()
         c4 = prefill_config4(pk, path, spec, local)  # BASELINE config 4, outside the timed region
+        try:  # the data-parallel streams row, outside the timed region; never fails the line
+            streams = streams_summary(pk, synth, path, spec, local)
+        except Exception as exc:  # noqa: BLE001
+            streams = {"error": str(exc)[:200]}
         if not args.no_cpu_baseline:
             cpu = cpu_baseline_sample(path, prompt, args.cpu_seconds)
 
@@ -400,6 +405,7 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "streams": streams,
         }
         print(json.dumps(line), flush=True)
     if dist:
@@ -472,6 +478,31 @@ def run_tp70(args):
         print(json.dumps(line), flush=True)
     eng.close()
     dist.destroy_process_group()
+
+
+def streams_summary(pk, synth, path, spec, device, n_streams=8, steps=128, warmup=4):
+    """Data-parallel streams on one GPU (outside the timed b = 1 region): n_streams
+    independent 323-token prompts, then `steps` batched steps at positions 323..451;
+    CUDA-event time of the steps."""
+    eng = pk.Engine(path, n_ctx=512, max_batch=32, device=device)  # a multiple of 4: the tiled attention
+    try:
+        weights = eng.info["stream_bytes"]
+        eng.streams_begin(n_streams)
+        for s in range(n_streams):
+            eng.stream_prefill(s, synth.prompt_ids(1000 + s, PROMPT_LEN, spec.n_vocab))
+        eng.streams_decode(warmup)
+        eng.streams_set_position(PROMPT_LEN)
+        _, ms = eng.streams_decode(steps, return_ms=True)
+    finally:
+        eng.close()
+    ms_step = ms / steps
+    step_bytes = weights + spec.kv_bytes_per_position() * n_streams * (PROMPT_LEN + 1 + steps / 2)
+    hbm, peak_kind = peaks()
+    gbs = step_bytes / (ms_step / 1000.0) / 1e9
+    return {"streams": n_streams, "tok_s": n_streams / (ms_step / 1000.0), "ms_per_step": ms_step,
+            "bytes_per_step": step_bytes, "achieved_gbs": gbs, "hbm_frac": gbs / hbm, "peak_kind": peak_kind,
+            "steps": steps,
+            "note": "bench.py --streams 8 for the full line (roofline, clocks, 16K case with --stream-ctx)"}
 
 
 def run_streams(args):
