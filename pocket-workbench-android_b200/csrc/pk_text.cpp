@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <queue>
 
 #include "pk_gguf.h"
 
@@ -392,10 +393,26 @@ struct Matcher {
     return false;
   }
 
+  static bool one(const Node &nd, char32_t c) {
+    return nd.kind == Node::Char ? c == nd.ch : nd.kind == Node::Any ? (c != U'\n' && c != U'\r') : class_match(nd, c);
+  }
+
   // Greedy: one more of the node (it must consume something) before the
   // rest; a repeated repeat or lookahead never repeats (:354-395).
   bool rep(const Node &r, const Node *rest, size_t rc, size_t pos, size_t count, Cont k) const {
     const Node &node = r.sub[0];
+    if (count == 0 && (node.kind == Node::Char || node.kind == Node::Any || node.kind == Node::Class)) {
+      // A one-character node: the recursion below would take the longest run
+      // and then try the rest after c = run, run - 1, ..., min characters.
+      // The same order as a loop, so a long run of letters or spaces costs no
+      // stack depth.
+      const size_t lim = r.max == kNoMax ? t.size() - pos : std::min(r.max, t.size() - pos);
+      size_t m = 0;
+      while (m < lim && one(node, t[pos + m])) m++;
+      for (size_t c = m + 1; c-- > 0;)
+        if (c >= r.min && seq(rest, rc, pos + c, k)) return true;
+      return false;
+    }
     const bool can_more = r.max == kNoMax || count < r.max;
     if (can_more && node.kind != Node::Repeat && node.kind != Node::Look) {
       const auto next = [&](size_t p2) { return p2 != pos && rep(r, rest, rc, p2, count + 1, k); };
@@ -585,25 +602,50 @@ void Tokenizer::encode_word(const std::u32string &word, std::vector<uint32_t> &o
       return;
     }
   }
-  std::vector<std::string> sym(mapped.size());
-  for (size_t i = 0; i < mapped.size(); i++) utf8_append(sym[i], mapped[i]);
-  const auto rank_of = [&](size_t i) -> uint32_t {
-    const auto it = merges_.find({sym[i], sym[i + 1]});
-    return it == merges_.end() ? UINT32_MAX : it->second;
-  };
-  std::vector<uint32_t> rank(sym.size() > 1 ? sym.size() - 1 : 0);
-  for (size_t i = 0; i < rank.size(); i++) rank[i] = rank_of(i);
-  while (!rank.empty()) {
-    size_t bi = 0;
-    for (size_t i = 1; i < rank.size(); i++)
-      if (rank[i] < rank[bi]) bi = i;
-    if (rank[bi] == UINT32_MAX) break;
-    sym[bi] += sym[bi + 1];
-    sym.erase(sym.begin() + (long)bi + 1);
-    rank.erase(rank.begin() + (long)bi);
-    if (bi < rank.size()) rank[bi] = rank_of(bi);
-    if (bi > 0) rank[bi - 1] = rank_of(bi - 1);
+  // Symbols as a linked list (indexed by their first character) and a heap
+  // of candidate pairs ordered by (rank, position): popping the smallest
+  // still-current pair is the reference's "lowest rank, leftmost" pick, in
+  // O(n log n) instead of a rescan per merge.  A pair is stale once either
+  // side has changed (version numbers).
+  const size_t n = mapped.size();
+  std::vector<std::string> sym(n);
+  for (size_t i = 0; i < n; i++) utf8_append(sym[i], mapped[i]);
+  std::vector<long> nxt(n), prv(n);
+  std::vector<uint32_t> ver(n, 0);
+  for (size_t i = 0; i < n; i++) {
+    nxt[i] = i + 1 < n ? (long)(i + 1) : -1;
+    prv[i] = (long)i - 1;
   }
+  struct Cand {
+    uint32_t rank;
+    size_t left, right;
+    uint32_t vl, vr;
+  };
+  const auto later = [](const Cand &a, const Cand &b) { return a.rank != b.rank ? a.rank > b.rank : a.left > b.left; };
+  std::priority_queue<Cand, std::vector<Cand>, decltype(later)> heap(later);
+  const auto push = [&](size_t l) {
+    const long r = nxt[l];
+    if (r < 0) return;
+    const auto it = merges_.find({sym[l], sym[(size_t)r]});
+    if (it != merges_.end()) heap.push(Cand{it->second, l, (size_t)r, ver[l], ver[(size_t)r]});
+  };
+  for (size_t i = 0; i + 1 < n; i++) push(i);
+  while (!heap.empty()) {
+    const Cand c = heap.top();
+    heap.pop();
+    if (ver[c.left] != c.vl || ver[c.right] != c.vr || nxt[c.left] != (long)c.right) continue;
+    sym[c.left] += sym[c.right];
+    sym[c.right].clear();
+    ver[c.left]++;
+    ver[c.right]++;
+    nxt[c.left] = nxt[c.right];
+    if (nxt[c.right] >= 0) prv[(size_t)nxt[c.right]] = (long)c.left;
+    if (prv[c.left] >= 0) push((size_t)prv[c.left]);
+    push(c.left);
+  }
+  std::vector<std::string> merged;
+  for (long i = n ? 0 : -1; i >= 0; i = nxt[(size_t)i]) merged.push_back(std::move(sym[(size_t)i]));
+  sym.swap(merged);
   std::u32string cs;
   for (const std::string &s : sym) {
     const auto it = token_to_id_.find(s);

@@ -269,3 +269,24 @@ def test_tokenizer_corners(text, ot, tmp_path):
     nometa = str(tmp_path / "nometa.gguf")
     synth.write_tokenizer_gguf(nometa, [], None)
     assert text.Tokenizer(nometa).encode("abc") == []
+
+
+def test_long_runs(text, ot):
+    """Runs of hundreds of thousands of letters, spaces or digits: the one-
+    character repeats run as loops, so the matches (checked against the
+    `regex` engine) come back without deep recursion, and a whole long text
+    tokenizes."""
+    import regex
+
+    cases = [(ot.PRE["gpt-2"][0], "a" * 300000 + " b"), (r"\s+(?!\S)|\s+", " " * 200000 + "x"),
+             (ot.PRE["minicpm5"][0], "7" * 30001), (ot.PRE["llama3"][0], "\n" * 50000 + "end " + "z" * 70000)]
+    for pat, t in cases:
+        assert text.find(pat, t) == [(m.start(), m.end()) for m in regex.finditer(pat, t)]
+
+
+def test_long_text_tokenizes(text, vocabs):
+    path, _, _, o = vocabs["gpt-2"]
+    tk = text.Tokenizer(path)
+    t = "x" * 100000 + " " * 100000 + "9" * 1000
+    ids = tk.encode(t, False)
+    assert tk.decode(ids) == t.encode()
