@@ -335,6 +335,13 @@ int pk_tokenize(const pk_tokenizer *tok, const char *text, size_t len, int parse
 int pk_token_bytes(const pk_tokenizer *tok, uint32_t id, uint8_t *out, size_t cap, size_t *n_out);
 /* 1 when id ends generation, else 0. */
 int pk_token_is_eog(const pk_tokenizer *tok, uint32_t id);
+/* model.rs:1355-1388 flush_utf8, for streaming the text of generated tokens (pk_token_bytes appended
+ * to a pending buffer after every token): the text ready in pending[0 .. *n_pending) -- the longest
+ * valid UTF-8 prefix, each invalid sequence (its maximal valid-so-far part) replaced by U+FFFD,
+ * repeated until only an incomplete trailing sequence or nothing is left.  That tail moves to the
+ * front of pending and *n_pending becomes its length.  Writes min(cap, n) text bytes to out and
+ * *n_out = n (at most 3 * *n_pending); PK_ERR_INVALID for n > cap, pending unchanged then. */
+int pk_utf8_flush(uint8_t *pending, size_t *n_pending, uint8_t *out, size_t cap, size_t *n_out);
 /* Host restatement for tests: the matches of a pre-tokenizer pattern (UTF-8, plen bytes) over a
  * UTF-8 text, as (start, end) code-point offsets, two entries per match.  Writes min(cap, n)
  * entries and *n_out = n; PK_ERR_INVALID for malformed UTF-8 or n > cap. */

@@ -641,6 +641,18 @@ int pk_token_bytes(const pk_tokenizer *t, uint32_t id, uint8_t *out, size_t cap,
 
 int pk_token_is_eog(const pk_tokenizer *t, uint32_t id) { return t && t->tok.is_eog(id) ? 1 : 0; }
 
+int pk_utf8_flush(uint8_t *pending, size_t *n_pending, uint8_t *out, size_t cap, size_t *n_out) {
+  if (!n_pending || (!pending && *n_pending) || (!out && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  std::string text;
+  const size_t used = pk::text::utf8_flush(pending, *n_pending, text);
+  const int rc = copy_out(reinterpret_cast<const uint8_t *>(text.data()), text.size(), out, cap, n_out,
+                          "pk_utf8_flush");
+  if (rc) return rc;
+  std::memmove(pending, pending + used, *n_pending - used);
+  *n_pending -= used;
+  return PK_OK;
+}
+
 int pk_text_find(const char *pattern, size_t plen, const char *text, size_t tlen, uint32_t *bounds, size_t cap,
                  size_t *n_out) {
   if ((!pattern && plen) || (!text && tlen) || (!bounds && cap)) return set_error(PK_ERR_INVALID, "null argument");

@@ -78,6 +78,55 @@ void utf8_append(std::string &o, char32_t c) {
   }
 }
 
+// Well-formed sequences (the Unicode standard's table of UTF-8 byte
+// sequences): the second byte's range depends on the lead byte, the others
+// are 80..BF.
+int utf8_sequence(const uint8_t *p, size_t n, size_t *bad) {
+  const uint8_t c0 = p[0];
+  int len;
+  uint8_t lo = 0x80, hi = 0xBF;  // range of the second byte
+  if (c0 < 0x80) return 1;
+  if (c0 >= 0xC2 && c0 <= 0xDF) len = 2;
+  else if (c0 == 0xE0) { len = 3; lo = 0xA0; }
+  else if ((c0 >= 0xE1 && c0 <= 0xEC) || c0 == 0xEE || c0 == 0xEF) len = 3;
+  else if (c0 == 0xED) { len = 3; hi = 0x9F; }
+  else if (c0 == 0xF0) { len = 4; lo = 0x90; }
+  else if (c0 >= 0xF1 && c0 <= 0xF3) len = 4;
+  else if (c0 == 0xF4) { len = 4; hi = 0x8F; }
+  else {
+    *bad = 1;  // 80..C1, F5..FF never start a sequence
+    return 0;
+  }
+  for (int i = 1; i < len; i++) {
+    if ((size_t)i >= n) return -1;
+    const uint8_t c = p[i];
+    const bool ok = i == 1 ? (c >= lo && c <= hi) : (c >= 0x80 && c <= 0xBF);
+    if (!ok) {
+      *bad = (size_t)i;
+      return 0;
+    }
+  }
+  return len;
+}
+
+size_t utf8_flush(const uint8_t *p, size_t n, std::string &out) {
+  size_t i = 0;
+  while (i < n) {
+    size_t bad = 0;
+    const int len = utf8_sequence(p + i, n - i, &bad);
+    if (len > 0) {
+      out.append(reinterpret_cast<const char *>(p + i), (size_t)len);
+      i += (size_t)len;
+    } else if (len == 0) {
+      out += "\xEF\xBF\xBD";  // U+FFFD
+      i += bad;
+    } else {
+      break;  // an incomplete sequence at the end waits for the next bytes
+    }
+  }
+  return i;
+}
+
 static std::string to_utf8(const std::u32string &s) {
   std::string o;
   o.reserve(s.size());

@@ -30,6 +30,15 @@ bool is_white_space(char32_t c);
 bool utf8_decode(const char *s, size_t n, std::u32string *out);
 void utf8_append(std::string &out, char32_t c);
 
+// One UTF-8 sequence at p[0 .. n): its length (1..4) when well formed; 0 and
+// *bad = the length of its longest well-formed-so-far part (at least 1) when
+// malformed; -1 when it is a well-formed prefix cut off by the end of p.
+int utf8_sequence(const uint8_t *p, size_t n, size_t *bad);
+// model.rs:1355-1388 flush_utf8: appends the ready text of pending to out
+// (U+FFFD for each malformed sequence) and returns how many bytes of
+// pending were consumed (the rest is an incomplete trailing sequence).
+size_t utf8_flush(const uint8_t *pending, size_t n, std::string &out);
+
 // A compiled pre-tokenizer pattern (regexlite.rs:1-481).
 class Pattern {
  public:

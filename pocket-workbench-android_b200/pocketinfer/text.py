@@ -65,6 +65,25 @@ class Tokenizer:
         return bool(lib().pk_token_is_eog(self.h, tid))
 
 
+class Utf8Stream:
+    """flush_utf8 (model.rs:1355-1388) over a stream of token bytes: feed()
+    returns the text that is ready; an incomplete trailing sequence waits."""
+
+    def __init__(self):
+        self.pending = b""
+
+    def feed(self, b: bytes) -> bytes:
+        data = self.pending + bytes(b)
+        buf = (C.c_uint8 * max(len(data), 1)).from_buffer_copy(data or b"\0")
+        n = C.c_size_t(len(data))
+        out = (C.c_uint8 * (3 * len(data) + 1))()
+        m = C.c_size_t()
+        _check(lib().pk_utf8_flush(C.cast(buf, C.c_void_p), C.byref(n), C.cast(out, C.c_void_p), len(out),
+                                   C.byref(m)))
+        self.pending = bytes(buf[: n.value])
+        return bytes(out[: m.value])
+
+
 def find(pattern: str, text: str) -> list:
     """The (start, end) code-point spans of the pattern's matches (regexlite.rs find)."""
     p, t = pattern.encode(), text.encode()
@@ -115,4 +134,4 @@ def thinking_on_suffix() -> str:
     return lib().pk_chat_thinking_suffix().decode()
 
 
-__all__ = ["Tokenizer", "find", "split", "chat_apply", "is_minicpm5", "direct_suffix", "thinking_on_suffix", "PkError"]
+__all__ = ["Tokenizer", "Utf8Stream", "find", "split", "chat_apply", "is_minicpm5", "direct_suffix", "thinking_on_suffix", "PkError"]

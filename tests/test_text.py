@@ -290,3 +290,31 @@ def test_long_text_tokenizes(text, vocabs):
     t = "x" * 100000 + " " * 100000 + "9" * 1000
     ids = tk.encode(t, False)
     assert tk.decode(ids) == t.encode()
+
+
+def test_utf8_flush_matches_decoder(text):
+    """flush_utf8 over token bytes cut at random points: after every piece, the
+    text so far is Python's decoding (with replacement: one U+FFFD per maximal
+    ill-formed part, as Rust's Utf8Error::error_len defines it) of all bytes
+    but the held-back tail, and that tail is only a cut-off well-formed
+    sequence ("unexpected end of data").  (Python's incremental decoder is not
+    the pin: it also holds back ED A0..BF, which Rust reports at once.)"""
+    rng = random.Random(29)
+    pieces = [c.encode() for c in "aè中😀"] + [b"\x80", b"\xc0", b"\xc2", b"\xe2\x82", b"\xed\xa0\x80", b"\xf0\x80",
+                                                b"\xf4\x90\x80\x80", b"\xff", b"\xe0\x9f\x80", b"\xf0\x9f"]
+    for _ in range(300):
+        data = b"".join(rng.choice(pieces) for _ in range(rng.randint(0, 30)))
+        cuts = sorted(rng.sample(range(len(data) + 1), min(len(data) + 1, rng.randint(0, 6))))
+        chunks = [data[a:b] for a, b in zip([0] + cuts, cuts + [len(data)])]
+        st = text.Utf8Stream()
+        got, seen = b"", b""
+        for ch in chunks:
+            got += st.feed(ch)
+            seen += ch
+            done = seen[: len(seen) - len(st.pending)]
+            assert got == done.decode("utf-8", "replace").encode(), (data, chunks)
+            if st.pending:
+                assert len(st.pending) <= 3
+                with pytest.raises(UnicodeDecodeError) as e:
+                    st.pending.decode("utf-8")
+                assert e.value.reason == "unexpected end of data"
