@@ -357,6 +357,16 @@ typedef struct {
  * bytes (no terminator) and *n_out = n; PK_ERR_INVALID for n > cap. */
 int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add_generation_prompt, char *out,
                   size_t cap, size_t *n_out);
+/* The prompt ids of a chat request as the reference's Android bridge builds them (jni.rs:416-456):
+ * the template over the kept turns, the direct-answer suffix when direct_answer is set, the template
+ * is MiniCPM5 and the text ends with the assistant header (*direct_applied = 1), then pk_tokenize with
+ * special tokens.  While the ids exceed n_ctx - 1024 (no limit when n_ctx < 1024), one old turn is
+ * dropped: the second kept turn, or the third when the first is a system turn; *n_dropped counts
+ * them.  PK_ERR_CONTEXT_FULL when only that many turns are left and the ids still do not fit.
+ * Writes min(cap, n) ids and *n_ids = n; PK_ERR_INVALID for n > cap. */
+int pk_chat_prompt(const pk_tokenizer *tok, const pk_chat_message *msgs, int n_msgs, int minicpm5,
+                   int direct_answer, size_t n_ctx, uint32_t *ids, size_t cap, size_t *n_ids, int *n_dropped,
+                   int *direct_applied);
 /* 1 when the tokenizer's pre name or the model name selects the MiniCPM5 template. */
 int pk_chat_is_minicpm5(const char *pre, const char *name);
 /* Suffixes a host appends after the generation prompt: a direct answer (empty reasoning block)

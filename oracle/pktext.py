@@ -11,6 +11,8 @@ to rust/pocketinfer/src/:
   regexlite.rs:461-481 split()
   tokenizer.rs:38-300  from_gguf, encode_word, encode_plain, encode, decode_token
   chat.rs:16-109       is_minicpm5, apply_minicpm5, apply_generic, suffixes
+  jni.rs:416-456       a chat request's prompt ids: template, direct-answer suffix,
+                       dropping old turns until n_ctx - 1024 holds the ids
 Character classes use Unicode properties computed here from `unicodedata`
 (general categories) and the White_Space list of the Unicode standard, not
 the library's generated tables.  Parity is pinned in tests against the `regex`
@@ -472,3 +474,23 @@ def apply_minicpm5(msgs, add_generation_prompt=True) -> str:
 def apply_generic(msgs, add_generation_prompt=True) -> str:
     out = "".join("<|im_start|>" + r + "\n" + c + "<|im_end|>\n" for r, c in msgs)
     return out + ("<|im_start|>assistant\n" if add_generation_prompt else "")
+
+
+def chat_prompt(tok: Tokenizer, msgs, minicpm5: bool, direct_answer: bool, n_ctx: int):
+    """jni.rs:416-456: (ids, dropped turns, direct suffix applied); raises
+    OverflowError where the bridge gives up (the context cannot hold it)."""
+    limit = n_ctx - 1024 if n_ctx >= 1024 else float("inf")  # usize wrap-around: no limit
+    kept = list(range(len(msgs)))
+    while True:
+        view = [msgs[i] for i in kept]
+        prompt = apply_minicpm5(view, True) if minicpm5 else apply_generic(view, True)
+        direct = bool(direct_answer and minicpm5 and prompt.endswith("<|im_start|>assistant\n"))
+        if direct:
+            prompt += "<think>\n\n</think>\n\n"
+        ids = tok.encode(prompt, True)
+        if len(ids) <= limit:
+            return ids, len(msgs) - len(kept), direct
+        oldest = 2 if kept and msgs[kept[0]][0] == "system" else 1
+        if len(kept) <= oldest + 1:
+            raise OverflowError("Latest request exceeds the context window.")
+        del kept[oldest]

@@ -682,6 +682,43 @@ int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add
   return copy_out(s.data(), s.size(), out, cap, n_out, "pk_chat_apply");
 }
 
+int pk_chat_prompt(const pk_tokenizer *t, const pk_chat_message *msgs, int n_msgs, int minicpm5, int direct_answer,
+                   size_t n_ctx, uint32_t *ids, size_t cap, size_t *n_ids, int *n_dropped, int *direct_applied) {
+  if (!t || (!msgs && n_msgs) || n_msgs < 0 || (!ids && cap)) return set_error(PK_ERR_INVALID, "null argument");
+  std::vector<pk::text::Message> all((size_t)n_msgs);
+  for (int i = 0; i < n_msgs; i++) {
+    if (!msgs[i].role || !msgs[i].content) return set_error(PK_ERR_INVALID, "message with a null role or content");
+    all[i].role = msgs[i].role;
+    all[i].content = msgs[i].content;
+  }
+  // n_ctx - 1024 as the bridge's unsigned arithmetic has it: below 1024 the
+  // difference wraps and nothing is dropped
+  const size_t limit = n_ctx >= 1024 ? n_ctx - 1024 : SIZE_MAX;
+  std::vector<size_t> kept((size_t)n_msgs);
+  for (size_t i = 0; i < kept.size(); i++) kept[i] = i;
+  std::vector<uint32_t> toks;
+  bool direct = false;
+  for (;;) {
+    std::vector<pk::text::Message> view;
+    for (size_t i : kept) view.push_back(all[i]);
+    std::string prompt = minicpm5 ? pk::text::apply_minicpm5(view, true) : pk::text::apply_generic(view, true);
+    const std::string head = "<|im_start|>assistant\n";
+    direct = direct_answer && minicpm5 && prompt.size() >= head.size() &&
+             prompt.compare(prompt.size() - head.size(), head.size(), head) == 0;
+    if (direct) prompt += pk::text::direct_suffix();
+    toks = t->tok.encode(prompt, true);
+    if (toks.size() <= limit) break;
+    const size_t oldest = (!kept.empty() && all[kept[0]].role == "system") ? 2 : 1;
+    if (kept.size() <= oldest + 1)
+      return set_error(PK_ERR_CONTEXT_FULL,
+                       "Latest request exceeds the context window. Select a larger window or shorten the message.");
+    kept.erase(kept.begin() + (long)oldest);
+  }
+  if (n_dropped) *n_dropped = n_msgs - (int)kept.size();
+  if (direct_applied) *direct_applied = direct ? 1 : 0;
+  return copy_out(toks.data(), toks.size(), ids, cap, n_ids, "pk_chat_prompt");
+}
+
 int pk_chat_is_minicpm5(const char *pre, const char *name) {
   return pk::text::is_minicpm5(pre ? pre : "", name ? name : "") ? 1 : 0;
 }

@@ -41,7 +41,7 @@ SYMBOLS = [
     "pk_tp_info_get", "pk_tp_split", "pk_tp_pick", "pk_sample_scratch_bytes", "pk_sample",
     "pk_streams_begin", "pk_stream_prefill", "pk_streams_decode", "pk_streams_set_position",
     "pk_tokenizer_load", "pk_tokenizer_free", "pk_tokenizer_info_get", "pk_tokenize", "pk_token_bytes",
-    "pk_token_is_eog", "pk_utf8_flush", "pk_text_find", "pk_chat_apply", "pk_chat_is_minicpm5", "pk_chat_direct_suffix", "pk_chat_thinking_suffix",
+    "pk_token_is_eog", "pk_utf8_flush", "pk_text_find", "pk_chat_apply", "pk_chat_prompt", "pk_chat_is_minicpm5", "pk_chat_direct_suffix", "pk_chat_thinking_suffix",
 ]
 
 
@@ -144,6 +144,7 @@ def lib():
         "pk_text_find": ([C.c_char_p, SZ, C.c_char_p, SZ, P, SZ, C.POINTER(SZ)], I),
         "pk_utf8_flush": ([P, C.POINTER(SZ), P, SZ, C.POINTER(SZ)], I),
         "pk_chat_apply": ([P, I, I, I, P, SZ, C.POINTER(SZ)], I), "pk_chat_is_minicpm5": ([C.c_char_p, C.c_char_p], I),
+        "pk_chat_prompt": ([P, P, I, I, I, SZ, P, SZ, C.POINTER(SZ), C.POINTER(I), C.POINTER(I)], I),
         "pk_chat_direct_suffix": ([], C.c_char_p), "pk_chat_thinking_suffix": ([], C.c_char_p),
     }
     for name, (args, res) in sig.items():

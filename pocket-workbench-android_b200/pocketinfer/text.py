@@ -122,6 +122,20 @@ def chat_apply(messages, minicpm5: bool = True, add_generation_prompt: bool = Tr
     return out.raw[: n.value].decode()
 
 
+def chat_prompt(tok: Tokenizer, messages, minicpm5: bool = True, direct_answer: bool = False,
+                n_ctx: int = 8192) -> dict:
+    """The request's prompt ids as the Android bridge builds them (jni.rs:416-456)."""
+    pairs = [(m["role"], m["content"]) if isinstance(m, dict) else tuple(m) for m in messages]
+    keep = [(r.encode(), c.encode()) for r, c in pairs]
+    arr = (ChatMessage * max(len(keep), 1))(*[ChatMessage(r, c) for r, c in keep])
+    cap = sum(len(r) + len(c) for r, c in keep) * 2 + 64
+    out = (C.c_uint32 * cap)()
+    n, dropped, direct = C.c_size_t(), C.c_int(), C.c_int()
+    _check(lib().pk_chat_prompt(tok.h, C.cast(arr, C.c_void_p), len(keep), int(minicpm5), int(direct_answer), n_ctx,
+                                C.cast(out, C.c_void_p), cap, C.byref(n), C.byref(dropped), C.byref(direct)))
+    return {"ids": list(out[: n.value]), "dropped": dropped.value, "direct_applied": bool(direct.value)}
+
+
 def is_minicpm5(pre: str, name: str) -> bool:
     return bool(lib().pk_chat_is_minicpm5(pre.encode(), name.encode()))
 
@@ -134,4 +148,4 @@ def thinking_on_suffix() -> str:
     return lib().pk_chat_thinking_suffix().decode()
 
 
-__all__ = ["Tokenizer", "Utf8Stream", "find", "split", "chat_apply", "is_minicpm5", "direct_suffix", "thinking_on_suffix", "PkError"]
+__all__ = ["Tokenizer", "Utf8Stream", "find", "split", "chat_apply", "chat_prompt", "is_minicpm5", "direct_suffix", "thinking_on_suffix", "PkError"]

@@ -318,3 +318,30 @@ def test_utf8_flush_matches_decoder(text):
                 with pytest.raises(UnicodeDecodeError) as e:
                     st.pending.decode("utf-8")
                 assert e.value.reason == "unexpected end of data"
+
+
+@pytest.mark.parametrize("pre", ["minicpm5", "gpt-2"])
+def test_chat_prompt_matches_bridge(text, ot, vocabs, pre):
+    """A chat request's prompt ids (jni.rs:416-456): template, direct-answer
+    suffix, and old turns dropped until the ids fit n_ctx - 1024 (the third
+    turn first when the first is a system turn), or the request refused."""
+    from pocketinfer import PkError
+
+    path, _, _, o = vocabs[pre]
+    tk = text.Tokenizer(path)
+    rng = random.Random(31)
+    roles = ["system", "user", "assistant", "user", "tool"]
+    for i in range(150):
+        msgs = [(rng.choice(roles) if j else rng.choice(["system", "user"]), rand_text(rng, rng.randint(1, 8)))
+                for j in range(rng.randint(1, 7))]
+        mini, direct = rng.random() < 0.7, rng.random() < 0.5
+        n_ctx = rng.choice([1024 + rng.randint(0, 120), 500, 8192])
+        try:
+            want = ot.chat_prompt(o, msgs, mini, direct, n_ctx)
+        except OverflowError:
+            with pytest.raises(PkError) as e:
+                text.chat_prompt(tk, msgs, mini, direct, n_ctx)
+            assert e.value.code == 6  # PK_ERR_CONTEXT_FULL
+            continue
+        got = text.chat_prompt(tk, msgs, mini, direct, n_ctx)
+        assert (got["ids"], got["dropped"], got["direct_applied"]) == want, (msgs, mini, direct, n_ctx)
