@@ -354,7 +354,7 @@ typedef struct {
 } pk_chat_message;
 /* The prompt text of a conversation: minicpm5 != 0 the MiniCPM5 template, else generic
  * <|im_start|>role turns; add_generation_prompt appends the assistant header.  Writes min(cap, n)
- * bytes (no terminator) and *n_out = n; PK_ERR_INVALID for n > cap. */
+ * bytes (no terminator) and *n_out = n; PK_ERR_INVALID for n > cap or a message that is not UTF-8. */
 int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add_generation_prompt, char *out,
                   size_t cap, size_t *n_out);
 /* The prompt ids of a chat request as the reference's Android bridge builds them (jni.rs:416-456):
@@ -363,7 +363,7 @@ int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add
  * special tokens.  While the ids exceed n_ctx - 1024 (no limit when n_ctx < 1024), one old turn is
  * dropped: the second kept turn, or the third when the first is a system turn; *n_dropped counts
  * them.  PK_ERR_CONTEXT_FULL when only that many turns are left and the ids still do not fit.
- * Writes min(cap, n) ids and *n_ids = n; PK_ERR_INVALID for n > cap. */
+ * Writes min(cap, n) ids and *n_ids = n; PK_ERR_INVALID for n > cap or a message that is not UTF-8. */
 int pk_chat_prompt(const pk_tokenizer *tok, const pk_chat_message *msgs, int n_msgs, int minicpm5,
                    int direct_answer, size_t n_ctx, uint32_t *ids, size_t cap, size_t *n_ids, int *n_dropped,
                    int *direct_applied);

@@ -581,6 +581,22 @@ struct pk_tokenizer {
 
 namespace {
 
+// Roles and contents of chat messages: present and valid UTF-8 (the
+// reference receives them as Rust strings, which always are).
+int read_messages(const pk_chat_message *msgs, int n_msgs, std::vector<pk::text::Message> &m) {
+  m.assign((size_t)n_msgs, pk::text::Message{});
+  std::u32string check;
+  for (int i = 0; i < n_msgs; i++) {
+    if (!msgs[i].role || !msgs[i].content) return set_error(PK_ERR_INVALID, "message with a null role or content");
+    m[i].role = msgs[i].role;
+    m[i].content = msgs[i].content;
+    if (!pk::text::utf8_decode(m[i].role.data(), m[i].role.size(), &check) ||
+        !pk::text::utf8_decode(m[i].content.data(), m[i].content.size(), &check))
+      return set_error(PK_ERR_INVALID, "message " + std::to_string(i) + " is not valid UTF-8");
+  }
+  return PK_OK;
+}
+
 template <class T>
 int copy_out(const T *src, size_t n, T *out, size_t cap, size_t *n_out, const char *what) {
   if (n_out) *n_out = n;
@@ -671,12 +687,8 @@ int pk_text_find(const char *pattern, size_t plen, const char *text, size_t tlen
 int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add_generation_prompt, char *out,
                   size_t cap, size_t *n_out) {
   if ((!msgs && n_msgs) || n_msgs < 0 || (!out && cap)) return set_error(PK_ERR_INVALID, "null argument");
-  std::vector<pk::text::Message> m((size_t)n_msgs);
-  for (int i = 0; i < n_msgs; i++) {
-    if (!msgs[i].role || !msgs[i].content) return set_error(PK_ERR_INVALID, "message with a null role or content");
-    m[i].role = msgs[i].role;
-    m[i].content = msgs[i].content;
-  }
+  std::vector<pk::text::Message> m;
+  if (const int rc = read_messages(msgs, n_msgs, m)) return rc;
   const std::string s = minicpm5 ? pk::text::apply_minicpm5(m, add_generation_prompt != 0)
                                  : pk::text::apply_generic(m, add_generation_prompt != 0);
   return copy_out(s.data(), s.size(), out, cap, n_out, "pk_chat_apply");
@@ -685,12 +697,8 @@ int pk_chat_apply(const pk_chat_message *msgs, int n_msgs, int minicpm5, int add
 int pk_chat_prompt(const pk_tokenizer *t, const pk_chat_message *msgs, int n_msgs, int minicpm5, int direct_answer,
                    size_t n_ctx, uint32_t *ids, size_t cap, size_t *n_ids, int *n_dropped, int *direct_applied) {
   if (!t || (!msgs && n_msgs) || n_msgs < 0 || (!ids && cap)) return set_error(PK_ERR_INVALID, "null argument");
-  std::vector<pk::text::Message> all((size_t)n_msgs);
-  for (int i = 0; i < n_msgs; i++) {
-    if (!msgs[i].role || !msgs[i].content) return set_error(PK_ERR_INVALID, "message with a null role or content");
-    all[i].role = msgs[i].role;
-    all[i].content = msgs[i].content;
-  }
+  std::vector<pk::text::Message> all;
+  if (const int rc = read_messages(msgs, n_msgs, all)) return rc;
   // n_ctx - 1024 as the bridge's unsigned arithmetic has it: below 1024 the
   // difference wraps and nothing is dropped
   const size_t limit = n_ctx >= 1024 ? n_ctx - 1024 : SIZE_MAX;

@@ -345,3 +345,23 @@ def test_chat_prompt_matches_bridge(text, ot, vocabs, pre):
             continue
         got = text.chat_prompt(tk, msgs, mini, direct, n_ctx)
         assert (got["ids"], got["dropped"], got["direct_applied"]) == want, (msgs, mini, direct, n_ctx)
+
+
+def test_chat_messages_must_be_utf8(text, vocabs):
+    import ctypes as C
+
+    from pocketinfer import PkError, lib
+
+    tk = text.Tokenizer(vocabs["gpt-2"][0])
+    arr = (text.ChatMessage * 2)(text.ChatMessage(b"user", b"ciao"), text.ChatMessage(b"user", b"ab\xff"))
+    n, d, f = C.c_size_t(), C.c_int(), C.c_int()
+    out = (C.c_uint32 * 64)()
+    assert lib().pk_chat_prompt(tk.h, C.cast(arr, C.c_void_p), 2, 1, 0, 8192, C.cast(out, C.c_void_p), 64,
+                                C.byref(n), C.byref(d), C.byref(f)) == 1
+    assert "UTF-8" in lib().pk_last_error().decode()
+    buf = C.create_string_buffer(256)
+    m = C.c_size_t()
+    assert lib().pk_chat_apply(C.cast(arr, C.c_void_p), 2, 1, 1, C.cast(buf, C.c_void_p), 256, C.byref(m)) == 1
+    assert lib().pk_chat_apply(C.cast(arr, C.c_void_p), 1, 1, 1, C.cast(buf, C.c_void_p), 256, C.byref(m)) == 0
+    with pytest.raises(PkError):
+        text.chat_prompt(tk, [("user", "x" * 50)], n_ctx=1024)  # no room at all: refused
