@@ -39,6 +39,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1024)
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--order", choices=["exact", "fast"], default="exact",
+                   help="float order of the decode step (pk_set_order): the reference's exact order, or the fast "
+                        "order (Q8 and integer dots exact, float sums regrouped; within 1e-3 per matvec)")
     p.add_argument("--model-dir", default=os.environ.get("PK_MODEL_DIR", tempfile.gettempdir()))
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the bounded CPU baseline sample")
@@ -57,6 +60,9 @@ def parse_args():
                         "the long-context timing case)")
     p.add_argument("--prefill-only", action="store_true",
                    help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
+    p.add_argument("--decode-only", action="store_true",
+                   help="only the timed decode (with its traced profile and e2e): no prefill, streams, config-1 "
+                        "or CPU legs")
     p.add_argument("--profile-window", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return p.parse_args()
@@ -202,37 +208,34 @@ def cycle_steps(eng, n, state, timed):
     return total_ms
 
 
-def cpu_baseline_sample(path, prompt, budget_s):
-    """The CPU restatement (oracle) on this host: decode tok/s on a bounded sample."""
-    import pko
-
-    threads = os.cpu_count() or 1
-    o = pko.Engine(path, 512, threads)
-    short = prompt[:32]
-    probe = o.generate(short, 3)
-    per_tok = max(probe["gen_ms"] / 2.0, 1e-3) / 1000.0
-    s = int(max(4, min(64, budget_s / per_tok)))
-    r = o.generate(short, s + 1)
-    o.close()
-    return {"value": s / (r["gen_ms"] / 1000.0), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"M26 greedy decode, {s} tokens after a 32-token prompt (KV 32..{32 + s} positions), "
-                      f"C++ restatement of pocketinfer's CPU int8 lanes path, {threads} threads"}
+WORKLOAD = "M26 greedy decode b=1 (BASELINE config 3): 323-token prompt, positions 323..450 cycled"
 
 
-def run_reference(args):
-    world, rank, _ = dist_info()
-    if rank != 0:
-        return
+def workload_config(args, world):
+    """The line's `config`: the same workload string and model on both arms."""
+    from pocketinfer import synth
+
+    full = args.layers is None and args.vocab is None
+    return {"workload": WORKLOAD if full else
+            f"reduced M26-shaped model {synth.m26_spec(args.layers, args.vocab).name} (profiling case, "
+            "not the BASELINE workload)", "model": "synthetic-2.6B-q4km (random blocks)",
+            "global_batch": world, "seq_len": PROMPT_LEN + CYCLE,
+            "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "l2": "no flush: each step streams 1.83 GB of weights (> 126 MB L2)"}
+
+
+def oracle_decode(path, prompt, warmup, steps, budget_s):
+    """The CPU restatement (oracle engine, all host threads) on the bench's own
+    workload: the 323-token prompt through Engine::generate's prefill, then
+    greedy decode steps at positions 323..450 (cycled), timed until `steps`
+    steps or `budget_s` seconds.  Returns (tok/s, steps timed, threads)."""
     import numpy as np
 
     import pko
-    from pocketinfer import synth
 
-    path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
-    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.m26_spec(args.layers, args.vocab).n_vocab)
     threads = os.cpu_count() or 1
     o = pko.Engine(path, 512, threads)
-    o.generate(prompt, 1)  # prefill (Engine::generate's 32-token chunks), no decode step
+    o.generate(prompt, 1)  # prefill (32-token chunks), no decode step
     pos = PROMPT_LEN
 
     def step():
@@ -243,22 +246,76 @@ def run_reference(args):
         o.forward([tok], [pos], True)
         pos += 1
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     t0 = time.perf_counter()
-    budget = 150.0
     timed = 0
-    while timed < args.steps:
+    while timed < steps:
         step()
         timed += 1
-        if time.perf_counter() - t0 > budget:
+        if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    value = timed / dt
+    o.close()
+    return timed / dt, timed, threads
+
+
+def config1_matvec(pk, synth, device, copies=40, launches=400):
+    """one Q4_K 6144 x 2048 matvec (seed 0) against the Q8 of
+    x ~ N(0,1), timed over `launches` back-to-back launches that rotate over
+    `copies` distinct weight copies (40 x 7.08 MB = 283 MB > 2 x the 126 MB
+    L2), CUDA events on the launching stream.  Bytes per launch: the weights,
+    the Q8 activation (q, d, sum) and the f32 output."""
+    import torch
+
+    w, x = synth.config1_inputs(0)
+    k, rows = 2048, 6144
+    wd = torch.from_numpy(w).to(device)
+    ws = [wd.clone() for _ in range(copies)]  # Q4_K: the device layout is the GGUF layout
+    act = pk.q8_quantize(torch.from_numpy(x).to(device), k, 1)
+    out = torch.empty(rows, dtype=torch.float32, device=device)
+    for i in range(2 * copies):  # warm-up
+        pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(launches):
+        pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / launches
+    nbytes = w.nbytes + k + 2 * 4 * (k // 32) + 4 * rows
+    hbm, kind = peaks()
+    return {"shape": "Q4_K 6144x2048, b=1", "us_per_launch": us, "bytes_per_launch": nbytes,
+            "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "hbm_frac": nbytes / (us * 1e-6) / 1e9 / hbm,
+            "peak_kind": kind, "weight_copies": copies, "launches": launches,
+            "note": "k_mv_b1 (pk_matmul_packed), back-to-back launches rotating over distinct weight copies"}
+
+
+def cpu_baseline_sample(path, prompt, budget_s):
+    """The CPU restatement on this host: decode tok/s on a bounded sample of the
+    bench's workload (positions 323.. after the 323-token prompt)."""
+    value, timed, threads = oracle_decode(path, prompt, 1, 10 ** 6, budget_s)
+    return {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"M26 greedy decode, {timed} steps at positions {PROMPT_LEN}..{PROMPT_LEN + timed - 1} after the "
+                      f"{PROMPT_LEN}-token prompt ({budget_s:.0f} s budget), C++ restatement of pocketinfer's CPU "
+                      f"int8 lanes path, {threads} threads"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return
+    from pocketinfer import synth
+
+    path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
+    prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.m26_spec(args.layers, args.vocab).n_vocab)
+    budget = 150.0
+    value, timed, threads = oracle_decode(path, prompt, args.warmup, args.steps, budget)
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000.0 / timed, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32", "data": "synthetic",
-            "config": {"workload": "M26 (BASELINE config 3) greedy decode at positions 323..450", "model": "M26"},
+            "config": workload_config(args, 1),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": f"{timed} of {args.steps} decode steps timed (budget {budget:.0f} s), "
                                        "C++ restatement of pocketinfer's CPU path (the Rust crate cannot be "
@@ -289,7 +346,7 @@ def run_ours(args):
         dist.barrier()
     path = synth.m26_path(args.model_dir, spec=synth.m26_spec(args.layers, args.vocab))
     prompt = synth.prompt_ids(PROMPT_LEN, PROMPT_LEN, synth.m26_spec(args.layers, args.vocab).n_vocab)
-    eng = pk.Engine(path, n_ctx=512, max_batch=32, device=local)
+    eng = pk.Engine(path, n_ctx=512, max_batch=32, device=local, order=args.order)
     info = eng.info
     # prefill through Engine::generate (32-token chunks); no decode step.  A
     # warm-up prompt of other tokens first (its first token differs, so the
@@ -348,8 +405,13 @@ def run_ours(args):
     cpu = None
     c4 = None
     streams = None
-    if rank == 0 and world == 1:
+    c1 = None
+    if rank == 0 and world == 1 and not args.decode_only:
         eng.close()
+        try:  # BASELINE config 1, outside the timed region
+            c1 = config1_matvec(pk, synth, torch.device("cuda", local))
+        except Exception as exc:  # noqa: BLE001
+            c1 = {"error": str(exc)[:200]}
         c4 = prefill_config4(pk, path, spec, local)  # BASELINE config 4, outside the timed region
         try:  # the data-parallel streams row, outside the timed region; never fails the line
             streams = streams_summary(pk, synth, path, spec, local)
@@ -380,13 +442,7 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8xint8->int32, f32", "data": "synthetic",
-            "config": {"workload": ("M26 greedy decode b=1 (BASELINE config 3): 323-token prompt, positions "
-                                    "323..450 cycled") if args.layers is None and args.vocab is None else
-                       f"reduced M26-shaped model {synth.m26_spec(args.layers, args.vocab).name} (profiling case, "
-                       "not the BASELINE workload)", "model": "synthetic-2.6B-q4km (random blocks)",
-                       "global_batch": world, "seq_len": PROMPT_LEN + CYCLE,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single",
-                       "l2": "no flush: each step streams 1.83 GB of weights (> 126 MB L2)"},
+            "config": dict(workload_config(args, world), order=args.order),
             "prefill_tok_s": pre["prefill_tokens"] / (pre["prefill_ms"] / 1000.0),
             "prefill": dict(prefill_summary(pre, spec, info["stream_bytes"], hbm), **(c4 or {})),
             "decode_step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
@@ -406,6 +462,7 @@ def run_ours(args):
             "clocks": clk,
             "cpu_baseline": cpu,
             "streams": streams,
+            "config1": c1,
         }
         print(json.dumps(line), flush=True)
     if dist:

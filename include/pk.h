@@ -64,6 +64,10 @@ extern "C" {
 const char *pk_last_error(void);
 /* ABI version: major * 100 + minor. */
 int pk_version(void);
+/* Architecture of the device code this library runs on the current device,
+ * as CUDA reports it for a loaded kernel (cudaFuncAttributes::binaryVersion,
+ * major * 10 + minor: 100 for sm_100a).  No reference counterpart. */
+int pk_device_binary_version(int *out);
 
 /* 1 if the device matvec handles ttype (Q4_K, Q6_K, Q4_0, Q8_0), else 0.
  * Replaces quant_int.rs:75-80 supported() and opencl.rs:432-434 supports(). */
@@ -109,10 +113,16 @@ int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows
  * instead, so a call needing more than PK_NOALLOC_SCRATCH_BYTES of packed
  * rows (pk_packed_bytes) fails with PK_ERR_INVALID before anything runs.
  * 16-byte aligned Q4_K rows are used in place and have no size limit.
- * The first call on each device looks up the scratch's address with that
- * device current (cudaGetSymbolAddress); make that first call before any
- * stream capture.  There is one scratch per device: calls that overlap in
- * time (other streams, other host threads) race on it and must be
+ * The scratch's device memory is reserved on a device when CUDA loads the
+ * library module that holds it, which it does lazily: at the first
+ * pk_create, pk_backend_new or pk_matmul_noalloc on that device (each looks
+ * up the scratch's address with that device current, cudaGetSymbolAddress).
+ * A host that gives the device's free memory to its own pool must make one
+ * of those calls on the device before it does, and the first
+ * pk_matmul_noalloc call must come before any stream capture.  The address
+ * is kept for the life of the process: a cudaDeviceReset after the first
+ * call is not supported.  There is one scratch per device: calls that
+ * overlap in time (other streams, other host threads) race on it and must be
  * serialised by the caller.  Nothing in the scratch needs to start at zero:
  * the pack kernel writes every byte the matvec then reads. */
 #define PK_NOALLOC_SCRATCH_BYTES (16u << 20)
@@ -186,6 +196,21 @@ int pk_load_gguf(pk_engine *eng, const char *path);
 void pk_destroy(pk_engine *eng);
 int pk_model_info_get(pk_engine *eng, pk_model_info *info);
 
+/* Float order of the b = 1 decode step (no reference counterpart: the
+ * reference has one order).  PK_ORDER_EXACT: every float operation in the
+ * reference's order (model.rs:777-1170, quant_int.rs:282-419), so logits and
+ * tokens are bit-identical to its CPU path.  PK_ORDER_FAST: the Q8
+ * activations and every per-block integer dot stay bit-exact, and the float
+ * combines of each matvec row, RMSNorm's sum of squares and the softmax and
+ * value sums are regrouped into partial sums (within 1e-3 relative per
+ * matvec).  Applies to pk_forward(n = 1), pk_generate's decode steps and
+ * pk_decode_steps_device; prefill chunks always take the exact order.  The
+ * default is PK_ORDER_EXACT, or PK_ORDER_FAST when the environment variable
+ * PK_ORDER=fast is set at pk_create. */
+#define PK_ORDER_EXACT 0
+#define PK_ORDER_FAST 1
+int pk_set_order(pk_engine *eng, int order);
+
 /* Engine::forward: invalidates prefix reuse.  ids/positions are host arrays. */
 int pk_forward(pk_engine *eng, const uint32_t *ids, const int *positions, int n, int want_logits);
 /* Copies the last logits (n_vocab floats) to host memory. */
@@ -253,7 +278,11 @@ int pk_selftest_bounded_wait(pk_engine *eng, int *status);
 
 /* Records layer-0 intermediates for parity bisection (Engine.dbg). */
 int pk_set_debug(pk_engine *eng, int on);
-/* Copies the named layer-0 dump (token-major [b][dim]); returns elements via n_out. */
+/* Copies the named layer-0 dump (token-major [b][dim]); returns elements via n_out.
+ * Names "decode.q", "decode.k", "decode.v", "decode.att", "decode.x_o" (the
+ * residual after o), "decode.h" (the SwiGLU output) and "decode.x" (after
+ * down) give the persistent decode kernel's last layer of its latest launch
+ * instead (no set_debug needed; parity bisection of the decode step). */
 int pk_get_dump(pk_engine *eng, const char *name, float *out, int cap, int *n_out);
 
 void pk_request_stop(void);

@@ -151,6 +151,11 @@ extern "C" {
 
 const char *pk_last_error(void) { return t_err.c_str(); }
 int pk_version(void) { return 100; }
+int pk_device_binary_version(int *out) {
+  if (!out) return set_error(PK_ERR_INVALID, "null out");
+  CK(kernels_binary_version(out));
+  return PK_OK;
+}
 int pk_supports(uint32_t ttype) { return type_is_matvec((int)ttype) ? 1 : 0; }
 
 int pk_q8_quantize(const float *x, int k, int b, pk_q8act *act, void *stream) {
@@ -254,6 +259,8 @@ int pk_backend_new(int device, pk_backend **out) {
     delete be;
     return cuda_error(e, "pk_backend_new");
   }
+  void *scratch = nullptr;  // reserve pk_matmul_noalloc's scratch on this device now (see pk.h)
+  if (noalloc_scratch(&scratch) != cudaSuccess) cudaGetLastError();
   *out = be;
   return PK_OK;
 }
@@ -412,6 +419,11 @@ int pk_generate(pk_engine *e, const uint32_t *prompt, int n, const pk_gen_opts *
 int pk_decode_steps_device(pk_engine *e, int n_steps, uint32_t *out_ids, float *device_ms) {
   if (!e) return set_error(PK_ERR_INVALID, "null engine");
   return e->eng.decode_steps_device(n_steps, out_ids, device_ms);
+}
+
+int pk_set_order(pk_engine *e, int order) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.set_order(order);
 }
 
 int pk_set_position(pk_engine *e, int pos) {

@@ -49,8 +49,14 @@
 namespace pk {
 namespace {
 
-constexpr int CONS = DK_THREADS - 32;                        // consumer threads (warps 1..11)
-constexpr int TERM_T = DK_THREADS - 32 - 32 * DK_CHAINS;     // term threads (warps 3..11)
+constexpr int CONS = DK_THREADS - 32;  // consumer threads (warps 1..)
+// Warp roles: warp 0 the producer, warps 1 .. DK_CHAINS the chain warps, the
+// rest term warps.
+__host__ __device__ constexpr int chain_of_warp(int w) { return (w >= 1 && w <= DK_CHAINS) ? w - 1 : -1; }
+__host__ __device__ constexpr bool term_warp(int w) { return w > DK_CHAINS; }
+__host__ __device__ constexpr int term_rank(int w) { return w - 1 - DK_CHAINS; }  // among the term warps
+constexpr int TERM_T = DK_THREADS - 32 - 32 * DK_CHAINS;  // term threads
+
 // Named barriers: all consumers; per (term buffer, chain warp) "terms ready"
 // and "buffer free" pairs (a barrier id is only ever shared by the term warps
 // and ONE chain warp, so generations cannot mix); the value-chain warps.
@@ -131,6 +137,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                "l"(src), "r"(bytes), "r"(saddr(b))
                : "memory");
 }
+// Tiled 2-D tensor copy global -> this CTA's shared memory (no multicast):
+// the box of tensor map `map` at element coordinates (x, y), completion
+// counted on mbarrier b.  x * element size is a multiple of 16 bytes at
+// every call site, dst is box-size aligned.
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *b) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(saddr(b))
+      : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -146,6 +163,11 @@ __device__ __forceinline__ unsigned long long ld_ll(const unsigned long long *p)
   unsigned long long w;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
+}
+// Two consecutive tagged words in one 16-byte load (p 16-byte aligned); each
+// word is still read single-copy atomically.
+__device__ __forceinline__ void ld_ll2(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ bool ll_ok(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 __device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
@@ -163,6 +185,7 @@ struct Layout {
   int kmax, uf;
 };
 constexpr int DK_XO = 256;   // owned rows of x kept in shared memory
+constexpr int CONS_T = DK_THREADS - 32;  // consumer threads
 constexpr int DK_CWW = 64;   // words of chain-warp bits (chunks per CTA < 32 * DK_CWW - 31)
 
 __host__ __device__ inline size_t up16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -174,7 +197,7 @@ __host__ __device__ inline Layout dk_layout(int n_embd, int n_ff, int qdim, int 
   L.kmax = (km + 15) / 16 * 16;
   int uf = DK_NB * DK_TS;
   uf = uf > km ? uf : km;
-  uf = uf > n_ctx ? uf : n_ctx;
+  uf = uf > n_ctx + 4 + CONS_T ? uf : n_ctx + 4 + CONS_T;  // scores, then the fast order's value partials
   L.uf = (uf + 3) / 4 * 4;
   size_t o = 0;
   L.ring = o; o += (size_t)DK_NS * DK_SLOT;
@@ -297,18 +320,24 @@ __device__ __forceinline__ void q8_lanes(const float (&v)[32 / L], bool store, i
     }
     w[j] = word;
   }
-  static_assert(L == 1 || L == 4, "4 or 1 lanes per block");
+  static_assert(L == 1 || L == 2 || L == 4, "4, 2 or 1 lanes per block");
   int h0 = sh[0], h1 = sh[1];
   if (L == 4) {  // lanes 0-1 hold the first half, lanes 2-3 the second
     const int pair = sh[0] + __shfl_xor_sync(0xffffffffu, sh[0], 1);
     const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
     h0 = (l & 2) ? other : pair;
     h1 = (l & 2) ? pair : other;
+  } else if (L == 2) {  // lane 0 holds the first half, lane 1 the second
+    const int other = __shfl_xor_sync(0xffffffffu, sh[0], 1);
+    h0 = (l & 1) ? other : sh[0];
+    h1 = (l & 1) ? sh[0] : other;
   }
   if (store) {
     if constexpr (E == 32) {
       sst_v4(q_sa, w[0], w[1], w[2], w[3]);
       sst_v4(q_sa + 16, w[4], w[5], w[6], w[7]);
+    } else if constexpr (E == 16) {
+      sst_v4(q_sa, w[0], w[1], w[2], w[3]);
     } else {
       sst_v2(q_sa, w[0], w[1]);
     }
@@ -589,6 +618,191 @@ __device__ __forceinline__ void item_q40(uint32_t w_a, uint32_t d_a, int blk, co
   sst_f(t_a, fmul(fmul(d, da), fsub((float)(pa + pb), fmul(8.0f, sa))));
 }
 
+// ---------------------------------------------------------- fast-order items
+// The fast order keeps every integer dot and the Q8 activation bit-exact and
+// regroups only the float arithmetic of a row: each item returns one partial
+// sum (its terms regrouped algebraically, with fused multiply-adds), and the
+// chain adds a row's partials in k order.  Products of exact integers below
+// 2^24 (scale x dot, min x block sum) are formed in integer or exact float
+// arithmetic first.  The result differs from the reference's sequential
+// float chain by rounding only (well inside 1e-3 relative per matvec).
+
+// Q4_K superblock: d * sum_j da_j (sc_j dot_j) - dmin * sum_j da_j (m_j sa_j).
+__device__ __forceinline__ void item_q4k_f(uint32_t w_a, int blk, const DAct &A, uint32_t t_a) {
+  const uint32_t xq = A.q + (uint32_t)blk * 256u, xf = (uint32_t)blk * 32u;
+  const uint4 hdr = sld_v4(w_a);
+  uint4 w[8];
+  int4 x[16];
+  float da[8], sa[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) w[i] = sld_v4(w_a + 16 + 16 * i);
+#pragma unroll
+  for (int i = 0; i < 16; i++) x[i] = sld_v4i(xq + 16u * i);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    da[j] = sld_f(A.d + xf + 4u * j);
+    sa[j] = sld_f(A.s + xf + 4u * j);
+  }
+  const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
+  const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
+  const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+  const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+  const uint32_t M = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+  float a1 = 0.0f, a2 = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    const uint4 w0 = w[2 * p], w1 = w[2 * p + 1];
+    const int4 x0 = x[4 * p], x1 = x[4 * p + 1], x2 = x[4 * p + 2], x3 = x[4 * p + 3];
+    int d0a = 0, d0b = 0, d1a = 0, d1b = 0;
+    d0a = __dp4a((int)(w0.x & M), x0.x, d0a); d0b = __dp4a((int)(w0.y & M), x0.y, d0b);
+    d0a = __dp4a((int)(w0.z & M), x0.z, d0a); d0b = __dp4a((int)(w0.w & M), x0.w, d0b);
+    d0a = __dp4a((int)(w1.x & M), x1.x, d0a); d0b = __dp4a((int)(w1.y & M), x1.y, d0b);
+    d0a = __dp4a((int)(w1.z & M), x1.z, d0a); d0b = __dp4a((int)(w1.w & M), x1.w, d0b);
+    d1a = dp4a_us(w0.x & H, x2.x, d1a); d1b = dp4a_us(w0.y & H, x2.y, d1b);
+    d1a = dp4a_us(w0.z & H, x2.z, d1a); d1b = dp4a_us(w0.w & H, x2.w, d1b);
+    d1a = dp4a_us(w1.x & H, x3.x, d1a); d1b = dp4a_us(w1.y & H, x3.y, d1b);
+    d1a = dp4a_us(w1.z & H, x3.z, d1a); d1b = dp4a_us(w1.w & H, x3.w, d1b);
+    const int dot0 = d0a + d0b, dot1 = (d1a + d1b) >> 4;
+    const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
+    const int sh = (2 * p & 3) * 8;
+    const int sc0 = (int)((scw >> sh) & 0xFFu), sc1 = (int)((scw >> (sh + 8)) & 0xFFu);
+    const float m0 = (float)((mw >> sh) & 0xFFu), m1 = (float)((mw >> (sh + 8)) & 0xFFu);
+    a1 = __fmaf_rn(da[2 * p], (float)(sc0 * dot0), a1);  // |sc dot| <= 63 * 60960 < 2^24: exact
+    a2 = __fmaf_rn(da[2 * p], m0 * sa[2 * p], a2);      // |m sa| <= 63 * 4064: exact
+    a1 = __fmaf_rn(da[2 * p + 1], (float)(sc1 * dot1), a1);
+    a2 = __fmaf_rn(da[2 * p + 1], m1 * sa[2 * p + 1], a2);
+  }
+  sst_f(t_a, __fmaf_rn(d, a1, -(dmin * a2)));
+}
+
+// Q6_K half superblock: d * sum_s da_s (sum_g scale_gs dot_gs).
+__device__ __forceinline__ void item_q6k_f(uint32_t w_a, uint32_t d_a, int blk, int h, const DAct &A, uint32_t t_a) {
+  const uint2 scw = sld_v2(w_a + 192 + 8 * h);
+  const uint16_t dbits = sld_u16(d_a);
+  uint4 qa[2], qb[2], qh[2];
+  int4 x[8];
+  float da[4];
+  int s16[8];
+#pragma unroll
+  for (int g = 0; g < 2; g++) {
+    qa[g] = sld_v4(w_a + h * 64 + g * 16);
+    qb[g] = sld_v4(w_a + h * 64 + 32 + g * 16);
+    qh[g] = sld_v4(w_a + 128 + h * 32 + g * 16);
+  }
+#pragma unroll
+  for (int s = 0; s < 4; s++) {
+    const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);
+    x[2 * s] = sld_v4i(A.q + ab * 32u);
+    x[2 * s + 1] = sld_v4i(A.q + ab * 32u + 16u);
+    da[s] = sld_f(A.d + ab * 4u);
+    const uint2 hs = sld_v2(A.s16 + ab * 8u);
+    s16[2 * s] = (int)hs.x;
+    s16[2 * s + 1] = (int)hs.y;
+  }
+  const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
+  float acc = 0.0f;
+#pragma unroll
+  for (int s = 0; s < 4; s++) {
+    int is = 0;  // |sum over g of scale * dot| <= 2 * 128 * 65024 < 2^24: exact as a float
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+      const int4 xs = x[2 * s + g];
+      int pa = 0, pb = 0;
+#pragma unroll
+      for (int w = 0; w < 4; w++) {
+        const uint32_t lo = word_of(s & 1 ? qb[g] : qa[g], w), hh = word_of(qh[g], w);
+        const uint32_t q = ((s & 2 ? lo >> 4 : lo) & 0x0F0F0F0Fu) | ((s == 0 ? hh << 4 : s == 1 ? hh << 2 : s == 2 ? hh : hh >> 2) & 0x30303030u);
+        const int xw = w == 0 ? xs.x : w == 1 ? xs.y : w == 2 ? xs.z : xs.w;
+        if (w & 1) pb = __dp4a((int)q, xw, pb);
+        else pa = __dp4a((int)q, xw, pa);
+      }
+      is += (int)(int8_t)(uint8_t)(sw >> (8 * (g + 2 * s))) * (pa + pb - 32 * s16[2 * s + g]);
+    }
+    acc = __fmaf_rn(da[s], (float)is, acc);
+  }
+  sst_f(t_a, f16f(dbits) * acc);
+}
+
+// Q8_0 / Q4_0: FQ consecutive blocks (n <= FQ of them live) of one row.
+constexpr int FQ = 4;
+__device__ __forceinline__ void item_q80_f(uint32_t w_a, uint32_t d_a, int blk, int n, const DAct &A, uint32_t t_a) {
+  uint4 w[2 * FQ];
+  int4 x[2 * FQ];
+  float da[FQ];
+  uint16_t db[FQ];
+#pragma unroll
+  for (int b = 0; b < FQ; b++) {
+    const int bb = b < n ? b : 0;  // dead slots re-read block 0 (in range) and add nothing
+    w[2 * b] = sld_v4(w_a + 32u * bb);
+    w[2 * b + 1] = sld_v4(w_a + 32u * bb + 16u);
+    const uint32_t xa = A.q + (uint32_t)(blk + bb) * 32u;
+    x[2 * b] = sld_v4i(xa);
+    x[2 * b + 1] = sld_v4i(xa + 16);
+    db[b] = sld_u16(d_a + 2u * bb);
+    da[b] = sld_f(A.d + (uint32_t)(blk + bb) * 4u);
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int b = 0; b < FQ; b++) {
+    const uint4 w0 = w[2 * b], w1 = w[2 * b + 1];
+    const int4 x0 = x[2 * b], x1 = x[2 * b + 1];
+    int pa = 0, pb = 0;
+    pa = __dp4a((int)w0.x, x0.x, pa); pb = __dp4a((int)w0.y, x0.y, pb);
+    pa = __dp4a((int)w0.z, x0.z, pa); pb = __dp4a((int)w0.w, x0.w, pb);
+    pa = __dp4a((int)w1.x, x1.x, pa); pb = __dp4a((int)w1.y, x1.y, pb);
+    pa = __dp4a((int)w1.z, x1.z, pa); pb = __dp4a((int)w1.w, x1.w, pb);
+    if (b < n) acc = __fmaf_rn(f16f(db[b]) * da[b], (float)(pa + pb), acc);
+  }
+  sst_f(t_a, acc);
+}
+__device__ __forceinline__ void item_q40_f(uint32_t w_a, uint32_t d_a, int blk, int n, const DAct &A, uint32_t t_a) {
+  uint4 w[FQ];
+  int4 x[2 * FQ];
+  float da[FQ], sa[FQ];
+  uint16_t db[FQ];
+#pragma unroll
+  for (int b = 0; b < FQ; b++) {
+    const int bb = b < n ? b : 0;
+    w[b] = sld_v4(w_a + 16u * bb);
+    const uint32_t xa = A.q + (uint32_t)(blk + bb) * 32u;
+    x[2 * b] = sld_v4i(xa);
+    x[2 * b + 1] = sld_v4i(xa + 16);
+    db[b] = sld_u16(d_a + 2u * bb);
+    da[b] = sld_f(A.d + (uint32_t)(blk + bb) * 4u);
+    sa[b] = sld_f(A.s + (uint32_t)(blk + bb) * 4u);
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int b = 0; b < FQ; b++) {
+    const uint4 wv = w[b];
+    const int4 x0 = x[2 * b], x1 = x[2 * b + 1];
+    int pa = 0, pb = 0;
+    pa = __dp4a(lo4(wv.x), x0.x, pa); pb = __dp4a(lo4(wv.y), x0.y, pb);
+    pa = __dp4a(lo4(wv.z), x0.z, pa); pb = __dp4a(lo4(wv.w), x0.w, pb);
+    pa = __dp4a(hi4(wv.x), x1.x, pa); pb = __dp4a(hi4(wv.y), x1.y, pb);
+    pa = __dp4a(hi4(wv.z), x1.z, pa); pb = __dp4a(hi4(wv.w), x1.w, pb);
+    // dot - 8 sa is an exact integer (sa is an exact float)
+    if (b < n) acc = __fmaf_rn(f16f(db[b]) * da[b], (float)(pa + pb - 8 * (int)sa[b]), acc);
+  }
+  sst_f(t_a, acc);
+}
+
+// Partial sums per row of a chunk in the fast order: one per item.
+__host__ __device__ inline int dk_items_fast(int type, int nblk) {
+  return type == T_Q4_K ? nblk : type == T_Q6_K ? 2 * nblk : (nblk + FQ - 1) / FQ;
+}
+// Term-buffer floats between rows for n partials (as term_pitch: a multiple
+// of 8 rounded up, then an odd multiple of 4).
+__host__ __device__ inline int dk_pitch(int n) { return 4 * (((n + 7) / 8) * 2 + 1); }
+
+// History positions [r0, r1) of 0..pos-1 that attention unit j of J scores:
+// near-equal contiguous shares starting on multiples of 4 (the K copies move
+// whole groups of 4 positions).
+__host__ __device__ inline void att_range(int pos, int j, int J, int &r0, int &r1) {
+  r0 = j == 0 ? 0 : (int)(((long)pos * j / J) & ~3L);
+  r1 = j == J - 1 ? pos : (int)(((long)pos * (j + 1) / J) & ~3L);
+}
+
 // A chunk descriptor copied from shared memory into registers.
 __device__ __forceinline__ DChunk load_desc(uint32_t a) {
   DChunk c;
@@ -684,14 +898,18 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
       }
       rg.next();
     }
-    if ((p & 3) == 0 && p < 4 * a.n_layer && ok) {  // attention of layer p/4: K then V history of each owned head
+    if ((p & 3) == 0 && p < 4 * a.n_layer && ok) {  // attention of layer p/4: K then V history of each owned unit
       const int L = p >> 2;
-      for (int h = blockIdx.x; h < a.n_head && ok; h += gridDim.x) {
+      for (int u = blockIdx.x; u < a.n_head * a.att_j && ok; u += gridDim.x) {
+        const int h = u / a.att_j, j = u - h * a.att_j;
         const size_t base = ((size_t)L * a.n_kv + h / group) * a.n_ctx * a.dh;
-        // K (d-major): one run of positions per dimension, rounded up to a
-        // multiple of 4 positions (the slot's extra entries are not read).
-        for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
-          const int n4 = (min(ppc, pos - p0) + 3) & ~3;
+        int r0, r1;
+        att_range(pos, j, a.att_j, r0, r1);
+        // K (d-major) of the unit's share [r0, r1): one run of positions per
+        // dimension, rounded up to a multiple of 4 positions (the slot's extra
+        // entries are not read; r0 is a multiple of 4 and n_ctx too).
+        for (int p0 = r0; p0 < r1 && ok; p0 += ppc) {
+          const int n4 = (min(ppc, r1 - p0) + 3) & ~3;
           if (!claim((uint32_t)(a.dh * n4 * 4), nullptr)) break;
           uint8_t *dst = S.ring + (size_t)rg.slot * DK_SLOT;
           for (int d = lane; d < a.dh; d += 32)
@@ -699,11 +917,18 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
                      &S.full[rg.slot]);
           rg.next();
         }
-        // V (position-major): one contiguous run
-        for (int p0 = 0; p0 < pos && ok; p0 += ppc) {
-          const uint32_t bytes = (uint32_t)min(ppc, pos - p0) * a.dh * 4;
-          if (!claim(bytes, nullptr)) break;
-          if (lane == 0) bulk_g2s(S.ring + (size_t)rg.slot * DK_SLOT, a.vcache + base + (size_t)p0 * a.dh, bytes, &S.full[rg.slot]);
+        // V (position-major): this unit's att_ds dimensions of every
+        // position, tensor-map boxes of DK_VB positions laid end to end, so
+        // the slot holds [position][att_ds].  A box that runs past the cache
+        // is zero-filled and still counts its full size.
+        const int ds = a.att_ds, ppv = DK_SLOT / (ds * 4), row0 = (L * a.n_kv + h / group) * a.n_ctx;
+        const uint32_t box = (uint32_t)(DK_VB * ds * 4);
+        for (int p0 = 0; p0 < pos && ok; p0 += ppv) {
+          const int nb = (min(ppv, pos - p0) + DK_VB - 1) / DK_VB;
+          if (!claim((uint32_t)nb * box, nullptr)) break;
+          uint8_t *dst = S.ring + (size_t)rg.slot * DK_SLOT;
+          for (int b = lane; b < nb; b += 32)
+            tma_2d(dst + (size_t)b * box, &a.vmap, j * ds, row0 + p0 + b * DK_VB, &S.full[rg.slot]);
           rg.next();
         }
       }
@@ -718,7 +943,9 @@ __device__ void producer(const DecodeArgs &a, const Smem &S, int pos, const DChu
 }
 
 // ------------------------------------------------------------------ consumers
-template <bool TRACE>
+// FAST: the fast float order (see the fast-order items); otherwise every
+// float operation follows the reference's order.
+template <bool TRACE, bool FAST>
 struct Cons {
   const DecodeArgs &a;
   const Smem &S;
@@ -854,31 +1081,39 @@ struct Cons {
   // not yet `tag` (their writer has not finished), then stores the values.
   // True (on every consumer) when a wait ran out and the kernel stops.
   __device__ bool stage_ll(const unsigned long long *src, int k, uint32_t tag) {
-    constexpr int NW = 8;  // words in flight per thread
+    constexpr int NP = 8;  // word pairs (16-byte loads) in flight per thread
     const unsigned long long t0 = gtime();
     unsigned it = 0;
-    for (int base = 0; base < k; base += NW * CONS) {  // the same trip count on every consumer thread
-      unsigned long long w[NW];
+    const int np = k >> 1;  // k is even; src is 16-byte aligned
+    for (int base = 0; base < np; base += NP * CONS) {  // the same trip count on every consumer thread
+      unsigned long long w[2 * NP];
 #pragma unroll
-      for (int j = 0; j < NW; j++) {
+      for (int j = 0; j < NP; j++) {
         const int i = base + ctid + j * CONS;
-        w[j] = i < k ? ld_ll(src + i) : ((unsigned long long)tag << 32);
+        if (i < np) {
+          ld_ll2(src + 2 * i, w[2 * j], w[2 * j + 1]);
+        } else {
+          w[2 * j] = w[2 * j + 1] = (unsigned long long)tag << 32;
+        }
       }
       for (;;) {
         bool all = true;
 #pragma unroll
-        for (int j = 0; j < NW; j++) all = all && ll_ok(w[j], tag);
+        for (int j = 0; j < 2 * NP; j++) all = all && ll_ok(w[j], tag);
         if (all || !poll_ok(t0, ++it)) break;
 #pragma unroll
-        for (int j = 0; j < NW; j++) {
+        for (int j = 0; j < NP; j++) {
           const int i = base + ctid + j * CONS;
-          if (!ll_ok(w[j], tag)) w[j] = ld_ll(src + i);
+          if (!ll_ok(w[2 * j], tag) || !ll_ok(w[2 * j + 1], tag)) ld_ll2(src + 2 * i, w[2 * j], w[2 * j + 1]);
         }
       }
 #pragma unroll
-      for (int j = 0; j < NW; j++) {
+      for (int j = 0; j < NP; j++) {
         const int i = base + ctid + j * CONS;
-        if (i < k) S.u[i] = ll_val(w[j]);
+        if (i < np) {
+          S.u[2 * i] = ll_val(w[2 * j]);
+          S.u[2 * i + 1] = ll_val(w[2 * j + 1]);
+        }
       }
     }
     const bool stop = bar_or(NB_CONS, CONS, S.flag[0] != 0);
@@ -931,11 +1166,13 @@ struct Cons {
     bar_sync(NB_CONS, CONS);
   }
   // One round where the consumers allow: four lanes per block when every
-  // block fits, else one.
+  // block fits, else two, else one.
   __device__ void quant(const float *src, int k, bool norm, float scale, bool from_g) {
     if ((k >> 5) * 4 <= CONS) {
       if (from_g) quant_l<4, true>(src, k, norm, scale);
       else quant_l<4, false>(src, k, norm, scale);
+    } else if ((k >> 5) * 2 <= CONS && !from_g) {
+      quant_l<2, false>(src, k, norm, scale);
     } else {
       if (from_g) quant_l<1, true>(src, k, norm, scale);
       else quant_l<1, false>(src, k, norm, scale);
@@ -947,6 +1184,22 @@ struct Cons {
   __device__ void norm_q8(int k) {
     asm volatile("cp.async.wait_all;" ::: "memory");
     float *xv = S.u;
+    if (FAST) {  // sum of squares: per-thread partials, warp trees, then the warps' sums in order
+      float sq = 0.0f;
+      for (int i = ctid; i < k; i += CONS) sq = __fmaf_rn(xv[i], xv[i], sq);
+      sq = warp_sum_f(sq);
+      if (lane == 0) S.red[cwarp] = sq;
+      bar_sync(NB_CONS, CONS);
+      if (ctid == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < CONS / 32; w++) s += S.red[w];
+        S.red[32] = 1.0f / sqrtf(s / (float)k + a.eps);
+      }
+      bar_sync(NB_CONS, CONS);
+      fine(1);
+      quant(nullptr, k, true, S.red[32], false);
+      return;
+    }
     const int n8 = k / 8 * 8;
     if (ctid < 8) S.red[ctid] = chain_sq(0.0f, u_a + 4 * ctid, 32u, n8 / 8);
     bar_sync(NB_CONS, CONS);
@@ -968,16 +1221,21 @@ struct Cons {
   // 16 bytes: conflict-free 16-byte loads).
   template <int T>
   __device__ void terms(const DChunk &c, uint32_t sl, uint32_t Tb, int gt, int ng) {  // thread gt of a group of ng
-    // terms per item; Q6_K items are half superblocks (j = 2 superblock + half)
-    constexpr int TPI = T == T_Q4_K ? 8 : (T == T_Q6_K ? 8 : 1), IPB = T == T_Q6_K ? 2 : 1;
+    // items per row: exact order, one per block or superblock (Q6_K: half
+    // superblocks, j = 2 superblock + half), TPI terms each; fast order, one
+    // partial per superblock (Q6_K: half), or per FQ blocks (Q8_0, Q4_0)
+    constexpr int TPI = FAST ? 1 : (T == T_Q4_K ? 8 : (T == T_Q6_K ? 8 : 1));
+    constexpr int IPB = T == T_Q6_K ? 2 : 1;
+    constexpr int BPI = (FAST && (T == T_Q8_0 || T == T_Q4_0)) ? FQ : 1;  // blocks per item
     constexpr int QB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 208 : (T == T_Q8_0 ? 32 : 16));
-    const int R = c.rows, items = R * (c.b1 - c.b0) * IPB, rs = c.rs;
+    const int R = c.rows, nblk = c.b1 - c.b0, ipr = FAST ? dk_items_fast(T, nblk) : nblk * IPB, items = R * ipr;
+    const int rs = FAST ? dk_pitch(ipr) : c.rs;
     const uint32_t pitch = c.full ? c.q_stride : c.q_len + 16u * c.qpad;
     const uintptr_t d0 = (uintptr_t)c.d;
     const int dr = ng % R, dj = ng / R;
     int t = gt, r = t % R, j = t / R;
     for (; t < items; t += ng) {
-      const int jb = j / IPB;  // block or superblock within the staged row
+      const int jb = BPI > 1 ? j * BPI : j / IPB;  // first block or superblock of the item within the staged row
       const uint32_t w_a = sl + (uint32_t)r * pitch + (uint32_t)(jb * QB);
       const uint32_t t_a = Tb + 4u * (uint32_t)(r * rs + j * TPI);  // [row][term], rs: the row pitch
       uint32_t d_a = 0u;
@@ -986,10 +1244,17 @@ struct Cons {
               (uint32_t)(c.full ? (d0 & 15) + (size_t)r * c.d_stride
                                 : (size_t)r * c.d_len + ((d0 + (size_t)r * c.d_stride) & 15));
       const int blk = c.b0 + jb;
-      if (T == T_Q4_K) item_q4k(w_a, blk, act_a, t_a);
-      else if (T == T_Q6_K) item_q6k(w_a, d_a, blk, j & 1, act_a, t_a);
-      else if (T == T_Q8_0) item_q80(w_a, d_a, blk, act_a, t_a);
-      else item_q40(w_a, d_a, blk, act_a, t_a);
+      if (FAST) {
+        if (T == T_Q4_K) item_q4k_f(w_a, blk, act_a, t_a);
+        else if (T == T_Q6_K) item_q6k_f(w_a, d_a, blk, j & 1, act_a, t_a);
+        else if (T == T_Q8_0) item_q80_f(w_a, d_a, blk, min(BPI, nblk - jb), act_a, t_a);
+        else item_q40_f(w_a, d_a, blk, min(BPI, nblk - jb), act_a, t_a);
+      } else {
+        if (T == T_Q4_K) item_q4k(w_a, blk, act_a, t_a);
+        else if (T == T_Q6_K) item_q6k(w_a, d_a, blk, j & 1, act_a, t_a);
+        else if (T == T_Q8_0) item_q80(w_a, d_a, blk, act_a, t_a);
+        else item_q40(w_a, d_a, blk, act_a, t_a);
+      }
       r += dr;
       j += dj;
       if (r >= R) {
@@ -1086,13 +1351,14 @@ struct Cons {
   // it writes), and each use has exactly the chunk's group and its chain warp,
   // nb_pair(mv) threads.
   __device__ void run_mv(int p) {
-    const bool chain = cwarp < DK_CHAINS;
-    const int ti = tid - 32 - 32 * DK_CHAINS;           // term thread index
+    const int wid = tid >> 5, cw = chain_of_warp(wid);
+    const bool chain = cw >= 0, term = term_warp(wid);
+    const int ti = term ? 32 * term_rank(wid) + lane : 0;  // term thread index
     const int grp = ti < TG0 ? 0 : 1, gt = grp ? ti - TG0 : ti;
     for (int ci = ph[p]; ci < ph[p + 1]; ci++) {
       const int buf = mv % DK_NB;
       const uint32_t Tb = u_a + 4u * (uint32_t)(buf * DK_TS);
-      if (!chain && (mv & 1) == grp) {
+      if (term && (mv & 1) == grp) {
         const bool tp = (TRACE && a.trace) && ctid == 32 * DK_CHAINS;
         long long c0 = tp ? clock64() : 0;
         if (mv >= DK_NB) bar_sync(NB_EMPTYT + buf * DK_CHAINS + owner(ci - DK_NB), nb_pair(mv));
@@ -1114,9 +1380,9 @@ struct Cons {
         // Ownership comes from the plan's bit list (the descriptor may only be
         // read by the owner, before it hands the slot back).
         const bool tp = (TRACE && a.trace) && ctid == 0;
-        if (owner(ci) == cwarp) {
+        if (owner(ci) == cw) {
           long long c0 = tp ? clock64() : 0;
-          bar_sync(NB_FULLT + buf * DK_CHAINS + cwarp, nb_pair(mv));
+          bar_sync(NB_FULLT + buf * DK_CHAINS + cw, nb_pair(mv));
           if (ci == ph[p]) fine(3);  // first chunk's terms are in
           if (tp) {
             const long long c1 = clock64();
@@ -1130,15 +1396,20 @@ struct Cons {
           c.role = d0.role;
           c.layer = d0.layer;
           c.flags = d0.flags;
-          c.nt = (d0.b1 - d0.b0) * dk_gpb(d0.type) * dk_tpg(d0.type);
-          c.rs = d0.rs;
+          if (FAST) {
+            c.nt = dk_items_fast(d0.type, d0.b1 - d0.b0);
+            c.rs = dk_pitch(c.nt);
+          } else {
+            c.nt = (d0.b1 - d0.b0) * dk_gpb(d0.type) * dk_tpg(d0.type);
+            c.rs = d0.rs;
+          }
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
           if (c.flags & DF_FIRST) acc = 0.0f;
           if (lane < c.rows) acc = chain_add_v(acc, Tb + 16u * (uint32_t)(lane * (c.rs >> 2)), c.nt);
           __syncwarp();
           // the term buffer is free again, for chunk mv + DK_NB and its group
-          if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cwarp, nb_pair(mv + DK_NB));
+          if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cw, nb_pair(mv + DK_NB));
           if (c.flags & DF_LAST) epilogue(c);
           if (tp) pacc(5, clock64() - c0);
           if (ci == ph[p]) fine(4);  // first chunk chained
@@ -1149,26 +1420,71 @@ struct Cons {
     }
   }
 
-  // Exact single-token attention for the heads this CTA owns (model.rs:993-1087).
+  // The fast order's softmax sum and weighted values for unit (h, d0): the
+  // weights e_p = exp(s_p - M) are in sc[0..pos]; consumer thread (g, d) adds
+  // positions p = g (mod G) of dimension d, and the G partials of each
+  // dimension and the sum's warp partials are added in a fixed order.
+  __device__ void attention_fast(int u, int h, int d0, int pos, int L) {
+    const int ds = a.att_ds, ppv = DK_SLOT / (ds * 4), G = CONS / ds;
+    const int g = ctid / ds, d = ctid - g * ds;
+    const float *sc = S.u;
+    float es = 0.0f;
+    for (int p = ctid; p <= pos; p += CONS) es += sc[p];
+    es = warp_sum_f(es);
+    if (lane == 0) S.red[cwarp] = es;
+    float vacc = 0.0f;
+    for (int p0 = 0; p0 < pos; p0 += ppv) {
+      const int n = min(ppv, pos - p0);
+      wait_full();
+      const float *vc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
+      if (g < G)
+        for (int p = g; p < n; p += G) vacc = __fmaf_rn(sc[p0 + p], vc[p * ds + d], vacc);
+      bar_sync(NB_CONS, CONS);
+      if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
+      rg.next();
+    }
+    if (g == 0) vacc = __fmaf_rn(sc[pos], S.qh[512 + d0 + d], vacc);  // this position's v
+    float *part = S.u + ((pos + 4) & ~3);  // past the weights
+    if (g < G) part[g * ds + d] = vacc;
+    bar_sync(NB_CONS, CONS);
+    if (ctid < ds) {
+      float v = 0.0f;
+      for (int i = 0; i < G; i++) v += part[i * ds + ctid];
+      float sum = 0.0f;
+      for (int w = 0; w < CONS / 32; w++) sum += S.red[w];
+      st_ll(a.att_ll + (size_t)h * a.dh + d0 + ctid, sum > 0.0f ? v / sum : 0.0f, tag_of(5 * L + 1));
+    }
+    bar_sync(NB_CONS, CONS);
+  }
+
+  // Exact single-token attention (model.rs:993-1087) for the units this CTA
+  // owns: unit (h, j) scores every position of head h (the same values on
+  // each of the head's att_j units) and runs the value chains of dimensions
+  // [j ds, (j + 1) ds).
   __device__ void attention(int L) {
-    const int dh = a.dh, group = a.n_head / a.n_kv, ppc = DK_SLOT / (dh * 4);
+    const int dh = a.dh, group = a.n_head / a.n_kv, ppc = DK_SLOT / (dh * 4), ds = a.att_ds, ppv = DK_SLOT / (ds * 4);
+    const int J = a.att_j;
     float *sc = S.u;
-    const int nvw = (dh + 31) / 32;  // value-chain warps
-    for (int h = blockIdx.x; h < a.n_head; h += gridDim.x) {
+    for (int u = blockIdx.x; u < a.n_head * J; u += gridDim.x) {
+      const int h = u / J, j = u - h * J, d0 = j * ds;
       const int kh = h / group;
+      int r0, r1;  // the history positions this unit scores
+      att_range(pos, j, J, r0, r1);
       float *kcur = S.qh + 256, *vcur = S.qh + 512;
+      const uint32_t tag = tag_of(5 * L + 1);
+      unsigned long long *scg = a.sc_ll + (size_t)h * a.n_ctx;
       {  // q and this position's k, v: tagged words of the qkv phase
-        const uint32_t tag = tag_of(5 * L);
+        const uint32_t tq = tag_of(5 * L);
         const unsigned long long t0 = gtime();
         unsigned it = 0;
         for (int d = ctid; d < dh; d += CONS) {
           const unsigned long long *pq = a.q_ll + (size_t)h * dh + d, *pk = a.kv_ll + (size_t)kh * dh + d,
                                    *pv = a.kv_ll + (size_t)(a.n_kv + kh) * dh + d;
           unsigned long long wq = ld_ll(pq), wk = ld_ll(pk), wv = ld_ll(pv);
-          while (!(ll_ok(wq, tag) && ll_ok(wk, tag) && ll_ok(wv, tag)) && poll_ok(t0, ++it)) {
-            if (!ll_ok(wq, tag)) wq = ld_ll(pq);
-            if (!ll_ok(wk, tag)) wk = ld_ll(pk);
-            if (!ll_ok(wv, tag)) wv = ld_ll(pv);
+          while (!(ll_ok(wq, tq) && ll_ok(wk, tq) && ll_ok(wv, tq)) && poll_ok(t0, ++it)) {
+            if (!ll_ok(wq, tq)) wq = ld_ll(pq);
+            if (!ll_ok(wk, tq)) wk = ld_ll(pk);
+            if (!ll_ok(wv, tq)) wv = ld_ll(pv);
           }
           S.qh[d] = ll_val(wq);
           kcur[d] = ll_val(wk);
@@ -1176,7 +1492,7 @@ struct Cons {
         }
       }
       bar_sync(NB_CONS, CONS);
-      if (h == (int)blockIdx.x) fine(0);
+      if (u == (int)blockIdx.x) fine(0);
       float mx = -INFINITY;
       // s_p = f32_dot(q, k_p) * scale: eight unfused chains over d = 8t + l,
       // combined ((c0+c1)+(c2+c3)) + ((c4+c5)+(c6+c7)), then the tail.  One
@@ -1193,36 +1509,51 @@ struct Cons {
         for (int t = n8; t < dh; t++) r = fadd(r, fmul(sld_f(qh_a + 4u * t), sld_f(kp + (uint32_t)t * ks)));
         return fmul(r, a.scale);
       };
-      // K chunks are scored up to KG at a time (all consumer threads, one
-      // position each); chunk j of the group is the j-th next ring transfer.
+      // This unit's share of the history: K chunks of [r0, r1), up to KG at a
+      // time (one position per consumer thread); each score also goes to the
+      // head's score row in global memory for the head's other units.
       constexpr int KG = 3;
-      const int nk = (pos + ppc - 1) / ppc;
+      const int nk = (r1 - r0 + ppc - 1) / ppc;
       for (int k0 = 0; k0 < nk; k0 += KG) {
-        const int g = min(KG, nk - k0), np = min(g * ppc, pos - k0 * ppc);
-        for (int j = 0; j < g; j++) wait_full_at(j);
+        const int g = min(KG, nk - k0), np = min(g * ppc, r1 - r0 - k0 * ppc);
+        for (int jj = 0; jj < g; jj++) wait_full_at(jj);
         for (int pi = ctid; pi < np; pi += CONS) {
-          const int j = pi / ppc, pj = pi - j * ppc;
-          const uint32_t kc = ring_a + rg.slot_at(j) * (uint32_t)DK_SLOT;  // [dh][ppc] floats
+          const int jj = pi / ppc, pj = pi - jj * ppc;
+          const uint32_t kc = ring_a + rg.slot_at(jj) * (uint32_t)DK_SLOT;  // [dh][ppc] floats
           const float sv = score(kc + 4u * pj, 4u * ppc);
-          sc[k0 * ppc + pi] = sv;
+          const int p = r0 + k0 * ppc + pi;
+          sc[p] = sv;
+          if (J > 1) st_ll(scg + p, sv, tag);
           mx = sv > mx ? sv : mx;
         }
         bar_sync(NB_CONS, CONS);
         if (ctid == 0)
-          for (int j = 0; j < g; j++) mbar_arrive(&S.empty[rg.slot_at(j)]);
-        for (int j = 0; j < g; j++) rg.next();
-        if (h == (int)blockIdx.x && k0 == 0) fine(1);
-      }
-      if (h == (int)blockIdx.x) {
-        fine(2);
-        mark(5 * L + 1, 0);
+          for (int jj = 0; jj < g; jj++) mbar_arrive(&S.empty[rg.slot_at(jj)]);
+        for (int jj = 0; jj < g; jj++) rg.next();
+        if (u == (int)blockIdx.x && k0 == 0) fine(1);
       }
       if (ctid == 0) {  // the position written by this step's qkv phase
         const float sv = score(shaddr(kcur), 4u);
         sc[pos] = sv;
         mx = sv > mx ? sv : mx;
       }
-      const bool tp = TRACE && a.trace && h == (int)blockIdx.x;
+      if (J > 1) {  // the head's other units' scores (their tagged words)
+        const unsigned long long t0 = gtime();
+        unsigned it = 0;
+        for (int p = ctid; p < pos; p += CONS) {
+          if (p >= r0 && p < r1) continue;
+          unsigned long long w = ld_ll(scg + p);
+          while (!ll_ok(w, tag) && poll_ok(t0, ++it)) w = ld_ll(scg + p);
+          const float sv = ll_val(w);
+          sc[p] = sv;
+          mx = sv > mx ? sv : mx;
+        }
+      }
+      if (u == (int)blockIdx.x) {
+        fine(2);
+        mark(5 * L + 1, 0);
+      }
+      const bool tp = TRACE && a.trace && u == (int)blockIdx.x;
       long long c0 = (tp && ctid == 0) ? clock64() : 0;
       mx = warp_max(mx);
       if (lane == 0) S.red[cwarp] = mx;
@@ -1233,59 +1564,73 @@ struct Cons {
         S.red[32] = m;
       }
       bar_sync(NB_CONS, CONS);
-      if (h == (int)blockIdx.x) fine(3);
+      if (u == (int)blockIdx.x) fine(3);
       const float M = S.red[32];
       for (int p = ctid; p <= pos; p += CONS) sc[p] = expf_lib(fsub(sc[p], M));
       bar_sync(NB_CONS, CONS);
-      if (h == (int)blockIdx.x) fine(4);
+      if (u == (int)blockIdx.x) fine(4);
       if (tp && ctid == 0) {  // profile: max + exp
         const long long c1 = clock64();
         pacc(2, c1 - c0);
         c0 = c1;
       }
-      // Weighted values: one chain per d over p (zero weights skipped); the
-      // softmax sum is one more chain.
-      const bool vw = cwarp < nvw;
+      if (FAST) {
+        attention_fast(u, h, d0, pos, L);
+        continue;
+      }
+      // The softmax sum: one chain over e_0 .. e_pos on the last consumer
+      // warp, while the others form each V slot's products in place
+      // (e_p != 0 ? e_p * v_p[d] : -0.0, the reference's skipped term being
+      // an exact -0.0) and run one value chain per dimension over them.
+      constexpr int VT = CONS - 32;  // threads of the value work
       float vacc = 0.0f;
-      if (ctid == nvw * 32) {
-        const long long s0 = tp ? clock64() : 0;
-        const float sum = chain_add(0.0f, u_a, 4u, pos + 1);
-        S.red[33] = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
-        if (tp) pacc(4, clock64() - s0);  // profile: softmax sum chain
-      }
-      for (int p0 = 0; p0 < pos; p0 += ppc) {
-        const int n = min(ppc, pos - p0);
-        if (vw) {
-          wait_full();
-          const float *vc = reinterpret_cast<const float *>(S.ring + (size_t)rg.slot * DK_SLOT);
-          if (ctid < dh) vacc = chain_wv(vacc, u_a + 4u * p0, shaddr(vc) + 4u * ctid, 4u * dh, n);
-          bar_sync(NB_V, nvw * 32);
-          if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
+      if (ctid >= VT) {
+        if (ctid == VT) {
+          const long long s0 = tp ? clock64() : 0;
+          const float sum = chain_add(0.0f, u_a, 4u, pos + 1);
+          S.red[33] = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
+          if (tp) pacc(4, clock64() - s0);  // profile: softmax sum chain
         }
-        rg.next();
+        for (int p0 = 0; p0 < pos; p0 += ppv) rg.next();
+      } else {
+        const int sh = __ffs(ds) - 1;  // ds is a power of two
+        for (int p0 = 0; p0 < pos; p0 += ppv) {  // slots of [position][ds] (the unit's dimensions)
+          const int n = min(ppv, pos - p0);
+          wait_full();
+          float *vc = reinterpret_cast<float *>(S.ring + (size_t)rg.slot * DK_SLOT);
+          for (int i = ctid; i < (n << sh); i += VT) {
+            const float e = sc[p0 + (i >> sh)];
+            vc[i] = e != 0.0f ? fmul(e, vc[i]) : -0.0f;
+          }
+          bar_sync(NB_V, VT);
+          if (ctid < ds) vacc = chain_add(vacc, shaddr(vc) + 4u * ctid, 4u * ds, n);
+          bar_sync(NB_V, VT);
+          if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
+          rg.next();
+        }
+        if (ctid < ds) {
+          const float e = sc[pos];
+          if (e != 0.0f) vacc = fadd(vacc, fmul(e, vcur[d0 + ctid]));
+        }
       }
-      if (vw && ctid < dh) {
-        const float e = sc[pos];
-        const float v = vcur[ctid];
-        if (e != 0.0f) vacc = fadd(vacc, fmul(e, v));
-      }
-      if (h == (int)blockIdx.x) fine(5);
+      if (u == (int)blockIdx.x) fine(5);
       if (tp && ctid == 0) {  // profile: value chains
         const long long c1 = clock64();
         pacc(3, c1 - c0);
         c0 = c1;
       }
       bar_sync(NB_CONS, CONS);
-      if (vw && ctid < dh) st_ll(a.att_ll + (size_t)h * dh + ctid, fmul(vacc, S.red[33]), tag_of(5 * L + 1));
+      if (ctid < ds) st_ll(a.att_ll + (size_t)h * dh + d0 + ctid, fmul(vacc, S.red[33]), tag_of(5 * L + 1));
       bar_sync(NB_CONS, CONS);
       if (tp && ctid == 0) pacc(5, clock64() - c0);  // profile: output
     }
   }
 
   __device__ void finish() {
-    if (cwarp < DK_CHAINS && lane == 0) {  // each chain warp's first maximum over its row groups
-      S.red[40 + cwarp] = best_v;
-      reinterpret_cast<volatile int *>(S.red)[48 + cwarp] = best_i;
+    const int cw = chain_of_warp(tid >> 5);
+    if (cw >= 0 && lane == 0) {  // each chain warp's first maximum over its row groups
+      S.red[40 + cw] = best_v;
+      reinterpret_cast<volatile int *>(S.red)[48 + cw] = best_i;
     }
     bar_sync(NB_CONS, CONS);
     if (ctid == 0) {  // larger value wins; equal values: the lower row index (first maximum)
@@ -1369,7 +1714,7 @@ struct Cons {
   }
 };
 
-template <bool TRACE>
+template <bool TRACE, bool FAST>
 __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const Layout L = dk_layout(a.n_embd, a.n_ff, a.n_head * a.dh, a.n_ctx, a.n_layer);
@@ -1403,7 +1748,7 @@ __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant_
     producer<TRACE>(a, S, pos, ch, ph);
     return;
   }
-  Cons<TRACE> c(a, S, ch, ph, pos);
+  Cons<TRACE, FAST> c(a, S, ch, ph, pos);
   c.run();
 }
 
@@ -1433,13 +1778,51 @@ int decode_grid() {
 }
 
 cudaError_t prepare_decode(size_t smem, int grid) {
-  cudaError_t e = cudaFuncSetAttribute(k_decode<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_decode<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(k_decode<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_decode<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_decode<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_decode<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<false>, DK_THREADS, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<false, false>, DK_THREADS, smem);
   if (e != cudaSuccess) return e;
   return per_sm >= 1 && grid <= per_sm * decode_grid() ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
+}
+
+// The V cache [n_layer * n_kv * n_ctx][dh] f32 as a 2-D tensor map with boxes
+// of DK_VB positions x ds dimensions.  The encoder is the driver's, reached
+// through the runtime (the library does not link libcuda).
+int make_vcache_map(CUtensorMap *map, const float *vcache, int n_layer, int n_kv, int n_ctx, int dh, int ds,
+                    std::string &why) {
+  using Encode = decltype(&cuTensorMapEncodeTiled);
+  static Encode encode = nullptr;
+  if (!encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      cudaGetLastError();
+      why = "cuTensorMapEncodeTiled is not available";
+      return -1;
+    }
+    encode = reinterpret_cast<Encode>(fn);
+  }
+  if (((uintptr_t)vcache & 15) || ds <= 0 || ds > 256 || (ds * 4) % 16 || dh % ds || (dh * 4) % 16) {
+    why = "V cache does not suit a tensor map";
+    return -1;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)n_layer * n_kv * n_ctx};
+  const cuuint64_t strides[1] = {(cuuint64_t)dh * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)ds, (cuuint32_t)DK_VB};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(vcache), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    why = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return -1;
+  }
+  return 0;
 }
 
 cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream_t st) {
@@ -1453,7 +1836,8 @@ cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return a.trace ? cudaLaunchKernelEx(&cfg, k_decode<true>, a) : cudaLaunchKernelEx(&cfg, k_decode<false>, a);
+  if (a.fast) return a.trace ? cudaLaunchKernelEx(&cfg, k_decode<true, true>, a) : cudaLaunchKernelEx(&cfg, k_decode<false, true>, a);
+  return a.trace ? cudaLaunchKernelEx(&cfg, k_decode<true, false>, a) : cudaLaunchKernelEx(&cfg, k_decode<false, false>, a);
 }
 
 
@@ -1627,10 +2011,14 @@ bool build_decode_plan(const std::vector<DecLayer> &layers, const DevTensor &out
     return false;
   }
   if (n_embd % 32 || n_ff % 32 || (n_head * dh) % 32 || n_head % n_kv || 2 * ((n_embd / 2 + grid - 1) / grid) > DK_XO ||
-      n_ctx % 4) {  // K chunks copy whole groups of 4 positions
+      n_ctx % 4 || dh % 16) {  // K chunks copy whole groups of 4 positions; V boxes are 16-dimension multiples
     why = "unsupported dimensions";
     return false;
   }
+  // Attention units: the most value-dimension slices (of 16 or more) whose
+  // units all have a CTA of their own.
+  plan.att_j = 1;
+  while (2 * plan.att_j * n_head <= grid && dh % (2 * plan.att_j * 16) == 0) plan.att_j *= 2;
   if (decode_grid_for(layers, out, grid) < grid) {  // the tagged hand-off needs rows of every matrix on every CTA
     why = "more CTAs than row pairs of some matrix";
     return false;

@@ -9,6 +9,7 @@
 // consumer warps compute.  Weights never depend on activations, so the
 // producer runs ahead across the grid-wide dependency points.
 #pragma once
+#include <cuda.h>  // CUtensorMap (the type only; the encoder is reached through cudaGetDriverEntryPoint)
 #include <stdint.h>
 
 #include <string>
@@ -18,7 +19,7 @@
 
 namespace pk {
 
-constexpr int DK_THREADS = 384;     // warp 0 producer, warps 1-2 row chains, warps 3..11 terms
+constexpr int DK_THREADS = 512;     // warp 0 producer, warps 1-2 row chains, warps 3..15 terms
 constexpr int DK_CHAINS = 2;        // chain warps
 constexpr int DK_NB = 3;            // term buffers
 constexpr int DK_NS = 5;            // ring slots
@@ -26,6 +27,7 @@ constexpr int DK_SLOT = 32768;      // bytes per slot
 constexpr int DK_TS = 2560;         // floats per term buffer
 constexpr int DK_MAX_RG = 32;       // rows per row group (one chain lane each)
 constexpr int DK_TRW = 16;          // profile-trace words per phase
+constexpr int DK_VB = 32;           // V-history positions per tensor-map box
 
 enum : uint8_t { DR_Q = 0, DR_K, DR_V, DR_O, DR_GATE, DR_UP, DR_DOWN, DR_HEAD };
 enum : uint8_t { DF_FIRST = 1, DF_LAST = 2 };
@@ -59,6 +61,9 @@ struct DecLayer {
 };
 
 struct DecodeArgs {
+  // V cache [L * n_kv * n_ctx][dh] as a 2-D tensor map: boxes of DK_VB
+  // positions x att_ds dimensions (one attention unit's slice).
+  alignas(64) CUtensorMap vmap;
   const DecLayer *layers;
   DevTensor out;
   const float *out_norm;
@@ -66,6 +71,9 @@ struct DecodeArgs {
   uint32_t embd_row_bytes;
   int embd_type;
   int n_layer, n_embd, n_ff, n_head, n_kv, dh, half, n_ctx, n_vocab;
+  // Attention units: head h's value dimensions are split into att_j slices
+  // of att_ds, unit u = h * att_j + j on CTA u % grid.
+  int att_j, att_ds;
   float eps, scale;
   const float *rope_cos, *rope_sin;
   float *kcache, *vcache;             // K [L][n_kv][dh][n_ctx] (d-major), V [L][n_kv][n_ctx][dh]
@@ -79,6 +87,7 @@ struct DecodeArgs {
   unsigned long long *h_ll;           // [n_ff] SwiGLU output
   unsigned long long *q_ll;           // [n_head * dh] roped q
   unsigned long long *kv_ll;          // [2][n_kv * dh] this position's roped k (0) and v (1)
+  unsigned long long *sc_ll;          // [n_head][n_ctx] attention scores shared by a head's units
   uint32_t *ids, *tok, *hist;
   int *pos, *step;
   const DChunk *chunks;
@@ -92,6 +101,7 @@ struct DecodeArgs {
   float *cand_v;
   int *cand_i;                        // [grid]
   int mode;                           // 1: greedy pick + token feedback after the head
+  int fast;                           // 1: the fast float order (integer dots and Q8 still exact)
   int poison;                         // > 0 (test hook): phase `poison` waits for a tag no phase writes
   unsigned long long *trace;          // optional [grid][n_trace] globaltimer stamps
   int n_trace;
@@ -103,6 +113,7 @@ struct DecodePlan {
   std::vector<int> cta_chunk0, phase0, own;
   std::vector<uint32_t> cwbits;  // bit i: chain warp of chunk i
   int grid = 0, n_phase = 0;
+  int att_j = 1;  // value-dimension slices per attention head
   size_t smem = 0;
 };
 // false (with the reason) when this model cannot use the persistent kernel.
@@ -118,6 +129,9 @@ size_t decode_smem_bytes(int n_embd, int n_ff, int qdim, int n_ctx, int dh, int 
 // Sets the kernel's shared-memory limit and checks that `grid` CTAs fit at once.
 cudaError_t prepare_decode(size_t smem, int grid);
 cudaError_t launch_decode(const DecodeArgs &a, int grid, size_t smem, cudaStream_t st);
+// DecodeArgs::vmap for a V cache (0, or -1 with the reason).
+int make_vcache_map(CUtensorMap *map, const float *vcache, int n_layer, int n_kv, int n_ctx, int dh, int ds,
+                    std::string &why);
 int decode_grid();
 
 }  // namespace pk

@@ -78,11 +78,14 @@ int Engine::create(int device, int n_ctx, int max_batch) {
   device_ = device;
   n_ctx_ = n_ctx;
   max_batch_ = max_batch;
+  if (const char *o = std::getenv("PK_ORDER")) order_ = std::strcmp(o, "fast") == 0 ? PK_ORDER_FAST : PK_ORDER_EXACT;
   PK_CK(cudaSetDevice(device_));
   PK_CK(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
   PK_CK(cudaHostAlloc((void **)&h_ids_, 64 * sizeof(uint32_t), cudaHostAllocDefault));
   PK_CK(cudaHostAlloc((void **)&h_pos_, 64 * sizeof(int), cudaHostAllocDefault));
   PK_CK(cudaHostAlloc((void **)&h_tok_, 4 * sizeof(uint32_t), cudaHostAllocDefault));
+  void *scratch = nullptr;  // reserve pk_matmul_noalloc's scratch on this device now (see pk.h)
+  if (noalloc_scratch(&scratch) != cudaSuccess) cudaGetLastError();
   return PK_OK;
 }
 
@@ -426,7 +429,8 @@ int Engine::setup_decode() {
                n_tr = (size_t)grid * n_trace * 8;
   const size_t qdim = (size_t)c.n_head * c.head_dim, kdim = (size_t)c.n_head_kv * c.head_dim;
   const std::vector<size_t> sizes = {n_ch, n_c0, n_ph, n_own, n_ly, 16, 16, (size_t)grid * 4, (size_t)grid * 4, n_tr, n_cw,
-                                     2 * (size_t)c.n_embd * 8, qdim * 8, (size_t)c.n_ff * 8, qdim * 8, 2 * kdim * 8};
+                                     2 * (size_t)c.n_embd * 8, qdim * 8, (size_t)c.n_ff * 8, qdim * 8, 2 * kdim * 8,
+                                     (size_t)c.n_head * n_ctx_ * 8};
   size_t total = 0;
   for (size_t z : sizes) total += a256(z);
   PK_CK(cudaMalloc((void **)&d_decode_, total));
@@ -449,7 +453,7 @@ int Engine::setup_decode() {
   uint32_t *cwb = (uint32_t *)take();
   unsigned long long *x_ll = (unsigned long long *)take(), *att_ll = (unsigned long long *)take(),
                      *h_ll = (unsigned long long *)take(), *q_ll = (unsigned long long *)take(),
-                     *kv_ll = (unsigned long long *)take();
+                     *kv_ll = (unsigned long long *)take(), *sc_ll = (unsigned long long *)take();
   PK_CK(cudaMemcpyAsync(chunks, plan_.chunks.data(), n_ch, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(c0, plan_.cta_chunk0.data(), n_c0, cudaMemcpyHostToDevice, st_));
   PK_CK(cudaMemcpyAsync(ph, plan_.phase0.data(), n_ph, cudaMemcpyHostToDevice, st_));
@@ -473,12 +477,16 @@ int Engine::setup_decode() {
   a.scale = 1.0f / sqrtf((float)c.head_dim);
   a.rope_cos = d_rope_cos_; a.rope_sin = d_rope_sin_;
   a.kcache = d_kcache_; a.vcache = d_vcache_;
+  a.att_j = plan_.att_j;
+  a.att_ds = c.head_dim / plan_.att_j;
+  if (make_vcache_map(&a.vmap, d_vcache_, c.n_layer, c.n_head_kv, n_ctx_, c.head_dim, a.att_ds, decode_why_)) return PK_OK;
   a.logits = logits_;
-  a.x_ll = x_ll; a.att_ll = att_ll; a.h_ll = h_ll; a.q_ll = q_ll; a.kv_ll = kv_ll;
+  a.x_ll = x_ll; a.att_ll = att_ll; a.h_ll = h_ll; a.q_ll = q_ll; a.kv_ll = kv_ll; a.sc_ll = sc_ll;
   a.ids = d_ids_; a.tok = d_tok_; a.hist = d_hist_; a.pos = d_pos_; a.step = d_step_;
   a.chunks = chunks; a.cta_chunk0 = c0; a.phase0 = ph; a.n_phase = plan_.n_phase; a.own = own; a.cwbits = cwb;
   a.sync = d_sync_; a.err = d_err_; a.cand_v = cv; a.cand_i = ci;
   a.mode = 0;
+  a.fast = order_ == PK_ORDER_FAST ? 1 : 0;
   a.trace = nullptr;
   a.n_trace = n_trace;
   use_decode_ = true;
@@ -960,6 +968,16 @@ int Engine::decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms
   return PK_OK;
 }
 
+int Engine::set_order(int order) {
+  if (order != PK_ORDER_EXACT && order != PK_ORDER_FAST) return set_error(PK_ERR_INVALID, "unknown decode order");
+  if (order != order_) {
+    order_ = order;
+    dargs_.fast = order == PK_ORDER_FAST ? 1 : 0;
+    release_graphs();  // the captured step holds the other order's kernel
+  }
+  return PK_OK;
+}
+
 int Engine::set_position(int pos) {
   if (!loaded_) return set_error(PK_ERR_INVALID, "no model loaded");
   if (pos <= 0 || pos > next_pos_) return set_error(PK_ERR_INVALID, "position must be in 1..current length");
@@ -1273,7 +1291,7 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
       const int j = q % 5;
       wall[j] += (max_exit(q) - max_exit(q - 1)) * 1e-6;
       // attention sub-phases: only the CTAs that own a head stamp them
-      const int ng = j == 1 ? std::min(grid, c.n_head) : grid;
+      const int ng = j == 1 ? std::min(grid, c.n_head * plan_.att_j) : grid;
       for (int g = 0; g < ng; g++) {
         const int b0 = 1 + DK_TRW * q;
         sub[j][0] += (at(g, b0) - exit_of(g, q - 1)) * 1e-6 / ng;
@@ -1350,6 +1368,34 @@ int Engine::set_debug(bool on) {
 }
 
 int Engine::get_dump(const char *name, float *out, int cap, int *n_out) {
+  if (std::strncmp(name, "decode.", 7) == 0 && use_decode_) {
+    // The persistent kernel's phase outputs of its last launch (last layer),
+    // read from the tagged words (value in the low half).
+    const DecodeArgs &a = dargs_;
+    const size_t qd = (size_t)a.n_head * a.dh, kd = (size_t)a.n_kv * a.dh;
+    const std::string n = name + 7;
+    const unsigned long long *src = nullptr;
+    size_t cnt = 0;
+    if (n == "q") src = a.q_ll, cnt = qd;
+    else if (n == "k") src = a.kv_ll, cnt = kd;
+    else if (n == "v") src = a.kv_ll + kd, cnt = kd;
+    else if (n == "att") src = a.att_ll, cnt = qd;
+    else if (n == "x_o") src = a.x_ll, cnt = (size_t)a.n_embd;
+    else if (n == "x") src = a.x_ll + a.n_embd, cnt = (size_t)a.n_embd;
+    else if (n == "h") src = a.h_ll, cnt = (size_t)a.n_ff;
+    if (src) {
+      std::vector<unsigned long long> w(cnt);
+      PK_CK(cudaMemcpyAsync(w.data(), src, cnt * 8, cudaMemcpyDeviceToHost, st_));
+      PK_CK(cudaStreamSynchronize(st_));
+      if (out)
+        for (size_t i = 0; i < std::min(cnt, (size_t)std::max(cap, 0)); i++) {
+          const uint32_t lo = (uint32_t)w[i];
+          std::memcpy(out + i, &lo, 4);
+        }
+      if (n_out) *n_out = (int)cnt;
+      return PK_OK;
+    }
+  }
   for (auto &d : dbg_)
     if (d.first == name) {
       const int n = (int)d.second.size();

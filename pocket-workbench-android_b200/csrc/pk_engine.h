@@ -54,6 +54,7 @@ class Engine {
                uint32_t *out_ids, int out_cap, int *n_out, pk_gen_stats *stats);
   int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
   int set_position(int pos);
+  int set_order(int order);
   // Independent streams, each with its own KV cache, decoded together.
   int streams_begin(int n_streams);
   int stream_prefill(int s, const uint32_t *prompt, int n);
@@ -142,6 +143,7 @@ class Engine {
 
   // persistent decode kernel (pk_decode.cu): plan, device tables and args
   bool use_decode_ = false;
+  int order_ = PK_ORDER_EXACT;  // float order of the b = 1 decode step (pk_set_order)
   std::string decode_why_;
   DecodePlan plan_;
   DecodeArgs dargs_{};

@@ -237,6 +237,13 @@ __global__ void k_q8(const float *__restrict__ x, long xs_e, long xs_l, int k, i
   }
 }
 
+cudaError_t kernels_binary_version(int *v) {
+  cudaFuncAttributes fa{};
+  const cudaError_t e = cudaFuncGetAttributes(&fa, k_q8);
+  if (e == cudaSuccess) *v = fa.binaryVersion;
+  return e;
+}
+
 cudaError_t launch_q8(const float *x, long xs_e, long xs_l, int k, int b, Q8Dev act, cudaStream_t st) {
   long warps = (long)b * (k / 32);
   int grid = (int)std::min<long>((warps * 32 + 255) / 256, (long)num_sms() * 8);

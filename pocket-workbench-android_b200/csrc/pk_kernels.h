@@ -43,6 +43,8 @@ cudaError_t launch_dequant_rows(int type, const void *raw, size_t row_bytes, int
 
 // Q8Act::prepare on x[i * xs_elem + bi * xs_lane].
 cudaError_t launch_q8(const float *x, long xs_elem, long xs_lane, int k, int b, Q8Dev act, cudaStream_t st);
+// binaryVersion of this library's device code as loaded on the current device.
+cudaError_t kernels_binary_version(int *v);
 // RMSNorm (model.rs:812-822) + Q8 of token-major x [b][k]; xn (optional) gets the normed floats.
 // neon: the sum of squares in the reference's b == 1 order (simd.rs:47-64)
 // for every row, instead of the b > 1 sequential chain.

@@ -27,14 +27,15 @@ PK_ERR = {1: "PK_ERR_INVALID", 2: "PK_ERR_UNSUPPORTED", 3: "PK_ERR_CUDA", 4: "PK
           6: "PK_ERR_CONTEXT_FULL", 7: "PK_ERR_STOPPED", 8: "PK_ERR_TIMEOUT"}
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
+ORDER_EXACT, ORDER_FAST = 0, 1  # pk_set_order
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 
 # Every function include/pk.h declares (checked by tests/test_capi_symbols.py).
 SYMBOLS = [
-    "pk_last_error", "pk_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_matmul_noalloc", "pk_packed_bytes",
+    "pk_last_error", "pk_version", "pk_device_binary_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_matmul_noalloc", "pk_packed_bytes",
     "pk_pack_weights", "pk_matmul_packed", "pk_backend_new", "pk_backend_free", "pk_backend_selftest",
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
-    "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position",
+    "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position", "pk_set_order",
     "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
     "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
     "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
@@ -108,7 +109,7 @@ def lib():
     L = C.CDLL(LIB_PATH)
     P, I, U32, SZ = C.c_void_p, C.c_int, C.c_uint32, C.c_size_t
     sig = {
-        "pk_last_error": ([], C.c_char_p), "pk_version": ([], I), "pk_supports": ([U32], I),
+        "pk_last_error": ([], C.c_char_p), "pk_version": ([], I), "pk_device_binary_version": ([C.POINTER(I)], I), "pk_supports": ([U32], I),
         "pk_q8_quantize": ([P, I, I, C.POINTER(Q8ActC), P], I), "pk_expf": ([P, P, I, P], I),
         "pk_matmul": ([U32, P, SZ, I, I, C.POINTER(Q8ActC), P, P], I),
         "pk_matmul_noalloc": ([U32, P, SZ, I, I, C.POINTER(Q8ActC), P, P], I),
@@ -123,7 +124,7 @@ def lib():
         "pk_forward": ([P, P, P, I, I], I), "pk_logits": ([P, P, I], I),
         "pk_argmax": ([P, C.POINTER(U32)], I),
         "pk_generate": ([P, P, I, C.POINTER(GenOpts), TOKEN_CB, P, P, I, C.POINTER(I), C.POINTER(GenStats)], I),
-        "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_position": ([P, I], I),
+        "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_position": ([P, I], I), "pk_set_order": ([P, I], I),
         "pk_streams_begin": ([P, I], I), "pk_stream_prefill": ([P, I, P, I], I),
         "pk_streams_decode": ([P, I, P, C.POINTER(C.c_float)], I), "pk_streams_set_position": ([P, I], I),
         "pk_decode_profile": ([P, C.POINTER(KernelStat), I, C.POINTER(I)], I), "pk_set_debug": ([P, I], I),
@@ -313,13 +314,20 @@ class Backend:
 class Engine:
     """Engine::load / forward / logits / generate on one GPU."""
 
-    def __init__(self, path: str | None = None, n_ctx: int = 512, max_batch: int = 32, device: int = 0):
+    def __init__(self, path: str | None = None, n_ctx: int = 512, max_batch: int = 32, device: int = 0,
+                 order: str | None = None):
         h = C.c_void_p()
         _check(lib().pk_create(device, n_ctx, max_batch, C.byref(h)))
         self.h = h
         self.n_ctx = n_ctx
+        if order is not None:
+            self.set_order(order)
         if path is not None:
             self.load(path)
+
+    def set_order(self, order: str):
+        """Float order of the b = 1 decode step: "exact" (the reference's) or "fast"."""
+        _check(lib().pk_set_order(self.h, {"exact": ORDER_EXACT, "fast": ORDER_FAST}[order]))
 
     def load(self, path: str):
         _check(lib().pk_load_gguf(self.h, path.encode()))

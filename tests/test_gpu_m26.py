@@ -17,19 +17,31 @@ pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 THREADS = max(1, os.cpu_count() or 1)
 
 
-def test_m26_323_prompt_then_128_greedy_tokens(pk, oracle):
+@pytest.fixture(scope="module")
+def m26_oracle(oracle):
+    """The CPU path's 128 greedy tokens and final logits (computed once)."""
     path = synth.m26_path(os.environ.get("PK_MODEL_DIR", tempfile.gettempdir()))
     prompt = synth.prompt_ids(323, 323, synth.M26.n_vocab)
-    g = pk.Engine(path, n_ctx=512, max_batch=32)
     o = oracle.Engine(path, 512, THREADS)
-    rg = g.generate(prompt, 128, stop_at_eog=False)
     ro = o.generate(prompt, 128)
+    return path, prompt, ro, o.logits()
+
+
+def test_m26_323_prompt_then_128_greedy_tokens(pk, m26_oracle):
+    """The exact decode order (the default): the reference's bits, so the
+    reference's 128 greedy ids.  (The fast order cannot be held to this on
+    this model: its random weights amplify a relative perturbation about
+    1.36x per layer, so the regrouped sums' ~1e-6 becomes ~20% of the last
+    layer by layer 40 -- test_gpu_fast_order.py measures it.)"""
+    path, prompt, ro, lo = m26_oracle
+    g = pk.Engine(path, n_ctx=512, max_batch=32, order="exact")
+    rg = g.generate(prompt, 128, stop_at_eog=False)
     assert rg["prefill_tokens"] == ro["prefill_tokens"] == 323
-    lg, lo = g.logits(), o.logits()
+    lg = g.logits()
     rel = float(np.max(np.abs(lg - lo)) / np.std(lo))
     top2 = np.sort(lo)[-2:]
     print(f"M26 logits max|diff|/std = {rel:.2e}; final top-2 gap {top2[1] - top2[0]:.4f}")
     mism = [i for i, (a, b) in enumerate(zip(rg["gen_ids"], ro["gen_ids"])) if a != b]
     assert not mism, f"first mismatch at step {mism[0]}"
     assert len(rg["gen_ids"]) == 128
-    assert rel < 1e-3
+    assert rel == 0.0  # the reference's bits
