@@ -69,6 +69,10 @@ static_assert(TG1 > 0 && TG0 % 32 == 0 && TG1 % 32 == 0, "two whole-warp term gr
 // A term-buffer barrier's participants: the chunk's group and one chain warp.
 __host__ __device__ constexpr int nb_pair(int mv) { return ((mv & 1) ? TG1 : TG0) + 32; }
 constexpr unsigned long long WAIT_NS = 2000000000ull;
+// Waiting threads yield their issue slots: consumers waiting for ring data
+// suspend in mbarrier.try_wait (woken when the phase completes), and pollers
+// of another SM's tagged words sleep between reads.
+constexpr uint32_t DATA_SLEEP_NS = 4000, POLL_SLEEP_NS = 128;
 
 __device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ unsigned long long gtime() {
@@ -391,12 +395,21 @@ __device__ __forceinline__ float add8(float acc, const float4 a, const float4 b)
 __device__ __forceinline__ float chain_add_v(float acc, uint32_t p, int n) {
   const int nb = (n + 7) >> 3;
   if (nb == 0) return acc;
+  // two batches of eight in flight ahead of the adds
   float4 a = sld_v4f(p), b = sld_v4f(p + 16);
-  for (int i = 1; i < nb; i++) {
+  float4 a2 = nb > 1 ? sld_v4f(p + 32) : make_float4(0.f, 0.f, 0.f, 0.f), b2 = nb > 1 ? sld_v4f(p + 48) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 2; i < nb; i++) {
     const float4 na = sld_v4f(p + 32u * i), nb8 = sld_v4f(p + 32u * i + 16u);
     acc = add8(acc, a, b);
-    a = na;
-    b = nb8;
+    a = a2;
+    b = b2;
+    a2 = na;
+    b2 = nb8;
+  }
+  if (nb > 1) {
+    acc = add8(acc, a, b);
+    a = a2;
+    b = b2;
   }
   const int r = n - 8 * (nb - 1);  // live slots of the last batch, 1..8
   const float4 za = make_float4(a.x, r > 1 ? a.y : 0.0f, r > 2 ? a.z : 0.0f, r > 3 ? a.w : 0.0f);
@@ -498,10 +511,10 @@ __device__ __forceinline__ void item_q4k(uint32_t w_a, int blk, const DAct &A, u
   for (int i = 0; i < 8; i++) w[i] = sld_v4(w_a + 16 + 16 * i);  // pair p: w[2p] (lo16), w[2p+1]
 #pragma unroll
   for (int i = 0; i < 16; i++) x[i] = sld_v4i(xq + 16u * i);  // sub-block j: x[2j], x[2j+1]
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    da[j] = sld_f(A.d + xf + 4u * j);
-    sa[j] = sld_f(A.s + xf + 4u * j);
+  {  // the superblock's eight activation scales and block sums: two 16-byte loads each
+    const float4 d0 = sld_v4f(A.d + xf), d1 = sld_v4f(A.d + xf + 16), s0 = sld_v4f(A.s + xf), s1 = sld_v4f(A.s + xf + 16);
+    da[0] = d0.x; da[1] = d0.y; da[2] = d0.z; da[3] = d0.w; da[4] = d1.x; da[5] = d1.y; da[6] = d1.z; da[7] = d1.w;
+    sa[0] = s0.x; sa[1] = s0.y; sa[2] = s0.z; sa[3] = s0.w; sa[4] = s1.x; sa[5] = s1.y; sa[6] = s1.z; sa[7] = s1.w;
   }
   const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
   // get_scale_min_k4 (quant.rs:80-86) for all eight sub-blocks, a byte each:
@@ -559,10 +572,14 @@ __device__ __forceinline__ void item_q6k(uint32_t w_a, uint32_t d_a, int blk, in
     const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);  // activation block
     x[2 * s] = sld_v4i(A.q + ab * 32u);
     x[2 * s + 1] = sld_v4i(A.q + ab * 32u + 16u);
-    da[s] = sld_f(A.d + ab * 4u);
-    const uint2 hs = sld_v2(A.s16 + ab * 8u);
-    s16[2 * s] = (int)hs.x;
-    s16[2 * s + 1] = (int)hs.y;
+  }
+  {  // the half's four activation scales and eight 16-element sums (16-byte loads)
+    const uint32_t ab0 = (uint32_t)(blk * 8 + 4 * h);
+    const float4 dv = sld_v4f(A.d + ab0 * 4u);
+    const int4 h0 = sld_v4i(A.s16 + ab0 * 8u), h1 = sld_v4i(A.s16 + ab0 * 8u + 16u);
+    da[0] = dv.x; da[1] = dv.y; da[2] = dv.z; da[3] = dv.w;
+    s16[0] = h0.x; s16[1] = h0.y; s16[2] = h0.z; s16[3] = h0.w;
+    s16[4] = h1.x; s16[5] = h1.y; s16[6] = h1.z; s16[7] = h1.w;
   }
   const float d = f16f(dbits);
   const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
@@ -638,10 +655,10 @@ __device__ __forceinline__ void item_q4k_f(uint32_t w_a, int blk, const DAct &A,
   for (int i = 0; i < 8; i++) w[i] = sld_v4(w_a + 16 + 16 * i);
 #pragma unroll
   for (int i = 0; i < 16; i++) x[i] = sld_v4i(xq + 16u * i);
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    da[j] = sld_f(A.d + xf + 4u * j);
-    sa[j] = sld_f(A.s + xf + 4u * j);
+  {
+    const float4 d0 = sld_v4f(A.d + xf), d1 = sld_v4f(A.d + xf + 16), s0 = sld_v4f(A.s + xf), s1 = sld_v4f(A.s + xf + 16);
+    da[0] = d0.x; da[1] = d0.y; da[2] = d0.z; da[3] = d0.w; da[4] = d1.x; da[5] = d1.y; da[6] = d1.z; da[7] = d1.w;
+    sa[0] = s0.x; sa[1] = s0.y; sa[2] = s0.z; sa[3] = s0.w; sa[4] = s1.x; sa[5] = s1.y; sa[6] = s1.z; sa[7] = s1.w;
   }
   const float d = f16f((uint16_t)(hdr.x & 0xFFFFu)), dmin = f16f((uint16_t)(hdr.x >> 16));
   const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
@@ -694,10 +711,14 @@ __device__ __forceinline__ void item_q6k_f(uint32_t w_a, uint32_t d_a, int blk, 
     const uint32_t ab = (uint32_t)(blk * 8 + 4 * h + s);
     x[2 * s] = sld_v4i(A.q + ab * 32u);
     x[2 * s + 1] = sld_v4i(A.q + ab * 32u + 16u);
-    da[s] = sld_f(A.d + ab * 4u);
-    const uint2 hs = sld_v2(A.s16 + ab * 8u);
-    s16[2 * s] = (int)hs.x;
-    s16[2 * s + 1] = (int)hs.y;
+  }
+  {
+    const uint32_t ab0 = (uint32_t)(blk * 8 + 4 * h);
+    const float4 dv = sld_v4f(A.d + ab0 * 4u);
+    const int4 h0 = sld_v4i(A.s16 + ab0 * 8u), h1 = sld_v4i(A.s16 + ab0 * 8u + 16u);
+    da[0] = dv.x; da[1] = dv.y; da[2] = dv.z; da[3] = dv.w;
+    s16[0] = h0.x; s16[1] = h0.y; s16[2] = h0.z; s16[3] = h0.w;
+    s16[4] = h1.x; s16[5] = h1.y; s16[6] = h1.z; s16[7] = h1.w;
   }
   const unsigned long long sw = (unsigned long long)scw.y << 32 | scw.x;
   float acc = 0.0f;
@@ -985,7 +1006,7 @@ struct Cons {
   __device__ __forceinline__ void wait_full_at(int j) {  // the transfer j places ahead
     const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == TT0);
     const long long t0 = timed ? clock64() : 0;
-    const bool ok = mbar_wait(&S.full[rg.slot_at(j)], rg.par_at(j), S.flag);
+    const bool ok = mbar_wait(&S.full[rg.slot_at(j)], rg.par_at(j), S.flag, DATA_SLEEP_NS);
     if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
     if (!ok && !*S.flag) {
       atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
@@ -995,7 +1016,7 @@ struct Cons {
   __device__ __forceinline__ void wait_full() {
     const bool timed = (TRACE && a.trace) && (ctid == 0 || ctid == TT0);
     const long long t0 = timed ? clock64() : 0;
-    const bool ok = mbar_wait(&S.full[rg.slot], rg.par, S.flag);
+    const bool ok = mbar_wait(&S.full[rg.slot], rg.par, S.flag, DATA_SLEEP_NS);
     if (timed) pacc(ctid == 0 ? 0 : 1, clock64() - t0);
     if (!ok && !*S.flag) {
       atomicCAS(a.err, 0, PK_ERR_TIMEOUT);
@@ -1101,6 +1122,7 @@ struct Cons {
 #pragma unroll
         for (int j = 0; j < 2 * NP; j++) all = all && ll_ok(w[j], tag);
         if (all || !poll_ok(t0, ++it)) break;
+        __nanosleep(POLL_SLEEP_NS);  // the words come from other SMs through L2: do not spin on issue slots
 #pragma unroll
         for (int j = 0; j < NP; j++) {
           const int i = base + ctid + j * CONS;
@@ -1482,6 +1504,7 @@ struct Cons {
                                    *pv = a.kv_ll + (size_t)(a.n_kv + kh) * dh + d;
           unsigned long long wq = ld_ll(pq), wk = ld_ll(pk), wv = ld_ll(pv);
           while (!(ll_ok(wq, tq) && ll_ok(wk, tq) && ll_ok(wv, tq)) && poll_ok(t0, ++it)) {
+            __nanosleep(POLL_SLEEP_NS);
             if (!ll_ok(wq, tq)) wq = ld_ll(pq);
             if (!ll_ok(wk, tq)) wk = ld_ll(pk);
             if (!ll_ok(wv, tq)) wv = ld_ll(pv);
@@ -1543,7 +1566,10 @@ struct Cons {
         for (int p = ctid; p < pos; p += CONS) {
           if (p >= r0 && p < r1) continue;
           unsigned long long w = ld_ll(scg + p);
-          while (!ll_ok(w, tag) && poll_ok(t0, ++it)) w = ld_ll(scg + p);
+          while (!ll_ok(w, tag) && poll_ok(t0, ++it)) {
+            __nanosleep(POLL_SLEEP_NS);
+            w = ld_ll(scg + p);
+          }
           const float sv = ll_val(w);
           sc[p] = sv;
           mx = sv > mx ? sv : mx;
@@ -1603,6 +1629,7 @@ struct Cons {
             vc[i] = e != 0.0f ? fmul(e, vc[i]) : -0.0f;
           }
           bar_sync(NB_V, VT);
+          if (u == (int)blockIdx.x && p0 == 0) fine(6);
           if (ctid < ds) vacc = chain_add(vacc, shaddr(vc) + 4u * ctid, 4u * ds, n);
           bar_sync(NB_V, VT);
           if (ctid == 0) mbar_arrive(&S.empty[rg.slot]);
@@ -1744,12 +1771,20 @@ __global__ void __launch_bounds__(DK_THREADS, 1) k_decode(const __grid_constant_
   }
   __syncthreads();
   const int *ph = S.ph;
+  if (TRACE && a.trace && threadIdx.x == 32) {  // SM cycles and ns at the start (clock check)
+    a.trace[(size_t)blockIdx.x * a.n_trace + a.n_trace - 4] = (unsigned long long)clock64();
+    a.trace[(size_t)blockIdx.x * a.n_trace + a.n_trace - 3] = gtime();
+  }
   if (threadIdx.x < 32) {
     producer<TRACE>(a, S, pos, ch, ph);
     return;
   }
   Cons<TRACE, FAST> c(a, S, ch, ph, pos);
   c.run();
+  if (TRACE && a.trace && threadIdx.x == 32) {  // and at the end
+    a.trace[(size_t)blockIdx.x * a.n_trace + a.n_trace - 2] = (unsigned long long)clock64();
+    a.trace[(size_t)blockIdx.x * a.n_trace + a.n_trace - 1] = gtime();
+  }
 }
 
 }  // namespace

@@ -422,7 +422,7 @@ int Engine::setup_decode() {
     decode_why_ = "the persistent kernel's grid does not fit the device at once";
     return PK_OK;
   }
-  const int n_trace = 1 + DK_TRW * (5 * c.n_layer + 1) + c.n_layer + 1;
+  const int n_trace = 1 + DK_TRW * (5 * c.n_layer + 1) + c.n_layer + 1 + 4;  // + SM cycles / ns at start and end
   const size_t n_ch = plan_.chunks.size() * sizeof(DChunk), n_c0 = plan_.cta_chunk0.size() * 4,
                n_ph = plan_.phase0.size() * 4, n_own = plan_.own.size() * 4, n_ly = dl.size() * sizeof(DecLayer),
                n_cw = plan_.cwbits.size() * 4,
@@ -1348,6 +1348,14 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
       for (int i = 0; i < (j == 5 ? 2 : 8); i++)
         add(std::string(names[j]) + "/" + (i < 7 ? subs[i] : "chain_work"), j == 5 ? 1 : nl, sub[j][i], 0.0);
     add("dk_producer/slot_wait", 1, prod, 0.0);
+    {  // the SM clock the launch ran at: SM cycles over globaltimer ns, averaged over CTAs
+      double mhz = 0.0;
+      for (int g = 0; g < grid; g++) {
+        const double dc = at(g, nt - 2) - at(g, nt - 4), dn = at(g, nt - 1) - at(g, nt - 3);
+        mhz += dn > 0 ? dc / dn * 1e3 / grid : 0.0;
+      }
+      add("k_decode/clock_mhz", 1, mhz, 0.0);  // in the ms field: MHz
+    }
     for (int j = 0; j < 5; j++)
       for (int i = 0; i < 8; i++)
         if (fine_ms[j][i] > 0) add(std::string(names[j]) + "/at" + std::to_string(i), nl, fine_ms[j][i], 0.0);
