@@ -292,6 +292,79 @@ def config1_matvec(pk, synth, device, copies=40, launches=400):
             "note": "k_mv_b1 (pk_matmul_packed), back-to-back launches rotating over distinct weight copies"}
 
 
+def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
+    """BASELINE config 5 (TP half) inside the scaling run: the 70B-shaped stack split
+    over this job's world, synthetic weights generated on each device, greedy b = 1
+    decode; every rank runs it, the time is the max over ranks."""
+    from pocketinfer import replicas, tp
+
+    model = dict(tp.M70)
+    eng = tp.TpEngine(rank, world, device=local, n_ctx=8 + warmup + steps + 16)
+    try:
+        t0 = time.time()
+        err = None
+        try:
+            eng.load_synthetic(model, seed=70)
+        except Exception as exc:  # noqa: BLE001
+            err = exc
+        load_s = time.time() - t0
+        # every rank learns whether all loaded before any of them enters the handle exchange
+        if replicas.max_over_ranks(1.0 if err else 0.0, dist, "cuda") > 0.0:
+            raise RuntimeError(f"tp70: a rank failed to load ({err})")
+        eng.connect() if world > 1 else eng.connect(exchange=lambda b: [b])
+        info = eng.info
+        eng.prefill([(7 * i + 3) % model["n_vocab"] for i in range(8)])
+        eng.decode(warmup)
+        if dist:
+            dist.barrier()
+        _, ms = eng.decode(steps, return_ms=True)
+    finally:
+        eng.close()
+    max_ms = replicas.max_over_ranks(ms, dist, "cuda")
+    ms_step = max_ms / steps
+    hbm, kind = peaks()
+    gbs = info["stream_bytes"] / (ms_step / 1000.0) / 1e9
+    return {"workload": "BASELINE config 5 TP: 80 L, d 8192, 64/8 heads x 128, FFN 28672, vocab 128256, b=1",
+            "parallelism": f"tp{world}", "value": 1000.0 / ms_step, "unit": "tok/s", "ms_per_step": ms_step,
+            "steps": steps, "per_rank_hbm_frac": gbs / hbm, "per_rank_stream_bytes": info["stream_bytes"],
+            "peak_kind": kind, "collectives_per_token": info["collectives_per_token"], "load_s": load_s,
+            "exchange": "partial row sums pushed to every rank's peer buffer over NVLink, added in rank order"}
+
+
+def dp_streams_leg(pk, synth, path, spec, world, rank, local, dist, per_gpu=8, ctx=4096, steps=64, warmup=3):
+    """BASELINE config 5 (DP half) inside the scaling run: per_gpu x world independent
+    greedy M26 streams dealt round-robin to the ranks, each prefilled with its own
+    ctx-token prompt (real prompt-filled caches), then batched steps at positions
+    ctx.. ; weak scaling, max over ranks."""
+    from pocketinfer import replicas
+
+    mine = replicas.assign_streams(per_gpu * world, rank, world)
+    n_ctx = ctx + warmup + steps + 4 - (ctx + warmup + steps) % 4
+    eng = pk.Engine(path, n_ctx=n_ctx, max_batch=32, device=local)
+    try:
+        weights = eng.info["stream_bytes"]
+        eng.streams_begin(len(mine))
+        t0 = time.time()
+        for s, sid in enumerate(mine):
+            eng.stream_prefill(s, synth.prompt_ids(5000 + sid, ctx, spec.n_vocab))
+        prefill_s = time.time() - t0
+        eng.streams_decode(warmup)
+        if dist:
+            dist.barrier()
+        _, ms = eng.streams_decode(steps, return_ms=True)
+    finally:
+        eng.close()
+    value, max_ms = replicas.replica_throughput(steps * len(mine), ms, world, dist, "cuda")
+    ms_step = max_ms / steps
+    hbm, kind = peaks()
+    step_bytes = weights + spec.kv_bytes_per_position() * len(mine) * (ctx + warmup + steps / 2)
+    gbs = step_bytes / (ms_step / 1000.0) / 1e9
+    return {"workload": f"M26, {per_gpu * world} greedy streams ({per_gpu} per GPU), {ctx}-token prompt each, "
+                        f"{steps} batched steps", "parallelism": f"dp{world} (streams)", "value": value,
+            "unit": "tok/s", "ms_per_step": ms_step, "per_gpu_hbm_frac": gbs / hbm, "per_gpu_bytes_per_step": step_bytes,
+            "peak_kind": kind, "prefill_s_per_gpu": prefill_s, "scaling": "weak"}
+
+
 def cpu_baseline_sample(path, prompt, budget_s):
     """The CPU restatement on this host: decode tok/s on a bounded sample of the
     bench's workload (positions 323.. after the 323-token prompt)."""
@@ -402,6 +475,19 @@ def run_ours(args):
     r = eng.generate(prompt, n_e2e + 1, stop_at_eog=False)
     e2e_value, _ = replicas.replica_throughput(n_e2e, r["gen_ms"], world, dist, "cuda")
 
+    # the partitioned rows of BASELINE config 5, on every rank (same collective steps everywhere)
+    tp_row = dp_row = None
+    if not args.decode_only and args.layers is None and args.vocab is None:
+        eng.close()
+        try:
+            tp_row = tp70_leg(world, rank, local, dist)
+        except Exception as exc:  # noqa: BLE001
+            tp_row = {"error": str(exc)[:200]}
+        try:
+            dp_row = dp_streams_leg(pk, synth, path, spec, world, rank, local, dist)
+        except Exception as exc:  # noqa: BLE001
+            dp_row = {"error": str(exc)[:200]}
+
     cpu = None
     c4 = None
     streams = None
@@ -463,6 +549,8 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "streams": streams,
             "config1": c1,
+            "tp70": tp_row,
+            "dp_streams": dp_row,
         }
         print(json.dumps(line), flush=True)
     if dist:
