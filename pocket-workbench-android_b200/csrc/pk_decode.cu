@@ -141,7 +141,7 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                "l"(src), "r"(bytes), "r"(saddr(b))
                : "memory");
 }
-// Tiled 2-D tensor copy global -> this CTA's shared memory (no multicast):
+// Tiled 2-D tensor copy global -> this CTA's own shared memory only:
 // the box of tensor map `map` at element coordinates (x, y), completion
 // counted on mbarrier b.  x * element size is a multiple of 16 bytes at
 // every call site, dst is box-size aligned.
