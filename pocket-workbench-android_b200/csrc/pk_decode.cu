@@ -1074,7 +1074,11 @@ struct Cons {
     if ((TRACE && a.trace) && ctid == 0) {
       stamp(1 + DK_TRW * q + 3, S.prof[q % 5 == 1 ? 0 : 1]);
       for (int i = 2; i < 6; i++) stamp(1 + DK_TRW * q + 2 + i, S.prof[i]);
-      for (int i = 0; i < 6; i++) S.prof[i] = 0ull;
+      if (q % 5 != 1) {  // matvec phases: chain-add cycles and terms chained (fine slots 6, 7 unused there)
+        stamp(1 + DK_TRW * q + 14, S.prof[6]);
+        stamp(1 + DK_TRW * q + 15, S.prof[7]);
+      }
+      for (int i = 0; i < 8; i++) S.prof[i] = 0ull;
     }
     // every consumer is done with this phase's shared buffers; stop together
     const bool stop = bar_or(NB_CONS, CONS, S.flag[0] != 0);
@@ -1428,7 +1432,12 @@ struct Cons {
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.empty[rg.slot]);  // every term warp is done with the slot
           if (c.flags & DF_FIRST) acc = 0.0f;
+          const long long ca = tp ? clock64() : 0;
           if (lane < c.rows) acc = chain_add_v(acc, Tb + 16u * (uint32_t)(lane * (c.rs >> 2)), c.nt);
+          if (tp) {  // profile (lane 0): its chain adds alone, and how many terms they covered
+            pacc(6, clock64() - ca);
+            pacc(7, c.nt);
+          }
           __syncwarp();
           // the term buffer is free again, for chunk mv + DK_NB and its group
           if (mv + DK_NB < mv_total) bar_arrive(NB_EMPTYT + buf * DK_CHAINS + cw, nb_pair(mv + DK_NB));

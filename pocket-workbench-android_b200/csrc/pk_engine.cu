@@ -1302,9 +1302,15 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
     }
     // fine stamps: average offset from the phase start, summed over layers
     double fine_ms[5][8] = {{0}};
+    double chain_cyc[5] = {0}, chain_terms[5] = {0};
     for (int q = 0; q < 5 * nl; q++) {
       const int j = q % 5;
-      for (int i = 0; i < 8; i++) {
+      if (j != 1)
+        for (int g = 0; g < grid; g++) {
+          chain_cyc[j] += at(g, 1 + DK_TRW * q + 14);
+          chain_terms[j] += at(g, 1 + DK_TRW * q + 15);
+        }
+      for (int i = 0; i < (j == 1 ? 8 : 6); i++) {
         double sum = 0;
         int cnt = 0;
         for (int g = 0; g < grid; g++) {
@@ -1348,6 +1354,9 @@ int Engine::decode_profile(pk_kernel_stat *out, int cap, int *n_out) {
       for (int i = 0; i < (j == 5 ? 2 : 8); i++)
         add(std::string(names[j]) + "/" + (i < 7 ? subs[i] : "chain_work"), j == 5 ? 1 : nl, sub[j][i], 0.0);
     add("dk_producer/slot_wait", 1, prod, 0.0);
+    for (int j = 0; j < 5; j++)  // chain warp 0: SM cycles per term of its row chains (in the ms field)
+      if (j != 1 && chain_terms[j] > 0)
+        add(std::string(names[j]) + "/chain_cycles_per_term", nl, chain_cyc[j] / chain_terms[j] * nl, 0.0);
     {  // the SM clock the launch ran at: SM cycles over globaltimer ns, averaged over CTAs
       double mhz = 0.0;
       for (int g = 0; g < grid; g++) {
