@@ -292,6 +292,28 @@ def config1_matvec(pk, synth, device, copies=40, launches=400):
             "note": "k_mv_b1 (pk_matmul_packed), back-to-back launches rotating over distinct weight copies"}
 
 
+def nccl_allreduce_us(dist, n, iters=200, warmup=20):
+    """Device time of one NCCL all-reduce (sum, f32) of the tensor-parallel exchange's
+    n floats over the job's ranks (NVLink), CUDA events, max over ranks: the library
+    collective the peer-memory exchange is measured against."""
+    import torch
+
+    from pocketinfer import replicas
+
+    x = torch.ones(n, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        dist.all_reduce(x)
+    e1.record()
+    torch.cuda.synchronize()
+    return replicas.max_over_ranks(e0.elapsed_time(e1) * 1000.0 / iters, dist, "cuda")
+
+
 def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
     """BASELINE config 5 (TP half) inside the scaling run: the 70B-shaped stack split
     over this job's world, synthetic weights generated on each device, greedy b = 1
@@ -324,7 +346,10 @@ def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
     ms_step = max_ms / steps
     hbm, kind = peaks()
     gbs = info["stream_bytes"] / (ms_step / 1000.0) / 1e9
+    nccl = nccl_allreduce_us(dist, model["n_embd"]) if dist and world > 1 else None
     return {"workload": "BASELINE config 5 TP: 80 L, d 8192, 64/8 heads x 128, FFN 28672, vocab 128256, b=1",
+            "nccl_allreduce_us": nccl,
+            "nccl_ms_per_token": nccl * info["collectives_per_token"] / 1000.0 if nccl else None,
             "parallelism": f"tp{world}", "value": 1000.0 / ms_step, "unit": "tok/s", "ms_per_step": ms_step,
             "steps": steps, "per_rank_hbm_frac": gbs / hbm, "per_rank_stream_bytes": info["stream_bytes"],
             "peak_kind": kind, "collectives_per_token": info["collectives_per_token"], "load_s": load_s,
