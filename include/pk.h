@@ -129,6 +129,19 @@ int pk_matmul(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows
 int pk_matmul_noalloc(uint32_t ttype, const void *w, size_t row_bytes, int k, int n_rows,
                       const pk_q8act *act, float *out, void *stream);
 
+/* Which tensor-core kernel runs the multi-lane (b > 8) matvecs of this
+ * process: every pk_matmul* call and every engine's prefill chunks.  No
+ * counterpart in the reference (its lanes path is CPU code,
+ * quant_int.rs:282-419).  PK_MATMUL_MMA_SYNC (the default): warp-level
+ * int8 mma.sync tiles.  PK_MATMUL_TCGEN05: one tcgen05.mma per 32-element
+ * block into TMEM, weights staged by tensor copies.  Both give the
+ * reference's bits; b <= 8 always uses the mma.sync tiles.  The environment
+ * variable PK_PREFILL_MMA=tc sets the tcgen05 path at load.  Calls in flight
+ * keep the kernel they were launched with. */
+#define PK_MATMUL_MMA_SYNC 0
+#define PK_MATMUL_TCGEN05 1
+int pk_set_matmul_path(int path);
+
 /* Device weight layout: bytes needed for n_rows x k of ttype (>= raw size). */
 size_t pk_packed_bytes(uint32_t ttype, int k, int n_rows);
 /* Raw GGUF blocks (device) -> device layout (device, 16-byte aligned). */

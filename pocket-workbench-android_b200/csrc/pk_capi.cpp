@@ -421,6 +421,12 @@ int pk_decode_steps_device(pk_engine *e, int n_steps, uint32_t *out_ids, float *
   return e->eng.decode_steps_device(n_steps, out_ids, device_ms);
 }
 
+int pk_set_matmul_path(int path) {
+  if (path != PK_MATMUL_MMA_SYNC && path != PK_MATMUL_TCGEN05) return set_error(PK_ERR_INVALID, "unknown matmul path");
+  set_mv_path(path);
+  return PK_OK;
+}
+
 int pk_set_order(pk_engine *e, int order) {
   if (!e) return set_error(PK_ERR_INVALID, "null engine");
   return e->eng.set_order(order);

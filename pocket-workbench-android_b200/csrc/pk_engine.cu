@@ -497,6 +497,15 @@ int Engine::setup_decode() {
 // error code.  The finish counter is reset and the tag epoch advanced (the
 // stopped launch did not advance it), so words that launch left behind can
 // never match the next launch's tags.
+// After b > 1 work: the tensor-core matvec's error word (a bounded wait in
+// one of its CTAs ran out), read and cleared.
+int Engine::check_tc_error() {
+  const int t = mv_tc_error(true);
+  if (t == PK_ERR_TIMEOUT) return set_error(PK_ERR_TIMEOUT, "a tensor-core matvec's bounded wait ran out");
+  if (t) return set_error(t, "reading the tensor-core matvec's error word");
+  return PK_OK;
+}
+
 int Engine::check_decode_error() {
   if (!use_decode_) return PK_OK;
   int err = 0;
@@ -725,6 +734,10 @@ int Engine::forward_inner(const uint32_t *ids, const int *pos, int b, bool want_
     const int rc = check_decode_error();
     if (rc) return rc;
   }
+  if (b > 1) {
+    const int rc = check_tc_error();
+    if (rc) return rc;
+  }
   next_pos_ = pos[b - 1] + 1;
   have_logits_ = want_logits;
   return PK_OK;
@@ -809,6 +822,7 @@ int Engine::prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, boo
   if (ej != cudaSuccess) return cuda_error(ej, "prefill lane join");
   if (es != cudaSuccess) return cuda_error(es, "prefill");
   PK_CK(cudaGetLastError());
+  if ((rc = check_tc_error())) return rc;
   if (*stopped) return PK_OK;
   next_pos_ = n;
   have_logits_ = true;

@@ -72,6 +72,7 @@ class Engine {
   int prefill_lanes(const uint32_t *prompt, int n, int off, int chunk, bool *stopped);
   int enqueue_streams_step();
   int setup_decode();
+  int check_tc_error();
   int check_decode_error();
   int ensure_graphs();
   void release_graphs();

@@ -20,6 +20,9 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "pk_device.cuh"
 #include "pk_quant.cuh"
@@ -1076,8 +1079,28 @@ static size_t mv_seg_smem(const DevTensor &w, int nbc) {
 // slices when the tiles are at most one per SM (a 16-warp CTA per SM with a
 // larger staged chunk), else one; b <= 8 uses one lane group with eight
 // slices (at most one tile per SM) or four.
+// The b > 8 matvec kernel: mma.sync tiles (0) or tcgen05 (1); the
+// environment variable PK_PREFILL_MMA=tc sets 1 at load.
+static std::atomic<int> g_mv_path{-1};
+static int mv_path() {
+  int v = g_mv_path.load();
+  if (v < 0) {
+    const char *e = std::getenv("PK_PREFILL_MMA");
+    int want = (e && std::strcmp(e, "tc") == 0) ? 1 : 0;
+    g_mv_path.compare_exchange_strong(v, want);
+    v = g_mv_path.load();
+  }
+  return v;
+}
+void set_mv_path(int path) { g_mv_path.store(path ? 1 : 0); }
+
 cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st) {
   if (n < 1 || n > MV_MAX_SEGS || act.b < 1) return cudaErrorInvalidValue;
+  if (act.b > 8 && mv_path() == 1) {
+    bool tc = true;
+    for (int i = 0; i < n; i++) tc = tc && mv_tc_supports(outs[i].w, act);
+    if (tc) return launch_mv_tc(n, outs, act, st);
+  }
   int tiles = 0;
   for (int i = 0; i < n; i++) {
     const MvOut &o = outs[i];

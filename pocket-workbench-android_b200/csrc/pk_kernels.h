@@ -64,7 +64,18 @@ struct MvOut {
   long os_row, os_lane;
   bool add;
 };
+// b > 8 runs on the tcgen05 tensor cores (pk_mv_tc.cu) when that path is
+// selected (set_mv_path(1), or PK_PREFILL_MMA=tc) and every matrix suits
+// it; otherwise, and for every b <= 8, on the mma.sync tiles.
 cudaError_t launch_mv_multi(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st);
+// The tcgen05 matvec (pk_mv_tc.cu): whether it takes this matrix and
+// activation, the launch, and its error word (0, or PK_ERR_TIMEOUT after a
+// bounded wait ran out; clear resets it).
+bool mv_tc_supports(const DevTensor &w, const Q8Dev &act);
+cudaError_t launch_mv_tc(int n, const MvOut *outs, const Q8Dev &act, cudaStream_t st);
+int mv_tc_error(bool clear);
+// Selects the b > 8 matvec kernel: 0 mma.sync tiles, 1 tcgen05.
+void set_mv_path(int path);
 
 // Single-lane matvec with the activation quantised inside each CTA:
 // src = x (k floats, optionally RMS-normalised by nw) or a precomputed Q8 act.

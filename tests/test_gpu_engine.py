@@ -53,6 +53,27 @@ def test_prefill_logits_match_oracle(pk, oracle, paths, name):
 
 
 @pytest.mark.parametrize("name", list(MODELS))
+def test_prefill_tcgen05_path_equals_mma_sync(pk, paths, name):
+    """A 77-token prompt (two full 32-token chunks and a 13-token one) gives the
+    same logits, bit for bit, on the tcgen05 matvec path as on the mma.sync
+    tiles; then one decode step on each."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(23, 77, spec.n_vocab)
+    out = {}
+    try:
+        for path in ("mma.sync", "tcgen05"):
+            pk.set_matmul_path(path)
+            g = pk.Engine(paths[name], n_ctx=256)
+            r = g.generate(prompt, 2, stop_at_eog=False)
+            out[path] = (r["gen_ids"], g.logits().view(np.uint32).copy())
+            g.close()
+    finally:
+        pk.set_matmul_path("mma.sync")
+    assert out["mma.sync"][0] == out["tcgen05"][0]
+    assert np.array_equal(out["mma.sync"][1], out["tcgen05"][1])
+
+
+@pytest.mark.parametrize("name", list(MODELS))
 def test_greedy_tokens_identical(pk, oracle, paths, name):
     spec = MODELS[name]
     prompt = synth.prompt_ids(17, 70, spec.n_vocab)

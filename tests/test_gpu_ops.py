@@ -32,6 +32,18 @@ def gpu_q8(pk, x, k, b):
     return act, act.q.cpu().numpy(), act.d.cpu().numpy(), act.sum.cpu().numpy()
 
 
+PATHS = ["mma.sync", "tcgen05"]
+
+
+@pytest.fixture
+def matmul_path(pk, request):
+    """Runs the test with the b > 8 matvec kernel the parameter names, then
+    puts the default (mma.sync) back."""
+    pk.set_matmul_path(request.param)
+    yield request.param
+    pk.set_matmul_path("mma.sync")
+
+
 def check_q8(pk, oracle, x, k, b):
     _, q, d, s = gpu_q8(pk, x, k, b)
     ref = oracle.Q8Act(x, k, b)
@@ -79,9 +91,10 @@ def random_rows(t, k, rows, seed):
     return synth.quant_blocks(spec, seed, rows, k)
 
 
+@pytest.mark.parametrize("matmul_path", PATHS, indirect=True)
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("b", [1, 3, 32, 40])
-def test_matvec_bitexact(pk, oracle, t, b):
+def test_matvec_bitexact(pk, oracle, t, b, matmul_path):
     k, rows = 1024, 96
     w = random_rows(t, k, rows, 1000 + t + b)
     x = synth.normal_f32(2000 + b, k * b)
@@ -94,9 +107,10 @@ def test_matvec_bitexact(pk, oracle, t, b):
     assert np.array_equal(bits(got_packed), bits(want))
 
 
+@pytest.mark.parametrize("matmul_path", PATHS, indirect=True)
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("k,rows,b", [(16384, 96, 32), (4096, 3072, 32), (4096, 8192, 20)])
-def test_matvec_lanes_slices_and_chunks(pk, oracle, t, k, rows, b):
+def test_matvec_lanes_slices_and_chunks(pk, oracle, t, k, rows, b, matmul_path):
     """Multi-lane matvec with each tile's k range split over four warps
     (few tiles) or kept in one (many tiles), rows staged in one or several
     chunks: bit-identical to the reference order in every case."""
@@ -108,10 +122,28 @@ def test_matvec_lanes_slices_and_chunks(pk, oracle, t, k, rows, b):
     assert np.array_equal(bits(got), bits(want))
 
 
+@pytest.mark.parametrize("matmul_path", PATHS, indirect=True)
+@pytest.mark.parametrize("t", [synth.Q8_0, synth.Q4_0])
+@pytest.mark.parametrize("k", [160, 5760])
+def test_matvec_partial_stage(pk, oracle, t, k, matmul_path):
+    """32-element block types whose k is not a multiple of 256: the tcgen05
+    path's last stage holds fewer than eight blocks (the M26 ffn_down has 180)."""
+    rows, b = 200, 32
+    w = random_rows(t, k, rows, 5000 + t + k)
+    x = synth.normal_f32(6000 + k, k * b)
+    act_gpu, *_ = gpu_q8(pk, x, k, b)
+    want = oracle_matmul(oracle, t, w, k, rows, oracle.Q8Act(x, k, b))
+    got = pk.matmul(t, dev(w), k, rows, act_gpu).cpu().numpy()
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("matmul_path", PATHS, indirect=True)
 @pytest.mark.parametrize("t", TYPES)
-def test_matvec_fully_random_bytes(pk, oracle, t):
-    """Every byte random (scales included), as in tests/quant_layout.rs:242-286."""
-    k, rows, b = 512, 64, 4
+@pytest.mark.parametrize("b", [4, 24])
+def test_matvec_fully_random_bytes(pk, oracle, t, b, matmul_path):
+    """Every byte random (scales included), as in tests/quant_layout.rs:242-286;
+    b = 4 always runs the mma.sync tiles, b = 24 the selected path."""
+    k, rows = 512, 64
     be, bb = oracle.type_block(t)
     w2 = synth.random_bytes(31 + t, rows * oracle.row_bytes(t, k)).reshape(-1, bb)
     w2[:, 0:2] = np.frombuffer(np.uint16(0x3200).tobytes(), np.uint8)  # finite f16 scales
