@@ -165,6 +165,23 @@ def prefill_summary(pre, spec, stream_bytes, hbm):
                     "of per-sub-block int8 dots (mma.sync tiles) bounds it, not the tensor pipe or HBM"}
 
 
+def prefill_tcgen05_leg(pk, path, spec, device, stream_bytes, hbm):
+    """The 323-token prefill again with the b > 8 matvecs on the tcgen05 kernel
+    (pk_set_matmul_path): same bits, measured beside the default mma.sync tiles."""
+    pk.set_matmul_path("tcgen05")
+    try:
+        eng = pk.Engine(path, n_ctx=512, max_batch=32, device=device)
+        eng.generate(synth_prompt(spec, 8, 96), 0, stop_at_eog=False)
+        pre = eng.generate(synth_prompt(spec, PROMPT_LEN, PROMPT_LEN), 0, stop_at_eog=False)
+        eng.close()
+    finally:
+        pk.set_matmul_path("mma.sync")
+    out = prefill_summary(pre, spec, stream_bytes, hbm)
+    out["note"] = ("b > 8 matvecs on tcgen05.mma kind::i8 (one MMA per 32-element block into TMEM, weights staged "
+                   "by tensor copies); the same bits as the default mma.sync tiles")
+    return out
+
+
 def prefill_config4(pk, path, spec, device):
     """BASELINE config 4 on the device: a 4096-token prompt prefilled in 32-token
     chunks, and the 323 -> 379 extension, whose second call reuses the 320
@@ -515,6 +532,7 @@ def run_ours(args):
 
     cpu = None
     c4 = None
+    pre_tc = None
     streams = None
     c1 = None
     if rank == 0 and world == 1 and not args.decode_only:
@@ -524,6 +542,10 @@ def run_ours(args):
         except Exception as exc:  # noqa: BLE001
             c1 = {"error": str(exc)[:200]}
         c4 = prefill_config4(pk, path, spec, local)  # BASELINE config 4, outside the timed region
+        try:  # the tcgen05 matvec path on the same prefill, outside the timed region
+            pre_tc = prefill_tcgen05_leg(pk, path, spec, local, info["stream_bytes"], peaks()[0])
+        except Exception as exc:  # noqa: BLE001
+            pre_tc = {"error": str(exc)[:200]}
         try:  # the data-parallel streams row, outside the timed region; never fails the line
             streams = streams_summary(pk, synth, path, spec, local)
         except Exception as exc:  # noqa: BLE001
@@ -556,6 +578,7 @@ def run_ours(args):
             "config": dict(workload_config(args, world), order=args.order),
             "prefill_tok_s": pre["prefill_tokens"] / (pre["prefill_ms"] / 1000.0),
             "prefill": dict(prefill_summary(pre, spec, info["stream_bytes"], hbm), **(c4 or {})),
+            "prefill_tcgen05": pre_tc,
             "decode_step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                                 "frac": step_gbs / hbm, "peak": hbm, "peak_kind": peak_kind},
             "roofline": {"bound": "hbm", "kernel": "k_decode", "achieved": achieved, "peak": hbm, "unit": "GB/s",
