@@ -224,6 +224,17 @@ int pk_model_info_get(pk_engine *eng, pk_model_info *info);
 #define PK_ORDER_FAST 1
 int pk_set_order(pk_engine *eng, int order);
 
+/* No counterpart in the reference (its KvCache, model.rs:352-387, is f32; its
+ * README:10,23 dropped an f16 cache): the entry type of the engine's K/V
+ * caches, set after pk_create and before pk_load_gguf.  PK_KV_F16 stores
+ * each K and V value rounded to nearest even, halving the cache (M26: 368,640
+ * instead of 737,280 bytes a position); every later read converts it back
+ * exactly, and all other arithmetic is unchanged.  With f16 entries decode
+ * runs the per-op kernels and attention the per-(token, head) kernel. */
+#define PK_KV_F32 0
+#define PK_KV_F16 1
+int pk_set_kv_type(pk_engine *eng, int type);
+
 /* Engine::forward: invalidates prefix reuse.  ids/positions are host arrays. */
 int pk_forward(pk_engine *eng, const uint32_t *ids, const int *positions, int n, int want_logits);
 /* Copies the last logits (n_vocab floats) to host memory. */

@@ -30,6 +30,7 @@
 #include "pk_oracle.h"
 
 #include <fcntl.h>
+#include <immintrin.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -981,6 +982,13 @@ struct pko_engine {
   std::vector<float> a_d;
   std::vector<int32_t> a_sum;
   bool int8_enabled = true, eog_enabled = true, dbg_on = false;
+  // Not in the reference (its KvCache is f32): store every K / V entry
+  // rounded to f16 (round to nearest even), the B200 library's f16 cache, so
+  // that mode has a bit-exact checker.
+  bool kv_f16 = false;
+  float kv_round(float x) const {
+    return kv_f16 ? _cvtsh_ss(_cvtss_sh(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC)) : x;
+  }
   std::vector<std::pair<std::string, std::vector<float>>> dbg;
   std::vector<uint32_t> kv_tokens;
   bool kv_int8_enabled = true;
@@ -1098,8 +1106,8 @@ struct pko_engine {
         for (size_t h = 0; h < n_kv; h++) {
           size_t base_k = ((l * n_kv + h) * n_ctx + positions[bi]) * dh;
           for (size_t d = 0; d < dh; d++) {
-            kv_k[base_k + d] = k[(h * dh + d) * b + bi];
-            kv_v[base_k + d] = v[(h * dh + d) * b + bi];
+            kv_k[base_k + d] = kv_round(k[(h * dh + d) * b + bi]);
+            kv_v[base_k + d] = kv_round(v[(h * dh + d) * b + bi]);
           }
         }
       for (size_t bi = 0; bi < b; bi++) {  // model.rs:993-1087 (aarch64 build)
@@ -1364,6 +1372,7 @@ pko_engine *pko_engine_load(const char *path, size_t n_ctx, size_t threads, char
 void pko_engine_free(pko_engine *e) { delete e; }
 void pko_engine_set_int8(pko_engine *e, int en) { e->int8_enabled = en != 0; }
 void pko_engine_set_eog(pko_engine *e, int en) { e->eog_enabled = en != 0; }
+void pko_engine_set_kv_f16(pko_engine *e, int on) { e->kv_f16 = on != 0; }
 size_t pko_engine_vocab(pko_engine *e) { return e->vocab; }
 void pko_engine_set_debug(pko_engine *e, int on) { e->dbg_on = on != 0; e->dbg.clear(); }
 

@@ -93,6 +93,9 @@ pko_engine *pko_engine_load(const char *path, size_t n_ctx, size_t threads, char
 void pko_engine_free(pko_engine *e);
 void pko_engine_set_int8(pko_engine *e, int enabled);
 void pko_engine_set_eog(pko_engine *e, int enabled);
+/* K / V cache entries rounded to f16 at store (round to nearest even): the
+ * checker of the B200 library's f16 cache.  The reference keeps f32. */
+void pko_engine_set_kv_f16(pko_engine *e, int on);
 size_t pko_engine_vocab(pko_engine *e);
 /* Engine::forward (public: invalidates prefix reuse).  0 = ok. */
 int pko_forward(pko_engine *e, const uint32_t *ids, const size_t *pos, size_t b, int want_logits,

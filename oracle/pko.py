@@ -59,6 +59,7 @@ def lib():
         L.pko_engine_free.argtypes = [P]
         L.pko_engine_set_int8.argtypes = [P, C.c_int]
         L.pko_engine_set_eog.argtypes = [P, C.c_int]
+        L.pko_engine_set_kv_f16.argtypes = [P, C.c_int]
         L.pko_engine_vocab.argtypes = [P]
         L.pko_engine_vocab.restype = sz
         L.pko_forward.argtypes = [P, P, P, sz, C.c_int, C.c_char_p, sz]
@@ -223,6 +224,10 @@ class Engine:
 
     def set_eog(self, on: bool):
         lib().pko_engine_set_eog(self.h, int(on))
+
+    def set_kv_f16(self, on: bool):
+        """Cache entries rounded to f16 at store (the library's f16 KV mode)."""
+        lib().pko_engine_set_kv_f16(self.h, int(on))
 
     def set_debug(self, on: bool):
         lib().pko_engine_set_debug(self.h, int(on))

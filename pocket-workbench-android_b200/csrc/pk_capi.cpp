@@ -427,6 +427,11 @@ int pk_set_matmul_path(int path) {
   return PK_OK;
 }
 
+int pk_set_kv_type(pk_engine *e, int type) {
+  if (!e) return set_error(PK_ERR_INVALID, "null engine");
+  return e->eng.set_kv_type(type);
+}
+
 int pk_set_order(pk_engine *e, int order) {
   if (!e) return set_error(PK_ERR_INVALID, "null engine");
   return e->eng.set_order(order);

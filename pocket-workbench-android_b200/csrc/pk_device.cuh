@@ -25,6 +25,19 @@ __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b)
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 
+// K/V cache entries: f32, or f16 when H (each value rounded to nearest even
+// at store, converted exactly at load).  i is an element index.
+template <bool H>
+__device__ __forceinline__ float kv_get(const float *base, size_t i) {
+  if (H) return __half2float(reinterpret_cast<const __half *>(base)[i]);
+  return base[i];
+}
+template <bool H>
+__device__ __forceinline__ void kv_put(float *base, size_t i, float v) {
+  if (H) reinterpret_cast<__half *>(base)[i] = __float2half_rn(v);
+  else base[i] = v;
+}
+
 // expf as the C library computes it (the function Rust's f32::exp calls):
 // the published table-driven method -- x * 32/ln2 = k + r with |r| <= 1/2,
 // 2^(k/32) from a 32-entry table, 2^(r/32) from a cubic, all in double with

@@ -274,7 +274,7 @@ int Engine::load(const char *path) {
   // ---- KV cache (model.rs:352-387), f32: V as the reference lays it out,
   // [layer][kv_head][n_ctx][dh]; K d-major, [layer][kv_head][dh][n_ctx], so a
   // run of positions of one dimension is contiguous for the score pass.
-  kv_bytes_ = 2 * (size_t)c.n_layer * c.n_head_kv * n_ctx_ * c.head_dim * 4;
+  kv_bytes_ = 2 * (size_t)c.n_layer * c.n_head_kv * n_ctx_ * c.head_dim * (kv_f16_ ? 2 : 4);
   PK_CK(cudaMalloc((void **)&d_kcache_, kv_bytes_ / 2));
   PK_CK(cudaMalloc((void **)&d_vcache_, kv_bytes_ / 2));
   PK_CK(cudaMemsetAsync(d_kcache_, 0, kv_bytes_ / 2, st_));
@@ -386,6 +386,10 @@ int Engine::setup_decode() {
   const char *env = std::getenv("PK_DECODE");
   if (env && std::strcmp(env, "ops") == 0) {
     decode_why_ = "PK_DECODE=ops";
+    return PK_OK;
+  }
+  if (kv_f16_) {
+    decode_why_ = "f16 KV cache: decode runs the per-op kernels";
     return PK_OK;
   }
   const Config &c = cfg_;
@@ -594,15 +598,15 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, i
   for (int l = 0; l < c.n_layer; l++) {
     if (cancellable && g_stop.load()) return set_error(PK_ERR_STOPPED, "generation stopped");
     const LayerDev &L = layers_[l];
-    float *kc = d_kcache_ + l * layer_kv, *vc = d_vcache_ + l * layer_kv;
-    at.kcache = kc; at.vcache = vc;
+    float *kc = kv_at(d_kcache_, l * layer_kv), *vc = kv_at(d_vcache_, l * layer_kv);
+    at.kcache = kc; at.vcache = vc; at.kv16 = kv_f16_ ? 1 : 0;
     if (b == 1) {
       QkvArgs qa;
       qa.wq = L.q; qa.wk = L.k; qa.wv = L.v;
       qa.src.x = S.x; qa.src.nw = L.attn_norm; qa.src.eps = c.rms_eps;
       qa.pos = S.pos; qa.rope_cos = d_rope_cos_; qa.rope_sin = d_rope_sin_;
       qa.half = c.n_rot / 2; qa.dh = dh; qa.n_ctx = n_ctx_;
-      qa.qout = S.q; qa.kcache = kc; qa.vcache = vc;
+      qa.qout = S.q; qa.kcache = kc; qa.vcache = vc; qa.kv16 = kv_f16_ ? 1 : 0;
       PROF("k_qkv_b1", mat_stream_bytes(L.q) + mat_stream_bytes(L.k) + mat_stream_bytes(L.v) + 2 * ne * f4 +
                            (qdim + 2 * kdim) * f4,
            launch_qkv_b1(qa, S.st));
@@ -630,7 +634,7 @@ int Engine::enqueue_forward(int b, bool want_logits, bool cancellable, int li, i
       PK_CK(launch_mv_multi(3, qkv, a, st));
       if (l == 0) { dump("Qcur-0", S.q, (size_t)b * qdim); dump("Kcur-0", S.k, (size_t)b * kdim); dump("Vcur-0", S.v, (size_t)b * kdim); }
       PK_CK(launch_rope_kv(S.q, S.k, S.v, b, S.pos, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
-                           n_ctx_, kc, vc, st));
+                           n_ctx_, kc, vc, st, 0, kv_f16_));
       if (kv & KV_RECORD) PK_CK(cudaEventRecord(kv_ev_[li][l], st));
       if (l == 0) dump("Qrope-0", S.q, (size_t)b * qdim);
       if (kv & KV_WAIT) PK_CK(cudaStreamWaitEvent(st, kv_ev_[(li + NLANES - 1) % NLANES][l], 0));
@@ -982,6 +986,16 @@ int Engine::decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms
   return PK_OK;
 }
 
+// The K/V cache's entry type, before the model loads (the caches are sized
+// then).  f16 entries are each value rounded to nearest even; attention then
+// runs on the per-(token, head) kernel and decode on the per-op kernels.
+int Engine::set_kv_type(int type) {
+  if (type != PK_KV_F32 && type != PK_KV_F16) return set_error(PK_ERR_INVALID, "unknown KV cache type");
+  if (loaded_) return set_error(PK_ERR_INVALID, "the KV cache type is set before the model loads");
+  kv_f16_ = type == PK_KV_F16;
+  return PK_OK;
+}
+
 int Engine::set_order(int order) {
   if (order != PK_ORDER_EXACT && order != PK_ORDER_FAST) return set_error(PK_ERR_INVALID, "unknown decode order");
   if (order != order_) {
@@ -1049,10 +1063,10 @@ int Engine::stream_prefill(int s, const uint32_t *prompt, int n) {
   for (int i = 0; i < n; i++)
     if (prompt[i] >= (uint32_t)vocab_) return set_error(PK_ERR_INVALID, "token out of vocab");
   PK_CK(cudaSetDevice(device_));
-  const size_t per = kv_bytes_ / 2 / 4;  // floats of one cache
+  const size_t per = (size_t)cfg_.n_layer * cfg_.n_head_kv * n_ctx_ * cfg_.head_dim;  // entries of one cache
   float *k0 = d_kcache_, *v0 = d_vcache_;
-  d_kcache_ = d_sk_ + (size_t)s * per;
-  d_vcache_ = d_sv_ + (size_t)s * per;
+  d_kcache_ = kv_at(d_sk_, (size_t)s * per);
+  d_vcache_ = kv_at(d_sv_, (size_t)s * per);
   kv_tokens_.clear();
   cached_prefill_len_ = 0;
   int rc = PK_OK;
@@ -1092,19 +1106,19 @@ int Engine::enqueue_streams_step() {
   PK_CK(launch_dequant_rows(embd_type_, embd_raw_, embd_row_bytes_, ne, d_sids_, S, x_, st_));
   for (int l = 0; l < c.n_layer; l++) {
     const LayerDev &L = layers_[l];
-    float *kc = d_sk_ + l * layer_kv, *vc = d_sv_ + l * layer_kv;
+    float *kc = kv_at(d_sk_, l * layer_kv), *vc = kv_at(d_sv_, l * layer_kv);
     Q8Dev a = act_;
     a.k = ne; a.b = S;
     PK_CK(launch_rmsnorm_q8(x_, L.attn_norm, c.rms_eps, ne, S, a, nullptr, st_, true));
     const MvOut qkv[3] = {{L.q, q_, 1, qdim, false}, {L.k, k_, 1, kdim, false}, {L.v, v_, 1, kdim, false}};
     PK_CK(launch_mv_multi(3, qkv, a, st_));
     PK_CK(launch_rope_kv(q_, k_, v_, S, d_spos_, d_rope_cos_, d_rope_sin_, c.n_rot / 2, dh, c.n_head, c.n_head_kv,
-                         n_ctx_, kc, vc, st_, stride));
+                         n_ctx_, kc, vc, st_, stride, kv_f16_));
     AttnArgs at{};
     at.q = q_; at.kcache = kc; at.vcache = vc; at.pos = d_spos_; at.out = attn_; at.b = S;
     at.n_head = c.n_head; at.n_kv = c.n_head_kv; at.dh = dh; at.n_ctx = n_ctx_;
     at.scale = 1.0f / sqrtf((float)dh); at.scores = att_scores_;
-    at.lane_stride = stride; at.b1_order = 1;
+    at.lane_stride = stride; at.b1_order = 1; at.kv16 = kv_f16_ ? 1 : 0;
     at.pmax = d_spmax_; at.pchunk = spchunk_;
     a.k = qdim;
     at.q8 = a;

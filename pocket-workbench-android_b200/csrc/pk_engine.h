@@ -55,6 +55,7 @@ class Engine {
   int decode_steps_device(int n_steps, uint32_t *out_ids, float *device_ms);
   int set_position(int pos);
   int set_order(int order);
+  int set_kv_type(int type);
   // Independent streams, each with its own KV cache, decoded together.
   int streams_begin(int n_streams);
   int stream_prefill(int s, const uint32_t *prompt, int n);
@@ -145,6 +146,11 @@ class Engine {
   // persistent decode kernel (pk_decode.cu): plan, device tables and args
   bool use_decode_ = false;
   int order_ = PK_ORDER_EXACT;  // float order of the b = 1 decode step (pk_set_order)
+  bool kv_f16_ = false;         // f16 K/V cache entries (pk_set_kv_type, before the model loads)
+  // base + elems cache entries (f32 or f16), as the caches' float pointer type
+  float *kv_at(float *base, size_t elems) const {
+    return reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(base) + elems * (kv_f16_ ? 2 : 4));
+  }
   std::string decode_why_;
   DecodePlan plan_;
   DecodeArgs dargs_{};

@@ -588,9 +588,15 @@ __global__ void __launch_bounds__(B1_THREADS) k_qkv_b1(QkvArgs a) {
         if ((d & 1) == 0) o = fsub(fmul(val, c), fmul(m.xv[tid + 1], s));
         else o = fadd(fmul(m.xv[tid - 1], s), fmul(val, c));
       }
+      const size_t ki = ((size_t)hd * a.dh + d) * a.n_ctx + pos, vi = ((size_t)hd * a.n_ctx + pos) * a.dh + d;
       if (seg == 0) a.qout[r] = o;
-      else if (seg == 1) a.kcache[((size_t)hd * a.dh + d) * a.n_ctx + pos] = o;  // K is d-major
-      else a.vcache[((size_t)hd * a.n_ctx + pos) * a.dh + d] = o;
+      else if (a.kv16) {
+        if (seg == 1) kv_put<true>(a.kcache, ki, o);  // K is d-major
+        else kv_put<true>(a.vcache, vi, o);
+      } else {
+        if (seg == 1) a.kcache[ki] = o;
+        else a.vcache[vi] = o;
+      }
     }
     __syncthreads();
   }
@@ -1144,7 +1150,8 @@ cudaError_t launch_mv_lanes(const DevTensor &w, const Q8Dev &act, float *out, lo
 // place; the rest write one K element (rotated) and one V element to the
 // cache.  grid = (b, element blocks).
 __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *pos, const float *rc, const float *rs,
-                          int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc, size_t lane_stride) {
+                          int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc, size_t lane_stride,
+                          int kv16) {
   pdl_trigger();
   pdl_wait();
   const int bi = blockIdx.x;
@@ -1162,8 +1169,7 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
     return;
   }
   const int e = i - nq, h = e / dh, d = e - h * dh;
-  kc += (size_t)bi * lane_stride;  // this token's own cache when every token has one
-  vc += (size_t)bi * lane_stride;
+  const size_t ls = (size_t)bi * lane_stride;  // this token's own cache when every token has one
   const float *kr = k + (long)bi * kdim;
   float o = kr[e];
   if (d < 2 * half) {
@@ -1172,16 +1178,23 @@ __global__ void k_rope_kv(float *q, const float *k, const float *v, const int *p
     if ((d & 1) == 0) o = fsub(fmul(kr[e], c), fmul(kr[e + 1], s));
     else o = fadd(fmul(kr[e - 1], s), fmul(kr[e], c));
   }
-  kc[((size_t)h * dh + d) * n_ctx + p] = o;  // K is d-major: [kv head][d][position]
-  vc[((size_t)h * n_ctx + p) * dh + d] = v[(long)bi * kdim + e];
+  const size_t ki = ls + ((size_t)h * dh + d) * n_ctx + p, vi = ls + ((size_t)h * n_ctx + p) * dh + d;
+  const float vv = v[(long)bi * kdim + e];
+  if (kv16) {  // K is d-major: [kv head][d][position]
+    kv_put<true>(kc, ki, o);
+    kv_put<true>(vc, vi, vv);
+  } else {
+    kc[ki] = o;
+    vc[vi] = vv;
+  }
 }
 
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rc,
                            const float *rs, int half, int dh, int n_head, int n_kv, int n_ctx, float *kc, float *vc,
-                           cudaStream_t st, size_t lane_stride) {
+                           cudaStream_t st, size_t lane_stride, bool kv16) {
   const int total = n_head * half + n_kv * dh;
   return launch(k_rope_kv, dim3(b, (total + 127) / 128), dim3(128), 0, st, q, k, v, pos, rc, rs, half, dh, n_head,
-                n_kv, n_ctx, kc, vc, lane_stride);
+                n_kv, n_ctx, kc, vc, lane_stride, kv16 ? 1 : 0);
 }
 
 __global__ void k_expf(const float *x, float *out, long n) {
@@ -1209,6 +1222,7 @@ cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st) {
 // Every thread below dh owns one d and runs its chain over p; one more
 // thread runs the sum chain.  Scores live in the per-(token, head) scratch
 // row, so any context length fits.
+template <bool KV16>
 __global__ void k_attn(AttnArgs a, int dot8) {
   __shared__ float qs[256];
   __shared__ float red[40];
@@ -1221,27 +1235,27 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   const long hb = (long)bi * a.n_head + h;
   for (int d = tid; d < dh; d += blockDim.x) qs[d] = a.q[hb * dh + d];
   __syncthreads();
-  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * dh;
-  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * dh;
+  // element offsets of this token's and head's K and V (f32 or f16 entries)
+  const size_t kb = (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * dh, vb = kb;
   float *sc = a.scores + hb * a.n_ctx;
   float mx = -INFINITY;
   const size_t nc = (size_t)a.n_ctx;
   for (int p = tid; p <= pos; p += blockDim.x) {
-    const float *kcol = kb + p;  // K is d-major: element d of position p at kcol[d * n_ctx]
+    const size_t kcol = kb + p;  // K is d-major: element d of position p at kcol + d * n_ctx
     float s;
     if (dot8) {
       float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       int d = 0;
       for (; d + 8 <= dh; d += 8) {
 #pragma unroll
-        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], kcol[(size_t)(d + u) * nc]));
+        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], kv_get<KV16>(a.kcache, kcol + (size_t)(d + u) * nc)));
       }
       s = fadd(fadd(c[0], c[1]), fadd(c[2], c[3]));
       s = fadd(s, fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
-      for (; d < dh; d++) s = fadd(s, fmul(qs[d], kcol[(size_t)d * nc]));
+      for (; d < dh; d++) s = fadd(s, fmul(qs[d], kv_get<KV16>(a.kcache, kcol + (size_t)d * nc)));
     } else {
       s = 0.0f;
-      for (int d = 0; d < dh; d++) s = fadd(s, fmul(qs[d], kcol[(size_t)d * nc]));
+      for (int d = 0; d < dh; d++) s = fadd(s, fmul(qs[d], kv_get<KV16>(a.kcache, kcol + (size_t)d * nc)));
     }
     s = fmul(s, a.scale);
     sc[p] = s;
@@ -1252,11 +1266,11 @@ __global__ void k_attn(AttnArgs a, int dot8) {
   __syncthreads();
   float acc = 0.0f;
   if (tid < dh) {
-    const float *vr = vb + tid;
+    const size_t vr = vb + tid;
 #pragma unroll 8
     for (int p = 0; p <= pos; p++) {
       const float e = sc[p];
-      const float v = vr[(size_t)p * dh];
+      const float v = kv_get<KV16>(a.vcache, vr + (size_t)p * dh);
       if (e != 0.0f) acc = fadd(acc, fmul(e, v));
     }
   }
@@ -1726,6 +1740,10 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
 }
 
 static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
+  if (a.kv16) {  // f16 cache entries: the per-(token, head) kernel, in either order
+    const bool dot8 = a.b == 1 || a.b1_order;
+    return launch(k_attn<true>, dim3(a.n_head, a.b), dim3(a.dh < 128 ? 128 : 256), 0, st, a, dot8 ? 1 : 0);
+  }
   if (a.b > 1 && !a.b1_order && a.lane_stride == 0 && a.n_ctx % 4 == 0 &&
       (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
     const size_t smem = ac_smem(a.dh);
@@ -1760,7 +1778,7 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
     return launch(kern, dim3(a.n_head, a.b), dim3(a.dh == 64 ? 128 : 256), smem, st, a);
   }
   const int threads = a.dh < 128 ? 128 : 256;
-  return launch(k_attn, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, dot8 ? 1 : 0);
+  return launch(k_attn<false>, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, dot8 ? 1 : 0);
 }
 
 // ------------------------------------------------------------ temperature / top-p sampling

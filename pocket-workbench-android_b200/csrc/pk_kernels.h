@@ -98,6 +98,7 @@ struct QkvArgs {
   float *qout = nullptr;   // [n_head * dh]
   float *kcache = nullptr; // this layer: K d-major [n_kv][dh][n_ctx]
   float *vcache = nullptr;
+  int kv16 = 0;            // 1: the caches hold f16 entries (same element offsets)
 };
 cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st);
 // Fused gate/up matvecs + SwiGLU (model.rs:1105-1115) for one token.
@@ -105,9 +106,10 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
                              cudaStream_t st);
 
 // RoPE + KV write for b tokens (token-major q [b][qdim], k/v [b][kdim]).
+// kv16: the caches hold f16 entries (each value rounded to nearest even).
 cudaError_t launch_rope_kv(float *q, const float *k, const float *v, int b, const int *pos, const float *rope_cos,
                            const float *rope_sin, int half, int dh, int n_head, int n_kv, int n_ctx, float *kcache,
-                           float *vcache, cudaStream_t st, size_t lane_stride = 0);
+                           float *vcache, cudaStream_t st, size_t lane_stride = 0, bool kv16 = false);
 // out[i] = expf_lib(x[i]) (the C library's expf, bit for bit).
 cudaError_t launch_expf(const float *x, float *out, long n, cudaStream_t st);
 
@@ -122,8 +124,9 @@ struct AttnArgs {
   float scale;
   float *scores;       // scratch [b][n_head][n_ctx]
   Q8Dev q8{};          // optional (q8.q != nullptr): Q8 of out, k = n_head * dh
-  size_t lane_stride = 0;  // floats from token i's K/V cache to token i + 1's (0: one shared cache)
+  size_t lane_stride = 0;  // elements from token i's K/V cache to token i + 1's (0: one shared cache)
   int b1_order = 0;        // 1: every token scored in the b == 1 order (simd.rs:19-43), one CTA each
+  int kv16 = 0;            // 1: the caches hold f16 entries (k_attn, one CTA per token and head)
   // b == 1 order over long histories: pchunk positions per scoring CTA (a
   // multiple of 128) and pmax scratch [b][n_head][ceil(n_ctx / pchunk)] for
   // their maxima; then the value pass runs one CTA per (token, head, 32 d).

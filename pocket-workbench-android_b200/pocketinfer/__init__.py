@@ -29,6 +29,7 @@ PK_ERR = {1: "PK_ERR_INVALID", 2: "PK_ERR_UNSUPPORTED", 3: "PK_ERR_CUDA", 4: "PK
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
 ORDER_EXACT, ORDER_FAST = 0, 1  # pk_set_order
 MATMUL_MMA_SYNC, MATMUL_TCGEN05 = 0, 1  # pk_set_matmul_path
+KV_F32, KV_F16 = 0, 1  # pk_set_kv_type
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 
 # Every function include/pk.h declares (checked by tests/test_capi_symbols.py).
@@ -36,7 +37,7 @@ SYMBOLS = [
     "pk_last_error", "pk_version", "pk_device_binary_version", "pk_supports", "pk_expf", "pk_q8_quantize", "pk_matmul", "pk_matmul_noalloc", "pk_packed_bytes",
     "pk_pack_weights", "pk_matmul_packed", "pk_set_matmul_path", "pk_backend_new", "pk_backend_free", "pk_backend_selftest",
     "pk_backend_supports", "pk_backend_matvec", "pk_create", "pk_load_gguf", "pk_destroy", "pk_model_info_get",
-    "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position", "pk_set_order",
+    "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position", "pk_set_order", "pk_set_kv_type",
     "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
     "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
     "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
@@ -125,7 +126,7 @@ def lib():
         "pk_forward": ([P, P, P, I, I], I), "pk_logits": ([P, P, I], I),
         "pk_argmax": ([P, C.POINTER(U32)], I),
         "pk_generate": ([P, P, I, C.POINTER(GenOpts), TOKEN_CB, P, P, I, C.POINTER(I), C.POINTER(GenStats)], I),
-        "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_matmul_path": ([I], I), "pk_set_position": ([P, I], I), "pk_set_order": ([P, I], I),
+        "pk_decode_steps_device": ([P, I, P, C.POINTER(C.c_float)], I), "pk_set_matmul_path": ([I], I), "pk_set_position": ([P, I], I), "pk_set_order": ([P, I], I), "pk_set_kv_type": ([P, I], I),
         "pk_streams_begin": ([P, I], I), "pk_stream_prefill": ([P, I, P, I], I),
         "pk_streams_decode": ([P, I, P, C.POINTER(C.c_float)], I), "pk_streams_set_position": ([P, I], I),
         "pk_decode_profile": ([P, C.POINTER(KernelStat), I, C.POINTER(I)], I), "pk_set_debug": ([P, I], I),
@@ -321,13 +322,15 @@ class Engine:
     """Engine::load / forward / logits / generate on one GPU."""
 
     def __init__(self, path: str | None = None, n_ctx: int = 512, max_batch: int = 32, device: int = 0,
-                 order: str | None = None):
+                 order: str | None = None, kv: str = "f32"):
         h = C.c_void_p()
         _check(lib().pk_create(device, n_ctx, max_batch, C.byref(h)))
         self.h = h
         self.n_ctx = n_ctx
         if order is not None:
             self.set_order(order)
+        if kv != "f32":  # "f16": f16 K/V cache entries (pk_set_kv_type), before the load
+            _check(lib().pk_set_kv_type(self.h, {"f32": KV_F32, "f16": KV_F16}[kv]))
         if path is not None:
             self.load(path)
 

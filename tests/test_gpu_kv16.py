@@ -1,0 +1,73 @@
+"""The f16 K/V cache option (pk_set_kv_type(PK_KV_F16)) against the CPU
+oracle with the same option (pko_engine_set_kv_f16): every K and V value is
+rounded to f16 (nearest even) when stored and converted back exactly when
+read, and all other arithmetic is the reference's, so logits and greedy
+tokens are the oracle's bits.  The reference itself keeps an f32 cache
+(model.rs:352-387); this is a B200 option, checked against the reference's
+arithmetic over f16-rounded cache entries."""
+import os
+
+import numpy as np
+import pytest
+
+from pocketinfer import synth
+
+pytestmark = pytest.mark.gpu
+THREADS = max(1, min(32, os.cpu_count() or 1))
+MODELS = {"tiny": synth.TINY, "q8down": synth.SMALL_Q8DOWN, "q40": synth.SMALL_Q40}
+
+
+@pytest.fixture(scope="module")
+def paths(tmp_path_factory):
+    d = tmp_path_factory.mktemp("kv16")
+    out = {}
+    for name, spec in MODELS.items():
+        out[name] = str(d / f"{name}.gguf")
+        synth.write_gguf(out[name], spec, seed=33)
+    return out
+
+
+def oracle_f16(oracle, path, n_ctx=256):
+    o = oracle.Engine(path, n_ctx, THREADS)
+    o.set_kv_f16(True)
+    return o
+
+
+@pytest.mark.parametrize("name", list(MODELS))
+def test_kv16_prefill_and_decode_match_oracle(pk, oracle, paths, name):
+    """A 77-token prompt (three chunks), then greedy tokens: the same logits
+    and token ids as the oracle's f16-cache engine, bit for bit."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(19, 77, spec.n_vocab)
+    g = pk.Engine(paths[name], n_ctx=256, kv="f16")
+    o = oracle_f16(oracle, paths[name])
+    rg = g.generate(prompt, 40, stop_at_eog=False)
+    ro = o.generate(prompt, 40)
+    assert rg["gen_ids"] == ro["gen_ids"]
+    assert np.array_equal(g.logits().view(np.uint32), o.logits().view(np.uint32))
+    # the f16 cache is half the f32 one
+    f32 = pk.Engine(paths[name], n_ctx=256)
+    assert g.model_info()["kv_bytes"] * 2 == f32.model_info()["kv_bytes"]
+
+
+@pytest.mark.parametrize("name", ["tiny", "q8down"])
+def test_kv16_streams_match_oracle(pk, oracle, paths, name):
+    """Independent streams over f16 caches, decoded in one batched step per
+    token: each stream's tokens are the oracle's f16-cache tokens for it."""
+    spec = MODELS[name]
+    prompts = [synth.prompt_ids(51 + i, n, spec.n_vocab) for i, n in enumerate((1, 20, 45))]
+    want = [oracle_f16(oracle, paths[name]).generate(p, 24)["gen_ids"] for p in prompts]
+    e = pk.Engine(paths[name], n_ctx=256, kv="f16")
+    e.streams_begin(len(prompts))
+    for s, p in enumerate(prompts):
+        e.stream_prefill(s, p)
+    got = e.streams_decode(24)
+    for s in range(len(prompts)):
+        assert got[s] == want[s]
+
+
+def test_kv16_set_after_load_is_rejected(pk, paths):
+    """The caches are sized at load, so the entry type can only change before it."""
+    g = pk.Engine(paths["tiny"], n_ctx=128)
+    assert pk.lib().pk_set_kv_type(g.h, pk.KV_F16) != 0
+    assert pk.lib().pk_set_kv_type(None, pk.KV_F16) != 0
