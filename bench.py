@@ -55,11 +55,17 @@ def parse_args():
     p.add_argument("--streams", type=int, default=0,
                    help="independent M26 streams per GPU decoded together (the data-parallel streams case)")
     p.add_argument("--stream-ctx", type=int, default=512, help="KV positions of each stream")
+    p.add_argument("--stream-prompt", type=int, default=None,
+                   help="prompt tokens prefilled into each stream's cache (default 323)")
+    p.add_argument("--kv", choices=("f32", "f16"), default="f32",
+                   help="K/V cache entry type of the streams case (pk_set_kv_type)")
     p.add_argument("--stream-pos", type=int, default=None,
                    help="decode the streams at this position (past the prompt: zero-filled cache entries; "
                         "the long-context timing case)")
     p.add_argument("--prefill-only", action="store_true",
                    help="only the prefill leg (warm-up prompt, then the measured 323-token prompt); prints its summary")
+    p.add_argument("--config1-only", action="store_true",
+                   help="only BASELINE config 1 (one Q4_K 6144x2048 matvec, rotating weight copies); prints its summary")
     p.add_argument("--decode-only", action="store_true",
                    help="only the timed decode (with its traced profile and e2e): no prefill, streams, config-1 "
                         "or CPU legs")
@@ -279,9 +285,12 @@ def oracle_decode(path, prompt, warmup, steps, budget_s):
 
 def config1_matvec(pk, synth, device, copies=40, launches=400):
     """one Q4_K 6144 x 2048 matvec (seed 0) against the Q8 of
-    x ~ N(0,1), timed over `launches` back-to-back launches that rotate over
-    `copies` distinct weight copies (40 x 7.08 MB = 283 MB > 2 x the 126 MB
-    L2), CUDA events on the launching stream.  Bytes per launch: the weights,
+    x ~ N(0,1), timed over `launches` launches that rotate over `copies`
+    distinct weight copies (40 x 7.08 MB = 283 MB > 2 x the 126 MB L2), CUDA
+    events on the launching stream.  The launches are captured in one CUDA
+    graph and replayed, so the time is the device's: one pk_matmul_packed call
+    issued from Python costs more host time than the kernel takes, and the
+    host-issued rate is reported beside it.  Bytes per launch: the weights,
     the Q8 activation (q, d, sum) and the f32 output."""
     import torch
 
@@ -291,22 +300,40 @@ def config1_matvec(pk, synth, device, copies=40, launches=400):
     ws = [wd.clone() for _ in range(copies)]  # Q4_K: the device layout is the GGUF layout
     act = pk.q8_quantize(torch.from_numpy(x).to(device), k, 1)
     out = torch.empty(rows, dtype=torch.float32, device=device)
-    for i in range(2 * copies):  # warm-up
-        pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.Stream(device)
+    with torch.cuda.stream(st):
+        for i in range(2 * copies):  # warm-up
+            pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out, stream=st.cuda_stream)
     torch.cuda.synchronize()
-    e0.record()
-    for i in range(launches):
-        pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out)
-    e1.record()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(launches):
+            pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out, stream=st.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / launches
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record()
+    for i in range(launches):
+        pk.matmul_packed(synth.Q4_K, ws[i % copies], k, rows, act, out=out)
+    h1.record()
+    torch.cuda.synchronize()
+    us_host = h0.elapsed_time(h1) * 1000.0 / launches
+    del graph
     nbytes = w.nbytes + k + 2 * 4 * (k // 32) + 4 * rows
     hbm, kind = peaks()
     return {"shape": "Q4_K 6144x2048, b=1", "us_per_launch": us, "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "hbm_frac": nbytes / (us * 1e-6) / 1e9 / hbm,
             "peak_kind": kind, "weight_copies": copies, "launches": launches,
-            "note": "k_mv_b1 (pk_matmul_packed), back-to-back launches rotating over distinct weight copies"}
+            "us_per_launch_host_issued": us_host,
+            "note": "k_mv_b1 (pk_matmul_packed), launches rotating over distinct weight copies, replayed from one "
+                    "CUDA graph (us_per_launch_host_issued: the same launches issued one by one from Python)"}
 
 
 def nccl_allreduce_us(dist, n, iters=200, warmup=20):
@@ -727,14 +754,17 @@ def run_streams(args):
     path = synth.m26_path(args.model_dir, spec=spec)
     mine = replicas.assign_streams(args.streams * world, rank, world)
     n_ctx = args.stream_ctx
-    p0 = args.stream_pos or PROMPT_LEN
-    if p0 < PROMPT_LEN or p0 + CYCLE > n_ctx:
-        raise SystemExit(f"need {PROMPT_LEN} <= --stream-pos and --stream-pos + {CYCLE} <= --stream-ctx")
-    eng = pk.Engine(path, n_ctx=n_ctx, max_batch=max(32, len(mine)), device=local)
+    plen = args.stream_prompt or PROMPT_LEN
+    p0 = args.stream_pos or plen
+    if p0 < plen or p0 + CYCLE > n_ctx:
+        raise SystemExit(f"need --stream-prompt <= --stream-pos and --stream-pos + {CYCLE} <= --stream-ctx")
+    eng = pk.Engine(path, n_ctx=n_ctx, max_batch=max(32, len(mine)), device=local, kv=args.kv)
     info = eng.info
     eng.streams_begin(len(mine))
+    t0 = time.time()
     for s, sid in enumerate(mine):  # every stream its own prompt, prefilled into its own cache
-        eng.stream_prefill(s, synth.prompt_ids(1000 + sid, PROMPT_LEN, spec.n_vocab))
+        eng.stream_prefill(s, synth.prompt_ids(1000 + sid, plen, spec.n_vocab))
+    prefill_s = time.time() - t0
 
     def cycle(n):
         total, done, pos = 0.0, 0, p0
@@ -776,7 +806,8 @@ def run_streams(args):
     if rank == 0:
         hbm, peak_kind = peaks()
         mean_pos = p0 + 1 + min(args.steps, CYCLE) / 2
-        step_bytes = info["stream_bytes"] + len(mine) * spec.kv_bytes_per_position() * mean_pos
+        kv_pos_bytes = spec.kv_bytes_per_position() // (2 if args.kv == "f16" else 1)
+        step_bytes = info["stream_bytes"] + len(mine) * kv_pos_bytes * mean_pos
         gbs = step_bytes / (ms_step / 1000.0) / 1e9
         line = {
             "metric": f"decode tok/s (2.6B Q4_K_M, {len(mine)} streams per GPU, batched)", "value": value,
@@ -784,12 +815,13 @@ def run_streams(args):
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xint8->int32, f32", "data": "synthetic",
             "config": {"workload": f"M26, {args.streams * world} independent greedy streams, {len(mine)} per GPU, "
-                                   f"{PROMPT_LEN}-token prompts, positions {p0}..{p0 + CYCLE} "
-                                   f"(rewound every {CYCLE} tokens), n_ctx {n_ctx} per stream"
-                                   + ("" if p0 == PROMPT_LEN else
-                                      f"; cache entries {PROMPT_LEN}..{p0 - 1} zero-filled (timing case)"),
-                       "model": spec.name, "parallelism": f"dp{world} (streams)",
+                                   f"{plen}-token prompts, positions {p0}..{p0 + CYCLE} "
+                                   f"(rewound every {CYCLE} tokens), n_ctx {n_ctx} per stream, {args.kv} K/V cache"
+                                   + ("" if p0 == plen else
+                                      f"; cache entries {plen}..{p0 - 1} zero-filled (timing case)"),
+                       "model": spec.name, "parallelism": f"dp{world} (streams)", "kv": args.kv,
                        "l2": "weights (1.5 GB) and caches exceed L2"},
+            "prefill_s_per_gpu": prefill_s,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "peak_kind": peak_kind, "bytes_per_step": step_bytes},
             "clocks": clk,
@@ -808,6 +840,13 @@ def main():
         run_streams(args)
     elif args.tp70:
         run_tp70(args)
+    elif args.config1_only:
+        import torch
+
+        import pocketinfer as pk
+        from pocketinfer import synth
+
+        print(json.dumps({"config1": config1_matvec(pk, synth, torch.device("cuda", 0))}), flush=True)
     else:
         run_ours(args)
 

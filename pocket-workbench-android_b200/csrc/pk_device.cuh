@@ -37,6 +37,17 @@ __device__ __forceinline__ void kv_put(float *base, size_t i, float v) {
   if (H) reinterpret_cast<__half *>(base)[i] = __float2half_rn(v);
   else base[i] = v;
 }
+// One staged cache element as f32, and four consecutive ones (p aligned to
+// four elements), for kernels templated on the entry type.
+__device__ __forceinline__ float kv_f(float v) { return v; }
+__device__ __forceinline__ float kv_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float4 kv_f4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 kv_f4(const __half *p) {
+  const uint2 u = *reinterpret_cast<const uint2 *>(p);
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
 
 // expf as the C library computes it (the function Rust's f32::exp calls):
 // the published table-driven method -- x * 32/ln2 = k + r with |r| <= 1/2,
@@ -46,7 +57,11 @@ __device__ __forceinline__ void kv_put(float *base, size_t i, float v) {
 // coefficients are the method's minimax constants.  This evaluation returns
 // the same bits as the host C library for every non-NaN float (checked over
 // all 2^32 inputs), which the parity of softmax and SwiGLU depends on.
-static __constant__ unsigned long long kExp2Tab[32] = {
+// The table is global memory read through the read-only data cache: the
+// lanes of a warp index it with unrelated k, and a constant-bank read would
+// be replayed once per distinct entry, where the L1 serves all 32 entries
+// (256 bytes) in two wavefronts.
+static __device__ const unsigned long long kExp2Tab[32] = {
     0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
     0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
     0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
@@ -69,7 +84,7 @@ __device__ __forceinline__ float expf_lib(float x) {
   const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
   kd = __dsub_rn(kd, kShift);
   const double r = __fma_rn(kInvLn2N, xd, -kd);
-  const double s = __longlong_as_double((long long)(kExp2Tab[ki & 31] + (ki << 47)));
+  const double s = __longlong_as_double((long long)(__ldg(&kExp2Tab[ki & 31]) + (ki << 47)));
   const double z = __fma_rn(kC0, r, kC1);
   const double r2 = __dmul_rn(r, r);
   double y = __fma_rn(kC2, r, 1.0);

@@ -23,6 +23,8 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "pk_device.cuh"
 #include "pk_quant.cuh"
@@ -220,9 +222,12 @@ __device__ float block_max(float v, float *red) {
   return red[32];
 }
 
+// A launch gets 48 KB of shared memory, static and dynamic together, unless
+// the kernel opts in to more.  The kernels here declare at most 1.2 KB of
+// static arrays, so any dynamic size above 44 KB opts in.
 template <typename K>
 static cudaError_t set_smem(K kernel, size_t smem) {
-  if (smem > 48 * 1024) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 44 * 1024) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   return cudaSuccess;
 }
 
@@ -261,7 +266,8 @@ __device__ float sum_sq_neon(const float *__restrict__ x, int n, float *red) {
   const int tid = threadIdx.x, n8 = n / 8 * 8;
   if (tid < 8) {
     float acc = 0.0f;
-#pragma unroll 8
+    // unrolled so the loads of 32 steps are issued ahead of their FMAs
+#pragma unroll 32
     for (int i = tid; i < n8; i += 8) acc = __fmaf_rn(x[i], x[i], acc);
     red[tid] = acc;
   }
@@ -308,25 +314,35 @@ __device__ float sum_sq_chain(const float *sq, int n, float *red) {
 // RMSNorm of token-major x [b][k] (model.rs:812-822) followed by Q8.  The
 // token's row, the norm weights and the squares are staged in shared
 // memory (dynamic, 3 x k floats, k a multiple of 32); each warp then
-// quantises its blocks three at a time.
+// quantises its blocks three at a time.  The weights are constant, so they
+// are staged before the wait for the kernel that writes x.
 __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restrict__ nw, float eps, int k, Q8Dev act,
                              float *__restrict__ xn, int neon) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[40];
-  const int n16 = (k + 15) & ~15;
-  float *ws = xs + n16, *sq = ws + n16;
-  pdl_trigger();
-  pdl_wait();
-  const int bi = blockIdx.x;
+  float *ws = xs + k, *sq = ws + k;
+  const int bi = blockIdx.x, n4 = k / 4;
   const float4 *x4 = reinterpret_cast<const float4 *>(x + (long)bi * k), *w4 = reinterpret_cast<const float4 *>(nw);
-  for (int i = threadIdx.x; i < n16 / 4; i += blockDim.x) {
-    const bool in = 4 * i < k;
-    const float4 v = in ? x4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (in) {
-      reinterpret_cast<float4 *>(xs)[i] = v;
-      reinterpret_cast<float4 *>(ws)[i] = w4[i];
+  pdl_trigger();
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) reinterpret_cast<float4 *>(ws)[i] = w4[i];
+  pdl_wait();
+  constexpr int U = 4;  // every load of the row in flight before the first store
+  for (int i0 = threadIdx.x; i0 < n4; i0 += U * blockDim.x) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = i0 + u * blockDim.x;
+      v[u] = i < n4 ? x4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    reinterpret_cast<float4 *>(sq)[i] = make_float4(fmul(v.x, v.x), fmul(v.y, v.y), fmul(v.z, v.z), fmul(v.w, v.w));
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = i0 + u * blockDim.x;
+      if (i < n4) {
+        reinterpret_cast<float4 *>(xs)[i] = v[u];
+        reinterpret_cast<float4 *>(sq)[i] =
+            make_float4(fmul(v[u].x, v[u].x), fmul(v[u].y, v[u].y), fmul(v[u].z, v[u].z), fmul(v[u].w, v[u].w));
+      }
+    }
   }
   __syncthreads();
   const float ss = neon ? sum_sq_neon(xs, k, red) : sum_sq_chain(sq, k, red);
@@ -356,7 +372,7 @@ __global__ void k_rmsnorm_q8(const float *__restrict__ x, const float *__restric
 cudaError_t launch_rmsnorm_q8(const float *x, const float *nw, float eps, int k, int b, Q8Dev act, float *xn,
                               cudaStream_t st, bool neon) {
   if (k % 32 != 0 || ((uintptr_t)x | (uintptr_t)nw) % 16 != 0) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)3 * ((k + 15) & ~15) * 4;
+  const size_t smem = (size_t)3 * k * 4;
   cudaError_t e = set_smem(k_rmsnorm_q8, smem);
   if (e != cudaSuccess) return e;
   return launch(k_rmsnorm_q8, dim3(b), dim3(256), smem, st, x, nw, eps, k, act, xn, neon ? 1 : 0);
@@ -396,26 +412,42 @@ cudaError_t launch_swiglu_q8(const float *g, const float *u, int k, int b, Q8Dev
 constexpr int B1_THREADS = 256;
 constexpr int B1_RT = 16;   // rows per tile
 constexpr int B1_TW = 256;  // terms per wave per row
+constexpr int B1_MIN_CTAS = 3;  // resident CTAs per SM the register budget must allow
 
 // Rows [r0, r0+nr) of W against one activation held in shared memory.
-// Returns the row's reference-ordered sum in threads [0, nr).
+// Returns the row's reference-ordered sum in threads [0, nr).  Each thread
+// issues the weight loads of U items before it computes any of them (an
+// item past the end loads a valid one again and stores nothing), so a wave
+// waits for about one global round trip instead of one per item.
 template <int T>
 __device__ float tile_b1(const DevTensor &W, int r0, int nr, const ActRef &A, float *Tsm) {
   constexpr int GE = Geo<T>::GE, TPG = Geo<T>::TPG, GW = B1_TW / TPG;
+  constexpr int U = TPG == 1 ? 4 : 2;
   const int G = W.k / GE;
   const int tid = threadIdx.x;
   float acc = 0.0f;
   for (int g0 = 0; g0 < G; g0 += GW) {
     const int gw = min(GW, G - g0);
     const int items = nr * gw;
-    for (int it = tid; it < items; it += B1_THREADS) {
-      const int rl = it / gw, gl = it - rl * gw;
-      GroupW<T> gwt;
-      gwt.load(W, r0 + rl, g0 + gl);
-      float t[TPG];
-      gwt.terms(A, t);
+    for (int it0 = tid; it0 < items; it0 += U * B1_THREADS) {
+      GroupW<T> gwt[U];
 #pragma unroll
-      for (int s = 0; s < TPG; s++) Tsm[(gl * TPG + s) * B1_RT + rl] = t[s];
+      for (int u = 0; u < U; u++) {
+        const int it = min(it0 + u * B1_THREADS, items - 1);
+        const int rl = it / gw, gl = it - rl * gw;
+        gwt[u].load(W, r0 + rl, g0 + gl);
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int it = it0 + u * B1_THREADS;
+        if (it < items) {
+          const int rl = it / gw, gl = it - rl * gw;
+          float t[TPG];
+          gwt[u].terms(A, t);
+#pragma unroll
+          for (int s = 0; s < TPG; s++) Tsm[(gl * TPG + s) * B1_RT + rl] = t[s];
+        }
+      }
     }
     __syncthreads();
     if (tid < nr) {
@@ -514,7 +546,7 @@ __device__ void act_prologue(const B1Src &src, int k, const B1Smem &m) {
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(B1_THREADS) k_mv_b1(DevTensor W, B1Src src, float *__restrict__ out, int add) {
+__global__ void __launch_bounds__(B1_THREADS, B1_MIN_CTAS) k_mv_b1(DevTensor W, B1Src src, float *__restrict__ out, int add) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tiles = (W.rows + B1_RT - 1) / B1_RT;
   if (threadIdx.x == 0)  // weights are constant: stream them in while the previous kernel runs
@@ -527,6 +559,8 @@ __global__ void __launch_bounds__(B1_THREADS) k_mv_b1(DevTensor W, B1Src src, fl
   const ActRef A{m.q, m.d, m.s};
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = t * B1_RT, nr = min(B1_RT, W.rows - r0);
+    const int tn = t + 2 * gridDim.x;  // two tiles ahead of this CTA's current one
+    if (threadIdx.x == 0 && tn < tiles) prefetch_rows(W, tn * B1_RT, min(B1_RT, W.rows - tn * B1_RT));
     const float acc = tile_b1_any(W, r0, nr, A, m.T);
     if ((int)threadIdx.x < nr) {
       const float v = fadd(0.0f, acc);  // Pool::matmul zero-fills, then out += acc
@@ -536,9 +570,25 @@ __global__ void __launch_bounds__(B1_THREADS) k_mv_b1(DevTensor W, B1Src src, fl
   }
 }
 
-static int b1_grid(int tiles, size_t smem) {
-  // Resident CTAs per SM bound by the 228 KB shared memory and 2048 threads.
-  int per_sm = (int)std::min<size_t>(8, std::max<size_t>(1, (227 * 1024) / std::max<size_t>(smem, 1)));
+// One CTA per tile, at most as many as fit on the GPU at once (the kernel's
+// registers and shared memory, from the occupancy calculator, cached per
+// kernel and size).
+template <typename K>
+static int b1_grid(K kernel, int tiles, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, size_t>, int> per_sm_of;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = per_sm_of.find({(const void *)kernel, smem});
+    if (it != per_sm_of.end()) per_sm = it->second;
+  }
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, B1_THREADS, smem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    std::lock_guard<std::mutex> lock(mu);
+    per_sm_of[{(const void *)kernel, smem}] = per_sm;
+  }
   return std::max(1, std::min(tiles, num_sms() * per_sm));
 }
 
@@ -548,11 +598,11 @@ cudaError_t launch_mv_b1(const DevTensor &w, const B1Src &src, float *out, bool 
   cudaError_t e = set_smem(k_mv_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (w.rows + B1_RT - 1) / B1_RT;
-  return launch(k_mv_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, w, src, out, add ? 1 : 0);
+  return launch(k_mv_b1, dim3(b1_grid(k_mv_b1, tiles, smem)), dim3(B1_THREADS), smem, st, w, src, out, add ? 1 : 0);
 }
 
 // q/k/v for one token + RoPE (model.rs:953-979) + KV write (model.rs:984-992).
-__global__ void __launch_bounds__(B1_THREADS) k_qkv_b1(QkvArgs a) {
+__global__ void __launch_bounds__(B1_THREADS, B1_MIN_CTAS) k_qkv_b1(QkvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tq = (a.wq.rows + B1_RT - 1) / B1_RT, tk = (a.wk.rows + B1_RT - 1) / B1_RT,
             tv = (a.wv.rows + B1_RT - 1) / B1_RT;
@@ -608,11 +658,11 @@ cudaError_t launch_qkv_b1(const QkvArgs &a, cudaStream_t st) {
   cudaError_t e = set_smem(k_qkv_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (a.wq.rows + B1_RT - 1) / B1_RT + (a.wk.rows + B1_RT - 1) / B1_RT + (a.wv.rows + B1_RT - 1) / B1_RT;
-  return launch(k_qkv_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, a);
+  return launch(k_qkv_b1, dim3(b1_grid(k_qkv_b1, tiles, smem)), dim3(B1_THREADS), smem, st, a);
 }
 
 // gate/up for one token + SwiGLU (model.rs:1105-1115).
-__global__ void __launch_bounds__(B1_THREADS) k_gateup_b1(DevTensor wg, DevTensor wu, B1Src src, float *__restrict__ h) {
+__global__ void __launch_bounds__(B1_THREADS, B1_MIN_CTAS) k_gateup_b1(DevTensor wg, DevTensor wu, B1Src src, float *__restrict__ h) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
   if (threadIdx.x == 0)
@@ -644,7 +694,7 @@ cudaError_t launch_gateup_b1(const DevTensor &wg, const DevTensor &wu, const B1S
   cudaError_t e = set_smem(k_gateup_b1, smem);
   if (e != cudaSuccess) return e;
   const int tiles = (wg.rows + B1_RT - 1) / B1_RT;
-  return launch(k_gateup_b1, dim3(b1_grid(tiles, smem)), dim3(B1_THREADS), smem, st, wg, wu, src, h);
+  return launch(k_gateup_b1, dim3(b1_grid(k_gateup_b1, tiles, smem)), dim3(B1_THREADS), smem, st, wg, wu, src, h);
 }
 
 // ------------------------------------------------- multi-lane matvec, tensor cores
@@ -1050,11 +1100,13 @@ struct MvSegs {
 template <int KS, int LG>
 __global__ void __launch_bounds__(32 * LG * KS, KS == 1 ? 5 : KS * LG == 4 ? 4 : 1) k_mv_mma(MvSegs ss, Q8Dev act) {
   extern __shared__ __align__(16) uint8_t mm_smem[];
-  pdl_trigger();
-  pdl_wait();
   const int bx = blockIdx.x;
   const MvSeg &S = (ss.n > 2 && bx >= ss.s[2].cta0) ? ss.s[2] : (ss.n > 1 && bx >= ss.s[1].cta0) ? ss.s[1] : ss.s[0];
   const int tb = bx - S.cta0;
+  // the tile's rows are constant: bring them into L2 while the previous kernel runs
+  if (threadIdx.x == 0 && blockIdx.y == 0) prefetch_rows(S.W, tb * MM_ROWS, min(MM_ROWS, S.W.rows - tb * MM_ROWS));
+  pdl_trigger();
+  pdl_wait();
   switch (S.W.type) {
     case T_Q4_K: mv_tile<T_Q4_K, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
     case T_Q6_K: mv_tile<T_Q6_K, KS, LG>(S.W, act, S.out, S.os_row, S.os_lane, S.add, tb, S.nbc, mm_smem); break;
@@ -1302,12 +1354,13 @@ __global__ void k_attn(AttnArgs a, int dot8) {
 //           which the V chain skips and which adds +0.0 exactly to a sum that
 //           starts at +0.0), then thread (token, 4 dims) runs four V chains
 //           and the token's sum chain over the tile in position order.
+// KT is the cache entry type (float, or __half converted exactly when read).
 constexpr int AC_THREADS = 256;
 __host__ __device__ constexpr int ac_group(int dh) { return 512 / dh < 8 ? 512 / dh : 8; }
 __host__ __device__ constexpr int ac_tile(int dh) { return dh <= 64 ? 128 : 64; }
-static size_t ac_smem(int dh) {
+static size_t ac_smem(int dh, size_t esz) {
   const int G = ac_group(dh), P = ac_tile(dh);
-  return sizeof(float) * ((size_t)2 * P * dh + (size_t)G * (P + 4) + (size_t)G * dh + AC_THREADS + 16);
+  return esz * 2 * P * dh + sizeof(float) * ((size_t)G * (P + 4) + (size_t)G * dh + AC_THREADS + 16);
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -1316,12 +1369,14 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait_ns() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // DHC: the head dimension as a compile-time constant (64, 128), or 0 for any.
-template <int DHC>
+template <int DHC, typename KT>
 __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   extern __shared__ __align__(16) float acs[];
+  constexpr int EPC = 16 / sizeof(KT);  // entries per 16-byte copy
   const int dh = DHC ? DHC : a.dh, G = ac_group(dh), P = ac_tile(dh), QP = P / 4, tid = threadIdx.x;
   const int h = blockIdx.y, kh = h / (a.n_head / a.n_kv), t0 = blockIdx.x * G;
-  float *buf0 = acs, *buf1 = acs + P * dh, *E = buf1 + P * dh, *qs = E + G * (P + 4), *red = qs + G * dh;
+  KT *buf0 = reinterpret_cast<KT *>(acs), *buf1 = buf0 + P * dh;
+  float *E = reinterpret_cast<float *>(buf1 + P * dh), *qs = E + G * (P + 4), *red = qs + G * dh;
   float *Ms = red + AC_THREADS;
   int *posv = (int *)(Ms + 8);
   pdl_trigger();
@@ -1339,17 +1394,18 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   for (int t = 0; t < G; t++) maxpos = max(maxpos, posv[t]);
   if (maxpos < 0) return;
   const int nt = maxpos / P + 1;
-  const float *kc = a.kcache + (size_t)kh * dh * a.n_ctx, *vc = a.vcache + (size_t)kh * a.n_ctx * dh;
-  auto stage_k = [&](int i, float *dst) {
-    const int p0 = i * P, nq = (min(P, maxpos + 1 - p0) + 3) >> 2;
-    for (int c = tid; c < dh * QP; c += AC_THREADS) {
-      const int d = c / QP, j = c - d * QP;
-      if (j < nq) cp_async16(dst + d * P + 4 * j, kc + (size_t)d * a.n_ctx + p0 + 4 * j);
+  const KT *kc = reinterpret_cast<const KT *>(a.kcache) + (size_t)kh * dh * a.n_ctx;
+  const KT *vc = reinterpret_cast<const KT *>(a.vcache) + (size_t)kh * a.n_ctx * dh;
+  auto stage_k = [&](int i, KT *dst) {
+    const int p0 = i * P, nq = (min(P, maxpos + 1 - p0) + EPC - 1) / EPC, CP = P / EPC;
+    for (int c = tid; c < dh * CP; c += AC_THREADS) {
+      const int d = c / CP, j = c - d * CP;
+      if (j < nq) cp_async16(dst + d * P + EPC * j, kc + (size_t)d * a.n_ctx + p0 + EPC * j);
     }
   };
-  auto stage_v = [&](int i, float *dst) {
-    const int p0 = i * P, nq = min(P, maxpos + 1 - p0) * dh / 4;
-    for (int c = tid; c < nq; c += AC_THREADS) cp_async16(dst + 4 * c, vc + (size_t)p0 * dh + 4 * c);
+  auto stage_v = [&](int i, KT *dst) {
+    const int p0 = i * P, nq = min(P, maxpos + 1 - p0) * dh / EPC;
+    for (int c = tid; c < nq; c += AC_THREADS) cp_async16(dst + EPC * c, vc + (size_t)p0 * dh + EPC * c);
   };
   // ---- pass 1: scores
   const int st = tid / QP, sq = tid - st * QP;
@@ -1366,12 +1422,12 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
     __syncthreads();
     const int p = i * P + 4 * sq;
     if (p <= spos) {
-      const float4 *kt = (const float4 *)((i & 1) ? buf1 : buf0) + sq;
+      const KT *kt = ((i & 1) ? buf1 : buf0) + 4 * sq;
       const float *qv = qs + st * dh;
       float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
 #pragma unroll 8
       for (int d = 0; d < dh; d++) {
-        const float4 k = kt[d * QP];
+        const float4 k = kv_f4(kt + d * P);
         const float qq = qv[d];
         c0 = fadd(c0, fmul(qq, k.x));
         c1 = fadd(c1, fmul(qq, k.y));
@@ -1402,7 +1458,7 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
   const float *Et = E + (vact ? vt : 0) * (P + 4);
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sum = 0.0f;
   for (int j = 0; j < nt; j++) {
-    const float *vb = ((nt + j) & 1) ? buf1 : buf0;
+    const KT *vb = ((nt + j) & 1) ? buf1 : buf0;
     if (j + 1 < nt) stage_v(j + 1, ((nt + j) & 1) ? buf0 : buf1);
     cp_async_commit();
     const int p0 = j * P;
@@ -1419,13 +1475,13 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
     __syncthreads();
     if (vact) {
       const int npr = (min(P, maxpos + 1 - p0) + 3) & ~3;
-      const float4 *vv = (const float4 *)vb + vd;
+      const KT *vv = vb + 4 * vd;
       for (int pl = 0; pl < npr; pl += 4) {
         const float4 e4 = *(const float4 *)(Et + pl);
         const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          const float4 v = vv[(pl + u) * H4];
+          const float4 v = kv_f4(vv + (pl + u) * dh);
           if (ev[u] != 0.0f) {
             acc[0] = fadd(acc[0], fmul(ev[u], v.x));
             acc[1] = fadd(acc[1], fmul(ev[u], v.y));
@@ -1471,39 +1527,53 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 //           e_p = exp(s_p - M) in shared memory, then thread d < DH runs its
 //           chain over the tile's positions in order (zero weights skipped)
 //           and thread DH the sum chain.
-// Same operations in the same order as k_attn, so the same bits.  Needs
-// n_ctx % 4 == 0 and 16-byte aligned K, V and score rows.
+// Same operations in the same order as k_attn, so the same bits.  KT is the
+// cache entry type (float, or __half converted exactly when read).  Needs
+// n_ctx and the lane stride multiples of 16 bytes' worth of entries, and
+// 16-byte aligned K, V and score rows.
 constexpr int AB_P = 128, AB_NS = 3;
-__host__ __device__ constexpr size_t ab_smem(int dh) { return (size_t)AB_NS * (dh * AB_P + AB_P) * 4; }
+__host__ __device__ constexpr size_t ab_smem(int dh, size_t esz) {
+  return (size_t)AB_NS * (dh * AB_P * esz + AB_P * 4);
+}
 
-template <int DH>
+template <int DH, typename KT>
 __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
-  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P;
+  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P, EPC = 16 / sizeof(KT);
   extern __shared__ __align__(16) float at_sm[];
-  float *const es = at_sm + NS * TILE;  // NS tiles of TILE floats, then e: [NS][P]
+  KT *const tiles = reinterpret_cast<KT *>(at_sm);
+  float *const es = reinterpret_cast<float *>(tiles + NS * TILE);  // NS tiles of TILE entries, then e: [NS][P]
   __shared__ float qs[DH];
   __shared__ float red[40];
   __shared__ float s_inv;
   const int h = blockIdx.x, bi = blockIdx.y, tid = threadIdx.x;
   const int kh = h / (a.n_head / a.n_kv);
+  const KT *kb = reinterpret_cast<const KT *>(a.kcache) + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  const KT *vb = reinterpret_cast<const KT *>(a.vcache) + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  {
+    // The history below this token's position is not written by the kernels
+    // this launch waits for: ask L2 for it while they run.  pos may not be
+    // final yet, so it is clamped to the cache and only sizes the hint.
+    const int hist = min(max(a.pos[bi], 0), a.n_ctx - 1);
+    if (tid < DH) prefetch_l2(kb + (size_t)tid * a.n_ctx, (uint32_t)(hist * sizeof(KT)));  // K row d = tid
+    else if (tid == DH) prefetch_l2(vb, (uint32_t)((size_t)hist * DH * sizeof(KT)));
+  }
   pdl_trigger();
   pdl_wait();
   const int pos = a.pos[bi], n = pos + 1, nt = (n + P - 1) / P;
   const long hb = (long)bi * a.n_head + h;
   if (tid < DH) qs[tid] = a.q[hb * DH + tid];
-  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
-  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
   float *sc = a.scores + hb * a.n_ctx;
   // K tile t into stage t % NS: [d][P] from the d-major cache, 16-byte chunks
   // holding a position <= pos.  Every call commits one group (empty past the
   // last tile), so "wait until NS - 1 groups are pending" completes tile t.
   auto load_k = [&](int t) {
     if (t < nt) {
-      float *dst = at_sm + (t % NS) * TILE;
-      const int p0 = t * P, nq = (min(P, n - p0) + 3) >> 2;
-      for (int c = tid; c < DH * (P / 4); c += NT) {
-        const int d = c >> 5, j = c & 31;
-        if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+      KT *dst = tiles + (t % NS) * TILE;
+      constexpr int CP = P / EPC;
+      const int p0 = t * P, nq = (min(P, n - p0) + EPC - 1) / EPC;
+      for (int c = tid; c < DH * CP; c += NT) {
+        const int d = c / CP, j = c % CP;
+        if (j < nq) cp_async16(dst + d * P + EPC * j, kb + (size_t)d * a.n_ctx + p0 + EPC * j);
       }
     }
     cp_async_commit();
@@ -1514,14 +1584,14 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     load_k(t + NS - 1);
     cp_async_wait_ns<NS - 1>();
     __syncthreads();
-    const float *cur = at_sm + (t % NS) * TILE;
+    const KT *cur = tiles + (t % NS) * TILE;
     const int p = t * P + tid;
     if (tid < P && p <= pos) {
       float c[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int d = 0; d < DH; d += 8) {
 #pragma unroll
-        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], cur[(d + u) * P + tid]));
+        for (int u = 0; u < 8; u++) c[u] = fadd(c[u], fmul(qs[d + u], kv_f(cur[(d + u) * P + tid])));
       }
       float sv = fadd(fadd(c[0], c[1]), fadd(c[2], c[3]));
       sv = fadd(sv, fadd(fadd(c[4], c[5]), fadd(c[6], c[7])));
@@ -1533,13 +1603,14 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
   }
   cp_async_wait_all();  // only empty groups are left
   const float M = block_max(mx, red);  // (its barriers also order the score stores before pass 2)
-  // V tile t into stage t % NS: P rows of DH floats (contiguous), and the scores of its positions
+  // V tile t into stage t % NS: P rows of DH entries (contiguous), and the scores of its positions
   auto load_v = [&](int t) {
     if (t < nt) {
-      float *dst = at_sm + (t % NS) * TILE, *edst = es + (t % NS) * P;
+      KT *dst = tiles + (t % NS) * TILE;
+      float *edst = es + (t % NS) * P;
       const int p0 = t * P, nv = min(P, n - p0);
-      const float *src = vb + (size_t)p0 * DH;
-      for (int c = tid; c < nv * (DH / 4); c += NT) cp_async16(dst + 4 * c, src + 4 * c);
+      const KT *src = vb + (size_t)p0 * DH;
+      for (int c = tid; c < nv * (DH / EPC); c += NT) cp_async16(dst + EPC * c, src + EPC * c);
       if (tid < ((nv + 3) >> 2)) cp_async16(edst + 4 * tid, sc + p0 + 4 * tid);
     }
     cp_async_commit();
@@ -1550,7 +1621,7 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     load_v(t + NS - 1);
     cp_async_wait_ns<NS - 1>();
     __syncthreads();
-    const float *cur = at_sm + (t % NS) * TILE;
+    const KT *cur = tiles + (t % NS) * TILE;
     float *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
     if (tid < nv) ec[tid] = expf_lib(fsub(ec[tid], M));
@@ -1559,7 +1630,7 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
 #pragma unroll 8
       for (int j = 0; j < nv; j++) {
         const float e = ec[j];
-        const float v = cur[j * DH + tid];
+        const float v = kv_f(cur[j * DH + tid]);
         if (e != 0.0f) acc = fadd(acc, fmul(e, v));
       }
     } else if (tid == DH) {
@@ -1603,10 +1674,11 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 //              in shared memory and runs the chains of d = 32 part .. +31
 //              over V's matching 128-byte row pieces, plus its own copy of
 //              the sum chain; its 32 outputs are one Q8 block.
-template <int DH>
+template <int DH, typename KT>
 __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
-  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P;
+  constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P, EPC = 16 / sizeof(KT);
   extern __shared__ __align__(16) float at_sm[];
+  KT *const tiles = reinterpret_cast<KT *>(at_sm);
   __shared__ float qs[DH];
   __shared__ float red[40];
   const int h = blockIdx.x, bi = blockIdx.y, c = blockIdx.z, tid = threadIdx.x;
@@ -1622,16 +1694,17 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
     return;
   }
   if (tid < DH) qs[tid] = a.q[hb * DH + tid];
-  const float *kb = a.kcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
+  const KT *kb = reinterpret_cast<const KT *>(a.kcache) + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH;
   float *sc = a.scores + hb * a.n_ctx;
   const int nt = (p_hi - p_lo + P - 1) / P;
   auto load_k = [&](int t) {
     if (t < nt) {
-      float *dst = at_sm + (t % NS) * TILE;
-      const int p0 = p_lo + t * P, nq = (min(P, p_hi - p0) + 3) >> 2;
-      for (int i = tid; i < DH * (P / 4); i += NT) {
-        const int d = i >> 5, j = i & 31;
-        if (j < nq) cp_async16(dst + d * P + 4 * j, kb + (size_t)d * a.n_ctx + p0 + 4 * j);
+      KT *dst = tiles + (t % NS) * TILE;
+      constexpr int CP = P / EPC;
+      const int p0 = p_lo + t * P, nq = (min(P, p_hi - p0) + EPC - 1) / EPC;
+      for (int i = tid; i < DH * CP; i += NT) {
+        const int d = i / CP, j = i % CP;
+        if (j < nq) cp_async16(dst + d * P + EPC * j, kb + (size_t)d * a.n_ctx + p0 + EPC * j);
       }
     }
     cp_async_commit();
@@ -1642,14 +1715,14 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
     load_k(t + NS - 1);
     cp_async_wait_ns<NS - 1>();
     __syncthreads();
-    const float *cur = at_sm + (t % NS) * TILE;
+    const KT *cur = tiles + (t % NS) * TILE;
     const int p = p_lo + t * P + tid;
     if (tid < P && p < p_hi) {
       float cc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int d = 0; d < DH; d += 8) {
 #pragma unroll
-        for (int u = 0; u < 8; u++) cc[u] = fadd(cc[u], fmul(qs[d + u], cur[(d + u) * P + tid]));
+        for (int u = 0; u < 8; u++) cc[u] = fadd(cc[u], fmul(qs[d + u], kv_f(cur[(d + u) * P + tid])));
       }
       float sv = fadd(fadd(cc[0], cc[1]), fadd(cc[2], cc[3]));
       sv = fadd(sv, fadd(fadd(cc[4], cc[5]), fadd(cc[6], cc[7])));
@@ -1664,14 +1737,20 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
   if (tid == 0) *pm = M;
 }
 
-constexpr int PV_P = 128, PV_NS = 3, PV_W = 32, PV_NT = 64;
-constexpr size_t pv_smem() { return (size_t)PV_NS * (PV_P * PV_W + PV_P) * 4; }
+// Stages of the value pass's ring: each CTA's chain is a long sequence of
+// 128-position tiles, so the copies of several tiles must be in flight to
+// cover the memory latency.  f16 pieces are half the size, so twice the
+// stages fit in the same shared memory (four CTAs per SM either way).
+constexpr int PV_P = 128, PV_W = 32, PV_NT = 64;
+__host__ __device__ constexpr int pv_stages(size_t esz) { return esz == 2 ? 6 : 3; }
+constexpr size_t pv_smem(size_t esz) { return (size_t)pv_stages(esz) * (PV_P * PV_W * esz + PV_P * 4); }
 
-template <int DH>
+template <int DH, typename KT>
 __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
-  constexpr int P = PV_P, NS = PV_NS, W = PV_W, NT = PV_NT;
+  constexpr int P = PV_P, NS = pv_stages(sizeof(KT)), W = PV_W, NT = PV_NT, EPC = 16 / sizeof(KT), CW = W / EPC;
   extern __shared__ __align__(16) float pv_sm[];
-  float *const es = pv_sm + NS * P * W;  // NS V pieces of P x W floats, then e: [NS][P]
+  KT *const pieces = reinterpret_cast<KT *>(pv_sm);
+  float *const es = reinterpret_cast<float *>(pieces + NS * P * W);  // NS V pieces of P x W entries, then e: [NS][P]
   __shared__ float s_m, s_inv;
   const int h = blockIdx.x, bi = blockIdx.y, part = blockIdx.z, tid = threadIdx.x;
   const int kh = h / (a.n_head / a.n_kv);
@@ -1687,15 +1766,16 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
   }
   __syncthreads();
   const float M = s_m;
-  const float *vb = a.vcache + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH + part * W;
+  const KT *vb = reinterpret_cast<const KT *>(a.vcache) + (size_t)bi * a.lane_stride + (size_t)kh * a.n_ctx * DH + part * W;
   const float *sc = a.scores + hb * a.n_ctx;
   auto load = [&](int t) {
     if (t < nt) {
-      float *dst = pv_sm + (t % NS) * P * W, *edst = es + (t % NS) * P;
+      KT *dst = pieces + (t % NS) * P * W;
+      float *edst = es + (t % NS) * P;
       const int p0 = t * P, nv = min(P, n - p0);
-      for (int i = tid; i < nv * (W / 4); i += NT) {
-        const int r = i >> 3, j = i & 7;
-        cp_async16(dst + r * W + 4 * j, vb + (size_t)(p0 + r) * DH + 4 * j);
+      for (int i = tid; i < nv * CW; i += NT) {
+        const int r = i / CW, j = i % CW;
+        cp_async16(dst + r * W + EPC * j, vb + (size_t)(p0 + r) * DH + EPC * j);
       }
       for (int i = tid; i < ((nv + 3) >> 2); i += NT) cp_async16(edst + 4 * i, sc + p0 + 4 * i);
     }
@@ -1707,7 +1787,7 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
     load(t + NS - 1);
     cp_async_wait_ns<NS - 1>();
     __syncthreads();
-    const float *cur = pv_sm + (t % NS) * P * W;
+    const KT *cur = pieces + (t % NS) * P * W;
     float *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
     for (int j = tid; j < nv; j += NT) ec[j] = expf_lib(fsub(ec[j], M));
@@ -1716,7 +1796,7 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
 #pragma unroll 8
       for (int j = 0; j < nv; j++) {
         const float e = ec[j];
-        const float v = cur[j * W + tid];
+        const float v = kv_f(cur[j * W + tid]);
         if (e != 0.0f) acc = fadd(acc, fmul(e, v));
       }
     } else if (tid == W) {
@@ -1739,46 +1819,54 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
   }
 }
 
-static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
-  if (a.kv16) {  // f16 cache entries: the per-(token, head) kernel, in either order
-    const bool dot8 = a.b == 1 || a.b1_order;
-    return launch(k_attn<true>, dim3(a.n_head, a.b), dim3(a.dh < 128 ? 128 : 256), 0, st, a, dot8 ? 1 : 0);
-  }
-  if (a.b > 1 && !a.b1_order && a.lane_stride == 0 && a.n_ctx % 4 == 0 &&
-      (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0) {
-    const size_t smem = ac_smem(a.dh);
+// KT: the cache entry type.  The tiled kernels copy 16-byte pieces, so they
+// need n_ctx, the lane stride and (for the chunk kernel) dh in whole pieces
+// and 16-byte aligned caches; otherwise k_attn reads entries one at a time.
+template <typename KT>
+static cudaError_t launch_attention_t(const AttnArgs &a, cudaStream_t st) {
+  constexpr int EPC = 16 / sizeof(KT);
+  constexpr size_t ESZ = sizeof(KT);
+  const bool aligned = (((uintptr_t)a.kcache | (uintptr_t)a.vcache) & 15) == 0 && a.n_ctx % EPC == 0;
+  if (a.b > 1 && !a.b1_order && a.lane_stride == 0 && aligned && a.dh % EPC == 0) {
+    const size_t smem = ac_smem(a.dh, ESZ);
     const int G = ac_group(a.dh);
     const dim3 grid((a.b + G - 1) / G, a.n_head);
-    void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_chunk<64> : a.dh == 128 ? k_attn_chunk<128> : k_attn_chunk<0>;
+    void (*kern)(AttnArgs) = a.dh == 64    ? k_attn_chunk<64, KT>
+                             : a.dh == 128 ? k_attn_chunk<128, KT>
+                                           : k_attn_chunk<0, KT>;
     cudaError_t e = set_smem(kern, smem);
     if (e != cudaSuccess) return e;
     return launch(kern, grid, dim3(AC_THREADS), smem, st, a);
   }
   const bool dot8 = a.b == 1 || a.b1_order;
-  const bool tiles = dot8 && (a.dh == 64 || a.dh == 128) && a.n_ctx % 4 == 0 && a.lane_stride % 4 == 0 &&
-                     (((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.scores) & 15) == 0;
+  const bool tiles = dot8 && (a.dh == 64 || a.dh == 128) && aligned && a.lane_stride % EPC == 0 &&
+                     ((uintptr_t)a.scores & 15) == 0;
   if (tiles && a.pmax && a.pchunk > 0) {
     if (a.pchunk % AB_P != 0) return cudaErrorInvalidValue;
     const int nch = (a.n_ctx + a.pchunk - 1) / a.pchunk;
-    void (*ks)(AttnArgs) = a.dh == 64 ? k_attn_sc<64> : k_attn_sc<128>;
-    void (*kv)(AttnArgs, int) = a.dh == 64 ? k_attn_pv<64> : k_attn_pv<128>;
-    const size_t s1 = (size_t)AB_NS * a.dh * AB_P * 4;
+    void (*ks)(AttnArgs) = a.dh == 64 ? k_attn_sc<64, KT> : k_attn_sc<128, KT>;
+    void (*kv)(AttnArgs, int) = a.dh == 64 ? k_attn_pv<64, KT> : k_attn_pv<128, KT>;
+    const size_t s1 = (size_t)AB_NS * a.dh * AB_P * ESZ;
     cudaError_t e = set_smem(ks, s1);
-    if (e == cudaSuccess) e = set_smem(kv, pv_smem());
+    if (e == cudaSuccess) e = set_smem(kv, pv_smem(ESZ));
     if (e == cudaSuccess)
       e = launch(ks, dim3(a.n_head, a.b, nch), dim3(a.dh == 64 ? 128 : 256), s1, st, a);
     if (e != cudaSuccess) return e;
-    return launch(kv, dim3(a.n_head, a.b, a.dh / PV_W), dim3(PV_NT), pv_smem(), st, a, nch);
+    return launch(kv, dim3(a.n_head, a.b, a.dh / PV_W), dim3(PV_NT), pv_smem(ESZ), st, a, nch);
   }
   if (tiles) {
-    const size_t smem = ab_smem(a.dh);
-    void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_b1t<64> : k_attn_b1t<128>;
+    const size_t smem = ab_smem(a.dh, ESZ);
+    void (*kern)(AttnArgs) = a.dh == 64 ? k_attn_b1t<64, KT> : k_attn_b1t<128, KT>;
     cudaError_t e = set_smem(kern, smem);
     if (e != cudaSuccess) return e;
     return launch(kern, dim3(a.n_head, a.b), dim3(a.dh == 64 ? 128 : 256), smem, st, a);
   }
   const int threads = a.dh < 128 ? 128 : 256;
-  return launch(k_attn<false>, dim3(dim3(a.n_head, a.b)), dim3(threads), 0, st, a, dot8 ? 1 : 0);
+  return launch(k_attn<(sizeof(KT) == 2)>, dim3(a.n_head, a.b), dim3(threads), 0, st, a, dot8 ? 1 : 0);
+}
+
+static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st) {
+  return a.kv16 ? launch_attention_t<__half>(a, st) : launch_attention_t<float>(a, st);
 }
 
 // ------------------------------------------------------------ temperature / top-p sampling

@@ -71,3 +71,39 @@ def test_kv16_set_after_load_is_rejected(pk, paths):
     g = pk.Engine(paths["tiny"], n_ctx=128)
     assert pk.lib().pk_set_kv_type(g.h, pk.KV_F16) != 0
     assert pk.lib().pk_set_kv_type(None, pk.KV_F16) != 0
+
+
+@pytest.mark.parametrize("name", ["tiny", "q8down"])
+def test_kv16_chunk_attention_equals_per_token_kernel(pk, paths, name):
+    """f16 entries through the shared-memory tile kernels (n_ctx = 256, whole
+    16-byte pieces of eight entries) give the same bits as the one-CTA-per-
+    token kernel (n_ctx = 252 is not a multiple of eight, so it takes that
+    path), across prefill chunks and the decode step."""
+    spec = MODELS[name]
+    prompt = synth.prompt_ids(13, 200, spec.n_vocab)
+    a, b = pk.Engine(paths[name], n_ctx=256, kv="f16"), pk.Engine(paths[name], n_ctx=252, kv="f16")
+    ra, rb = a.generate(prompt, 24, stop_at_eog=False), b.generate(prompt, 24, stop_at_eog=False)
+    assert ra["gen_ids"] == rb["gen_ids"]
+    assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
+
+
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+def test_streams_long_history_match_oracle(pk, oracle, paths, kv):
+    """Above 1024 positions the streams' attention is split (scores over
+    512-position chunks on many CTAs, then value chains per 32 d); each
+    stream's greedy tokens equal the oracle's for that prompt alone, with an
+    f32 or an f16 cache, across chunk edges."""
+    spec = MODELS["tiny"]
+    prompts = [synth.prompt_ids(41 + i, n, spec.n_vocab) for i, n in enumerate((3, 530, 1100))]
+    want = []
+    for p in prompts:
+        o = oracle.Engine(paths["tiny"], 1536, THREADS)
+        o.set_kv_f16(kv == "f16")
+        want.append(o.generate(p, 24)["gen_ids"])
+    e = pk.Engine(paths["tiny"], n_ctx=1536, kv=kv)
+    e.streams_begin(len(prompts))
+    for s, p in enumerate(prompts):
+        e.stream_prefill(s, p)
+    first, rest = e.streams_decode(9), e.streams_decode(15)
+    for s in range(len(prompts)):
+        assert first[s] + rest[s] == want[s]
