@@ -37,6 +37,14 @@ __device__ __forceinline__ void kv_put(float *base, size_t i, float v) {
   if (H) reinterpret_cast<__half *>(base)[i] = __float2half_rn(v);
   else base[i] = v;
 }
+// acc + e * v, or acc itself when e == 0 (a zero weight is skipped).
+// acc + (-0.0) is acc for every acc, +-0, inf and NaN included, so choosing
+// -0.0 for the skipped product gives the skip's bits while the select stays
+// off the chain: each step of a chain waits for one add only.
+__device__ __forceinline__ float add_weighted(float acc, float e, float v) {
+  return fadd(acc, e != 0.0f ? fmul(e, v) : -0.0f);
+}
+
 // One staged cache element as f32, and four consecutive ones (p aligned to
 // four elements), for kernels templated on the entry type.
 __device__ __forceinline__ float kv_f(float v) { return v; }

@@ -1323,7 +1323,7 @@ __global__ void k_attn(AttnArgs a, int dot8) {
     for (int p = 0; p <= pos; p++) {
       const float e = sc[p];
       const float v = kv_get<KV16>(a.vcache, vr + (size_t)p * dh);
-      if (e != 0.0f) acc = fadd(acc, fmul(e, v));
+      acc = add_weighted(acc, e, v);
     }
   }
   if (tid == (dh < (int)blockDim.x ? dh : 0)) {
@@ -1482,12 +1482,10 @@ __global__ void __launch_bounds__(AC_THREADS) k_attn_chunk(AttnArgs a) {
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           const float4 v = kv_f4(vv + (pl + u) * dh);
-          if (ev[u] != 0.0f) {
-            acc[0] = fadd(acc[0], fmul(ev[u], v.x));
-            acc[1] = fadd(acc[1], fmul(ev[u], v.y));
-            acc[2] = fadd(acc[2], fmul(ev[u], v.z));
-            acc[3] = fadd(acc[3], fmul(ev[u], v.w));
-          }
+          acc[0] = add_weighted(acc[0], ev[u], v.x);
+          acc[1] = add_weighted(acc[1], ev[u], v.y);
+          acc[2] = add_weighted(acc[2], ev[u], v.z);
+          acc[3] = add_weighted(acc[3], ev[u], v.w);
           sum = fadd(sum, ev[u]);
         }
       }
@@ -1533,7 +1531,7 @@ static cudaError_t launch_attention_k(const AttnArgs &a, cudaStream_t st);
 // 16-byte aligned K, V and score rows.
 constexpr int AB_P = 128, AB_NS = 3;
 __host__ __device__ constexpr size_t ab_smem(int dh, size_t esz) {
-  return (size_t)AB_NS * (dh * AB_P * esz + AB_P * 4);
+  return (size_t)AB_NS * (dh * AB_P * esz + AB_P * 4) + (esz == 4 ? 0 : (size_t)AB_P * dh * 4);
 }
 
 template <int DH, typename KT>
@@ -1541,7 +1539,9 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
   constexpr int P = AB_P, NS = AB_NS, NT = DH == 64 ? 128 : 256, TILE = DH * P, EPC = 16 / sizeof(KT);
   extern __shared__ __align__(16) float at_sm[];
   KT *const tiles = reinterpret_cast<KT *>(at_sm);
-  float *const es = reinterpret_cast<float *>(tiles + NS * TILE);  // NS tiles of TILE entries, then e: [NS][P]
+  // NS tiles of TILE entries, then e: [NS][P], then (f16) the V products [P][DH]
+  float *const es = reinterpret_cast<float *>(tiles + NS * TILE);
+  float *const prod_buf = es + NS * P;
   __shared__ float qs[DH];
   __shared__ float red[40];
   __shared__ float s_inv;
@@ -1626,13 +1626,23 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     const int nv = min(P, n - t * P);
     if (tid < nv) ec[tid] = expf_lib(fsub(ec[tid], M));
     __syncthreads();
+    // the tile's products e_p * v_p[d] by every thread (-0.0 for a zero
+    // weight, which the chain then adds exactly as a skip), so that each
+    // chain step below waits for one add; f32 products overwrite the tile
+    float *const pr = sizeof(KT) == 4 ? reinterpret_cast<float *>(tiles + (t % NS) * TILE) : prod_buf;
+    for (int i = tid; i < nv * (DH / 4); i += NT) {
+      const int j = i / (DH / 4), d4 = 4 * (i % (DH / 4));
+      const float e = ec[j];
+      const float4 v = kv_f4(cur + j * DH + d4);
+      const bool z = e == 0.0f;
+      *reinterpret_cast<float4 *>(pr + j * DH + d4) =
+          make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
+                      z ? -0.0f : fmul(e, v.w));
+    }
+    __syncthreads();
     if (tid < DH) {
 #pragma unroll 8
-      for (int j = 0; j < nv; j++) {
-        const float e = ec[j];
-        const float v = kv_f(cur[j * DH + tid]);
-        if (e != 0.0f) acc = fadd(acc, fmul(e, v));
-      }
+      for (int j = 0; j < nv; j++) acc = fadd(acc, pr[j * DH + tid]);
     } else if (tid == DH) {
 #pragma unroll 8
       for (int j = 0; j < nv; j++) sum = fadd(sum, ec[j]);
@@ -1737,20 +1747,28 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_sc(AttnArgs a) {
   if (tid == 0) *pm = M;
 }
 
-// Stages of the value pass's ring: each CTA's chain is a long sequence of
-// 128-position tiles, so the copies of several tiles must be in flight to
-// cover the memory latency.  f16 pieces are half the size, so twice the
-// stages fit in the same shared memory (four CTAs per SM either way).
-constexpr int PV_P = 128, PV_W = 32, PV_NT = 64;
-__host__ __device__ constexpr int pv_stages(size_t esz) { return esz == 2 ? 6 : 3; }
-constexpr size_t pv_smem(size_t esz) { return (size_t)pv_stages(esz) * (PV_P * PV_W * esz + PV_P * 4); }
+// The value pass: one CTA of 256 threads per (stream, head, 64 of the head's
+// dims), three stages of V pieces and scores.  Per 128-position tile every
+// thread takes part in the exps and in the products e_p * v_p[d] (four dims
+// at a time, -0.0 for a zero weight: adding it leaves the chain as skipping
+// would), then each of the 64 chain threads only loads and adds, in
+// position order, with the loads unrolled ahead of the adds, while one more
+// thread runs the sum chain.  f32 products overwrite their V piece; f16 ones
+// (twice the size) go to a separate [P][W] buffer.
+constexpr int PV_P = 128, PV_W = 64, PV_NT = 256, PV_NS = 3;
+constexpr size_t pv_smem(size_t esz) {
+  return (size_t)PV_NS * (PV_P * PV_W * esz + PV_P * 4) + (esz == 4 ? 0 : (size_t)PV_P * PV_W * 4);
+}
 
 template <int DH, typename KT>
 __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
-  constexpr int P = PV_P, NS = pv_stages(sizeof(KT)), W = PV_W, NT = PV_NT, EPC = 16 / sizeof(KT), CW = W / EPC;
+  constexpr int P = PV_P, NS = PV_NS, W = PV_W, NT = PV_NT, EPC = 16 / sizeof(KT), CW = W / EPC;
+  static_assert(DH % W == 0 && W % 32 == 0, "whole Q8 blocks per CTA");
   extern __shared__ __align__(16) float pv_sm[];
   KT *const pieces = reinterpret_cast<KT *>(pv_sm);
-  float *const es = reinterpret_cast<float *>(pieces + NS * P * W);  // NS V pieces of P x W entries, then e: [NS][P]
+  // NS V pieces of P x W entries, then e: [NS][P], then (f16) the products [P][W]
+  float *const es = reinterpret_cast<float *>(pieces + NS * P * W);
+  float *const prod_buf = es + NS * P;
   __shared__ float s_m, s_inv;
   const int h = blockIdx.x, bi = blockIdx.y, part = blockIdx.z, tid = threadIdx.x;
   const int kh = h / (a.n_head / a.n_kv);
@@ -1792,15 +1810,22 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
     const int nv = min(P, n - t * P);
     for (int j = tid; j < nv; j += NT) ec[j] = expf_lib(fsub(ec[j], M));
     __syncthreads();
+    float *const pr = sizeof(KT) == 4 ? reinterpret_cast<float *>(pieces + (t % NS) * P * W) : prod_buf;
+    for (int i = tid; i < nv * (W / 4); i += NT) {
+      const int j = i / (W / 4), d4 = 4 * (i % (W / 4));
+      const float e = ec[j];
+      const float4 v = kv_f4(cur + j * W + d4);
+      const bool z = e == 0.0f;
+      *reinterpret_cast<float4 *>(pr + j * W + d4) =
+          make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
+                      z ? -0.0f : fmul(e, v.w));
+    }
+    __syncthreads();
     if (tid < W) {
-#pragma unroll 8
-      for (int j = 0; j < nv; j++) {
-        const float e = ec[j];
-        const float v = kv_f(cur[j * W + tid]);
-        if (e != 0.0f) acc = fadd(acc, fmul(e, v));
-      }
+#pragma unroll 16
+      for (int j = 0; j < nv; j++) acc = fadd(acc, pr[j * W + tid]);
     } else if (tid == W) {
-#pragma unroll 8
+#pragma unroll 16
       for (int j = 0; j < nv; j++) sum = fadd(sum, ec[j]);
     }
     __syncthreads();
@@ -1808,12 +1833,12 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
   cp_async_wait_all();
   if (tid == W) s_inv = sum > 0.0f ? fdiv(1.0f, sum) : 0.0f;
   __syncthreads();
-  if (tid < W) {
+  if (tid < W) {  // warp w holds Q8 block (h * DH + part * W) / 32 + w of the token's row
     const float o = fmul(acc, s_inv);
     a.out[hb * DH + part * W + tid] = o;
     if (a.q8.q) {
-      const int qk = a.n_head * DH, blk = (h * DH + part * W) >> 5;
-      q8_block_lane(o, tid, a.q8.q + (long)bi * qk + blk * 32, a.q8.d + (long)bi * (qk >> 5) + blk,
+      const int qk = a.n_head * DH, blk = (h * DH + part * W + tid) >> 5;
+      q8_block_lane(o, tid & 31, a.q8.q + (long)bi * qk + blk * 32, a.q8.d + (long)bi * (qk >> 5) + blk,
                     a.q8.s + (long)bi * (qk >> 5) + blk);
     }
   }

@@ -15,13 +15,16 @@ from pocketinfer import synth
 pytestmark = pytest.mark.gpu
 THREADS = max(1, min(32, os.cpu_count() or 1))
 MODELS = {"tiny": synth.TINY, "q8down": synth.SMALL_Q8DOWN, "q40": synth.SMALL_Q40}
+# head_dim 128: the split value pass runs two 64-dim parts per head
+DH128 = synth.ModelSpec("tiny-dh128", n_layer=2, n_embd=256, n_head=2, n_head_kv=1, head_dim=128, n_ff=512,
+                        n_vocab=1000)
 
 
 @pytest.fixture(scope="module")
 def paths(tmp_path_factory):
     d = tmp_path_factory.mktemp("kv16")
     out = {}
-    for name, spec in MODELS.items():
+    for name, spec in list(MODELS.items()) + [("dh128", DH128)]:
         out[name] = str(d / f"{name}.gguf")
         synth.write_gguf(out[name], spec, seed=33)
     return out
@@ -88,19 +91,21 @@ def test_kv16_chunk_attention_equals_per_token_kernel(pk, paths, name):
 
 
 @pytest.mark.parametrize("kv", ["f32", "f16"])
-def test_streams_long_history_match_oracle(pk, oracle, paths, kv):
+@pytest.mark.parametrize("name", ["tiny", "dh128"])
+def test_streams_long_history_match_oracle(pk, oracle, paths, kv, name):
     """Above 1024 positions the streams' attention is split (scores over
-    512-position chunks on many CTAs, then value chains per 32 d); each
-    stream's greedy tokens equal the oracle's for that prompt alone, with an
-    f32 or an f16 cache, across chunk edges."""
-    spec = MODELS["tiny"]
+    512-position chunks on many CTAs, then the value chains of 64 dims per
+    CTA over 64-position tiles); each stream's greedy tokens equal the
+    oracle's for that prompt alone, with an f32 or an f16 cache, across chunk
+    and tile edges, at head_dim 64 and 128."""
+    spec = DH128 if name == "dh128" else MODELS[name]
     prompts = [synth.prompt_ids(41 + i, n, spec.n_vocab) for i, n in enumerate((3, 530, 1100))]
     want = []
     for p in prompts:
-        o = oracle.Engine(paths["tiny"], 1536, THREADS)
+        o = oracle.Engine(paths[name], 1536, THREADS)
         o.set_kv_f16(kv == "f16")
         want.append(o.generate(p, 24)["gen_ids"])
-    e = pk.Engine(paths["tiny"], n_ctx=1536, kv=kv)
+    e = pk.Engine(paths[name], n_ctx=1536, kv=kv)
     e.streams_begin(len(prompts))
     for s, p in enumerate(prompts):
         e.stream_prefill(s, p)
