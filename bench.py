@@ -52,6 +52,8 @@ def parse_args():
                    help="tensor-parallel decode of the 70B-shaped stack (BASELINE config 5), one rank per GPU "
                         "(world = the torchrun world size); prints its own JSON line")
     p.add_argument("--tp-layers", type=int, default=None, help="layers of that stack (default 80)")
+    p.add_argument("--tp-collective", choices=("peer", "nccl"), default="peer",
+                   help="the o / down exchange of --tp70: own peer-memory push, or an NCCL all-reduce")
     p.add_argument("--streams", type=int, default=0,
                    help="independent M26 streams per GPU decoded together (the data-parallel streams case)")
     p.add_argument("--stream-ctx", type=int, default=512, help="KV positions of each stream")
@@ -358,10 +360,28 @@ def nccl_allreduce_us(dist, n, iters=200, warmup=20):
     return replicas.max_over_ranks(e0.elapsed_time(e1) * 1000.0 / iters, dist, "cuda")
 
 
+PEER_EXCHANGE = "partial row sums pushed to every rank's peer buffer over NVLink, added in rank order"
+NCCL_EXCHANGE = "partial row sums through an NCCL all-reduce on the engine's stream, then added to the residual"
+
+
 def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
     """BASELINE config 5 (TP half) inside the scaling run: the 70B-shaped stack split
     over this job's world, synthetic weights generated on each device, greedy b = 1
-    decode; every rank runs it, the time is the max over ranks."""
+    decode; every rank runs it, the time is the max over ranks.  With more than one
+    rank it runs once per exchange (own peer-memory push, NCCL all-reduce) and
+    reports the faster as ``value``."""
+    peer = tp70_run(world, rank, local, dist, steps, warmup, "peer")
+    if world == 1:
+        return peer
+    nccl = tp70_run(world, rank, local, dist, steps, warmup, "nccl")
+    best = nccl if nccl["value"] > peer["value"] else peer
+    out = dict(best)
+    out["by_collective"] = {"peer": {k: peer[k] for k in ("value", "ms_per_step", "per_rank_hbm_frac")},
+                            "nccl": {k: nccl[k] for k in ("value", "ms_per_step", "per_rank_hbm_frac")}}
+    return out
+
+
+def tp70_run(world, rank, local, dist, steps, warmup, collective):
     from pocketinfer import replicas, tp
 
     model = dict(tp.M70)
@@ -377,7 +397,10 @@ def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
         # every rank learns whether all loaded before any of them enters the handle exchange
         if replicas.max_over_ranks(1.0 if err else 0.0, dist, "cuda") > 0.0:
             raise RuntimeError(f"tp70: a rank failed to load ({err})")
-        eng.connect() if world > 1 else eng.connect(exchange=lambda b: [b])
+        if world > 1:
+            eng.connect(collective=collective)
+        else:
+            eng.connect(exchange=lambda b: [b])
         info = eng.info
         eng.prefill([(7 * i + 3) % model["n_vocab"] for i in range(8)])
         eng.decode(warmup)
@@ -397,7 +420,7 @@ def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
             "parallelism": f"tp{world}", "value": 1000.0 / ms_step, "unit": "tok/s", "ms_per_step": ms_step,
             "steps": steps, "per_rank_hbm_frac": gbs / hbm, "per_rank_stream_bytes": info["stream_bytes"],
             "peak_kind": kind, "collectives_per_token": info["collectives_per_token"], "load_s": load_s,
-            "exchange": "partial row sums pushed to every rank's peer buffer over NVLink, added in rank order"}
+            "collective": collective, "exchange": NCCL_EXCHANGE if collective == "nccl" else PEER_EXCHANGE}
 
 
 def dp_streams_leg(pk, synth, path, spec, world, rank, local, dist, per_gpu=8, ctx=4096, steps=64, warmup=3):
@@ -660,7 +683,10 @@ def run_tp70(args):
     t0 = time.time()
     eng.load_synthetic(model, seed=70)
     load_s = time.time() - t0
-    eng.connect()
+    if world > 1:
+        eng.connect(collective=args.tp_collective)
+    else:
+        eng.connect()
     info = eng.info
     prompt = [(7 * i + 3) % model["n_vocab"] for i in range(8)]
     eng.prefill(prompt)
@@ -688,8 +714,8 @@ def run_tp70(args):
                        if not args.tp_layers else f"70B-shaped stack cut to {model['n_layer']} layers",
                        "parallelism": f"tp{world}", "prompt": len(prompt),
                        "collectives_per_token": info["collectives_per_token"],
-                       "exchange": "partial row sums (n_embd f32) pushed to every rank's peer buffer, added in "
-                                   "rank order; own push/sum kernels over NVLink peer memory"},
+                       "collective": args.tp_collective if world > 1 else "none",
+                       "exchange": NCCL_EXCHANGE if args.tp_collective == "nccl" and world > 1 else PEER_EXCHANGE},
             "per_rank": {"stream_bytes": info["stream_bytes"], "achieved_gbs": gbs, "hbm_frac": gbs / hbm,
                          "peak": hbm, "peak_kind": peak_kind, "weight_bytes": info["weight_bytes"],
                          "load_s": load_s},

@@ -348,6 +348,15 @@ int pk_tp_handle_bytes(void);
 /* This rank's handle (after a load); then every rank passes all T handles in rank order. */
 int pk_tp_ipc_handle(pk_tp *tp, void *out);
 int pk_tp_open_peers(pk_tp *tp, const void *handles);
+/* The o / down exchange through an NCCL all-reduce instead of the peer-memory
+ * push (no counterpart in the reference, which runs on one device).  Rank 0
+ * makes an id with pk_tp_nccl_id (pk_tp_nccl_id_bytes bytes); every rank
+ * passes that id to pk_tp_use_nccl after pk_tp_open_peers, and the call
+ * returns once all T ranks have joined.  NCCL is loaded at the first call
+ * (the process's libnccl.so.2); PK_ERR_UNSUPPORTED when none can be loaded. */
+int pk_tp_nccl_id_bytes(void);
+int pk_tp_nccl_id(void *out);
+int pk_tp_use_nccl(pk_tp *tp, const void *id);
 /* The prompt as b = 1 steps; the last step picks the first generated token. */
 int pk_tp_prefill(pk_tp *tp, const uint32_t *prompt, int n);
 /* n_steps tokens as pk_decode_steps_device: the token picked last, then the next n_steps - 1; the

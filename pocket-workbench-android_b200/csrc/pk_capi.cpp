@@ -551,6 +551,15 @@ int pk_tp_open_peers(pk_tp *t, const void *handles) {
   return t->eng.open_peers(handles);
 }
 
+int pk_tp_nccl_id_bytes(void) { return tp_nccl_id_bytes(); }
+
+int pk_tp_nccl_id(void *out) { return tp_nccl_id(out); }
+
+int pk_tp_use_nccl(pk_tp *t, const void *id) {
+  if (!t || !id) return set_error(PK_ERR_INVALID, "null argument");
+  return t->eng.use_nccl(id);
+}
+
 int pk_tp_prefill(pk_tp *t, const uint32_t *prompt, int n) {
   if (!t || !prompt) return set_error(PK_ERR_INVALID, "null argument");
   return t->eng.prefill(prompt, n);

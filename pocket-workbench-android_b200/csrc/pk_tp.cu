@@ -13,7 +13,12 @@
 // Slots alternate by the parity of the sequence number: a rank can only
 // publish sequence s + 1 after every rank published s, which each does only
 // after it finished reading s - 1 from the slots s + 1 reuses.
+// Alternatively (use_nccl) the o / down partials go through an NCCL
+// all-reduce on the engine's stream, and k_tp_add adds the sum to x.
 #include "pk_tp.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -95,13 +100,60 @@ __global__ void __launch_bounds__(256) k_tp_push(const float *__restrict__ src, 
     const float4 v = __ldcg(reinterpret_cast<const float4 *>(src) + j);
     reinterpret_cast<float4 *>(P.slots[dst] + ((size_t)par * world + rank) * n)[j] = v;
   }
-  __threadfence_system();
+  // The CTA's stores, ordered by the barrier, then one system-scope fence by
+  // the thread that counts the CTA in (the grid barrier's pattern): the fence
+  // is cumulative over what the barrier made visible to that thread.
   __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
   if (threadIdx.x == 0 && atomicAdd(count, 1u) == gridDim.x - 1) {  // every CTA's stores are out
     *count = 0;
     __threadfence_system();
     for (int dst = 0; dst < world; dst++) st_release_sys(P.flags[dst] + rank, seq);
   }
+}
+
+// x += part after an NCCL all-reduce of the partials (at T = 2 the sum of
+// the two partials is the same in either order, so x gets the peer
+// exchange's bits).
+__global__ void __launch_bounds__(256) k_tp_add(float *x, int n, const float *part) {
+  pdl_trigger();
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] = fadd(x[i], part[i]);
+}
+
+// NCCL, loaded on first use so that the library does not depend on it: the
+// process's copy when one is loaded already (a PyTorch process has one),
+// else the system's libnccl.so.2.
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*get_id)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+  const char *(*err)(ncclResult_t) = nullptr;
+};
+
+const NcclApi &nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi a;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char *e = dlerror();
+      a.why = e ? e : "dlopen(libnccl.so.2) failed";
+      return a;
+    }
+    a.get_id = reinterpret_cast<decltype(a.get_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.err = reinterpret_cast<decltype(a.err)>(dlsym(h, "ncclGetErrorString"));
+    a.ok = a.get_id && a.init_rank && a.all_reduce && a.destroy && a.err;
+    if (!a.ok) a.why = "libnccl.so.2 lacks an entry point";
+    return a;
+  }();
+  return api;
 }
 
 __global__ void __launch_bounds__(256) k_tp_sum(float *x, int n, const float *slots, const unsigned long long *flags,
@@ -260,6 +312,7 @@ bool tp_split(const Config &c, int vocab, int rank, int world, int o_block, int 
 
 TpEngine::~TpEngine() {
   if (st_) cudaStreamSynchronize(st_);
+  if (nccl_comm_) nccl_api().destroy(static_cast<ncclComm_t>(nccl_comm_));
   for (void *p : peer_base_)
     if (p) cudaIpcCloseMemHandle(p);
   cudaFree(d_weights_);
@@ -597,12 +650,51 @@ int TpEngine::finish_load(const Config &c, int vocab) {
   return PK_OK;
 }
 
-int TpEngine::allreduce_add(const float *part, float *x) {
+int TpEngine::allreduce_add(float *part, float *x) {
   ++seq_;
   const int ne = cfg_.n_embd;
+  if (nccl_comm_) {
+    const NcclApi &n = nccl_api();
+    const ncclResult_t r =
+        n.all_reduce(part, part, (size_t)ne, ncclFloat32, ncclSum, static_cast<ncclComm_t>(nccl_comm_), st_);
+    if (r != ncclSuccess) return set_error(PK_ERR_CUDA, std::string("ncclAllReduce: ") + n.err(r));
+    PK_CK(tp_launch(k_tp_add, dim3(8), dim3(256), 0, st_, x, ne, (const float *)part));
+    return PK_OK;
+  }
   PK_CK(tp_launch(k_tp_push, dim3(TP_PUSH_CTAS), dim3(256), 0, st_, part, ne, peers_, rank_, world_, seq_, d_count_));
   PK_CK(tp_launch(k_tp_sum, dim3(8), dim3(256), 0, st_, x, ne, (const float *)peers_.slots[rank_],
                   (const unsigned long long *)peers_.flags[rank_], world_, seq_, d_err_));
+  return PK_OK;
+}
+
+int tp_nccl_id_bytes() { return (int)sizeof(ncclUniqueId); }
+
+int tp_nccl_id(void *out) {
+  if (!out) return set_error(PK_ERR_INVALID, "null id buffer");
+  const NcclApi &n = nccl_api();
+  if (!n.ok) return set_error(PK_ERR_UNSUPPORTED, "NCCL is not available: " + n.why);
+  ncclUniqueId id;
+  const ncclResult_t r = n.get_id(&id);
+  if (r != ncclSuccess) return set_error(PK_ERR_CUDA, std::string("ncclGetUniqueId: ") + n.err(r));
+  std::memcpy(out, &id, sizeof id);
+  return PK_OK;
+}
+
+// Collective over the T ranks: every rank calls it with rank 0's id and
+// blocks until all have joined.
+int TpEngine::use_nccl(const void *id) {
+  if (!peers_open_) return set_error(PK_ERR_INVALID, "open the peers first");
+  if (!id) return set_error(PK_ERR_INVALID, "null NCCL id");
+  if (nccl_comm_) return set_error(PK_ERR_INVALID, "the NCCL exchange is already in use");
+  const NcclApi &n = nccl_api();
+  if (!n.ok) return set_error(PK_ERR_UNSUPPORTED, "NCCL is not available: " + n.why);
+  PK_CK(cudaSetDevice(device_));
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof uid);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = n.init_rank(&comm, world_, uid, rank_);
+  if (r != ncclSuccess) return set_error(PK_ERR_CUDA, std::string("ncclCommInitRank: ") + n.err(r));
+  nccl_comm_ = comm;
   return PK_OK;
 }
 

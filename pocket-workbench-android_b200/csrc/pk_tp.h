@@ -56,6 +56,11 @@ struct TpPeers {
   unsigned long long *flags[TP_MAX];    // [T]: the last sequence number rank s published here
 };
 
+// Bytes of an NCCL unique id, and a new one (rank 0 makes it, every rank
+// passes it to TpEngine::use_nccl).  NCCL is loaded on first use.
+int tp_nccl_id_bytes();
+int tp_nccl_id(void *out);
+
 class TpEngine {
  public:
   ~TpEngine();
@@ -63,6 +68,9 @@ class TpEngine {
   size_t exchange_bytes() const;
   int ipc_handle(void *out);  // cudaIpcMemHandle_t of this rank's exchange buffer
   int open_peers(const void *handles);  // T handles in rank order
+  // The o / down exchange through an NCCL all-reduce (every rank, after
+  // open_peers, with the same unique id) instead of the peer-memory push.
+  int use_nccl(const void *id);
   int load(const char *path);
   int load_synthetic(const Config &c, int vocab, uint64_t seed);
   int prefill(const uint32_t *prompt, int n);  // b = 1 steps; ends with the first generated token on the device
@@ -73,7 +81,7 @@ class TpEngine {
  private:
   int finish_load(const Config &c, int vocab);
   int step(bool feedback);  // one token: layers, head, first maximum over shards
-  int allreduce_add(const float *part, float *x);
+  int allreduce_add(float *part, float *x);
   int check_error();
 
   int device_ = 0, n_ctx_ = 0, rank_ = 0, world_ = 1;
@@ -101,6 +109,7 @@ class TpEngine {
   void *peer_base_[TP_MAX] = {};    // opened peer buffers (nullptr for the own rank)
   TpPeers peers_{};
   unsigned long long seq_ = 0;
+  void *nccl_comm_ = nullptr;  // ncclComm_t once use_nccl succeeded
   int next_pos_ = 0;
   uint32_t last_tok_ = 0;
   bool have_tok_ = false;

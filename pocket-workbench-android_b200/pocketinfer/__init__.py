@@ -40,7 +40,8 @@ SYMBOLS = [
     "pk_forward", "pk_logits", "pk_argmax", "pk_generate", "pk_decode_steps_device", "pk_set_position", "pk_set_order", "pk_set_kv_type",
     "pk_decode_profile", "pk_selftest_bounded_wait", "pk_set_debug", "pk_get_dump", "pk_request_stop",
     "pk_clear_stop", "pk_tp_create", "pk_tp_destroy", "pk_tp_load_gguf", "pk_tp_load_synthetic",
-    "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
+    "pk_tp_handle_bytes", "pk_tp_ipc_handle", "pk_tp_open_peers", "pk_tp_nccl_id_bytes", "pk_tp_nccl_id",
+    "pk_tp_use_nccl", "pk_tp_prefill", "pk_tp_decode", "pk_tp_logits",
     "pk_tp_info_get", "pk_tp_split", "pk_tp_pick", "pk_sample_scratch_bytes", "pk_sample",
     "pk_streams_begin", "pk_stream_prefill", "pk_streams_decode", "pk_streams_set_position",
     "pk_tokenizer_load", "pk_tokenizer_free", "pk_tokenizer_info_get", "pk_tokenize", "pk_token_bytes",
@@ -136,6 +137,7 @@ def lib():
         "pk_tp_create": ([I, I, I, I, C.POINTER(P)], I), "pk_tp_destroy": ([P], None),
         "pk_tp_load_gguf": ([P, C.c_char_p], I), "pk_tp_load_synthetic": ([P, C.POINTER(TpModel), C.c_uint64], I),
         "pk_tp_handle_bytes": ([], I), "pk_tp_ipc_handle": ([P, P], I), "pk_tp_open_peers": ([P, P], I),
+        "pk_tp_nccl_id_bytes": ([], I), "pk_tp_nccl_id": ([P], I), "pk_tp_use_nccl": ([P, P], I),
         "pk_tp_prefill": ([P, P, I], I), "pk_tp_decode": ([P, I, P, C.POINTER(C.c_float)], I),
         "pk_tp_logits": ([P, P, I, C.POINTER(I), C.POINTER(I)], I), "pk_tp_info_get": ([P, C.POINTER(TpInfo)], I),
         "pk_tp_split": ([I, I, I, I, I, I, I, I, I, P], I), "pk_tp_pick": ([P, P, I], U32),

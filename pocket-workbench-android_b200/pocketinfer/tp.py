@@ -77,8 +77,14 @@ class TpEngine:
         _check(lib().pk_tp_ipc_handle(self.h, C.cast(buf, C.c_void_p)))
         return bytes(buf)
 
-    def connect(self, exchange=allgather_bytes):
-        """Exchange peer-memory handles (``exchange(bytes) -> [bytes] * world`` in rank order) and open them."""
+    def connect(self, exchange=allgather_bytes, collective: str = "peer"):
+        """Exchange peer-memory handles (``exchange(bytes) -> [bytes] * world`` in rank order) and open them.
+
+        ``collective="nccl"`` then moves the o / down exchange onto an NCCL
+        all-reduce: rank 0's NCCL id goes to every rank through ``exchange``
+        and every rank joins the communicator (pk_tp_use_nccl)."""
+        if collective not in ("peer", "nccl"):
+            raise PkError(1, "collective must be 'peer' or 'nccl'")
         mine = self.handle()
         allh = exchange(mine)
         if len(allh) != self.world or allh[self.rank] != mine:
@@ -87,6 +93,15 @@ class TpEngine:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         _check(lib().pk_tp_open_peers(self.h, C.cast(buf, C.c_void_p)))
         self.connected = True
+        if collective == "nccl":
+            n = lib().pk_tp_nccl_id_bytes()
+            idb = (C.c_uint8 * n)()
+            if self.rank == 0:
+                _check(lib().pk_tp_nccl_id(C.cast(idb, C.c_void_p)))
+            ids = exchange(bytes(idb))
+            root = (C.c_uint8 * n).from_buffer_copy(ids[0])
+            _check(lib().pk_tp_use_nccl(self.h, C.cast(root, C.c_void_p)))
+        self.collective = collective
 
     def prefill(self, prompt):
         import numpy as np

@@ -62,15 +62,15 @@ def _free_port():
     return port
 
 
-def _tp2_worker(rank, world, port, path, prompt, n, q):
+def _tp2_worker(rank, world, port, path, prompt, n, q, collective="peer"):
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         t = tp.TpEngine(rank, world, device=rank, n_ctx=256)
         t.load(path)
-        t.connect()
+        t.connect(collective=collective)
         t.prefill(prompt)
         lg, v0 = t.logits()
         ids = t.decode(n)
@@ -83,14 +83,19 @@ def _tp2_worker(rank, world, port, path, prompt, n, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_matches_tp1(pk, paths):
+@pytest.mark.parametrize("collective", ["peer", "nccl"])
+def test_tp2_matches_tp1(pk, paths, collective):
+    """T = 2 (two GPUs, two processes) against T = 1: logits within 1e-3 of
+    their spread and the same greedy tokens, with the o / down exchange on
+    the peer-memory push or on an NCCL all-reduce."""
     spec = MODELS["q40"]
     prompt = synth.prompt_ids(43, 24, spec.n_vocab)
     n = 24
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp2_worker, args=(r, 2, port, paths["q40"], prompt, n, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp2_worker, args=(r, 2, port, paths["q40"], prompt, n, q, collective))
+             for r in range(2)]
     for p in procs:
         p.start()
     out = sorted([q.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
