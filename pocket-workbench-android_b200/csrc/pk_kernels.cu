@@ -1624,20 +1624,33 @@ __global__ void __launch_bounds__(DH == 64 ? 128 : 256) k_attn_b1t(AttnArgs a) {
     const KT *cur = tiles + (t % NS) * TILE;
     float *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
-    if (tid < nv) ec[tid] = expf_lib(fsub(ec[tid], M));
-    __syncthreads();
+    bool zero = false;  // a weight of this tile underflowed to 0
+    if (tid < nv) {
+      ec[tid] = expf_lib(fsub(ec[tid], M));
+      zero = ec[tid] == 0.0f;
+    }
+    const bool any_zero = __syncthreads_or(zero) != 0;  // uniform over the CTA
     // the tile's products e_p * v_p[d] by every thread (-0.0 for a zero
     // weight, which the chain then adds exactly as a skip), so that each
     // chain step below waits for one add; f32 products overwrite the tile
     float *const pr = sizeof(KT) == 4 ? reinterpret_cast<float *>(tiles + (t % NS) * TILE) : prod_buf;
-    for (int i = tid; i < nv * (DH / 4); i += NT) {
-      const int j = i / (DH / 4), d4 = 4 * (i % (DH / 4));
-      const float e = ec[j];
-      const float4 v = kv_f4(cur + j * DH + d4);
-      const bool z = e == 0.0f;
-      *reinterpret_cast<float4 *>(pr + j * DH + d4) =
-          make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
-                      z ? -0.0f : fmul(e, v.w));
+    if (!any_zero) {  // no weight is 0: the plain products
+      for (int i = tid; i < nv * (DH / 4); i += NT) {
+        const int j = i / (DH / 4), d4 = 4 * (i % (DH / 4));
+        const float e = ec[j];
+        const float4 v = kv_f4(cur + j * DH + d4);
+        *reinterpret_cast<float4 *>(pr + j * DH + d4) = make_float4(fmul(e, v.x), fmul(e, v.y), fmul(e, v.z), fmul(e, v.w));
+      }
+    } else {
+      for (int i = tid; i < nv * (DH / 4); i += NT) {
+        const int j = i / (DH / 4), d4 = 4 * (i % (DH / 4));
+        const float e = ec[j];
+        const float4 v = kv_f4(cur + j * DH + d4);
+        const bool z = e == 0.0f;
+        *reinterpret_cast<float4 *>(pr + j * DH + d4) =
+            make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
+                        z ? -0.0f : fmul(e, v.w));
+      }
     }
     __syncthreads();
     if (tid < DH) {
@@ -1808,17 +1821,30 @@ __global__ void __launch_bounds__(PV_NT) k_attn_pv(AttnArgs a, int nch) {
     const KT *cur = pieces + (t % NS) * P * W;
     float *ec = es + (t % NS) * P;
     const int nv = min(P, n - t * P);
-    for (int j = tid; j < nv; j += NT) ec[j] = expf_lib(fsub(ec[j], M));
-    __syncthreads();
+    bool zero = false;  // a weight of this tile underflowed to 0
+    for (int j = tid; j < nv; j += NT) {
+      ec[j] = expf_lib(fsub(ec[j], M));
+      zero = zero || ec[j] == 0.0f;
+    }
+    const bool any_zero = __syncthreads_or(zero) != 0;  // uniform over the CTA
     float *const pr = sizeof(KT) == 4 ? reinterpret_cast<float *>(pieces + (t % NS) * P * W) : prod_buf;
-    for (int i = tid; i < nv * (W / 4); i += NT) {
-      const int j = i / (W / 4), d4 = 4 * (i % (W / 4));
-      const float e = ec[j];
-      const float4 v = kv_f4(cur + j * W + d4);
-      const bool z = e == 0.0f;
-      *reinterpret_cast<float4 *>(pr + j * W + d4) =
-          make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
-                      z ? -0.0f : fmul(e, v.w));
+    if (!any_zero) {  // no weight is 0: the plain products
+      for (int i = tid; i < nv * (W / 4); i += NT) {
+        const int j = i / (W / 4), d4 = 4 * (i % (W / 4));
+        const float e = ec[j];
+        const float4 v = kv_f4(cur + j * W + d4);
+        *reinterpret_cast<float4 *>(pr + j * W + d4) = make_float4(fmul(e, v.x), fmul(e, v.y), fmul(e, v.z), fmul(e, v.w));
+      }
+    } else {
+      for (int i = tid; i < nv * (W / 4); i += NT) {
+        const int j = i / (W / 4), d4 = 4 * (i % (W / 4));
+        const float e = ec[j];
+        const float4 v = kv_f4(cur + j * W + d4);
+        const bool z = e == 0.0f;
+        *reinterpret_cast<float4 *>(pr + j * W + d4) =
+            make_float4(z ? -0.0f : fmul(e, v.x), z ? -0.0f : fmul(e, v.y), z ? -0.0f : fmul(e, v.z),
+                        z ? -0.0f : fmul(e, v.w));
+      }
     }
     __syncthreads();
     if (tid < W) {
