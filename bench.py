@@ -373,7 +373,12 @@ def tp70_leg(world, rank, local, dist, steps=16, warmup=3):
     peer = tp70_run(world, rank, local, dist, steps, warmup, "peer")
     if world == 1:
         return peer
-    nccl = tp70_run(world, rank, local, dist, steps, warmup, "nccl")
+    try:
+        nccl = tp70_run(world, rank, local, dist, steps, warmup, "nccl")
+    except Exception as exc:  # noqa: BLE001 -- every rank fails the same way (see TpEngine.connect)
+        out = dict(peer)
+        out["nccl_error"] = str(exc)[:200]
+        return out
     best = nccl if nccl["value"] > peer["value"] else peer
     out = dict(best)
     out["by_collective"] = {"peer": {k: peer[k] for k in ("value", "ms_per_step", "per_rank_hbm_frac")},

@@ -94,11 +94,20 @@ class TpEngine:
         _check(lib().pk_tp_open_peers(self.h, C.cast(buf, C.c_void_p)))
         self.connected = True
         if collective == "nccl":
+            # rank 0 always takes part in the id exchange (an empty id when it
+            # could not make one), so every rank fails together, not only rank 0
             n = lib().pk_tp_nccl_id_bytes()
-            idb = (C.c_uint8 * n)()
+            mine_id, why = b"", ""
             if self.rank == 0:
-                _check(lib().pk_tp_nccl_id(C.cast(idb, C.c_void_p)))
-            ids = exchange(bytes(idb))
+                idb = (C.c_uint8 * n)()
+                try:
+                    _check(lib().pk_tp_nccl_id(C.cast(idb, C.c_void_p)))
+                    mine_id = bytes(idb)
+                except PkError as e:
+                    why = str(e)
+            ids = exchange(mine_id)
+            if len(ids[0]) != n:
+                raise PkError(2, "rank 0 could not make an NCCL id" + (f": {why}" if why else ""))
             root = (C.c_uint8 * n).from_buffer_copy(ids[0])
             _check(lib().pk_tp_use_nccl(self.h, C.cast(root, C.c_void_p)))
         self.collective = collective

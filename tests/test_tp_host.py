@@ -112,3 +112,59 @@ def test_handle_exchange_is_rank_ordered_over_gloo():
         p.join(timeout=60)
     for _, got in out:
         assert got == [bytes([0]) * 64, bytes([1]) * 64]
+
+
+class _FakeLib:
+    """The C entry points TpEngine.connect calls, with pk_tp_nccl_id failing."""
+
+    def __init__(self):
+        self.used_nccl = False
+
+    def pk_tp_handle_bytes(self):
+        return 4
+
+    def pk_tp_ipc_handle(self, h, out):
+        return 0
+
+    def pk_tp_open_peers(self, h, handles):
+        return 0
+
+    def pk_tp_nccl_id_bytes(self):
+        return 8
+
+    def pk_tp_nccl_id(self, out):
+        return 2  # PK_ERR_UNSUPPORTED: no NCCL here
+
+    def pk_tp_use_nccl(self, h, ident):
+        self.used_nccl = True
+        return 0
+
+    def pk_last_error(self):
+        return b"NCCL is not available"
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_nccl_connect_failure_reaches_every_rank(monkeypatch, rank):
+    """When rank 0 cannot make an NCCL id it still takes part in the id
+    exchange (an empty id), so every rank raises instead of the others
+    waiting in the exchange until the process group times out; no rank
+    joins a communicator."""
+    import pocketinfer
+
+    fake = _FakeLib()
+    monkeypatch.setattr(tp, "lib", lambda: fake)
+    monkeypatch.setattr(pocketinfer, "lib", lambda: fake)
+    eng = tp.TpEngine.__new__(tp.TpEngine)
+    eng.rank, eng.world, eng.h, eng.connected = rank, 2, None, False
+    sent = []
+
+    def exchange(blob):  # rank 0's blob first, as an all-gather in rank order
+        sent.append(blob)
+        if len(blob) == 4:  # the peer handles
+            return [b"\0" * 4, b"\0" * 4]
+        return [blob if rank == 0 else b"", b""]
+
+    with pytest.raises(PkError, match="rank 0 could not make an NCCL id"):
+        eng.connect(exchange=exchange, collective="nccl")
+    assert len(sent) == 2 and not fake.used_nccl
+    eng.h = None
